@@ -1,0 +1,398 @@
+#!/usr/bin/env python
+"""MoE-layer tokens/s on B200 for the DeepSeek-V2 MoE sublayer (one JSON line on rank 0).
+
+Headline workload (the int8 decode config): one decode step of
+B = 8 tokens through 11 MoE layers with distinct seeded weights (the configs[3] stack; the
+2.6 GB of weights rotate through the 126 MB L2, so no step reads its weights from L2).
+value = B * layers / step time = MoE-layer tokens/s; every step routes, runs the routed
+experts, the shared experts and the combine, captured as one CUDA graph of the public API
+calls. Sub-configs (int8/bf16 x B = 1/8) ride along in "configs".
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+N > 1 (torchrun): the decode path does not shard (B <= 8), so each rank runs an
+independent replica ("replicas only"); value = sum over ranks, time = max over ranks.
+--impl reference times the reference's fp32 CPU path (the oracle port in torch) on the host
+cores with the same config and metric; rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import importlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from datetime import timedelta
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+PKG = "unlimited-ocr-max_b200"
+
+H, I, E, TOPK, S = 1280, 896, 64, 6, 2
+W_E_BF16 = 3 * I * H * 2                                   # 6 881 280 B per routed expert
+W_E_INT8 = 3 * I * H + (I * (H // 128) * 2 + H * (I // 128)) * 4  # 3 548 160 B
+W_SH = 3 * (S * I) * H * 2                                 # 13 762 560 B
+W_G = E * H * 2                                            # 163 840 B
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=200)
+    p.add_argument("--warmup", type=int, default=20)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--batch", type=int, default=8)
+    p.add_argument("--layers", type=int, default=11)
+    p.add_argument("--no-sub", action="store_true", help="skip the ride-along sub-configs")
+    p.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------------------------------------
+# clocks
+# ---------------------------------------------------------------------------------------------
+
+
+class ClockSampler:
+    """nvidia-smi sampling during the measured load (recipe's query line)."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits", "-lms", "50",
+                 "-i", str(self.gpu)], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"], "samples": 0}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons, power = [], [], set(), []
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [c.strip() for c in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+                power.append(float(f[3]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm), "power_w_max": max(power)}
+
+
+def physical_gpu_index(local_rank: int) -> int:
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        parts = [p for p in vis.split(",") if p.strip()]
+        if local_rank < len(parts) and parts[local_rank].strip().isdigit():
+            return int(parts[local_rank])
+    return local_rank
+
+
+def measured_peaks() -> tuple[float, str]:
+    try:
+        d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return float(d["hbm_gbs"]), "measured"
+    except Exception:  # noqa: BLE001
+        return 6650.0, "fallback"
+
+
+# ---------------------------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------------------------
+
+
+def build_stack(uocr, synth, int8: bool, layers: int, B: int, device, seed0: int):
+    import torch
+
+    cfg = uocr.MoEConfig(int8_experts=int8)
+    mods, xs, outs, ids, wts = [], [], [], [], []
+    for l in range(layers):
+        st = synth.layer_state(cfg, seed0 + l, device=device)
+        mods.append(uocr.UocrMoE(cfg, device=device).load_state_dict(st))
+        del st
+        xs.append(synth.hidden_states(B, H, seed0 + 100 + l, device=device))
+        outs.append(torch.empty((B, H), dtype=torch.float32, device=device))
+        ids.append(torch.empty((B, TOPK), dtype=torch.int32, device=device))
+        wts.append(torch.empty((B, TOPK), dtype=torch.float32, device=device))
+    torch.cuda.empty_cache()
+    return mods, xs, outs, ids, wts
+
+
+def time_stack(torch, mods, xs, outs, ids, wts, steps, warmup, dist, sampler=None, settle_s=0.0):
+    """Capture the step (all layers' public decode calls) in a CUDA graph; time `steps` replays."""
+    def step():
+        for m, x, o, i, w in zip(mods, xs, outs, ids, wts):
+            m.decode_rows(x, out=o, ids=i, wts=w)
+
+    step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+        t0 = time.time()
+        while time.time() - t0 < settle_s:  # untimed load so the sampler sees the clocks under load
+            for _ in range(50):
+                g.replay()
+            torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    ms = a.elapsed_time(b) / steps
+    if dist:
+        t = torch.tensor([ms], device=xs[0].device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return g, ms, clocks
+
+
+def algorithmic_bytes(torch, ids_list, int8: bool, B: int) -> int:
+    total = 0
+    we = W_E_INT8 if int8 else W_E_BF16
+    for ids in ids_list:
+        U = int(torch.unique(ids).numel())
+        total += U * we + W_SH + W_G + B * H * 8
+    return total
+
+
+def time_e2e(torch, g, xs, outs, steps, warmup):
+    """Public API end to end: H2D of every layer's input from pinned host memory, the step,
+    D2H of every layer's output, all inside the timed region."""
+    xh = [x.cpu().pin_memory() for x in xs]
+    oh = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
+
+    def one():
+        for h, d in zip(xh, xs):
+            d.copy_(h, non_blocking=True)
+        g.replay()
+        for h, d in zip(oh, outs):
+            h.copy_(d, non_blocking=True)
+
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        one()
+    b.record()
+    torch.cuda.synchronize()
+    nbytes = sum(x.numel() * 4 for x in xs)
+    return a.elapsed_time(b) / steps, nbytes, sum(o.numel() * 4 for o in outs)
+
+
+class CpuDecode:
+    """The reference's fp32 CPU decode path (MoE.decode_rows restated in torch, the oracle port)
+    on all host cores, one MoE layer of the benchmark's shape."""
+
+    def __init__(self, int8: bool, B: int, seed: int = 7):
+        import numpy as np
+        import torch
+
+        from oracle import moe_oracle as o
+
+        self.cores = len(os.sched_getaffinity(0))
+        torch.set_num_threads(self.cores)
+        uocr = importlib.import_module(PKG)
+        synth = importlib.import_module(f"{PKG}.synth")
+        st = synth.layer_state(uocr.MoEConfig(int8_experts=int8), seed, device="cpu")
+        bits = lambda t: t.view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+        kw = dict(router=bits(st["gate.gate_score.weight"]), shared_gate=bits(st["shared_experts.gate_proj.weight"]),
+                  shared_up=bits(st["shared_experts.up_proj.weight"]),
+                  shared_down=bits(st["shared_experts.down_proj.weight"]))
+        for n in ("gate", "up", "down"):
+            t = st[f"experts.{n}_proj"]
+            kw[n] = t.numpy() if int8 else bits(t)
+            if int8:
+                kw[f"{n}_scales"] = st[f"experts.{n}_proj_scales"].numpy()
+        self.layer = o.TorchCpuLayer(o.MoEConfig(), o.MoEWeights(**kw))
+        self.x = synth.hidden_states(B, H, seed + 1, device="cpu")
+        self.B, self.int8 = B, int8
+        self.layer.decode_rows(self.x)  # warm-up
+
+    def step_seconds(self) -> float:
+        t0 = time.perf_counter()
+        self.layer.decode_rows(self.x)
+        return time.perf_counter() - t0
+
+    def rate(self, budget_s: float = 12.0):
+        n, el = 0, 0.0
+        while el < budget_s and n < 2000:
+            el += self.step_seconds()
+            n += 1
+        sample = f"{n} single-layer decode steps of B={self.B} ({'int8' if self.int8 else 'bf16'}), {el:.1f} s"
+        return self.B * n / el, self.cores, sample
+
+
+def run_ours(args):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    dist = None
+    if world > 1:
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    uocr = importlib.import_module(PKG)
+    synth = importlib.import_module(f"{PKG}.synth")
+    uocr.load()
+    B, L = args.batch, args.layers
+
+    mods, xs, outs, ids, wts = build_stack(uocr, synth, True, L, B, device, 1000)
+    sampler = ClockSampler(physical_gpu_index(local))
+    g, ms, clocks = time_stack(torch, mods, xs, outs, ids, wts, args.steps, args.warmup, dist, sampler, settle_s=1.5)
+    step_bytes = algorithmic_bytes(torch, ids, True, B)
+    peak, peak_src = measured_peaks()
+    achieved = step_bytes / (ms * 1e-3) / 1e9
+    value = world * B * L / (ms * 1e-3)
+    e2e_ms, h2d, d2h = time_e2e(torch, g, xs, outs, max(args.steps // 4, 10), 3)
+    if dist:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    finite = all(bool(torch.isfinite(o).all()) for o in outs)
+    del g
+    subs = {}
+    if not args.no_sub:
+        del mods, xs, outs, ids, wts
+        torch.cuda.empty_cache()
+        for int8, b in ((True, 1), (False, 1), (False, 8)):
+            m2, x2, o2, i2, w2 = build_stack(uocr, synth, int8, L, b, device, 2000 + 10 * b + int8)
+            g2, ms2, _ = time_stack(torch, m2, x2, o2, i2, w2, args.steps, args.warmup, dist)
+            by = algorithmic_bytes(torch, i2, int8, b)
+            subs[f"decode_{'int8' if int8 else 'bf16'}_b{b}"] = {
+                "value": world * b * L / (ms2 * 1e-3), "unit": "tokens/s", "us_per_layer": ms2 * 1e3 / L,
+                "hbm_gbs": by / (ms2 * 1e-3) / 1e9, "frac": by / (ms2 * 1e-3) / 1e9 / peak}
+            del g2, m2, x2, o2, i2, w2
+            torch.cuda.empty_cache()
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        v, cores, sample = CpuDecode(True, B).rate()
+        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+    if rank == 0:
+        launches_per_step = 4 * L  # route, gate/up, down, combine per layer
+        line = {
+            "metric": "MoE-layer tokens/s (decode, int8 routed experts, B=8)",
+            "value": value,
+            "unit": "tokens/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": ms,
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "int8 weights x fp32 activations, fp32 accumulate",
+            "data": "synthetic (seeded random-init weights N(0,0.02)->bf16->int8 G=128; hidden N(0,1) RMS-normalised)",
+            "config": {
+                "workload": "configs[1] int8 decode B=8 over an 11-layer stack of distinct layers (configs[3] shape)",
+                "hidden": H, "experts": E, "top_k": TOPK, "shared": S, "moe_intermediate": I,
+                "batch": B, "layers_per_step": L,
+                "l2": f"weights rotate over {L} layers ({step_bytes / 1e9:.2f} GB algorithmic per step) >> 126 MB L2",
+                "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                "execution": "one CUDA graph per step of the public decode calls",
+            },
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": peak_src, "scope": "whole decode layer step (route+experts+combine)",
+                         "algorithmic_bytes_per_step": step_bytes, "traffic": None},
+            "e2e": {"value": world * B * L / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+            "gpu_launches": launches_per_step * args.steps,
+            "clocks": clocks,
+            "cpu_baseline": cpu,
+            "configs": subs,
+            "outputs_finite": finite,
+        }
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def run_reference(args):
+    """The reference arm: its fp32 CPU decode path (the oracle port) on this box's host cores.
+    A step is one single-layer decode step of B tokens (a bounded sample of the workload)."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    B = args.batch
+    cpu = CpuDecode(True, B)
+    for _ in range(args.warmup):
+        cpu.step_seconds()
+    times, total = [], 0.0
+    for _ in range(args.steps):
+        t = cpu.step_seconds()
+        times.append(t)
+        total += t
+        if total > 90.0:
+            break
+    value = B / statistics.median(times)
+    line = {
+        "impl": "reference",
+        "metric": "MoE-layer tokens/s (decode, int8 routed experts, B=8)",
+        "value": value, "unit": "tokens/s", "n_gpus": world, "steps": len(times), "warmup": args.warmup,
+        "ms_per_step": 1e3 * statistics.median(times), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "fp32 (the reference's CPU path)", "data": "synthetic",
+        "config": {"workload": "configs[1] int8 decode B=8, one MoE layer per step", "batch": B},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cpu.cores, "kind": "port",
+                         "sample": f"{len(times)} single-layer decode steps of B={B}, median step"},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,155 @@
+/*
+ * uocr_moe.h -- C ABI of libuocr_moe.so, the B200 (sm_100a) implementation of the
+ * DeepSeek-V2 mixture-of-experts sublayer of the Unlimited-OCR decoder.
+ *
+ * Conventions for every entry point:
+ *   - all tensor pointers are DEVICE pointers, row-major and packed, owned by the caller;
+ *     no entry point allocates device memory;
+ *   - bf16 tensors are passed as uint16_t bit patterns;
+ *   - work is enqueued asynchronously on `stream` (a cudaStream_t; NULL = legacy default);
+ *   - the return value is a status: UOCR_OK (0) or an error code; on error,
+ *     uocr_last_error() returns a thread-local message. Shape errors are detected on the
+ *     host before anything is launched and carry the reference op's message text;
+ *   - out-of-range expert ids are clamped to [0, E) on the device, never faulting
+ *     (kernels/moe_routing.mojo:11-16 of the reference).
+ */
+#ifndef UOCR_MOE_H
+#define UOCR_MOE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef void* uocr_stream_t; /* cudaStream_t */
+
+/* Only the functions of this header are exported from libuocr_moe.so. */
+#if defined(__GNUC__)
+#define UOCR_API __attribute__((visibility("default")))
+#else
+#define UOCR_API
+#endif
+
+enum {
+    UOCR_OK = 0,
+    UOCR_EINVAL = 1,      /* bad shape or argument (host-side check, nothing launched) */
+    UOCR_ECUDA = 2,       /* a CUDA runtime call failed */
+    UOCR_EDEVICE = 3,     /* a device-side bounded wait gave up (see uocr_moe_device_status) */
+    UOCR_EUNSUPPORTED = 4 /* a configuration this build does not implement */
+};
+
+/* Thread-local message of the last failed call on this thread ("" if none). */
+UOCR_API const char* uocr_last_error(void);
+/* ABI version of this header (bumped on any signature change). */
+UOCR_API int uocr_abi_version(void);
+
+/* ------------------------------------------------------------------------------------ *
+ * The reference's MoE custom ops, 1:1 (same arguments, same shape checks and messages,
+ * same clamp and empty-batch behaviour). Each tensor is given with its dims, as the
+ * reference op receives whole tensors.
+ * ------------------------------------------------------------------------------------ */
+
+/* moe_bf16_qmv: out[s,n] = sum_k f32(w[clamp(ids[s]),n,k]) * x[s,k]   (fp32 accumulate)
+ * Replaces @register("moe_bf16_qmv"), unlimited_ocr_max/kernels/moe_bf16.mojo:264-345,
+ * staged by StackedExperts._qmv (unlimited_ocr_max/decoder.py:355-366).
+ * Every row's bits are independent of the other rows of the call. */
+UOCR_API int uocr_moe_bf16_qmv(float* out, int64_t out_rows, int64_t out_cols,
+                      const float* x, int64_t x_rows, int64_t x_cols,
+                      const int32_t* expert_ids, int64_t ids_len,
+                      const uint16_t* w, int64_t w_e, int64_t w_n, int64_t w_k,
+                      uocr_stream_t stream);
+
+/* moe_int8_qmv: out[s,n] = sum_g scales[e,n,g] * sum_{k in g} f32(w[e,n,k]) * x[s,k],
+ * e = clamp(ids[s]), in the reference's exact fp32 operation order (gsum = fma(q, x, gsum)
+ * in ascending k, then acc = fma(scale, gsum, acc)), so the output bits equal the
+ * reference op's. Replaces @register("moe_int8_qmv"), kernels/moe_int8.mojo:181-258. */
+UOCR_API int uocr_moe_int8_qmv(float* out, int64_t out_rows, int64_t out_cols,
+                      const float* x, int64_t x_rows, int64_t x_cols,
+                      const int32_t* expert_ids, int64_t ids_len,
+                      const int8_t* w, int64_t w_e, int64_t w_n, int64_t w_k,
+                      const float* scales, int64_t s_e, int64_t s_n, int64_t s_g,
+                      uocr_stream_t stream);
+
+/* int8_dequant_expert: out[n,k] = bf16_rne(f32(w[e,n,k]) * scales[e,n,k/G]), e = clamp(*idx).
+ * Bit-exact. Replaces @register("int8_dequant_expert"), kernels/moe_int8.mojo:261-342. */
+UOCR_API int uocr_int8_dequant_expert(uint16_t* out, int64_t out_n, int64_t out_k,
+                             const int8_t* w, int64_t w_e, int64_t w_n, int64_t w_k,
+                             const float* scales, int64_t s_e, int64_t s_n, int64_t s_g,
+                             const int32_t* expert_idx, int64_t idx_len,
+                             uocr_stream_t stream);
+
+/* dense_bf16_qmv[tile]: out[m,n] = sum_k f32(W[n,k]) * x[m,k] with W held K-blocked as
+ * w[k/16, n, k%16]. Replaces @register("dense_bf16_qmv"), kernels/dense_bf16.mojo:119-158
+ * (wrapper decoder.py:166-184). `tile` >= 1 is accepted for interface parity; a row's bits
+ * do not depend on it. */
+UOCR_API int uocr_dense_bf16_qmv(float* out, int64_t out_rows, int64_t out_cols,
+                        const float* x, int64_t x_rows, int64_t x_cols,
+                        const uint16_t* w, int64_t w_kb, int64_t w_n, int64_t w_blk,
+                        int tile, uocr_stream_t stream);
+
+/* ------------------------------------------------------------------------------------ *
+ * The MoE sublayer (MoE.decode_rows / MoE.__call__, unlimited_ocr_max/decoder.py:641-667).
+ * ------------------------------------------------------------------------------------ */
+
+/* One layer's device-resident weights, in this library's packed layout (see
+ * uocr_moe_pack_gate_up / uocr_moe_pack_shared). Plain pointers, caller-owned. */
+typedef struct uocr_moe_layer {
+    int32_t hidden;     /* H (1280) */
+    int32_t inter;      /* I, moe_intermediate_size (896); multiple of 128 */
+    int32_t n_routed;   /* E (64), <= 64 */
+    int32_t n_shared;   /* S (2): shared_experts_dim = S * I */
+    int32_t top_k;      /* k (6) */
+    int32_t group;      /* int8 group size along K (128) */
+    int32_t int8;       /* 1: routed stacks int8 + fp32 scales; 0: bf16 */
+    int32_t reserved;
+    const uint16_t* router;     /* bf16 [E, H]  (gate.gate_score.weight) */
+    const void* w13;            /* routed gate|up, packed [E, 2I, H], bf16 or int8 */
+    const float* s13;           /* int8 only: [E, 2I, H/G], packed like w13 */
+    const void* w2;             /* routed down [E, H, I], bf16 or int8 (reference layout) */
+    const float* s2;            /* int8 only: [E, H, I/G] */
+    const uint16_t* w13_shared; /* shared gate|up as S experts, packed [S, 2I, H] bf16 */
+    const uint16_t* w2_shared;  /* shared down as S experts [S, H, I] bf16 */
+} uocr_moe_layer;
+
+/* Pack the reference's gate/up stacks [E, I, H] (experts.gate_proj / experts.up_proj,
+ * decoder.py:305-307) into w13 [E, 2I, H]: rows interleaved in blocks of 128 (gate rows
+ * 128b..128b+127, then up rows 128b..128b+127). elem_bytes = 2 (bf16), 1 (int8) or 4 (the
+ * fp32 int8 scales [E, I, H/G], packed with the same row order). */
+UOCR_API int uocr_moe_pack_gate_up(const void* gate, const void* up, int64_t E, int64_t I, int64_t H,
+                          int elem_bytes, void* w13_out, uocr_stream_t stream);
+
+/* Pack the shared experts (shared_experts.{gate,up,down}_proj.weight as [S*I, H], [S*I, H],
+ * [H, S*I] in plain [out, in] order) into w13_shared [S, 2I, H] and w2_shared [S, H, I]:
+ * shared expert s owns intermediate rows [s*I, (s+1)*I). */
+UOCR_API int uocr_moe_pack_shared(const uint16_t* gate, const uint16_t* up, const uint16_t* down,
+                         int64_t S, int64_t I, int64_t H,
+                         uint16_t* w13_out, uint16_t* w2_out, uocr_stream_t stream);
+
+/* Router: MoEGate.__call__ (decoder.py:509-514): fp32 logits x @ router^T (+ optional
+ * per-expert bias, a benchmark input), softmax over all E experts, greedy top-k by
+ * (probability desc, expert index asc), no renormalisation. ids [T, k] int32 and
+ * weights [T, k] fp32 in score order. Bit-exact with the oracle's stated fp32 order. */
+UOCR_API int uocr_moe_route(const float* x, int64_t T, int64_t H, const uint16_t* router, int64_t E,
+                   const float* bias, int64_t top_k, int32_t* ids_out, float* wts_out,
+                   uocr_stream_t stream);
+
+/* Decode step (MoE.decode_rows, decoder.py:641-655): x [B, H] fp32, 1 <= B <= 8 ->
+ * out [B, H] fp32 = routed top-k experts weighted by the router + shared experts.
+ * ids_out / wts_out (nullable) receive the routing. `workspace` must hold
+ * uocr_moe_decode_workspace_bytes(L, B) bytes (256-byte aligned). */
+UOCR_API size_t uocr_moe_decode_workspace_bytes(const uocr_moe_layer* L, int64_t B);
+UOCR_API int uocr_moe_decode(const uocr_moe_layer* L, const float* x, int64_t B, const float* bias,
+                    float* out, int32_t* ids_out, float* wts_out,
+                    void* workspace, size_t workspace_bytes, uocr_stream_t stream);
+
+/* Status word of a workspace after the stream's work finished (synchronises `stream`):
+ * 0 if every device-side bounded wait completed, else a nonzero code. */
+UOCR_API int uocr_moe_device_status(const void* workspace, uocr_stream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* UOCR_MOE_H */

@@ -1,0 +1,132 @@
+"""The C ABI boundary on any host: the library loads, exports every entry point the header
+declares, and the host-side checks refuse bad calls with the reference ops' messages before
+anything reaches a device. No compute call is made here."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+ROOT = Path(__file__).resolve().parents[1]
+HEADER = ROOT / "include" / "uocr_moe.h"
+
+
+def header_functions() -> list[str]:
+    text = re.sub(r"/\*.*?\*/", "", HEADER.read_text(), flags=re.S)
+    return sorted(set(re.findall(r"\b(uocr_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_header_declares_the_reference_ops():
+    names = header_functions()
+    for op in ("uocr_moe_bf16_qmv", "uocr_moe_int8_qmv", "uocr_int8_dequant_expert", "uocr_dense_bf16_qmv",
+               "uocr_moe_route", "uocr_moe_decode"):
+        assert op in names
+
+
+def test_library_exports_every_declared_symbol(uocr):
+    lib = uocr.load()
+    missing = [n for n in header_functions() if not hasattr(lib, n)]
+    assert not missing, missing
+    from importlib import import_module
+
+    sigs = import_module("unlimited-ocr-max_b200._lib").SIGNATURES
+    assert sorted(sigs) == header_functions()
+    assert lib.uocr_abi_version() == 1
+
+
+def test_only_the_c_abi_is_exported(uocr):
+    """-fvisibility=hidden: the kernels and helpers are not part of the ABI."""
+    import subprocess
+
+    out = subprocess.run(["nm", "-D", "--defined-only", str(uocr.LIB_PATH)], capture_output=True, text=True).stdout
+    ours = sorted({line.split()[-1] for line in out.splitlines() if " T " in line and "uocr" in line})
+    assert ours == header_functions()
+
+
+def _null_call(lib, name, *args):
+    fn = getattr(lib, name)
+    return fn(*args), lib.uocr_last_error().decode()
+
+
+@pytest.mark.parametrize(
+    "dims,message",
+    [
+        ((6, 8, 5, 32, 6, 5, 8, 32), "moe_bf16_qmv: x and output disagree on k"),
+        ((6, 8, 6, 32, 5, 5, 8, 32), "moe_bf16_qmv: expert_ids and output disagree on k"),
+        ((6, 8, 6, 32, 6, 5, 9, 32), "moe_bf16_qmv: w and output disagree on N"),
+        ((6, 8, 6, 24, 6, 5, 8, 32), "moe_bf16_qmv: w and x disagree on K"),
+        ((6, 8, 6, 32, 6, 0, 8, 32), "moe_bf16_qmv: the expert stack is empty"),
+    ],
+)
+def test_bf16_qmv_shape_errors(uocr, dims, message):
+    """kernels/moe_bf16.mojo:276-285, checked before any launch (null device pointers are fine)."""
+    out_r, out_c, x_r, x_c, ids_l, w_e, w_n, w_k = dims
+    rc, err = _null_call(uocr.load(), "uocr_moe_bf16_qmv", None, out_r, out_c, None, x_r, x_c, None, ids_l, None,
+                         w_e, w_n, w_k, None)
+    assert rc == 1 and err == message
+
+
+def test_int8_qmv_group_miscount(uocr):
+    rc, err = _null_call(uocr.load(), "uocr_moe_int8_qmv", None, 2, 4, None, 2, 32, None, 2, None, 3, 4, 32, None,
+                         3, 4, 5, None)
+    assert rc == 1 and err == "moe_int8_qmv: K must be a multiple of the group count"
+
+
+def test_dequant_checks(uocr):
+    lib = uocr.load()
+    rc, err = _null_call(lib, "uocr_int8_dequant_expert", None, 4, 32, None, 3, 4, 32, None, 3, 4, 5, None, 1, None)
+    assert rc == 1 and err == "int8_dequant_expert: K must be a multiple of the group count"
+    rc, err = _null_call(lib, "uocr_int8_dequant_expert", None, 4, 32, None, 3, 4, 32, None, 3, 4, 4, None, 2, None)
+    assert rc == 1 and err == "int8_dequant_expert: `expert_idx` must be a single int32"
+
+
+def test_dense_checks(uocr):
+    lib = uocr.load()
+    rc, err = _null_call(lib, "uocr_dense_bf16_qmv", None, 2, 8, None, 2, 32, None, 2, 8, 8, 1, None)
+    assert rc == 1 and err == "dense_bf16_qmv: w is not K-blocked by KBLOCK"
+    rc, err = _null_call(lib, "uocr_dense_bf16_qmv", None, 2, 8, None, 2, 48, None, 2, 8, 16, 1, None)
+    assert rc == 1 and err == "dense_bf16_qmv: w and x disagree on K"
+
+
+def test_zero_rows_launch_nothing(uocr):
+    """k = 0 returns OK without touching the device (a warm-up launch can have no rows)."""
+    rc, _ = _null_call(uocr.load(), "uocr_moe_bf16_qmv", None, 0, 8, None, 0, 32, None, 0, None, 5, 8, 32, None)
+    assert rc == 0
+
+
+def test_decode_rejects_bad_layers(uocr):
+    lib = uocr.load()
+    L = uocr._lib.UocrMoeLayer()
+    L.hidden, L.inter, L.n_routed, L.n_shared, L.top_k, L.group = 1280, 896, 64, 2, 6, 128
+    rc = lib.uocr_moe_decode(ctypes.byref(L), None, 1, None, None, None, None, None, 0, None)
+    assert rc == 1 and "null weight pointer" in lib.uocr_last_error().decode()
+    L.inter = 900
+    rc = lib.uocr_moe_decode(ctypes.byref(L), None, 1, None, None, None, None, None, 0, None)
+    assert rc == 1 and "multiple of 128" in lib.uocr_last_error().decode()
+    assert lib.uocr_moe_decode_workspace_bytes(ctypes.byref(L), 8) > 0
+
+
+def test_ops_refuse_cpu_tensors(uocr):
+    """No CPU fallback: host tensors are an error, not a slow path."""
+    x = torch.zeros(2, 32)
+    ids = torch.zeros(2, dtype=torch.int32)
+    w = torch.zeros(3, 4, 32, dtype=torch.bfloat16)
+    with pytest.raises(ValueError, match="CUDA tensor"):
+        uocr.ops.moe_bf16_qmv(x, ids, w)
+    with pytest.raises(ValueError, match="CUDA device only"):
+        uocr.UocrMoE(uocr.MoEConfig(), device="cpu")
+
+
+def test_config_validation(uocr):
+    C = uocr.MoEConfig
+    with pytest.raises(uocr.ConfigError, match="renormalisation"):
+        C(norm_topk_prob=True)
+    with pytest.raises(uocr.ConfigError, match="scoring_func"):
+        C(scoring_func="sigmoid")
+    with pytest.raises(uocr.ConfigError, match="group size"):
+        C(hidden_size=1216, int8_experts=True)
+    assert C().shared_experts_dim == 1792

@@ -1,0 +1,15 @@
+"""B200-native (sm_100a) DeepSeek-V2 MoE block of the Unlimited-OCR decoder.
+
+Import with ``importlib.import_module("unlimited-ocr-max_b200")`` (the directory name is
+not a Python identifier). Public surface:
+
+* ``MoEConfig``, ``UocrMoE`` -- the reference's ``MoE`` module surface (decoder.py:517-667);
+* ``ops`` -- the reference's custom ops ``moe_bf16_qmv``, ``moe_int8_qmv``,
+  ``int8_dequant_expert``, ``dense_bf16_qmv`` and the gate ``route``;
+* ``weights`` -- checkpoint-name stacking and int8 detection (weight_adapters.py);
+* ``build`` -- compiles ``libuocr_moe.so`` in-tree.
+"""
+
+from . import ops  # noqa: F401
+from ._lib import LIB_PATH, load  # noqa: F401
+from .moe import ConfigError, MoEConfig, UocrMoE  # noqa: F401

@@ -1,0 +1,99 @@
+"""ctypes binding of ``libuocr_moe.so`` (the C ABI declared in ``include/uocr_moe.h``).
+
+There is no fallback: if the library is missing and cannot be built, importing the ops
+fails loudly.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import threading
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libuocr_moe.so"
+
+UOCR_OK, UOCR_EINVAL, UOCR_ECUDA, UOCR_EDEVICE, UOCR_EUNSUPPORTED = 0, 1, 2, 3, 4
+
+P = ctypes.c_void_p
+I32 = ctypes.c_int
+I64 = ctypes.c_int64
+SZ = ctypes.c_size_t
+
+
+class UocrMoeLayer(ctypes.Structure):
+    """Mirror of ``struct uocr_moe_layer`` (include/uocr_moe.h)."""
+
+    _fields_ = [
+        ("hidden", ctypes.c_int32),
+        ("inter", ctypes.c_int32),
+        ("n_routed", ctypes.c_int32),
+        ("n_shared", ctypes.c_int32),
+        ("top_k", ctypes.c_int32),
+        ("group", ctypes.c_int32),
+        ("int8", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("router", P),
+        ("w13", P),
+        ("s13", P),
+        ("w2", P),
+        ("s2", P),
+        ("w13_shared", P),
+        ("w2_shared", P),
+    ]
+
+
+#: name -> (restype, argtypes) for every exported entry point
+SIGNATURES: dict[str, tuple] = {
+    "uocr_last_error": (ctypes.c_char_p, []),
+    "uocr_abi_version": (I32, []),
+    "uocr_moe_bf16_qmv": (I32, [P, I64, I64, P, I64, I64, P, I64, P, I64, I64, I64, P]),
+    "uocr_moe_int8_qmv": (I32, [P, I64, I64, P, I64, I64, P, I64, P, I64, I64, I64, P, I64, I64, I64, P]),
+    "uocr_int8_dequant_expert": (I32, [P, I64, I64, P, I64, I64, I64, P, I64, I64, I64, P, I64, P]),
+    "uocr_dense_bf16_qmv": (I32, [P, I64, I64, P, I64, I64, P, I64, I64, I64, I32, P]),
+    "uocr_moe_pack_gate_up": (I32, [P, P, I64, I64, I64, I32, P, P]),
+    "uocr_moe_pack_shared": (I32, [P, P, P, I64, I64, I64, P, P, P]),
+    "uocr_moe_route": (I32, [P, I64, I64, P, I64, P, I64, P, P, P]),
+    "uocr_moe_decode_workspace_bytes": (SZ, [ctypes.POINTER(UocrMoeLayer), I64]),
+    "uocr_moe_decode": (I32, [ctypes.POINTER(UocrMoeLayer), P, I64, P, P, P, P, P, SZ, P]),
+    "uocr_moe_device_status": (I32, [P, P]),
+}
+
+_lock = threading.Lock()
+_lib: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """Load (building first if absent) ``libuocr_moe.so`` and declare its signatures."""
+    global _lib
+    with _lock:
+        if _lib is None:
+            if not LIB_PATH.exists():
+                from . import build as _build
+
+                _build.build()
+            lib = ctypes.CDLL(str(LIB_PATH))
+            for name, (res, args) in SIGNATURES.items():
+                fn = getattr(lib, name)
+                fn.restype = res
+                fn.argtypes = args
+            _lib = lib
+    return _lib
+
+
+class UocrError(RuntimeError):
+    """A libuocr_moe call failed (status code + message)."""
+
+    def __init__(self, code: int, message: str):
+        super().__init__(message)
+        self.code = code
+
+
+def check(code: int) -> None:
+    """Raise the reference's error kinds: shape errors as ValueError with the op's message."""
+    if code == UOCR_OK:
+        return
+    msg = load().uocr_last_error().decode()
+    if code == UOCR_EINVAL:
+        raise ValueError(msg)
+    raise UocrError(code, msg)

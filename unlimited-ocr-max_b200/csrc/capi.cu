@@ -1,0 +1,310 @@
+// The C ABI of libuocr_moe.so (include/uocr_moe.h): host-side argument checks with the
+// reference ops' error messages, then kernel launches on the caller's stream.
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+#include <string>
+#include <unordered_map>
+
+#include "../../include/uocr_moe.h"
+#include "common.cuh"
+#include "kernels.h"
+
+namespace {
+
+thread_local std::string g_last_error;
+
+int fail(int code, const char* fmt, ...) {
+    char buf[512];
+    va_list ap;
+    va_start(ap, fmt);
+    vsnprintf(buf, sizeof buf, fmt, ap);
+    va_end(ap);
+    g_last_error = buf;
+    return code;
+}
+
+int ok() {
+    g_last_error.clear();
+    return UOCR_OK;
+}
+
+int cuda_status(cudaError_t err, const char* what) {
+    if (err != cudaSuccess) return fail(UOCR_ECUDA, "%s: %s", what, cudaGetErrorString(err));
+    return ok();
+}
+
+cudaStream_t S(uocr_stream_t s) { return reinterpret_cast<cudaStream_t>(s); }
+
+size_t align256(size_t n) { return (n + 255) & ~size_t(255); }
+
+bool a16(const void* p) { return uocr::aligned16(p); }
+
+}  // namespace
+
+namespace uocr {
+
+cudaError_t ensure_smem_optin(const void* kernel, size_t bytes) {
+    static std::mutex mu;
+    static std::unordered_map<const void*, size_t> granted;  // per device would matter only across GPUs
+    std::lock_guard<std::mutex> lock(mu);
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    const void* key = reinterpret_cast<const char*>(kernel) + dev;  // distinct per (kernel, device)
+    auto it = granted.find(key);
+    if (it != granted.end() && it->second >= bytes) return cudaSuccess;
+    if (bytes <= 48 * 1024 && it == granted.end()) {
+        granted[key] = 48 * 1024;
+        if (bytes <= 48 * 1024) return cudaSuccess;
+    }
+    err = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)bytes);
+    if (err == cudaSuccess) granted[key] = bytes;
+    return err;
+}
+
+}  // namespace uocr
+
+extern "C" {
+
+const char* uocr_last_error(void) { return g_last_error.c_str(); }
+
+int uocr_abi_version(void) { return 1; }
+
+// ---------------------------------------------------------------------------------------
+// reference op shims
+// ---------------------------------------------------------------------------------------
+
+int uocr_moe_bf16_qmv(float* out, int64_t out_rows, int64_t out_cols, const float* x, int64_t x_rows, int64_t x_cols,
+                      const int32_t* expert_ids, int64_t ids_len, const uint16_t* w, int64_t w_e, int64_t w_n,
+                      int64_t w_k, uocr_stream_t stream) {
+    // kernels/moe_bf16.mojo:276-285
+    if (x_rows != out_rows) return fail(UOCR_EINVAL, "moe_bf16_qmv: x and output disagree on k");
+    if (ids_len != out_rows) return fail(UOCR_EINVAL, "moe_bf16_qmv: expert_ids and output disagree on k");
+    if (w_n != out_cols) return fail(UOCR_EINVAL, "moe_bf16_qmv: w and output disagree on N");
+    if (w_k != x_cols) return fail(UOCR_EINVAL, "moe_bf16_qmv: w and x disagree on K");
+    if (w_e < 1) return fail(UOCR_EINVAL, "moe_bf16_qmv: the expert stack is empty");
+    if (out_rows == 0 || out_cols == 0) return ok();
+    if (w_k > INT32_MAX || w_n > INT32_MAX || w_e > INT32_MAX)
+        return fail(UOCR_EUNSUPPORTED, "moe_bf16_qmv: dims beyond int32");
+    const bool vec = (w_k % 8 == 0) && a16(w) && a16(x);
+    for (int64_t r0 = 0; r0 < out_rows; r0 += 65535) {
+        const int rows = (int)std::min<int64_t>(65535, out_rows - r0);
+        uocr::launch_bf16_qmv(out + r0 * out_cols, x + r0 * x_cols, expert_ids + r0, w, rows, (int)w_e, (int)w_n,
+                              (int)w_k, vec, S(stream));
+    }
+    return cuda_status(cudaGetLastError(), "moe_bf16_qmv: launch");
+}
+
+int uocr_moe_int8_qmv(float* out, int64_t out_rows, int64_t out_cols, const float* x, int64_t x_rows, int64_t x_cols,
+                      const int32_t* expert_ids, int64_t ids_len, const int8_t* w, int64_t w_e, int64_t w_n,
+                      int64_t w_k, const float* scales, int64_t s_e, int64_t s_n, int64_t s_g,
+                      uocr_stream_t stream) {
+    // kernels/moe_int8.mojo:196-212
+    if (x_rows != out_rows) return fail(UOCR_EINVAL, "moe_int8_qmv: x and output disagree on k");
+    if (ids_len != out_rows) return fail(UOCR_EINVAL, "moe_int8_qmv: expert_ids and output disagree on k");
+    if (w_n != out_cols) return fail(UOCR_EINVAL, "moe_int8_qmv: w and output disagree on N");
+    if (w_k != x_cols) return fail(UOCR_EINVAL, "moe_int8_qmv: w and x disagree on K");
+    if (w_e < 1) return fail(UOCR_EINVAL, "moe_int8_qmv: the expert stack is empty");
+    if (s_e != w_e) return fail(UOCR_EINVAL, "moe_int8_qmv: scales and w disagree on E");
+    if (s_n != w_n) return fail(UOCR_EINVAL, "moe_int8_qmv: scales and w disagree on N");
+    if (s_g < 1 || w_k % s_g != 0) return fail(UOCR_EINVAL, "moe_int8_qmv: K must be a multiple of the group count");
+    if (out_rows == 0 || out_cols == 0) return ok();
+    if (w_k > INT32_MAX || w_n > INT32_MAX || w_e > INT32_MAX || out_rows > INT32_MAX)
+        return fail(UOCR_EUNSUPPORTED, "moe_int8_qmv: dims beyond int32");
+    const int64_t gsize = w_k / s_g;
+    const bool vec = (gsize % 16 == 0) && (w_k % 16 == 0) && a16(w);
+    uocr::launch_int8_qmv(out, x, expert_ids, w, scales, (int)out_rows, (int)w_e, (int)w_n, (int)w_k, (int)s_g, vec,
+                          S(stream));
+    return cuda_status(cudaGetLastError(), "moe_int8_qmv: launch");
+}
+
+int uocr_int8_dequant_expert(uint16_t* out, int64_t out_n, int64_t out_k, const int8_t* w, int64_t w_e, int64_t w_n,
+                             int64_t w_k, const float* scales, int64_t s_e, int64_t s_n, int64_t s_g,
+                             const int32_t* expert_idx, int64_t idx_len, uocr_stream_t stream) {
+    // kernels/moe_int8.mojo:274-297
+    if (w_n != out_n) return fail(UOCR_EINVAL, "int8_dequant_expert: w and output disagree on N");
+    if (w_k != out_k) return fail(UOCR_EINVAL, "int8_dequant_expert: w and output disagree on K");
+    if (w_e < 1) return fail(UOCR_EINVAL, "int8_dequant_expert: the expert stack is empty");
+    if (s_e != w_e) return fail(UOCR_EINVAL, "int8_dequant_expert: scales and w disagree on E");
+    if (s_n != w_n) return fail(UOCR_EINVAL, "int8_dequant_expert: scales and w disagree on N");
+    if (idx_len != 1) return fail(UOCR_EINVAL, "int8_dequant_expert: `expert_idx` must be a single int32");
+    if (s_g < 1 || w_k % s_g != 0)
+        return fail(UOCR_EINVAL, "int8_dequant_expert: K must be a multiple of the group count");
+    if (out_n == 0 || out_k == 0) return ok();
+    if (w_k > INT32_MAX || w_n > INT32_MAX || w_e > INT32_MAX)
+        return fail(UOCR_EUNSUPPORTED, "int8_dequant_expert: dims beyond int32");
+    uocr::launch_int8_dequant(out, w, scales, expert_idx, (int)w_e, (int)w_n, (int)w_k, (int)s_g, S(stream));
+    return cuda_status(cudaGetLastError(), "int8_dequant_expert: launch");
+}
+
+int uocr_dense_bf16_qmv(float* out, int64_t out_rows, int64_t out_cols, const float* x, int64_t x_rows,
+                        int64_t x_cols, const uint16_t* w, int64_t w_kb, int64_t w_n, int64_t w_blk, int tile,
+                        uocr_stream_t stream) {
+    // kernels/dense_bf16.mojo:130-145, decoder.py:174-178
+    if (tile < 1) return fail(UOCR_EINVAL, "dense_bf16_qmv: tile must be >= 1");
+    if (out_rows != x_rows) return fail(UOCR_EINVAL, "dense_bf16_qmv: x and output disagree on M");
+    if (w_n != out_cols) return fail(UOCR_EINVAL, "dense_bf16_qmv: w and output disagree on N");
+    if (w_blk != 16) return fail(UOCR_EINVAL, "dense_bf16_qmv: w is not K-blocked by KBLOCK");
+    if (w_kb * 16 != x_cols) return fail(UOCR_EINVAL, "dense_bf16_qmv: w and x disagree on K");
+    if (out_rows == 0 || out_cols == 0) return ok();
+    if (x_cols > INT32_MAX || w_n > INT32_MAX) return fail(UOCR_EUNSUPPORTED, "dense_bf16_qmv: dims beyond int32");
+    const bool vec = a16(w) && a16(x);
+    for (int64_t r0 = 0; r0 < out_rows; r0 += 65535) {
+        const int rows = (int)std::min<int64_t>(65535, out_rows - r0);
+        uocr::launch_dense_bf16_qmv(out + r0 * out_cols, x + r0 * x_cols, w, rows, (int)w_n, (int)x_cols, vec,
+                                    S(stream));
+    }
+    return cuda_status(cudaGetLastError(), "dense_bf16_qmv: launch");
+}
+
+// ---------------------------------------------------------------------------------------
+// packing
+// ---------------------------------------------------------------------------------------
+
+int uocr_moe_pack_gate_up(const void* gate, const void* up, int64_t E, int64_t I, int64_t H, int elem_bytes,
+                          void* w13_out, uocr_stream_t stream) {
+    if (E < 1 || I < 1 || H < 1) return fail(UOCR_EINVAL, "pack_gate_up: empty stack");
+    if (I % 128) return fail(UOCR_EINVAL, "pack_gate_up: I=%lld is not a multiple of 128", (long long)I);
+    if (elem_bytes != 1 && elem_bytes != 2 && elem_bytes != 4)
+        return fail(UOCR_EINVAL, "pack_gate_up: elem_bytes must be 1, 2 or 4");
+    if ((H * elem_bytes) % 4) return fail(UOCR_EINVAL, "pack_gate_up: a row must be a multiple of 4 bytes");
+    if (!gate || !up || !w13_out) return fail(UOCR_EINVAL, "pack_gate_up: null pointer");
+    if ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) | reinterpret_cast<uintptr_t>(w13_out)) & 3)
+        return fail(UOCR_EINVAL, "pack_gate_up: pointers must be 4-byte aligned");
+    return cuda_status(uocr::launch_pack_gate_up(gate, up, E, I, H, elem_bytes, w13_out, S(stream)),
+                       "pack_gate_up: launch");
+}
+
+int uocr_moe_pack_shared(const uint16_t* gate, const uint16_t* up, const uint16_t* down, int64_t S_, int64_t I,
+                         int64_t H, uint16_t* w13_out, uint16_t* w2_out, uocr_stream_t stream) {
+    if (S_ < 1 || I < 1 || H < 1) return fail(UOCR_EINVAL, "pack_shared: empty");
+    if (I % 128) return fail(UOCR_EINVAL, "pack_shared: I=%lld is not a multiple of 128", (long long)I);
+    if (H % 2) return fail(UOCR_EINVAL, "pack_shared: H must be even");
+    if (!gate || !up || !down || !w13_out || !w2_out) return fail(UOCR_EINVAL, "pack_shared: null pointer");
+    return cuda_status(uocr::launch_pack_shared(gate, up, down, S_, I, H, w13_out, w2_out, S(stream)),
+                       "pack_shared: launch");
+}
+
+// ---------------------------------------------------------------------------------------
+// router
+// ---------------------------------------------------------------------------------------
+
+static int check_router(int64_t T, int64_t H, int64_t E, int64_t top_k, const float* x, const uint16_t* router,
+                        const float* bias, const void* ids, const void* wts) {
+    if (T < 0) return fail(UOCR_EINVAL, "route: negative token count");
+    if (H < 64 || H % 64) return fail(UOCR_EINVAL, "route: hidden=%lld must be a positive multiple of 64", (long long)H);
+    if (E < 1 || E > 64) return fail(UOCR_EUNSUPPORTED, "route: %lld experts; this build routes 1..64", (long long)E);
+    if (top_k < 1 || top_k > E) return fail(UOCR_EINVAL, "route: top_k=%lld outside [1, E]", (long long)top_k);
+    if (T > 0 && (!x || !router || !ids || !wts)) return fail(UOCR_EINVAL, "route: null pointer");
+    if (!a16(x) || !a16(router)) return fail(UOCR_EINVAL, "route: x and router must be 16-byte aligned");
+    (void)bias;
+    return ok();
+}
+
+int uocr_moe_route(const float* x, int64_t T, int64_t H, const uint16_t* router, int64_t E, const float* bias,
+                   int64_t top_k, int32_t* ids_out, float* wts_out, uocr_stream_t stream) {
+    int rc = check_router(T, H, E, top_k, x, router, bias, ids_out, wts_out);
+    if (rc) return rc;
+    if (T == 0) return ok();
+    if (T > INT32_MAX / 8) return fail(UOCR_EUNSUPPORTED, "route: too many tokens");
+    return cuda_status(uocr::launch_route(x, (int)T, (int)H, router, (int)E, bias, (int)top_k, ids_out, wts_out,
+                                          S(stream)),
+                       "route: launch");
+}
+
+// ---------------------------------------------------------------------------------------
+// decode step
+// ---------------------------------------------------------------------------------------
+
+namespace {
+
+struct DecodeLayout {
+    size_t status, ids, wts, h, y, total;
+};
+
+DecodeLayout decode_layout(const uocr_moe_layer* L, int64_t B) {
+    DecodeLayout d{};
+    const size_t pairs = (size_t)(L->top_k + L->n_shared) * (size_t)B;
+    size_t off = 0;
+    d.status = off; off += 256;
+    d.ids = off; off += align256(sizeof(int32_t) * (size_t)B * L->top_k);
+    d.wts = off; off += align256(sizeof(float) * (size_t)B * L->top_k);
+    d.h = off; off += align256(sizeof(float) * pairs * (size_t)L->inter);
+    d.y = off; off += align256(sizeof(float) * pairs * (size_t)L->hidden);
+    d.total = off;
+    return d;
+}
+
+int check_layer(const uocr_moe_layer* L, const char* who) {
+    if (!L) return fail(UOCR_EINVAL, "%s: null layer", who);
+    if (L->hidden < 64 || L->hidden % 64)
+        return fail(UOCR_EINVAL, "%s: hidden=%d must be a positive multiple of 64", who, L->hidden);
+    if (L->inter < 128 || L->inter % 128)
+        return fail(UOCR_EINVAL, "%s: inter=%d must be a positive multiple of 128", who, L->inter);
+    if (L->n_routed < 1 || L->n_routed > 64) return fail(UOCR_EUNSUPPORTED, "%s: n_routed=%d outside 1..64", who, L->n_routed);
+    if (L->n_shared < 0) return fail(UOCR_EINVAL, "%s: n_shared < 0", who);
+    if (L->top_k < 1 || L->top_k > L->n_routed) return fail(UOCR_EINVAL, "%s: top_k=%d outside [1, E]", who, L->top_k);
+    if (L->int8) {
+        if (L->group < 8 || L->group % 8 || L->hidden % L->group || L->inter % L->group)
+            return fail(UOCR_EINVAL, "%s: int8 group size %d must divide hidden and inter (multiple of 8)", who, L->group);
+        if (!L->s13 || !L->s2) return fail(UOCR_EINVAL, "%s: int8 layer without scales", who);
+    }
+    if (!L->router || !L->w13 || !L->w2) return fail(UOCR_EINVAL, "%s: null weight pointer", who);
+    if (L->n_shared > 0 && (!L->w13_shared || !L->w2_shared)) return fail(UOCR_EINVAL, "%s: null shared weights", who);
+    if (!a16(L->router) || !a16(L->w13) || !a16(L->w2) || (L->n_shared && (!a16(L->w13_shared) || !a16(L->w2_shared))))
+        return fail(UOCR_EINVAL, "%s: weights must be 16-byte aligned", who);
+    return ok();
+}
+
+}  // namespace
+
+size_t uocr_moe_decode_workspace_bytes(const uocr_moe_layer* L, int64_t B) {
+    if (!L || B < 1) return 0;
+    return decode_layout(L, B).total;
+}
+
+int uocr_moe_decode(const uocr_moe_layer* L, const float* x, int64_t B, const float* bias, float* out,
+                    int32_t* ids_out, float* wts_out, void* workspace, size_t workspace_bytes, uocr_stream_t stream) {
+    int rc = check_layer(L, "moe_decode");
+    if (rc) return rc;
+    if (B < 1 || B > 8) return fail(UOCR_EINVAL, "moe_decode: B=%lld outside 1..8 (use moe_prefill)", (long long)B);
+    if (!x || !out || !workspace) return fail(UOCR_EINVAL, "moe_decode: null pointer");
+    if (!a16(x) || !a16(out)) return fail(UOCR_EINVAL, "moe_decode: x and out must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(workspace) & 255) return fail(UOCR_EINVAL, "moe_decode: workspace must be 256-byte aligned");
+    const DecodeLayout d = decode_layout(L, B);
+    if (workspace_bytes < d.total)
+        return fail(UOCR_EINVAL, "moe_decode: workspace of %zu bytes, need %zu", workspace_bytes, d.total);
+    char* ws = reinterpret_cast<char*>(workspace);
+    cudaStream_t st = S(stream);
+    int32_t* ids = ids_out ? ids_out : reinterpret_cast<int32_t*>(ws + d.ids);
+    float* wts = wts_out ? wts_out : reinterpret_cast<float*>(ws + d.wts);
+    cudaError_t err = cudaMemsetAsync(ws + d.status, 0, sizeof(uint32_t), st);
+    if (err != cudaSuccess) return cuda_status(err, "moe_decode: status reset");
+    err = uocr::launch_route(x, (int)B, L->hidden, L->router, L->n_routed, bias, L->top_k, ids, wts, st);
+    if (err != cudaSuccess) return cuda_status(err, "moe_decode: route");
+    uocr::DecodeArgs a{};
+    a.B = (int)B; a.H = L->hidden; a.I = L->inter; a.E = L->n_routed; a.S = L->n_shared; a.topk = L->top_k;
+    a.G = L->int8 ? L->group : 128; a.int8 = L->int8;
+    a.x = x; a.ids = ids; a.wts = wts;
+    a.w13 = L->w13; a.s13 = L->s13; a.w2 = L->w2; a.s2 = L->s2;
+    a.w13_shared = L->w13_shared; a.w2_shared = L->w2_shared;
+    a.h = reinterpret_cast<float*>(ws + d.h);
+    a.y = reinterpret_cast<float*>(ws + d.y);
+    a.out = out;
+    a.status = reinterpret_cast<uint32_t*>(ws + d.status);
+    return cuda_status(uocr::launch_decode_experts(a, st), "moe_decode: experts");
+}
+
+int uocr_moe_device_status(const void* workspace, uocr_stream_t stream) {
+    if (!workspace) return fail(UOCR_EINVAL, "device_status: null workspace");
+    cudaError_t err = cudaStreamSynchronize(S(stream));
+    if (err != cudaSuccess) return cuda_status(err, "device_status: synchronize");
+    uint32_t status = 0;
+    err = cudaMemcpy(&status, workspace, sizeof status, cudaMemcpyDeviceToHost);
+    if (err != cudaSuccess) return cuda_status(err, "device_status: read");
+    if (status) return fail(UOCR_EDEVICE, "device_status: a device-side wait gave up (code %u)", status);
+    return ok();
+}
+
+}  // extern "C"

@@ -1,0 +1,49 @@
+// Internal launch interface between capi.cu (argument checks, the C ABI) and the kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stddef.h>
+#include <stdint.h>
+
+namespace uocr {
+
+// shims.cu
+void launch_bf16_qmv(float* out, const float* x, const int32_t* ids, const uint16_t* w, int rows, int E, int N,
+                     int K, bool vec, cudaStream_t st);
+void launch_int8_qmv(float* out, const float* x, const int32_t* ids, const int8_t* w, const float* scales, int rows,
+                     int E, int N, int K, int groups, bool vec, cudaStream_t st);
+void launch_int8_dequant(uint16_t* out, const int8_t* w, const float* scales, const int32_t* idx, int E, int N,
+                         int K, int groups, cudaStream_t st);
+void launch_dense_bf16_qmv(float* out, const float* x, const uint16_t* w, int M, int N, int K, bool vec,
+                           cudaStream_t st);
+
+// route.cu
+cudaError_t launch_route(const float* x, int T, int H, const uint16_t* wg, int E, const float* bias, int topk,
+                         int32_t* ids, float* wts, cudaStream_t st);
+
+// decode.cu
+struct DecodeArgs {
+    int B, H, I, E, S, topk, G, int8;
+    const float* x;
+    const int32_t* ids;
+    const float* wts;
+    const void* w13;
+    const float* s13;
+    const void* w2;
+    const float* s2;
+    const uint16_t* w13_shared;
+    const uint16_t* w2_shared;
+    float* h;     // [(k+S)*B, I]
+    float* y;     // [(k+S)*B, H]
+    float* out;   // [B, H]
+    uint32_t* status;
+};
+cudaError_t launch_decode_experts(const DecodeArgs& a, cudaStream_t st);
+
+// pack.cu
+cudaError_t launch_pack_gate_up(const void* gate, const void* up, long E, long I, long H, int esz, void* out,
+                                cudaStream_t st);
+cudaError_t launch_pack_shared(const uint16_t* gate, const uint16_t* up, const uint16_t* down, long S, long I, long H,
+                               uint16_t* w13, uint16_t* w2, cudaStream_t st);
+
+}  // namespace uocr

@@ -1,0 +1,129 @@
+"""torch-tensor wrappers over the C ABI, one per reference op.
+
+Each wrapper takes the same tensors as the reference's custom op (kernels/*.mojo
+``@register``) or graph function, checks device and dtype, and passes raw device pointers
+plus the current CUDA stream to ``libuocr_moe.so``. Shape errors come back from the library
+with the reference op's message and are raised as ``ValueError``. Nothing here computes on
+the host; a non-CUDA tensor is an error, never a CPU fallback.
+"""
+
+from __future__ import annotations
+
+import torch
+
+from ._lib import check, load
+
+KBLOCK = 16  # decoder.py:72
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _need_cuda(op: str, *tensors: torch.Tensor) -> None:
+    for t in tensors:
+        if not isinstance(t, torch.Tensor) or not t.is_cuda:
+            raise ValueError(f"{op}: every tensor must be a CUDA tensor (no CPU path)")
+    dev = tensors[0].device
+    for t in tensors[1:]:
+        if t.device != dev:
+            raise ValueError(f"{op}: tensors on different devices ({dev} vs {t.device})")
+
+
+def _need(op: str, t: torch.Tensor, name: str, dtype: torch.dtype, rank: int) -> torch.Tensor:
+    if t.dtype != dtype:
+        raise TypeError(f"{op}: {name} must be {dtype}, got {t.dtype}")
+    if t.dim() != rank:
+        raise ValueError(f"{op}: {name} must be rank {rank}, got shape {tuple(t.shape)}")
+    return t if t.is_contiguous() else t.contiguous()
+
+
+def moe_bf16_qmv(x: torch.Tensor, expert_ids: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """``moe_bf16_qmv(x f32[k,K], ids i32[k], w bf16[E,N,K]) -> f32[k,N]`` (kernels/moe_bf16.mojo:264)."""
+    op = "moe_bf16_qmv"
+    _need_cuda(op, x, expert_ids, w)
+    x = _need(op, x, "x", torch.float32, 2)
+    expert_ids = _need(op, expert_ids, "expert_ids", torch.int32, 1)
+    w = _need(op, w, "w", torch.bfloat16, 3)
+    if out is None:
+        out = torch.empty((x.shape[0], w.shape[1]), dtype=torch.float32, device=x.device)
+    out = _need(op, out, "output", torch.float32, 2)
+    check(load().uocr_moe_bf16_qmv(
+        out.data_ptr(), out.shape[0], out.shape[1], x.data_ptr(), x.shape[0], x.shape[1],
+        expert_ids.data_ptr(), expert_ids.shape[0], w.data_ptr(), *w.shape, _stream(x)))
+    return out
+
+
+def moe_int8_qmv(x: torch.Tensor, expert_ids: torch.Tensor, w: torch.Tensor, scales: torch.Tensor,
+                 out: torch.Tensor | None = None) -> torch.Tensor:
+    """``moe_int8_qmv(x, ids, w i8[E,N,K], scales f32[E,N,K/G]) -> f32[k,N]`` (kernels/moe_int8.mojo:181)."""
+    op = "moe_int8_qmv"
+    _need_cuda(op, x, expert_ids, w, scales)
+    x = _need(op, x, "x", torch.float32, 2)
+    expert_ids = _need(op, expert_ids, "expert_ids", torch.int32, 1)
+    w = _need(op, w, "w", torch.int8, 3)
+    scales = _need(op, scales, "scales", torch.float32, 3)
+    if out is None:
+        out = torch.empty((x.shape[0], w.shape[1]), dtype=torch.float32, device=x.device)
+    out = _need(op, out, "output", torch.float32, 2)
+    check(load().uocr_moe_int8_qmv(
+        out.data_ptr(), out.shape[0], out.shape[1], x.data_ptr(), x.shape[0], x.shape[1],
+        expert_ids.data_ptr(), expert_ids.shape[0], w.data_ptr(), *w.shape, scales.data_ptr(), *scales.shape,
+        _stream(x)))
+    return out
+
+
+def int8_dequant_expert(w: torch.Tensor, scales: torch.Tensor, expert_idx: torch.Tensor,
+                        out: torch.Tensor | None = None) -> torch.Tensor:
+    """``int8_dequant_expert(w, scales, idx i32[1]) -> bf16[N,K]`` (kernels/moe_int8.mojo:261)."""
+    op = "int8_dequant_expert"
+    _need_cuda(op, w, scales, expert_idx)
+    w = _need(op, w, "w", torch.int8, 3)
+    scales = _need(op, scales, "scales", torch.float32, 3)
+    expert_idx = _need(op, expert_idx, "expert_idx", torch.int32, 1)
+    if out is None:
+        out = torch.empty((w.shape[1], w.shape[2]), dtype=torch.bfloat16, device=w.device)
+    out = _need(op, out, "output", torch.bfloat16, 2)
+    check(load().uocr_int8_dequant_expert(
+        out.data_ptr(), out.shape[0], out.shape[1], w.data_ptr(), *w.shape, scales.data_ptr(), *scales.shape,
+        expert_idx.data_ptr(), expert_idx.shape[0], _stream(w)))
+    return out
+
+
+def dense_bf16_qmv(x: torch.Tensor, w: torch.Tensor, *, tile: int | None = None,
+                   out: torch.Tensor | None = None) -> torch.Tensor:
+    """``dense_bf16_qmv[tile](x f32[M,K], w bf16[K/16,N,16]) -> f32[M,N]`` (kernels/dense_bf16.mojo:119)."""
+    op = "dense_bf16_qmv"
+    _need_cuda(op, x, w)
+    x = _need(op, x, "x", torch.float32, 2)
+    w = _need(op, w, "w", torch.bfloat16, 3)
+    if out is None:
+        out = torch.empty((x.shape[0], w.shape[1]), dtype=torch.float32, device=x.device)
+    out = _need(op, out, "output", torch.float32, 2)
+    check(load().uocr_dense_bf16_qmv(
+        out.data_ptr(), out.shape[0], out.shape[1], x.data_ptr(), x.shape[0], x.shape[1],
+        w.data_ptr(), *w.shape, 1 if tile is None else int(tile), _stream(x)))
+    return out
+
+
+def route(x: torch.Tensor, router: torch.Tensor, bias: torch.Tensor | None = None, top_k: int = 6):
+    """MoEGate.__call__ (decoder.py:509-514): ``(ids i32[T,k], weights f32[T,k])`` in score order.
+
+    ``router`` is the bf16 ``gate.gate_score.weight [E, H]``; ``bias`` an optional fp32 ``[E]``
+    added to the logits before the softmax (a benchmark input; the reference has none).
+    """
+    op = "route"
+    _need_cuda(op, x, router, *([] if bias is None else [bias]))
+    x = _need(op, x, "x", torch.float32, 2)
+    router = _need(op, router, "router", torch.bfloat16, 2)
+    if bias is not None:
+        bias = _need(op, bias, "bias", torch.float32, 1)
+    T, H = x.shape
+    E = router.shape[0]
+    if router.shape[1] != H:
+        raise ValueError(f"route: router and x disagree on the hidden size ({router.shape[1]} vs {H})")
+    ids = torch.empty((T, top_k), dtype=torch.int32, device=x.device)
+    wts = torch.empty((T, top_k), dtype=torch.float32, device=x.device)
+    check(load().uocr_moe_route(x.data_ptr(), T, H, router.data_ptr(), E, 0 if bias is None else bias.data_ptr(),
+                                top_k, ids.data_ptr(), wts.data_ptr(), _stream(x)))
+    return ids, wts
