@@ -144,6 +144,18 @@ UOCR_API int uocr_moe_decode(const uocr_moe_layer* L, const float* x, int64_t B,
                     float* out, int32_t* ids_out, float* wts_out,
                     void* workspace, size_t workspace_bytes, uocr_stream_t stream);
 
+/* Decode step without a caller workspace. No counterpart in the reference: added for callers
+ * that cannot allocate device memory (a plugin host that passes an operator only its inputs
+ * and outputs, or a runtime whose device memory is reserved up front). Same computation as
+ * uocr_moe_decode; its scratch is a fixed array inside the library, of
+ * uocr_moe_decode_noalloc_max_bytes() bytes (1 MiB) on every GPU that loads the library,
+ * held until exit. Layers and batches needing more scratch are refused with UOCR_EINVAL.
+ * Calls on one device share that array: calls that overlap on the GPU race. The first call
+ * on a device looks up the array's address and should come before any stream capture. */
+UOCR_API size_t uocr_moe_decode_noalloc_max_bytes(void);
+UOCR_API int uocr_moe_decode_noalloc(const uocr_moe_layer* L, const float* x, int64_t B,
+                                     const float* bias, float* out, uocr_stream_t stream);
+
 /* Status word of a workspace after the stream's work finished (synchronises `stream`):
  * 0 if every device-side bounded wait completed, else a nonzero code. */
 UOCR_API int uocr_moe_device_status(const void* workspace, uocr_stream_t stream);

@@ -44,6 +44,11 @@ bool a16(const void* p) { return uocr::aligned16(p); }
 
 namespace uocr {
 
+int set_error(int code, const char* msg) {
+    g_last_error = msg;
+    return code;
+}
+
 cudaError_t ensure_smem_optin(const void* kernel, size_t bytes) {
     static std::mutex mu;
     static std::unordered_map<const void*, size_t> granted;  // per device would matter only across GPUs
