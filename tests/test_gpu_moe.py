@@ -114,3 +114,19 @@ def test_full_size_decode_layer(uocr, oracle, int8):
         assert oracle.rel_err(got, ref) <= 1e-4, B
         # the north-star bar against the fp32 reference path
         assert np.max(np.abs(got - ref)) <= 2e-2 and oracle.rel_l2(got, ref) <= 1e-2
+
+
+def test_decode_status_clean_and_repeatable(uocr, oracle):
+    """The self-resetting control block: many calls in a row give identical bits and leave
+    the device status word clear (no bounded wait expired)."""
+    import ctypes
+
+    orig, _ = ri.moe_weights(ri.SMALL_MOE, 2)
+    moe = uocr.UocrMoE(small_cfg(uocr, False)).load_state_dict(orig)
+    x = torch.from_numpy(np.random.default_rng(5).standard_normal((6, 256)).astype(np.float32)).to(DEV)
+    first = moe.decode_rows(x).clone()
+    for _ in range(20):
+        assert torch.equal(moe.decode_rows(x), first)
+    lib = uocr.load()
+    rc = lib.uocr_moe_device_status(moe.workspace(6).data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, lib.uocr_last_error().decode()

@@ -225,14 +225,16 @@ int uocr_moe_route(const float* x, int64_t T, int64_t H, const uint16_t* router,
 namespace {
 
 struct DecodeLayout {
-    size_t status, ids, wts, h, y, total;
+    size_t ctl, logits, table, ids, wts, h, y, total;
 };
 
 DecodeLayout decode_layout(const uocr_moe_layer* L, int64_t B) {
     DecodeLayout d{};
     const size_t pairs = (size_t)(L->top_k + L->n_shared) * (size_t)B;
     size_t off = 0;
-    d.status = off; off += 256;
+    d.ctl = off; off += align256(sizeof(uocr::DecodeCtl));
+    d.logits = off; off += align256(sizeof(float) * 8 * 64);
+    d.table = off; off += align256(sizeof(uocr::RouteTable));
     d.ids = off; off += align256(sizeof(int32_t) * (size_t)B * L->top_k);
     d.wts = off; off += align256(sizeof(float) * (size_t)B * L->top_k);
     d.h = off; off += align256(sizeof(float) * pairs * (size_t)L->inter);
@@ -274,31 +276,32 @@ int uocr_moe_decode(const uocr_moe_layer* L, const float* x, int64_t B, const fl
     int rc = check_layer(L, "moe_decode");
     if (rc) return rc;
     if (B < 1 || B > 8) return fail(UOCR_EINVAL, "moe_decode: B=%lld outside 1..8 (use moe_prefill)", (long long)B);
+    if (L->n_shared > 64 || L->n_shared + std::min<int64_t>(L->n_routed, L->top_k * B) > uocr::kDecodeMaxSlots)
+        return fail(UOCR_EUNSUPPORTED, "moe_decode: too many expert slots");
+    if (L->hidden / 16 > uocr::kDecodeMaxJBlocks) return fail(UOCR_EUNSUPPORTED, "moe_decode: hidden above 8192");
     if (!x || !out || !workspace) return fail(UOCR_EINVAL, "moe_decode: null pointer");
     if (!a16(x) || !a16(out)) return fail(UOCR_EINVAL, "moe_decode: x and out must be 16-byte aligned");
+    if (bias && (reinterpret_cast<uintptr_t>(bias) & 3)) return fail(UOCR_EINVAL, "moe_decode: bias must be 4-byte aligned");
     if (reinterpret_cast<uintptr_t>(workspace) & 255) return fail(UOCR_EINVAL, "moe_decode: workspace must be 256-byte aligned");
     const DecodeLayout d = decode_layout(L, B);
     if (workspace_bytes < d.total)
         return fail(UOCR_EINVAL, "moe_decode: workspace of %zu bytes, need %zu", workspace_bytes, d.total);
     char* ws = reinterpret_cast<char*>(workspace);
-    cudaStream_t st = S(stream);
-    int32_t* ids = ids_out ? ids_out : reinterpret_cast<int32_t*>(ws + d.ids);
-    float* wts = wts_out ? wts_out : reinterpret_cast<float*>(ws + d.wts);
-    cudaError_t err = cudaMemsetAsync(ws + d.status, 0, sizeof(uint32_t), st);
-    if (err != cudaSuccess) return cuda_status(err, "moe_decode: status reset");
-    err = uocr::launch_route(x, (int)B, L->hidden, L->router, L->n_routed, bias, L->top_k, ids, wts, st);
-    if (err != cudaSuccess) return cuda_status(err, "moe_decode: route");
     uocr::DecodeArgs a{};
     a.B = (int)B; a.H = L->hidden; a.I = L->inter; a.E = L->n_routed; a.S = L->n_shared; a.topk = L->top_k;
     a.G = L->int8 ? L->group : 128; a.int8 = L->int8;
-    a.x = x; a.ids = ids; a.wts = wts;
+    a.x = x; a.router = L->router; a.bias = bias;
+    a.ids = ids_out ? ids_out : reinterpret_cast<int32_t*>(ws + d.ids);
+    a.wts = wts_out ? wts_out : reinterpret_cast<float*>(ws + d.wts);
     a.w13 = L->w13; a.s13 = L->s13; a.w2 = L->w2; a.s2 = L->s2;
     a.w13_shared = L->w13_shared; a.w2_shared = L->w2_shared;
     a.h = reinterpret_cast<float*>(ws + d.h);
     a.y = reinterpret_cast<float*>(ws + d.y);
     a.out = out;
-    a.status = reinterpret_cast<uint32_t*>(ws + d.status);
-    return cuda_status(uocr::launch_decode_experts(a, st), "moe_decode: experts");
+    a.ctl = reinterpret_cast<uocr::DecodeCtl*>(ws + d.ctl);
+    a.logits = reinterpret_cast<float*>(ws + d.logits);
+    a.table = reinterpret_cast<uocr::RouteTable*>(ws + d.table);
+    return cuda_status(uocr::launch_decode_layer(a, S(stream)), "moe_decode: launch");
 }
 
 int uocr_moe_device_status(const void* workspace, uocr_stream_t stream) {
@@ -308,7 +311,11 @@ int uocr_moe_device_status(const void* workspace, uocr_stream_t stream) {
     uint32_t status = 0;
     err = cudaMemcpy(&status, workspace, sizeof status, cudaMemcpyDeviceToHost);
     if (err != cudaSuccess) return cuda_status(err, "device_status: read");
-    if (status) return fail(UOCR_EDEVICE, "device_status: a device-side wait gave up (code %u)", status);
+    if (status) {
+        // sticky until read: clear it so the next failure is reported afresh
+        cudaMemset(const_cast<void*>(workspace), 0, sizeof status);
+        return fail(UOCR_EDEVICE, "device_status: a device-side wait gave up (code %u)", status);
+    }
     return ok();
 }
 

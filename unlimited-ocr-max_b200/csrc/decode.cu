@@ -1,275 +1,691 @@
-// Decode-step MoE sublayer (MoE.decode_rows, unlimited_ocr_max/decoder.py:641-655) for
-// B <= 8 tokens: HBM-bound weight streaming.
+// Decode-step MoE sublayer (MoE.decode_rows, unlimited_ocr_max/decoder.py:641-655) for B <= 8
+// tokens, as ONE persistent kernel per layer. HBM-bound: the job is to stream the touched
+// experts' weights at full bandwidth, once each.
 //
-// Pairs. Routed (token t, slot s) is pair t*k + s; shared expert q's copy of token t is
-// pair k*B + q*B + t. Every pair is one SwiGLU expert evaluation:
-//   h[p, n]  = silu(Wg[e, n, :] . x[t]) * (Wu[e, n, :] . x[t])          (gate/up kernel)
-//   y[p, j]  = Wd[e, j, :] . h[p]                                      (down kernel)
-//   out[t,j] = sum_s w[t,s] * y[t*k+s, j] + sum_q y[k*B+q*B+t, j]        (combine kernel)
-// Work items are (expert slot, row block). Expert slots 0..S-1 are the shared experts;
-// slot S+r is the r-th distinct routed expert in ascending id. Every item reads its rows
-// of the expert ONCE for all the pairs routed to that expert (the reference's "read once"
-// property, kernels/moe_routing.mojo:1-16). A pair's sums use only its own token and
-// expert, so its bits do not depend on B or on which tokens share an expert.
+// Pairs. Routed (token t, slot s) is pair t*k + s; shared expert q's copy of token t is pair
+// k*B + q*B + t. Expert slots: 0..S-1 are the shared experts, S+u is the u-th distinct routed
+// expert in ascending id (the reference's rows-grouped-by-expert, kernels/moe_routing.mojo).
+//
+// Work items, claimed in this order from an atomic queue (so an item only ever waits for
+// items claimed before it, which are already running: no deadlock at any grid size):
+//   ROUTE r   logits of experts [8r, 8r+8) for all B tokens; the last ROUTE item runs the
+//             softmax + top-k (bit-exact with the oracle) and publishes the routing table;
+//   GU        (slot, 8 intermediate rows): gate and up rows of the slot's expert, SwiGLU,
+//             h[pair][n] for every pair on that expert -- each weight row read once;
+//   DOWN      (slot, 16 output rows): y[pair][j] = Wd[e][j] . h[pair]; the last DOWN item of
+//             an output block (all S + U slots done) combines
+//             out[t][j] = sum_s w[t,s] y[t*k+s][j] + sum_q y_shared[q][t][j]   (fixed order).
+// A warp-specialised CTA: one producer warp claims items and streams each item's weight rows
+// with cp.async.bulk into a ring of shared-memory stages (mbarrier full/empty pairs); eight
+// consumer warps compute from shared memory. A pair's arithmetic uses only its own token and
+// expert, so every output row is bitwise independent of the batch it rides in.
+//
+// Every device-side wait is bounded (sm100.cuh: kWaitBudgetNs): on expiry it records a
+// status code in the workspace and the kernel winds down. The control counters reset
+// themselves at the end of each launch (the last CTA to finish clears them), so a
+// zero-filled workspace stays valid across calls.
+#include <algorithm>
+
 #include "common.cuh"
 #include "kernels.h"
+#include "sm100.cuh"
 
 namespace uocr {
 
-constexpr int kDecWarps = 8;
-constexpr int kDecRowsPerWarp = 4;
-constexpr int kDecRowsPerCta = kDecWarps * kDecRowsPerWarp;  // 32
+constexpr int kConsumerWarps = 8;
+constexpr int kConsumers = kConsumerWarps * 32;       // 256
+constexpr int kThreads = kConsumers + 32;              // + producer warp
+constexpr int kRB = 8;                                 // intermediate rows per GU item
+constexpr int kRJ = 16;                                // output rows per DOWN item
+constexpr int kUnit = 64;                              // K elements per compute unit
+constexpr int kPad = 68;                               // padded floats per 64-element slice
 constexpr int kMaxB = 8;
+constexpr int kRouteExperts = 8;                       // experts per ROUTE item
 
-struct ExpertSlot {
-    int valid;
-    int expert;             // routed expert id, or shared expert index
-    int shared;             // 1 for a shared expert
-    int count;              // pairs served
-    int pair[kMaxB];        // pair index per served token
-    int token[kMaxB];       // token index per served pair
-    float weight[kMaxB];    // routing weight (1 for shared)
+enum ItemType : int { kDone = 0, kRoute = 1, kGateUp = 2, kDown = 3 };
+
+struct ItemMeta {
+    int type, slot, block, expert, shared, count, int8, pad;
+    int pair[kMaxB];
+    int token[kMaxB];
+    float weight[kMaxB];
 };
 
-// Resolve blockIdx.y into the expert slot this CTA serves (thread 0 only).
-__device__ void resolve_slot(ExpertSlot& es, int u, const DecodeArgs& a) {
-    es.valid = 0;
-    es.count = 0;
-    const int kB = a.topk * a.B;
-    if (u < a.S) {
-        es.valid = 1;
-        es.shared = 1;
-        es.expert = u;
-        es.count = a.B;
-        for (int t = 0; t < a.B; ++t) {
-            es.pair[t] = kB + u * a.B + t;
-            es.token[t] = t;
-            es.weight[t] = 1.0f;
+struct Smem {
+    uint64_t* full;
+    uint64_t* empty;
+    ItemMeta* meta;
+    float* xs;     // [B][H/64][68]
+    float* hs;     // [8][I/64][68]
+    float* part;   // partial sums
+    unsigned char* stages;
+    int* flag;     // small scratch ints
+};
+
+UOCR_DEV unsigned char* stage_ptr(const Smem& s, int st, uint32_t stage_bytes) {
+    return s.stages + (size_t)st * stage_bytes;
+}
+
+// ---- item enumeration -------------------------------------------------------------------
+struct Plan {
+    int NR, NGB, NDB, MR, S;
+    uint32_t total;
+};
+
+UOCR_DEV Plan make_plan(const DecodeArgs& a) {
+    Plan p;
+    p.NR = (a.E + kRouteExperts - 1) / kRouteExperts;
+    p.NGB = a.I / kRB;
+    p.NDB = a.H / kRJ;
+    p.MR = min(a.E, a.topk * a.B);
+    p.S = a.S;
+    p.total = (uint32_t)(p.NR + (p.S + p.MR) * (p.NGB + p.NDB));
+    return p;
+}
+
+UOCR_DEV void decode_item(const Plan& p, uint32_t i, int& type, int& slot, int& block) {
+    if (i < (uint32_t)p.NR) { type = kRoute; slot = 0; block = (int)i; return; }
+    i -= p.NR;
+    const uint32_t gu = (uint32_t)(p.S + p.MR) * p.NGB;
+    if (i < gu) { type = kGateUp; slot = (int)(i / p.NGB); block = (int)(i % p.NGB); return; }
+    i -= gu;
+    type = kDown; slot = (int)(i / p.NDB); block = (int)(i % p.NDB);
+}
+
+UOCR_DEV float x_at(const float* xs, int NKX, int t, int k) { return xs[(t * NKX + k / kUnit) * kPad + (k % kUnit)]; }
+
+// ---- ROUTE -----------------------------------------------------------------------------------
+// Thread (expert j, segment s) fma-chains router row j's segment s against every token (the
+// oracle's order); segments summed in ascending order; bias added; logits to global.
+UOCR_DEV void do_route(const DecodeArgs& a, const Smem& sm, const Plan& p, int r, int ctid) {
+    const int H = a.H, B = a.B, L = H / 8, NKX = H / kUnit;
+    const int jl = ctid >> 3, s = ctid & 7;  // 64 threads: 8 experts x 8 segments
+    const int j = r * kRouteExperts + jl;
+    if (ctid < 64 && j < a.E) {
+        float acc[kMaxB];
+#pragma unroll
+        for (int b = 0; b < kMaxB; ++b) acc[b] = 0.0f;
+        const uint16_t* wrow = a.router + (size_t)j * H + s * L;
+        for (int kk = 0; kk < L; kk += 8) {
+            float wf[8];
+            unpack_bf16x8(*reinterpret_cast<const uint4*>(wrow + kk), wf);
+            const int k0 = s * L + kk;
+#pragma unroll
+            for (int b = 0; b < kMaxB; ++b) {
+                if (b < B) {
+                    const float* xr = sm.xs + (b * NKX + k0 / kUnit) * kPad + (k0 % kUnit);  // 8 | 64: no straddle
+                    const float4 xa = *reinterpret_cast<const float4*>(xr);
+                    const float4 xb = *reinterpret_cast<const float4*>(xr + 4);
+                    float v = acc[b];
+                    v = __fmaf_rn(wf[0], xa.x, v); v = __fmaf_rn(wf[1], xa.y, v);
+                    v = __fmaf_rn(wf[2], xa.z, v); v = __fmaf_rn(wf[3], xa.w, v);
+                    v = __fmaf_rn(wf[4], xb.x, v); v = __fmaf_rn(wf[5], xb.y, v);
+                    v = __fmaf_rn(wf[6], xb.z, v); v = __fmaf_rn(wf[7], xb.w, v);
+                    acc[b] = v;
+                }
+            }
         }
-        return;
+#pragma unroll
+        for (int b = 0; b < kMaxB; ++b) sm.part[(jl * 8 + s) * kMaxB + b] = acc[b];
     }
-    unsigned long long used = 0ull;
-    for (int p = 0; p < kB; ++p) used |= 1ull << clamp_expert(a.ids[p], a.E);
-    int r = u - a.S;
-    if (r >= __popcll(used)) return;
-    for (int i = 0; i < r; ++i) used &= used - 1ull;  // drop the r lowest set bits
-    const int e = __ffsll(used) - 1;
-    es.valid = 1;
-    es.shared = 0;
-    es.expert = e;
-    for (int p = 0; p < kB; ++p) {
-        if (clamp_expert(a.ids[p], a.E) == e) {
-            es.pair[es.count] = p;
-            es.token[es.count] = p / a.topk;
-            es.weight[es.count] = a.wts[p];
-            ++es.count;
+    named_bar_sync(1, kConsumers);
+    if (ctid < kRouteExperts * B) {
+        const int jj = ctid / B, b = ctid % B, jg = r * kRouteExperts + jj;
+        if (jg < a.E) {
+            float total = sm.part[(jj * 8 + 0) * kMaxB + b];
+#pragma unroll
+            for (int q = 1; q < 8; ++q) total = __fadd_rn(total, sm.part[(jj * 8 + q) * kMaxB + b]);
+            if (a.bias) total = __fadd_rn(total, a.bias[jg]);
+            a.logits[b * 64 + jg] = total;
+            __threadfence();
         }
     }
-}
-
-// One 8-element chunk of a weight row (bf16 or int8) as fp32.
-template <bool kInt8>
-UOCR_DEV void load_chunk(const void* row, int k0, float (&f)[8]) {
-    if (kInt8) {
-        const uint2 v = ldg_nc_v2(reinterpret_cast<const int8_t*>(row) + k0);
-        unpack_s8x8(v.x, v.y, f);
-    } else {
-        unpack_bf16x8(ldg_nc_v4(reinterpret_cast<const uint16_t*>(row) + k0), f);
+    named_bar_sync(1, kConsumers);
+    if (ctid == 0) sm.flag[0] = (atomicAdd(&a.ctl->route_done, 1u) == (uint32_t)p.NR - 1) ? 1 : 0;
+    named_bar_sync(1, kConsumers);
+    if (!sm.flag[0]) return;
+    // the last ROUTE item: softmax + top-k per token (warp b serves token b), then the table
+    __threadfence();
+    const int warp = ctid >> 5, lane = ctid & 31;
+    if (warp < B) {
+        const int b = warp, E = a.E, k = a.topk;
+        const bool v0 = lane < E, v1 = lane + 32 < E;
+        const float l0 = v0 ? __ldcg(a.logits + b * 64 + lane) : -INFINITY;
+        const float l1 = v1 ? __ldcg(a.logits + b * 64 + lane + 32) : -INFINITY;
+        float m = fmaxf(l0, l1);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+        const float e0 = v0 ? uocr_exp(__fsub_rn(l0, m)) : 0.0f;
+        const float e1 = v1 ? uocr_exp(__fsub_rn(l1, m)) : 0.0f;
+        float sum = __fadd_rn(e0, e1);
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, off));
+        float p0 = v0 ? __fdiv_rn(e0, sum) : -1.0f;
+        float p1 = v1 ? __fdiv_rn(e1, sum) : -1.0f;
+        for (int rr = 0; rr < k; ++rr) {
+            float bp = p0;
+            int bi = lane;
+            if (p1 > bp) { bp = p1; bi = lane + 32; }
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) {
+                const float op = __shfl_xor_sync(0xffffffffu, bp, off);
+                const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+                if (op > bp || (op == bp && oi < bi)) { bp = op; bi = oi; }
+            }
+            if (bi == lane) p0 = -2.0f;
+            if (bi == lane + 32) p1 = -2.0f;
+            if (lane == 0) {
+                a.ids[b * k + rr] = bi;
+                a.wts[b * k + rr] = bp;
+                sm.flag[8 + b * k + rr] = bi;  // smem copy for the table build
+                reinterpret_cast<float*>(sm.flag)[8 + kMaxB * 8 + b * k + rr] = bp;
+            }
+        }
+    }
+    named_bar_sync(1, kConsumers);
+    if (ctid == 0) {
+        const int kB = a.topk * B;
+        unsigned long long used = 0ull;
+        for (int q = 0; q < kB; ++q) used |= 1ull << sm.flag[8 + q];
+        RouteTable* tb = a.table;
+        int U = 0;
+        while (used) {
+            const int e = __ffsll(used) - 1;
+            used &= used - 1ull;
+            int c = 0;
+            for (int q = 0; q < kB; ++q) {
+                if (sm.flag[8 + q] == e) {
+                    tb->pair[U][c] = q;
+                    tb->token[U][c] = q / a.topk;
+                    tb->weight[U][c] = reinterpret_cast<float*>(sm.flag)[8 + kMaxB * 8 + q];
+                    ++c;
+                }
+            }
+            tb->expert[U] = e;
+            tb->count[U] = c;
+            ++U;
+        }
+        tb->U = U;
+        __threadfence();
+        st_release_gpu(&a.ctl->route_ready, 1u);
     }
 }
 
-UOCR_DEV float dot8(const float (&w)[8], const float* xs) {
-    const float4 xa = *reinterpret_cast<const float4*>(xs);
-    const float4 xb = *reinterpret_cast<const float4*>(xs + 4);
-    float d = __fmul_rn(w[0], xa.x);
-    d = __fmaf_rn(w[1], xa.y, d);
-    d = __fmaf_rn(w[2], xa.z, d);
-    d = __fmaf_rn(w[3], xa.w, d);
-    d = __fmaf_rn(w[4], xb.x, d);
-    d = __fmaf_rn(w[5], xb.y, d);
-    d = __fmaf_rn(w[6], xb.z, d);
-    d = __fmaf_rn(w[7], xb.w, d);
-    return d;
-}
-
-// ---- gate/up + SwiGLU -----------------------------------------------------------------
-// CTA = (row block of 32 intermediate rows, expert slot); warp = 4 rows, one at a time;
-// lane l reads the 8-element chunks k0 = 8l + 256j of the gate row and the up row.
-template <bool kRoutedInt8>
-__global__ void __launch_bounds__(kDecWarps * 32)
-decode_gate_up_kernel(DecodeArgs a) {
-    extern __shared__ float xs[];  // [count][H]
-    __shared__ ExpertSlot es;
-    if (threadIdx.x == 0) resolve_slot(es, blockIdx.y, a);
-    __syncthreads();
-    if (!es.valid) return;
-    const int H = a.H, I = a.I, c = es.count;
-    for (int i = threadIdx.x; i < c * H; i += blockDim.x) {
-        const int ci = i / H;
-        xs[i] = a.x[(size_t)es.token[ci] * H + (i - ci * H)];
-    }
-    __syncthreads();
-
-    const bool int8 = kRoutedInt8 && !es.shared;
-    const size_t expert_rows = (size_t)2 * I;
-    const void* wbase;
-    const float* sbase = nullptr;
-    if (es.shared) {
-        wbase = a.w13_shared + (size_t)es.expert * expert_rows * H;
-    } else if (kRoutedInt8) {
-        wbase = reinterpret_cast<const int8_t*>(a.w13) + (size_t)es.expert * expert_rows * H;
-        sbase = a.s13 + (size_t)es.expert * expert_rows * (H / a.G);
-    } else {
-        wbase = reinterpret_cast<const uint16_t*>(a.w13) + (size_t)es.expert * expert_rows * H;
-    }
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int gsz = a.G;
-    for (int i = 0; i < kDecRowsPerWarp; ++i) {
-        const int n = blockIdx.x * kDecRowsPerCta + warp * kDecRowsPerWarp + i;
-        if (n >= I) break;
-        const int pg = (n / 128) * 256 + (n % 128);  // packed gate row
-        const int pu = pg + 128;                     // packed up row
-        const size_t esz = int8 ? 1 : 2;
-        const char* rg = reinterpret_cast<const char*>(wbase) + (size_t)pg * H * esz;
-        const char* ru = reinterpret_cast<const char*>(wbase) + (size_t)pu * H * esz;
+// ---- GU -----------------------------------------------------------------------------------------
+template <bool kI8>
+UOCR_DEV void gu_units(const DecodeArgs& a, const Smem& sm, const ItemMeta& m, const unsigned char* stage,
+                       uint32_t row_stride, int ctid) {
+    const int H = a.H, NKX = H / kUnit, c = m.count;
+    const int units = kRB * NKX;
+    for (int u = ctid; u < units; u += kConsumers) {
+        const int r = u % kRB, ks = u / kRB;
+        const unsigned char* grow = stage + (size_t)r * row_stride;
+        const unsigned char* urow = stage + (size_t)(kRB + r) * row_stride;
         float ag[kMaxB], au[kMaxB];
 #pragma unroll
         for (int q = 0; q < kMaxB; ++q) ag[q] = au[q] = 0.0f;
-        for (int k0 = lane * 8; k0 < H; k0 += 256) {
-            float wgf[8], wuf[8];
-            float sg = 1.0f, su = 1.0f;
-            if (int8) {
-                load_chunk<true>(rg, k0, wgf);
-                load_chunk<true>(ru, k0, wuf);
-                sg = sbase[(size_t)pg * (H / gsz) + k0 / gsz];
-                su = sbase[(size_t)pu * (H / gsz) + k0 / gsz];
-            } else {
-                load_chunk<false>(rg, k0, wgf);
-                load_chunk<false>(ru, k0, wuf);
-            }
+        if (!kI8) {
+#pragma unroll 2
+            for (int j = 0; j < kUnit / 8; ++j) {
+                float fg[8], fu[8];
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(grow + ks * kUnit * 2 + j * 16), fg);
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(urow + ks * kUnit * 2 + j * 16), fu);
 #pragma unroll
-            for (int q = 0; q < kMaxB; ++q) {
-                if (q < c) {
-                    const float* xq = xs + q * H + k0;
-                    if (int8) {
-                        ag[q] = __fmaf_rn(sg, dot8(wgf, xq), ag[q]);
-                        au[q] = __fmaf_rn(su, dot8(wuf, xq), au[q]);
-                    } else {
-                        ag[q] = __fadd_rn(ag[q], dot8(wgf, xq));
-                        au[q] = __fadd_rn(au[q], dot8(wuf, xq));
+                for (int q = 0; q < kMaxB; ++q) {
+                    if (q < c) {
+                        const float* xr = sm.xs + (m.token[q] * NKX + ks) * kPad + j * 8;
+                        const float4 xa = *reinterpret_cast<const float4*>(xr);
+                        const float4 xb = *reinterpret_cast<const float4*>(xr + 4);
+                        const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+                        float g = ag[q], v = au[q];
+#pragma unroll
+                        for (int e = 0; e < 8; ++e) {
+                            g = __fmaf_rn(fg[e], xv[e], g);
+                            v = __fmaf_rn(fu[e], xv[e], v);
+                        }
+                        ag[q] = g;
+                        au[q] = v;
                     }
                 }
             }
+        } else {
+#pragma unroll 1
+            for (int j = 0; j < kUnit / 16; ++j) {
+                const uint4 wg = *reinterpret_cast<const uint4*>(grow + ks * kUnit + j * 16);
+                const uint4 wu = *reinterpret_cast<const uint4*>(urow + ks * kUnit + j * 16);
+                float fg[16], fu[16];
+                unpack_s8x8(wg.x, wg.y, *reinterpret_cast<float(*)[8]>(fg));
+                unpack_s8x8(wg.z, wg.w, *reinterpret_cast<float(*)[8]>(fg + 8));
+                unpack_s8x8(wu.x, wu.y, *reinterpret_cast<float(*)[8]>(fu));
+                unpack_s8x8(wu.z, wu.w, *reinterpret_cast<float(*)[8]>(fu + 8));
+#pragma unroll
+                for (int q = 0; q < kMaxB; ++q) {
+                    if (q < c) {
+                        const float* xr = sm.xs + (m.token[q] * NKX + ks) * kPad + j * 16;
+                        float g = ag[q], v = au[q];
+#pragma unroll
+                        for (int h4 = 0; h4 < 4; ++h4) {
+                            const float4 xv = *reinterpret_cast<const float4*>(xr + 4 * h4);
+                            g = __fmaf_rn(fg[4 * h4 + 0], xv.x, g); v = __fmaf_rn(fu[4 * h4 + 0], xv.x, v);
+                            g = __fmaf_rn(fg[4 * h4 + 1], xv.y, g); v = __fmaf_rn(fu[4 * h4 + 1], xv.y, v);
+                            g = __fmaf_rn(fg[4 * h4 + 2], xv.z, g); v = __fmaf_rn(fu[4 * h4 + 2], xv.z, v);
+                            g = __fmaf_rn(fg[4 * h4 + 3], xv.w, g); v = __fmaf_rn(fu[4 * h4 + 3], xv.w, v);
+                        }
+                        ag[q] = g;
+                        au[q] = v;
+                    }
+                }
+            }
+            // the unit lies in one quantisation group: scale the partial sums (group sum, then scale)
+            const int n = m.block * kRB + r;
+            const int pg = (n / 128) * 256 + (n % 128);
+            const size_t groups = (size_t)H / a.G;
+            const float* sb = a.s13 + (size_t)m.expert * 2 * a.I * groups;
+            const float sg = __ldg(sb + (size_t)pg * groups + (ks * kUnit) / a.G);
+            const float su = __ldg(sb + (size_t)(pg + 128) * groups + (ks * kUnit) / a.G);
+#pragma unroll
+            for (int q = 0; q < kMaxB; ++q) { ag[q] = __fmul_rn(ag[q], sg); au[q] = __fmul_rn(au[q], su); }
         }
 #pragma unroll
         for (int q = 0; q < kMaxB; ++q) {
             if (q < c) {
-                const float g = warp_sum_butterfly(ag[q]);
-                const float u = warp_sum_butterfly(au[q]);
-                if (lane == 0) a.h[(size_t)es.pair[q] * I + n] = silu(g) * u;
+                sm.part[((r * NKX + ks) * kMaxB + q) * 2 + 0] = ag[q];
+                sm.part[((r * NKX + ks) * kMaxB + q) * 2 + 1] = au[q];
             }
         }
     }
 }
 
-// ---- down ---------------------------------------------------------------------------------
-template <bool kRoutedInt8>
-__global__ void __launch_bounds__(kDecWarps * 32)
-decode_down_kernel(DecodeArgs a) {
-    extern __shared__ float hs[];  // [count][I]
-    __shared__ ExpertSlot es;
-    if (threadIdx.x == 0) resolve_slot(es, blockIdx.y, a);
-    __syncthreads();
-    if (!es.valid) return;
-    const int H = a.H, I = a.I, c = es.count;
-    for (int i = threadIdx.x; i < c * I; i += blockDim.x) {
-        const int ci = i / I;
-        hs[i] = a.h[(size_t)es.pair[ci] * I + (i - ci * I)];
+UOCR_DEV void do_gate_up(const DecodeArgs& a, const Smem& sm, const ItemMeta& m, const unsigned char* stage,
+                         uint32_t row_stride, int ctid) {
+    if (m.int8)
+        gu_units<true>(a, sm, m, stage, row_stride, ctid);
+    else
+        gu_units<false>(a, sm, m, stage, row_stride, ctid);
+    named_bar_sync(1, kConsumers);
+    const int NKX = a.H / kUnit, c = m.count;
+    for (int t = ctid; t < kRB * c; t += kConsumers) {
+        const int r = t / c, q = t % c;
+        float g = sm.part[((r * NKX + 0) * kMaxB + q) * 2 + 0];
+        float u = sm.part[((r * NKX + 0) * kMaxB + q) * 2 + 1];
+        for (int ks = 1; ks < NKX; ++ks) {
+            g = __fadd_rn(g, sm.part[((r * NKX + ks) * kMaxB + q) * 2 + 0]);
+            u = __fadd_rn(u, sm.part[((r * NKX + ks) * kMaxB + q) * 2 + 1]);
+        }
+        a.h[(size_t)m.pair[q] * a.I + m.block * kRB + r] = silu(g) * u;
+        __threadfence();
     }
-    __syncthreads();
-    const bool int8 = kRoutedInt8 && !es.shared;
-    const void* wbase;
-    const float* sbase = nullptr;
-    if (es.shared) {
-        wbase = a.w2_shared + (size_t)es.expert * H * I;
-    } else if (kRoutedInt8) {
-        wbase = reinterpret_cast<const int8_t*>(a.w2) + (size_t)es.expert * H * I;
-        sbase = a.s2 + (size_t)es.expert * H * (I / a.G);
-    } else {
-        wbase = reinterpret_cast<const uint16_t*>(a.w2) + (size_t)es.expert * H * I;
-    }
-    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int gsz = a.G;
-    for (int i = 0; i < kDecRowsPerWarp; ++i) {
-        const int j = blockIdx.x * kDecRowsPerCta + warp * kDecRowsPerWarp + i;
-        if (j >= H) break;
-        const size_t esz = int8 ? 1 : 2;
-        const char* rw = reinterpret_cast<const char*>(wbase) + (size_t)j * I * esz;
+    named_bar_sync(1, kConsumers);
+    if (ctid == 0) atomicAdd(&a.ctl->gu_done[m.slot], 1u);
+}
+
+// ---- DOWN -------------------------------------------------------------------------------------
+template <bool kI8>
+UOCR_DEV void down_units(const DecodeArgs& a, const Smem& sm, const ItemMeta& m, const unsigned char* stage,
+                         uint32_t row_stride, int ctid) {
+    const int I = a.I, NKI = I / kUnit, c = m.count;
+    const int units = kRJ * NKI;
+    for (int u = ctid; u < units; u += kConsumers) {
+        const int r = u % kRJ, ks = u / kRJ;
+        const unsigned char* wrow = stage + (size_t)r * row_stride;
         float acc[kMaxB];
 #pragma unroll
         for (int q = 0; q < kMaxB; ++q) acc[q] = 0.0f;
-        for (int k0 = lane * 8; k0 < I; k0 += 256) {
-            float wf[8];
-            float sc = 1.0f;
-            if (int8) {
-                load_chunk<true>(rw, k0, wf);
-                sc = sbase[(size_t)j * (I / gsz) + k0 / gsz];
-            } else {
-                load_chunk<false>(rw, k0, wf);
-            }
+        if (!kI8) {
+#pragma unroll 2
+            for (int j = 0; j < kUnit / 8; ++j) {
+                float f[8];
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(wrow + ks * kUnit * 2 + j * 16), f);
 #pragma unroll
-            for (int q = 0; q < kMaxB; ++q) {
-                if (q < c) {
-                    const float d = dot8(wf, hs + q * I + k0);
-                    acc[q] = int8 ? __fmaf_rn(sc, d, acc[q]) : __fadd_rn(acc[q], d);
+                for (int q = 0; q < kMaxB; ++q) {
+                    if (q < c) {
+                        const float* hr = sm.hs + (q * NKI + ks) * kPad + j * 8;
+                        const float4 ha = *reinterpret_cast<const float4*>(hr);
+                        const float4 hb = *reinterpret_cast<const float4*>(hr + 4);
+                        float v = acc[q];
+                        v = __fmaf_rn(f[0], ha.x, v); v = __fmaf_rn(f[1], ha.y, v);
+                        v = __fmaf_rn(f[2], ha.z, v); v = __fmaf_rn(f[3], ha.w, v);
+                        v = __fmaf_rn(f[4], hb.x, v); v = __fmaf_rn(f[5], hb.y, v);
+                        v = __fmaf_rn(f[6], hb.z, v); v = __fmaf_rn(f[7], hb.w, v);
+                        acc[q] = v;
+                    }
                 }
             }
+        } else {
+#pragma unroll 1
+            for (int j = 0; j < kUnit / 16; ++j) {
+                const uint4 w = *reinterpret_cast<const uint4*>(wrow + ks * kUnit + j * 16);
+                float f[16];
+                unpack_s8x8(w.x, w.y, *reinterpret_cast<float(*)[8]>(f));
+                unpack_s8x8(w.z, w.w, *reinterpret_cast<float(*)[8]>(f + 8));
+#pragma unroll
+                for (int q = 0; q < kMaxB; ++q) {
+                    if (q < c) {
+                        const float* hr = sm.hs + (q * NKI + ks) * kPad + j * 16;
+                        float v = acc[q];
+#pragma unroll
+                        for (int h4 = 0; h4 < 4; ++h4) {
+                            const float4 hv = *reinterpret_cast<const float4*>(hr + 4 * h4);
+                            v = __fmaf_rn(f[4 * h4 + 0], hv.x, v);
+                            v = __fmaf_rn(f[4 * h4 + 1], hv.y, v);
+                            v = __fmaf_rn(f[4 * h4 + 2], hv.z, v);
+                            v = __fmaf_rn(f[4 * h4 + 3], hv.w, v);
+                        }
+                        acc[q] = v;
+                    }
+                }
+            }
+            const int jrow = m.block * kRJ + r;
+            const size_t groups = (size_t)I / a.G;
+            const float sc = __ldg(a.s2 + ((size_t)m.expert * a.H + jrow) * groups + (ks * kUnit) / a.G);
+#pragma unroll
+            for (int q = 0; q < kMaxB; ++q) acc[q] = __fmul_rn(acc[q], sc);
         }
 #pragma unroll
-        for (int q = 0; q < kMaxB; ++q) {
-            if (q < c) {
-                const float v = warp_sum_butterfly(acc[q]);
-                if (lane == 0) a.y[(size_t)es.pair[q] * H + j] = v;
-            }
-        }
+        for (int q = 0; q < kMaxB; ++q)
+            if (q < c) sm.part[(r * NKI + ks) * kMaxB + q] = acc[q];
     }
 }
 
-// ---- combine ------------------------------------------------------------------------------
-__global__ void __launch_bounds__(256)
-decode_combine_kernel(DecodeArgs a) {
-    const int t = blockIdx.x;
-    const int kB = a.topk * a.B;
-    for (int j = threadIdx.x; j < a.H; j += blockDim.x) {
+UOCR_DEV void do_down(const DecodeArgs& a, const Smem& sm, const Plan& p, const ItemMeta& m,
+                      const unsigned char* stage, uint32_t row_stride, int ctid) {
+    const int I = a.I, NKI = I / kUnit, c = m.count;
+    // the slot's gate/up must be complete before its h is read
+    if (ctid == 0) sm.flag[1] = wait_counter_geq(&a.ctl->gu_done[m.slot], (uint32_t)p.NGB, &a.ctl->status) ? 1 : 0;
+    named_bar_sync(1, kConsumers);
+    const bool ready = sm.flag[1] != 0;
+    if (ready) {
+        for (int i = ctid; i < c * (I / 4); i += kConsumers) {
+            const int q = i / (I / 4), k = (i % (I / 4)) * 4;
+            const float4 v = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)m.pair[q] * I + k));
+            *reinterpret_cast<float4*>(sm.hs + (q * NKI + k / kUnit) * kPad + (k % kUnit)) = v;
+        }
+    }
+    named_bar_sync(1, kConsumers);
+    if (ready) {
+        if (m.int8)
+            down_units<true>(a, sm, m, stage, row_stride, ctid);
+        else
+            down_units<false>(a, sm, m, stage, row_stride, ctid);
+    }
+    named_bar_sync(1, kConsumers);
+    if (ready) {
+        for (int t = ctid; t < kRJ * c; t += kConsumers) {
+            const int r = t / c, q = t % c;
+            float y = sm.part[(r * NKI + 0) * kMaxB + q];
+            for (int ks = 1; ks < NKI; ++ks) y = __fadd_rn(y, sm.part[(r * NKI + ks) * kMaxB + q]);
+            a.y[(size_t)m.pair[q] * a.H + m.block * kRJ + r] = y;
+            __threadfence();
+        }
+    }
+    named_bar_sync(1, kConsumers);
+    if (ctid == 0) {
+        const uint32_t done = atomicAdd(&a.ctl->j_done[m.block], 1u) + 1u;
+        int fin = 0;
+        if (wait_counter_geq(&a.ctl->route_ready, 1u, &a.ctl->status)) {
+            const int U = __ldcg(&a.table->U);
+            fin = (done == (uint32_t)(p.S + U)) ? 1 : 0;
+        }
+        sm.flag[2] = fin;
+    }
+    named_bar_sync(1, kConsumers);
+    if (!sm.flag[2]) return;
+    __threadfence();
+    const int B = a.B, k = a.topk, kB = k * B;
+    for (int t = ctid; t < kRJ * B; t += kConsumers) {
+        const int r = t % kRJ, b = t / kRJ;
+        const int j = m.block * kRJ + r;
         float acc = 0.0f;
-        for (int s = 0; s < a.topk; ++s) {
-            const int p = t * a.topk + s;
-            acc = __fmaf_rn(a.wts[p], a.y[(size_t)p * a.H + j], acc);
+        for (int s = 0; s < k; ++s) {
+            const int pr = b * k + s;
+            acc = __fmaf_rn(__ldcg(a.wts + pr), __ldcg(a.y + (size_t)pr * a.H + j), acc);
         }
-        for (int q = 0; q < a.S; ++q) acc = __fadd_rn(acc, a.y[(size_t)(kB + q * a.B + t) * a.H + j]);
-        a.out[(size_t)t * a.H + j] = acc;
+        for (int q = 0; q < a.S; ++q) acc = __fadd_rn(acc, __ldcg(a.y + (size_t)(kB + q * B + b) * a.H + j));
+        a.out[(size_t)b * a.H + j] = acc;
     }
 }
 
-cudaError_t launch_decode_experts(const DecodeArgs& a, cudaStream_t st) {
-    const int slots = a.S + a.topk * a.B;
-    {
-        const size_t smem = sizeof(float) * (size_t)a.B * a.H;
-        dim3 grid((a.I + kDecRowsPerCta - 1) / kDecRowsPerCta, slots);
-        auto k = a.int8 ? decode_gate_up_kernel<true> : decode_gate_up_kernel<false>;
-        cudaError_t err = ensure_smem_optin(reinterpret_cast<const void*>(k), smem);
-        if (err != cudaSuccess) return err;
-        k<<<grid, kDecWarps * 32, smem, st>>>(a);
+// ---- producer -----------------------------------------------------------------------------
+UOCR_DEV bool fill_meta(const DecodeArgs& a, const Plan& p, ItemMeta& m, int type, int slot, int block,
+                        bool& route_seen) {
+    m.type = type;
+    m.slot = slot;
+    m.block = block;
+    m.int8 = 0;
+    m.count = 0;
+    if (type == kRoute) return true;
+    if (slot < p.S) {
+        m.shared = 1;
+        m.expert = slot;
+        m.count = a.B;
+        for (int t = 0; t < a.B; ++t) {
+            m.pair[t] = a.topk * a.B + slot * a.B + t;
+            m.token[t] = t;
+            m.weight[t] = 1.0f;
+        }
+        return true;
     }
-    {
-        const size_t smem = sizeof(float) * (size_t)a.B * a.I;
-        dim3 grid((a.H + kDecRowsPerCta - 1) / kDecRowsPerCta, slots);
-        auto k = a.int8 ? decode_down_kernel<true> : decode_down_kernel<false>;
-        cudaError_t err = ensure_smem_optin(reinterpret_cast<const void*>(k), smem);
-        if (err != cudaSuccess) return err;
-        k<<<grid, kDecWarps * 32, smem, st>>>(a);
+    if (!route_seen) {
+        if (!wait_counter_geq(&a.ctl->route_ready, 1u, &a.ctl->status)) return false;
+        route_seen = true;
     }
-    decode_combine_kernel<<<a.B, 256, 0, st>>>(a);
+    const int u = slot - p.S;
+    if (u >= __ldcg(&a.table->U)) {
+        m.type = -1;  // no such slot this step
+        return true;
+    }
+    m.shared = 0;
+    m.int8 = a.int8;
+    m.expert = __ldcg(&a.table->expert[u]);
+    m.count = __ldcg(&a.table->count[u]);
+    for (int q = 0; q < m.count; ++q) {
+        m.pair[q] = __ldcg(&a.table->pair[u][q]);
+        m.token[q] = __ldcg(&a.table->token[u][q]);
+        m.weight[q] = __ldcg(&a.table->weight[u][q]);
+    }
+    return true;
+}
+
+UOCR_DEV void producer(const DecodeArgs& a, const Smem& sm, const Plan& p, int nst, uint32_t stage_bytes,
+                       uint32_t gu_stride_b16, uint32_t gu_stride_i8, uint32_t dn_stride_b16, uint32_t dn_stride_i8,
+                       volatile int* abort_flag) {
+    bool route_seen = false;
+    int n = 0;
+    bool ok = true;
+    while (true) {
+        const uint32_t i = atomicAdd(&a.ctl->queue, 1u);
+        if (i >= p.total) break;
+        int type, slot, block;
+        decode_item(p, i, type, slot, block);
+        ItemMeta m;
+        if (!fill_meta(a, p, m, type, slot, block, route_seen)) { ok = false; break; }
+        if (m.type < 0) continue;
+        const int st = n % nst, round = n / nst;
+        if (round > 0 && !mbar_wait(&sm.empty[st], (round - 1) & 1, &a.ctl->status)) { ok = false; break; }
+        sm.meta[st] = m;
+        unsigned char* dst = stage_ptr(sm, st, stage_bytes);
+        if (type == kRoute) {
+            mbar_arrive(&sm.full[st]);
+        } else if (type == kGateUp) {
+            const int esz = m.int8 ? 1 : 2;
+            const uint32_t rb = (uint32_t)a.H * esz;
+            const uint32_t stride = m.int8 ? gu_stride_i8 : gu_stride_b16;
+            const unsigned char* base =
+                m.shared ? reinterpret_cast<const unsigned char*>(a.w13_shared) + (size_t)m.expert * 2 * a.I * rb
+                         : reinterpret_cast<const unsigned char*>(a.w13) + (size_t)m.expert * 2 * a.I * rb;
+            mbar_arrive_expect_tx(&sm.full[st], 2u * kRB * rb);
+            const int n0 = block * kRB;
+            const int pg0 = (n0 / 128) * 256 + (n0 % 128);
+            for (int r = 0; r < kRB; ++r) {
+                bulk_g2s(dst + (size_t)r * stride, base + (size_t)(pg0 + r) * rb, rb, &sm.full[st]);
+                bulk_g2s(dst + (size_t)(kRB + r) * stride, base + (size_t)(pg0 + 128 + r) * rb, rb, &sm.full[st]);
+            }
+        } else {
+            const int esz = m.int8 ? 1 : 2;
+            const uint32_t rb = (uint32_t)a.I * esz;
+            const uint32_t stride = m.int8 ? dn_stride_i8 : dn_stride_b16;
+            const unsigned char* base =
+                m.shared ? reinterpret_cast<const unsigned char*>(a.w2_shared) + (size_t)m.expert * a.H * rb
+                         : reinterpret_cast<const unsigned char*>(a.w2) + (size_t)m.expert * a.H * rb;
+            mbar_arrive_expect_tx(&sm.full[st], (uint32_t)kRJ * rb);
+            for (int r = 0; r < kRJ; ++r)
+                bulk_g2s(dst + (size_t)r * stride, base + (size_t)(block * kRJ + r) * rb, rb, &sm.full[st]);
+        }
+        ++n;
+    }
+    if (!ok) {
+        *abort_flag = 1;
+        // wait (bounded) for the copies already issued into stages the consumers will not drain
+        for (int q = max(0, n - nst); q < n; ++q) mbar_wait(&sm.full[q % nst], (q / nst) & 1, nullptr);
+        return;
+    }
+    const int st = n % nst, round = n / nst;
+    if (round > 0 && !mbar_wait(&sm.empty[st], (round - 1) & 1, &a.ctl->status)) {
+        *abort_flag = 1;
+        return;
+    }
+    sm.meta[st].type = kDone;
+    mbar_arrive(&sm.full[st]);
+}
+
+// ---- the kernel ---------------------------------------------------------------------------------
+__global__ void __launch_bounds__(kThreads, 1)
+decode_layer_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_meta, uint32_t off_xs, uint32_t off_hs,
+                    uint32_t off_part, uint32_t off_flag, uint32_t off_stages) {
+    extern __shared__ __align__(1024) unsigned char smem[];
+    __shared__ int abort_flag;
+    Smem sm;
+    sm.full = reinterpret_cast<uint64_t*>(smem);
+    sm.empty = sm.full + nst;
+    sm.meta = reinterpret_cast<ItemMeta*>(smem + off_meta);
+    sm.xs = reinterpret_cast<float*>(smem + off_xs);
+    sm.hs = reinterpret_cast<float*>(smem + off_hs);
+    sm.part = reinterpret_cast<float*>(smem + off_part);
+    sm.flag = reinterpret_cast<int*>(smem + off_flag);
+    sm.stages = smem + off_stages;
+    const Plan p = make_plan(a);
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        for (int s = 0; s < nst; ++s) {
+            mbar_init(&sm.full[s], 1);
+            mbar_init(&sm.empty[s], 1);
+        }
+        abort_flag = 0;
+        fence_mbar_init();
+    }
+    // stage the tokens: xs[b][k/64][k%64]
+    const int NKX = a.H / kUnit;
+    for (int i = tid; i < a.B * (a.H / 4); i += kThreads) {
+        const int b = i / (a.H / 4), k = (i % (a.H / 4)) * 4;
+        const float4 v = *reinterpret_cast<const float4*>(a.x + (size_t)b * a.H + k);
+        *reinterpret_cast<float4*>(sm.xs + (b * NKX + k / kUnit) * kPad + (k % kUnit)) = v;
+    }
+    __syncthreads();
+
+    const uint32_t gu_b16 = (uint32_t)a.H * 2 + 16, gu_i8 = (uint32_t)a.H + 16;
+    const uint32_t dn_b16 = (uint32_t)a.I * 2 + 16, dn_i8 = (uint32_t)a.I + 16;
+    if (tid >= kConsumers) {
+        if (tid == kConsumers) producer(a, sm, p, nst, stage_bytes, gu_b16, gu_i8, dn_b16, dn_i8, &abort_flag);
+        __syncwarp();
+    } else {
+        const int ctid = tid;
+        int n = 0;
+        while (true) {
+            const int st = n % nst;
+            const uint32_t parity = (n / nst) & 1;
+            // bounded wait that also gives up when the producer aborted
+            if (ctid == 0) {
+                int ok = 1;
+                const uint64_t t0 = global_timer_ns();
+                while (!mbar_try_wait(&sm.full[st], parity)) {
+                    if (*reinterpret_cast<volatile int*>(&abort_flag) ||
+                        global_timer_ns() - t0 > kWaitBudgetNs) {
+                        set_status(&a.ctl->status, kStatusWaitTimeout);
+                        ok = 0;
+                        break;
+                    }
+                }
+                sm.flag[3] = ok;
+            }
+            named_bar_sync(1, kConsumers);
+            if (!sm.flag[3]) break;
+            const ItemMeta& m = sm.meta[st];
+            if (m.type == kDone) break;
+            const unsigned char* stage = stage_ptr(sm, st, stage_bytes);
+            if (m.type == kRoute) {
+                do_route(a, sm, p, m.block, ctid);
+            } else if (m.type == kGateUp) {
+                do_gate_up(a, sm, m, stage, m.int8 ? gu_i8 : gu_b16, ctid);
+            } else {
+                do_down(a, sm, p, m, stage, m.int8 ? dn_i8 : dn_b16, ctid);
+            }
+            named_bar_sync(1, kConsumers);
+            if (ctid == 0) mbar_arrive(&sm.empty[st]);
+            ++n;
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence();
+        if (atomicAdd(&a.ctl->cta_done, 1u) == gridDim.x - 1) {
+            // last CTA: leave the control block zeroed for the next launch (status stays)
+            __threadfence();
+            a.ctl->queue = 0;
+            a.ctl->route_done = 0;
+            a.ctl->route_ready = 0;
+            for (int s = 0; s < p.S + p.MR; ++s) a.ctl->gu_done[s] = 0;
+            for (int j = 0; j < p.NDB; ++j) a.ctl->j_done[j] = 0;
+            __threadfence();
+            a.ctl->cta_done = 0;
+        }
+    }
+}
+
+// ---- host side ------------------------------------------------------------------------------------
+static size_t up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+cudaError_t launch_decode_layer(const DecodeArgs& a, cudaStream_t st) {
+    const int NKX = a.H / kUnit, NKI = a.I / kUnit;
+    const uint32_t gu_stage_b16 = 2u * kRB * ((uint32_t)a.H * 2 + 16);
+    const uint32_t gu_stage_i8 = 2u * kRB * ((uint32_t)a.H + 16);
+    const uint32_t dn_stage_b16 = (uint32_t)kRJ * ((uint32_t)a.I * 2 + 16);
+    const uint32_t dn_stage_i8 = (uint32_t)kRJ * ((uint32_t)a.I + 16);
+    // shared experts are always bf16, so a stage must hold a bf16 item
+    uint32_t stage_bytes = max(max(gu_stage_b16, dn_stage_b16), max(gu_stage_i8, dn_stage_i8));
+    stage_bytes = (uint32_t)up(stage_bytes, 128);
+    const size_t xs_bytes = sizeof(float) * (size_t)a.B * NKX * kPad;
+    const size_t hs_bytes = sizeof(float) * (size_t)kMaxB * NKI * kPad;
+    const size_t part_bytes =
+        sizeof(float) * max((size_t)kRB * NKX * kMaxB * 2, max((size_t)kRJ * NKI * kMaxB, (size_t)64 * 8 * kMaxB));
+    const size_t flag_bytes = sizeof(int) * (8 + 2 * kMaxB * 8 + 8);
+    int dev = 0, max_smem = 0, sms = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const int kMaxStages = 8;
+    size_t fixed = up(16 * kMaxStages, 128) + up(sizeof(ItemMeta) * kMaxStages, 128) + up(xs_bytes, 128) +
+                   up(hs_bytes, 128) + up(part_bytes, 128) + up(flag_bytes, 128) + 1024;
+    int nst = (int)std::min<size_t>(kMaxStages, ((size_t)max_smem - fixed) / stage_bytes);
+    if (nst < 2) return cudaErrorInvalidConfiguration;
+    size_t off = 0;
+    off += up(16 * (size_t)nst, 128);
+    const size_t off_meta = off; off += up(sizeof(ItemMeta) * nst, 128);
+    const size_t off_xs = off; off += up(xs_bytes, 128);
+    const size_t off_hs = off; off += up(hs_bytes, 128);
+    const size_t off_part = off; off += up(part_bytes, 128);
+    const size_t off_flag = off; off += up(flag_bytes, 128);
+    const size_t off_stages = up(off, 1024); off = off_stages + (size_t)nst * stage_bytes;
+    const size_t smem = off;
+    err = ensure_smem_optin(reinterpret_cast<const void*>(decode_layer_kernel), smem);
+    if (err != cudaSuccess) return err;
+    const int NR = (a.E + kRouteExperts - 1) / kRouteExperts;
+    const int MR = min(a.E, a.topk * a.B);
+    const long total = NR + (long)(a.S + MR) * (a.I / kRB + a.H / kRJ);
+    const int grid = (int)std::min<long>(total, (long)sms);
+    decode_layer_kernel<<<grid, kThreads, smem, st>>>(a, nst, stage_bytes, (uint32_t)off_meta, (uint32_t)off_xs,
+                                                     (uint32_t)off_hs, (uint32_t)off_part, (uint32_t)off_flag,
+                                                     (uint32_t)off_stages);
     return cudaGetLastError();
 }
 

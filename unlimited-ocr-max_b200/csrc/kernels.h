@@ -22,23 +22,50 @@ cudaError_t launch_route(const float* x, int T, int H, const uint16_t* wg, int E
                          int32_t* ids, float* wts, cudaStream_t st);
 
 // decode.cu
+// Control block at the start of a decode workspace. Zero-filled once by the caller; every
+// launch leaves it zeroed again except `status`, which is sticky until read.
+struct DecodeCtl {
+    uint32_t status;
+    uint32_t queue, route_done, route_ready, cta_done;
+    uint32_t pad[11];
+    uint32_t gu_done[128];  // per expert slot: gate/up items finished
+    uint32_t j_done[512];   // per 16-row output block: down items finished
+};
+constexpr int kDecodeMaxSlots = 128;
+constexpr int kDecodeMaxJBlocks = 512;
+
+// The step's routing grouped by expert (written by the last ROUTE item).
+struct RouteTable {
+    int U;  // distinct routed experts
+    int pad[3];
+    int expert[64];
+    int count[64];
+    int pair[64][8];
+    int token[64][8];
+    float weight[64][8];
+};
+
 struct DecodeArgs {
     int B, H, I, E, S, topk, G, int8;
     const float* x;
-    const int32_t* ids;
-    const float* wts;
+    const uint16_t* router;
+    const float* bias;
+    int32_t* ids;
+    float* wts;
     const void* w13;
     const float* s13;
     const void* w2;
     const float* s2;
     const uint16_t* w13_shared;
     const uint16_t* w2_shared;
-    float* h;     // [(k+S)*B, I]
-    float* y;     // [(k+S)*B, H]
-    float* out;   // [B, H]
-    uint32_t* status;
+    float* h;       // [(k+S)*B, I]
+    float* y;       // [(k+S)*B, H]
+    float* out;     // [B, H]
+    DecodeCtl* ctl;
+    float* logits;  // [8][64]
+    RouteTable* table;
 };
-cudaError_t launch_decode_experts(const DecodeArgs& a, cudaStream_t st);
+cudaError_t launch_decode_layer(const DecodeArgs& a, cudaStream_t st);
 
 // pack.cu
 cudaError_t launch_pack_gate_up(const void* gate, const void* up, long E, long I, long H, int esz, void* out,

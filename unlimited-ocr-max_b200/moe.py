@@ -177,7 +177,7 @@ class UocrMoE:
         ws = self._ws.get(B)
         if ws is None:
             nbytes = load().uocr_moe_decode_workspace_bytes(ctypes.byref(self.layer), B)
-            ws = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+            ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)  # the control block starts zeroed
             self._ws[B] = ws
         return ws
 
