@@ -12,8 +12,10 @@
 // The array is a file-scope __device__ variable: every GPU that loads the library holds
 // kNoAllocScratchBytes of it until the process exits. All calls on a device share it and it
 // keeps the previous call's contents, so two calls whose work overlaps on the GPU (different
-// streams without ordering between them) race on it. The status word is cleared on every
-// call; every other scratch byte a call reads is written earlier in the same call.
+// streams without ordering between them) race on it. The kernel's control counters at the
+// start of the array are zero when the library is loaded (a __device__ array is zero-filled)
+// and every call leaves them zero again; every other scratch byte a call reads is written
+// earlier in the same call.
 //
 // The first call on each device looks up the array's device address (cudaGetSymbolAddress,
 // with that device current) and caches it; that first call should come before any stream
@@ -83,6 +85,6 @@ extern "C" UOCR_API int uocr_moe_decode_noalloc(const uocr_moe_layer* L, const f
         return uocr::set_error(UOCR_ECUDA, m.c_str());
     }
     // The regular entry point with the in-library array as its workspace (it validates the
-    // layer, clears the status word, and keeps the routing in the workspace).
+    // layer and keeps the routing in the workspace).
     return uocr_moe_decode(L, x, B, bias, out, nullptr, nullptr, base, kNoAllocScratchBytes, stream);
 }
