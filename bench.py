@@ -314,7 +314,7 @@ def run_ours(args):
         v, cores, sample = CpuDecode(True, B).rate()
         cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
     if rank == 0:
-        launches_per_step = 4 * L  # route, gate/up, down, combine per layer
+        launches_per_step = L  # one fused decode kernel per layer
         line = {
             "metric": "MoE-layer tokens/s (decode, int8 routed experts, B=8)",
             "value": value,

@@ -41,20 +41,31 @@ constexpr int kUnit = 64;                              // K elements per compute
 constexpr int kPad = 68;                               // padded floats per 64-element slice
 constexpr int kMaxB = 8;
 constexpr int kRouteExperts = 8;                       // experts per ROUTE item
+constexpr int kClaim = 4;                              // items claimed per queue atomic
+constexpr int kMaxSlotsSm = 72;                        // shared (<= 8) + routed (<= 64) slots
 
 enum ItemType : int { kDone = 0, kRoute = 1, kGateUp = 2, kDown = 3 };
 
 struct ItemMeta {
-    int type, slot, block, expert, shared, count, int8, pad;
-    int pair[kMaxB];
-    int token[kMaxB];
-    float weight[kMaxB];
+    int type, slot, block, pad;
+};
+
+// Slots of this step: rows [0, S) the shared experts, [S, S+U) the routed experts.
+struct SlotTable {
+    int nslot;
+    int pad[3];
+    int expert[kMaxSlotsSm];
+    int count[kMaxSlotsSm];
+    int pair[kMaxSlotsSm][kMaxB];
+    int token[kMaxSlotsSm][kMaxB];
+    float weight[kMaxSlotsSm][kMaxB];
 };
 
 struct Smem {
     uint64_t* full;
     uint64_t* empty;
     ItemMeta* meta;
+    SlotTable* tbl;
     float* xs;     // [B][H/64][68]
     float* hs;     // [8][I/64][68]
     float* part;   // partial sums
@@ -92,11 +103,10 @@ UOCR_DEV void decode_item(const Plan& p, uint32_t i, int& type, int& slot, int& 
     type = kDown; slot = (int)(i / p.NDB); block = (int)(i % p.NDB);
 }
 
-UOCR_DEV float x_at(const float* xs, int NKX, int t, int k) { return xs[(t * NKX + k / kUnit) * kPad + (k % kUnit)]; }
-
 // ---- ROUTE -----------------------------------------------------------------------------------
 // Thread (expert j, segment s) fma-chains router row j's segment s against every token (the
-// oracle's order); segments summed in ascending order; bias added; logits to global.
+// oracle's order); segments summed in ascending order; bias added; logits to global. The last
+// ROUTE item to finish runs softmax + top-k and publishes the routing grouped by expert.
 UOCR_DEV void do_route(const DecodeArgs& a, const Smem& sm, const Plan& p, int r, int ctid) {
     const int H = a.H, B = a.B, L = H / 8, NKX = H / kUnit;
     const int jl = ctid >> 3, s = ctid & 7;  // 64 threads: 8 experts x 8 segments
@@ -137,18 +147,21 @@ UOCR_DEV void do_route(const DecodeArgs& a, const Smem& sm, const Plan& p, int r
             for (int q = 1; q < 8; ++q) total = __fadd_rn(total, sm.part[(jj * 8 + q) * kMaxB + b]);
             if (a.bias) total = __fadd_rn(total, a.bias[jg]);
             a.logits[b * 64 + jg] = total;
-            __threadfence();
         }
     }
     named_bar_sync(1, kConsumers);
-    if (ctid == 0) sm.flag[0] = (atomicAdd(&a.ctl->route_done, 1u) == (uint32_t)p.NR - 1) ? 1 : 0;
+    if (ctid == 0) {
+        __threadfence();
+        sm.flag[0] = (atomicAdd(&a.ctl->route_done, 1u) == (uint32_t)p.NR - 1) ? 1 : 0;
+    }
     named_bar_sync(1, kConsumers);
     if (!sm.flag[0]) return;
-    // the last ROUTE item: softmax + top-k per token (warp b serves token b), then the table
     __threadfence();
-    const int warp = ctid >> 5, lane = ctid & 31;
+    int* ids_s = sm.flag + 16;                               // [kB]
+    float* wts_s = reinterpret_cast<float*>(sm.flag + 16 + 64);  // [kB]
+    const int warp = ctid >> 5, lane = ctid & 31, k = a.topk, E = a.E;
     if (warp < B) {
-        const int b = warp, E = a.E, k = a.topk;
+        const int b = warp;
         const bool v0 = lane < E, v1 = lane + 32 < E;
         const float l0 = v0 ? __ldcg(a.logits + b * 64 + lane) : -INFINITY;
         const float l1 = v1 ? __ldcg(a.logits + b * 64 + lane + 32) : -INFINITY;
@@ -177,35 +190,43 @@ UOCR_DEV void do_route(const DecodeArgs& a, const Smem& sm, const Plan& p, int r
             if (lane == 0) {
                 a.ids[b * k + rr] = bi;
                 a.wts[b * k + rr] = bp;
-                sm.flag[8 + b * k + rr] = bi;  // smem copy for the table build
-                reinterpret_cast<float*>(sm.flag)[8 + kMaxB * 8 + b * k + rr] = bp;
+                ids_s[b * k + rr] = bi;
+                wts_s[b * k + rr] = bp;
             }
         }
     }
     named_bar_sync(1, kConsumers);
-    if (ctid == 0) {
-        const int kB = a.topk * B;
-        unsigned long long used = 0ull;
-        for (int q = 0; q < kB; ++q) used |= 1ull << sm.flag[8 + q];
-        RouteTable* tb = a.table;
-        int U = 0;
-        while (used) {
-            const int e = __ffsll(used) - 1;
-            used &= used - 1ull;
-            int c = 0;
+    // group by expert: thread e (< 64) owns expert e; its row is the number of used experts below it
+    const int kB = k * B;
+    int c = 0;
+    if (ctid < 64) {
+        for (int q = 0; q < kB; ++q) c += (ids_s[q] == ctid);
+        const unsigned bal = __ballot_sync(0xffffffffu, c > 0);
+        if (lane == 0) sm.flag[8 + warp] = (int)bal;
+    }
+    named_bar_sync(1, kConsumers);
+    if (ctid < 64) {
+        const unsigned long long used =
+            (unsigned long long)(unsigned)sm.flag[8] | ((unsigned long long)(unsigned)sm.flag[9] << 32);
+        if (c > 0) {
+            const int u = __popcll(used & ((1ull << ctid) - 1ull));
+            RouteTable* tb = a.table;
+            int n = 0;
             for (int q = 0; q < kB; ++q) {
-                if (sm.flag[8 + q] == e) {
-                    tb->pair[U][c] = q;
-                    tb->token[U][c] = q / a.topk;
-                    tb->weight[U][c] = reinterpret_cast<float*>(sm.flag)[8 + kMaxB * 8 + q];
-                    ++c;
+                if (ids_s[q] == ctid) {
+                    tb->pair[u][n] = q;
+                    tb->token[u][n] = q / k;
+                    tb->weight[u][n] = wts_s[q];
+                    ++n;
                 }
             }
-            tb->expert[U] = e;
-            tb->count[U] = c;
-            ++U;
+            tb->expert[u] = ctid;
+            tb->count[u] = c;
         }
-        tb->U = U;
+        if (ctid == 0) a.table->U = __popcll(used);
+    }
+    named_bar_sync(1, kConsumers);
+    if (ctid == 0) {
         __threadfence();
         st_release_gpu(&a.ctl->route_ready, 1u);
     }
@@ -213,9 +234,10 @@ UOCR_DEV void do_route(const DecodeArgs& a, const Smem& sm, const Plan& p, int r
 
 // ---- GU -----------------------------------------------------------------------------------------
 template <bool kI8>
-UOCR_DEV void gu_units(const DecodeArgs& a, const Smem& sm, const ItemMeta& m, const unsigned char* stage,
+UOCR_DEV void gu_units(const DecodeArgs& a, const Smem& sm, int slot, int block, const unsigned char* stage,
                        uint32_t row_stride, int ctid) {
-    const int H = a.H, NKX = H / kUnit, c = m.count;
+    const SlotTable& tb = *sm.tbl;
+    const int H = a.H, NKX = H / kUnit, c = tb.count[slot];
     const int units = kRB * NKX;
     for (int u = ctid; u < units; u += kConsumers) {
         const int r = u % kRB, ks = u / kRB;
@@ -233,7 +255,7 @@ UOCR_DEV void gu_units(const DecodeArgs& a, const Smem& sm, const ItemMeta& m, c
 #pragma unroll
                 for (int q = 0; q < kMaxB; ++q) {
                     if (q < c) {
-                        const float* xr = sm.xs + (m.token[q] * NKX + ks) * kPad + j * 8;
+                        const float* xr = sm.xs + (tb.token[slot][q] * NKX + ks) * kPad + j * 8;
                         const float4 xa = *reinterpret_cast<const float4*>(xr);
                         const float4 xb = *reinterpret_cast<const float4*>(xr + 4);
                         const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
@@ -261,7 +283,7 @@ UOCR_DEV void gu_units(const DecodeArgs& a, const Smem& sm, const ItemMeta& m, c
 #pragma unroll
                 for (int q = 0; q < kMaxB; ++q) {
                     if (q < c) {
-                        const float* xr = sm.xs + (m.token[q] * NKX + ks) * kPad + j * 16;
+                        const float* xr = sm.xs + (tb.token[slot][q] * NKX + ks) * kPad + j * 16;
                         float g = ag[q], v = au[q];
 #pragma unroll
                         for (int h4 = 0; h4 < 4; ++h4) {
@@ -276,11 +298,11 @@ UOCR_DEV void gu_units(const DecodeArgs& a, const Smem& sm, const ItemMeta& m, c
                     }
                 }
             }
-            // the unit lies in one quantisation group: scale the partial sums (group sum, then scale)
-            const int n = m.block * kRB + r;
+            // the unit lies in one quantisation group: scale its partial sums (group sum, then scale)
+            const int n = block * kRB + r;
             const int pg = (n / 128) * 256 + (n % 128);
             const size_t groups = (size_t)H / a.G;
-            const float* sb = a.s13 + (size_t)m.expert * 2 * a.I * groups;
+            const float* sb = a.s13 + (size_t)tb.expert[slot] * 2 * a.I * groups;
             const float sg = __ldg(sb + (size_t)pg * groups + (ks * kUnit) / a.G);
             const float su = __ldg(sb + (size_t)(pg + 128) * groups + (ks * kUnit) / a.G);
 #pragma unroll
@@ -296,34 +318,12 @@ UOCR_DEV void gu_units(const DecodeArgs& a, const Smem& sm, const ItemMeta& m, c
     }
 }
 
-UOCR_DEV void do_gate_up(const DecodeArgs& a, const Smem& sm, const ItemMeta& m, const unsigned char* stage,
-                         uint32_t row_stride, int ctid) {
-    if (m.int8)
-        gu_units<true>(a, sm, m, stage, row_stride, ctid);
-    else
-        gu_units<false>(a, sm, m, stage, row_stride, ctid);
-    named_bar_sync(1, kConsumers);
-    const int NKX = a.H / kUnit, c = m.count;
-    for (int t = ctid; t < kRB * c; t += kConsumers) {
-        const int r = t / c, q = t % c;
-        float g = sm.part[((r * NKX + 0) * kMaxB + q) * 2 + 0];
-        float u = sm.part[((r * NKX + 0) * kMaxB + q) * 2 + 1];
-        for (int ks = 1; ks < NKX; ++ks) {
-            g = __fadd_rn(g, sm.part[((r * NKX + ks) * kMaxB + q) * 2 + 0]);
-            u = __fadd_rn(u, sm.part[((r * NKX + ks) * kMaxB + q) * 2 + 1]);
-        }
-        a.h[(size_t)m.pair[q] * a.I + m.block * kRB + r] = silu(g) * u;
-        __threadfence();
-    }
-    named_bar_sync(1, kConsumers);
-    if (ctid == 0) atomicAdd(&a.ctl->gu_done[m.slot], 1u);
-}
-
 // ---- DOWN -------------------------------------------------------------------------------------
 template <bool kI8>
-UOCR_DEV void down_units(const DecodeArgs& a, const Smem& sm, const ItemMeta& m, const unsigned char* stage,
+UOCR_DEV void down_units(const DecodeArgs& a, const Smem& sm, int slot, int block, const unsigned char* stage,
                          uint32_t row_stride, int ctid) {
-    const int I = a.I, NKI = I / kUnit, c = m.count;
+    const SlotTable& tb = *sm.tbl;
+    const int I = a.I, NKI = I / kUnit, c = tb.count[slot];
     const int units = kRJ * NKI;
     for (int u = ctid; u < units; u += kConsumers) {
         const int r = u % kRJ, ks = u / kRJ;
@@ -375,9 +375,9 @@ UOCR_DEV void down_units(const DecodeArgs& a, const Smem& sm, const ItemMeta& m,
                     }
                 }
             }
-            const int jrow = m.block * kRJ + r;
+            const int jrow = block * kRJ + r;
             const size_t groups = (size_t)I / a.G;
-            const float sc = __ldg(a.s2 + ((size_t)m.expert * a.H + jrow) * groups + (ks * kUnit) / a.G);
+            const float sc = __ldg(a.s2 + ((size_t)tb.expert[slot] * a.H + jrow) * groups + (ks * kUnit) / a.G);
 #pragma unroll
             for (int q = 0; q < kMaxB; ++q) acc[q] = __fmul_rn(acc[q], sc);
         }
@@ -387,177 +387,248 @@ UOCR_DEV void down_units(const DecodeArgs& a, const Smem& sm, const ItemMeta& m,
     }
 }
 
-UOCR_DEV void do_down(const DecodeArgs& a, const Smem& sm, const Plan& p, const ItemMeta& m,
-                      const unsigned char* stage, uint32_t row_stride, int ctid) {
-    const int I = a.I, NKI = I / kUnit, c = m.count;
-    // the slot's gate/up must be complete before its h is read
-    if (ctid == 0) sm.flag[1] = wait_counter_geq(&a.ctl->gu_done[m.slot], (uint32_t)p.NGB, &a.ctl->status) ? 1 : 0;
-    named_bar_sync(1, kConsumers);
-    const bool ready = sm.flag[1] != 0;
-    if (ready) {
-        for (int i = ctid; i < c * (I / 4); i += kConsumers) {
-            const int q = i / (I / 4), k = (i % (I / 4)) * 4;
-            const float4 v = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)m.pair[q] * I + k));
-            *reinterpret_cast<float4*>(sm.hs + (q * NKI + k / kUnit) * kPad + (k % kUnit)) = v;
-        }
-    }
-    named_bar_sync(1, kConsumers);
-    if (ready) {
-        if (m.int8)
-            down_units<true>(a, sm, m, stage, row_stride, ctid);
-        else
-            down_units<false>(a, sm, m, stage, row_stride, ctid);
-    }
-    named_bar_sync(1, kConsumers);
-    if (ready) {
-        for (int t = ctid; t < kRJ * c; t += kConsumers) {
-            const int r = t / c, q = t % c;
-            float y = sm.part[(r * NKI + 0) * kMaxB + q];
-            for (int ks = 1; ks < NKI; ++ks) y = __fadd_rn(y, sm.part[(r * NKI + ks) * kMaxB + q]);
-            a.y[(size_t)m.pair[q] * a.H + m.block * kRJ + r] = y;
-            __threadfence();
-        }
-    }
-    named_bar_sync(1, kConsumers);
-    if (ctid == 0) {
-        const uint32_t done = atomicAdd(&a.ctl->j_done[m.block], 1u) + 1u;
-        int fin = 0;
-        if (wait_counter_geq(&a.ctl->route_ready, 1u, &a.ctl->status)) {
-            const int U = __ldcg(&a.table->U);
-            fin = (done == (uint32_t)(p.S + U)) ? 1 : 0;
-        }
-        sm.flag[2] = fin;
-    }
-    named_bar_sync(1, kConsumers);
-    if (!sm.flag[2]) return;
-    __threadfence();
-    const int B = a.B, k = a.topk, kB = k * B;
-    for (int t = ctid; t < kRJ * B; t += kConsumers) {
-        const int r = t % kRJ, b = t / kRJ;
-        const int j = m.block * kRJ + r;
-        float acc = 0.0f;
-        for (int s = 0; s < k; ++s) {
-            const int pr = b * k + s;
-            acc = __fmaf_rn(__ldcg(a.wts + pr), __ldcg(a.y + (size_t)pr * a.H + j), acc);
-        }
-        for (int q = 0; q < a.S; ++q) acc = __fadd_rn(acc, __ldcg(a.y + (size_t)(kB + q * B + b) * a.H + j));
-        a.out[(size_t)b * a.H + j] = acc;
-    }
-}
-
-// ---- producer -----------------------------------------------------------------------------
-UOCR_DEV bool fill_meta(const DecodeArgs& a, const Plan& p, ItemMeta& m, int type, int slot, int block,
-                        bool& route_seen) {
-    m.type = type;
-    m.slot = slot;
-    m.block = block;
-    m.int8 = 0;
-    m.count = 0;
-    if (type == kRoute) return true;
-    if (slot < p.S) {
-        m.shared = 1;
-        m.expert = slot;
-        m.count = a.B;
-        for (int t = 0; t < a.B; ++t) {
-            m.pair[t] = a.topk * a.B + slot * a.B + t;
-            m.token[t] = t;
-            m.weight[t] = 1.0f;
-        }
-        return true;
-    }
-    if (!route_seen) {
-        if (!wait_counter_geq(&a.ctl->route_ready, 1u, &a.ctl->status)) return false;
-        route_seen = true;
-    }
-    const int u = slot - p.S;
-    if (u >= __ldcg(&a.table->U)) {
-        m.type = -1;  // no such slot this step
-        return true;
-    }
-    m.shared = 0;
-    m.int8 = a.int8;
-    m.expert = __ldcg(&a.table->expert[u]);
-    m.count = __ldcg(&a.table->count[u]);
-    for (int q = 0; q < m.count; ++q) {
-        m.pair[q] = __ldcg(&a.table->pair[u][q]);
-        m.token[q] = __ldcg(&a.table->token[u][q]);
-        m.weight[q] = __ldcg(&a.table->weight[u][q]);
-    }
-    return true;
-}
-
-UOCR_DEV void producer(const DecodeArgs& a, const Smem& sm, const Plan& p, int nst, uint32_t stage_bytes,
-                       uint32_t gu_stride_b16, uint32_t gu_stride_i8, uint32_t dn_stride_b16, uint32_t dn_stride_i8,
-                       volatile int* abort_flag) {
-    bool route_seen = false;
+// ---- producer warp --------------------------------------------------------------------------
+// Lane 0 claims items kClaim at a time and drives the mbarriers; the whole warp copies the
+// routing table into shared memory once and issues the bulk copies (one weight row per lane).
+UOCR_DEV void producer_warp(const DecodeArgs& a, const Smem& sm, const Plan& p, int nst, uint32_t stage_bytes,
+                            uint32_t gu_b16, uint32_t gu_i8, uint32_t dn_b16, uint32_t dn_i8, volatile int* abort_flag) {
+    const int lane = threadIdx.x & 31;
+    bool have_table = false;
     int n = 0;
     bool ok = true;
+    uint32_t next = 0, left = 0;
     while (true) {
-        const uint32_t i = atomicAdd(&a.ctl->queue, 1u);
+        if (left == 0) {
+            uint32_t base = 0;
+            if (lane == 0) base = atomicAdd(&a.ctl->queue, (uint32_t)kClaim);
+            next = __shfl_sync(0xffffffffu, base, 0);
+            left = kClaim;
+        }
+        const uint32_t i = next++;
+        --left;
         if (i >= p.total) break;
         int type, slot, block;
         decode_item(p, i, type, slot, block);
-        ItemMeta m;
-        if (!fill_meta(a, p, m, type, slot, block, route_seen)) { ok = false; break; }
-        if (m.type < 0) continue;
+        if (type != kRoute && slot >= p.S) {
+            if (!have_table) {
+                int got = 1;
+                if (lane == 0) got = wait_counter_geq(&a.ctl->route_ready, 1u, &a.ctl->status) ? 1 : 0;
+                got = __shfl_sync(0xffffffffu, got, 0);
+                if (!got) { ok = false; break; }
+                __syncwarp();
+                const RouteTable* g = a.table;
+                const int U = __ldcg(&g->U);
+                for (int u = lane; u < U; u += 32) {
+                    const int row = p.S + u;
+                    sm.tbl->expert[row] = __ldcg(&g->expert[u]);
+                    sm.tbl->count[row] = __ldcg(&g->count[u]);
+#pragma unroll
+                    for (int q = 0; q < kMaxB; ++q) {
+                        sm.tbl->pair[row][q] = __ldcg(&g->pair[u][q]);
+                        sm.tbl->token[row][q] = __ldcg(&g->token[u][q]);
+                        sm.tbl->weight[row][q] = __ldcg(&g->weight[u][q]);
+                    }
+                }
+                if (lane == 0) sm.tbl->nslot = p.S + U;
+                __syncwarp();
+                have_table = true;
+            }
+            if (slot >= sm.tbl->nslot) continue;  // no such routed expert this step
+        }
         const int st = n % nst, round = n / nst;
-        if (round > 0 && !mbar_wait(&sm.empty[st], (round - 1) & 1, &a.ctl->status)) { ok = false; break; }
-        sm.meta[st] = m;
+        int got = 1;
+        if (lane == 0 && round > 0) got = mbar_wait(&sm.empty[st], (round - 1) & 1, &a.ctl->status) ? 1 : 0;
+        got = __shfl_sync(0xffffffffu, got, 0);
+        if (!got) { ok = false; break; }
+        if (lane == 0) {
+            sm.meta[st].type = type;
+            sm.meta[st].slot = slot;
+            sm.meta[st].block = block;
+        }
         unsigned char* dst = stage_ptr(sm, st, stage_bytes);
         if (type == kRoute) {
-            mbar_arrive(&sm.full[st]);
-        } else if (type == kGateUp) {
-            const int esz = m.int8 ? 1 : 2;
-            const uint32_t rb = (uint32_t)a.H * esz;
-            const uint32_t stride = m.int8 ? gu_stride_i8 : gu_stride_b16;
-            const unsigned char* base =
-                m.shared ? reinterpret_cast<const unsigned char*>(a.w13_shared) + (size_t)m.expert * 2 * a.I * rb
-                         : reinterpret_cast<const unsigned char*>(a.w13) + (size_t)m.expert * 2 * a.I * rb;
-            mbar_arrive_expect_tx(&sm.full[st], 2u * kRB * rb);
-            const int n0 = block * kRB;
-            const int pg0 = (n0 / 128) * 256 + (n0 % 128);
-            for (int r = 0; r < kRB; ++r) {
-                bulk_g2s(dst + (size_t)r * stride, base + (size_t)(pg0 + r) * rb, rb, &sm.full[st]);
-                bulk_g2s(dst + (size_t)(kRB + r) * stride, base + (size_t)(pg0 + 128 + r) * rb, rb, &sm.full[st]);
-            }
+            if (lane == 0) mbar_arrive(&sm.full[st]);
         } else {
-            const int esz = m.int8 ? 1 : 2;
-            const uint32_t rb = (uint32_t)a.I * esz;
-            const uint32_t stride = m.int8 ? dn_stride_i8 : dn_stride_b16;
-            const unsigned char* base =
-                m.shared ? reinterpret_cast<const unsigned char*>(a.w2_shared) + (size_t)m.expert * a.H * rb
-                         : reinterpret_cast<const unsigned char*>(a.w2) + (size_t)m.expert * a.H * rb;
-            mbar_arrive_expect_tx(&sm.full[st], (uint32_t)kRJ * rb);
-            for (int r = 0; r < kRJ; ++r)
-                bulk_g2s(dst + (size_t)r * stride, base + (size_t)(block * kRJ + r) * rb, rb, &sm.full[st]);
+            const bool shared = slot < p.S;
+            const bool i8 = !shared && a.int8;
+            const int expert = sm.tbl->expert[slot];
+            if (type == kGateUp) {
+                const uint32_t rb = (uint32_t)a.H * (i8 ? 1 : 2);
+                const uint32_t stride = i8 ? gu_i8 : gu_b16;
+                const unsigned char* base =
+                    shared ? reinterpret_cast<const unsigned char*>(a.w13_shared) + (size_t)expert * 2 * a.I * rb
+                           : reinterpret_cast<const unsigned char*>(a.w13) + (size_t)expert * 2 * a.I * rb;
+                if (lane == 0) mbar_arrive_expect_tx(&sm.full[st], 2u * kRB * rb);
+                __syncwarp();
+                const int n0 = block * kRB;
+                const int pg0 = (n0 / 128) * 256 + (n0 % 128);
+                if (lane < 2 * kRB) {
+                    const int r = lane % kRB;
+                    const int prow = pg0 + r + (lane >= kRB ? 128 : 0);
+                    bulk_g2s(dst + (size_t)lane * stride, base + (size_t)prow * rb, rb, &sm.full[st]);
+                }
+            } else {
+                const uint32_t rb = (uint32_t)a.I * (i8 ? 1 : 2);
+                const uint32_t stride = i8 ? dn_i8 : dn_b16;
+                const unsigned char* base =
+                    shared ? reinterpret_cast<const unsigned char*>(a.w2_shared) + (size_t)expert * a.H * rb
+                           : reinterpret_cast<const unsigned char*>(a.w2) + (size_t)expert * a.H * rb;
+                if (lane == 0) mbar_arrive_expect_tx(&sm.full[st], (uint32_t)kRJ * rb);
+                __syncwarp();
+                if (lane < kRJ)
+                    bulk_g2s(dst + (size_t)lane * stride, base + (size_t)(block * kRJ + lane) * rb, rb, &sm.full[st]);
+            }
         }
+        __syncwarp();
         ++n;
     }
     if (!ok) {
-        *abort_flag = 1;
-        // wait (bounded) for the copies already issued into stages the consumers will not drain
-        for (int q = max(0, n - nst); q < n; ++q) mbar_wait(&sm.full[q % nst], (q / nst) & 1, nullptr);
+        if (lane == 0) {
+            *abort_flag = 1;
+            // wait (bounded) for the copies already issued into stages the consumers may not drain
+            for (int q = max(0, n - nst); q < n; ++q) mbar_wait(&sm.full[q % nst], (q / nst) & 1, nullptr);
+        }
+        __syncwarp();
         return;
     }
-    const int st = n % nst, round = n / nst;
-    if (round > 0 && !mbar_wait(&sm.empty[st], (round - 1) & 1, &a.ctl->status)) {
-        *abort_flag = 1;
-        return;
+    if (lane == 0) {
+        const int st = n % nst, round = n / nst;
+        if (round > 0 && !mbar_wait(&sm.empty[st], (round - 1) & 1, &a.ctl->status)) {
+            *abort_flag = 1;
+        } else {
+            sm.meta[st].type = kDone;
+            mbar_arrive(&sm.full[st]);
+        }
     }
-    sm.meta[st].type = kDone;
-    mbar_arrive(&sm.full[st]);
+    __syncwarp();
+}
+
+// ---- consumers ---------------------------------------------------------------------------------
+UOCR_DEV void consumers(const DecodeArgs& a, const Smem& sm, const Plan& p, int nst, uint32_t stage_bytes,
+                        uint32_t gu_b16, uint32_t gu_i8, uint32_t dn_b16, uint32_t dn_i8, volatile int* abort_flag,
+                        int ctid) {
+    const int NKX = a.H / kUnit, NKI = a.I / kUnit, B = a.B, k = a.topk, kB = k * B;
+    const SlotTable& tb = *sm.tbl;
+    int n = 0;
+    int staged_slot = -1;
+    while (true) {
+        const int st = n % nst;
+        const uint32_t parity = (n / nst) & 1;
+        if (ctid == 0) {
+            int ok = 1;
+            const uint64_t t0 = global_timer_ns();
+            while (!mbar_try_wait(&sm.full[st], parity)) {
+                if (*abort_flag || global_timer_ns() - t0 > kWaitBudgetNs) {
+                    set_status(&a.ctl->status, kStatusWaitTimeout);
+                    ok = 0;
+                    break;
+                }
+            }
+            sm.flag[3] = ok;
+        }
+        named_bar_sync(1, kConsumers);
+        if (!sm.flag[3]) break;
+        const int type = sm.meta[st].type, slot = sm.meta[st].slot, block = sm.meta[st].block;
+        if (type == kDone) break;
+        const unsigned char* stage = stage_ptr(sm, st, stage_bytes);
+        if (type == kRoute) {
+            do_route(a, sm, p, block, ctid);
+            named_bar_sync(1, kConsumers);
+            if (ctid == 0) mbar_arrive(&sm.empty[st]);
+        } else if (type == kGateUp) {
+            const bool i8 = slot >= p.S && a.int8;
+            if (i8)
+                gu_units<true>(a, sm, slot, block, stage, gu_i8, ctid);
+            else
+                gu_units<false>(a, sm, slot, block, stage, gu_b16, ctid);
+            named_bar_sync(1, kConsumers);
+            if (ctid == 0) mbar_arrive(&sm.empty[st]);  // stage consumed
+            const int c = tb.count[slot];
+            for (int t = ctid; t < kRB * c; t += kConsumers) {
+                const int r = t / c, q = t % c;
+                float g = sm.part[((r * NKX + 0) * kMaxB + q) * 2 + 0];
+                float u = sm.part[((r * NKX + 0) * kMaxB + q) * 2 + 1];
+                for (int ks = 1; ks < NKX; ++ks) {
+                    g = __fadd_rn(g, sm.part[((r * NKX + ks) * kMaxB + q) * 2 + 0]);
+                    u = __fadd_rn(u, sm.part[((r * NKX + ks) * kMaxB + q) * 2 + 1]);
+                }
+                a.h[(size_t)tb.pair[slot][q] * a.I + block * kRB + r] = silu(g) * u;
+            }
+            named_bar_sync(1, kConsumers);
+            if (ctid == 0) {
+                __threadfence();
+                atomicAdd(&a.ctl->gu_done[slot], 1u);
+            }
+        } else {
+            const int c = tb.count[slot];
+            if (slot != staged_slot) {
+                // the slot's gate/up must be complete before its h is read (one waiter per warp)
+                if ((ctid & 31) == 0) {
+                    if (!wait_counter_geq(&a.ctl->gu_done[slot], (uint32_t)p.NGB, &a.ctl->status)) *abort_flag = 1;
+                }
+                __syncwarp();
+                for (int i = ctid; i < c * (a.I / 4); i += kConsumers) {
+                    const int q = i / (a.I / 4), kk = (i % (a.I / 4)) * 4;
+                    const float4 v = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)tb.pair[slot][q] * a.I + kk));
+                    *reinterpret_cast<float4*>(sm.hs + (q * NKI + kk / kUnit) * kPad + (kk % kUnit)) = v;
+                }
+                named_bar_sync(1, kConsumers);
+                staged_slot = slot;
+            }
+            const bool i8 = slot >= p.S && a.int8;
+            if (i8)
+                down_units<true>(a, sm, slot, block, stage, dn_i8, ctid);
+            else
+                down_units<false>(a, sm, slot, block, stage, dn_b16, ctid);
+            named_bar_sync(1, kConsumers);
+            if (ctid == 0) mbar_arrive(&sm.empty[st]);
+            for (int t = ctid; t < kRJ * c; t += kConsumers) {
+                const int r = t / c, q = t % c;
+                float y = sm.part[(r * NKI + 0) * kMaxB + q];
+                for (int ks = 1; ks < NKI; ++ks) y = __fadd_rn(y, sm.part[(r * NKI + ks) * kMaxB + q]);
+                a.y[(size_t)tb.pair[slot][q] * a.H + block * kRJ + r] = y;
+            }
+            named_bar_sync(1, kConsumers);
+            if (ctid == 0) {
+                __threadfence();
+                const uint32_t done = atomicAdd(&a.ctl->j_done[block], 1u) + 1u;
+                int fin = 0;
+                if (wait_counter_geq(&a.ctl->route_ready, 1u, &a.ctl->status))
+                    fin = (done == (uint32_t)(p.S + __ldcg(&a.table->U))) ? 1 : 0;
+                sm.flag[2] = fin;
+                if (fin) __threadfence();
+            }
+            named_bar_sync(1, kConsumers);
+            if (sm.flag[2]) {
+                // the last DOWN item of this output block: out = sum_s w y_routed + sum_q y_shared
+                for (int t = ctid; t < kRJ * B; t += kConsumers) {
+                    const int r = t % kRJ, b = t / kRJ;
+                    const int j = block * kRJ + r;
+                    float acc = 0.0f;
+                    for (int s = 0; s < k; ++s) {
+                        const int pr = b * k + s;
+                        acc = __fmaf_rn(__ldcg(a.wts + pr), __ldcg(a.y + (size_t)pr * a.H + j), acc);
+                    }
+                    for (int q = 0; q < a.S; ++q) acc = __fadd_rn(acc, __ldcg(a.y + (size_t)(kB + q * B + b) * a.H + j));
+                    a.out[(size_t)b * a.H + j] = acc;
+                }
+            }
+        }
+        ++n;
+    }
 }
 
 // ---- the kernel ---------------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads, 1)
-decode_layer_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_meta, uint32_t off_xs, uint32_t off_hs,
-                    uint32_t off_part, uint32_t off_flag, uint32_t off_stages) {
+decode_layer_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_meta, uint32_t off_tbl, uint32_t off_xs,
+                    uint32_t off_hs, uint32_t off_part, uint32_t off_flag, uint32_t off_stages) {
     extern __shared__ __align__(1024) unsigned char smem[];
     __shared__ int abort_flag;
     Smem sm;
     sm.full = reinterpret_cast<uint64_t*>(smem);
     sm.empty = sm.full + nst;
     sm.meta = reinterpret_cast<ItemMeta*>(smem + off_meta);
+    sm.tbl = reinterpret_cast<SlotTable*>(smem + off_tbl);
     sm.xs = reinterpret_cast<float*>(smem + off_xs);
     sm.hs = reinterpret_cast<float*>(smem + off_hs);
     sm.part = reinterpret_cast<float*>(smem + off_part);
@@ -573,6 +644,16 @@ decode_layer_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_me
         abort_flag = 0;
         fence_mbar_init();
     }
+    // shared-expert slots are known before routing
+    if (tid < a.S) {
+        sm.tbl->expert[tid] = tid;
+        sm.tbl->count[tid] = a.B;
+        for (int t = 0; t < kMaxB; ++t) {
+            sm.tbl->pair[tid][t] = a.topk * a.B + tid * a.B + t;
+            sm.tbl->token[tid][t] = t;
+            sm.tbl->weight[tid][t] = 1.0f;
+        }
+    }
     // stage the tokens: xs[b][k/64][k%64]
     const int NKX = a.H / kUnit;
     for (int i = tid; i < a.B * (a.H / 4); i += kThreads) {
@@ -584,46 +665,10 @@ decode_layer_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_me
 
     const uint32_t gu_b16 = (uint32_t)a.H * 2 + 16, gu_i8 = (uint32_t)a.H + 16;
     const uint32_t dn_b16 = (uint32_t)a.I * 2 + 16, dn_i8 = (uint32_t)a.I + 16;
-    if (tid >= kConsumers) {
-        if (tid == kConsumers) producer(a, sm, p, nst, stage_bytes, gu_b16, gu_i8, dn_b16, dn_i8, &abort_flag);
-        __syncwarp();
-    } else {
-        const int ctid = tid;
-        int n = 0;
-        while (true) {
-            const int st = n % nst;
-            const uint32_t parity = (n / nst) & 1;
-            // bounded wait that also gives up when the producer aborted
-            if (ctid == 0) {
-                int ok = 1;
-                const uint64_t t0 = global_timer_ns();
-                while (!mbar_try_wait(&sm.full[st], parity)) {
-                    if (*reinterpret_cast<volatile int*>(&abort_flag) ||
-                        global_timer_ns() - t0 > kWaitBudgetNs) {
-                        set_status(&a.ctl->status, kStatusWaitTimeout);
-                        ok = 0;
-                        break;
-                    }
-                }
-                sm.flag[3] = ok;
-            }
-            named_bar_sync(1, kConsumers);
-            if (!sm.flag[3]) break;
-            const ItemMeta& m = sm.meta[st];
-            if (m.type == kDone) break;
-            const unsigned char* stage = stage_ptr(sm, st, stage_bytes);
-            if (m.type == kRoute) {
-                do_route(a, sm, p, m.block, ctid);
-            } else if (m.type == kGateUp) {
-                do_gate_up(a, sm, m, stage, m.int8 ? gu_i8 : gu_b16, ctid);
-            } else {
-                do_down(a, sm, p, m, stage, m.int8 ? dn_i8 : dn_b16, ctid);
-            }
-            named_bar_sync(1, kConsumers);
-            if (ctid == 0) mbar_arrive(&sm.empty[st]);
-            ++n;
-        }
-    }
+    if (tid >= kConsumers)
+        producer_warp(a, sm, p, nst, stage_bytes, gu_b16, gu_i8, dn_b16, dn_i8, &abort_flag);
+    else
+        consumers(a, sm, p, nst, stage_bytes, gu_b16, gu_i8, dn_b16, dn_i8, &abort_flag, tid);
     __syncthreads();
     if (tid == 0) {
         __threadfence();
@@ -647,45 +692,42 @@ static size_t up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 cudaError_t launch_decode_layer(const DecodeArgs& a, cudaStream_t st) {
     const int NKX = a.H / kUnit, NKI = a.I / kUnit;
     const uint32_t gu_stage_b16 = 2u * kRB * ((uint32_t)a.H * 2 + 16);
-    const uint32_t gu_stage_i8 = 2u * kRB * ((uint32_t)a.H + 16);
     const uint32_t dn_stage_b16 = (uint32_t)kRJ * ((uint32_t)a.I * 2 + 16);
-    const uint32_t dn_stage_i8 = (uint32_t)kRJ * ((uint32_t)a.I + 16);
     // shared experts are always bf16, so a stage must hold a bf16 item
-    uint32_t stage_bytes = max(max(gu_stage_b16, dn_stage_b16), max(gu_stage_i8, dn_stage_i8));
-    stage_bytes = (uint32_t)up(stage_bytes, 128);
+    const uint32_t stage_bytes = (uint32_t)up(std::max(gu_stage_b16, dn_stage_b16), 128);
     const size_t xs_bytes = sizeof(float) * (size_t)a.B * NKX * kPad;
-    const size_t hs_bytes = sizeof(float) * (size_t)kMaxB * NKI * kPad;
-    const size_t part_bytes =
-        sizeof(float) * max((size_t)kRB * NKX * kMaxB * 2, max((size_t)kRJ * NKI * kMaxB, (size_t)64 * 8 * kMaxB));
-    const size_t flag_bytes = sizeof(int) * (8 + 2 * kMaxB * 8 + 8);
+    const size_t hs_bytes = sizeof(float) * (size_t)a.B * NKI * kPad;
+    const size_t part_bytes = sizeof(float) * std::max((size_t)kRB * NKX * kMaxB * 2,
+                                                       std::max((size_t)kRJ * NKI * kMaxB, (size_t)64 * 8 * kMaxB));
+    const size_t flag_bytes = sizeof(int) * (16 + 64 + 64);
     int dev = 0, max_smem = 0, sms = 0;
     cudaError_t err = cudaGetDevice(&dev);
     if (err != cudaSuccess) return err;
     cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const int kMaxStages = 8;
-    size_t fixed = up(16 * kMaxStages, 128) + up(sizeof(ItemMeta) * kMaxStages, 128) + up(xs_bytes, 128) +
-                   up(hs_bytes, 128) + up(part_bytes, 128) + up(flag_bytes, 128) + 1024;
-    int nst = (int)std::min<size_t>(kMaxStages, ((size_t)max_smem - fixed) / stage_bytes);
+    const size_t fixed = up(16 * kMaxStages, 128) + up(sizeof(ItemMeta) * kMaxStages, 128) + up(sizeof(SlotTable), 128) +
+                         up(xs_bytes, 128) + up(hs_bytes, 128) + up(part_bytes, 128) + up(flag_bytes, 128) + 2048;
+    const int nst = (int)std::min<size_t>(kMaxStages, ((size_t)max_smem - fixed) / stage_bytes);
     if (nst < 2) return cudaErrorInvalidConfiguration;
-    size_t off = 0;
-    off += up(16 * (size_t)nst, 128);
+    size_t off = up(16 * (size_t)nst, 128);
     const size_t off_meta = off; off += up(sizeof(ItemMeta) * nst, 128);
+    const size_t off_tbl = off; off += up(sizeof(SlotTable), 128);
     const size_t off_xs = off; off += up(xs_bytes, 128);
     const size_t off_hs = off; off += up(hs_bytes, 128);
     const size_t off_part = off; off += up(part_bytes, 128);
     const size_t off_flag = off; off += up(flag_bytes, 128);
-    const size_t off_stages = up(off, 1024); off = off_stages + (size_t)nst * stage_bytes;
-    const size_t smem = off;
+    const size_t off_stages = up(off, 1024);
+    const size_t smem = off_stages + (size_t)nst * stage_bytes;
     err = ensure_smem_optin(reinterpret_cast<const void*>(decode_layer_kernel), smem);
     if (err != cudaSuccess) return err;
     const int NR = (a.E + kRouteExperts - 1) / kRouteExperts;
-    const int MR = min(a.E, a.topk * a.B);
+    const int MR = std::min(a.E, a.topk * a.B);
     const long total = NR + (long)(a.S + MR) * (a.I / kRB + a.H / kRJ);
-    const int grid = (int)std::min<long>(total, (long)sms);
-    decode_layer_kernel<<<grid, kThreads, smem, st>>>(a, nst, stage_bytes, (uint32_t)off_meta, (uint32_t)off_xs,
-                                                     (uint32_t)off_hs, (uint32_t)off_part, (uint32_t)off_flag,
-                                                     (uint32_t)off_stages);
+    const int grid = (int)std::min<long>((total + kClaim - 1) / kClaim, (long)sms);
+    decode_layer_kernel<<<grid, kThreads, smem, st>>>(a, nst, stage_bytes, (uint32_t)off_meta, (uint32_t)off_tbl,
+                                                     (uint32_t)off_xs, (uint32_t)off_hs, (uint32_t)off_part,
+                                                     (uint32_t)off_flag, (uint32_t)off_stages);
     return cudaGetLastError();
 }
 
