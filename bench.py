@@ -50,6 +50,8 @@ def parse():
     p.add_argument("--layers", type=int, default=11)
     p.add_argument("--no-sub", action="store_true", help="skip the ride-along sub-configs")
     p.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    p.add_argument("--settle", type=float, default=1.5,
+                   help="seconds of untimed replays before timing, while the clock sampler runs")
     return p.parse_args()
 
 
@@ -284,7 +286,8 @@ def run_ours(args):
 
     mods, xs, outs, ids, wts = build_stack(uocr, synth, True, L, B, device, 1000)
     sampler = ClockSampler(physical_gpu_index(local))
-    g, ms, clocks = time_stack(torch, mods, xs, outs, ids, wts, args.steps, args.warmup, dist, sampler, settle_s=1.5)
+    g, ms, clocks = time_stack(torch, mods, xs, outs, ids, wts, args.steps, args.warmup, dist, sampler,
+                                settle_s=args.settle)
     step_bytes = algorithmic_bytes(torch, ids, True, B)
     peak, peak_src = measured_peaks()
     achieved = step_bytes / (ms * 1e-3) / 1e9
