@@ -90,13 +90,12 @@ UOCR_DEV Plan make_plan(const DecodeArgs& a) {
     p.NDB = a.H / kRJ;
     p.MR = min(a.E, a.topk * a.B);
     p.S = a.S;
-    p.total = (uint32_t)(p.NR + (p.S + p.MR) * (p.NGB + p.NDB));
+    p.total = (uint32_t)((p.S + p.MR) * (p.NGB + p.NDB));
     return p;
 }
 
+// Main-queue item i (the ROUTE items have their own counter, one per claim).
 UOCR_DEV void decode_item(const Plan& p, uint32_t i, int& type, int& slot, int& block) {
-    if (i < (uint32_t)p.NR) { type = kRoute; slot = 0; block = (int)i; return; }
-    i -= p.NR;
     const uint32_t gu = (uint32_t)(p.S + p.MR) * p.NGB;
     if (i < gu) { type = kGateUp; slot = (int)(i / p.NGB); block = (int)(i % p.NGB); return; }
     i -= gu;
@@ -107,36 +106,42 @@ UOCR_DEV void decode_item(const Plan& p, uint32_t i, int& type, int& slot, int& 
 // Thread (expert j, segment s) fma-chains router row j's segment s against every token (the
 // oracle's order); segments summed in ascending order; bias added; logits to global. The last
 // ROUTE item to finish runs softmax + top-k and publishes the routing grouped by expert.
-UOCR_DEV void do_route(const DecodeArgs& a, const Smem& sm, const Plan& p, int r, int ctid) {
+UOCR_DEV void do_route(const DecodeArgs& a, const Smem& sm, const Plan& p, int r, const unsigned char* stage,
+                      uint32_t row_stride, int ctid) {
     const int H = a.H, B = a.B, L = H / 8, NKX = H / kUnit;
-    const int jl = ctid >> 3, s = ctid & 7;  // 64 threads: 8 experts x 8 segments
+    // thread (token group tg, expert jl, segment s): router row jl (staged) segment s against
+    // tokens tg*TPG .. tg*TPG+TPG-1
+    const int tg = ctid >> 6, jl = (ctid >> 3) & 7, s = ctid & 7;
+    const int TPG = (B + 3) / 4;
     const int j = r * kRouteExperts + jl;
-    if (ctid < 64 && j < a.E) {
-        float acc[kMaxB];
-#pragma unroll
-        for (int b = 0; b < kMaxB; ++b) acc[b] = 0.0f;
-        const uint16_t* wrow = a.router + (size_t)j * H + s * L;
+    if (j < a.E && tg * TPG < B) {
+        float acc[2] = {0.0f, 0.0f};
+        const uint16_t* wrow = reinterpret_cast<const uint16_t*>(stage + (size_t)jl * row_stride) + s * L;
         for (int kk = 0; kk < L; kk += 8) {
             float wf[8];
             unpack_bf16x8(*reinterpret_cast<const uint4*>(wrow + kk), wf);
             const int k0 = s * L + kk;
 #pragma unroll
-            for (int b = 0; b < kMaxB; ++b) {
-                if (b < B) {
+            for (int bb = 0; bb < 2; ++bb) {
+                const int b = tg * TPG + bb;
+                if (bb < TPG && b < B) {
                     const float* xr = sm.xs + (b * NKX + k0 / kUnit) * kPad + (k0 % kUnit);  // 8 | 64: no straddle
                     const float4 xa = *reinterpret_cast<const float4*>(xr);
                     const float4 xb = *reinterpret_cast<const float4*>(xr + 4);
-                    float v = acc[b];
+                    float v = acc[bb];
                     v = __fmaf_rn(wf[0], xa.x, v); v = __fmaf_rn(wf[1], xa.y, v);
                     v = __fmaf_rn(wf[2], xa.z, v); v = __fmaf_rn(wf[3], xa.w, v);
                     v = __fmaf_rn(wf[4], xb.x, v); v = __fmaf_rn(wf[5], xb.y, v);
                     v = __fmaf_rn(wf[6], xb.z, v); v = __fmaf_rn(wf[7], xb.w, v);
-                    acc[b] = v;
+                    acc[bb] = v;
                 }
             }
         }
 #pragma unroll
-        for (int b = 0; b < kMaxB; ++b) sm.part[(jl * 8 + s) * kMaxB + b] = acc[b];
+        for (int bb = 0; bb < 2; ++bb) {
+            const int b = tg * TPG + bb;
+            if (bb < TPG && b < B) sm.part[(jl * 8 + s) * kMaxB + b] = acc[bb];
+        }
     }
     named_bar_sync(1, kConsumers);
     if (ctid < kRouteExperts * B) {
@@ -397,18 +402,31 @@ UOCR_DEV void producer_warp(const DecodeArgs& a, const Smem& sm, const Plan& p, 
     int n = 0;
     bool ok = true;
     uint32_t next = 0, left = 0;
+    bool routes_left = true;
     while (true) {
-        if (left == 0) {
-            uint32_t base = 0;
-            if (lane == 0) base = atomicAdd(&a.ctl->queue, (uint32_t)kClaim);
-            next = __shfl_sync(0xffffffffu, base, 0);
-            left = kClaim;
+        int type = kRoute, slot = 0, block = 0;
+        if (routes_left) {
+            uint32_t r = 0;
+            if (lane == 0) r = atomicAdd(&a.ctl->route_q, 1u);
+            r = __shfl_sync(0xffffffffu, r, 0);
+            if (r < (uint32_t)p.NR) {
+                block = (int)r;
+            } else {
+                routes_left = false;
+            }
         }
-        const uint32_t i = next++;
-        --left;
-        if (i >= p.total) break;
-        int type, slot, block;
-        decode_item(p, i, type, slot, block);
+        if (!routes_left) {
+            if (left == 0) {
+                uint32_t base = 0;
+                if (lane == 0) base = atomicAdd(&a.ctl->queue, (uint32_t)kClaim);
+                next = __shfl_sync(0xffffffffu, base, 0);
+                left = kClaim;
+            }
+            const uint32_t i = next++;
+            --left;
+            if (i >= p.total) break;
+            decode_item(p, i, type, slot, block);
+        }
         if (type != kRoute && slot >= p.S) {
             if (!have_table) {
                 int got = 1;
@@ -447,7 +465,15 @@ UOCR_DEV void producer_warp(const DecodeArgs& a, const Smem& sm, const Plan& p, 
         }
         unsigned char* dst = stage_ptr(sm, st, stage_bytes);
         if (type == kRoute) {
-            if (lane == 0) mbar_arrive(&sm.full[st]);
+            // the ROUTE item's router rows
+            const uint32_t rb = (uint32_t)a.H * 2;
+            const int j0 = block * kRouteExperts;
+            const int nrow = min(kRouteExperts, a.E - j0);
+            if (lane == 0) mbar_arrive_expect_tx(&sm.full[st], (uint32_t)nrow * rb);
+            __syncwarp();
+            if (lane < nrow)
+                bulk_g2s(dst + (size_t)lane * gu_b16, reinterpret_cast<const unsigned char*>(a.router) + (size_t)(j0 + lane) * rb,
+                         rb, &sm.full[st]);
         } else {
             const bool shared = slot < p.S;
             const bool i8 = !shared && a.int8;
@@ -532,7 +558,7 @@ UOCR_DEV void consumers(const DecodeArgs& a, const Smem& sm, const Plan& p, int 
         if (type == kDone) break;
         const unsigned char* stage = stage_ptr(sm, st, stage_bytes);
         if (type == kRoute) {
-            do_route(a, sm, p, block, ctid);
+            do_route(a, sm, p, block, stage, gu_b16, ctid);
             named_bar_sync(1, kConsumers);
             if (ctid == 0) mbar_arrive(&sm.empty[st]);
         } else if (type == kGateUp) {
@@ -563,10 +589,10 @@ UOCR_DEV void consumers(const DecodeArgs& a, const Smem& sm, const Plan& p, int 
             const int c = tb.count[slot];
             if (slot != staged_slot) {
                 // the slot's gate/up must be complete before its h is read (one waiter per warp)
-                if ((ctid & 31) == 0) {
+                if (ctid == 0) {
                     if (!wait_counter_geq(&a.ctl->gu_done[slot], (uint32_t)p.NGB, &a.ctl->status)) *abort_flag = 1;
                 }
-                __syncwarp();
+                named_bar_sync(1, kConsumers);
                 for (int i = ctid; i < c * (a.I / 4); i += kConsumers) {
                     const int q = i / (a.I / 4), kk = (i % (a.I / 4)) * 4;
                     const float4 v = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)tb.pair[slot][q] * a.I + kk));
@@ -678,6 +704,7 @@ decode_layer_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_me
             a.ctl->queue = 0;
             a.ctl->route_done = 0;
             a.ctl->route_ready = 0;
+            a.ctl->route_q = 0;
             for (int s = 0; s < p.S + p.MR; ++s) a.ctl->gu_done[s] = 0;
             for (int j = 0; j < p.NDB; ++j) a.ctl->j_done[j] = 0;
             __threadfence();
@@ -723,8 +750,8 @@ cudaError_t launch_decode_layer(const DecodeArgs& a, cudaStream_t st) {
     if (err != cudaSuccess) return err;
     const int NR = (a.E + kRouteExperts - 1) / kRouteExperts;
     const int MR = std::min(a.E, a.topk * a.B);
-    const long total = NR + (long)(a.S + MR) * (a.I / kRB + a.H / kRJ);
-    const int grid = (int)std::min<long>((total + kClaim - 1) / kClaim, (long)sms);
+    const long total = (long)(a.S + MR) * (a.I / kRB + a.H / kRJ);
+    const int grid = (int)std::min<long>(NR + (total + kClaim - 1) / kClaim, (long)sms);
     decode_layer_kernel<<<grid, kThreads, smem, st>>>(a, nst, stage_bytes, (uint32_t)off_meta, (uint32_t)off_tbl,
                                                      (uint32_t)off_xs, (uint32_t)off_hs, (uint32_t)off_part,
                                                      (uint32_t)off_flag, (uint32_t)off_stages);
