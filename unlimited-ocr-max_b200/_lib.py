@@ -57,6 +57,7 @@ SIGNATURES: dict[str, tuple] = {
     "uocr_moe_decode_workspace_bytes": (SZ, [ctypes.POINTER(UocrMoeLayer), I64]),
     "uocr_moe_decode": (I32, [ctypes.POINTER(UocrMoeLayer), P, I64, P, P, P, P, P, SZ, P]),
     "uocr_moe_device_status": (I32, [P, P]),
+    "uocr_moe_decode_set_trace": (I32, [P, SZ]),
     "uocr_moe_decode_noalloc_max_bytes": (SZ, []),
     "uocr_moe_decode_noalloc": (I32, [ctypes.POINTER(UocrMoeLayer), P, I64, P, P, P]),
 }

@@ -44,6 +44,9 @@ bool a16(const void* p) { return uocr::aligned16(p); }
 
 namespace uocr {
 
+unsigned long long* g_decode_trace = nullptr;
+size_t g_decode_trace_bytes = 0;
+
 int set_error(int code, const char* msg) {
     g_last_error = msg;
     return code;
@@ -302,6 +305,12 @@ int uocr_moe_decode(const uocr_moe_layer* L, const float* x, int64_t B, const fl
     a.logits = reinterpret_cast<float*>(ws + d.logits);
     a.table = reinterpret_cast<uocr::RouteTable*>(ws + d.table);
     return cuda_status(uocr::launch_decode_layer(a, S(stream)), "moe_decode: launch");
+}
+
+int uocr_moe_decode_set_trace(void* device_buffer, size_t bytes) {
+    uocr::g_decode_trace = reinterpret_cast<unsigned long long*>(device_buffer);
+    uocr::g_decode_trace_bytes = device_buffer ? bytes : 0;
+    return ok();
 }
 
 int uocr_moe_device_status(const void* workspace, uocr_stream_t stream) {

@@ -537,12 +537,14 @@ UOCR_DEV void consumers(const DecodeArgs& a, const Smem& sm, const Plan& p, int 
     const SlotTable& tb = *sm.tbl;
     int n = 0;
     int staged_slot = -1;
+    unsigned long long* tr = a.trace ? a.trace + (size_t)blockIdx.x * a.trace_items * 4 : nullptr;
     while (true) {
         const int st = n % nst;
         const uint32_t parity = (n / nst) & 1;
         if (ctid == 0) {
             int ok = 1;
             const uint64_t t0 = global_timer_ns();
+            if (tr && n < a.trace_items) tr[n * 4 + 0] = t0;
             while (!mbar_try_wait(&sm.full[st], parity)) {
                 if (*abort_flag || global_timer_ns() - t0 > kWaitBudgetNs) {
                     set_status(&a.ctl->status, kStatusWaitTimeout);
@@ -551,6 +553,11 @@ UOCR_DEV void consumers(const DecodeArgs& a, const Smem& sm, const Plan& p, int 
                 }
             }
             sm.flag[3] = ok;
+            if (tr && n < a.trace_items) {
+                tr[n * 4 + 1] = global_timer_ns();
+                tr[n * 4 + 3] = ((unsigned long long)sm.meta[st].type << 48) | ((unsigned long long)sm.meta[st].slot << 24) |
+                                (unsigned long long)sm.meta[st].block;
+            }
         }
         named_bar_sync(1, kConsumers);
         if (!sm.flag[3]) break;
@@ -640,6 +647,7 @@ UOCR_DEV void consumers(const DecodeArgs& a, const Smem& sm, const Plan& p, int 
                 }
             }
         }
+        if (ctid == 0 && tr && n < a.trace_items) tr[n * 4 + 2] = global_timer_ns();
         ++n;
     }
 }
@@ -752,7 +760,12 @@ cudaError_t launch_decode_layer(const DecodeArgs& a, cudaStream_t st) {
     const int MR = std::min(a.E, a.topk * a.B);
     const long total = (long)(a.S + MR) * (a.I / kRB + a.H / kRJ);
     const int grid = (int)std::min<long>(NR + (total + kClaim - 1) / kClaim, (long)sms);
-    decode_layer_kernel<<<grid, kThreads, smem, st>>>(a, nst, stage_bytes, (uint32_t)off_meta, (uint32_t)off_tbl,
+    DecodeArgs args = a;
+    if (g_decode_trace) {
+        args.trace = g_decode_trace;
+        args.trace_items = (int)(g_decode_trace_bytes / (sizeof(unsigned long long) * 4 * (size_t)grid));
+    }
+    decode_layer_kernel<<<grid, kThreads, smem, st>>>(args, nst, stage_bytes, (uint32_t)off_meta, (uint32_t)off_tbl,
                                                      (uint32_t)off_xs, (uint32_t)off_hs, (uint32_t)off_part,
                                                      (uint32_t)off_flag, (uint32_t)off_stages);
     return cudaGetLastError();

@@ -64,7 +64,12 @@ struct DecodeArgs {
     DecodeCtl* ctl;
     float* logits;  // [8][64]
     RouteTable* table;
+    unsigned long long* trace;  // optional per-CTA item timeline (diagnostics), null = off
+    int trace_items;            // items recorded per CTA
 };
+// diagnostics: the trace buffer the next decode launches record into (capi.cu)
+extern unsigned long long* g_decode_trace;
+extern size_t g_decode_trace_bytes;
 cudaError_t launch_decode_layer(const DecodeArgs& a, cudaStream_t st);
 
 // pack.cu
