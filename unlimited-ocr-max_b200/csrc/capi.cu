@@ -279,9 +279,10 @@ int uocr_moe_decode(const uocr_moe_layer* L, const float* x, int64_t B, const fl
     int rc = check_layer(L, "moe_decode");
     if (rc) return rc;
     if (B < 1 || B > 8) return fail(UOCR_EINVAL, "moe_decode: B=%lld outside 1..8 (use moe_prefill)", (long long)B);
-    if (L->n_shared > 64 || L->n_shared + std::min<int64_t>(L->n_routed, L->top_k * B) > uocr::kDecodeMaxSlots)
-        return fail(UOCR_EUNSUPPORTED, "moe_decode: too many expert slots");
-    if (L->hidden / 16 > uocr::kDecodeMaxJBlocks) return fail(UOCR_EUNSUPPORTED, "moe_decode: hidden above 8192");
+    if (L->n_shared > uocr::kDecodeMaxShared) return fail(UOCR_EUNSUPPORTED, "moe_decode: more than 8 shared experts");
+    if (L->hidden % 128 || L->inter % 128)
+        return fail(UOCR_EUNSUPPORTED, "moe_decode: hidden and inter must be multiples of 128");
+    if (L->hidden > 8192 || L->inter > 8192) return fail(UOCR_EUNSUPPORTED, "moe_decode: hidden/inter above 8192");
     if (!x || !out || !workspace) return fail(UOCR_EINVAL, "moe_decode: null pointer");
     if (!a16(x) || !a16(out)) return fail(UOCR_EINVAL, "moe_decode: x and out must be 16-byte aligned");
     if (bias && (reinterpret_cast<uintptr_t>(bias) & 3)) return fail(UOCR_EINVAL, "moe_decode: bias must be 4-byte aligned");

@@ -1,29 +1,28 @@
 // Decode-step MoE sublayer (MoE.decode_rows, unlimited_ocr_max/decoder.py:641-655) for B <= 8
-// tokens, as ONE persistent kernel per layer. HBM-bound: the job is to stream the touched
-// experts' weights at full bandwidth, once each.
+// tokens: three kernels chained by programmatic dependent launch (PDL), each streaming its
+// weights from HBM once.
 //
-// Pairs. Routed (token t, slot s) is pair t*k + s; shared expert q's copy of token t is pair
-// k*B + q*B + t. Expert slots: 0..S-1 are the shared experts, S+u is the u-th distinct routed
-// expert in ascending id (the reference's rows-grouped-by-expert, kernels/moe_routing.mojo).
+//   K1 route   8 CTAs x 8 experts: fp32 router logits in the oracle's order, then the last
+//              CTA runs softmax + top-k (bit-exact) and groups the routing by expert
+//              ("slots": 0..S-1 the shared experts, S+u the u-th distinct routed expert in
+//              ascending id; each slot lists its (pair, token, weight) entries).
+//   K2 gate/up persistent: items (slot, rows, token group) -> h[pair][n] = silu(g) * u.
+//   K3 down    CTA b owns output rows [b*H/G, (b+1)*H/G); it walks every slot, computes
+//              y[slot][token][row] and finishes with the routing-weighted combine
+//              out[t][j] = sum over t's slots in order of (w * y or y), no cross-CTA state.
+// Pairs: routed (token t, slot s) is pair t*k + s; shared expert q's copy of token t is pair
+// k*B + q*B + t. A pair's arithmetic uses only its own token and expert and a token's slots are
+// summed in ascending order, so every output row is bitwise independent of the batch.
 //
-// Work items, claimed in this order from an atomic queue (so an item only ever waits for
-// items claimed before it, which are already running: no deadlock at any grid size):
-//   ROUTE r   logits of experts [8r, 8r+8) for all B tokens; the last ROUTE item runs the
-//             softmax + top-k (bit-exact with the oracle) and publishes the routing table;
-//   GU        (slot, 8 intermediate rows): gate and up rows of the slot's expert, SwiGLU,
-//             h[pair][n] for every pair on that expert -- each weight row read once;
-//   DOWN      (slot, 16 output rows): y[pair][j] = Wd[e][j] . h[pair]; the last DOWN item of
-//             an output block (all S + U slots done) combines
-//             out[t][j] = sum_s w[t,s] y[t*k+s][j] + sum_q y_shared[q][t][j]   (fixed order).
-// A warp-specialised CTA: one producer warp claims items and streams each item's weight rows
-// with cp.async.bulk into a ring of shared-memory stages (mbarrier full/empty pairs); eight
-// consumer warps compute from shared memory. A pair's arithmetic uses only its own token and
-// expert, so every output row is bitwise independent of the batch it rides in.
+// K2 and K3 are warp-specialised: one producer warp streams each work item's bytes (weight
+// rows, int8 scales, and for K3 the pairs' h rows) with cp.async.bulk into a ring of shared-
+// memory stages guarded by full/empty mbarriers; each of the 8 consumer warps owns whole
+// items, so an SM keeps up to 8 items in flight with no CTA-wide barrier per item. Stage s is
+// always consumed by warp s % 8 (the stage count is a multiple of 8), so a warp never waits on
+// an mbarrier phase more than one round ahead of the last one it saw.
 //
-// Every device-side wait is bounded (sm100.cuh: kWaitBudgetNs): on expiry it records a
-// status code in the workspace and the kernel winds down. The control counters reset
-// themselves at the end of each launch (the last CTA to finish clears them), so a
-// zero-filled workspace stays valid across calls.
+// Every device-side wait is bounded (sm100.cuh, kWaitBudgetNs): on expiry the waiter records a
+// status code in the workspace and the kernel winds down without writing its output.
 #include <algorithm>
 
 #include "common.cuh"
@@ -32,25 +31,15 @@
 
 namespace uocr {
 
-constexpr int kConsumerWarps = 8;
-constexpr int kConsumers = kConsumerWarps * 32;       // 256
-constexpr int kThreads = kConsumers + 32;              // + producer warp
-constexpr int kRB = 8;                                 // intermediate rows per GU item
-constexpr int kRJ = 16;                                // output rows per DOWN item
-constexpr int kUnit = 64;                              // K elements per compute unit
-constexpr int kPad = 68;                               // padded floats per 64-element slice
+constexpr int kCW = 8;                       // consumer warps
+constexpr int kThreads = (kCW + 1) * 32;     // + producer warp
 constexpr int kMaxB = 8;
-constexpr int kRouteExperts = 8;                       // experts per ROUTE item
-constexpr int kClaim = 4;                              // items claimed per queue atomic
-constexpr int kMaxSlotsSm = 72;                        // shared (<= 8) + routed (<= 64) slots
+constexpr int kGuTok = 4;                    // tokens per K2 item
+constexpr int kDnTok = 2;                    // tokens per K3 item
+constexpr int kRouteExperts = 8;             // experts per K1 CTA
+constexpr int kMaxSlotsSm = 72;              // shared (<= 8) + routed (<= 64)
 
-enum ItemType : int { kDone = 0, kRoute = 1, kGateUp = 2, kDown = 3 };
-
-struct ItemMeta {
-    int type, slot, block, pad;
-};
-
-// Slots of this step: rows [0, S) the shared experts, [S, S+U) the routed experts.
+// Slots of this step in shared memory: rows [0, S) the shared experts, [S, S+U) routed.
 struct SlotTable {
     int nslot;
     int pad[3];
@@ -61,110 +50,176 @@ struct SlotTable {
     float weight[kMaxSlotsSm][kMaxB];
 };
 
-struct Smem {
-    uint64_t* full;
-    uint64_t* empty;
-    ItemMeta* meta;
-    SlotTable* tbl;
-    float* xs;     // [B][H/64][68]
-    float* hs;     // [8][I/64][68]
-    float* part;   // partial sums
-    unsigned char* stages;
-    int* flag;     // small scratch ints
+struct ItemMeta {
+    int type;    // 0 end marker, 1 work
+    int slot, rows0, nrows, q0, nq;
+    int sc_off;  // byte offset of the int8 scales inside the stage
+    int h_off;   // K3: byte offset of the h rows inside the stage
 };
 
-UOCR_DEV unsigned char* stage_ptr(const Smem& s, int st, uint32_t stage_bytes) {
-    return s.stages + (size_t)st * stage_bytes;
+// The shared-expert slots (known from the shape alone).
+UOCR_DEV void load_shared_slots(SlotTable* tb, const DecodeArgs& a, int tid, int nthreads) {
+    const int kB = a.topk * a.B;
+    for (int s = tid; s < a.S; s += nthreads) {
+        tb->expert[s] = s;
+        tb->count[s] = a.B;
+        for (int t = 0; t < kMaxB; ++t) {
+            tb->pair[s][t] = kB + s * a.B + t;
+            tb->token[s][t] = t;
+            tb->weight[s][t] = 1.0f;
+        }
+    }
+    if (tid == 0) tb->nslot = a.S;
 }
 
-// ---- item enumeration -------------------------------------------------------------------
-struct Plan {
-    int NR, NGB, NDB, MR, S;
-    uint32_t total;
-};
-
-UOCR_DEV Plan make_plan(const DecodeArgs& a) {
-    Plan p;
-    p.NR = (a.E + kRouteExperts - 1) / kRouteExperts;
-    p.NGB = a.I / kRB;
-    p.NDB = a.H / kRJ;
-    p.MR = min(a.E, a.topk * a.B);
-    p.S = a.S;
-    p.total = (uint32_t)((p.S + p.MR) * (p.NGB + p.NDB));
-    return p;
+// The routed slots, from the route kernel's table (call after the dependency wait).
+UOCR_DEV void load_routed_slots(SlotTable* tb, const DecodeArgs& a, int lane) {
+    const RouteTable* g = a.table;
+    const int U = __ldcg(&g->U);
+    for (int u = lane; u < U; u += 32) {
+        const int row = a.S + u;
+        tb->expert[row] = __ldcg(&g->expert[u]);
+        tb->count[row] = __ldcg(&g->count[u]);
+#pragma unroll
+        for (int q = 0; q < kMaxB; ++q) {
+            tb->pair[row][q] = __ldcg(&g->pair[u][q]);
+            tb->token[row][q] = __ldcg(&g->token[u][q]);
+            tb->weight[row][q] = __ldcg(&g->weight[u][q]);
+        }
+    }
+    __syncwarp();
+    if (lane == 0) tb->nslot = a.S + U;
+    __syncwarp();
 }
 
-// Main-queue item i (the ROUTE items have their own counter, one per claim).
-UOCR_DEV void decode_item(const Plan& p, uint32_t i, int& type, int& slot, int& block) {
-    const uint32_t gu = (uint32_t)(p.S + p.MR) * p.NGB;
-    if (i < gu) { type = kGateUp; slot = (int)(i / p.NGB); block = (int)(i % p.NGB); return; }
-    i -= gu;
-    type = kDown; slot = (int)(i / p.NDB); block = (int)(i % p.NDB);
+// A consumer's bounded wait on a full barrier; gives up when the producer aborted.
+UOCR_DEV bool consumer_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, uint32_t* status) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*abort_flag || global_timer_ns() - t0 > kWaitBudgetNs) {
+            set_status(status, kStatusWaitTimeout);
+            return false;
+        }
+    }
+    return true;
 }
 
-// ---- ROUTE -----------------------------------------------------------------------------------
-// Thread (expert j, segment s) fma-chains router row j's segment s against every token (the
-// oracle's order); segments summed in ascending order; bias added; logits to global. The last
-// ROUTE item to finish runs softmax + top-k and publishes the routing grouped by expert.
-UOCR_DEV void do_route(const DecodeArgs& a, const Smem& sm, const Plan& p, int r, const unsigned char* stage,
-                      uint32_t row_stride, int ctid) {
-    const int H = a.H, B = a.B, L = H / 8, NKX = H / kUnit;
-    // thread (token group tg, expert jl, segment s): router row jl (staged) segment s against
-    // tokens tg*TPG .. tg*TPG+TPG-1
-    const int tg = ctid >> 6, jl = (ctid >> 3) & 7, s = ctid & 7;
-    const int TPG = (B + 3) / 4;
-    const int j = r * kRouteExperts + jl;
-    if (j < a.E && tg * TPG < B) {
-        float acc[2] = {0.0f, 0.0f};
-        const uint16_t* wrow = reinterpret_cast<const uint16_t*>(stage + (size_t)jl * row_stride) + s * L;
-        for (int kk = 0; kk < L; kk += 8) {
-            float wf[8];
-            unpack_bf16x8(*reinterpret_cast<const uint4*>(wrow + kk), wf);
-            const int k0 = s * L + kk;
+// Four consecutive weights (bf16 or int8) at element offset k of a staged row -> fp32.
+template <bool kI8>
+UOCR_DEV void load4(const unsigned char* row, int k, float (&w)[4]) {
+    if (kI8) {
+        const uint32_t v = *reinterpret_cast<const uint32_t*>(row + k) ^ 0x80808080u;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) w[i] = s8_byte_to_f32(v, i);
+    } else {
+        const uint2 v = *reinterpret_cast<const uint2*>(row + 2 * k);
+        w[0] = bf16lo(v.x); w[1] = bf16hi(v.x); w[2] = bf16lo(v.y); w[3] = bf16hi(v.y);
+    }
+}
+
+UOCR_DEV float dot4(const float (&w)[4], const float4& x, float acc) {
+    acc = __fmaf_rn(w[0], x.x, acc);
+    acc = __fmaf_rn(w[1], x.y, acc);
+    acc = __fmaf_rn(w[2], x.z, acc);
+    acc = __fmaf_rn(w[3], x.w, acc);
+    return acc;
+}
+
+// Diagnostics timeline: per CTA `items` records of {wait start, data ready, done, slot<<32|n}.
+UOCR_DEV unsigned long long* trace_rec(const DecodeArgs& a, int half, int n) {
+    if (!a.trace || n >= a.trace_items / 2) return nullptr;
+    return a.trace + ((size_t)blockIdx.x * a.trace_items + (size_t)half * (a.trace_items / 2) + n) * 4;
+}
+
+// ======================================================================================
+// K1: route
+// ======================================================================================
+// Thread (token group tg, expert jl, segment s) fma-chains router row jl's segment s against
+// tokens tg*TPG..: the oracle's per-segment chain; segments then summed in ascending order.
+__global__ void __launch_bounds__(256)
+decode_route_kernel(DecodeArgs a) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    const int H = a.H, B = a.B, L = H / 8, E = a.E, k = a.topk;
+    const int LW = L + 8;   // padded bf16 segment stride
+    const int LX = L + 4;   // padded fp32 segment stride
+    uint16_t* ws = reinterpret_cast<uint16_t*>(smem);                          // [8 experts][8 segs][LW]
+    float* xs = reinterpret_cast<float*>(smem + sizeof(uint16_t) * 64 * LW);    // [B][8 segs][LX]
+    float* part = xs + kMaxB * 8 * LX;                                          // [(jl*8+s)*kMaxB+b]
+    int* flag = reinterpret_cast<int*>(part + 64 * kMaxB);                      // [16 + 64 + 64]
+    const int tid = threadIdx.x;
+    const int j0 = blockIdx.x * kRouteExperts;
+    // router rows (weights, independent of the previous kernel) before the dependency wait
+    for (int i = tid; i < kRouteExperts * (H / 8); i += blockDim.x) {
+        const int jl = i / (H / 8), k8 = (i % (H / 8)) * 8;
+        if (j0 + jl < E) {
+            const uint4 v = *reinterpret_cast<const uint4*>(a.router + (size_t)(j0 + jl) * H + k8);
+            *reinterpret_cast<uint4*>(ws + (jl * 8 + k8 / L) * LW + (k8 % L)) = v;
+        }
+    }
+    pdl_wait_prior_grid();
+    pdl_launch_dependents();
+    for (int i = tid; i < B * (H / 4); i += blockDim.x) {
+        const int b = i / (H / 4), k4 = (i % (H / 4)) * 4;
+        const float4 v = *reinterpret_cast<const float4*>(a.x + (size_t)b * H + k4);
+        *reinterpret_cast<float4*>(xs + (b * 8 + k4 / L) * LX + (k4 % L)) = v;
+    }
+    __syncthreads();
+    {
+        const int tg = tid >> 6, jl = (tid >> 3) & 7, s = tid & 7;
+        const int TPG = (B + 3) / 4;
+        if (j0 + jl < E && tg * TPG < B) {
+            float acc[2] = {0.0f, 0.0f};
+            const uint16_t* wr = ws + (jl * 8 + s) * LW;
+            for (int kk = 0; kk < L; kk += 8) {
+                float wf[8];
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(wr + kk), wf);
+#pragma unroll
+                for (int bb = 0; bb < 2; ++bb) {
+                    const int b = tg * TPG + bb;
+                    if (bb < TPG && b < B) {
+                        const float* xr = xs + (b * 8 + s) * LX + kk;
+                        const float4 xa = *reinterpret_cast<const float4*>(xr);
+                        const float4 xb = *reinterpret_cast<const float4*>(xr + 4);
+                        float v = acc[bb];
+                        v = __fmaf_rn(wf[0], xa.x, v); v = __fmaf_rn(wf[1], xa.y, v);
+                        v = __fmaf_rn(wf[2], xa.z, v); v = __fmaf_rn(wf[3], xa.w, v);
+                        v = __fmaf_rn(wf[4], xb.x, v); v = __fmaf_rn(wf[5], xb.y, v);
+                        v = __fmaf_rn(wf[6], xb.z, v); v = __fmaf_rn(wf[7], xb.w, v);
+                        acc[bb] = v;
+                    }
+                }
+            }
 #pragma unroll
             for (int bb = 0; bb < 2; ++bb) {
                 const int b = tg * TPG + bb;
-                if (bb < TPG && b < B) {
-                    const float* xr = sm.xs + (b * NKX + k0 / kUnit) * kPad + (k0 % kUnit);  // 8 | 64: no straddle
-                    const float4 xa = *reinterpret_cast<const float4*>(xr);
-                    const float4 xb = *reinterpret_cast<const float4*>(xr + 4);
-                    float v = acc[bb];
-                    v = __fmaf_rn(wf[0], xa.x, v); v = __fmaf_rn(wf[1], xa.y, v);
-                    v = __fmaf_rn(wf[2], xa.z, v); v = __fmaf_rn(wf[3], xa.w, v);
-                    v = __fmaf_rn(wf[4], xb.x, v); v = __fmaf_rn(wf[5], xb.y, v);
-                    v = __fmaf_rn(wf[6], xb.z, v); v = __fmaf_rn(wf[7], xb.w, v);
-                    acc[bb] = v;
-                }
+                if (bb < TPG && b < B) part[(jl * 8 + s) * kMaxB + b] = acc[bb];
             }
         }
+    }
+    __syncthreads();
+    if (tid < kRouteExperts * B) {
+        const int jl = tid / B, b = tid % B, j = j0 + jl;
+        if (j < E) {
+            float total = part[(jl * 8 + 0) * kMaxB + b];
 #pragma unroll
-        for (int bb = 0; bb < 2; ++bb) {
-            const int b = tg * TPG + bb;
-            if (bb < TPG && b < B) sm.part[(jl * 8 + s) * kMaxB + b] = acc[bb];
+            for (int q = 1; q < 8; ++q) total = __fadd_rn(total, part[(jl * 8 + q) * kMaxB + b]);
+            if (a.bias) total = __fadd_rn(total, a.bias[j]);
+            a.logits[b * 64 + j] = total;
         }
     }
-    named_bar_sync(1, kConsumers);
-    if (ctid < kRouteExperts * B) {
-        const int jj = ctid / B, b = ctid % B, jg = r * kRouteExperts + jj;
-        if (jg < a.E) {
-            float total = sm.part[(jj * 8 + 0) * kMaxB + b];
-#pragma unroll
-            for (int q = 1; q < 8; ++q) total = __fadd_rn(total, sm.part[(jj * 8 + q) * kMaxB + b]);
-            if (a.bias) total = __fadd_rn(total, a.bias[jg]);
-            a.logits[b * 64 + jg] = total;
-        }
-    }
-    named_bar_sync(1, kConsumers);
-    if (ctid == 0) {
+    __syncthreads();
+    if (tid == 0) {
         __threadfence();
-        sm.flag[0] = (atomicAdd(&a.ctl->route_done, 1u) == (uint32_t)p.NR - 1) ? 1 : 0;
+        flag[0] = (atomicAdd(&a.ctl->route_done, 1u) == gridDim.x - 1) ? 1 : 0;
     }
-    named_bar_sync(1, kConsumers);
-    if (!sm.flag[0]) return;
+    __syncthreads();
+    if (!flag[0]) return;
+    // the last CTA: softmax + top-k per token (warp b serves token b), then group by expert
     __threadfence();
-    int* ids_s = sm.flag + 16;                               // [kB]
-    float* wts_s = reinterpret_cast<float*>(sm.flag + 16 + 64);  // [kB]
-    const int warp = ctid >> 5, lane = ctid & 31, k = a.topk, E = a.E;
+    int* ids_s = flag + 16;
+    float* wts_s = reinterpret_cast<float*>(flag + 16 + 64);
+    const int warp = tid >> 5, lane = tid & 31;
     if (warp < B) {
         const int b = warp;
         const bool v0 = lane < E, v1 = lane + 32 < E;
@@ -200,574 +255,531 @@ UOCR_DEV void do_route(const DecodeArgs& a, const Smem& sm, const Plan& p, int r
             }
         }
     }
-    named_bar_sync(1, kConsumers);
-    // group by expert: thread e (< 64) owns expert e; its row is the number of used experts below it
+    __syncthreads();
     const int kB = k * B;
     int c = 0;
-    if (ctid < 64) {
-        for (int q = 0; q < kB; ++q) c += (ids_s[q] == ctid);
+    if (tid < 64) {
+        for (int q = 0; q < kB; ++q) c += (ids_s[q] == tid);
         const unsigned bal = __ballot_sync(0xffffffffu, c > 0);
-        if (lane == 0) sm.flag[8 + warp] = (int)bal;
+        if (lane == 0) flag[8 + warp] = (int)bal;
     }
-    named_bar_sync(1, kConsumers);
-    if (ctid < 64) {
+    __syncthreads();
+    if (tid < 64) {
         const unsigned long long used =
-            (unsigned long long)(unsigned)sm.flag[8] | ((unsigned long long)(unsigned)sm.flag[9] << 32);
+            (unsigned long long)(unsigned)flag[8] | ((unsigned long long)(unsigned)flag[9] << 32);
         if (c > 0) {
-            const int u = __popcll(used & ((1ull << ctid) - 1ull));
+            const int u = __popcll(used & ((1ull << tid) - 1ull));
             RouteTable* tb = a.table;
             int n = 0;
             for (int q = 0; q < kB; ++q) {
-                if (ids_s[q] == ctid) {
+                if (ids_s[q] == tid) {
                     tb->pair[u][n] = q;
                     tb->token[u][n] = q / k;
                     tb->weight[u][n] = wts_s[q];
                     ++n;
                 }
             }
-            tb->expert[u] = ctid;
+            tb->expert[u] = tid;
             tb->count[u] = c;
         }
-        if (ctid == 0) a.table->U = __popcll(used);
-    }
-    named_bar_sync(1, kConsumers);
-    if (ctid == 0) {
-        __threadfence();
-        st_release_gpu(&a.ctl->route_ready, 1u);
-    }
-}
-
-// ---- GU -----------------------------------------------------------------------------------------
-template <bool kI8>
-UOCR_DEV void gu_units(const DecodeArgs& a, const Smem& sm, int slot, int block, const unsigned char* stage,
-                       uint32_t row_stride, int ctid) {
-    const SlotTable& tb = *sm.tbl;
-    const int H = a.H, NKX = H / kUnit, c = tb.count[slot];
-    const int units = kRB * NKX;
-    for (int u = ctid; u < units; u += kConsumers) {
-        const int r = u % kRB, ks = u / kRB;
-        const unsigned char* grow = stage + (size_t)r * row_stride;
-        const unsigned char* urow = stage + (size_t)(kRB + r) * row_stride;
-        float ag[kMaxB], au[kMaxB];
-#pragma unroll
-        for (int q = 0; q < kMaxB; ++q) ag[q] = au[q] = 0.0f;
-        if (!kI8) {
-#pragma unroll 2
-            for (int j = 0; j < kUnit / 8; ++j) {
-                float fg[8], fu[8];
-                unpack_bf16x8(*reinterpret_cast<const uint4*>(grow + ks * kUnit * 2 + j * 16), fg);
-                unpack_bf16x8(*reinterpret_cast<const uint4*>(urow + ks * kUnit * 2 + j * 16), fu);
-#pragma unroll
-                for (int q = 0; q < kMaxB; ++q) {
-                    if (q < c) {
-                        const float* xr = sm.xs + (tb.token[slot][q] * NKX + ks) * kPad + j * 8;
-                        const float4 xa = *reinterpret_cast<const float4*>(xr);
-                        const float4 xb = *reinterpret_cast<const float4*>(xr + 4);
-                        const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-                        float g = ag[q], v = au[q];
-#pragma unroll
-                        for (int e = 0; e < 8; ++e) {
-                            g = __fmaf_rn(fg[e], xv[e], g);
-                            v = __fmaf_rn(fu[e], xv[e], v);
-                        }
-                        ag[q] = g;
-                        au[q] = v;
-                    }
-                }
-            }
-        } else {
-#pragma unroll 1
-            for (int j = 0; j < kUnit / 16; ++j) {
-                const uint4 wg = *reinterpret_cast<const uint4*>(grow + ks * kUnit + j * 16);
-                const uint4 wu = *reinterpret_cast<const uint4*>(urow + ks * kUnit + j * 16);
-                float fg[16], fu[16];
-                unpack_s8x8(wg.x, wg.y, *reinterpret_cast<float(*)[8]>(fg));
-                unpack_s8x8(wg.z, wg.w, *reinterpret_cast<float(*)[8]>(fg + 8));
-                unpack_s8x8(wu.x, wu.y, *reinterpret_cast<float(*)[8]>(fu));
-                unpack_s8x8(wu.z, wu.w, *reinterpret_cast<float(*)[8]>(fu + 8));
-#pragma unroll
-                for (int q = 0; q < kMaxB; ++q) {
-                    if (q < c) {
-                        const float* xr = sm.xs + (tb.token[slot][q] * NKX + ks) * kPad + j * 16;
-                        float g = ag[q], v = au[q];
-#pragma unroll
-                        for (int h4 = 0; h4 < 4; ++h4) {
-                            const float4 xv = *reinterpret_cast<const float4*>(xr + 4 * h4);
-                            g = __fmaf_rn(fg[4 * h4 + 0], xv.x, g); v = __fmaf_rn(fu[4 * h4 + 0], xv.x, v);
-                            g = __fmaf_rn(fg[4 * h4 + 1], xv.y, g); v = __fmaf_rn(fu[4 * h4 + 1], xv.y, v);
-                            g = __fmaf_rn(fg[4 * h4 + 2], xv.z, g); v = __fmaf_rn(fu[4 * h4 + 2], xv.z, v);
-                            g = __fmaf_rn(fg[4 * h4 + 3], xv.w, g); v = __fmaf_rn(fu[4 * h4 + 3], xv.w, v);
-                        }
-                        ag[q] = g;
-                        au[q] = v;
-                    }
-                }
-            }
-            // the unit lies in one quantisation group: scale its partial sums (group sum, then scale)
-            const int n = block * kRB + r;
-            const int pg = (n / 128) * 256 + (n % 128);
-            const size_t groups = (size_t)H / a.G;
-            const float* sb = a.s13 + (size_t)tb.expert[slot] * 2 * a.I * groups;
-            const float sg = __ldg(sb + (size_t)pg * groups + (ks * kUnit) / a.G);
-            const float su = __ldg(sb + (size_t)(pg + 128) * groups + (ks * kUnit) / a.G);
-#pragma unroll
-            for (int q = 0; q < kMaxB; ++q) { ag[q] = __fmul_rn(ag[q], sg); au[q] = __fmul_rn(au[q], su); }
-        }
-#pragma unroll
-        for (int q = 0; q < kMaxB; ++q) {
-            if (q < c) {
-                sm.part[((r * NKX + ks) * kMaxB + q) * 2 + 0] = ag[q];
-                sm.part[((r * NKX + ks) * kMaxB + q) * 2 + 1] = au[q];
-            }
+        if (tid == 0) {
+            a.table->U = __popcll(used);
+            a.ctl->route_done = 0;  // single-use election counter: leave it zeroed
         }
     }
 }
 
-// ---- DOWN -------------------------------------------------------------------------------------
-template <bool kI8>
-UOCR_DEV void down_units(const DecodeArgs& a, const Smem& sm, int slot, int block, const unsigned char* stage,
-                         uint32_t row_stride, int ctid) {
-    const SlotTable& tb = *sm.tbl;
-    const int I = a.I, NKI = I / kUnit, c = tb.count[slot];
-    const int units = kRJ * NKI;
-    for (int u = ctid; u < units; u += kConsumers) {
-        const int r = u % kRJ, ks = u / kRJ;
-        const unsigned char* wrow = stage + (size_t)r * row_stride;
-        float acc[kMaxB];
-#pragma unroll
-        for (int q = 0; q < kMaxB; ++q) acc[q] = 0.0f;
-        if (!kI8) {
-#pragma unroll 2
-            for (int j = 0; j < kUnit / 8; ++j) {
-                float f[8];
-                unpack_bf16x8(*reinterpret_cast<const uint4*>(wrow + ks * kUnit * 2 + j * 16), f);
-#pragma unroll
-                for (int q = 0; q < kMaxB; ++q) {
-                    if (q < c) {
-                        const float* hr = sm.hs + (q * NKI + ks) * kPad + j * 8;
-                        const float4 ha = *reinterpret_cast<const float4*>(hr);
-                        const float4 hb = *reinterpret_cast<const float4*>(hr + 4);
-                        float v = acc[q];
-                        v = __fmaf_rn(f[0], ha.x, v); v = __fmaf_rn(f[1], ha.y, v);
-                        v = __fmaf_rn(f[2], ha.z, v); v = __fmaf_rn(f[3], ha.w, v);
-                        v = __fmaf_rn(f[4], hb.x, v); v = __fmaf_rn(f[5], hb.y, v);
-                        v = __fmaf_rn(f[6], hb.z, v); v = __fmaf_rn(f[7], hb.w, v);
-                        acc[q] = v;
-                    }
-                }
-            }
-        } else {
-#pragma unroll 1
-            for (int j = 0; j < kUnit / 16; ++j) {
-                const uint4 w = *reinterpret_cast<const uint4*>(wrow + ks * kUnit + j * 16);
-                float f[16];
-                unpack_s8x8(w.x, w.y, *reinterpret_cast<float(*)[8]>(f));
-                unpack_s8x8(w.z, w.w, *reinterpret_cast<float(*)[8]>(f + 8));
-#pragma unroll
-                for (int q = 0; q < kMaxB; ++q) {
-                    if (q < c) {
-                        const float* hr = sm.hs + (q * NKI + ks) * kPad + j * 16;
-                        float v = acc[q];
-#pragma unroll
-                        for (int h4 = 0; h4 < 4; ++h4) {
-                            const float4 hv = *reinterpret_cast<const float4*>(hr + 4 * h4);
-                            v = __fmaf_rn(f[4 * h4 + 0], hv.x, v);
-                            v = __fmaf_rn(f[4 * h4 + 1], hv.y, v);
-                            v = __fmaf_rn(f[4 * h4 + 2], hv.z, v);
-                            v = __fmaf_rn(f[4 * h4 + 3], hv.w, v);
-                        }
-                        acc[q] = v;
-                    }
-                }
-            }
-            const int jrow = block * kRJ + r;
-            const size_t groups = (size_t)I / a.G;
-            const float sc = __ldg(a.s2 + ((size_t)tb.expert[slot] * a.H + jrow) * groups + (ks * kUnit) / a.G);
-#pragma unroll
-            for (int q = 0; q < kMaxB; ++q) acc[q] = __fmul_rn(acc[q], sc);
-        }
-#pragma unroll
-        for (int q = 0; q < kMaxB; ++q)
-            if (q < c) sm.part[(r * NKI + ks) * kMaxB + q] = acc[q];
-    }
+// ======================================================================================
+// K2: gate/up + SwiGLU
+// ======================================================================================
+// Items per slot: (I / RB) row blocks x ceil(count / kGuTok) token groups, RB = 2 row pairs
+// for bf16 weights and 4 for int8, so every item is ~10 KB. Items are dealt round-robin over
+// the CTAs; shared slots first (they need no routing), then routed slots.
+UOCR_DEV int gu_rb(const DecodeArgs& a, int slot) { return (slot >= a.S && a.int8) ? 4 : 2; }
+
+UOCR_DEV int gu_items_of(const DecodeArgs& a, const SlotTable& tb, int slot) {
+    return (a.I / gu_rb(a, slot)) * ((tb.count[slot] + kGuTok - 1) / kGuTok);
 }
 
-// ---- producer warp --------------------------------------------------------------------------
-// Lane 0 claims items kClaim at a time and drives the mbarriers; the whole warp copies the
-// routing table into shared memory once and issues the bulk copies (one weight row per lane).
-UOCR_DEV void producer_warp(const DecodeArgs& a, const Smem& sm, const Plan& p, int nst, uint32_t stage_bytes,
-                            uint32_t gu_b16, uint32_t gu_i8, uint32_t dn_b16, uint32_t dn_i8, volatile int* abort_flag) {
-    const int lane = threadIdx.x & 31;
-    bool have_table = false;
-    int n = 0;
-    bool ok = true;
-    uint32_t next = 0, left = 0;
-    bool routes_left = true;
+// item index i within slots [first, ...) -> (slot, row block, token group)
+UOCR_DEV void gu_decode(const DecodeArgs& a, const SlotTable& tb, int first, int i, int& slot, int& rblk, int& tg) {
+    int s = first;
     while (true) {
-        int type = kRoute, slot = 0, block = 0;
-        if (routes_left) {
-            uint32_t r = 0;
-            if (lane == 0) r = atomicAdd(&a.ctl->route_q, 1u);
-            r = __shfl_sync(0xffffffffu, r, 0);
-            if (r < (uint32_t)p.NR) {
-                block = (int)r;
-            } else {
-                routes_left = false;
-            }
-        }
-        if (!routes_left) {
-            if (left == 0) {
-                uint32_t base = 0;
-                if (lane == 0) base = atomicAdd(&a.ctl->queue, (uint32_t)kClaim);
-                next = __shfl_sync(0xffffffffu, base, 0);
-                left = kClaim;
-            }
-            const uint32_t i = next++;
-            --left;
-            if (i >= p.total) break;
-            decode_item(p, i, type, slot, block);
-        }
-        if (type != kRoute && slot >= p.S) {
-            if (!have_table) {
-                int got = 1;
-                if (lane == 0) got = wait_counter_geq(&a.ctl->route_ready, 1u, &a.ctl->status) ? 1 : 0;
-                got = __shfl_sync(0xffffffffu, got, 0);
-                if (!got) { ok = false; break; }
-                __syncwarp();
-                const RouteTable* g = a.table;
-                const int U = __ldcg(&g->U);
-                for (int u = lane; u < U; u += 32) {
-                    const int row = p.S + u;
-                    sm.tbl->expert[row] = __ldcg(&g->expert[u]);
-                    sm.tbl->count[row] = __ldcg(&g->count[u]);
+        const int n = gu_items_of(a, tb, s);
+        if (i < n) break;
+        i -= n;
+        ++s;
+    }
+    const int ntg = (tb.count[s] + kGuTok - 1) / kGuTok;
+    slot = s;
+    rblk = i / ntg;
+    tg = i % ntg;
+}
+
+template <bool kI8>
+UOCR_DEV void gu_item(const DecodeArgs& a, const SlotTable& tb, const float* xs, const ItemMeta& m,
+                      const unsigned char* stage, int lane) {
+    const int H = a.H;
+    const int esz = kI8 ? 1 : 2;
+    const int NG = H / a.G;
+    const float* gsc = reinterpret_cast<const float*>(stage + m.sc_off);
+    const float* usc = gsc + m.nrows * NG;
+    for (int r = 0; r < m.nrows; ++r) {
+        const unsigned char* grow = stage + (size_t)r * H * esz;
+        const unsigned char* urow = stage + (size_t)(m.nrows + r) * H * esz;
+        float ag[kGuTok], au[kGuTok];
 #pragma unroll
-                    for (int q = 0; q < kMaxB; ++q) {
-                        sm.tbl->pair[row][q] = __ldcg(&g->pair[u][q]);
-                        sm.tbl->token[row][q] = __ldcg(&g->token[u][q]);
-                        sm.tbl->weight[row][q] = __ldcg(&g->weight[u][q]);
+        for (int q = 0; q < kGuTok; ++q) ag[q] = au[q] = 0.0f;
+        for (int j = 0; j < H / 128; ++j) {
+            const int k = 4 * (lane + 32 * j);
+            float wg[4], wu[4];
+            load4<kI8>(grow, k, wg);
+            load4<kI8>(urow, k, wu);
+            float sg = 1.0f, su = 1.0f;
+            if (kI8) {
+                sg = gsc[r * NG + k / a.G];
+                su = usc[r * NG + k / a.G];
+            }
+#pragma unroll
+            for (int q = 0; q < kGuTok; ++q) {
+                if (q < m.nq) {
+                    const float4 xv =
+                        *reinterpret_cast<const float4*>(xs + (size_t)tb.token[m.slot][m.q0 + q] * H + k);
+                    if (kI8) {
+                        ag[q] = __fmaf_rn(sg, dot4(wg, xv, 0.0f), ag[q]);
+                        au[q] = __fmaf_rn(su, dot4(wu, xv, 0.0f), au[q]);
+                    } else {
+                        ag[q] = dot4(wg, xv, ag[q]);
+                        au[q] = dot4(wu, xv, au[q]);
                     }
                 }
-                if (lane == 0) sm.tbl->nslot = p.S + U;
-                __syncwarp();
-                have_table = true;
-            }
-            if (slot >= sm.tbl->nslot) continue;  // no such routed expert this step
-        }
-        const int st = n % nst, round = n / nst;
-        int got = 1;
-        if (lane == 0 && round > 0) got = mbar_wait(&sm.empty[st], (round - 1) & 1, &a.ctl->status) ? 1 : 0;
-        got = __shfl_sync(0xffffffffu, got, 0);
-        if (!got) { ok = false; break; }
-        if (lane == 0) {
-            sm.meta[st].type = type;
-            sm.meta[st].slot = slot;
-            sm.meta[st].block = block;
-        }
-        unsigned char* dst = stage_ptr(sm, st, stage_bytes);
-        if (type == kRoute) {
-            // the ROUTE item's router rows
-            const uint32_t rb = (uint32_t)a.H * 2;
-            const int j0 = block * kRouteExperts;
-            const int nrow = min(kRouteExperts, a.E - j0);
-            if (lane == 0) mbar_arrive_expect_tx(&sm.full[st], (uint32_t)nrow * rb);
-            __syncwarp();
-            if (lane < nrow)
-                bulk_g2s(dst + (size_t)lane * gu_b16, reinterpret_cast<const unsigned char*>(a.router) + (size_t)(j0 + lane) * rb,
-                         rb, &sm.full[st]);
-        } else {
-            const bool shared = slot < p.S;
-            const bool i8 = !shared && a.int8;
-            const int expert = sm.tbl->expert[slot];
-            if (type == kGateUp) {
-                const uint32_t rb = (uint32_t)a.H * (i8 ? 1 : 2);
-                const uint32_t stride = i8 ? gu_i8 : gu_b16;
-                const unsigned char* base =
-                    shared ? reinterpret_cast<const unsigned char*>(a.w13_shared) + (size_t)expert * 2 * a.I * rb
-                           : reinterpret_cast<const unsigned char*>(a.w13) + (size_t)expert * 2 * a.I * rb;
-                if (lane == 0) mbar_arrive_expect_tx(&sm.full[st], 2u * kRB * rb);
-                __syncwarp();
-                const int n0 = block * kRB;
-                const int pg0 = (n0 / 128) * 256 + (n0 % 128);
-                if (lane < 2 * kRB) {
-                    const int r = lane % kRB;
-                    const int prow = pg0 + r + (lane >= kRB ? 128 : 0);
-                    bulk_g2s(dst + (size_t)lane * stride, base + (size_t)prow * rb, rb, &sm.full[st]);
-                }
-            } else {
-                const uint32_t rb = (uint32_t)a.I * (i8 ? 1 : 2);
-                const uint32_t stride = i8 ? dn_i8 : dn_b16;
-                const unsigned char* base =
-                    shared ? reinterpret_cast<const unsigned char*>(a.w2_shared) + (size_t)expert * a.H * rb
-                           : reinterpret_cast<const unsigned char*>(a.w2) + (size_t)expert * a.H * rb;
-                if (lane == 0) mbar_arrive_expect_tx(&sm.full[st], (uint32_t)kRJ * rb);
-                __syncwarp();
-                if (lane < kRJ)
-                    bulk_g2s(dst + (size_t)lane * stride, base + (size_t)(block * kRJ + lane) * rb, rb, &sm.full[st]);
             }
         }
-        __syncwarp();
-        ++n;
-    }
-    if (!ok) {
-        if (lane == 0) {
-            *abort_flag = 1;
-            // wait (bounded) for the copies already issued into stages the consumers may not drain
-            for (int q = max(0, n - nst); q < n; ++q) mbar_wait(&sm.full[q % nst], (q / nst) & 1, nullptr);
-        }
-        __syncwarp();
-        return;
-    }
-    if (lane == 0) {
-        const int st = n % nst, round = n / nst;
-        if (round > 0 && !mbar_wait(&sm.empty[st], (round - 1) & 1, &a.ctl->status)) {
-            *abort_flag = 1;
-        } else {
-            sm.meta[st].type = kDone;
-            mbar_arrive(&sm.full[st]);
-        }
-    }
-    __syncwarp();
-}
-
-// ---- consumers ---------------------------------------------------------------------------------
-UOCR_DEV void consumers(const DecodeArgs& a, const Smem& sm, const Plan& p, int nst, uint32_t stage_bytes,
-                        uint32_t gu_b16, uint32_t gu_i8, uint32_t dn_b16, uint32_t dn_i8, volatile int* abort_flag,
-                        int ctid) {
-    const int NKX = a.H / kUnit, NKI = a.I / kUnit, B = a.B, k = a.topk, kB = k * B;
-    const SlotTable& tb = *sm.tbl;
-    int n = 0;
-    int staged_slot = -1;
-    unsigned long long* tr = a.trace ? a.trace + (size_t)blockIdx.x * a.trace_items * 4 : nullptr;
-    while (true) {
-        const int st = n % nst;
-        const uint32_t parity = (n / nst) & 1;
-        if (ctid == 0) {
-            int ok = 1;
-            const uint64_t t0 = global_timer_ns();
-            if (tr && n < a.trace_items) tr[n * 4 + 0] = t0;
-            while (!mbar_try_wait(&sm.full[st], parity)) {
-                if (*abort_flag || global_timer_ns() - t0 > kWaitBudgetNs) {
-                    set_status(&a.ctl->status, kStatusWaitTimeout);
-                    ok = 0;
-                    break;
-                }
-            }
-            sm.flag[3] = ok;
-            if (tr && n < a.trace_items) {
-                tr[n * 4 + 1] = global_timer_ns();
-                tr[n * 4 + 3] = ((unsigned long long)sm.meta[st].type << 48) | ((unsigned long long)sm.meta[st].slot << 24) |
-                                (unsigned long long)sm.meta[st].block;
+#pragma unroll
+        for (int q = 0; q < kGuTok; ++q) {
+            if (q < m.nq) {
+                const float g = warp_sum_butterfly(ag[q]);
+                const float u = warp_sum_butterfly(au[q]);
+                if (lane == q) a.h[(size_t)tb.pair[m.slot][m.q0 + q] * a.I + m.rows0 + r] = silu(g) * u;
             }
         }
-        named_bar_sync(1, kConsumers);
-        if (!sm.flag[3]) break;
-        const int type = sm.meta[st].type, slot = sm.meta[st].slot, block = sm.meta[st].block;
-        if (type == kDone) break;
-        const unsigned char* stage = stage_ptr(sm, st, stage_bytes);
-        if (type == kRoute) {
-            do_route(a, sm, p, block, stage, gu_b16, ctid);
-            named_bar_sync(1, kConsumers);
-            if (ctid == 0) mbar_arrive(&sm.empty[st]);
-        } else if (type == kGateUp) {
-            const bool i8 = slot >= p.S && a.int8;
-            if (i8)
-                gu_units<true>(a, sm, slot, block, stage, gu_i8, ctid);
-            else
-                gu_units<false>(a, sm, slot, block, stage, gu_b16, ctid);
-            named_bar_sync(1, kConsumers);
-            if (ctid == 0) mbar_arrive(&sm.empty[st]);  // stage consumed
-            const int c = tb.count[slot];
-            for (int t = ctid; t < kRB * c; t += kConsumers) {
-                const int r = t / c, q = t % c;
-                float g = sm.part[((r * NKX + 0) * kMaxB + q) * 2 + 0];
-                float u = sm.part[((r * NKX + 0) * kMaxB + q) * 2 + 1];
-                for (int ks = 1; ks < NKX; ++ks) {
-                    g = __fadd_rn(g, sm.part[((r * NKX + ks) * kMaxB + q) * 2 + 0]);
-                    u = __fadd_rn(u, sm.part[((r * NKX + ks) * kMaxB + q) * 2 + 1]);
-                }
-                a.h[(size_t)tb.pair[slot][q] * a.I + block * kRB + r] = silu(g) * u;
-            }
-            named_bar_sync(1, kConsumers);
-            if (ctid == 0) {
-                __threadfence();
-                atomicAdd(&a.ctl->gu_done[slot], 1u);
-            }
-        } else {
-            const int c = tb.count[slot];
-            if (slot != staged_slot) {
-                // the slot's gate/up must be complete before its h is read (one waiter per warp)
-                if (ctid == 0) {
-                    if (!wait_counter_geq(&a.ctl->gu_done[slot], (uint32_t)p.NGB, &a.ctl->status)) *abort_flag = 1;
-                }
-                named_bar_sync(1, kConsumers);
-                for (int i = ctid; i < c * (a.I / 4); i += kConsumers) {
-                    const int q = i / (a.I / 4), kk = (i % (a.I / 4)) * 4;
-                    const float4 v = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)tb.pair[slot][q] * a.I + kk));
-                    *reinterpret_cast<float4*>(sm.hs + (q * NKI + kk / kUnit) * kPad + (kk % kUnit)) = v;
-                }
-                named_bar_sync(1, kConsumers);
-                staged_slot = slot;
-            }
-            const bool i8 = slot >= p.S && a.int8;
-            if (i8)
-                down_units<true>(a, sm, slot, block, stage, dn_i8, ctid);
-            else
-                down_units<false>(a, sm, slot, block, stage, dn_b16, ctid);
-            named_bar_sync(1, kConsumers);
-            if (ctid == 0) mbar_arrive(&sm.empty[st]);
-            for (int t = ctid; t < kRJ * c; t += kConsumers) {
-                const int r = t / c, q = t % c;
-                float y = sm.part[(r * NKI + 0) * kMaxB + q];
-                for (int ks = 1; ks < NKI; ++ks) y = __fadd_rn(y, sm.part[(r * NKI + ks) * kMaxB + q]);
-                a.y[(size_t)tb.pair[slot][q] * a.H + block * kRJ + r] = y;
-            }
-            named_bar_sync(1, kConsumers);
-            if (ctid == 0) {
-                __threadfence();
-                const uint32_t done = atomicAdd(&a.ctl->j_done[block], 1u) + 1u;
-                int fin = 0;
-                if (wait_counter_geq(&a.ctl->route_ready, 1u, &a.ctl->status))
-                    fin = (done == (uint32_t)(p.S + __ldcg(&a.table->U))) ? 1 : 0;
-                sm.flag[2] = fin;
-                if (fin) __threadfence();
-            }
-            named_bar_sync(1, kConsumers);
-            if (sm.flag[2]) {
-                // the last DOWN item of this output block: out = sum_s w y_routed + sum_q y_shared
-                for (int t = ctid; t < kRJ * B; t += kConsumers) {
-                    const int r = t % kRJ, b = t / kRJ;
-                    const int j = block * kRJ + r;
-                    float acc = 0.0f;
-                    for (int s = 0; s < k; ++s) {
-                        const int pr = b * k + s;
-                        acc = __fmaf_rn(__ldcg(a.wts + pr), __ldcg(a.y + (size_t)pr * a.H + j), acc);
-                    }
-                    for (int q = 0; q < a.S; ++q) acc = __fadd_rn(acc, __ldcg(a.y + (size_t)(kB + q * B + b) * a.H + j));
-                    a.out[(size_t)b * a.H + j] = acc;
-                }
-            }
-        }
-        if (ctid == 0 && tr && n < a.trace_items) tr[n * 4 + 2] = global_timer_ns();
-        ++n;
     }
 }
 
-// ---- the kernel ---------------------------------------------------------------------------------
 __global__ void __launch_bounds__(kThreads, 1)
-decode_layer_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_meta, uint32_t off_tbl, uint32_t off_xs,
-                    uint32_t off_hs, uint32_t off_part, uint32_t off_flag, uint32_t off_stages) {
-    extern __shared__ __align__(1024) unsigned char smem[];
+decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl, uint32_t off_meta,
+                      uint32_t off_xs, uint32_t off_stages) {
+    extern __shared__ __align__(16) unsigned char smem[];
     __shared__ int abort_flag;
-    Smem sm;
-    sm.full = reinterpret_cast<uint64_t*>(smem);
-    sm.empty = sm.full + nst;
-    sm.meta = reinterpret_cast<ItemMeta*>(smem + off_meta);
-    sm.tbl = reinterpret_cast<SlotTable*>(smem + off_tbl);
-    sm.xs = reinterpret_cast<float*>(smem + off_xs);
-    sm.hs = reinterpret_cast<float*>(smem + off_hs);
-    sm.part = reinterpret_cast<float*>(smem + off_part);
-    sm.flag = reinterpret_cast<int*>(smem + off_flag);
-    sm.stages = smem + off_stages;
-    const Plan p = make_plan(a);
-    const int tid = threadIdx.x;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + nst;
+    SlotTable* tb = reinterpret_cast<SlotTable*>(smem + off_tbl);
+    ItemMeta* meta = reinterpret_cast<ItemMeta*>(smem + off_meta);
+    float* xs = reinterpret_cast<float*>(smem + off_xs);
+    unsigned char* stages = smem + off_stages;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     if (tid == 0) {
         for (int s = 0; s < nst; ++s) {
-            mbar_init(&sm.full[s], 1);
-            mbar_init(&sm.empty[s], 1);
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
         }
         abort_flag = 0;
         fence_mbar_init();
+        pdl_launch_dependents();  // K3 waits for this grid before it reads h
     }
-    // shared-expert slots are known before routing
-    if (tid < a.S) {
-        sm.tbl->expert[tid] = tid;
-        sm.tbl->count[tid] = a.B;
-        for (int t = 0; t < kMaxB; ++t) {
-            sm.tbl->pair[tid][t] = a.topk * a.B + tid * a.B + t;
-            sm.tbl->token[tid][t] = t;
-            sm.tbl->weight[tid][t] = 1.0f;
-        }
-    }
-    // stage the tokens: xs[b][k/64][k%64]
-    const int NKX = a.H / kUnit;
-    for (int i = tid; i < a.B * (a.H / 4); i += kThreads) {
-        const int b = i / (a.H / 4), k = (i % (a.H / 4)) * 4;
-        const float4 v = *reinterpret_cast<const float4*>(a.x + (size_t)b * a.H + k);
-        *reinterpret_cast<float4*>(sm.xs + (b * NKX + k / kUnit) * kPad + (k % kUnit)) = v;
-    }
+    // the tokens (complete: the route kernel let this grid launch only after its own wait)
+    for (int i = tid; i < a.B * (a.H / 4); i += blockDim.x)
+        reinterpret_cast<float4*>(xs)[i] = reinterpret_cast<const float4*>(a.x)[i];
+    load_shared_slots(tb, a, tid, blockDim.x);
     __syncthreads();
 
-    const uint32_t gu_b16 = (uint32_t)a.H * 2 + 16, gu_i8 = (uint32_t)a.H + 16;
-    const uint32_t dn_b16 = (uint32_t)a.I * 2 + 16, dn_i8 = (uint32_t)a.I + 16;
-    if (tid >= kConsumers)
-        producer_warp(a, sm, p, nst, stage_bytes, gu_b16, gu_i8, dn_b16, dn_i8, &abort_flag);
-    else
-        consumers(a, sm, p, nst, stage_bytes, gu_b16, gu_i8, dn_b16, dn_i8, &abort_flag, tid);
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence();
-        if (atomicAdd(&a.ctl->cta_done, 1u) == gridDim.x - 1) {
-            // last CTA: leave the control block zeroed for the next launch (status stays)
-            __threadfence();
-            a.ctl->queue = 0;
-            a.ctl->route_done = 0;
-            a.ctl->route_ready = 0;
-            a.ctl->route_q = 0;
-            for (int s = 0; s < p.S + p.MR; ++s) a.ctl->gu_done[s] = 0;
-            for (int j = 0; j < p.NDB; ++j) a.ctl->j_done[j] = 0;
-            __threadfence();
-            a.ctl->cta_done = 0;
+    if (warp == kCW) {
+        // ---------------- producer ----------------
+        int n = 0;
+        bool ok = true;
+        for (int phase = 0; phase < 2 && ok; ++phase) {
+            if (phase == 1) {
+                pdl_wait_prior_grid();  // the routing table
+                load_routed_slots(tb, a, lane);
+            }
+            const int first = phase == 0 ? 0 : a.S;
+            const int last = phase == 0 ? a.S : tb->nslot;
+            int total = 0;
+            for (int s = first; s < last; ++s) total += gu_items_of(a, *tb, s);
+            for (int i = blockIdx.x; i < total; i += gridDim.x) {
+                int slot, rblk, tg;
+                gu_decode(a, *tb, first, i, slot, rblk, tg);
+                const int st = n % nst, round = n / nst;
+                int got = 1;
+                if (lane == 0 && round > 0) got = mbar_wait(&empty[st], (round - 1) & 1, &a.ctl->status) ? 1 : 0;
+                got = __shfl_sync(0xffffffffu, got, 0);
+                if (!got) { ok = false; break; }
+                const bool i8 = slot >= a.S && a.int8;
+                const int RB = gu_rb(a, slot);
+                const int esz = i8 ? 1 : 2;
+                const uint32_t blk = (uint32_t)RB * a.H * esz;
+                const int n0 = rblk * RB;
+                const int pg0 = (n0 / 128) * 256 + (n0 % 128);
+                const int e = tb->expert[slot];
+                const unsigned char* wbase =
+                    slot < a.S ? reinterpret_cast<const unsigned char*>(a.w13_shared) + (size_t)e * 2 * a.I * a.H * 2
+                               : reinterpret_cast<const unsigned char*>(a.w13) + (size_t)e * 2 * a.I * a.H * esz;
+                const int NG = a.H / a.G;
+                const uint32_t scb = (uint32_t)RB * NG * 4;
+                unsigned char* dst = stages + (size_t)st * stage_bytes;
+                if (lane == 0) {
+                    ItemMeta& m = meta[st];
+                    m.type = 1;
+                    m.slot = slot;
+                    m.rows0 = n0;
+                    m.nrows = RB;
+                    m.q0 = tg * kGuTok;
+                    m.nq = min(kGuTok, tb->count[slot] - tg * kGuTok);
+                    m.sc_off = (int)(2 * blk);
+                    m.h_off = 0;
+                    mbar_arrive_expect_tx(&full[st], 2 * blk + (i8 ? 2 * scb : 0));
+                }
+                __syncwarp();
+                if (lane == 0) bulk_g2s(dst, wbase + (size_t)pg0 * a.H * esz, blk, &full[st]);
+                if (lane == 1) bulk_g2s(dst + blk, wbase + (size_t)(pg0 + 128) * a.H * esz, blk, &full[st]);
+                if (i8) {
+                    const unsigned char* sb =
+                        reinterpret_cast<const unsigned char*>(a.s13) + (size_t)e * 2 * a.I * NG * 4;
+                    if (lane == 2) bulk_g2s(dst + 2 * blk, sb + (size_t)pg0 * NG * 4, scb, &full[st]);
+                    if (lane == 3) bulk_g2s(dst + 2 * blk + scb, sb + (size_t)(pg0 + 128) * NG * 4, scb, &full[st]);
+                }
+                __syncwarp();
+                ++n;
+            }
+        }
+        if (lane == 0) {
+            if (!ok) {
+                abort_flag = 1;
+                for (int q = max(0, n - nst); q < n; ++q) mbar_wait(&full[q % nst], (q / nst) & 1, nullptr);
+            } else {
+                // one end marker per consumer warp (stage n belongs to warp n % 8)
+                for (int w = 0; w < kCW; ++w, ++n) {
+                    const int st = n % nst, round = n / nst;
+                    if (round > 0 && !mbar_wait(&empty[st], (round - 1) & 1, &a.ctl->status)) {
+                        abort_flag = 1;
+                        break;
+                    }
+                    meta[st].type = 0;
+                    mbar_arrive(&full[st]);
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------- consumer warp: ring entries warp, warp + 8, ... ----------------
+        for (int n = warp;; n += kCW) {
+            const int st = n % nst;
+            unsigned long long* tr = trace_rec(a, 0, n);
+            if (tr && lane == 0) tr[0] = global_timer_ns();
+            int ok = 1;
+            if (lane == 0) ok = consumer_wait(&full[st], (n / nst) & 1, &abort_flag, &a.ctl->status) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            const ItemMeta& m = meta[st];
+            if (m.type == 0) break;
+            if (tr && lane == 0) tr[1] = global_timer_ns();
+            const unsigned char* stage = stages + (size_t)st * stage_bytes;
+            if (m.slot >= a.S && a.int8)
+                gu_item<true>(a, *tb, xs, m, stage, lane);
+            else
+                gu_item<false>(a, *tb, xs, m, stage, lane);
+            __syncwarp();
+            if (tr && lane == 0) {
+                tr[2] = global_timer_ns();
+                tr[3] = ((unsigned long long)m.slot << 32) | (unsigned)m.rows0;
+            }
+            if (lane == 0) mbar_arrive(&empty[st]);
         }
     }
 }
 
-// ---- host side ------------------------------------------------------------------------------------
+// ======================================================================================
+// K3: down + combine
+// ======================================================================================
+template <bool kI8>
+UOCR_DEV void down_item(const DecodeArgs& a, const SlotTable& tb, const ItemMeta& m, const unsigned char* stage,
+                        float* ybuf, int nrows_cta, int lane) {
+    const int I = a.I;
+    const int esz = kI8 ? 1 : 2;
+    const int NG = I / a.G;
+    const float* sc = reinterpret_cast<const float*>(stage + m.sc_off);
+    const float* hs = reinterpret_cast<const float*>(stage + m.h_off);
+    for (int r = 0; r < m.nrows; ++r) {
+        const unsigned char* wrow = stage + (size_t)r * I * esz;
+        float acc[kDnTok];
+#pragma unroll
+        for (int q = 0; q < kDnTok; ++q) acc[q] = 0.0f;
+        for (int j = 0; j < I / 128; ++j) {
+            const int k = 4 * (lane + 32 * j);
+            float w[4];
+            load4<kI8>(wrow, k, w);
+            const float s = kI8 ? sc[r * NG + k / a.G] : 1.0f;
+#pragma unroll
+            for (int q = 0; q < kDnTok; ++q) {
+                if (q < m.nq) {
+                    const float4 hv = *reinterpret_cast<const float4*>(hs + (size_t)q * I + k);
+                    acc[q] = kI8 ? __fmaf_rn(s, dot4(w, hv, 0.0f), acc[q]) : dot4(w, hv, acc[q]);
+                }
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < kDnTok; ++q) {
+            if (q < m.nq) {
+                const float y = warp_sum_butterfly(acc[q]);
+                const int t = tb.token[m.slot][m.q0 + q];
+                if (lane == 0) ybuf[((size_t)m.slot * kMaxB + t) * nrows_cta + r] = y;
+            }
+        }
+    }
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+decode_down_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl, uint32_t off_meta,
+                   uint32_t off_ybuf, uint32_t off_stages) {
+    extern __shared__ __align__(16) unsigned char smem[];
+    __shared__ int abort_flag;
+    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
+    uint64_t* empty = full + nst;
+    SlotTable* tb = reinterpret_cast<SlotTable*>(smem + off_tbl);
+    ItemMeta* meta = reinterpret_cast<ItemMeta*>(smem + off_meta);
+    float* ybuf = reinterpret_cast<float*>(smem + off_ybuf);
+    unsigned char* stages = smem + off_stages;
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int j0 = (int)((long)blockIdx.x * a.H / gridDim.x);
+    const int j1 = (int)((long)(blockIdx.x + 1) * a.H / gridDim.x);
+    const int nr = j1 - j0;
+    if (tid == 0) {
+        for (int s = 0; s < nst; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        abort_flag = 0;
+        fence_mbar_init();
+        pdl_launch_dependents();  // the next layer's route kernel waits for this grid itself
+    }
+    load_shared_slots(tb, a, tid, blockDim.x);
+    __syncthreads();
+
+    if (warp == kCW) {
+        // ---------------- producer ----------------
+        int n = 0;
+        bool ok = true;
+        bool waited = false;
+        for (int slot = 0; ok; ++slot) {
+            if (slot == a.S) {
+                // routed slots: their table (K1) and every h (K2) are complete once K2 is
+                pdl_wait_prior_grid();
+                waited = true;
+                load_routed_slots(tb, a, lane);
+            }
+            if (slot >= tb->nslot) break;
+            const bool i8 = slot >= a.S && a.int8;
+            const int esz = i8 ? 1 : 2;
+            const int e = tb->expert[slot];
+            const unsigned char* wbase =
+                slot < a.S ? reinterpret_cast<const unsigned char*>(a.w2_shared) + (size_t)e * a.H * a.I * 2
+                           : reinterpret_cast<const unsigned char*>(a.w2) + (size_t)e * a.H * a.I * esz;
+            const uint32_t wbytes = (uint32_t)nr * a.I * esz;
+            const int NG = a.I / a.G;
+            // int8 scales of rows [j0, j1): a 16-byte aligned superset of the block
+            const size_t sc_off = ((size_t)e * a.H + j0) * NG * 4;
+            const size_t sc_a = sc_off & ~size_t(15);
+            const uint32_t sc_delta = (uint32_t)(sc_off - sc_a);
+            const uint32_t scb = (uint32_t)((sc_delta + (size_t)nr * NG * 4 + 15) & ~size_t(15));
+            const uint32_t h_off = (uint32_t)((wbytes + (i8 ? scb : 0u) + 15u) & ~15u);
+            const uint32_t hrow = (uint32_t)a.I * 4;
+            const int c = tb->count[slot];
+            for (int q0 = 0; q0 < c; q0 += kDnTok) {
+                const int nq = min(kDnTok, c - q0);
+                const int st = n % nst, round = n / nst;
+                int got = 1;
+                if (lane == 0 && round > 0) got = mbar_wait(&empty[st], (round - 1) & 1, &a.ctl->status) ? 1 : 0;
+                got = __shfl_sync(0xffffffffu, got, 0);
+                if (!got) { ok = false; break; }
+                unsigned char* dst = stages + (size_t)st * stage_bytes;
+                if (lane == 0) {
+                    ItemMeta& m = meta[st];
+                    m.type = 1;
+                    m.slot = slot;
+                    m.rows0 = j0;
+                    m.nrows = nr;
+                    m.q0 = q0;
+                    m.nq = nq;
+                    m.sc_off = (int)(wbytes + sc_delta);
+                    m.h_off = (int)h_off;
+                    mbar_arrive_expect_tx(&full[st], wbytes + (i8 ? scb : 0u) + (uint32_t)nq * hrow);
+                }
+                __syncwarp();
+                // weights first: they do not depend on the previous kernel
+                if (lane == 0) bulk_g2s(dst, wbase + (size_t)j0 * a.I * esz, wbytes, &full[st]);
+                if (i8 && lane == 1)
+                    bulk_g2s(dst + wbytes, reinterpret_cast<const unsigned char*>(a.s2) + sc_a, scb, &full[st]);
+                if (!waited) {
+                    pdl_wait_prior_grid();  // h comes from K2
+                    waited = true;
+                }
+                __syncwarp();
+                if (lane < nq) bulk_g2s(dst + h_off, a.h + (size_t)tb->pair[slot][q0 + lane] * a.I, hrow, &full[st]);
+                __syncwarp();
+                ++n;
+            }
+        }
+        if (lane == 0) {
+            if (!ok) {
+                abort_flag = 1;
+                for (int q = max(0, n - nst); q < n; ++q) mbar_wait(&full[q % nst], (q / nst) & 1, nullptr);
+            } else {
+                for (int w = 0; w < kCW; ++w, ++n) {
+                    const int st = n % nst, round = n / nst;
+                    if (round > 0 && !mbar_wait(&empty[st], (round - 1) & 1, &a.ctl->status)) {
+                        abort_flag = 1;
+                        break;
+                    }
+                    meta[st].type = 0;
+                    mbar_arrive(&full[st]);
+                }
+            }
+        }
+        __syncwarp();
+    } else {
+        for (int n = warp;; n += kCW) {
+            const int st = n % nst;
+            unsigned long long* tr = trace_rec(a, 1, n);
+            if (tr && lane == 0) tr[0] = global_timer_ns();
+            int ok = 1;
+            if (lane == 0) ok = consumer_wait(&full[st], (n / nst) & 1, &abort_flag, &a.ctl->status) ? 1 : 0;
+            ok = __shfl_sync(0xffffffffu, ok, 0);
+            if (!ok) break;
+            const ItemMeta& m = meta[st];
+            if (m.type == 0) break;
+            if (tr && lane == 0) tr[1] = global_timer_ns();
+            const unsigned char* stage = stages + (size_t)st * stage_bytes;
+            if (m.slot >= a.S && a.int8)
+                down_item<true>(a, *tb, m, stage, ybuf, nr, lane);
+            else
+                down_item<false>(a, *tb, m, stage, ybuf, nr, lane);
+            __syncwarp();
+            if (tr && lane == 0) {
+                tr[2] = global_timer_ns();
+                tr[3] = ((unsigned long long)m.slot << 32) | (unsigned)m.q0;
+            }
+            if (lane == 0) mbar_arrive(&empty[st]);
+        }
+    }
+    __syncthreads();
+    if (abort_flag) return;
+    // combine: a token's slots in ascending order (shared first, then its experts by id)
+    const int B = a.B;
+    for (int i = tid; i < nr * B; i += blockDim.x) {
+        const int r = i % nr, t = i / nr;
+        float acc = 0.0f;
+        for (int s = 0; s < tb->nslot; ++s) {
+            const int c = tb->count[s];
+            for (int q = 0; q < c; ++q) {
+                if (tb->token[s][q] == t) {
+                    const float y = ybuf[((size_t)s * kMaxB + t) * nr + r];
+                    acc = s < a.S ? __fadd_rn(acc, y) : __fmaf_rn(tb->weight[s][q], y, acc);
+                }
+            }
+        }
+        a.out[(size_t)t * a.H + j0 + r] = acc;
+    }
+}
+
+// ======================================================================================
+// host side
+// ======================================================================================
 static size_t up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-cudaError_t launch_decode_layer(const DecodeArgs& a, cudaStream_t st) {
-    const int NKX = a.H / kUnit, NKI = a.I / kUnit;
-    const uint32_t gu_stage_b16 = 2u * kRB * ((uint32_t)a.H * 2 + 16);
-    const uint32_t dn_stage_b16 = (uint32_t)kRJ * ((uint32_t)a.I * 2 + 16);
-    // shared experts are always bf16, so a stage must hold a bf16 item
-    const uint32_t stage_bytes = (uint32_t)up(std::max(gu_stage_b16, dn_stage_b16), 128);
-    const size_t xs_bytes = sizeof(float) * (size_t)a.B * NKX * kPad;
-    const size_t hs_bytes = sizeof(float) * (size_t)a.B * NKI * kPad;
-    const size_t part_bytes = sizeof(float) * std::max((size_t)kRB * NKX * kMaxB * 2,
-                                                       std::max((size_t)kRJ * NKI * kMaxB, (size_t)64 * 8 * kMaxB));
-    const size_t flag_bytes = sizeof(int) * (16 + 64 + 64);
+static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    return cudaLaunchKernelExC(&cfg, fn, args);
+}
+
+cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
+    DecodeArgs a = a_in;
     int dev = 0, max_smem = 0, sms = 0;
     cudaError_t err = cudaGetDevice(&dev);
     if (err != cudaSuccess) return err;
     cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    const int kMaxStages = 8;
-    const size_t fixed = up(16 * kMaxStages, 128) + up(sizeof(ItemMeta) * kMaxStages, 128) + up(sizeof(SlotTable), 128) +
-                         up(xs_bytes, 128) + up(hs_bytes, 128) + up(part_bytes, 128) + up(flag_bytes, 128) + 2048;
-    const int nst = (int)std::min<size_t>(kMaxStages, ((size_t)max_smem - fixed) / stage_bytes);
-    if (nst < 2) return cudaErrorInvalidConfiguration;
-    size_t off = up(16 * (size_t)nst, 128);
-    const size_t off_meta = off; off += up(sizeof(ItemMeta) * nst, 128);
-    const size_t off_tbl = off; off += up(sizeof(SlotTable), 128);
-    const size_t off_xs = off; off += up(xs_bytes, 128);
-    const size_t off_hs = off; off += up(hs_bytes, 128);
-    const size_t off_part = off; off += up(part_bytes, 128);
-    const size_t off_flag = off; off += up(flag_bytes, 128);
-    const size_t off_stages = up(off, 1024);
-    const size_t smem = off_stages + (size_t)nst * stage_bytes;
-    err = ensure_smem_optin(reinterpret_cast<const void*>(decode_layer_kernel), smem);
-    if (err != cudaSuccess) return err;
-    const int NR = (a.E + kRouteExperts - 1) / kRouteExperts;
-    const int MR = std::min(a.E, a.topk * a.B);
-    const long total = (long)(a.S + MR) * (a.I / kRB + a.H / kRJ);
-    const int grid = (int)std::min<long>(NR + (total + kClaim - 1) / kClaim, (long)sms);
-    DecodeArgs args = a;
     if (g_decode_trace) {
-        args.trace = g_decode_trace;
-        args.trace_items = (int)(g_decode_trace_bytes / (sizeof(unsigned long long) * 4 * (size_t)grid));
+        a.trace = g_decode_trace;
+        a.trace_items = (int)(g_decode_trace_bytes / (sizeof(unsigned long long) * 4 * (size_t)sms)) & ~1;
     }
-    decode_layer_kernel<<<grid, kThreads, smem, st>>>(args, nst, stage_bytes, (uint32_t)off_meta, (uint32_t)off_tbl,
-                                                     (uint32_t)off_xs, (uint32_t)off_hs, (uint32_t)off_part,
-                                                     (uint32_t)off_flag, (uint32_t)off_stages);
+
+    // ---- K1
+    {
+        const int L = a.H / 8;
+        const size_t smem = sizeof(uint16_t) * 64 * (L + 8) + sizeof(float) * (kMaxB * 8 * (L + 4) + 64 * kMaxB) +
+                            sizeof(int) * (16 + 128);
+        err = ensure_smem_optin(reinterpret_cast<const void*>(decode_route_kernel), smem);
+        if (err != cudaSuccess) return err;
+        void* args[] = {&a};
+        const int nr = (a.E + kRouteExperts - 1) / kRouteExperts;
+        err = launch_pdl(reinterpret_cast<const void*>(decode_route_kernel), dim3(nr), dim3(256), smem, st, args);
+        if (err != cudaSuccess) return err;
+    }
+    // ---- K2
+    {
+        // a stage holds a bf16 item (2 row pairs) or an int8 item (4 row pairs + scales)
+        const uint32_t b16 = 2u * 2 * a.H * 2;
+        const uint32_t i8 = 2u * 4 * a.H + 2u * 4 * (a.H / a.G) * 4;
+        uint32_t stage_bytes = (uint32_t)up(std::max(b16, a.int8 ? i8 : 0u), 128);
+        const size_t off_tbl = up(16 * 16, 128);
+        const size_t off_meta = off_tbl + up(sizeof(SlotTable), 128);
+        const size_t off_xs = off_meta + up(sizeof(ItemMeta) * 16, 128);
+        const size_t off_stages = up(off_xs + sizeof(float) * a.B * a.H, 1024);
+        int nst = (int)std::min<size_t>(16, ((size_t)max_smem - off_stages) / stage_bytes);
+        nst = nst / kCW * kCW;
+        if (nst < kCW) return cudaErrorInvalidConfiguration;
+        const size_t smem = off_stages + (size_t)nst * stage_bytes;
+        err = ensure_smem_optin(reinterpret_cast<const void*>(decode_gate_up_kernel), smem);
+        if (err != cudaSuccess) return err;
+        uint32_t ot = (uint32_t)off_tbl, om = (uint32_t)off_meta, ox = (uint32_t)off_xs, os = (uint32_t)off_stages;
+        void* args[] = {&a, &nst, &stage_bytes, &ot, &om, &ox, &os};
+        err = launch_pdl(reinterpret_cast<const void*>(decode_gate_up_kernel), dim3(sms), dim3(kThreads), smem, st,
+                         args);
+        if (err != cudaSuccess) return err;
+    }
+    // ---- K3
+    {
+        const int grid = std::min(sms, a.H);
+        const int nr_max = (a.H + grid - 1) / grid;
+        const uint32_t w16 = (uint32_t)nr_max * a.I * 2;
+        const uint32_t w8 = (uint32_t)nr_max * a.I + (uint32_t)up((size_t)nr_max * (a.I / a.G) * 4 + 16, 16);
+        uint32_t stage_bytes =
+            (uint32_t)up(up(std::max(w16, a.int8 ? w8 : 0u), 16) + (size_t)kDnTok * a.I * 4, 128);
+        const int slots = a.S + std::min(a.E, a.topk * a.B);
+        const size_t off_tbl = up(16 * 16, 128);
+        const size_t off_meta = off_tbl + up(sizeof(SlotTable), 128);
+        const size_t off_ybuf = off_meta + up(sizeof(ItemMeta) * 16, 128);
+        const size_t off_stages = up(off_ybuf + sizeof(float) * (size_t)slots * kMaxB * nr_max, 1024);
+        int nst = (int)std::min<size_t>(16, ((size_t)max_smem - off_stages) / stage_bytes);
+        nst = nst / kCW * kCW;
+        if (nst < kCW) return cudaErrorInvalidConfiguration;
+        const size_t smem = off_stages + (size_t)nst * stage_bytes;
+        err = ensure_smem_optin(reinterpret_cast<const void*>(decode_down_kernel), smem);
+        if (err != cudaSuccess) return err;
+        uint32_t ot = (uint32_t)off_tbl, om = (uint32_t)off_meta, oy = (uint32_t)off_ybuf, os = (uint32_t)off_stages;
+        void* args[] = {&a, &nst, &stage_bytes, &ot, &om, &oy, &os};
+        err = launch_pdl(reinterpret_cast<const void*>(decode_down_kernel), dim3(grid), dim3(kThreads), smem, st, args);
+        if (err != cudaSuccess) return err;
+    }
     return cudaGetLastError();
 }
 

@@ -26,13 +26,10 @@ cudaError_t launch_route(const float* x, int T, int H, const uint16_t* wg, int E
 // launch leaves it zeroed again except `status`, which is sticky until read.
 struct DecodeCtl {
     uint32_t status;
-    uint32_t queue, route_done, route_ready, cta_done, route_q;
-    uint32_t pad[10];
-    uint32_t gu_done[128];  // per expert slot: gate/up items finished
-    uint32_t j_done[512];   // per 16-row output block: down items finished
+    uint32_t route_done;  // route-kernel CTAs finished (the last one resets it)
+    uint32_t pad[62];
 };
-constexpr int kDecodeMaxSlots = 128;
-constexpr int kDecodeMaxJBlocks = 512;
+constexpr int kDecodeMaxShared = 8;
 
 // The step's routing grouped by expert (written by the last ROUTE item).
 struct RouteTable {
