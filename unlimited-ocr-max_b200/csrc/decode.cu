@@ -624,7 +624,9 @@ decode_down_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl
                     waited = true;
                 }
                 __syncwarp();
-                if (lane < nq) bulk_g2s(dst + h_off, a.h + (size_t)tb->pair[slot][q0 + lane] * a.I, hrow, &full[st]);
+                if (lane < nq)
+                    bulk_g2s(dst + h_off + (size_t)lane * hrow, a.h + (size_t)tb->pair[slot][q0 + lane] * a.I, hrow,
+                             &full[st]);
                 __syncwarp();
                 ++n;
             }
