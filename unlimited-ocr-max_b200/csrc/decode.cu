@@ -316,53 +316,118 @@ UOCR_DEV void gu_decode(const DecodeArgs& a, const SlotTable& tb, int first, int
     tg = i % ntg;
 }
 
-template <bool kI8>
-UOCR_DEV void gu_item(const DecodeArgs& a, const SlotTable& tb, const float* xs, const ItemMeta& m,
-                      const unsigned char* stage, int lane) {
-    const int H = a.H;
-    const int esz = kI8 ? 1 : 2;
+// One warp, one item: kRB row pairs against up to kGuTok tokens. Lane l owns the 4-element
+// chunks k = 4(l + 32j), j < NJ = H/128. A token's chunks sit in registers while every row of the
+// item streams past; all rows' partial sums are reduced together (independent butterflies).
+template <bool kI8, int kRB, int NJ>
+UOCR_DEV void gu_item_t(const DecodeArgs& a, const SlotTable& tb, const float* __restrict__ xs, int slot, int rows0,
+                        int q0, int nq, const unsigned char* __restrict__ stage, int sc_off, int lane) {
+    const int H = NJ * 128;
+    constexpr int esz = kI8 ? 1 : 2;
     const int NG = H / a.G;
-    const float* gsc = reinterpret_cast<const float*>(stage + m.sc_off);
-    const float* usc = gsc + m.nrows * NG;
-    for (int r = 0; r < m.nrows; ++r) {
-        const unsigned char* grow = stage + (size_t)r * H * esz;
-        const unsigned char* urow = stage + (size_t)(m.nrows + r) * H * esz;
-        float ag[kGuTok], au[kGuTok];
+    const float* gsc = reinterpret_cast<const float*>(stage + sc_off);
+    const float* usc = gsc + kRB * NG;
+    for (int q = 0; q < nq; ++q) {
+        const int t = tb.token[slot][q0 + q];
+        const int pair = tb.pair[slot][q0 + q];
+        float4 xr[NJ];
 #pragma unroll
-        for (int q = 0; q < kGuTok; ++q) ag[q] = au[q] = 0.0f;
-        for (int j = 0; j < H / 128; ++j) {
-            const int k = 4 * (lane + 32 * j);
-            float wg[4], wu[4];
-            load4<kI8>(grow, k, wg);
-            load4<kI8>(urow, k, wu);
-            float sg = 1.0f, su = 1.0f;
-            if (kI8) {
-                sg = gsc[r * NG + k / a.G];
-                su = usc[r * NG + k / a.G];
-            }
+        for (int j = 0; j < NJ; ++j) xr[j] = *reinterpret_cast<const float4*>(xs + (size_t)t * H + 4 * (lane + 32 * j));
+#pragma unroll 1
+        for (int r = 0; r < kRB; ++r) {
+            const unsigned char* grow = stage + (size_t)r * H * esz;
+            const unsigned char* urow = stage + (size_t)(kRB + r) * H * esz;
+            float ga = 0.0f, ua = 0.0f;
 #pragma unroll
-            for (int q = 0; q < kGuTok; ++q) {
-                if (q < m.nq) {
-                    const float4 xv =
-                        *reinterpret_cast<const float4*>(xs + (size_t)tb.token[m.slot][m.q0 + q] * H + k);
-                    if (kI8) {
-                        ag[q] = __fmaf_rn(sg, dot4(wg, xv, 0.0f), ag[q]);
-                        au[q] = __fmaf_rn(su, dot4(wu, xv, 0.0f), au[q]);
-                    } else {
-                        ag[q] = dot4(wg, xv, ag[q]);
-                        au[q] = dot4(wu, xv, au[q]);
-                    }
+            for (int j = 0; j < NJ; ++j) {
+                const int k = 4 * (lane + 32 * j);
+                float wg[4], wu[4];
+                load4<kI8>(grow, k, wg);
+                load4<kI8>(urow, k, wu);
+                if (kI8) {
+                    ga = __fmaf_rn(gsc[r * NG + k / a.G], dot4(wg, xr[j], 0.0f), ga);
+                    ua = __fmaf_rn(usc[r * NG + k / a.G], dot4(wu, xr[j], 0.0f), ua);
+                } else {
+                    ga = dot4(wg, xr[j], ga);
+                    ua = dot4(wu, xr[j], ua);
                 }
             }
+#pragma unroll
+            for (int off = 16; off >= 1; off >>= 1) {
+                ga = __fadd_rn(ga, __shfl_xor_sync(0xffffffffu, ga, off));
+                ua = __fadd_rn(ua, __shfl_xor_sync(0xffffffffu, ua, off));
+            }
+            if (lane == 0) a.h[(size_t)pair * a.I + rows0 + r] = silu(ga) * ua;
+        }
+    }
+}
+
+// Generic K-length fallback (any H multiple of 128): the same order, runtime trip count.
+template <bool kI8, int kRB>
+UOCR_DEV void gu_item_any(const DecodeArgs& a, const SlotTable& tb, const float* __restrict__ xs, int slot, int rows0,
+                          int q0, int nq, const unsigned char* __restrict__ stage, int sc_off, int lane) {
+    const int H = a.H, NJ = H / 128;
+    constexpr int esz = kI8 ? 1 : 2;
+    const int NG = H / a.G;
+    const float* gsc = reinterpret_cast<const float*>(stage + sc_off);
+    const float* usc = gsc + kRB * NG;
+    for (int q = 0; q < nq; ++q) {
+        const int t = tb.token[slot][q0 + q];
+        const int pair = tb.pair[slot][q0 + q];
+        float g[kRB], u[kRB];
+#pragma unroll
+        for (int r = 0; r < kRB; ++r) {
+            const unsigned char* grow = stage + (size_t)r * H * esz;
+            const unsigned char* urow = stage + (size_t)(kRB + r) * H * esz;
+            float ga = 0.0f, ua = 0.0f;
+            for (int j = 0; j < NJ; ++j) {
+                const int k = 4 * (lane + 32 * j);
+                const float4 xv = *reinterpret_cast<const float4*>(xs + (size_t)t * H + k);
+                float wg[4], wu[4];
+                load4<kI8>(grow, k, wg);
+                load4<kI8>(urow, k, wu);
+                if (kI8) {
+                    ga = __fmaf_rn(gsc[r * NG + k / a.G], dot4(wg, xv, 0.0f), ga);
+                    ua = __fmaf_rn(usc[r * NG + k / a.G], dot4(wu, xv, 0.0f), ua);
+                } else {
+                    ga = dot4(wg, xv, ga);
+                    ua = dot4(wu, xv, ua);
+                }
+            }
+            g[r] = ga;
+            u[r] = ua;
         }
 #pragma unroll
-        for (int q = 0; q < kGuTok; ++q) {
-            if (q < m.nq) {
-                const float g = warp_sum_butterfly(ag[q]);
-                const float u = warp_sum_butterfly(au[q]);
-                if (lane == q) a.h[(size_t)tb.pair[m.slot][m.q0 + q] * a.I + m.rows0 + r] = silu(g) * u;
+        for (int off = 16; off >= 1; off >>= 1) {
+#pragma unroll
+            for (int r = 0; r < kRB; ++r) {
+                g[r] = __fadd_rn(g[r], __shfl_xor_sync(0xffffffffu, g[r], off));
+                u[r] = __fadd_rn(u[r], __shfl_xor_sync(0xffffffffu, u[r], off));
             }
         }
+        if (lane < kRB) {
+            float gv = g[0], uv = u[0];
+#pragma unroll
+            for (int r = 1; r < kRB; ++r)
+                if (lane == r) { gv = g[r]; uv = u[r]; }
+            a.h[(size_t)pair * a.I + rows0 + lane] = silu(gv) * uv;
+        }
+    }
+}
+
+UOCR_DEV void gu_item(const DecodeArgs& a, const SlotTable& tb, const float* xs, const ItemMeta& m,
+                      const unsigned char* stage, int lane) {
+    const int slot = m.slot, rows0 = m.rows0, q0 = m.q0, nq = m.nq, sc = m.sc_off;
+    const bool i8 = slot >= a.S && a.int8;
+    const int NJ = a.H / 128;
+    if (i8) {
+        if (NJ == 10) gu_item_t<true, 4, 10>(a, tb, xs, slot, rows0, q0, nq, stage, sc, lane);
+        else if (NJ == 2) gu_item_t<true, 4, 2>(a, tb, xs, slot, rows0, q0, nq, stage, sc, lane);
+        else gu_item_any<true, 4>(a, tb, xs, slot, rows0, q0, nq, stage, sc, lane);
+    } else {
+        if (NJ == 10) gu_item_t<false, 2, 10>(a, tb, xs, slot, rows0, q0, nq, stage, sc, lane);
+        else if (NJ == 2) gu_item_t<false, 2, 2>(a, tb, xs, slot, rows0, q0, nq, stage, sc, lane);
+        else gu_item_any<false, 2>(a, tb, xs, slot, rows0, q0, nq, stage, sc, lane);
     }
 }
 
@@ -406,9 +471,11 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             const int last = phase == 0 ? a.S : tb->nslot;
             int total = 0;
             for (int s = first; s < last; ++s) total += gu_items_of(a, *tb, s);
+            int cur_slot = first, cur_base = 0;  // items of slots before cur_slot
             for (int i = blockIdx.x; i < total; i += gridDim.x) {
-                int slot, rblk, tg;
-                gu_decode(a, *tb, first, i, slot, rblk, tg);
+                while (i >= cur_base + gu_items_of(a, *tb, cur_slot)) cur_base += gu_items_of(a, *tb, cur_slot++);
+                const int ntg = (tb->count[cur_slot] + kGuTok - 1) / kGuTok;
+                const int slot = cur_slot, rblk = (i - cur_base) / ntg, tg = (i - cur_base) % ntg;
                 const int st = n % nst, round = n / nst;
                 int got = 1;
                 if (lane == 0 && round > 0) got = mbar_wait(&empty[st], (round - 1) & 1, &a.ctl->status) ? 1 : 0;
@@ -484,10 +551,7 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             if (m.type == 0) break;
             if (tr && lane == 0) tr[1] = global_timer_ns();
             const unsigned char* stage = stages + (size_t)st * stage_bytes;
-            if (m.slot >= a.S && a.int8)
-                gu_item<true>(a, *tb, xs, m, stage, lane);
-            else
-                gu_item<false>(a, *tb, xs, m, stage, lane);
+            gu_item(a, *tb, xs, m, stage, lane);
             __syncwarp();
             if (tr && lane == 0) {
                 tr[2] = global_timer_ns();
@@ -501,27 +565,82 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
 // ======================================================================================
 // K3: down + combine
 // ======================================================================================
-template <bool kI8>
-UOCR_DEV void down_item(const DecodeArgs& a, const SlotTable& tb, const ItemMeta& m, const unsigned char* stage,
-                        float* ybuf, int nrows_cta, int lane) {
-    const int I = a.I;
-    const int esz = kI8 ? 1 : 2;
+// One warp, one item: this CTA's nr output rows against up to kDnTok tokens of one slot. Lane l
+// owns the chunks k = 4(l + 32j), j < NJ = I/128; the tokens' h chunks stay in registers while
+// the rows stream past; all rows' partial sums are reduced together.
+constexpr int kMaxRowsCta = 16;
+
+template <bool kI8, int NJ>
+UOCR_DEV void down_item_t(const DecodeArgs& a, const SlotTable& tb, int slot, int q0, int nq, int nr,
+                          const unsigned char* __restrict__ stage, int sc_off, int h_off, float* ybuf, int lane) {
+    const int I = NJ * 128;
+    constexpr int esz = kI8 ? 1 : 2;
     const int NG = I / a.G;
-    const float* sc = reinterpret_cast<const float*>(stage + m.sc_off);
-    const float* hs = reinterpret_cast<const float*>(stage + m.h_off);
-    for (int r = 0; r < m.nrows; ++r) {
-        const unsigned char* wrow = stage + (size_t)r * I * esz;
-        float acc[kDnTok];
+    const float* sc = reinterpret_cast<const float*>(stage + sc_off);
+    const float* hs = reinterpret_cast<const float*>(stage + h_off);
+    float4 hr[kDnTok][NJ];
 #pragma unroll
-        for (int q = 0; q < kDnTok; ++q) acc[q] = 0.0f;
-        for (int j = 0; j < I / 128; ++j) {
+    for (int q = 0; q < kDnTok; ++q)
+#pragma unroll
+        for (int j = 0; j < NJ; ++j)
+            hr[q][j] = q < nq ? *reinterpret_cast<const float4*>(hs + (size_t)q * I + 4 * (lane + 32 * j))
+                              : make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int r0 = 0; r0 < nr; r0 += 4) {
+        float acc[4][kDnTok];
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr) {
+            const int r = min(r0 + rr, nr - 1);
+            const unsigned char* wrow = stage + (size_t)r * I * esz;
+#pragma unroll
+            for (int q = 0; q < kDnTok; ++q) acc[rr][q] = 0.0f;
+#pragma unroll
+            for (int j = 0; j < NJ; ++j) {
+                const int k = 4 * (lane + 32 * j);
+                float w[4];
+                load4<kI8>(wrow, k, w);
+                const float s = kI8 ? sc[r * NG + k / a.G] : 1.0f;
+#pragma unroll
+                for (int q = 0; q < kDnTok; ++q)
+                    acc[rr][q] = kI8 ? __fmaf_rn(s, dot4(w, hr[q][j], 0.0f), acc[rr][q]) : dot4(w, hr[q][j], acc[rr][q]);
+            }
+        }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1)
+#pragma unroll
+            for (int rr = 0; rr < 4; ++rr)
+#pragma unroll
+                for (int q = 0; q < kDnTok; ++q)
+                    acc[rr][q] = __fadd_rn(acc[rr][q], __shfl_xor_sync(0xffffffffu, acc[rr][q], off));
+        if (lane == 0) {
+#pragma unroll
+            for (int rr = 0; rr < 4; ++rr)
+#pragma unroll
+                for (int q = 0; q < kDnTok; ++q)
+                    if (r0 + rr < nr && q < nq)
+                        ybuf[((size_t)slot * kMaxB + tb.token[slot][q0 + q]) * nr + r0 + rr] = acc[rr][q];
+        }
+    }
+}
+
+template <bool kI8>
+UOCR_DEV void down_item_any(const DecodeArgs& a, const SlotTable& tb, int slot, int q0, int nq, int nr,
+                            const unsigned char* __restrict__ stage, int sc_off, int h_off, float* ybuf, int lane) {
+    const int I = a.I, NJ = I / 128;
+    constexpr int esz = kI8 ? 1 : 2;
+    const int NG = I / a.G;
+    const float* sc = reinterpret_cast<const float*>(stage + sc_off);
+    const float* hs = reinterpret_cast<const float*>(stage + h_off);
+    for (int r = 0; r < nr; ++r) {
+        const unsigned char* wrow = stage + (size_t)r * I * esz;
+        float acc[kDnTok] = {0.0f, 0.0f};
+        for (int j = 0; j < NJ; ++j) {
             const int k = 4 * (lane + 32 * j);
             float w[4];
             load4<kI8>(wrow, k, w);
             const float s = kI8 ? sc[r * NG + k / a.G] : 1.0f;
 #pragma unroll
             for (int q = 0; q < kDnTok; ++q) {
-                if (q < m.nq) {
+                if (q < nq) {
                     const float4 hv = *reinterpret_cast<const float4*>(hs + (size_t)q * I + k);
                     acc[q] = kI8 ? __fmaf_rn(s, dot4(w, hv, 0.0f), acc[q]) : dot4(w, hv, acc[q]);
                 }
@@ -529,12 +648,25 @@ UOCR_DEV void down_item(const DecodeArgs& a, const SlotTable& tb, const ItemMeta
         }
 #pragma unroll
         for (int q = 0; q < kDnTok; ++q) {
-            if (q < m.nq) {
-                const float y = warp_sum_butterfly(acc[q]);
-                const int t = tb.token[m.slot][m.q0 + q];
-                if (lane == 0) ybuf[((size_t)m.slot * kMaxB + t) * nrows_cta + r] = y;
-            }
+            const float y = warp_sum_butterfly(acc[q]);
+            if (lane == 0 && q < nq) ybuf[((size_t)slot * kMaxB + tb.token[slot][q0 + q]) * nr + r] = y;
         }
+    }
+}
+
+UOCR_DEV void down_item(const DecodeArgs& a, const SlotTable& tb, const ItemMeta& m, const unsigned char* stage,
+                        float* ybuf, int nr, int lane) {
+    const int slot = m.slot, q0 = m.q0, nq = m.nq, sc = m.sc_off, ho = m.h_off;
+    const bool i8 = slot >= a.S && a.int8;
+    const int NJ = a.I / 128;
+    if (i8) {
+        if (NJ == 7) down_item_t<true, 7>(a, tb, slot, q0, nq, nr, stage, sc, ho, ybuf, lane);
+        else if (NJ == 1) down_item_t<true, 1>(a, tb, slot, q0, nq, nr, stage, sc, ho, ybuf, lane);
+        else down_item_any<true>(a, tb, slot, q0, nq, nr, stage, sc, ho, ybuf, lane);
+    } else {
+        if (NJ == 7) down_item_t<false, 7>(a, tb, slot, q0, nq, nr, stage, sc, ho, ybuf, lane);
+        else if (NJ == 1) down_item_t<false, 1>(a, tb, slot, q0, nq, nr, stage, sc, ho, ybuf, lane);
+        else down_item_any<false>(a, tb, slot, q0, nq, nr, stage, sc, ho, ybuf, lane);
     }
 }
 
@@ -661,10 +793,7 @@ decode_down_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl
             if (m.type == 0) break;
             if (tr && lane == 0) tr[1] = global_timer_ns();
             const unsigned char* stage = stages + (size_t)st * stage_bytes;
-            if (m.slot >= a.S && a.int8)
-                down_item<true>(a, *tb, m, stage, ybuf, nr, lane);
-            else
-                down_item<false>(a, *tb, m, stage, ybuf, nr, lane);
+            down_item(a, *tb, m, stage, ybuf, nr, lane);
             __syncwarp();
             if (tr && lane == 0) {
                 tr[2] = global_timer_ns();
