@@ -31,8 +31,10 @@
 
 namespace uocr {
 
-constexpr int kCW = 8;                       // consumer warps
+constexpr int kCW = 8;                       // K2 consumer warps
 constexpr int kThreads = (kCW + 1) * 32;     // + producer warp
+constexpr int kCW3 = 4;                      // K3 consumer warps (two stages each)
+constexpr int kThreads3 = (kCW3 + 1) * 32;
 constexpr int kMaxB = 8;
 constexpr int kGuTok = 4;                    // tokens per K2 item
 constexpr int kDnTok = 2;                    // tokens per K3 item
@@ -90,19 +92,6 @@ UOCR_DEV void load_routed_slots(SlotTable* tb, const DecodeArgs& a, int lane) {
     __syncwarp();
     if (lane == 0) tb->nslot = a.S + U;
     __syncwarp();
-}
-
-// A consumer's bounded wait on a full barrier; gives up when the producer aborted.
-UOCR_DEV bool consumer_wait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, uint32_t* status) {
-    if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = global_timer_ns();
-    while (!mbar_try_wait(bar, parity)) {
-        if (*abort_flag || global_timer_ns() - t0 > kWaitBudgetNs) {
-            set_status(status, kStatusWaitTimeout);
-            return false;
-        }
-    }
-    return true;
 }
 
 // Four consecutive weights (bf16 or int8) at element offset k of a staged row -> fp32.
@@ -477,10 +466,10 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                 const int ntg = (tb->count[cur_slot] + kGuTok - 1) / kGuTok;
                 const int slot = cur_slot, rblk = (i - cur_base) / ntg, tg = (i - cur_base) % ntg;
                 const int st = n % nst, round = n / nst;
-                int got = 1;
-                if (lane == 0 && round > 0) got = mbar_wait(&empty[st], (round - 1) & 1, &a.ctl->status) ? 1 : 0;
-                got = __shfl_sync(0xffffffffu, got, 0);
-                if (!got) { ok = false; break; }
+                if (round > 0 && !mbar_wait_warp(&empty[st], (round - 1) & 1, nullptr, &a.ctl->status)) {
+                    ok = false;
+                    break;
+                }
                 const bool i8 = slot >= a.S && a.int8;
                 const int RB = gu_rb(a, slot);
                 const int esz = i8 ? 1 : 2;
@@ -543,10 +532,7 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             const int st = n % nst;
             unsigned long long* tr = trace_rec(a, 0, n);
             if (tr && lane == 0) tr[0] = global_timer_ns();
-            int ok = 1;
-            if (lane == 0) ok = consumer_wait(&full[st], (n / nst) & 1, &abort_flag, &a.ctl->status) ? 1 : 0;
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) break;
+            if (!mbar_wait_warp(&full[st], (n / nst) & 1, &abort_flag, &a.ctl->status)) break;
             const ItemMeta& m = meta[st];
             if (m.type == 0) break;
             if (tr && lane == 0) tr[1] = global_timer_ns();
@@ -670,7 +656,7 @@ UOCR_DEV void down_item(const DecodeArgs& a, const SlotTable& tb, const ItemMeta
     }
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads3, 1)
 decode_down_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl, uint32_t off_meta,
                    uint32_t off_ybuf, uint32_t off_stages) {
     extern __shared__ __align__(16) unsigned char smem[];
@@ -697,7 +683,7 @@ decode_down_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl
     load_shared_slots(tb, a, tid, blockDim.x);
     __syncthreads();
 
-    if (warp == kCW) {
+    if (warp == kCW3) {
         // ---------------- producer ----------------
         int n = 0;
         bool ok = true;
@@ -729,10 +715,10 @@ decode_down_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl
             for (int q0 = 0; q0 < c; q0 += kDnTok) {
                 const int nq = min(kDnTok, c - q0);
                 const int st = n % nst, round = n / nst;
-                int got = 1;
-                if (lane == 0 && round > 0) got = mbar_wait(&empty[st], (round - 1) & 1, &a.ctl->status) ? 1 : 0;
-                got = __shfl_sync(0xffffffffu, got, 0);
-                if (!got) { ok = false; break; }
+                if (round > 0 && !mbar_wait_warp(&empty[st], (round - 1) & 1, nullptr, &a.ctl->status)) {
+                    ok = false;
+                    break;
+                }
                 unsigned char* dst = stages + (size_t)st * stage_bytes;
                 if (lane == 0) {
                     ItemMeta& m = meta[st];
@@ -768,7 +754,7 @@ decode_down_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl
                 abort_flag = 1;
                 for (int q = max(0, n - nst); q < n; ++q) mbar_wait(&full[q % nst], (q / nst) & 1, nullptr);
             } else {
-                for (int w = 0; w < kCW; ++w, ++n) {
+                for (int w = 0; w < kCW3; ++w, ++n) {
                     const int st = n % nst, round = n / nst;
                     if (round > 0 && !mbar_wait(&empty[st], (round - 1) & 1, &a.ctl->status)) {
                         abort_flag = 1;
@@ -781,14 +767,11 @@ decode_down_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl
         }
         __syncwarp();
     } else {
-        for (int n = warp;; n += kCW) {
+        for (int n = warp;; n += kCW3) {
             const int st = n % nst;
             unsigned long long* tr = trace_rec(a, 1, n);
             if (tr && lane == 0) tr[0] = global_timer_ns();
-            int ok = 1;
-            if (lane == 0) ok = consumer_wait(&full[st], (n / nst) & 1, &abort_flag, &a.ctl->status) ? 1 : 0;
-            ok = __shfl_sync(0xffffffffu, ok, 0);
-            if (!ok) break;
+            if (!mbar_wait_warp(&full[st], (n / nst) & 1, &abort_flag, &a.ctl->status)) break;
             const ItemMeta& m = meta[st];
             if (m.type == 0) break;
             if (tr && lane == 0) tr[1] = global_timer_ns();
@@ -901,14 +884,14 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
         const size_t off_ybuf = off_meta + up(sizeof(ItemMeta) * 16, 128);
         const size_t off_stages = up(off_ybuf + sizeof(float) * (size_t)slots * kMaxB * nr_max, 1024);
         int nst = (int)std::min<size_t>(16, ((size_t)max_smem - off_stages) / stage_bytes);
-        nst = nst / kCW * kCW;
-        if (nst < kCW) return cudaErrorInvalidConfiguration;
+        nst = nst / kCW3 * kCW3;
+        if (nst < kCW3) return cudaErrorInvalidConfiguration;
         const size_t smem = off_stages + (size_t)nst * stage_bytes;
         err = ensure_smem_optin(reinterpret_cast<const void*>(decode_down_kernel), smem);
         if (err != cudaSuccess) return err;
         uint32_t ot = (uint32_t)off_tbl, om = (uint32_t)off_meta, oy = (uint32_t)off_ybuf, os = (uint32_t)off_stages;
         void* args[] = {&a, &nst, &stage_bytes, &ot, &om, &oy, &os};
-        err = launch_pdl(reinterpret_cast<const void*>(decode_down_kernel), dim3(grid), dim3(kThreads), smem, st, args);
+        err = launch_pdl(reinterpret_cast<const void*>(decode_down_kernel), dim3(grid), dim3(kThreads3), smem, st, args);
         if (err != cudaSuccess) return err;
     }
     return cudaGetLastError();

@@ -62,6 +62,28 @@ UOCR_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
     return true;
 }
 
+// Whole-warp bounded wait (every lane calls it; the result is warp-uniform). Polls with a short
+// sleep between tries so waiting warps leave the issue slots to the working ones; the global
+// timer is read every 32 polls. `abort_flag` (optional) ends the wait early.
+UOCR_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag, uint32_t* status) {
+    if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+    uint64_t t0 = 0;
+    for (uint32_t spin = 1;; ++spin) {
+        __nanosleep(40);
+        if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
+        if ((spin & 31) == 0) {
+            int give_up = 0;
+            if ((threadIdx.x & 31) == 0) {
+                const uint64_t now = global_timer_ns();
+                if (t0 == 0) t0 = now;
+                give_up = (abort_flag && *abort_flag) || (now - t0 > kWaitBudgetNs);
+                if (give_up) set_status(status, kStatusWaitTimeout);
+            }
+            if (__shfl_sync(0xffffffffu, give_up, 0)) return false;
+        }
+    }
+}
+
 // ---- bulk async copy global -> shared (no tensor map), completes on an mbarrier ----------
 // dst, src 16-byte aligned; bytes a multiple of 16.
 UOCR_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
