@@ -283,6 +283,8 @@ int uocr_moe_decode(const uocr_moe_layer* L, const float* x, int64_t B, const fl
     if (L->hidden % 128 || L->inter % 128)
         return fail(UOCR_EUNSUPPORTED, "moe_decode: hidden and inter must be multiples of 128");
     if (L->hidden > 8192 || L->inter > 8192) return fail(UOCR_EUNSUPPORTED, "moe_decode: hidden/inter above 8192");
+    if (L->int8 && L->group != 128)
+        return fail(UOCR_EUNSUPPORTED, "moe_decode: int8 experts need the checkpoint's group size 128");
     if (!x || !out || !workspace) return fail(UOCR_EINVAL, "moe_decode: null pointer");
     if (!a16(x) || !a16(out)) return fail(UOCR_EINVAL, "moe_decode: x and out must be 16-byte aligned");
     if (bias && (reinterpret_cast<uintptr_t>(bias) & 3)) return fail(UOCR_EINVAL, "moe_decode: bias must be 4-byte aligned");

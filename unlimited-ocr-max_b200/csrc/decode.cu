@@ -311,11 +311,11 @@ UOCR_DEV void gu_decode(const DecodeArgs& a, const SlotTable& tb, int first, int
 template <bool kI8, int kRB, int NJ>
 UOCR_DEV void gu_item_t(const DecodeArgs& a, const SlotTable& tb, const float* __restrict__ xs, int slot, int rows0,
                         int q0, int nq, const unsigned char* __restrict__ stage, int sc_off, int lane) {
+    // int8 groups are 128 wide along K and lane l's chunk j is k = 4(l + 32j): group j
     const int H = NJ * 128;
     constexpr int esz = kI8 ? 1 : 2;
-    const int NG = H / a.G;
     const float* gsc = reinterpret_cast<const float*>(stage + sc_off);
-    const float* usc = gsc + kRB * NG;
+    const float* usc = gsc + kRB * NJ;
     for (int q = 0; q < nq; ++q) {
         const int t = tb.token[slot][q0 + q];
         const int pair = tb.pair[slot][q0 + q];
@@ -324,29 +324,31 @@ UOCR_DEV void gu_item_t(const DecodeArgs& a, const SlotTable& tb, const float* _
         for (int j = 0; j < NJ; ++j) xr[j] = *reinterpret_cast<const float4*>(xs + (size_t)t * H + 4 * (lane + 32 * j));
 #pragma unroll 1
         for (int r = 0; r < kRB; ++r) {
-            const unsigned char* grow = stage + (size_t)r * H * esz;
-            const unsigned char* urow = stage + (size_t)(kRB + r) * H * esz;
-            float ga = 0.0f, ua = 0.0f;
+            // one row pair, four chains: gate / up x even / odd chunks
+            float acc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
 #pragma unroll
             for (int j = 0; j < NJ; ++j) {
                 const int k = 4 * (lane + 32 * j);
-                float wg[4], wu[4];
-                load4<kI8>(grow, k, wg);
-                load4<kI8>(urow, k, wu);
-                if (kI8) {
-                    ga = __fmaf_rn(gsc[r * NG + k / a.G], dot4(wg, xr[j], 0.0f), ga);
-                    ua = __fmaf_rn(usc[r * NG + k / a.G], dot4(wu, xr[j], 0.0f), ua);
-                } else {
-                    ga = dot4(wg, xr[j], ga);
-                    ua = dot4(wu, xr[j], ua);
+#pragma unroll
+                for (int gu = 0; gu < 2; ++gu) {
+                    float w[4];
+                    load4<kI8>(stage + (size_t)(gu * kRB + r) * H * esz, k, w);
+                    if (kI8) {
+                        const float sc = (gu ? usc : gsc)[r * NJ + j];
+                        acc[gu][j & 1] = __fmaf_rn(sc, dot4(w, xr[j], 0.0f), acc[gu][j & 1]);
+                    } else {
+                        acc[gu][j & 1] = dot4(w, xr[j], acc[gu][j & 1]);
+                    }
                 }
             }
+            float g = __fadd_rn(acc[0][0], acc[0][1]);
+            float u = __fadd_rn(acc[1][0], acc[1][1]);
 #pragma unroll
             for (int off = 16; off >= 1; off >>= 1) {
-                ga = __fadd_rn(ga, __shfl_xor_sync(0xffffffffu, ga, off));
-                ua = __fadd_rn(ua, __shfl_xor_sync(0xffffffffu, ua, off));
+                g = __fadd_rn(g, __shfl_xor_sync(0xffffffffu, g, off));
+                u = __fadd_rn(u, __shfl_xor_sync(0xffffffffu, u, off));
             }
-            if (lane == 0) a.h[(size_t)pair * a.I + rows0 + r] = silu(ga) * ua;
+            if (lane == 0) a.h[(size_t)pair * a.I + rows0 + r] = silu(g) * u;
         }
     }
 }
@@ -357,7 +359,7 @@ UOCR_DEV void gu_item_any(const DecodeArgs& a, const SlotTable& tb, const float*
                           int q0, int nq, const unsigned char* __restrict__ stage, int sc_off, int lane) {
     const int H = a.H, NJ = H / 128;
     constexpr int esz = kI8 ? 1 : 2;
-    const int NG = H / a.G;
+    const int NG = NJ;  // groups of 128 along K
     const float* gsc = reinterpret_cast<const float*>(stage + sc_off);
     const float* usc = gsc + kRB * NG;
     for (int q = 0; q < nq; ++q) {
@@ -376,8 +378,8 @@ UOCR_DEV void gu_item_any(const DecodeArgs& a, const SlotTable& tb, const float*
                 load4<kI8>(grow, k, wg);
                 load4<kI8>(urow, k, wu);
                 if (kI8) {
-                    ga = __fmaf_rn(gsc[r * NG + k / a.G], dot4(wg, xv, 0.0f), ga);
-                    ua = __fmaf_rn(usc[r * NG + k / a.G], dot4(wu, xv, 0.0f), ua);
+                    ga = __fmaf_rn(gsc[r * NG + j], dot4(wg, xv, 0.0f), ga);
+                    ua = __fmaf_rn(usc[r * NG + j], dot4(wu, xv, 0.0f), ua);
                 } else {
                     ga = dot4(wg, xv, ga);
                     ua = dot4(wu, xv, ua);
@@ -559,9 +561,9 @@ constexpr int kMaxRowsCta = 16;
 template <bool kI8, int NJ>
 UOCR_DEV void down_item_t(const DecodeArgs& a, const SlotTable& tb, int slot, int q0, int nq, int nr,
                           const unsigned char* __restrict__ stage, int sc_off, int h_off, float* ybuf, int lane) {
+    // int8 groups are 128 wide along K: lane l's chunk j is group j
     const int I = NJ * 128;
     constexpr int esz = kI8 ? 1 : 2;
-    const int NG = I / a.G;
     const float* sc = reinterpret_cast<const float*>(stage + sc_off);
     const float* hs = reinterpret_cast<const float*>(stage + h_off);
     float4 hr[kDnTok][NJ];
@@ -572,38 +574,44 @@ UOCR_DEV void down_item_t(const DecodeArgs& a, const SlotTable& tb, int slot, in
             hr[q][j] = q < nq ? *reinterpret_cast<const float4*>(hs + (size_t)q * I + 4 * (lane + 32 * j))
                               : make_float4(0.f, 0.f, 0.f, 0.f);
     for (int r0 = 0; r0 < nr; r0 += 4) {
-        float acc[4][kDnTok];
+        float acc[4][kDnTok][2];
 #pragma unroll
-        for (int rr = 0; rr < 4; ++rr) {
-            const int r = min(r0 + rr, nr - 1);
-            const unsigned char* wrow = stage + (size_t)r * I * esz;
+        for (int rr = 0; rr < 4; ++rr)
 #pragma unroll
-            for (int q = 0; q < kDnTok; ++q) acc[rr][q] = 0.0f;
+            for (int q = 0; q < kDnTok; ++q) acc[rr][q][0] = acc[rr][q][1] = 0.0f;
 #pragma unroll
-            for (int j = 0; j < NJ; ++j) {
-                const int k = 4 * (lane + 32 * j);
+        for (int j = 0; j < NJ; ++j) {
+            const int k = 4 * (lane + 32 * j);
+#pragma unroll
+            for (int rr = 0; rr < 4; ++rr) {
+                const int r = min(r0 + rr, nr - 1);
                 float w[4];
-                load4<kI8>(wrow, k, w);
-                const float s = kI8 ? sc[r * NG + k / a.G] : 1.0f;
+                load4<kI8>(stage + (size_t)r * I * esz, k, w);
+                const float s = kI8 ? sc[r * NJ + j] : 1.0f;
 #pragma unroll
                 for (int q = 0; q < kDnTok; ++q)
-                    acc[rr][q] = kI8 ? __fmaf_rn(s, dot4(w, hr[q][j], 0.0f), acc[rr][q]) : dot4(w, hr[q][j], acc[rr][q]);
+                    acc[rr][q][j & 1] = kI8 ? __fmaf_rn(s, dot4(w, hr[q][j], 0.0f), acc[rr][q][j & 1])
+                                            : dot4(w, hr[q][j], acc[rr][q][j & 1]);
             }
         }
+        float v[4][kDnTok];
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr)
+#pragma unroll
+            for (int q = 0; q < kDnTok; ++q) v[rr][q] = __fadd_rn(acc[rr][q][0], acc[rr][q][1]);
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1)
 #pragma unroll
             for (int rr = 0; rr < 4; ++rr)
 #pragma unroll
-                for (int q = 0; q < kDnTok; ++q)
-                    acc[rr][q] = __fadd_rn(acc[rr][q], __shfl_xor_sync(0xffffffffu, acc[rr][q], off));
+                for (int q = 0; q < kDnTok; ++q) v[rr][q] = __fadd_rn(v[rr][q], __shfl_xor_sync(0xffffffffu, v[rr][q], off));
         if (lane == 0) {
 #pragma unroll
             for (int rr = 0; rr < 4; ++rr)
 #pragma unroll
                 for (int q = 0; q < kDnTok; ++q)
                     if (r0 + rr < nr && q < nq)
-                        ybuf[((size_t)slot * kMaxB + tb.token[slot][q0 + q]) * nr + r0 + rr] = acc[rr][q];
+                        ybuf[((size_t)slot * kMaxB + tb.token[slot][q0 + q]) * nr + r0 + rr] = v[rr][q];
         }
     }
 }
@@ -613,7 +621,7 @@ UOCR_DEV void down_item_any(const DecodeArgs& a, const SlotTable& tb, int slot, 
                             const unsigned char* __restrict__ stage, int sc_off, int h_off, float* ybuf, int lane) {
     const int I = a.I, NJ = I / 128;
     constexpr int esz = kI8 ? 1 : 2;
-    const int NG = I / a.G;
+    const int NG = NJ;  // groups of 128 along K
     const float* sc = reinterpret_cast<const float*>(stage + sc_off);
     const float* hs = reinterpret_cast<const float*>(stage + h_off);
     for (int r = 0; r < nr; ++r) {
@@ -623,7 +631,7 @@ UOCR_DEV void down_item_any(const DecodeArgs& a, const SlotTable& tb, int slot, 
             const int k = 4 * (lane + 32 * j);
             float w[4];
             load4<kI8>(wrow, k, w);
-            const float s = kI8 ? sc[r * NG + k / a.G] : 1.0f;
+            const float s = kI8 ? sc[r * NG + j] : 1.0f;
 #pragma unroll
             for (int q = 0; q < kDnTok; ++q) {
                 if (q < nq) {
