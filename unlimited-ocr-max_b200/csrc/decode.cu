@@ -308,37 +308,74 @@ UOCR_DEV void gu_decode(const DecodeArgs& a, const SlotTable& tb, int first, int
 // One warp, one item: kRB row pairs against up to kGuTok tokens. Lane l owns the 4-element
 // chunks k = 4(l + 32j), j < NJ = H/128. A token's chunks sit in registers while every row of the
 // item streams past; all rows' partial sums are reduced together (independent butterflies).
+// Weight words of one row for chunks j < NJ: int8 -> one u32 (4 weights), bf16 -> two u32.
+template <bool kI8, int NJ>
+UOCR_DEV void lds_row(uint32_t row, int lane, uint32_t (&w)[NJ][kI8 ? 1 : 2]) {
+#pragma unroll
+    for (int j = 0; j < NJ; ++j) {
+        const uint32_t k = 4u * (lane + 32 * j);
+        if (kI8) {
+            w[j][0] = lds_u32(row + k);
+        } else {
+            const uint2 v = lds_u64(row + 2 * k);
+            w[j][0] = v.x;
+            w[j][kI8 ? 0 : 1] = v.y;
+        }
+    }
+}
+
+template <bool kI8>
+UOCR_DEV void unpack4(const uint32_t* w, float (&f)[4]) {
+    if (kI8) {
+        const uint32_t v = w[0] ^ 0x80808080u;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) f[i] = s8_byte_to_f32(v, i);
+    } else {
+        f[0] = bf16lo(w[0]); f[1] = bf16hi(w[0]); f[2] = bf16lo(w[1]); f[3] = bf16hi(w[1]);
+    }
+}
+
 template <bool kI8, int kRB, int NJ>
 UOCR_DEV void gu_item_t(const DecodeArgs& a, const SlotTable& tb, const float* __restrict__ xs, int slot, int rows0,
                         int q0, int nq, const unsigned char* __restrict__ stage, int sc_off, int lane) {
     // int8 groups are 128 wide along K and lane l's chunk j is k = 4(l + 32j): group j
     const int H = NJ * 128;
     constexpr int esz = kI8 ? 1 : 2;
-    const float* gsc = reinterpret_cast<const float*>(stage + sc_off);
-    const float* usc = gsc + kRB * NJ;
+    const uint32_t st_s = smem_addr(stage);
+    const uint32_t xs_s = smem_addr(xs);
+    const uint32_t gsc_s = st_s + sc_off;
+    const uint32_t usc_s = gsc_s + kRB * NJ * 4;
     for (int q = 0; q < nq; ++q) {
         const int t = tb.token[slot][q0 + q];
         const int pair = tb.pair[slot][q0 + q];
         float4 xr[NJ];
 #pragma unroll
-        for (int j = 0; j < NJ; ++j) xr[j] = *reinterpret_cast<const float4*>(xs + (size_t)t * H + 4 * (lane + 32 * j));
+        for (int j = 0; j < NJ; ++j) xr[j] = lds_f128(xs_s + 4u * ((uint32_t)t * H + 4 * (lane + 32 * j)));
 #pragma unroll 1
         for (int r = 0; r < kRB; ++r) {
-            // one row pair, four chains: gate / up x even / odd chunks
+            uint32_t wg[NJ][kI8 ? 1 : 2], wu[NJ][kI8 ? 1 : 2];
+            lds_row<kI8, NJ>(st_s + (uint32_t)r * H * esz, lane, wg);
+            lds_row<kI8, NJ>(st_s + (uint32_t)(kRB + r) * H * esz, lane, wu);
+            float sg[NJ], su[NJ];
+            if (kI8) {
+#pragma unroll
+                for (int j = 0; j < NJ; ++j) {
+                    sg[j] = lds_f32(gsc_s + 4u * (r * NJ + j));
+                    su[j] = lds_f32(usc_s + 4u * (r * NJ + j));
+                }
+            }
             float acc[2][2] = {{0.0f, 0.0f}, {0.0f, 0.0f}};
 #pragma unroll
             for (int j = 0; j < NJ; ++j) {
-                const int k = 4 * (lane + 32 * j);
-#pragma unroll
-                for (int gu = 0; gu < 2; ++gu) {
-                    float w[4];
-                    load4<kI8>(stage + (size_t)(gu * kRB + r) * H * esz, k, w);
-                    if (kI8) {
-                        const float sc = (gu ? usc : gsc)[r * NJ + j];
-                        acc[gu][j & 1] = __fmaf_rn(sc, dot4(w, xr[j], 0.0f), acc[gu][j & 1]);
-                    } else {
-                        acc[gu][j & 1] = dot4(w, xr[j], acc[gu][j & 1]);
-                    }
+                float fg[4], fu[4];
+                unpack4<kI8>(wg[j], fg);
+                unpack4<kI8>(wu[j], fu);
+                if (kI8) {
+                    acc[0][j & 1] = __fmaf_rn(sg[j], dot4(fg, xr[j], 0.0f), acc[0][j & 1]);
+                    acc[1][j & 1] = __fmaf_rn(su[j], dot4(fu, xr[j], 0.0f), acc[1][j & 1]);
+                } else {
+                    acc[0][j & 1] = dot4(fg, xr[j], acc[0][j & 1]);
+                    acc[1][j & 1] = dot4(fu, xr[j], acc[1][j & 1]);
                 }
             }
             float g = __fadd_rn(acc[0][0], acc[0][1]);
@@ -564,50 +601,52 @@ UOCR_DEV void down_item_t(const DecodeArgs& a, const SlotTable& tb, int slot, in
     // int8 groups are 128 wide along K: lane l's chunk j is group j
     const int I = NJ * 128;
     constexpr int esz = kI8 ? 1 : 2;
-    const float* sc = reinterpret_cast<const float*>(stage + sc_off);
-    const float* hs = reinterpret_cast<const float*>(stage + h_off);
+    const uint32_t st_s = smem_addr(stage);
+    const uint32_t sc_s = st_s + sc_off;
+    const uint32_t hs_s = st_s + h_off;
     float4 hr[kDnTok][NJ];
 #pragma unroll
     for (int q = 0; q < kDnTok; ++q)
 #pragma unroll
         for (int j = 0; j < NJ; ++j)
-            hr[q][j] = q < nq ? *reinterpret_cast<const float4*>(hs + (size_t)q * I + 4 * (lane + 32 * j))
+            hr[q][j] = q < nq ? lds_f128(hs_s + 4u * ((uint32_t)q * I + 4 * (lane + 32 * j)))
                               : make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int r0 = 0; r0 < nr; r0 += 4) {
-        float acc[4][kDnTok][2];
+    for (int r0 = 0; r0 < nr; r0 += 2) {
+        float v[2][kDnTok];
 #pragma unroll
-        for (int rr = 0; rr < 4; ++rr)
+        for (int rr = 0; rr < 2; ++rr) {
+            const int r = min(r0 + rr, nr - 1);
+            uint32_t w[NJ][kI8 ? 1 : 2];
+            lds_row<kI8, NJ>(st_s + (uint32_t)r * I * esz, lane, w);
+            float s[NJ];
+            if (kI8) {
 #pragma unroll
-            for (int q = 0; q < kDnTok; ++q) acc[rr][q][0] = acc[rr][q][1] = 0.0f;
+                for (int j = 0; j < NJ; ++j) s[j] = lds_f32(sc_s + 4u * (r * NJ + j));
+            }
+            float acc[kDnTok][2];
 #pragma unroll
-        for (int j = 0; j < NJ; ++j) {
-            const int k = 4 * (lane + 32 * j);
+            for (int q = 0; q < kDnTok; ++q) acc[q][0] = acc[q][1] = 0.0f;
 #pragma unroll
-            for (int rr = 0; rr < 4; ++rr) {
-                const int r = min(r0 + rr, nr - 1);
-                float w[4];
-                load4<kI8>(stage + (size_t)r * I * esz, k, w);
-                const float s = kI8 ? sc[r * NJ + j] : 1.0f;
+            for (int j = 0; j < NJ; ++j) {
+                float f[4];
+                unpack4<kI8>(w[j], f);
 #pragma unroll
                 for (int q = 0; q < kDnTok; ++q)
-                    acc[rr][q][j & 1] = kI8 ? __fmaf_rn(s, dot4(w, hr[q][j], 0.0f), acc[rr][q][j & 1])
-                                            : dot4(w, hr[q][j], acc[rr][q][j & 1]);
+                    acc[q][j & 1] = kI8 ? __fmaf_rn(s[j], dot4(f, hr[q][j], 0.0f), acc[q][j & 1])
+                                        : dot4(f, hr[q][j], acc[q][j & 1]);
             }
+#pragma unroll
+            for (int q = 0; q < kDnTok; ++q) v[rr][q] = __fadd_rn(acc[q][0], acc[q][1]);
         }
-        float v[4][kDnTok];
-#pragma unroll
-        for (int rr = 0; rr < 4; ++rr)
-#pragma unroll
-            for (int q = 0; q < kDnTok; ++q) v[rr][q] = __fadd_rn(acc[rr][q][0], acc[rr][q][1]);
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1)
 #pragma unroll
-            for (int rr = 0; rr < 4; ++rr)
+            for (int rr = 0; rr < 2; ++rr)
 #pragma unroll
                 for (int q = 0; q < kDnTok; ++q) v[rr][q] = __fadd_rn(v[rr][q], __shfl_xor_sync(0xffffffffu, v[rr][q], off));
         if (lane == 0) {
 #pragma unroll
-            for (int rr = 0; rr < 4; ++rr)
+            for (int rr = 0; rr < 2; ++rr)
 #pragma unroll
                 for (int q = 0; q < kDnTok; ++q)
                     if (r0 + rr < nr && q < nq)

@@ -94,6 +94,29 @@ UOCR_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar
         : "memory");
 }
 
+// ---- explicit shared-memory loads (32-bit shared addresses) --------------------------------
+// The hot loops read their stages through these so every access is an LDS, never a generic load.
+UOCR_DEV uint32_t lds_u32(uint32_t a) {
+    uint32_t v;
+    asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
+    return v;
+}
+UOCR_DEV uint2 lds_u64(uint32_t a) {
+    uint2 v;
+    asm volatile("ld.shared.v2.u32 {%0, %1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
+    return v;
+}
+UOCR_DEV float lds_f32(uint32_t a) {
+    float v;
+    asm volatile("ld.shared.f32 %0, [%1];" : "=f"(v) : "r"(a));
+    return v;
+}
+UOCR_DEV float4 lds_f128(uint32_t a) {
+    float4 v;
+    asm volatile("ld.shared.v4.f32 {%0, %1, %2, %3}, [%4];" : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w) : "r"(a));
+    return v;
+}
+
 // ---- global flags with gpu-scope ordering -------------------------------------------------
 UOCR_DEV uint32_t ld_acquire_gpu(const uint32_t* p) {
     uint32_t v;
