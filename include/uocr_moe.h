@@ -157,10 +157,10 @@ UOCR_API int uocr_moe_decode_noalloc(const uocr_moe_layer* L, const float* x, in
                                      const float* bias, float* out, uocr_stream_t stream);
 
 /* Diagnostics: record a per-CTA timeline of the work items of subsequent uocr_moe_decode
- * launches into `device_buffer` (zero-filled by the caller; per item: wait start, data ready,
- * item done in global-timer ns, and type/slot/block). NULL turns recording off. Not
- * thread-safe; for profiling only. No counterpart in the reference (its profiler is
- * server-level). */
+ * launches into `device_buffer` (zero-filled by the caller; per item 8 words: consumer wait
+ * start, data ready, item done, slot/rows, producer issue time, all in global-timer ns).
+ * NULL turns recording off. Not thread-safe; for profiling only. No counterpart in the
+ * reference (its profiler is server-level). */
 UOCR_API int uocr_moe_decode_set_trace(void* device_buffer, size_t bytes);
 
 /* Status word of a workspace after the stream's work finished (synchronises `stream`):

@@ -115,10 +115,11 @@ UOCR_DEV float dot4(const float (&w)[4], const float4& x, float acc) {
     return acc;
 }
 
-// Diagnostics timeline: per CTA `items` records of {wait start, data ready, done, slot<<32|n}.
+// Diagnostics timeline: per CTA `items` records of 8 words
+// {consumer wait start, data ready, done, slot<<32|rows, producer issue, 0, 0, 0} (global-timer ns).
 UOCR_DEV unsigned long long* trace_rec(const DecodeArgs& a, int half, int n) {
     if (!a.trace || n >= a.trace_items / 2) return nullptr;
-    return a.trace + ((size_t)blockIdx.x * a.trace_items + (size_t)half * (a.trace_items / 2) + n) * 4;
+    return a.trace + ((size_t)blockIdx.x * a.trace_items + (size_t)half * (a.trace_items / 2) + n) * 8;
 }
 
 // ======================================================================================
@@ -543,6 +544,10 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                     if (lane == 2) bulk_g2s(dst + 2 * blk, sb + (size_t)pg0 * NG * 4, scb, &full[st]);
                     if (lane == 3) bulk_g2s(dst + 2 * blk + scb, sb + (size_t)(pg0 + 128) * NG * 4, scb, &full[st]);
                 }
+                if (lane == 0) {
+                    unsigned long long* tr = trace_rec(a, 0, n);
+                    if (tr) tr[4] = global_timer_ns();
+                }
                 __syncwarp();
                 ++n;
             }
@@ -792,6 +797,10 @@ decode_down_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl
                 if (lane < nq)
                     bulk_g2s(dst + h_off + (size_t)lane * hrow, a.h + (size_t)tb->pair[slot][q0 + lane] * a.I, hrow,
                              &full[st]);
+                if (lane == 0) {
+                    unsigned long long* tr = trace_rec(a, 1, n);
+                    if (tr) tr[4] = global_timer_ns();
+                }
                 __syncwarp();
                 ++n;
             }
@@ -880,7 +889,7 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     if (g_decode_trace) {
         a.trace = g_decode_trace;
-        a.trace_items = (int)(g_decode_trace_bytes / (sizeof(unsigned long long) * 4 * (size_t)sms)) & ~1;
+        a.trace_items = (int)(g_decode_trace_bytes / (sizeof(unsigned long long) * 8 * (size_t)sms)) & ~1;
     }
 
     // ---- K1
