@@ -489,8 +489,12 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
 
     if (warp == kCW) {
         // ---------------- producer ----------------
-        int n = 0;
+        // Each CTA takes a contiguous range of the phase's items and walks it incrementally
+        // (slot, row block, token group), so the per-item work is a handful of instructions.
+        int n = 0, st = 0;
+        uint32_t round = 0;
         bool ok = true;
+        const int NG = a.H / a.G;
         for (int phase = 0; phase < 2 && ok; ++phase) {
             if (phase == 1) {
                 pdl_wait_prior_grid();  // the routing table
@@ -499,29 +503,41 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             const int first = phase == 0 ? 0 : a.S;
             const int last = phase == 0 ? a.S : tb->nslot;
             int total = 0;
-            for (int s = first; s < last; ++s) total += gu_items_of(a, *tb, s);
-            int cur_slot = first, cur_base = 0;  // items of slots before cur_slot
-            for (int i = blockIdx.x; i < total; i += gridDim.x) {
-                while (i >= cur_base + gu_items_of(a, *tb, cur_slot)) cur_base += gu_items_of(a, *tb, cur_slot++);
-                const int ntg = (tb->count[cur_slot] + kGuTok - 1) / kGuTok;
-                const int slot = cur_slot, rblk = (i - cur_base) / ntg, tg = (i - cur_base) % ntg;
-                const int st = n % nst, round = n / nst;
+            for (int s2 = first; s2 < last; ++s2) total += gu_items_of(a, *tb, s2);
+            const int lo = (int)((long)blockIdx.x * total / gridDim.x);
+            const int hi = (int)((long)(blockIdx.x + 1) * total / gridDim.x);
+            if (lo >= hi) continue;
+            int slot = first, base = 0;
+            while (lo >= base + gu_items_of(a, *tb, slot)) base += gu_items_of(a, *tb, slot++);
+            // per-slot constants
+            int count = 0, ntg = 0, RB = 0, nrb = 0, esz = 0;
+            bool i8 = false;
+            uint32_t blk = 0, scb = 0;
+            const unsigned char* wbase = nullptr;
+            const unsigned char* sbase = nullptr;
+            auto enter_slot = [&](int sl) {
+                count = tb->count[sl];
+                ntg = (count + kGuTok - 1) / kGuTok;
+                i8 = sl >= a.S && a.int8;
+                RB = i8 ? 4 : 2;
+                nrb = a.I / RB;
+                esz = i8 ? 1 : 2;
+                blk = (uint32_t)RB * a.H * esz;
+                scb = (uint32_t)RB * NG * 4;
+                const int e = tb->expert[sl];
+                wbase = sl < a.S ? reinterpret_cast<const unsigned char*>(a.w13_shared) + (size_t)e * 2 * a.I * a.H * 2
+                                 : reinterpret_cast<const unsigned char*>(a.w13) + (size_t)e * 2 * a.I * a.H * esz;
+                sbase = i8 ? reinterpret_cast<const unsigned char*>(a.s13) + (size_t)e * 2 * a.I * NG * 4 : nullptr;
+            };
+            enter_slot(slot);
+            int rblk = (lo - base) / ntg, tg = (lo - base) % ntg;
+            for (int i = lo; i < hi; ++i) {
                 if (round > 0 && !mbar_wait_warp(&empty[st], (round - 1) & 1, nullptr, &a.ctl->status)) {
                     ok = false;
                     break;
                 }
-                const bool i8 = slot >= a.S && a.int8;
-                const int RB = gu_rb(a, slot);
-                const int esz = i8 ? 1 : 2;
-                const uint32_t blk = (uint32_t)RB * a.H * esz;
                 const int n0 = rblk * RB;
                 const int pg0 = (n0 / 128) * 256 + (n0 % 128);
-                const int e = tb->expert[slot];
-                const unsigned char* wbase =
-                    slot < a.S ? reinterpret_cast<const unsigned char*>(a.w13_shared) + (size_t)e * 2 * a.I * a.H * 2
-                               : reinterpret_cast<const unsigned char*>(a.w13) + (size_t)e * 2 * a.I * a.H * esz;
-                const int NG = a.H / a.G;
-                const uint32_t scb = (uint32_t)RB * NG * 4;
                 unsigned char* dst = stages + (size_t)st * stage_bytes;
                 if (lane == 0) {
                     ItemMeta& m = meta[st];
@@ -530,26 +546,29 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                     m.rows0 = n0;
                     m.nrows = RB;
                     m.q0 = tg * kGuTok;
-                    m.nq = min(kGuTok, tb->count[slot] - tg * kGuTok);
+                    m.nq = min(kGuTok, count - tg * kGuTok);
                     m.sc_off = (int)(2 * blk);
                     m.h_off = 0;
                     mbar_arrive_expect_tx(&full[st], 2 * blk + (i8 ? 2 * scb : 0));
-                }
-                __syncwarp();
-                if (lane == 0) bulk_g2s(dst, wbase + (size_t)pg0 * a.H * esz, blk, &full[st]);
-                if (lane == 1) bulk_g2s(dst + blk, wbase + (size_t)(pg0 + 128) * a.H * esz, blk, &full[st]);
-                if (i8) {
-                    const unsigned char* sb =
-                        reinterpret_cast<const unsigned char*>(a.s13) + (size_t)e * 2 * a.I * NG * 4;
-                    if (lane == 2) bulk_g2s(dst + 2 * blk, sb + (size_t)pg0 * NG * 4, scb, &full[st]);
-                    if (lane == 3) bulk_g2s(dst + 2 * blk + scb, sb + (size_t)(pg0 + 128) * NG * 4, scb, &full[st]);
-                }
-                if (lane == 0) {
+                    bulk_g2s(dst, wbase + (size_t)pg0 * a.H * esz, blk, &full[st]);
+                    bulk_g2s(dst + blk, wbase + (size_t)(pg0 + 128) * a.H * esz, blk, &full[st]);
+                    if (i8) {
+                        bulk_g2s(dst + 2 * blk, sbase + (size_t)pg0 * NG * 4, scb, &full[st]);
+                        bulk_g2s(dst + 2 * blk + scb, sbase + (size_t)(pg0 + 128) * NG * 4, scb, &full[st]);
+                    }
                     unsigned long long* tr = trace_rec(a, 0, n);
                     if (tr) tr[4] = global_timer_ns();
                 }
                 __syncwarp();
                 ++n;
+                if (++st == nst) { st = 0; ++round; }
+                if (++tg == ntg) {
+                    tg = 0;
+                    if (++rblk == nrb) {
+                        rblk = 0;
+                        if (++slot < last) enter_slot(slot);
+                    }
+                }
             }
         }
         if (lane == 0) {
@@ -559,24 +578,25 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             } else {
                 // one end marker per consumer warp (stage n belongs to warp n % 8)
                 for (int w = 0; w < kCW; ++w, ++n) {
-                    const int st = n % nst, round = n / nst;
                     if (round > 0 && !mbar_wait(&empty[st], (round - 1) & 1, &a.ctl->status)) {
                         abort_flag = 1;
                         break;
                     }
                     meta[st].type = 0;
                     mbar_arrive(&full[st]);
+                    if (++st == nst) { st = 0; ++round; }
                 }
             }
         }
         __syncwarp();
     } else {
         // ---------------- consumer warp: ring entries warp, warp + 8, ... ----------------
+        int st = warp;
+        uint32_t par = 0;
         for (int n = warp;; n += kCW) {
-            const int st = n % nst;
             unsigned long long* tr = trace_rec(a, 0, n);
             if (tr && lane == 0) tr[0] = global_timer_ns();
-            if (!mbar_wait_warp(&full[st], (n / nst) & 1, &abort_flag, &a.ctl->status)) break;
+            if (!mbar_wait_warp(&full[st], par, &abort_flag, &a.ctl->status)) break;
             const ItemMeta& m = meta[st];
             if (m.type == 0) break;
             if (tr && lane == 0) tr[1] = global_timer_ns();
@@ -588,6 +608,8 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                 tr[3] = ((unsigned long long)m.slot << 32) | (unsigned)m.rows0;
             }
             if (lane == 0) mbar_arrive(&empty[st]);
+            st += kCW;
+            if (st >= nst) { st -= nst; par ^= 1; }
         }
     }
 }
@@ -737,7 +759,8 @@ decode_down_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl
 
     if (warp == kCW3) {
         // ---------------- producer ----------------
-        int n = 0;
+        int n = 0, st = 0;
+        uint32_t round = 0;
         bool ok = true;
         bool waited = false;
         for (int slot = 0; ok; ++slot) {
@@ -766,7 +789,6 @@ decode_down_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl
             const int c = tb->count[slot];
             for (int q0 = 0; q0 < c; q0 += kDnTok) {
                 const int nq = min(kDnTok, c - q0);
-                const int st = n % nst, round = n / nst;
                 if (round > 0 && !mbar_wait_warp(&empty[st], (round - 1) & 1, nullptr, &a.ctl->status)) {
                     ok = false;
                     break;
@@ -803,6 +825,7 @@ decode_down_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl
                 }
                 __syncwarp();
                 ++n;
+                if (++st == nst) { st = 0; ++round; }
             }
         }
         if (lane == 0) {
@@ -811,23 +834,24 @@ decode_down_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl
                 for (int q = max(0, n - nst); q < n; ++q) mbar_wait(&full[q % nst], (q / nst) & 1, nullptr);
             } else {
                 for (int w = 0; w < kCW3; ++w, ++n) {
-                    const int st = n % nst, round = n / nst;
                     if (round > 0 && !mbar_wait(&empty[st], (round - 1) & 1, &a.ctl->status)) {
                         abort_flag = 1;
                         break;
                     }
                     meta[st].type = 0;
                     mbar_arrive(&full[st]);
+                    if (++st == nst) { st = 0; ++round; }
                 }
             }
         }
         __syncwarp();
     } else {
+        int st = warp;
+        uint32_t par = 0;
         for (int n = warp;; n += kCW3) {
-            const int st = n % nst;
             unsigned long long* tr = trace_rec(a, 1, n);
             if (tr && lane == 0) tr[0] = global_timer_ns();
-            if (!mbar_wait_warp(&full[st], (n / nst) & 1, &abort_flag, &a.ctl->status)) break;
+            if (!mbar_wait_warp(&full[st], par, &abort_flag, &a.ctl->status)) break;
             const ItemMeta& m = meta[st];
             if (m.type == 0) break;
             if (tr && lane == 0) tr[1] = global_timer_ns();
@@ -839,6 +863,8 @@ decode_down_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl
                 tr[3] = ((unsigned long long)m.slot << 32) | (unsigned)m.q0;
             }
             if (lane == 0) mbar_arrive(&empty[st]);
+            st += kCW3;
+            if (st >= nst) { st -= nst; par ^= 1; }
         }
     }
     __syncthreads();
