@@ -532,9 +532,15 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             enter_slot(slot);
             int rblk = (lo - base) / ntg, tg = (lo - base) % ntg;
             for (int i = lo; i < hi; ++i) {
+                unsigned long long t_top = 0;
+                if (a.trace && lane == 0) t_top = global_timer_ns();
                 if (round > 0 && !mbar_wait_warp(&empty[st], (round - 1) & 1, nullptr, &a.ctl->status)) {
                     ok = false;
                     break;
+                }
+                if (a.trace && lane == 0) {
+                    unsigned long long* tr = trace_rec(a, 0, n);
+                    if (tr) { tr[6] = t_top; tr[5] = global_timer_ns(); }
                 }
                 const int n0 = rblk * RB;
                 const int pg0 = (n0 / 128) * 256 + (n0 % 128);
@@ -550,12 +556,18 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                     m.sc_off = (int)(2 * blk);
                     m.h_off = 0;
                     mbar_arrive_expect_tx(&full[st], 2 * blk + (i8 ? 2 * scb : 0));
-                    bulk_g2s(dst, wbase + (size_t)pg0 * a.H * esz, blk, &full[st]);
-                    bulk_g2s(dst + blk, wbase + (size_t)(pg0 + 128) * a.H * esz, blk, &full[st]);
-                    if (i8) {
-                        bulk_g2s(dst + 2 * blk, sbase + (size_t)pg0 * NG * 4, scb, &full[st]);
-                        bulk_g2s(dst + 2 * blk + scb, sbase + (size_t)(pg0 + 128) * NG * 4, scb, &full[st]);
-                    }
+                }
+                __syncwarp();
+                // the item's copies, one per lane, issued by a single instruction
+                {
+                    const int up = lane & 1;                // 0: gate block, 1: up block
+                    const bool is_sc = lane >= 2;           // lanes 2, 3: the int8 scales
+                    const int prow = pg0 + (up ? 128 : 0);
+                    unsigned char* d = dst + (is_sc ? 2 * blk + up * scb : up * blk);
+                    const unsigned char* src = is_sc ? sbase + (size_t)prow * NG * 4 : wbase + (size_t)prow * a.H * esz;
+                    if (lane < (i8 ? 4 : 2)) bulk_g2s(d, src, is_sc ? scb : blk, &full[st]);
+                }
+                if (lane == 0) {
                     unsigned long long* tr = trace_rec(a, 0, n);
                     if (tr) tr[4] = global_timer_ns();
                 }
@@ -807,18 +819,36 @@ decode_down_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl
                     mbar_arrive_expect_tx(&full[st], wbytes + (i8 ? scb : 0u) + (uint32_t)nq * hrow);
                 }
                 __syncwarp();
-                // weights first: they do not depend on the previous kernel
-                if (lane == 0) bulk_g2s(dst, wbase + (size_t)j0 * a.I * esz, wbytes, &full[st]);
-                if (i8 && lane == 1)
-                    bulk_g2s(dst + wbytes, reinterpret_cast<const unsigned char*>(a.s2) + sc_a, scb, &full[st]);
                 if (!waited) {
-                    pdl_wait_prior_grid();  // h comes from K2
+                    // h comes from K2; the first item's weight copy is issued before the wait
+                    if (lane == 0) bulk_g2s(dst, wbase + (size_t)j0 * a.I * esz, wbytes, &full[st]);
+                    if (i8 && lane == 1)
+                        bulk_g2s(dst + wbytes, reinterpret_cast<const unsigned char*>(a.s2) + sc_a, scb, &full[st]);
+                    pdl_wait_prior_grid();
                     waited = true;
+                    __syncwarp();
+                    if (lane < nq)
+                        bulk_g2s(dst + h_off + (size_t)lane * hrow, a.h + (size_t)tb->pair[slot][q0 + lane] * a.I,
+                                 hrow, &full[st]);
+                } else {
+                    // lane 0 weights, lane 1 int8 scales, lanes 2.. the tokens' h rows: one instruction
+                    unsigned char* d;
+                    const void* src;
+                    uint32_t bytes;
+                    bool go;
+                    if (lane == 0) {
+                        d = dst; src = wbase + (size_t)j0 * a.I * esz; bytes = wbytes; go = true;
+                    } else if (lane == 1) {
+                        d = dst + wbytes; src = reinterpret_cast<const unsigned char*>(a.s2) + sc_a; bytes = scb; go = i8;
+                    } else {
+                        const int q = lane - 2;
+                        d = dst + h_off + (size_t)q * hrow;
+                        src = a.h + (size_t)tb->pair[slot][q0 + min(q, nq - 1)] * a.I;
+                        bytes = hrow;
+                        go = q < nq;
+                    }
+                    if (go) bulk_g2s(d, src, bytes, &full[st]);
                 }
-                __syncwarp();
-                if (lane < nq)
-                    bulk_g2s(dst + h_off + (size_t)lane * hrow, a.h + (size_t)tb->pair[slot][q0 + lane] * a.I, hrow,
-                             &full[st]);
                 if (lane == 0) {
                     unsigned long long* tr = trace_rec(a, 1, n);
                     if (tr) tr[4] = global_timer_ns();
