@@ -144,6 +144,20 @@ UOCR_API int uocr_moe_decode(const uocr_moe_layer* L, const float* x, int64_t B,
                     float* out, int32_t* ids_out, float* wts_out,
                     void* workspace, size_t workspace_bytes, uocr_stream_t stream);
 
+/* Prefill (MoE.__call__, decoder.py:657-667, routed part as _routed_native, decoder.py:606-614:
+ * moe_create_indices + grouped_matmul_ragged + the weighted mix): x [T, H] fp32, T >= 1 ->
+ * out [T, H] fp32. Tokens are permuted into expert-contiguous rows and both expert
+ * projections run as grouped bf16 GEMMs on the tensor cores (fp32 accumulate, bf16
+ * activations between them); int8 stacks are dequantized to bf16 first with
+ * int8_dequant_expert's bits. Needs hidden a multiple of 256. ids_out / wts_out (nullable)
+ * receive the routing, bit-identical to uocr_moe_route. `workspace` must hold
+ * uocr_moe_prefill_workspace_bytes(L, T) bytes (256-byte aligned; its first word is the
+ * device status word: zero-fill it once). */
+UOCR_API size_t uocr_moe_prefill_workspace_bytes(const uocr_moe_layer* L, int64_t T);
+UOCR_API int uocr_moe_prefill(const uocr_moe_layer* L, const float* x, int64_t T, const float* bias,
+                              float* out, int32_t* ids_out, float* wts_out,
+                              void* workspace, size_t workspace_bytes, uocr_stream_t stream);
+
 /* Decode step without a caller workspace. No counterpart in the reference: added for callers
  * that cannot allocate device memory (a plugin host that passes an operator only its inputs
  * and outputs, or a runtime whose device memory is reserved up front). Same computation as

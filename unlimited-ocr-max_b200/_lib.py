@@ -56,6 +56,8 @@ SIGNATURES: dict[str, tuple] = {
     "uocr_moe_route": (I32, [P, I64, I64, P, I64, P, I64, P, P, P]),
     "uocr_moe_decode_workspace_bytes": (SZ, [ctypes.POINTER(UocrMoeLayer), I64]),
     "uocr_moe_decode": (I32, [ctypes.POINTER(UocrMoeLayer), P, I64, P, P, P, P, P, SZ, P]),
+    "uocr_moe_prefill_workspace_bytes": (SZ, [ctypes.POINTER(UocrMoeLayer), I64]),
+    "uocr_moe_prefill": (I32, [ctypes.POINTER(UocrMoeLayer), P, I64, P, P, P, P, P, SZ, P]),
     "uocr_moe_device_status": (I32, [P, P]),
     "uocr_moe_decode_set_trace": (I32, [P, SZ]),
     "uocr_moe_decode_noalloc_max_bytes": (SZ, []),

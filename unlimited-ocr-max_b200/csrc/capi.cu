@@ -310,6 +310,41 @@ int uocr_moe_decode(const uocr_moe_layer* L, const float* x, int64_t B, const fl
     return cuda_status(uocr::launch_decode_layer(a, S(stream)), "moe_decode: launch");
 }
 
+size_t uocr_moe_prefill_workspace_bytes(const uocr_moe_layer* L, int64_t T) {
+    if (!L || T < 1 || T > (int64_t(1) << 24)) return 0;
+    return uocr::prefill_layout((int)T, L->hidden, L->inter, L->n_routed, L->n_shared, L->top_k, L->int8 != 0).total;
+}
+
+int uocr_moe_prefill(const uocr_moe_layer* L, const float* x, int64_t T, const float* bias, float* out,
+                     int32_t* ids_out, float* wts_out, void* workspace, size_t workspace_bytes, uocr_stream_t stream) {
+    int rc = check_layer(L, "moe_prefill");
+    if (rc) return rc;
+    if (T < 1 || T > (int64_t(1) << 24)) return fail(UOCR_EINVAL, "moe_prefill: T=%lld outside 1..2^24", (long long)T);
+    if ((int64_t)(L->top_k + L->n_shared) * T >= (int64_t(1) << 31))
+        return fail(UOCR_EUNSUPPORTED, "moe_prefill: (top_k + n_shared) * T rows exceed int32");
+    if (L->n_shared > uocr::kDecodeMaxShared) return fail(UOCR_EUNSUPPORTED, "moe_prefill: more than 8 shared experts");
+    if (L->hidden % 256) return fail(UOCR_EUNSUPPORTED, "moe_prefill: hidden=%d must be a multiple of 256", L->hidden);
+    if (!x || !out || !workspace) return fail(UOCR_EINVAL, "moe_prefill: null pointer");
+    if (!a16(x) || !a16(out)) return fail(UOCR_EINVAL, "moe_prefill: x and out must be 16-byte aligned");
+    if (bias && (reinterpret_cast<uintptr_t>(bias) & 3)) return fail(UOCR_EINVAL, "moe_prefill: bias must be 4-byte aligned");
+    if (reinterpret_cast<uintptr_t>(workspace) & 255) return fail(UOCR_EINVAL, "moe_prefill: workspace must be 256-byte aligned");
+    const uocr::PrefillLayout d =
+        uocr::prefill_layout((int)T, L->hidden, L->inter, L->n_routed, L->n_shared, L->top_k, L->int8 != 0);
+    if (workspace_bytes < d.total)
+        return fail(UOCR_EINVAL, "moe_prefill: workspace of %zu bytes, need %zu", workspace_bytes, d.total);
+    char* ws = reinterpret_cast<char*>(workspace);
+    uocr::PrefillArgs a{};
+    a.T = (int)T; a.H = L->hidden; a.I = L->inter; a.E = L->n_routed; a.S = L->n_shared; a.topk = L->top_k;
+    a.G = L->int8 ? L->group : 128; a.int8 = L->int8;
+    a.x = x; a.router = L->router; a.bias = bias;
+    a.ids = ids_out ? ids_out : reinterpret_cast<int32_t*>(ws + d.ids);
+    a.wts = wts_out ? wts_out : reinterpret_cast<float*>(ws + d.wts);
+    a.w13 = L->w13; a.s13 = L->s13; a.w2 = L->w2; a.s2 = L->s2;
+    a.w13_shared = L->w13_shared; a.w2_shared = L->w2_shared;
+    a.out = out;
+    return cuda_status(uocr::launch_prefill(a, ws, d, S(stream)), "moe_prefill: launch");
+}
+
 int uocr_moe_decode_set_trace(void* device_buffer, size_t bytes) {
     uocr::g_decode_trace = reinterpret_cast<unsigned long long*>(device_buffer);
     uocr::g_decode_trace_bytes = device_buffer ? bytes : 0;

@@ -69,6 +69,44 @@ extern unsigned long long* g_decode_trace;
 extern size_t g_decode_trace_bytes;
 cudaError_t launch_decode_layer(const DecodeArgs& a, cudaStream_t st);
 
+// prefill.cu
+constexpr int kPrefillMaxGroups = 64 + kDecodeMaxShared;
+
+// One GEMM group: `rows` consecutive rows of A from `a_base`, written to output rows from
+// `out_base`, against weight stack `wrow0` of the routed (shared == 0) or shared weights.
+struct PrefillGroup {
+    int a_base, out_base, rows, wrow0, shared;
+};
+// The groups with at least one row, and the prefix of their 128-row M tiles.
+struct PrefillPlan {
+    int ngroups;
+    int pad[3];
+    int mtile_prefix[kPrefillMaxGroups + 1];
+    PrefillGroup g[kPrefillMaxGroups];
+};
+
+struct PrefillArgs {
+    int T, H, I, E, S, topk, G, int8;
+    const float* x;  // [T, H]
+    const uint16_t* router;
+    const float* bias;
+    int32_t* ids;  // [T, topk]
+    float* wts;    // [T, topk]
+    const void* w13;
+    const float* s13;
+    const void* w2;
+    const float* s2;
+    const uint16_t* w13_shared;
+    const uint16_t* w2_shared;
+    float* out;  // [T, H]
+};
+// Byte offsets of the prefill workspace regions (status word first).
+struct PrefillLayout {
+    size_t status, ids, wts, chunk_counts, chunk_base, plan1, plan2, dest, src_tok, xperm, h, y, w13, w2, total;
+};
+PrefillLayout prefill_layout(int T, int H, int I, int E, int S, int topk, bool int8);
+cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& d, cudaStream_t st);
+
 // pack.cu
 cudaError_t launch_pack_gate_up(const void* gate, const void* up, long E, long I, long H, int esz, void* out,
                                 cudaStream_t st);

@@ -1,0 +1,553 @@
+// Prefill MoE sublayer (MoE.__call__, unlimited_ocr_max/decoder.py:657-667; the accelerator path
+// _routed_native, decoder.py:606-614, which routes through moe_create_indices +
+// grouped_matmul_ragged): tokens are permuted into expert-contiguous rows and the expert
+// products run as grouped GEMMs on the tcgen05 tensor cores (bf16 operands, fp32 accumulate).
+//
+//   route      route.cu (bit-exact gate)
+//   permute    counting sort of the T*k (token, slot) entries by expert, stable in entry order
+//              (chunk histograms -> scan -> warp-match ranks), then the rows cast to bf16:
+//              xperm[p] = bf16(x[token of p]); rows [kT, (k+1)T) hold bf16(x) in token order, the
+//              A operand of both shared experts
+//   GEMM1      per group (64 routed experts + S shared): [rows, H] x w13[e]^T -> 2I packed gate|up
+//              columns, SwiGLU in the epilogue -> h[rows, I] bf16
+//   GEMM2      per group: [rows, I] x w2[e]^T -> y[rows, H] fp32
+//   combine    out[t] = sum_s w[t,s] * y[dest(t,s)] + sum_q y[shared q, t] (fixed order)
+//
+// GEMM: persistent CTAs, one per SM; warp 0 issues TMA loads of A (128 x 64) and B (256 x 64)
+// tiles into a 4-stage shared-memory ring (128-byte swizzle); warp 1 allocates 512 TMEM columns
+// and one of its threads issues tcgen05.mma (M=128, N=256, K=16 per instruction) into one of
+// two TMEM accumulators; warps 2-5 drain the other accumulator (tcgen05.ld), so the epilogue
+// of one tile overlaps the MMAs of the next. Rows of a tile past its group's end are computed
+// and discarded. No cluster multicast is used anywhere.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <algorithm>
+#include <mutex>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "sm100.cuh"
+
+namespace uocr {
+
+// ======================================================================================
+// permute
+// ======================================================================================
+constexpr int kChunk = 256;  // entries per histogram chunk (one CTA, one thread each)
+
+__global__ void __launch_bounds__(kChunk) prefill_hist_kernel(const int32_t* __restrict__ ids, int n, int E,
+                                                              int* __restrict__ chunk_counts) {
+    __shared__ int hist[64];
+    if (threadIdx.x < 64) hist[threadIdx.x] = 0;
+    __syncthreads();
+    const int q = blockIdx.x * kChunk + threadIdx.x;
+    if (q < n) atomicAdd(&hist[clamp_expert(ids[q], E)], 1);
+    __syncthreads();
+    if (threadIdx.x < 64) chunk_counts[blockIdx.x * 64 + threadIdx.x] = hist[threadIdx.x];
+}
+
+// One CTA: per expert, exclusive prefix of the chunk histograms; the group tables of both GEMMs.
+__global__ void __launch_bounds__(64) prefill_scan_kernel(const int* __restrict__ chunk_counts, int nchunks, int E,
+                                                          int S, int T, int topk, int* __restrict__ chunk_base,
+                                                          PrefillPlan* __restrict__ plan1,
+                                                          PrefillPlan* __restrict__ plan2) {
+    __shared__ int total[64];
+    __shared__ int base[65];
+    const int e = threadIdx.x;
+    int sum = 0;
+    if (e < E)
+        for (int c = 0; c < nchunks; ++c) sum += chunk_counts[c * 64 + e];
+    total[e] = e < E ? sum : 0;
+    __syncthreads();
+    if (e == 0) {
+        int acc = 0;
+        for (int i = 0; i < 64; ++i) {
+            base[i] = acc;
+            acc += total[i];
+        }
+        base[64] = acc;
+    }
+    __syncthreads();
+    if (e < E) {
+        int acc = base[e];
+        for (int c = 0; c < nchunks; ++c) {
+            chunk_base[c * 64 + e] = acc;
+            acc += chunk_counts[c * 64 + e];
+        }
+    }
+    if (e == 0) {
+        const int kT = topk * T;
+        int ng = 0, mt = 0;
+        for (int g = 0; g < E + S; ++g) {
+            PrefillGroup G1, G2;
+            if (g < E) {
+                G1.a_base = base[g]; G1.out_base = base[g]; G1.rows = total[g]; G1.wrow0 = g; G1.shared = 0;
+                G2 = G1;
+            } else {
+                const int q = g - E;
+                G1.a_base = kT; G1.out_base = kT + q * T; G1.rows = T; G1.wrow0 = q; G1.shared = 1;
+                G2.a_base = kT + q * T; G2.out_base = kT + q * T; G2.rows = T; G2.wrow0 = q; G2.shared = 1;
+            }
+            if (G1.rows == 0) continue;
+            plan1->mtile_prefix[ng] = mt;
+            plan2->mtile_prefix[ng] = mt;
+            plan1->g[ng] = G1;
+            plan2->g[ng] = G2;
+            mt += (G1.rows + 127) / 128;
+            ++ng;
+        }
+        plan1->mtile_prefix[ng] = mt;
+        plan2->mtile_prefix[ng] = mt;
+        plan1->ngroups = ng;
+        plan2->ngroups = ng;
+    }
+}
+
+// Rank of each entry among the entries of its expert (stable in entry order) -> destination row.
+__global__ void __launch_bounds__(kChunk) prefill_scatter_kernel(const int32_t* __restrict__ ids, int n, int E,
+                                                                 int topk, const int* __restrict__ chunk_base,
+                                                                 int* __restrict__ dest, int* __restrict__ src_tok) {
+    __shared__ int wcount[kChunk / 32][64];
+    const int q = blockIdx.x * kChunk + threadIdx.x;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    for (int i = threadIdx.x; i < (kChunk / 32) * 64; i += kChunk) (&wcount[0][0])[i] = 0;
+    __syncthreads();
+    const int e = q < n ? clamp_expert(ids[q], E) : -1;
+    const unsigned same = __match_any_sync(0xffffffffu, e);
+    const int rank_in_warp = __popc(same & ((1u << lane) - 1u));
+    if (e >= 0 && rank_in_warp == 0) wcount[warp][e] = __popc(same);
+    __syncthreads();
+    if (e >= 0) {
+        int before = 0;
+        for (int w = 0; w < warp; ++w) before += wcount[w][e];
+        const int p = chunk_base[blockIdx.x * 64 + e] + before + rank_in_warp;
+        dest[q] = p;
+        src_tok[p] = q / topk;
+    }
+}
+
+// xperm[p] = bf16(x[src_tok[p]]) for p < kT; xperm[kT + t] = bf16(x[t]). One warp per row.
+__global__ void __launch_bounds__(256) prefill_gather_kernel(const float* __restrict__ x, int T, int H, int kT,
+                                                             const int* __restrict__ src_tok,
+                                                             uint16_t* __restrict__ xperm) {
+    const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+    const int lane = threadIdx.x & 31;
+    if (row >= kT + T) return;
+    const int t = row < kT ? src_tok[row] : row - kT;
+    const float* src = x + (size_t)t * H;
+    uint16_t* dst = xperm + (size_t)row * H;
+    for (int k = lane * 8; k < H; k += 256) {
+        const float4 a = *reinterpret_cast<const float4*>(src + k);
+        const float4 b = *reinterpret_cast<const float4*>(src + k + 4);
+        uint4 o;
+        o.x = (uint32_t)f32_to_bf16_rne(a.x) | ((uint32_t)f32_to_bf16_rne(a.y) << 16);
+        o.y = (uint32_t)f32_to_bf16_rne(a.z) | ((uint32_t)f32_to_bf16_rne(a.w) << 16);
+        o.z = (uint32_t)f32_to_bf16_rne(b.x) | ((uint32_t)f32_to_bf16_rne(b.y) << 16);
+        o.w = (uint32_t)f32_to_bf16_rne(b.z) | ((uint32_t)f32_to_bf16_rne(b.w) << 16);
+        *reinterpret_cast<uint4*>(dst + k) = o;
+    }
+}
+
+// int8 routed stacks -> bf16 (the int8 prefill's B operands): bf16_rne(f32(q) * scale), exactly
+// int8_dequant_expert's bits (kernels/moe_int8.mojo:330-340), for a whole [rows, K] stack.
+__global__ void __launch_bounds__(256) prefill_dequant_kernel(const int8_t* __restrict__ w, const float* __restrict__ s,
+                                                              long rows, int K, int G, uint16_t* __restrict__ out) {
+    const long i = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+    if (i >= rows * K) return;
+    const long r = i / K;
+    const int k = (int)(i - r * K);
+    const uint2 v = *reinterpret_cast<const uint2*>(w + i);
+    float f[8];
+    unpack_s8x8(v.x, v.y, f);
+    const float* sr = s + r * (K / G);
+    uint16_t o[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) o[j] = f32_to_bf16_rne(__fmul_rn(f[j], sr[(k + j) / G]));
+    *reinterpret_cast<uint4*>(out + i) = *reinterpret_cast<const uint4*>(o);
+}
+
+// out[t][j] = sum_s w[t,s] * y[dest[t*k+s]][j] + sum_q y[kT + q*T + t][j]
+__global__ void __launch_bounds__(256) prefill_combine_kernel(const float* __restrict__ y, const float* __restrict__ wts,
+                                                              const int* __restrict__ dest, int T, int H, int topk,
+                                                              int S, float* __restrict__ out) {
+    const int t = blockIdx.x;
+    const int kT = topk * T;
+    for (int j = threadIdx.x * 4; j < H; j += blockDim.x * 4) {
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s = 0; s < topk; ++s) {
+            const float w = wts[t * topk + s];
+            const float4 v = *reinterpret_cast<const float4*>(y + (size_t)dest[t * topk + s] * H + j);
+            acc.x = __fmaf_rn(w, v.x, acc.x);
+            acc.y = __fmaf_rn(w, v.y, acc.y);
+            acc.z = __fmaf_rn(w, v.z, acc.z);
+            acc.w = __fmaf_rn(w, v.w, acc.w);
+        }
+        for (int q = 0; q < S; ++q) {
+            const float4 v = *reinterpret_cast<const float4*>(y + (size_t)(kT + q * T + t) * H + j);
+            acc.x = __fadd_rn(acc.x, v.x);
+            acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z);
+            acc.w = __fadd_rn(acc.w, v.w);
+        }
+        *reinterpret_cast<float4*>(out + (size_t)t * H + j) = acc;
+    }
+}
+
+// ======================================================================================
+// grouped GEMM on tcgen05
+// ======================================================================================
+constexpr int kBM = 128, kBN = 256, kBK = 64;
+constexpr int kGStages = 4;
+constexpr uint32_t kATile = kBM * kBK * 2;  // 16 KB
+constexpr uint32_t kBTile = kBN * kBK * 2;  // 32 KB
+constexpr int kGemmThreads = 192;           // producer, MMA, 4 epilogue warps
+constexpr uint32_t kTmemCols = 512;         // two 256-column accumulators
+
+enum GemmEpi : int { kEpiSwiGLU = 0, kEpiF32 = 1 };
+
+struct GemmSmem {
+    uint64_t full[kGStages], empty[kGStages], tfull[2], tempty[2], done;
+    uint32_t tmem_base;
+    int abort_flag;
+};
+
+UOCR_DEV void gemm_decode_tile(const PrefillPlan& P, int NT, int tile, int& g, int& mloc, int& n) {
+    const int mt = tile / NT;
+    n = tile - mt * NT;
+    g = 0;
+    while (P.mtile_prefix[g + 1] <= mt) ++g;
+    mloc = mt - P.mtile_prefix[g];
+}
+
+// Bounded single-thread mbarrier wait that also honours the CTA abort flag.
+UOCR_DEV bool gwait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, uint32_t* status) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (!mbar_try_wait(bar, parity)) {
+        if (*abort_flag) return false;
+        if (global_timer_ns() - t0 > kWaitBudgetNs) {
+            set_status(status, kStatusWaitTimeout);
+            *abort_flag = 1;
+            return false;
+        }
+    }
+    return true;
+}
+
+template <int kEpi>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                    const __grid_constant__ CUtensorMap tmBs, const PrefillPlan* __restrict__ plan_g, int NT, int KT,
+                    int b_rows_per_group, void* __restrict__ out, int out_ld, uint32_t* status) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + kGStages * kATile;
+    GemmSmem* gs = reinterpret_cast<GemmSmem*>(smem + kGStages * (kATile + kBTile));
+    PrefillPlan* P = reinterpret_cast<PrefillPlan*>(reinterpret_cast<uint8_t*>(gs) + 256);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    volatile int* abort_flag = &gs->abort_flag;
+
+    for (int i = tid; i < (int)(sizeof(PrefillPlan) / 4); i += blockDim.x)
+        reinterpret_cast<int*>(P)[i] = reinterpret_cast<const int*>(plan_g)[i];
+    if (tid == 0) {
+        for (int s = 0; s < kGStages; ++s) {
+            mbar_init(&gs->full[s], 1);
+            mbar_init(&gs->empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&gs->tfull[a], 1);
+            mbar_init(&gs->tempty[a], 4);
+        }
+        mbar_init(&gs->done, 1);
+        gs->abort_flag = 0;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+        tma_prefetch_desc(&tmBs);
+    }
+    if (warp == 1) tmem_alloc(&gs->tmem_base, kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = gs->tmem_base;
+    const int total = P->mtile_prefix[P->ngroups] * NT;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer ----------------
+            int s = 0;
+            uint32_t round = 0;
+            for (int tile = blockIdx.x; tile < total && !*abort_flag; tile += gridDim.x) {
+                int g, mloc, n;
+                gemm_decode_tile(*P, NT, tile, g, mloc, n);
+                const PrefillGroup& G = P->g[g];
+                const int a_row = G.a_base + mloc * kBM;
+                const int b_row = G.wrow0 * b_rows_per_group + n * kBN;
+                const CUtensorMap* mb = G.shared ? &tmBs : &tmB;
+                for (int kt = 0; kt < KT; ++kt) {
+                    if (round > 0 && !gwait(&gs->empty[s], (round - 1) & 1, abort_flag, status)) break;
+                    mbar_arrive_expect_tx(&gs->full[s], kATile + kBTile);
+                    tma_load_2d(sA + s * kATile, &tmA, kt * kBK, a_row, &gs->full[s]);
+                    tma_load_2d(sB + s * kBTile, mb, kt * kBK, b_row, &gs->full[s]);
+                    if (++s == kGStages) { s = 0; ++round; }
+                }
+            }
+            // copies still in flight complete before the CTA may exit
+            for (int i = 0; i < kGStages; ++i) {
+                int ss = s - 1 - i;
+                uint32_t rr = round;
+                if (ss < 0) { ss += kGStages; if (rr == 0) break; --rr; }
+                mbar_wait(&gs->full[ss], rr & 1, nullptr);
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (lane == 0) {
+            // ---------------- MMA issuer ----------------
+            constexpr uint32_t idesc = umma_idesc_bf16(kBM, kBN);
+            int s = 0, acc = 0;
+            uint32_t round = 0, around = 0;
+            bool issued = false;
+            for (int tile = blockIdx.x; tile < total && !*abort_flag; tile += gridDim.x) {
+                if (around > 0 && !gwait(&gs->tempty[acc], (around - 1) & 1, abort_flag, status)) break;
+                tc_fence_after();
+                const uint32_t tmem_d = tmem_base + (uint32_t)acc * kBN;
+                bool ok = true;
+                for (int kt = 0; kt < KT; ++kt) {
+                    if (!gwait(&gs->full[s], round & 1, abort_flag, status)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t ad = umma_desc_sw128(smem_addr(sA + s * kATile));
+                    const uint64_t bd = umma_desc_sw128(smem_addr(sB + s * kBTile));
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk)
+                        umma_f16(tmem_d, ad + 2 * kk, bd + 2 * kk, idesc, (kt | kk) != 0 ? 1u : 0u);
+                    issued = true;
+                    umma_commit(&gs->empty[s]);
+                    if (++s == kGStages) { s = 0; ++round; }
+                }
+                if (!ok) break;
+                umma_commit(&gs->tfull[acc]);
+                if (++acc == 2) { acc = 0; ++around; }
+            }
+            if (issued) {
+                // every MMA of this CTA has completed before TMEM is released
+                umma_commit(&gs->done);
+                mbar_wait(&gs->done, 0, nullptr);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue: warps 2..5 own TMEM lanes 32*(warp%4) .. +31 ----------------
+        const int quarter = warp & 3;
+        const int row_in_tile = quarter * 32 + lane;
+        int acc = 0;
+        uint32_t around = 0;
+        for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
+            int g, mloc, n;
+            gemm_decode_tile(*P, NT, tile, g, mloc, n);
+            const PrefillGroup& G = P->g[g];
+            if (!mbar_wait_warp(&gs->tfull[acc], around & 1, abort_flag, status)) break;
+            tc_fence_after();
+            const int rows_valid = min(kBM, G.rows - mloc * kBM);
+            const bool live = row_in_tile < rows_valid;
+            const size_t out_row = (size_t)G.out_base + (size_t)mloc * kBM + row_in_tile;
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)acc * kBN;
+            if (kEpi == kEpiSwiGLU) {
+                // packed columns: [0,128) gate rows n*128.., [128,256) up rows n*128..
+                uint16_t* h = reinterpret_cast<uint16_t*>(out) + out_row * out_ld + (size_t)n * (kBN / 2);
+#pragma unroll 1
+                for (int c = 0; c < 4; ++c) {
+                    uint32_t gr[32], ur[32];
+                    tmem_ld_32x32b_x32(taddr + c * 32, gr);
+                    tmem_ld_32x32b_x32(taddr + 128 + c * 32, ur);
+                    tmem_wait_ld();
+                    uint32_t pk[16];
+#pragma unroll
+                    for (int i = 0; i < 16; ++i) {
+                        const float g0 = __uint_as_float(gr[2 * i]), g1 = __uint_as_float(gr[2 * i + 1]);
+                        const float u0 = __uint_as_float(ur[2 * i]), u1 = __uint_as_float(ur[2 * i + 1]);
+                        pk[i] = (uint32_t)f32_to_bf16_rne(silu(g0) * u0) | ((uint32_t)f32_to_bf16_rne(silu(g1) * u1) << 16);
+                    }
+                    if (live) {
+#pragma unroll
+                        for (int v = 0; v < 4; ++v)
+                            *reinterpret_cast<uint4*>(h + c * 32 + v * 8) =
+                                make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+                    }
+                }
+            } else {
+                float* y = reinterpret_cast<float*>(out) + out_row * out_ld + (size_t)n * kBN;
+#pragma unroll 1
+                for (int c = 0; c < kBN / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(taddr + c * 32, r);
+                    tmem_wait_ld();
+                    if (live) {
+#pragma unroll
+                        for (int v = 0; v < 8; ++v)
+                            *reinterpret_cast<uint4*>(y + c * 32 + v * 4) =
+                                make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&gs->tempty[acc]);
+            if (++acc == 2) { acc = 0; ++around; }
+        }
+    }
+    __syncthreads();
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// ======================================================================================
+// host side
+// ======================================================================================
+static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+    });
+    return fn;
+}
+
+// 2-D bf16 [rows, cols] row-major, box {64, box_rows}, 128-byte swizzle, zero fill out of bounds.
+static bool make_map_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[2] = {cols, rows};
+    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint32_t box[2] = {64, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
+size_t gemm_smem_bytes() {
+    return 1024 + kGStages * (kATile + kBTile) + 256 + sizeof(PrefillPlan);
+}
+
+static cudaError_t launch_gemm(int epi, const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& Bs,
+                               const PrefillPlan* plan, int NT, int KT, int b_rows_per_group, void* out, int out_ld,
+                               int max_tiles, uint32_t* status, cudaStream_t st) {
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const size_t smem = gemm_smem_bytes();
+    const void* fn = epi == kEpiSwiGLU ? reinterpret_cast<const void*>(grouped_gemm_kernel<kEpiSwiGLU>)
+                                       : reinterpret_cast<const void*>(grouped_gemm_kernel<kEpiF32>);
+    cudaError_t err = ensure_smem_optin(fn, smem);
+    if (err != cudaSuccess) return err;
+    const int grid = std::max(1, std::min(sms, max_tiles));
+    if (epi == kEpiSwiGLU)
+        grouped_gemm_kernel<kEpiSwiGLU><<<grid, kGemmThreads, smem, st>>>(A, B, Bs, plan, NT, KT, b_rows_per_group, out,
+                                                                         out_ld, status);
+    else
+        grouped_gemm_kernel<kEpiF32><<<grid, kGemmThreads, smem, st>>>(A, B, Bs, plan, NT, KT, b_rows_per_group, out,
+                                                                      out_ld, status);
+    return cudaGetLastError();
+}
+
+PrefillLayout prefill_layout(int T, int H, int I, int E, int S, int topk, bool int8) {
+    auto al = [](size_t n) { return (n + 255) & ~size_t(255); };
+    PrefillLayout d{};
+    const size_t kT = (size_t)topk * T;
+    const size_t nchunks = (kT + kChunk - 1) / kChunk;
+    size_t off = 0;
+    d.status = off; off += 256;
+    d.ids = off; off += al(sizeof(int32_t) * kT);
+    d.wts = off; off += al(sizeof(float) * kT);
+    d.chunk_counts = off; off += al(sizeof(int) * nchunks * 64);
+    d.chunk_base = off; off += al(sizeof(int) * nchunks * 64);
+    d.plan1 = off; off += al(sizeof(PrefillPlan));
+    d.plan2 = off; off += al(sizeof(PrefillPlan));
+    d.dest = off; off += al(sizeof(int) * kT);
+    d.src_tok = off; off += al(sizeof(int) * kT);
+    d.xperm = off; off += al(sizeof(uint16_t) * (kT + T) * H);
+    d.h = off; off += al(sizeof(uint16_t) * (kT + (size_t)S * T) * I);
+    d.y = off; off += al(sizeof(float) * (kT + (size_t)S * T) * H);
+    d.w13 = d.w2 = 0;
+    if (int8) {
+        d.w13 = off; off += al(sizeof(uint16_t) * (size_t)E * 2 * I * H);
+        d.w2 = off; off += al(sizeof(uint16_t) * (size_t)E * H * I);
+    }
+    d.total = off;
+    return d;
+}
+
+cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& d, cudaStream_t st) {
+    const int T = a.T, H = a.H, I = a.I, E = a.E, S = a.S, k = a.topk;
+    const int kT = k * T;
+    const int nchunks = (kT + kChunk - 1) / kChunk;
+    int32_t* ids = a.ids;
+    float* wts = a.wts;
+    int* chunk_counts = reinterpret_cast<int*>(ws + d.chunk_counts);
+    int* chunk_base = reinterpret_cast<int*>(ws + d.chunk_base);
+    PrefillPlan* plan1 = reinterpret_cast<PrefillPlan*>(ws + d.plan1);
+    PrefillPlan* plan2 = reinterpret_cast<PrefillPlan*>(ws + d.plan2);
+    int* dest = reinterpret_cast<int*>(ws + d.dest);
+    int* src_tok = reinterpret_cast<int*>(ws + d.src_tok);
+    uint16_t* xperm = reinterpret_cast<uint16_t*>(ws + d.xperm);
+    uint16_t* h = reinterpret_cast<uint16_t*>(ws + d.h);
+    float* y = reinterpret_cast<float*>(ws + d.y);
+    uint32_t* status = reinterpret_cast<uint32_t*>(ws + d.status);
+
+    cudaError_t err = launch_route(a.x, T, H, a.router, E, a.bias, k, ids, wts, st);
+    if (err != cudaSuccess) return err;
+    prefill_hist_kernel<<<nchunks, kChunk, 0, st>>>(ids, kT, E, chunk_counts);
+    prefill_scan_kernel<<<1, 64, 0, st>>>(chunk_counts, nchunks, E, S, T, k, chunk_base, plan1, plan2);
+    prefill_scatter_kernel<<<nchunks, kChunk, 0, st>>>(ids, kT, E, k, chunk_base, dest, src_tok);
+    prefill_gather_kernel<<<(kT + T + 7) / 8, 256, 0, st>>>(a.x, T, H, kT, src_tok, xperm);
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+
+    const void* w13 = a.w13;
+    const void* w2 = a.w2;
+    if (a.int8) {
+        uint16_t* w13d = reinterpret_cast<uint16_t*>(ws + d.w13);
+        uint16_t* w2d = reinterpret_cast<uint16_t*>(ws + d.w2);
+        const long n13 = (long)E * 2 * I * H, n2 = (long)E * H * I;
+        prefill_dequant_kernel<<<(unsigned)((n13 / 8 + 255) / 256), 256, 0, st>>>(
+            reinterpret_cast<const int8_t*>(a.w13), a.s13, (long)E * 2 * I, H, a.G, w13d);
+        prefill_dequant_kernel<<<(unsigned)((n2 / 8 + 255) / 256), 256, 0, st>>>(
+            reinterpret_cast<const int8_t*>(a.w2), a.s2, (long)E * H, I, a.G, w2d);
+        w13 = w13d;
+        w2 = w2d;
+    }
+    // upper bound of m-tiles (the plan holds the exact count on the device)
+    const int max_mtiles = (kT + 127) / 128 + E + S * ((T + 127) / 128);
+    CUtensorMap mA1, mB1, mBs1, mA2, mB2, mBs2;
+    if (!make_map_bf16(&mA1, xperm, (uint64_t)kT + T, H, kBM) ||
+        !make_map_bf16(&mB1, w13, (uint64_t)E * 2 * I, H, kBN) ||
+        !make_map_bf16(&mA2, h, (uint64_t)kT + (uint64_t)S * T, I, kBM) ||
+        !make_map_bf16(&mB2, w2, (uint64_t)E * H, I, kBN))
+        return cudaErrorInvalidValue;
+    if (S > 0) {
+        if (!make_map_bf16(&mBs1, a.w13_shared, (uint64_t)S * 2 * I, H, kBN) ||
+            !make_map_bf16(&mBs2, a.w2_shared, (uint64_t)S * H, I, kBN))
+            return cudaErrorInvalidValue;
+    } else {
+        mBs1 = mB1;  // no shared groups in the plan: never read
+        mBs2 = mB2;
+    }
+    err = launch_gemm(kEpiSwiGLU, mA1, mB1, mBs1, plan1, (2 * I) / kBN, H / kBK, 2 * I, h, I, max_mtiles * ((2 * I) / kBN),
+                      status, st);
+    if (err != cudaSuccess) return err;
+    err = launch_gemm(kEpiF32, mA2, mB2, mBs2, plan2, H / kBN, I / kBK, H, y, H, max_mtiles * (H / kBN), status, st);
+    if (err != cudaSuccess) return err;
+    prefill_combine_kernel<<<T, 256, 0, st>>>(y, wts, dest, T, H, k, S, a.out);
+    return cudaGetLastError();
+}
+
+}  // namespace uocr

@@ -214,8 +214,41 @@ class UocrMoE:
                 ws.data_ptr(), ws.numel(), stream))
         return out
 
+    def prefill_workspace(self, T: int) -> torch.Tensor:
+        """The prefill scratch for up to ``T`` tokens (kept and grown; its status word starts zeroed)."""
+        nbytes = load().uocr_moe_prefill_workspace_bytes(ctypes.byref(self.layer), T)
+        if nbytes == 0:
+            raise ValueError(f"UocrMoE: no prefill workspace for T={T}")
+        ws = self._ws.get(-1)
+        if ws is None or ws.numel() < nbytes:
+            self._ws.pop(-1, None)
+            ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+            self._ws[-1] = ws
+        return ws
+
+    def prefill(self, x: torch.Tensor, *, out: torch.Tensor | None = None, ids: torch.Tensor | None = None,
+                wts: torch.Tensor | None = None) -> torch.Tensor:
+        """The prefill MoE (decoder.py:657-667, routed part as _routed_native, decoder.py:606-614):
+        tokens permuted by expert, grouped bf16 GEMMs on the tensor cores, weighted combine."""
+        x = self._check_x(x)
+        T = x.shape[0]
+        if out is None:
+            out = torch.empty_like(x)
+        if T == 0:
+            return out
+        ws = self.prefill_workspace(T)
+        check(load().uocr_moe_prefill(
+            ctypes.byref(self.layer), x.data_ptr(), T, 0 if self.bias is None else self.bias.data_ptr(),
+            out.data_ptr(), 0 if ids is None else ids.data_ptr(), 0 if wts is None else wts.data_ptr(),
+            ws.data_ptr(), ws.numel(), torch.cuda.current_stream(x.device).cuda_stream))
+        return out
+
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
-        """MoE.__call__ (decoder.py:657-667): the prefill's MoE over ``x [T, H]``."""
+        """MoE.__call__ (decoder.py:657-667): the MoE over ``x [T, H]``. Up to DECODE_MAX_B rows
+        run the decode kernels (exact fp32 products, one weight read per selected expert);
+        longer inputs run :meth:`prefill` when hidden_size is a multiple of 256."""
+        if x.dim() == 2 and x.shape[0] > DECODE_MAX_B and self.config.hidden_size % 256 == 0:
+            return self.prefill(x)
         return self.decode_rows(x)
 
     def route(self, x: torch.Tensor):
