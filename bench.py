@@ -52,6 +52,10 @@ def parse():
     p.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     p.add_argument("--settle", type=float, default=1.5,
                    help="seconds of untimed replays before timing, while the clock sampler runs")
+    p.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+                   help="decode: configs[1]/[3] int8 B=8 decode stack (the headline); "
+                        "prefill: configs[2] bf16 prefill of 4096 tokens")
+    p.add_argument("--tokens", type=int, default=4096, help="prefill tokens (configs[2]: 4096)")
     return p.parse_args()
 
 
@@ -124,6 +128,15 @@ def measured_peaks() -> tuple[float, str]:
         return float(d["hbm_gbs"]), "measured"
     except Exception:  # noqa: BLE001
         return 6650.0, "fallback"
+
+
+def measured_tc_peak() -> tuple[float, str]:
+    """Dense bf16 TFLOP/s: the burst figure (a prefill layer is timed alone, not in a long loop)."""
+    try:
+        d = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+        return float(d["bf16_tflops"]), "measured"
+    except Exception:  # noqa: BLE001
+        return 1590.0, "fallback"
 
 
 # ---------------------------------------------------------------------------------------------
@@ -222,6 +235,105 @@ def time_e2e(torch, g, xs, outs, steps, warmup):
     return a.elapsed_time(b) / steps, nbytes, sum(o.numel() * 4 for o in outs)
 
 
+# prefill: per token 2 * (6 * 3 * I * H + 3 * (S * I) * H + E * H) flop
+PREFILL_FLOP_PER_TOKEN = 2 * (TOPK * 3 * I * H + 3 * (S * I) * H + E * H)  # 55 214 080
+
+
+def prefill_case(torch, uocr, synth, int8: bool, T: int, device, seed: int):
+    """One layer with an N(0, 1) per-expert logit bias, T tokens."""
+    cfg = uocr.MoEConfig(int8_experts=int8)
+    st = synth.layer_state(cfg, seed, device=device)
+    moe = uocr.UocrMoE(cfg, device=device).load_state_dict(st)
+    del st
+    moe.bias = synth.skew_bias(E, seed + 1, device=device)
+    x = synth.hidden_states(T, H, seed + 2, device=device)
+    out = torch.empty_like(x)
+    ids = torch.empty((T, TOPK), dtype=torch.int32, device=device)
+    wts = torch.empty((T, TOPK), dtype=torch.float32, device=device)
+    return moe, x, out, ids, wts
+
+
+def time_prefill(torch, moe, x, out, ids, wts, steps, warmup, dist, sampler=None, settle_s=0.0):
+    """The public prefill call captured in a CUDA graph; `steps` timed replays. Every replay
+    reads the touched experts' weights (up to 440 MB bf16) and writes ~300 MB of permuted rows
+    and expert outputs, more than the 126 MB L2."""
+    def step():
+        moe.prefill(x, out=out, ids=ids, wts=wts)
+
+    step()
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        step()
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    if sampler:
+        sampler.start()
+        t0 = time.time()
+        while time.time() - t0 < settle_s:
+            for _ in range(10):
+                g.replay()
+            torch.cuda.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        g.replay()
+    b.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop() if sampler else None
+    ms = a.elapsed_time(b) / steps
+    if dist:
+        t = torch.tensor([ms], device=x.device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item())
+    return g, ms, clocks
+
+
+def prefill_e2e(torch, moe, x, out, steps, warmup):
+    """Public prefill call end to end: pinned H2D of x, the layer, D2H of out, all timed."""
+    xh = x.cpu().pin_memory()
+    oh = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+
+    def one():
+        x.copy_(xh, non_blocking=True)
+        moe.prefill(x, out=out)
+        oh.copy_(out, non_blocking=True)
+
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(steps):
+        one()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / steps, x.numel() * 4, out.numel() * 4
+
+
+#: kernels one prefill call launches: route, histogram, scan, scatter, gather, 2 GEMMs, combine
+#: (+ 2 dequant passes for int8 stacks)
+PREFILL_LAUNCHES = 8
+
+
+def prefill_row(torch, uocr, synth, int8, T, steps, warmup, dist, device, seed):
+    moe, x, out, ids, wts = prefill_case(torch, uocr, synth, int8, T, device, seed)
+    g, ms, _ = time_prefill(torch, moe, x, out, ids, wts, steps, warmup, dist)
+    del g
+    tc, _ = measured_tc_peak()
+    tflops = PREFILL_FLOP_PER_TOKEN * T / (ms * 1e-3) / 1e12
+    counts = torch.bincount(ids.flatten().long(), minlength=E)
+    row = {"value": T / (ms * 1e-3), "unit": "tokens/s", "tokens": T, "ms_per_layer": ms, "tflops": tflops,
+           "tc_frac": tflops / tc, "max_expert_rows": int(counts.max()), "experts_used": int((counts > 0).sum())}
+    del moe, x, out, ids, wts
+    torch.cuda.empty_cache()
+    return row
+
+
 class CpuDecode:
     """The reference's fp32 CPU decode path (MoE.decode_rows restated in torch, the oracle port)
     on all host cores, one MoE layer of the benchmark's shape."""
@@ -265,6 +377,96 @@ class CpuDecode:
         return self.B * n / el, self.cores, sample
 
 
+class CpuPrefill:
+    """The reference's fp32 CPU prefill path (MoE.__call__ on CPU: the dense 64-expert router
+    chain, decoder.py:568-584, 657-667, restated in torch) on all host cores, over a bounded
+    sample of the configs[2] tokens."""
+
+    def __init__(self, T_sample: int = 256, seed: int = 3000):
+        import numpy as np
+        import torch
+
+        from oracle import moe_oracle as o
+
+        self.cores = len(os.sched_getaffinity(0))
+        torch.set_num_threads(self.cores)
+        uocr = importlib.import_module(PKG)
+        synth = importlib.import_module(f"{PKG}.synth")
+        st = synth.layer_state(uocr.MoEConfig(), seed, device="cpu")
+        bits = lambda t: t.view(torch.int16).numpy().view(np.uint16)  # noqa: E731
+        kw = {n: bits(st[f"experts.{n}_proj"]) for n in ("gate", "up", "down")}
+        kw.update(router=bits(st["gate.gate_score.weight"]), shared_gate=bits(st["shared_experts.gate_proj.weight"]),
+                  shared_up=bits(st["shared_experts.up_proj.weight"]),
+                  shared_down=bits(st["shared_experts.down_proj.weight"]))
+        self.layer = o.TorchCpuLayer(o.MoEConfig(), o.MoEWeights(**kw))
+        self.bias = synth.skew_bias(E, seed + 1, device="cpu")
+        self.x = synth.hidden_states(T_sample, H, seed + 2, device="cpu")
+        self.T = T_sample
+        self.layer.prefill_dense(self.x[:16], self.bias)  # warm-up
+
+    def step_seconds(self) -> float:
+        t0 = time.perf_counter()
+        self.layer.prefill_dense(self.x, self.bias)
+        return time.perf_counter() - t0
+
+    def rate(self, budget_s: float = 15.0):
+        n, el = 0, 0.0
+        while el < budget_s and n < 200:
+            el += self.step_seconds()
+            n += 1
+        sample = f"{n} dense-64-expert prefill passes over {self.T} of the 4096 tokens (bf16 weights as fp32), {el:.1f} s"
+        return self.T * n / el, self.cores, sample
+
+
+def run_prefill(args, torch, uocr, synth, dist, world, rank, device):
+    """one bf16 MoE layer over 4096 tokens with an N(0, 1) expert bias."""
+    T = args.tokens
+    moe, x, out, ids, wts = prefill_case(torch, uocr, synth, False, T, device, 3000)
+    sampler = ClockSampler(physical_gpu_index(int(os.environ.get("LOCAL_RANK", "0"))))
+    g, ms, clocks = time_prefill(torch, moe, x, out, ids, wts, args.steps, args.warmup, dist, sampler,
+                                 settle_s=args.settle)
+    del g
+    e2e_ms, h2d, d2h = prefill_e2e(torch, moe, x, out, max(args.steps // 4, 10), 3)
+    if dist:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+    tc, tc_src = measured_tc_peak()
+    flop = PREFILL_FLOP_PER_TOKEN * T
+    tflops = flop / (ms * 1e-3) / 1e12
+    counts = torch.bincount(ids.flatten().long(), minlength=E)
+    finite = bool(torch.isfinite(out).all())
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu:
+        v, cores, sample = CpuPrefill().rate()
+        cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
+    if rank != 0:
+        return
+    line = {
+        "metric": "MoE-layer tokens/s (prefill 4096, bf16)",
+        "value": world * T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16 operands, fp32 accumulate (fp32 in/out)",
+        "data": "synthetic (seeded N(0,0.02)->bf16 weights; hidden N(0,1) RMS-normalised; N(0,1) expert bias)",
+        "config": {"workload": "configs[2] prefill bf16, 4096 tokens, N(0,1) per-expert logit bias",
+                   "hidden": H, "experts": E, "top_k": TOPK, "shared": S, "moe_intermediate": I, "tokens": T,
+                   "l2": "each replay streams the touched experts (<= 440 MB) and ~300 MB of activations >> 126 MB L2",
+                   "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
+                   "execution": "one CUDA graph per step of the public prefill call",
+                   "max_expert_rows": int(counts.max()), "experts_used": int((counts > 0).sum())},
+        "roofline": {"bound": "tensor", "achieved": tflops, "peak": tc, "unit": "TFLOP/s", "frac": tflops / tc,
+                     "peak_source": tc_src + " (burst)", "scope": "whole prefill layer (route..combine)",
+                     "algorithmic_flop_per_step": flop, "traffic": None},
+        "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
+        "gpu_launches": PREFILL_LAUNCHES * args.steps,
+        "clocks": clocks,
+        "cpu_baseline": cpu,
+        "outputs_finite": finite,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_ours(args):
     import torch
 
@@ -282,6 +484,12 @@ def run_ours(args):
     uocr = importlib.import_module(PKG)
     synth = importlib.import_module(f"{PKG}.synth")
     uocr.load()
+    if args.workload == "prefill":
+        run_prefill(args, torch, uocr, synth, dist, world, rank, device)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     B, L = args.batch, args.layers
 
     mods, xs, outs, ids, wts = build_stack(uocr, synth, True, L, B, device, 1000)
@@ -303,7 +511,7 @@ def run_ours(args):
     if not args.no_sub:
         del mods, xs, outs, ids, wts
         torch.cuda.empty_cache()
-        for int8, b in ((True, 1), (False, 1), (False, 8)):
+        for int8, b in ((True, 1), (True, 4), (False, 1), (False, 4), (False, 8)):
             m2, x2, o2, i2, w2 = build_stack(uocr, synth, int8, L, b, device, 2000 + 10 * b + int8)
             g2, ms2, _ = time_stack(torch, m2, x2, o2, i2, w2, args.steps, args.warmup, dist)
             by = algorithmic_bytes(torch, i2, int8, b)
@@ -312,12 +520,17 @@ def run_ours(args):
                 "hbm_gbs": by / (ms2 * 1e-3) / 1e9, "frac": by / (ms2 * 1e-3) / 1e9 / peak}
             del g2, m2, x2, o2, i2, w2
             torch.cuda.empty_cache()
+        psteps = max(args.steps // 10, 10)
+        for int8 in (False, True):
+            r = prefill_row(torch, uocr, synth, int8, args.tokens, psteps, max(args.warmup // 4, 3), dist, device, 3000)
+            r["value"] *= world
+            subs[f"prefill_{'int8' if int8 else 'bf16'}_{args.tokens}"] = r
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         v, cores, sample = CpuDecode(True, B).rate()
         cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
     if rank == 0:
-        launches_per_step = L  # one fused decode kernel per layer
+        launches_per_step = 3 * L  # per layer: route, gate|up experts, down experts + combine
         line = {
             "metric": "MoE-layer tokens/s (decode, int8 routed experts, B=8)",
             "value": value,
@@ -362,6 +575,30 @@ def run_reference(args):
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
+        return
+    if args.workload == "prefill":
+        cpu = CpuPrefill()
+        for _ in range(min(args.warmup, 3)):
+            cpu.step_seconds()
+        times, total = [], 0.0
+        for _ in range(args.steps):
+            t = cpu.step_seconds()
+            times.append(t)
+            total += t
+            if total > 90.0:
+                break
+        value = cpu.T / statistics.median(times)
+        print(json.dumps({
+            "impl": "reference", "metric": "MoE-layer tokens/s (prefill 4096, bf16)", "value": value,
+            "unit": "tokens/s", "n_gpus": world, "steps": len(times), "warmup": args.warmup,
+            "ms_per_step": 1e3 * statistics.median(times), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "fp32 (the reference's CPU path)", "data": "synthetic",
+            "config": {"workload": "configs[2] prefill bf16 (dense 64-expert CPU chain), a bounded token sample",
+                       "tokens_per_step": cpu.T},
+            "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": cpu.cores, "kind": "port",
+                             "sample": f"{len(times)} passes over {cpu.T} tokens, median"},
+            "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        }), flush=True)
         return
     B = args.batch
     cpu = CpuDecode(True, B)
