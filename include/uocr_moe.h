@@ -93,36 +93,50 @@ UOCR_API int uocr_dense_bf16_qmv(float* out, int64_t out_rows, int64_t out_cols,
  * The MoE sublayer (MoE.decode_rows / MoE.__call__, unlimited_ocr_max/decoder.py:641-667).
  * ------------------------------------------------------------------------------------ */
 
-/* One layer's device-resident weights, in this library's packed layout (see
- * uocr_moe_pack_gate_up / uocr_moe_pack_shared). Plain pointers, caller-owned. */
+/* One layer's device-resident weights, in this library's packed layout (uocr_moe_pack_w13,
+ * uocr_moe_pack_w2, uocr_moe_pack_shared). Plain pointers, caller-owned. */
 typedef struct uocr_moe_layer {
-    int32_t hidden;     /* H (1280) */
+    int32_t hidden;     /* H (1280), multiple of 128 */
     int32_t inter;      /* I, moe_intermediate_size (896); multiple of 128 */
     int32_t n_routed;   /* E (64), <= 64 */
     int32_t n_shared;   /* S (2): shared_experts_dim = S * I */
     int32_t top_k;      /* k (6) */
     int32_t group;      /* int8 group size along K (128) */
-    int32_t int8;       /* 1: routed stacks int8 + fp32 scales; 0: bf16 */
+    int32_t int8;       /* 1: routed stacks int8 with fp32 scales inside the blocks; 0: bf16 */
     int32_t reserved;
     const uint16_t* router;     /* bf16 [E, H]  (gate.gate_score.weight) */
-    const void* w13;            /* routed gate|up, packed [E, 2I, H], bf16 or int8 */
-    const float* s13;           /* int8 only: [E, 2I, H/G], packed like w13 */
-    const void* w2;             /* routed down [E, H, I], bf16 or int8 (reference layout) */
-    const float* s2;            /* int8 only: [E, H, I/G] */
-    const uint16_t* w13_shared; /* shared gate|up as S experts, packed [S, 2I, H] bf16 */
+    const void* w13;            /* routed gate|up blocks (uocr_moe_pack_w13) */
+    const void* w2;             /* routed down blocks (uocr_moe_pack_w2) */
+    const uint16_t* w13_shared; /* shared gate|up as S bf16 experts (uocr_moe_pack_shared) */
     const uint16_t* w2_shared;  /* shared down as S experts [S, H, I] bf16 */
 } uocr_moe_layer;
 
-/* Pack the reference's gate/up stacks [E, I, H] (experts.gate_proj / experts.up_proj,
- * decoder.py:305-307) into w13 [E, 2I, H]: rows interleaved in blocks of 128 (gate rows
- * 128b..128b+127, then up rows 128b..128b+127). elem_bytes = 2 (bf16), 1 (int8) or 4 (the
- * fp32 int8 scales [E, I, H/G], packed with the same row order). */
-UOCR_API int uocr_moe_pack_gate_up(const void* gate, const void* up, int64_t E, int64_t I, int64_t H,
-                          int elem_bytes, void* w13_out, uocr_stream_t stream);
+/* Packed layouts (the reference keeps the checkpoint's [E, N, K] stacks, decoder.py:305-313;
+ * this library re-lays them out once at load so that one decode work item is one contiguous
+ * block):
+ *   w13: per expert, I/P blocks of P row pairs (P = 8 bf16, 16 int8):
+ *        [gate rows (P x H) | up rows (P x H) | int8: gate scales (P x H/G fp32) | up scales]
+ *        (for bf16: the [E*2I, H] matrix with gate and up rows interleaved in groups of 8);
+ *   w2:  per expert, H/32 blocks of 32 rows: [rows (32 x I) | int8: scales (32 x I/G fp32)]
+ *        (for bf16: the plain [E, H, I] stack).
+ * Sizes in bytes for E experts: */
+UOCR_API size_t uocr_moe_w13_bytes(int64_t E, int64_t I, int64_t H, int64_t group, int int8);
+UOCR_API size_t uocr_moe_w2_bytes(int64_t E, int64_t H, int64_t I, int64_t group, int int8);
+
+/* Pack experts.gate_proj / experts.up_proj [E, I, H] (bf16 or int8; for int8 also their
+ * _scales [E, I, H/G] fp32, decoder.py:305-313) into w13_out (uocr_moe_w13_bytes bytes). */
+UOCR_API int uocr_moe_pack_w13(const void* gate, const void* up, const float* gate_scales,
+                               const float* up_scales, int64_t E, int64_t I, int64_t H, int64_t group,
+                               int int8, void* w13_out, uocr_stream_t stream);
+
+/* Pack experts.down_proj [E, H, I] (+ int8 _scales [E, H, I/G]) into w2_out. */
+UOCR_API int uocr_moe_pack_w2(const void* down, const float* down_scales, int64_t E, int64_t H, int64_t I,
+                              int64_t group, int int8, void* w2_out, uocr_stream_t stream);
 
 /* Pack the shared experts (shared_experts.{gate,up,down}_proj.weight as [S*I, H], [S*I, H],
- * [H, S*I] in plain [out, in] order) into w13_shared [S, 2I, H] and w2_shared [S, H, I]:
- * shared expert s owns intermediate rows [s*I, (s+1)*I). */
+ * [H, S*I] in plain [out, in] order) into w13_shared (uocr_moe_w13_bytes(S, I, H, 128, 0)
+ * bytes, bf16 blocks) and w2_shared [S, H, I]: shared expert s owns intermediate rows
+ * [s*I, (s+1)*I). */
 UOCR_API int uocr_moe_pack_shared(const uint16_t* gate, const uint16_t* up, const uint16_t* down,
                          int64_t S, int64_t I, int64_t H,
                          uint16_t* w13_out, uint16_t* w2_out, uocr_stream_t stream);

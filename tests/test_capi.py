@@ -35,7 +35,7 @@ def test_library_exports_every_declared_symbol(uocr):
 
     sigs = import_module("unlimited-ocr-max_b200._lib").SIGNATURES
     assert sorted(sigs) == header_functions()
-    assert lib.uocr_abi_version() == 1
+    assert lib.uocr_abi_version() == 2
 
 
 def test_only_the_c_abi_is_exported(uocr):
@@ -130,3 +130,18 @@ def test_config_validation(uocr):
     with pytest.raises(uocr.ConfigError, match="group size"):
         C(hidden_size=1216, int8_experts=True)
     assert C().shared_experts_dim == 1792
+
+
+def test_packed_sizes_and_refusals(uocr):
+    """Packed block sizes follow the layout; bad packing calls are refused on the host."""
+    L = uocr.load()
+    # int8 w13: per block of 16 row pairs 2*16*H bytes + 2*16*(H/128) fp32 scales
+    assert L.uocr_moe_w13_bytes(64, 896, 1280, 128, 1) == 64 * (896 // 16) * (2 * 16 * 1280 + 2 * 16 * 10 * 4)
+    assert L.uocr_moe_w13_bytes(64, 896, 1280, 128, 0) == 64 * 2 * 896 * 1280 * 2
+    assert L.uocr_moe_w2_bytes(64, 1280, 896, 128, 1) == 64 * (1280 // 32) * (32 * 896 + 32 * 7 * 4)
+    assert L.uocr_moe_w2_bytes(64, 1280, 896, 128, 0) == 64 * 1280 * 896 * 2
+    assert L.uocr_moe_w13_bytes(64, 896, 1280, 64, 1) == 0  # only the checkpoint's G = 128
+    rc = L.uocr_moe_pack_w13(None, None, None, None, 4, 100, 256, 128, 0, None, None)
+    assert rc == 1 and b"pack_w13" in L.uocr_last_error()
+    rc = L.uocr_moe_pack_w2(None, None, 4, 256, 896, 64, 1, None, None)
+    assert rc == 4 and b"group size" in L.uocr_last_error()

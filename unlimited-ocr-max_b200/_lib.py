@@ -35,9 +35,7 @@ class UocrMoeLayer(ctypes.Structure):
         ("reserved", ctypes.c_int32),
         ("router", P),
         ("w13", P),
-        ("s13", P),
         ("w2", P),
-        ("s2", P),
         ("w13_shared", P),
         ("w2_shared", P),
     ]
@@ -51,7 +49,10 @@ SIGNATURES: dict[str, tuple] = {
     "uocr_moe_int8_qmv": (I32, [P, I64, I64, P, I64, I64, P, I64, P, I64, I64, I64, P, I64, I64, I64, P]),
     "uocr_int8_dequant_expert": (I32, [P, I64, I64, P, I64, I64, I64, P, I64, I64, I64, P, I64, P]),
     "uocr_dense_bf16_qmv": (I32, [P, I64, I64, P, I64, I64, P, I64, I64, I64, I32, P]),
-    "uocr_moe_pack_gate_up": (I32, [P, P, I64, I64, I64, I32, P, P]),
+    "uocr_moe_w13_bytes": (SZ, [I64, I64, I64, I64, I32]),
+    "uocr_moe_w2_bytes": (SZ, [I64, I64, I64, I64, I32]),
+    "uocr_moe_pack_w13": (I32, [P, P, P, P, I64, I64, I64, I64, I32, P, P]),
+    "uocr_moe_pack_w2": (I32, [P, P, I64, I64, I64, I64, I32, P, P]),
     "uocr_moe_pack_shared": (I32, [P, P, P, I64, I64, I64, P, P, P]),
     "uocr_moe_route": (I32, [P, I64, I64, P, I64, P, I64, P, P, P]),
     "uocr_moe_decode_workspace_bytes": (SZ, [ctypes.POINTER(UocrMoeLayer), I64]),

@@ -9,6 +9,7 @@
 #include "../../include/uocr_moe.h"
 #include "common.cuh"
 #include "kernels.h"
+#include "layout.h"
 
 namespace {
 
@@ -77,7 +78,7 @@ extern "C" {
 
 const char* uocr_last_error(void) { return g_last_error.c_str(); }
 
-int uocr_abi_version(void) { return 1; }
+int uocr_abi_version(void) { return 2; }
 
 // ---------------------------------------------------------------------------------------
 // reference op shims
@@ -170,25 +171,57 @@ int uocr_dense_bf16_qmv(float* out, int64_t out_rows, int64_t out_cols, const fl
 // packing
 // ---------------------------------------------------------------------------------------
 
-int uocr_moe_pack_gate_up(const void* gate, const void* up, int64_t E, int64_t I, int64_t H, int elem_bytes,
-                          void* w13_out, uocr_stream_t stream) {
-    if (E < 1 || I < 1 || H < 1) return fail(UOCR_EINVAL, "pack_gate_up: empty stack");
-    if (I % 128) return fail(UOCR_EINVAL, "pack_gate_up: I=%lld is not a multiple of 128", (long long)I);
-    if (elem_bytes != 1 && elem_bytes != 2 && elem_bytes != 4)
-        return fail(UOCR_EINVAL, "pack_gate_up: elem_bytes must be 1, 2 or 4");
-    if ((H * elem_bytes) % 4) return fail(UOCR_EINVAL, "pack_gate_up: a row must be a multiple of 4 bytes");
-    if (!gate || !up || !w13_out) return fail(UOCR_EINVAL, "pack_gate_up: null pointer");
-    if ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) | reinterpret_cast<uintptr_t>(w13_out)) & 3)
-        return fail(UOCR_EINVAL, "pack_gate_up: pointers must be 4-byte aligned");
-    return cuda_status(uocr::launch_pack_gate_up(gate, up, E, I, H, elem_bytes, w13_out, S(stream)),
-                       "pack_gate_up: launch");
+static int check_pack(const char* who, int64_t E, int64_t N, int64_t K, int64_t G, int int8) {
+    if (E < 1 || N < 1 || K < 1) return fail(UOCR_EINVAL, "%s: empty stack", who);
+    if (K % 128) return fail(UOCR_EINVAL, "%s: K=%lld is not a multiple of 128", who, (long long)K);
+    if (int8 && (G != 128)) return fail(UOCR_EUNSUPPORTED, "%s: int8 group size %lld (this build packs G = 128)", who, (long long)G);
+    return ok();
+}
+
+size_t uocr_moe_w13_bytes(int64_t E, int64_t I, int64_t H, int64_t group, int int8) {
+    if (E < 1 || I < 16 || H < 128 || I % 16 || H % 128 || (int8 && group != 128)) return 0;
+    return (size_t)E * uocr::w13_expert_bytes((int)I, (int)H, (int)(int8 ? group : 128), int8 != 0);
+}
+
+size_t uocr_moe_w2_bytes(int64_t E, int64_t H, int64_t I, int64_t group, int int8) {
+    if (E < 1 || I < 128 || H < 32 || I % 128 || H % 32 || (int8 && group != 128)) return 0;
+    return (size_t)E * uocr::w2_expert_bytes((int)H, (int)I, (int)(int8 ? group : 128), int8 != 0);
+}
+
+int uocr_moe_pack_w13(const void* gate, const void* up, const float* gate_scales, const float* up_scales, int64_t E,
+                      int64_t I, int64_t H, int64_t group, int int8, void* w13_out, uocr_stream_t stream) {
+    int rc = check_pack("pack_w13", E, I, H, group, int8);
+    if (rc) return rc;
+    if (I % 16) return fail(UOCR_EINVAL, "pack_w13: I=%lld is not a multiple of 16", (long long)I);
+    if (!gate || !up || !w13_out || (int8 && (!gate_scales || !up_scales)))
+        return fail(UOCR_EINVAL, "pack_w13: null pointer");
+    if ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) | reinterpret_cast<uintptr_t>(w13_out) |
+         reinterpret_cast<uintptr_t>(gate_scales) | reinterpret_cast<uintptr_t>(up_scales)) & 3)
+        return fail(UOCR_EINVAL, "pack_w13: pointers must be 4-byte aligned");
+    return cuda_status(uocr::launch_pack_w13(gate, up, gate_scales, up_scales, (int)E, (int)I, (int)H,
+                                             int8 ? (int)group : 128, int8 != 0, w13_out, S(stream)),
+                       "pack_w13: launch");
+}
+
+int uocr_moe_pack_w2(const void* down, const float* down_scales, int64_t E, int64_t H, int64_t I, int64_t group,
+                     int int8, void* w2_out, uocr_stream_t stream) {
+    int rc = check_pack("pack_w2", E, H, I, group, int8);
+    if (rc) return rc;
+    if (H % 32) return fail(UOCR_EINVAL, "pack_w2: H=%lld is not a multiple of 32", (long long)H);
+    if (!down || !w2_out || (int8 && !down_scales)) return fail(UOCR_EINVAL, "pack_w2: null pointer");
+    if ((reinterpret_cast<uintptr_t>(down) | reinterpret_cast<uintptr_t>(w2_out) |
+         reinterpret_cast<uintptr_t>(down_scales)) & 3)
+        return fail(UOCR_EINVAL, "pack_w2: pointers must be 4-byte aligned");
+    return cuda_status(uocr::launch_pack_w2(down, down_scales, (int)E, (int)H, (int)I, int8 ? (int)group : 128,
+                                            int8 != 0, w2_out, S(stream)),
+                       "pack_w2: launch");
 }
 
 int uocr_moe_pack_shared(const uint16_t* gate, const uint16_t* up, const uint16_t* down, int64_t S_, int64_t I,
                          int64_t H, uint16_t* w13_out, uint16_t* w2_out, uocr_stream_t stream) {
     if (S_ < 1 || I < 1 || H < 1) return fail(UOCR_EINVAL, "pack_shared: empty");
     if (I % 128) return fail(UOCR_EINVAL, "pack_shared: I=%lld is not a multiple of 128", (long long)I);
-    if (H % 2) return fail(UOCR_EINVAL, "pack_shared: H must be even");
+    if (H % 128) return fail(UOCR_EINVAL, "pack_shared: H=%lld is not a multiple of 128", (long long)H);
     if (!gate || !up || !down || !w13_out || !w2_out) return fail(UOCR_EINVAL, "pack_shared: null pointer");
     return cuda_status(uocr::launch_pack_shared(gate, up, down, S_, I, H, w13_out, w2_out, S(stream)),
                        "pack_shared: launch");
@@ -228,7 +261,7 @@ int uocr_moe_route(const float* x, int64_t T, int64_t H, const uint16_t* router,
 namespace {
 
 struct DecodeLayout {
-    size_t ctl, logits, table, ids, wts, h, y, total;
+    size_t ctl, row_done, logits, table, ids, wts, h, y, total;
 };
 
 DecodeLayout decode_layout(const uocr_moe_layer* L, int64_t B) {
@@ -236,6 +269,7 @@ DecodeLayout decode_layout(const uocr_moe_layer* L, int64_t B) {
     const size_t pairs = (size_t)(L->top_k + L->n_shared) * (size_t)B;
     size_t off = 0;
     d.ctl = off; off += align256(sizeof(uocr::DecodeCtl));
+    d.row_done = off; off += align256(sizeof(uint32_t) * (size_t)(L->hidden / 4));
     d.logits = off; off += align256(sizeof(float) * 8 * 64);
     d.table = off; off += align256(sizeof(uocr::RouteTable));
     d.ids = off; off += align256(sizeof(int32_t) * (size_t)B * L->top_k);
@@ -248,18 +282,17 @@ DecodeLayout decode_layout(const uocr_moe_layer* L, int64_t B) {
 
 int check_layer(const uocr_moe_layer* L, const char* who) {
     if (!L) return fail(UOCR_EINVAL, "%s: null layer", who);
-    if (L->hidden < 64 || L->hidden % 64)
-        return fail(UOCR_EINVAL, "%s: hidden=%d must be a positive multiple of 64", who, L->hidden);
+    if (L->hidden < 128 || L->hidden % 128)
+        return fail(UOCR_EINVAL, "%s: hidden=%d must be a positive multiple of 128", who, L->hidden);
     if (L->inter < 128 || L->inter % 128)
         return fail(UOCR_EINVAL, "%s: inter=%d must be a positive multiple of 128", who, L->inter);
     if (L->n_routed < 1 || L->n_routed > 64) return fail(UOCR_EUNSUPPORTED, "%s: n_routed=%d outside 1..64", who, L->n_routed);
     if (L->n_shared < 0) return fail(UOCR_EINVAL, "%s: n_shared < 0", who);
     if (L->top_k < 1 || L->top_k > L->n_routed) return fail(UOCR_EINVAL, "%s: top_k=%d outside [1, E]", who, L->top_k);
-    if (L->int8) {
-        if (L->group < 8 || L->group % 8 || L->hidden % L->group || L->inter % L->group)
-            return fail(UOCR_EINVAL, "%s: int8 group size %d must divide hidden and inter (multiple of 8)", who, L->group);
-        if (!L->s13 || !L->s2) return fail(UOCR_EINVAL, "%s: int8 layer without scales", who);
-    }
+    if (L->int8 && L->group != 128)
+        return fail(UOCR_EUNSUPPORTED, "%s: int8 experts need the checkpoint's group size 128", who);
+    if (L->top_k > uocr::kDecodeMaxTopk)
+        return fail(UOCR_EUNSUPPORTED, "%s: top_k=%d above %d", who, L->top_k, uocr::kDecodeMaxTopk);
     if (!L->router || !L->w13 || !L->w2) return fail(UOCR_EINVAL, "%s: null weight pointer", who);
     if (L->n_shared > 0 && (!L->w13_shared || !L->w2_shared)) return fail(UOCR_EINVAL, "%s: null shared weights", who);
     if (!a16(L->router) || !a16(L->w13) || !a16(L->w2) || (L->n_shared && (!a16(L->w13_shared) || !a16(L->w2_shared))))
@@ -280,11 +313,7 @@ int uocr_moe_decode(const uocr_moe_layer* L, const float* x, int64_t B, const fl
     if (rc) return rc;
     if (B < 1 || B > 8) return fail(UOCR_EINVAL, "moe_decode: B=%lld outside 1..8 (use moe_prefill)", (long long)B);
     if (L->n_shared > uocr::kDecodeMaxShared) return fail(UOCR_EUNSUPPORTED, "moe_decode: more than 8 shared experts");
-    if (L->hidden % 128 || L->inter % 128)
-        return fail(UOCR_EUNSUPPORTED, "moe_decode: hidden and inter must be multiples of 128");
     if (L->hidden > 8192 || L->inter > 8192) return fail(UOCR_EUNSUPPORTED, "moe_decode: hidden/inter above 8192");
-    if (L->int8 && L->group != 128)
-        return fail(UOCR_EUNSUPPORTED, "moe_decode: int8 experts need the checkpoint's group size 128");
     if (!x || !out || !workspace) return fail(UOCR_EINVAL, "moe_decode: null pointer");
     if (!a16(x) || !a16(out)) return fail(UOCR_EINVAL, "moe_decode: x and out must be 16-byte aligned");
     if (bias && (reinterpret_cast<uintptr_t>(bias) & 3)) return fail(UOCR_EINVAL, "moe_decode: bias must be 4-byte aligned");
@@ -299,8 +328,9 @@ int uocr_moe_decode(const uocr_moe_layer* L, const float* x, int64_t B, const fl
     a.x = x; a.router = L->router; a.bias = bias;
     a.ids = ids_out ? ids_out : reinterpret_cast<int32_t*>(ws + d.ids);
     a.wts = wts_out ? wts_out : reinterpret_cast<float*>(ws + d.wts);
-    a.w13 = L->w13; a.s13 = L->s13; a.w2 = L->w2; a.s2 = L->s2;
+    a.w13 = L->w13; a.w2 = L->w2;
     a.w13_shared = L->w13_shared; a.w2_shared = L->w2_shared;
+    a.row_done = reinterpret_cast<uint32_t*>(ws + d.row_done);
     a.h = reinterpret_cast<float*>(ws + d.h);
     a.y = reinterpret_cast<float*>(ws + d.y);
     a.out = out;
@@ -339,7 +369,7 @@ int uocr_moe_prefill(const uocr_moe_layer* L, const float* x, int64_t T, const f
     a.x = x; a.router = L->router; a.bias = bias;
     a.ids = ids_out ? ids_out : reinterpret_cast<int32_t*>(ws + d.ids);
     a.wts = wts_out ? wts_out : reinterpret_cast<float*>(ws + d.wts);
-    a.w13 = L->w13; a.s13 = L->s13; a.w2 = L->w2; a.s2 = L->s2;
+    a.w13 = L->w13; a.w2 = L->w2;
     a.w13_shared = L->w13_shared; a.w2_shared = L->w2_shared;
     a.out = out;
     return cuda_status(uocr::launch_prefill(a, ws, d, S(stream)), "moe_prefill: launch");

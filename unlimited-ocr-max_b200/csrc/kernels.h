@@ -30,16 +30,21 @@ struct DecodeCtl {
     uint32_t pad[62];
 };
 constexpr int kDecodeMaxShared = 8;
+constexpr int kDecodeMaxTopk = 8;
 
-// The step's routing grouped by expert (written by the last ROUTE item).
+// The step's routing grouped by expert (written by the route kernel's last CTA). Routed slot u
+// (the u-th distinct expert, ascending id) owns rows [base[u], base[u] + count[u]) of the h and
+// y scratch; shared expert q owns rows [qB, qB + B) (row qB + t is token t).
 struct RouteTable {
     int U;  // distinct routed experts
     int pad[3];
     int expert[64];
     int count[64];
-    int pair[64][8];
+    int base[64];
     int token[64][8];
     float weight[64][8];
+    int tok_row[8][kDecodeMaxTopk];    // token t's routed rows, ascending expert id
+    float tok_w[8][kDecodeMaxTopk];    // and their routing weights
 };
 
 struct DecodeArgs {
@@ -49,17 +54,16 @@ struct DecodeArgs {
     const float* bias;
     int32_t* ids;
     float* wts;
-    const void* w13;
-    const float* s13;
+    const void* w13;   // packed blocks (layout.h), int8 scales inline
     const void* w2;
-    const float* s2;
     const uint16_t* w13_shared;
     const uint16_t* w2_shared;
-    float* h;       // [(k+S)*B, I]
-    float* y;       // [(k+S)*B, H]
+    float* h;       // [(k+S)*B, I], slot-contiguous rows
+    float* y;       // [(k+S)*B, H], slot-contiguous rows
     float* out;     // [B, H]
     DecodeCtl* ctl;
-    float* logits;  // [8][64]
+    uint32_t* row_done;  // [H/4] combine counters (self-resetting)
+    float* logits;       // [8][64]
     RouteTable* table;
     unsigned long long* trace;  // optional per-CTA item timeline (diagnostics), null = off
     int trace_items;            // items recorded per CTA
@@ -93,9 +97,7 @@ struct PrefillArgs {
     int32_t* ids;  // [T, topk]
     float* wts;    // [T, topk]
     const void* w13;
-    const float* s13;
     const void* w2;
-    const float* s2;
     const uint16_t* w13_shared;
     const uint16_t* w2_shared;
     float* out;  // [T, H]
@@ -108,8 +110,10 @@ PrefillLayout prefill_layout(int T, int H, int I, int E, int S, int topk, bool i
 cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& d, cudaStream_t st);
 
 // pack.cu
-cudaError_t launch_pack_gate_up(const void* gate, const void* up, long E, long I, long H, int esz, void* out,
-                                cudaStream_t st);
+cudaError_t launch_pack_w13(const void* gate, const void* up, const float* gs, const float* us, int E, int I, int H,
+                            int G, bool int8, void* out, cudaStream_t st);
+cudaError_t launch_pack_w2(const void* down, const float* ds, int E, int H, int I, int G, bool int8, void* out,
+                           cudaStream_t st);
 cudaError_t launch_pack_shared(const uint16_t* gate, const uint16_t* up, const uint16_t* down, long S, long I, long H,
                                uint16_t* w13, uint16_t* w2, cudaStream_t st);
 

@@ -1,48 +1,71 @@
 // Weight layout transforms, run once at load (the part of weight_adapters.stack_expert_weights
 // that concerns the MoE tensors, unlimited_ocr_max/weight_adapters.py:121-163, re-laid out
-// for this library's kernels). Bit copies only.
+// into the blocks of layout.h). Bit copies only.
 #include "common.cuh"
 #include "kernels.h"
+#include "layout.h"
 
 namespace uocr {
 
-// Copy `bytes` bytes (a multiple of 4) from src to dst with 32-bit words, one row per CTA.
-__device__ void copy_row_words(uint32_t* dst, const uint32_t* src, long words) {
+// Copy `words` 32-bit words, the CTA's threads striding over them.
+__device__ void copy_words(uint32_t* dst, const uint32_t* src, long words) {
     for (long i = threadIdx.x; i < words; i += blockDim.x) dst[i] = src[i];
 }
 
-// gate/up [E, I, H] -> [E, 2I, H], rows interleaved in blocks of 128:
-// packed row 256b + r    <- gate row 128b + r
-// packed row 256b+128+r  <- up   row 128b + r
-__global__ void pack_gate_up_kernel(const char* gate, const char* up, long I, long row_bytes, char* out) {
-    const long prow = blockIdx.x;          // packed row within the expert
-    const long e = blockIdx.y;
-    const long blk = prow / 256, r = prow % 256;
-    const bool is_up = r >= 128;
-    const long src_row = blk * 128 + (r % 128);
-    const char* src = (is_up ? up : gate) + (e * I + src_row) * row_bytes;
-    char* dst = out + (e * 2 * I + prow) * row_bytes;
-    copy_row_words(reinterpret_cast<uint32_t*>(dst), reinterpret_cast<const uint32_t*>(src), row_bytes / 4);
+// One CTA per (block, expert): gate/up rows [pP, pP+P) and, for int8, their scales.
+__global__ void pack_w13_kernel(const char* gate, const char* up, const float* gs, const float* us, int I, int H,
+                                int G, int esz, int P, size_t block_bytes, char* out) {
+    const long b = blockIdx.x, e = blockIdx.y;
+    const long row0 = e * I + b * P;  // first source row (gate and up share row numbers)
+    const size_t rb = (size_t)H * esz;
+    char* dst = out + (e * (I / P) + b) * block_bytes;
+    copy_words(reinterpret_cast<uint32_t*>(dst), reinterpret_cast<const uint32_t*>(gate + row0 * rb), P * rb / 4);
+    copy_words(reinterpret_cast<uint32_t*>(dst + P * rb), reinterpret_cast<const uint32_t*>(up + row0 * rb),
+               P * rb / 4);
+    if (gs) {
+        const long ng = H / G;
+        float* ds = reinterpret_cast<float*>(dst + 2 * P * rb);
+        copy_words(reinterpret_cast<uint32_t*>(ds), reinterpret_cast<const uint32_t*>(gs + row0 * ng), P * ng);
+        copy_words(reinterpret_cast<uint32_t*>(ds + P * ng), reinterpret_cast<const uint32_t*>(us + row0 * ng),
+                   P * ng);
+    }
 }
 
-cudaError_t launch_pack_gate_up(const void* gate, const void* up, long E, long I, long H, int esz, void* out,
-                                cudaStream_t st) {
-    dim3 grid((unsigned)(2 * I), (unsigned)E);
-    pack_gate_up_kernel<<<grid, 128, 0, st>>>(reinterpret_cast<const char*>(gate), reinterpret_cast<const char*>(up),
-                                              I, H * esz, reinterpret_cast<char*>(out));
+cudaError_t launch_pack_w13(const void* gate, const void* up, const float* gs, const float* us, int E, int I, int H,
+                            int G, bool int8, void* out, cudaStream_t st) {
+    const int P = w13_pairs(int8);
+    dim3 grid((unsigned)(I / P), (unsigned)E);
+    pack_w13_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const char*>(gate), reinterpret_cast<const char*>(up),
+                                          int8 ? gs : nullptr, int8 ? us : nullptr, I, H, G, int8 ? 1 : 2, P,
+                                          w13_block_bytes(H, G, int8), reinterpret_cast<char*>(out));
     return cudaGetLastError();
 }
 
-// shared experts: gate/up [S*I, H] -> [S, 2I, H] (interleaved as above); down [H, S*I] -> [S, H, I]
-__global__ void pack_shared_gate_up_kernel(const uint16_t* gate, const uint16_t* up, long I, long H, uint16_t* out) {
-    const long prow = blockIdx.x, s = blockIdx.y;
-    const long blk = prow / 256, r = prow % 256;
-    const long src_row = s * I + blk * 128 + (r % 128);
-    const uint16_t* src = (r >= 128 ? up : gate) + src_row * H;
-    uint16_t* dst = out + (s * 2 * I + prow) * H;
-    copy_row_words(reinterpret_cast<uint32_t*>(dst), reinterpret_cast<const uint32_t*>(src), H / 2);
+// One CTA per (block, expert): down rows [32b, 32b+32) and, for int8, their scales.
+__global__ void pack_w2_kernel(const char* down, const float* ds, int H, int I, int G, int esz, size_t block_bytes,
+                               char* out) {
+    const long b = blockIdx.x, e = blockIdx.y;
+    const long row0 = e * H + b * kW2Rows;
+    const size_t rb = (size_t)I * esz;
+    char* dst = out + (e * (H / kW2Rows) + b) * block_bytes;
+    copy_words(reinterpret_cast<uint32_t*>(dst), reinterpret_cast<const uint32_t*>(down + row0 * rb),
+               kW2Rows * rb / 4);
+    if (ds) {
+        const long ng = I / G;
+        copy_words(reinterpret_cast<uint32_t*>(dst + kW2Rows * rb), reinterpret_cast<const uint32_t*>(ds + row0 * ng),
+                   kW2Rows * ng);
+    }
 }
 
+cudaError_t launch_pack_w2(const void* down, const float* ds, int E, int H, int I, int G, bool int8, void* out,
+                           cudaStream_t st) {
+    dim3 grid((unsigned)(H / kW2Rows), (unsigned)E);
+    pack_w2_kernel<<<grid, 256, 0, st>>>(reinterpret_cast<const char*>(down), int8 ? ds : nullptr, H, I, G,
+                                         int8 ? 1 : 2, w2_block_bytes(I, G, int8), reinterpret_cast<char*>(out));
+    return cudaGetLastError();
+}
+
+// shared experts: gate/up [S*I, H] -> bf16 w13 blocks of S pseudo-experts; down [H, S*I] -> [S, H, I]
 __global__ void pack_shared_down_kernel(const uint16_t* down, long S, long I, long H, uint16_t* out) {
     const long j = blockIdx.x, s = blockIdx.y;
     const uint16_t* src = down + j * S * I + s * I;
@@ -52,7 +75,8 @@ __global__ void pack_shared_down_kernel(const uint16_t* down, long S, long I, lo
 
 cudaError_t launch_pack_shared(const uint16_t* gate, const uint16_t* up, const uint16_t* down, long S, long I, long H,
                                uint16_t* w13, uint16_t* w2, cudaStream_t st) {
-    pack_shared_gate_up_kernel<<<dim3((unsigned)(2 * I), (unsigned)S), 128, 0, st>>>(gate, up, I, H, w13);
+    cudaError_t err = launch_pack_w13(gate, up, nullptr, nullptr, (int)S, (int)I, (int)H, 128, false, w13, st);
+    if (err != cudaSuccess) return err;
     pack_shared_down_kernel<<<dim3((unsigned)H, (unsigned)S), 128, 0, st>>>(down, S, I, H, w2);
     return cudaGetLastError();
 }

@@ -27,6 +27,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "layout.h"
 #include "sm100.cuh"
 
 namespace uocr {
@@ -149,21 +150,49 @@ __global__ void __launch_bounds__(256) prefill_gather_kernel(const float* __rest
     }
 }
 
-// int8 routed stacks -> bf16 (the int8 prefill's B operands): bf16_rne(f32(q) * scale), exactly
-// int8_dequant_expert's bits (kernels/moe_int8.mojo:330-340), for a whole [rows, K] stack.
-__global__ void __launch_bounds__(256) prefill_dequant_kernel(const int8_t* __restrict__ w, const float* __restrict__ s,
-                                                              long rows, int K, int G, uint16_t* __restrict__ out) {
+// int8 gate|up blocks (layout.h) -> the bf16 gate|up row matrix (8-row interleave): each bf16
+// element is bf16_rne(f32(q) * scale), int8_dequant_expert's bits (kernels/moe_int8.mojo:330-340).
+// Thread: 8 consecutive elements of one bf16 row.
+__global__ void __launch_bounds__(256) prefill_dequant_w13_kernel(const unsigned char* __restrict__ w, long rows, int I,
+                                                                  int H, int G, size_t blk_bytes,
+                                                                  uint16_t* __restrict__ out) {
     const long i = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 8;
-    if (i >= rows * K) return;
-    const long r = i / K;
-    const int k = (int)(i - r * K);
-    const uint2 v = *reinterpret_cast<const uint2*>(w + i);
+    if (i >= rows * H) return;
+    const long prow = i / H;  // bf16 packed row: 16-row groups of 8 gate then 8 up rows
+    const int k = (int)(i - prow * H);
+    const long per_e = 2L * I;
+    const long e = prow / per_e, pr = prow - e * per_e;
+    const bool is_up = (pr & 15) >= 8;
+    const long r = (pr >> 4) * 8 + (pr & 7);  // gate/up row within the expert
+    const long b16 = r >> 4, j = r & 15;      // int8 block of 16 row pairs, row within it
+    const unsigned char* blk = w + (size_t)(e * (I / 16) + b16) * blk_bytes;
+    const unsigned char* src = blk + (size_t)(is_up ? 16 + j : j) * H + k;
+    const float* sc = reinterpret_cast<const float*>(blk + 32 * (size_t)H) + (is_up ? 16 : 0) * (H / G) + j * (H / G);
+    const uint2 v = *reinterpret_cast<const uint2*>(src);
     float f[8];
     unpack_s8x8(v.x, v.y, f);
-    const float* sr = s + r * (K / G);
     uint16_t o[8];
 #pragma unroll
-    for (int j = 0; j < 8; ++j) o[j] = f32_to_bf16_rne(__fmul_rn(f[j], sr[(k + j) / G]));
+    for (int q = 0; q < 8; ++q) o[q] = f32_to_bf16_rne(__fmul_rn(f[q], sc[(k + q) / G]));
+    *reinterpret_cast<uint4*>(out + i) = *reinterpret_cast<const uint4*>(o);
+}
+
+// int8 down blocks (32 rows + scales) -> bf16 [E*H, I].
+__global__ void __launch_bounds__(256) prefill_dequant_w2_kernel(const unsigned char* __restrict__ w, long rows, int I,
+                                                                 int G, size_t blk_bytes, uint16_t* __restrict__ out) {
+    const long i = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 8;
+    if (i >= rows * I) return;
+    const long row = i / I;  // e * H + j
+    const int k = (int)(i - row * I);
+    const unsigned char* blk = w + (size_t)(row / kW2Rows) * blk_bytes;
+    const int j = (int)(row % kW2Rows);
+    const uint2 v = *reinterpret_cast<const uint2*>(blk + (size_t)j * I + k);
+    const float* sc = reinterpret_cast<const float*>(blk + (size_t)kW2Rows * I) + j * (I / G);
+    float f[8];
+    unpack_s8x8(v.x, v.y, f);
+    uint16_t o[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) o[q] = f32_to_bf16_rne(__fmul_rn(f[q], sc[(k + q) / G]));
     *reinterpret_cast<uint4*>(out + i) = *reinterpret_cast<const uint4*>(o);
 }
 
@@ -355,26 +384,25 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             const size_t out_row = (size_t)G.out_base + (size_t)mloc * kBM + row_in_tile;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)acc * kBN;
             if (kEpi == kEpiSwiGLU) {
-                // packed columns: [0,128) gate rows n*128.., [128,256) up rows n*128..
+                // tile columns in groups of 16: 8 gate rows then the same 8 up rows, so columns
+                // [32c, 32c + 32) give h columns [16c, 16c + 16) of this tile's 128
                 uint16_t* h = reinterpret_cast<uint16_t*>(out) + out_row * out_ld + (size_t)n * (kBN / 2);
 #pragma unroll 1
-                for (int c = 0; c < 4; ++c) {
-                    uint32_t gr[32], ur[32];
-                    tmem_ld_32x32b_x32(taddr + c * 32, gr);
-                    tmem_ld_32x32b_x32(taddr + 128 + c * 32, ur);
+                for (int c = 0; c < kBN / 32; ++c) {
+                    uint32_t r[32];
+                    tmem_ld_32x32b_x32(taddr + c * 32, r);
                     tmem_wait_ld();
-                    uint32_t pk[16];
+                    uint32_t pk[8];
 #pragma unroll
-                    for (int i = 0; i < 16; ++i) {
-                        const float g0 = __uint_as_float(gr[2 * i]), g1 = __uint_as_float(gr[2 * i + 1]);
-                        const float u0 = __uint_as_float(ur[2 * i]), u1 = __uint_as_float(ur[2 * i + 1]);
+                    for (int i = 0; i < 8; ++i) {
+                        const int c0 = (2 * i) / 8 * 16 + (2 * i) % 8;  // gate column of h column 2i
+                        const float g0 = __uint_as_float(r[c0]), g1 = __uint_as_float(r[c0 + 1]);
+                        const float u0 = __uint_as_float(r[c0 + 8]), u1 = __uint_as_float(r[c0 + 9]);
                         pk[i] = (uint32_t)f32_to_bf16_rne(silu(g0) * u0) | ((uint32_t)f32_to_bf16_rne(silu(g1) * u1) << 16);
                     }
                     if (live) {
-#pragma unroll
-                        for (int v = 0; v < 4; ++v)
-                            *reinterpret_cast<uint4*>(h + c * 32 + v * 8) =
-                                make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+                        *reinterpret_cast<uint4*>(h + c * 16) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                        *reinterpret_cast<uint4*>(h + c * 16 + 8) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
                     }
                 }
             } else {
@@ -518,10 +546,11 @@ cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& 
         uint16_t* w13d = reinterpret_cast<uint16_t*>(ws + d.w13);
         uint16_t* w2d = reinterpret_cast<uint16_t*>(ws + d.w2);
         const long n13 = (long)E * 2 * I * H, n2 = (long)E * H * I;
-        prefill_dequant_kernel<<<(unsigned)((n13 / 8 + 255) / 256), 256, 0, st>>>(
-            reinterpret_cast<const int8_t*>(a.w13), a.s13, (long)E * 2 * I, H, a.G, w13d);
-        prefill_dequant_kernel<<<(unsigned)((n2 / 8 + 255) / 256), 256, 0, st>>>(
-            reinterpret_cast<const int8_t*>(a.w2), a.s2, (long)E * H, I, a.G, w2d);
+        prefill_dequant_w13_kernel<<<(unsigned)((n13 / 8 + 255) / 256), 256, 0, st>>>(
+            reinterpret_cast<const unsigned char*>(a.w13), (long)E * 2 * I, I, H, a.G, w13_block_bytes(H, a.G, true),
+            w13d);
+        prefill_dequant_w2_kernel<<<(unsigned)((n2 / 8 + 255) / 256), 256, 0, st>>>(
+            reinterpret_cast<const unsigned char*>(a.w2), (long)E * H, I, a.G, w2_block_bytes(I, a.G, true), w2d);
         w13 = w13d;
         w2 = w2d;
     }

@@ -65,8 +65,8 @@ class MoEConfig:
             for name in ("hidden_size", "moe_intermediate_size"):
                 if getattr(self, name) % INT8_GROUP_SIZE:
                     raise ConfigError(f"int8 experts need {name} divisible by the group size {INT8_GROUP_SIZE}")
-        if self.hidden_size % 64:
-            raise ConfigError("hidden_size must be a multiple of 64 (router segments, 16-byte loads)")
+        if self.hidden_size % 128:
+            raise ConfigError("hidden_size must be a multiple of 128 (packed weight blocks, 16-byte loads)")
         if self.moe_intermediate_size % 128:
             raise ConfigError("moe_intermediate_size must be a multiple of 128 (gate|up packing)")
         if not 1 <= self.num_experts_per_tok <= self.n_routed_experts <= 64:
@@ -133,24 +133,29 @@ class UocrMoE:
         wdt = torch.int8 if cfg.int8_experts else torch.bfloat16
         gate = on_dev("experts.gate_proj", wdt, (E, I, H))
         up = on_dev("experts.up_proj", wdt, (E, I, H))
-        t["w2"] = on_dev("experts.down_proj", wdt, (E, H, I))
-        t["w13"] = torch.empty((E, 2 * I, H), dtype=wdt, device=dev)
-        stream = torch.cuda.current_stream(dev).cuda_stream
+        G = INT8_GROUP_SIZE
         L = load()
-        check(L.uocr_moe_pack_gate_up(gate.data_ptr(), up.data_ptr(), E, I, H, gate.element_size(), t["w13"].data_ptr(), stream))
+        stream = torch.cuda.current_stream(dev).cuda_stream
+        i8 = int(cfg.int8_experts)
+        scales = {}
         if cfg.int8_experts:
-            G = INT8_GROUP_SIZE
-            gs = on_dev("experts.gate_proj_scales", torch.float32, (E, I, H // G))
-            us = on_dev("experts.up_proj_scales", torch.float32, (E, I, H // G))
-            t["s2"] = on_dev("experts.down_proj_scales", torch.float32, (E, H, I // G))
-            t["s13"] = torch.empty((E, 2 * I, H // G), dtype=torch.float32, device=dev)
-            check(L.uocr_moe_pack_gate_up(gs.data_ptr(), us.data_ptr(), E, I, H // G, 4, t["s13"].data_ptr(), stream))
+            scales["gate"] = on_dev("experts.gate_proj_scales", torch.float32, (E, I, H // G))
+            scales["up"] = on_dev("experts.up_proj_scales", torch.float32, (E, I, H // G))
+            scales["down"] = on_dev("experts.down_proj_scales", torch.float32, (E, H, I // G))
+        down = on_dev("experts.down_proj", wdt, (E, H, I))
+        ptr = lambda n: scales[n].data_ptr() if n in scales else None  # noqa: E731
+        t["w13"] = torch.empty(L.uocr_moe_w13_bytes(E, I, H, G, i8), dtype=torch.uint8, device=dev)
+        t["w2"] = torch.empty(L.uocr_moe_w2_bytes(E, H, I, G, i8), dtype=torch.uint8, device=dev)
+        check(L.uocr_moe_pack_w13(gate.data_ptr(), up.data_ptr(), ptr("gate"), ptr("up"), E, I, H, G, i8,
+                                  t["w13"].data_ptr(), stream))
+        check(L.uocr_moe_pack_w2(down.data_ptr(), ptr("down"), E, H, I, G, i8, t["w2"].data_ptr(), stream))
+        del scales, down
         sg = _unkblock(state["shared_experts.gate_proj.weight"]).to(dev, torch.bfloat16).contiguous()
         su = _unkblock(state["shared_experts.up_proj.weight"]).to(dev, torch.bfloat16).contiguous()
         sd = _unkblock(state["shared_experts.down_proj.weight"]).to(dev, torch.bfloat16).contiguous()
         if tuple(sg.shape) != (S * I, H) or tuple(su.shape) != (S * I, H) or tuple(sd.shape) != (H, S * I):
             raise ValueError("shared_experts: projections do not match shared_experts_dim")
-        t["w13s"] = torch.empty((S, 2 * I, H), dtype=torch.bfloat16, device=dev)
+        t["w13s"] = torch.empty(L.uocr_moe_w13_bytes(S, I, H, G, 0) // 2, dtype=torch.bfloat16, device=dev)
         t["w2s"] = torch.empty((S, H, I), dtype=torch.bfloat16, device=dev)
         check(L.uocr_moe_pack_shared(sg.data_ptr(), su.data_ptr(), sd.data_ptr(), S, I, H,
                                      t["w13s"].data_ptr(), t["w2s"].data_ptr(), stream))
@@ -161,8 +166,6 @@ class UocrMoE:
         lay.top_k, lay.group, lay.int8 = cfg.num_experts_per_tok, INT8_GROUP_SIZE, int(cfg.int8_experts)
         lay.router = t["router"].data_ptr()
         lay.w13, lay.w2 = t["w13"].data_ptr(), t["w2"].data_ptr()
-        lay.s13 = t["s13"].data_ptr() if cfg.int8_experts else None
-        lay.s2 = t["s2"].data_ptr() if cfg.int8_experts else None
         lay.w13_shared, lay.w2_shared = t["w13s"].data_ptr(), t["w2s"].data_ptr()
         self._layer = lay
         return self
