@@ -530,7 +530,7 @@ def run_ours(args):
         v, cores, sample = CpuDecode(True, B).rate()
         cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
     if rank == 0:
-        launches_per_step = 3 * L  # per layer: route, gate|up experts, down experts + combine
+        launches_per_step = 2 * L  # per layer: route + gate|up experts, down experts + combine
         line = {
             "metric": "MoE-layer tokens/s (decode, int8 routed experts, B=8)",
             "value": value,

@@ -108,17 +108,19 @@ typedef struct uocr_moe_layer {
     const void* w13;            /* routed gate|up blocks (uocr_moe_pack_w13) */
     const void* w2;             /* routed down blocks (uocr_moe_pack_w2) */
     const uint16_t* w13_shared; /* shared gate|up as S bf16 experts (uocr_moe_pack_shared) */
-    const uint16_t* w2_shared;  /* shared down as S experts [S, H, I] bf16 */
+    const uint16_t* w2_shared;  /* shared down as S bf16 experts (uocr_moe_pack_shared) */
 } uocr_moe_layer;
 
 /* Packed layouts (the reference keeps the checkpoint's [E, N, K] stacks, decoder.py:305-313;
  * this library re-lays them out once at load so that one decode work item is one contiguous
  * block):
+ *   every packed row of K elements is followed by 16 bytes of padding;
  *   w13: per expert, I/P blocks of P row pairs (P = 8 bf16, 16 int8):
  *        [gate rows (P x H) | up rows (P x H) | int8: gate scales (P x H/G fp32) | up scales]
- *        (for bf16: the [E*2I, H] matrix with gate and up rows interleaved in groups of 8);
+ *        (for bf16: the [E*2I, H] matrix, row stride H + 8, gate and up rows interleaved in
+ *        groups of 8);
  *   w2:  per expert, H/32 blocks of 32 rows: [rows (32 x I) | int8: scales (32 x I/G fp32)]
- *        (for bf16: the plain [E, H, I] stack).
+ *        (for bf16: the [E*H, I] matrix, row stride I + 8).
  * Sizes in bytes for E experts: */
 UOCR_API size_t uocr_moe_w13_bytes(int64_t E, int64_t I, int64_t H, int64_t group, int int8);
 UOCR_API size_t uocr_moe_w2_bytes(int64_t E, int64_t H, int64_t I, int64_t group, int int8);
@@ -135,8 +137,8 @@ UOCR_API int uocr_moe_pack_w2(const void* down, const float* down_scales, int64_
 
 /* Pack the shared experts (shared_experts.{gate,up,down}_proj.weight as [S*I, H], [S*I, H],
  * [H, S*I] in plain [out, in] order) into w13_shared (uocr_moe_w13_bytes(S, I, H, 128, 0)
- * bytes, bf16 blocks) and w2_shared [S, H, I]: shared expert s owns intermediate rows
- * [s*I, (s+1)*I). */
+ * bytes) and w2_shared (uocr_moe_w2_bytes(S, H, I, 128, 0) bytes), bf16 layouts as above:
+ * shared expert s owns intermediate rows [s*I, (s+1)*I). */
 UOCR_API int uocr_moe_pack_shared(const uint16_t* gate, const uint16_t* up, const uint16_t* down,
                          int64_t S, int64_t I, int64_t H,
                          uint16_t* w13_out, uint16_t* w2_out, uocr_stream_t stream);

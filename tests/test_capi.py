@@ -135,11 +135,12 @@ def test_config_validation(uocr):
 def test_packed_sizes_and_refusals(uocr):
     """Packed block sizes follow the layout; bad packing calls are refused on the host."""
     L = uocr.load()
-    # int8 w13: per block of 16 row pairs 2*16*H bytes + 2*16*(H/128) fp32 scales
-    assert L.uocr_moe_w13_bytes(64, 896, 1280, 128, 1) == 64 * (896 // 16) * (2 * 16 * 1280 + 2 * 16 * 10 * 4)
-    assert L.uocr_moe_w13_bytes(64, 896, 1280, 128, 0) == 64 * 2 * 896 * 1280 * 2
-    assert L.uocr_moe_w2_bytes(64, 1280, 896, 128, 1) == 64 * (1280 // 32) * (32 * 896 + 32 * 7 * 4)
-    assert L.uocr_moe_w2_bytes(64, 1280, 896, 128, 0) == 64 * 1280 * 896 * 2
+    # every packed row carries 16 bytes of padding; int8 w13: per block of 16 row pairs
+    # 32 rows of (H + 16) bytes + 2*16*(H/128) fp32 scales
+    assert L.uocr_moe_w13_bytes(64, 896, 1280, 128, 1) == 64 * (896 // 16) * (32 * (1280 + 16) + 2 * 16 * 10 * 4)
+    assert L.uocr_moe_w13_bytes(64, 896, 1280, 128, 0) == 64 * (896 // 8) * 16 * (2 * 1280 + 16)
+    assert L.uocr_moe_w2_bytes(64, 1280, 896, 128, 1) == 64 * (1280 // 32) * (32 * (896 + 16) + 32 * 7 * 4)
+    assert L.uocr_moe_w2_bytes(64, 1280, 896, 128, 0) == 64 * 1280 * (2 * 896 + 16)
     assert L.uocr_moe_w13_bytes(64, 896, 1280, 64, 1) == 0  # only the checkpoint's G = 128
     rc = L.uocr_moe_pack_w13(None, None, None, None, 4, 100, 256, 128, 0, None, None)
     assert rc == 1 and b"pack_w13" in L.uocr_last_error()

@@ -1,6 +1,7 @@
 """The packed weight blocks (uocr_moe_pack_w13 / _w2 / _shared) byte for byte against a numpy
-statement of the layout: w13 blocks of P row pairs [gate P rows | up P rows | int8: gate
-scales | up scales] (P = 8 bf16, 16 int8); w2 blocks of 32 rows [rows | int8: scales]."""
+statement of the layout: every row followed by 16 zero bytes; w13 blocks of P row pairs
+[gate P rows | up P rows | int8: gate scales | up scales] (P = 8 bf16, 16 int8); w2 blocks of
+32 rows [rows | int8: scales]."""
 
 from __future__ import annotations
 
@@ -12,13 +13,20 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
+PAD = 16
+
+
+def padded(rows: np.ndarray) -> bytes:
+    return b"".join(r.tobytes() + bytes(PAD) for r in rows)
+
+
 def w13_ref(gate: np.ndarray, up: np.ndarray, gs, us, P: int) -> bytes:
     E, I, H = gate.shape
     out = bytearray()
     for e in range(E):
         for b in range(I // P):
             rows = slice(b * P, (b + 1) * P)
-            out += gate[e, rows].tobytes() + up[e, rows].tobytes()
+            out += padded(gate[e, rows]) + padded(up[e, rows])
             if gs is not None:
                 out += gs[e, rows].tobytes() + us[e, rows].tobytes()
     return bytes(out)
@@ -30,7 +38,7 @@ def w2_ref(down: np.ndarray, ds) -> bytes:
     for e in range(E):
         for b in range(H // 32):
             rows = slice(b * 32, (b + 1) * 32)
-            out += down[e, rows].tobytes()
+            out += padded(down[e, rows])
             if ds is not None:
                 out += ds[e, rows].tobytes()
     return bytes(out)
@@ -76,10 +84,10 @@ def test_pack_shared_blocks(uocr):
     down = rng.integers(0, 1 << 16, (H, S * I), dtype=np.uint16)
     dev = lambda a: torch.from_numpy(a.view(np.int16)).to(DEV)  # noqa: E731
     o13 = torch.zeros(L.uocr_moe_w13_bytes(S, I, H, 128, 0), dtype=torch.uint8, device=DEV)
-    o2 = torch.zeros(S * H * I * 2, dtype=torch.uint8, device=DEV)
+    o2 = torch.zeros(L.uocr_moe_w2_bytes(S, H, I, 128, 0), dtype=torch.uint8, device=DEV)
     assert L.uocr_moe_pack_shared(dev(gate).data_ptr(), dev(up).data_ptr(), dev(down).data_ptr(), S, I, H,
                                   o13.data_ptr(), o2.data_ptr(), torch.cuda.current_stream().cuda_stream) == 0
     torch.cuda.synchronize()
     assert o13.cpu().numpy().tobytes() == w13_ref(gate.reshape(S, I, H), up.reshape(S, I, H), None, None, 8)
     want2 = np.stack([down[:, q * I:(q + 1) * I] for q in range(S)])
-    assert o2.cpu().numpy().tobytes() == want2.tobytes()
+    assert o2.cpu().numpy().tobytes() == padded(want2.reshape(S * H, I))

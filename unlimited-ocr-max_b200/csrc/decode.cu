@@ -28,6 +28,7 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "layout.h"
+#include "mma.cuh"
 #include "sm100.cuh"
 
 namespace uocr {
@@ -49,6 +50,7 @@ struct SlotTable {
     int base[kMaxSlotsSm];
     int token[kMaxSlotsSm][kMaxB];
     float weight[kMaxSlotsSm][kMaxB];
+    signed char pos[kMaxSlotsSm][kMaxB];  // pos[slot][t]: entry of token t in the slot, -1 if none
 };
 
 struct ItemMeta {
@@ -67,6 +69,7 @@ UOCR_DEV void load_shared_slots(SlotTable* tb, const DecodeArgs& a, int tid, int
         for (int t = 0; t < kMaxB; ++t) {
             tb->token[s][t] = t;
             tb->weight[s][t] = 1.0f;
+            tb->pos[s][t] = t < a.B ? (signed char)t : (signed char)-1;
         }
     }
     if (tid == 0) tb->nslot = a.S;
@@ -99,51 +102,188 @@ UOCR_DEV unsigned long long* trace_rec(const DecodeArgs& a, int half, int n) {
     return a.trace + ((size_t)blockIdx.x * a.trace_items + (size_t)half * (a.trace_items / 2) + n) * 8;
 }
 
-// Weight words of one staged row for lane l's chunks k = 4(l + 32j), j < NJ:
-// int8 -> one u32 (4 weights), bf16 -> two u32.
-template <bool kI8, int NJ>
-UOCR_DEV void lds_row(uint32_t row, int lane, uint32_t (&w)[NJ][kI8 ? 1 : 2]) {
+// ---- tensor-core tile products (mma.cuh) -------------------------------------------------
+// Rows live in shared memory with a stride of `rowb` bytes; a k-step is 32 bytes of a row.
+// Lane (g, t) loads 8 bytes at 8t of rows g and g + 8 of the 16-row tile starting at `rows_s`.
+//
+// s8 weights, int8-digit activations: k-steps [s0, s1) of the tile; digits `xd_s` in fragment
+// order ([k-step][digit][lane] x 8 bytes), their scales sig[col * NG + group]; per-row weight
+// scales at sc_s + 4 * (row * NG + group) for the tile's rows row0 + g, row0 + g + 8. Adds the
+// fp32 products to acc (C layout: (g, 2t), (g, 2t + 1), (g + 8, 2t), (g + 8, 2t + 1)).
+UOCR_DEV void mma_tile_s8(uint32_t rows_s, uint32_t rowb, int row0, uint32_t sc_s, int NG, int s0, int s1,
+                          uint32_t xd_s, const float* sig, int lane, float (&acc)[4]) {
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t ra = rows_s + (uint32_t)g * rowb + 8u * t, rb = ra + 8u * rowb;
+    for (int s = s0; s < s1;) {
+        const int grp = s >> 2;
+        const int se = min(s1, (grp + 1) << 2);
+        int c[3][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}, {0, 0, 0, 0}};
+        for (; s < se; ++s) {
+            const uint2 A0 = lds_u64(ra + 32u * s), A1 = lds_u64(rb + 32u * s);
 #pragma unroll
-    for (int j = 0; j < NJ; ++j) {
-        const uint32_t k = 4u * (lane + 32 * j);
-        if (kI8) {
-            w[j][0] = lds_u32(row + k);
-        } else {
-            const uint2 v = lds_u64(row + 2 * k);
-            w[j][0] = v.x;
-            w[j][kI8 ? 0 : 1] = v.y;
+            for (int d = 0; d < 3; ++d) {
+                const uint2 Bd = lds_u64(xd_s + 8u * ((s * 3 + d) * 32 + lane));
+                mma_s8(c[d], A0.x, A1.x, A0.y, A1.y, Bd.x, Bd.y);
+            }
+        }
+        const float slo = lds_f32(sc_s + 4u * ((row0 + g) * NG + grp));
+        const float shi = lds_f32(sc_s + 4u * ((row0 + g + 8) * NG + grp));
+        const float sg0 = sig[(2 * t) * NG + grp], sg1 = sig[(2 * t + 1) * NG + grp];
+        acc[0] = __fmaf_rn(undigit(c[0][0], c[1][0], c[2][0]), slo * sg0, acc[0]);
+        acc[1] = __fmaf_rn(undigit(c[0][1], c[1][1], c[2][1]), slo * sg1, acc[1]);
+        acc[2] = __fmaf_rn(undigit(c[0][2], c[1][2], c[2][2]), shi * sg0, acc[2]);
+        acc[3] = __fmaf_rn(undigit(c[0][3], c[1][3], c[2][3]), shi * sg1, acc[3]);
+    }
+}
+
+// bf16 weights, fp32 activations xf (column n = row n of xf, stride ldx floats) split into
+// three bf16 terms on the fly: k-steps [s0, s1) (16 values each).
+UOCR_DEV void mma_tile_bf16(uint32_t rows_s, uint32_t rowb, int s0, int s1, uint32_t xf_s, int ldx, int lane,
+                            float (&acc)[4]) {
+    const int g = lane >> 2, t = lane & 3;
+    const uint32_t ra = rows_s + (uint32_t)g * rowb + 8u * t, rb = ra + 8u * rowb;
+    const uint32_t xa = xf_s + 4u * ((uint32_t)g * ldx + 4 * t);
+    for (int s = s0; s < s1; ++s) {
+        const uint2 A0 = lds_u64(ra + 32u * s), A1 = lds_u64(rb + 32u * s);
+        const float4 v = lds_f128(xa + 64u * s);
+        uint32_t b0[3], b1[3];
+        bf16_terms(v.x, v.y, b0[0], b0[1], b0[2]);
+        bf16_terms(v.z, v.w, b1[0], b1[1], b1[2]);
+#pragma unroll
+        for (int q = 0; q < 3; ++q) mma_bf16(acc, A0.x, A1.x, A0.y, A1.y, b0[q], b1[q]);
+    }
+}
+
+// ---- register-resident activation fragments ----------------------------------------------
+// A warp that always covers the same k-steps [s0, s0 + n) keeps their activation fragments in
+// registers; an item then only loads its weight fragments (all of them before the first
+// product) and the products run back to back.
+template <int MAXS>
+struct FragS8 {
+    uint2 b[MAXS][3];    // digits d0..d2 of the warp's columns (lane: column g, bytes 8t..8t+7)
+    float sg[MAXS][2];   // digit scale of columns 2t, 2t+1 in the k-step's group
+};
+
+template <int MAXS>
+UOCR_DEV void load_frag_s8(FragS8<MAXS>& f, uint32_t xd_s, const float* sig, int NG, int s0, int n, int lane) {
+    const int t = lane & 3;
+    const uint32_t sig_s = smem_addr(sig);
+#pragma unroll
+    for (int i = 0; i < MAXS; ++i) {
+        if (i < n) {
+            const int s = s0 + i;
+#pragma unroll
+            for (int d = 0; d < 3; ++d) f.b[i][d] = lds_u64(xd_s + 8u * ((s * 3 + d) * 32 + lane));
+            f.sg[i][0] = lds_f32(sig_s + 4u * ((2 * t) * NG + (s >> 2)));
+            f.sg[i][1] = lds_f32(sig_s + 4u * ((2 * t + 1) * NG + (s >> 2)));
         }
     }
 }
 
-template <bool kI8>
-UOCR_DEV void unpack4(const uint32_t* w, float (&f)[4]) {
-    if (kI8) {
-        const uint32_t v = w[0] ^ 0x80808080u;
+// s8 tile product over the warp's k-steps with register-resident digits (see mma_tile_s8).
+template <int MAXS>
+UOCR_DEV void mma_tile_s8_reg(uint32_t rows_s, uint32_t rowb, int row0, uint32_t sc_s, int NG, int s0, int n,
+                              const FragS8<MAXS>& f, int lane, float (&acc)[4]) {
+    const int g = lane >> 2;
+    const uint32_t ra = rows_s + (uint32_t)g * rowb + 8u * (lane & 3), rb = ra + 8u * rowb;
+    const uint32_t sa = sc_s + 4u * ((row0 + g) * NG), sb = sc_s + 4u * ((row0 + g + 8) * NG);
+    // even and odd k-steps accumulate separately: six independent product chains in flight
+    int c[2][3][4] = {};
 #pragma unroll
-        for (int i = 0; i < 4; ++i) f[i] = s8_byte_to_f32(v, i);
-    } else {
-        f[0] = bf16lo(w[0]); f[1] = bf16hi(w[0]); f[2] = bf16lo(w[1]); f[3] = bf16hi(w[1]);
+    for (int i = 0; i < MAXS; ++i) {
+        if (i < n) {
+            const int s = s0 + i;
+            const uint2 A0 = lds_u64_nv(ra + 32u * s), A1 = lds_u64_nv(rb + 32u * s);
+#pragma unroll
+            for (int d = 0; d < 3; ++d) mma_s8(c[i & 1][d], A0.x, A1.x, A0.y, A1.y, f.b[i][d].x, f.b[i][d].y);
+            if (i == n - 1 || ((s + 1) & 3) == 0) {  // the k-step closes a 128-group
+                const float slo = lds_f32_nv(sa + 4u * (s >> 2)), shi = lds_f32_nv(sb + 4u * (s >> 2));
+                int v[3][4];
+#pragma unroll
+                for (int d = 0; d < 3; ++d)
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) v[d][j] = c[0][d][j] + c[1][d][j];
+                acc[0] = __fmaf_rn(undigit(v[0][0], v[1][0], v[2][0]), slo * f.sg[i][0], acc[0]);
+                acc[1] = __fmaf_rn(undigit(v[0][1], v[1][1], v[2][1]), slo * f.sg[i][1], acc[1]);
+                acc[2] = __fmaf_rn(undigit(v[0][2], v[1][2], v[2][2]), shi * f.sg[i][0], acc[2]);
+                acc[3] = __fmaf_rn(undigit(v[0][3], v[1][3], v[2][3]), shi * f.sg[i][1], acc[3]);
+#pragma unroll
+                for (int h = 0; h < 2; ++h)
+#pragma unroll
+                    for (int d = 0; d < 3; ++d) c[h][d][0] = c[h][d][1] = c[h][d][2] = c[h][d][3] = 0;
+            }
+        }
     }
 }
 
-UOCR_DEV float dot4(const float (&w)[4], const float4& x, float acc) {
-    acc = __fmaf_rn(w[0], x.x, acc);
-    acc = __fmaf_rn(w[1], x.y, acc);
-    acc = __fmaf_rn(w[2], x.z, acc);
-    acc = __fmaf_rn(w[3], x.w, acc);
-    return acc;
+template <int MAXS>
+struct FragBf16 {
+    uint2 b[MAXS][3];  // bf16 terms t0..t2 of the warp's column (lane: column g, values 4t..4t+3)
+};
+
+template <int MAXS>
+UOCR_DEV void load_frag_bf16(FragBf16<MAXS>& f, uint32_t xf_s, int ldx, int s0, int n, int lane) {
+    const uint32_t xa = xf_s + 4u * ((uint32_t)(lane >> 2) * ldx + 4 * (lane & 3));
+#pragma unroll
+    for (int i = 0; i < MAXS; ++i) {
+        if (i < n) {
+            const float4 v = lds_f128(xa + 64u * (s0 + i));
+            uint32_t b0[3], b1[3];
+            bf16_terms(v.x, v.y, b0[0], b0[1], b0[2]);
+            bf16_terms(v.z, v.w, b1[0], b1[1], b1[2]);
+#pragma unroll
+            for (int q = 0; q < 3; ++q) f.b[i][q] = make_uint2(b0[q], b1[q]);
+        }
+    }
 }
 
-// Sum each of the N values over the warp (every lane gets every total).
-template <int N>
-UOCR_DEV void warp_sum_n(float (&v)[N]) {
+// bf16 tile product over the warp's k-steps with register-resident terms; one accumulator per
+// term keeps three independent chains in flight.
+template <int MAXS>
+UOCR_DEV void mma_tile_bf16_reg(uint32_t rows_s, uint32_t rowb, int s0, int n, const FragBf16<MAXS>& f, int lane,
+                                float (&acc)[4]) {
+    const uint32_t ra = rows_s + (uint32_t)(lane >> 2) * rowb + 8u * (lane & 3), rb = ra + 8u * rowb;
+    float c[2][3][4] = {};  // (k-step parity, term): six independent chains
 #pragma unroll
-    for (int off = 16; off >= 1; off >>= 1)
+    for (int i = 0; i < MAXS; ++i) {
+        if (i < n) {
+            const uint2 A0 = lds_u64_nv(ra + 32u * (s0 + i)), A1 = lds_u64_nv(rb + 32u * (s0 + i));
 #pragma unroll
-        for (int i = 0; i < N; ++i) v[i] = __fadd_rn(v[i], __shfl_xor_sync(0xffffffffu, v[i], off));
+            for (int q = 0; q < 3; ++q) mma_bf16(c[i & 1][q], A0.x, A1.x, A0.y, A1.y, f.b[i][q].x, f.b[i][q].y);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < 4; ++j) acc[j] += (c[0][0][j] + c[1][0][j]) + (c[0][1][j] + c[1][1][j]) + (c[0][2][j] + c[1][2][j]);
 }
 
+// Activations of up to 8 columns (rows of xf, stride ldx; rows >= valid read as zero) as int8
+// digits in fragment order: one warp per (column, 128-group), a lane per 4 values.
+UOCR_DEV void stage_digits(const float* xf, int ldx, int K, int valid, uint32_t* xd, float* sig, int warp, int lane,
+                           int nwarps) {
+    const int NG = K / 128;
+    for (int u = warp; u < kMaxB * NG; u += nwarps) {
+        const int col = u / NG, grp = u % NG;
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (col < valid) v = *reinterpret_cast<const float4*>(xf + (size_t)col * ldx + grp * 128 + 4 * lane);
+        float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+        float sg, inv;
+        digit_scale(m, sg, inv);
+        if (lane == 0) sig[col * NG + grp] = sg;
+        int d[4][3];
+        to_digits(v.x, inv, d[0][0], d[0][1], d[0][2]);
+        to_digits(v.y, inv, d[1][0], d[1][1], d[1][2]);
+        to_digits(v.z, inv, d[2][0], d[2][1], d[2][2]);
+        to_digits(v.w, inv, d[3][0], d[3][1], d[3][2]);
+        // values k = 128 grp + 4 lane .. + 3: k-step 4 grp + lane / 8, bytes 4 (lane % 8) of it,
+        // i.e. fragment lane 4 col + (lane % 8) / 2, half lane % 2
+        const int s = grp * 4 + (lane >> 3), fl = 4 * col + ((lane & 7) >> 1), half = lane & 1;
+#pragma unroll
+        for (int q = 0; q < 3; ++q)
+            xd[((s * 3 + q) * 32 + fl) * 2 + half] = pack_s8x4(d[0][q], d[1][q], d[2][q], d[3][q]);
+    }
+}
 
 // ======================================================================================
 // routing inside a CTA (the 8 consumer warps of K2)
@@ -165,7 +305,8 @@ struct RouteSmem {
 // and lane + 32). `part` is >= 8 * kMaxB * 64 floats of scratch. Then the slot table: routed
 // slot u is the u-th used expert; its rows start after the shared experts' S * B rows.
 // CTA 0 also writes ids / wts and the global RouteTable (read by K3).
-UOCR_DEV void cta_route(const DecodeArgs& a, const float* xs, float* part, RouteSmem* rs, SlotTable* tb, int tid) {
+UOCR_DEV void cta_route(const DecodeArgs& a, const float* xs, int ldx, float* part, RouteSmem* rs, SlotTable* tb,
+                       int tid) {
     const int warp = tid >> 5, lane = tid & 31;
     const int H = a.H, L = H / 8, B = a.B, E = a.E, k = a.topk;
     {
@@ -184,7 +325,7 @@ UOCR_DEV void cta_route(const DecodeArgs& a, const float* xs, float* part, Route
 #pragma unroll
             for (int t = 0; t < kMaxB; ++t) {
                 if (t < B) {
-                    const uint32_t xr = xs_s + 4u * (uint32_t)(t * H + kk);
+                    const uint32_t xr = xs_s + 4u * (uint32_t)(t * ldx + kk);
                     const float4 xa = lds_f128(xr), xb = lds_f128(xr + 16);
                     const float x8[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
                     float u0 = acc[0][t], u1 = acc[1][t];
@@ -276,8 +417,10 @@ UOCR_DEV void cta_route(const DecodeArgs& a, const float* xs, float* part, Route
         int base = a.S * B;
         for (int e = 0; e < tid; ++e) base += rs->cnt[e];
         int n = 0;
+        for (int t = 0; t < kMaxB; ++t) tb->pos[row][t] = -1;
         for (int q = 0; q < kB; ++q) {
             if (rs->ids[q] == tid) {
+                tb->pos[row][q / k] = (signed char)n;
                 tb->token[row][n] = q / k;
                 tb->weight[row][n] = rs->wts[q];
                 rs->rowof[q] = base + n;
@@ -351,166 +494,106 @@ UOCR_DEV void slot_range(long long pre, long long c, int n, const Partition& p, 
 // ======================================================================================
 // Items: (slot, block) with I / P blocks per slot, P = 16 row pairs for int8 stacks and 8 for
 // bf16 (one packed block, layout.h). Shared slots first (streamed while the CTA routes), then
-// routed slots.
+// routed slots. In an item all 8 consumer warps split the block's K range: int8 blocks are two
+// 16-row tiles (gate, up) x 4 K quarters, bf16 blocks one tile [8 gate | 8 up rows] x 8 K
+// eighths; the partial sums meet in shared memory and the SwiGLU is applied per (pair, token).
 UOCR_DEV int gu_pairs(const DecodeArgs& a, int slot) { return (slot >= a.S && a.int8) ? 16 : 8; }
-// relative cost of one item: weight bytes plus per-token work
-UOCR_DEV long long gu_cost(const SlotTable& tb, int slot) { return 6 + tb.count[slot]; }
+// relative cost of one item (its bytes dominate; tokens ride along in the tensor-core product)
+UOCR_DEV long long gu_cost(const DecodeArgs& a, const SlotTable&, int) { return 1; }
 
-// One warp's share of an item for tokens [q0, q0 + NQ) of the slot: row pairs
-// [warp * PW, warp * PW + PW). Lane l owns the chunks k = 4(l + 32j), j < NJ = H/128 (for int8,
-// chunk j lies in scale group j); the tokens' chunks stay in registers while the rows stream.
-template <bool kI8, int NJ, int NQ>
-UOCR_DEV void gu_rows_t(const DecodeArgs& a, const SlotTable& tb, uint32_t xs_s, int slot, int blk, int q0,
-                        uint32_t stage_s, int lane, int warp) {
-    constexpr int P = kI8 ? 16 : 8;
-    constexpr int PW = P / kCW;
-    constexpr int H = NJ * 128;
-    constexpr uint32_t rowb = kI8 ? H : 2 * H;
-    const uint32_t gsc_s = stage_s + 2u * P * rowb;  // int8 gate scales [P][NJ], then up scales
-    const uint32_t usc_s = gsc_s + 4u * P * NJ;
-    const int base = tb.base[slot];
-    float4 xr[NQ][NJ];
-#pragma unroll
-    for (int q = 0; q < NQ; ++q) {
-        const int t = tb.token[slot][q0 + q];
-#pragma unroll
-        for (int j = 0; j < NJ; ++j) xr[q][j] = lds_f128(xs_s + 4u * ((uint32_t)t * H + 4 * (lane + 32 * j)));
-    }
-#pragma unroll 1
-    for (int pp = 0; pp < PW; ++pp) {
-        const int p = warp * PW + pp;
-        uint32_t wg[NJ][kI8 ? 1 : 2], wu[NJ][kI8 ? 1 : 2];
-        lds_row<kI8, NJ>(stage_s + (uint32_t)p * rowb, lane, wg);
-        lds_row<kI8, NJ>(stage_s + (uint32_t)(P + p) * rowb, lane, wu);
-        float acc[2 * NQ][2];
-#pragma unroll
-        for (int i = 0; i < 2 * NQ; ++i) acc[i][0] = acc[i][1] = 0.0f;
-#pragma unroll
-        for (int j = 0; j < NJ; ++j) {
-            float fg[4], fu[4];
-            unpack4<kI8>(wg[j], fg);
-            unpack4<kI8>(wu[j], fu);
-            if (kI8) {
-                const float sg = lds_f32(gsc_s + 4u * (p * NJ + j));
-                const float su = lds_f32(usc_s + 4u * (p * NJ + j));
-#pragma unroll
-                for (int q = 0; q < NQ; ++q) {
-                    acc[2 * q][j & 1] = __fmaf_rn(sg, dot4(fg, xr[q][j], 0.0f), acc[2 * q][j & 1]);
-                    acc[2 * q + 1][j & 1] = __fmaf_rn(su, dot4(fu, xr[q][j], 0.0f), acc[2 * q + 1][j & 1]);
-                }
-            } else {
-#pragma unroll
-                for (int q = 0; q < NQ; ++q) {
-                    acc[2 * q][j & 1] = dot4(fg, xr[q][j], acc[2 * q][j & 1]);
-                    acc[2 * q + 1][j & 1] = dot4(fu, xr[q][j], acc[2 * q + 1][j & 1]);
-                }
-            }
-        }
-        float v[2 * NQ];
-#pragma unroll
-        for (int i = 0; i < 2 * NQ; ++i) v[i] = __fadd_rn(acc[i][0], acc[i][1]);
-        warp_sum_n<2 * NQ>(v);
-        if (lane < NQ) {
-            float g = v[0], u = v[1];
-#pragma unroll
-            for (int q = 1; q < NQ; ++q)
-                if (lane == q) { g = v[2 * q]; u = v[2 * q + 1]; }
-            a.h[(size_t)(base + q0 + lane) * a.I + blk * P + p] = silu(g) * u;
-        }
-    }
-}
+// Partial tiles of items n, n-1, n-2: item n's finish runs after item n+1's products, and a
+// warp releases item n's buffer only after that finish.
+constexpr int kRedBufs = 3;
+struct GuSmem {
+    float red[kRedBufs][kCW][16][8];
+};
 
-template <bool kI8, int NJ>
-UOCR_DEV void gu_item_t(const DecodeArgs& a, const SlotTable& tb, uint32_t xs_s, int slot, int blk, uint32_t stage_s,
-                        int lane, int warp) {
-    const int cnt = tb.count[slot];
-    int q0 = 0;
-    for (; q0 + 2 <= cnt; q0 += 2) gu_rows_t<kI8, NJ, 2>(a, tb, xs_s, slot, blk, q0, stage_s, lane, warp);
-    if (q0 < cnt) gu_rows_t<kI8, NJ, 1>(a, tb, xs_s, slot, blk, q0, stage_s, lane, warp);
-}
+// Activation fragments a K2 warp keeps in registers: its k-steps of x are fixed for the CTA.
+// Layers up to H = 128 * kK2RegSteps use them; larger ones read the fragments from shared memory.
+constexpr int kK2RegSteps = 10;
 
-// Any H multiple of 128 (activations re-read from shared memory per chunk).
-template <bool kI8>
-UOCR_DEV void gu_item_any(const DecodeArgs& a, const SlotTable& tb, const float* xs, int slot, int blk,
-                          const unsigned char* stage, int lane, int warp) {
-    const int P = kI8 ? 16 : 8, PW = P / kCW, H = a.H, NJ = H / 128;
-    const size_t rowb = kI8 ? H : 2 * (size_t)H;
-    const float* gsc = reinterpret_cast<const float*>(stage + 2 * P * rowb);
-    const float* usc = gsc + P * NJ;
-    const int cnt = tb.count[slot], base = tb.base[slot];
-    for (int q = 0; q < cnt; ++q) {
-        const float* xt = xs + (size_t)tb.token[slot][q] * H;
-        for (int pp = 0; pp < PW; ++pp) {
-            const int p = warp * PW + pp;
-            const unsigned char* gr = stage + p * rowb;
-            const unsigned char* ur = stage + (P + p) * rowb;
-            float g = 0.0f, u = 0.0f;
-            for (int j = 0; j < NJ; ++j) {
-                const int k = 4 * (lane + 32 * j);
-                const float4 xv = *reinterpret_cast<const float4*>(xt + k);
-                uint32_t wg[2], wu[2];
-                if (kI8) {
-                    wg[0] = *reinterpret_cast<const uint32_t*>(gr + k);
-                    wu[0] = *reinterpret_cast<const uint32_t*>(ur + k);
-                } else {
-                    const uint2 g2 = *reinterpret_cast<const uint2*>(gr + 2 * k);
-                    const uint2 u2 = *reinterpret_cast<const uint2*>(ur + 2 * k);
-                    wg[0] = g2.x; wg[1] = g2.y; wu[0] = u2.x; wu[1] = u2.y;
-                }
-                float fg[4], fu[4];
-                unpack4<kI8>(wg, fg);
-                unpack4<kI8>(wu, fu);
-                if (kI8) {
-                    g = __fmaf_rn(gsc[p * NJ + j], dot4(fg, xv, 0.0f), g);
-                    u = __fmaf_rn(usc[p * NJ + j], dot4(fu, xv, 0.0f), u);
-                } else {
-                    g = dot4(fg, xv, g);
-                    u = dot4(fu, xv, u);
-                }
-            }
-            float v[2] = {g, u};
-            warp_sum_n<2>(v);
-            if (lane == 0) a.h[(size_t)(base + q) * a.I + blk * P + p] = silu(v[0]) * v[1];
-        }
-    }
-}
-
-UOCR_DEV void gu_item(const DecodeArgs& a, const SlotTable& tb, const float* xs, int slot, int blk,
-                      const unsigned char* stage, int lane, int warp) {
-    const bool i8 = slot >= a.S && a.int8;
-    const int NJ = a.H / 128;
-    const uint32_t xs_s = smem_addr(xs), st_s = smem_addr(stage);
+// The warp's partial tile of one item. int8 blocks: tile warp / 4 (gate, up), K quarter
+// warp % 4 (H / 128 k-steps of 32); bf16 blocks: K eighth `warp` (H / 128 k-steps of 16).
+template <bool kI8L>
+UOCR_DEV void gu_partial(const DecodeArgs& a, bool i8, uint32_t stage_s, uint32_t xf_s, int ldx, uint32_t xd_s,
+                         const float* xsig, const FragS8<kK2RegSteps>& f8, const FragBf16<kK2RegSteps>& f16,
+                         bool reg, int lane, int warp, float (&acc)[4]) {
+    acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
+    const int n = a.H / 128;  // k-steps per warp, both kinds
     if (i8) {
-        if (NJ == 10) gu_item_t<true, 10>(a, tb, xs_s, slot, blk, st_s, lane, warp);
-        else if (NJ == 2) gu_item_t<true, 2>(a, tb, xs_s, slot, blk, st_s, lane, warp);
-        else gu_item_any<true>(a, tb, xs, slot, blk, stage, lane, warp);
+        const uint32_t rowb = (uint32_t)packed_row_bytes(a.H, true);
+        const int tile = warp >> 2, s0 = (warp & 3) * n;
+        const uint32_t rows = stage_s + (uint32_t)tile * 16 * rowb, sc = stage_s + 32 * rowb;
+        if (kI8L && reg) mma_tile_s8_reg<kK2RegSteps>(rows, rowb, tile * 16, sc, n, s0, n, f8, lane, acc);
+        else mma_tile_s8(rows, rowb, tile * 16, sc, n, s0, s0 + n, xd_s, xsig, lane, acc);
     } else {
-        if (NJ == 10) gu_item_t<false, 10>(a, tb, xs_s, slot, blk, st_s, lane, warp);
-        else if (NJ == 2) gu_item_t<false, 2>(a, tb, xs_s, slot, blk, st_s, lane, warp);
-        else gu_item_any<false>(a, tb, xs, slot, blk, stage, lane, warp);
+        const uint32_t rowb = (uint32_t)packed_row_bytes(a.H, false);
+        if (!kI8L && reg) mma_tile_bf16_reg<kK2RegSteps>(stage_s, rowb, warp * n, n, f16, lane, acc);
+        else mma_tile_bf16(stage_s, rowb, warp * n, warp * n + n, xf_s, ldx, lane, acc);
     }
 }
 
+UOCR_DEV void store_partial(float (&red)[kCW][16][8], int warp, int lane, const float (&acc)[4]) {
+    const int g = lane >> 2, t = lane & 3;
+    *reinterpret_cast<float2*>(&red[warp][g][2 * t]) = make_float2(acc[0], acc[1]);
+    *reinterpret_cast<float2*>(&red[warp][g + 8][2 * t]) = make_float2(acc[2], acc[3]);
+}
+
+// h[slot row][blk * P + p] = silu(g) * u for the slot's tokens, from the partial tiles.
+UOCR_DEV void gu_finish(const DecodeArgs& a, const SlotTable& tb, bool i8, int slot, int blk,
+                        const float (&red)[kCW][16][8], int tid) {
+    const int p = tid >> 3, n = tid & 7;
+    float g = 0.0f, u = 0.0f;
+    int P;
+    if (i8) {
+        P = 16;
+        if (p >= 16) return;
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            g += red[q][p][n];
+            u += red[4 + q][p][n];
+        }
+    } else {
+        P = 8;
+        if (p >= 8) return;
+#pragma unroll
+        for (int w = 0; w < kCW; ++w) {
+            g += red[w][p][n];
+            u += red[w][8 + p][n];
+        }
+    }
+    const int pos = tb.pos[slot][n];
+    if (pos >= 0) a.h[(size_t)(tb.base[slot] + pos) * a.I + blk * P + p] = silu(g) * u;
+}
+
+template <bool kI8L>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl, uint32_t off_route,
-                      uint32_t off_meta, uint32_t off_xs, uint32_t off_stages) {
+                      uint32_t off_meta, uint32_t off_gu, uint32_t off_xf, uint32_t off_xd, uint32_t off_sig,
+                      uint32_t off_stages) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ int abort_flag;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + nst;
     uint64_t* table_ready = empty + nst;
+    uint64_t* redbar = table_ready + 1;  // [kRedBufs]: all warps' partial tiles of an item are stored
     SlotTable* tb = reinterpret_cast<SlotTable*>(smem + off_tbl);
     RouteSmem* rs = reinterpret_cast<RouteSmem*>(smem + off_route);
     ItemMeta* meta = reinterpret_cast<ItemMeta*>(smem + off_meta);
-    float* xs = reinterpret_cast<float*>(smem + off_xs);
+    GuSmem* gs = reinterpret_cast<GuSmem*>(smem + off_gu);
+    float* xf = reinterpret_cast<float*>(smem + off_xf);
+    uint32_t* xd = reinterpret_cast<uint32_t*>(smem + off_xd);
+    float* xsig = reinterpret_cast<float*>(smem + off_sig);
     unsigned char* stages = smem + off_stages;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const int ldx = a.H + 4;
     if (tid == 0) {
         for (int s = 0; s < nst; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&empty[s], kCW);
         }
         mbar_init(table_ready, 1);
+        for (int b = 0; b < kRedBufs; ++b) mbar_init(&redbar[b], kCW);
         abort_flag = 0;
         fence_mbar_init();
         pdl_launch_dependents();  // K3 launches early; it waits for this grid before it reads h
@@ -561,7 +644,7 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             const int first = phase == 0 ? 0 : a.S;
             const int last = phase == 0 ? a.S : tb->nslot;
             auto items = [&](int s) { return a.I / gu_pairs(a, s); };
-            auto cost = [&](int s) { return gu_cost(*tb, s); };
+            auto cost = [&](int s) { return gu_cost(a, *tb, s); };
             const Partition p = cta_share(first, last, cost, items);
             long long pre = 0;
             for (int s = first; s < last && ok; ++s) {
@@ -585,154 +668,103 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
         }
         __syncwarp();
     } else {
-        // ---------------- consumers: route, then every warp takes its rows of every item ----------------
-        // the tokens (complete once the previous layer's grid is)
+        // ---------------- consumers: route, stage the digits, then the items ----------------
+        // the tokens (complete once the previous layer's grid is); rows B..7 stay zero
         pdl_wait_prior_grid();
-        for (int i = tid; i < a.B * (a.H / 4); i += kCW * 32)
-            reinterpret_cast<float4*>(xs)[i] = __ldcg(reinterpret_cast<const float4*>(a.x) + i);
+        for (int i = tid; i < kMaxB * (a.H / 4); i += kCW * 32) {
+            const int t = i / (a.H / 4), c4 = i % (a.H / 4);
+            const float4 v = t < a.B ? __ldcg(reinterpret_cast<const float4*>(a.x) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
+            *reinterpret_cast<float4*>(xf + (size_t)t * ldx + 4 * c4) = v;
+        }
         named_bar_sync(kBarConsumers, kCW * 32);
-        cta_route(a, xs, reinterpret_cast<float*>(stages + (size_t)(nst - 1) * stage_bytes), rs, tb, tid);
+        cta_route(a, xf, ldx, reinterpret_cast<float*>(stages + (size_t)(nst - 1) * stage_bytes), rs, tb, tid);
         if (tid == 0) mbar_arrive(table_ready);
+        if (a.int8) {
+            stage_digits(xf, ldx, a.H, a.B, xd, xsig, warp, lane, kCW);
+            named_bar_sync(kBarConsumers, kCW * 32);
+        }
+        const uint32_t xf_s = smem_addr(xf), xd_s = smem_addr(xd);
+        // this warp's activation fragments, fixed for the CTA
+        const int nks = a.H / 128;
+        const bool reg = nks <= kK2RegSteps;
+        FragS8<kK2RegSteps> f8;
+        FragBf16<kK2RegSteps> f16;
+        if (kI8L && reg) load_frag_s8<kK2RegSteps>(f8, xd_s, xsig, nks, (warp & 3) * nks, nks, lane);
+        if (!kI8L && reg) load_frag_bf16<kK2RegSteps>(f16, xf_s, ldx, warp * nks, nks, lane);
+        // Item n: products, stage release, partial tile stored; then item n-1 is finished (its
+        // partial tiles are complete once every warp has arrived) and item n's buffer released.
+        int pend_slot = -1, pend_blk = 0, pend_n = 0;
+        bool pend_i8 = false, ok = true;
+        auto finish_pending = [&]() {
+            const int b = pend_n % kRedBufs;
+            ok = mbar_wait_warp(&redbar[b], (pend_n / kRedBufs) & 1, &abort_flag, &a.ctl->status);
+            if (ok) gu_finish(a, *tb, pend_i8, pend_slot, pend_blk, gs->red[b], tid);
+        };
         for (int n = 0;; ++n) {
             const int st = n % nst;
             unsigned long long* tr = warp == 0 ? trace_rec(a, 0, n) : nullptr;
             if (tr && lane == 0) tr[0] = global_timer_ns();
-            if (!mbar_wait_warp(&full[st], (n / nst) & 1, &abort_flag, &a.ctl->status)) break;
+            if (!mbar_wait_warp(&full[st], (n / nst) & 1, &abort_flag, &a.ctl->status)) {
+                ok = false;
+                break;
+            }
             const int slot = meta[st].slot, blk = meta[st].blk;
             if (slot < 0) break;
             if (tr && lane == 0) tr[1] = global_timer_ns();
-            gu_item(a, *tb, xs, slot, blk, stages + (size_t)st * stage_bytes, lane, warp);
+            const bool i8 = slot >= a.S && a.int8;
+            const uint32_t stage_s = launder(smem_addr(stages + (size_t)st * stage_bytes));
+            float acc[4];
+            gu_partial<kI8L>(a, i8, stage_s, xf_s, ldx, xd_s, xsig, f8, f16, reg, lane, warp, acc);
+            fence_regs(acc);
             __syncwarp();
+            if (tr && lane == 0) tr[5] = global_timer_ns();
+            if (lane == 0) mbar_arrive(&empty[st]);  // the stage is free once the warp's products are done
+            store_partial(gs->red[n % kRedBufs], warp, lane, acc);
+            if (pend_slot >= 0) {
+                finish_pending();
+                if (!ok) break;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&redbar[n % kRedBufs]);
             if (tr && lane == 0) {
+                tr[6] = global_timer_ns();
                 tr[2] = global_timer_ns();
                 tr[3] = ((unsigned long long)slot << 32) | (unsigned)blk;
             }
-            if (lane == 0) mbar_arrive(&empty[st]);
+            pend_slot = slot;
+            pend_blk = blk;
+            pend_i8 = i8;
+            pend_n = n;
         }
+        if (ok && pend_slot >= 0) finish_pending();
     }
 }
 
 // ======================================================================================
 // K3: down + combine
 // ======================================================================================
-// Items: (slot, 32-row block) with H / 32 blocks per slot; an item is its weight block (one
-// copy) and the slot's h rows (one copy), placed back to back in a byte ring. Warp w computes
-// rows [4w, 4w + 4) of the block for all the slot's tokens.
-UOCR_DEV long long dn_cost(const DecodeArgs& a, const SlotTable& tb, int slot) {
-    return ((slot >= a.S && a.int8) ? 4 : 8) + tb.count[slot];
+// Items: (slot, 32-row block) with H / 32 blocks per slot, each one bulk copy of its weight
+// block; the first item of each run of a slot in this CTA also carries the slot's h rows. At a
+// run's start the consumers stage those rows (fp32, padded) and, for int8 weights, their digits.
+// All 8 warps split each item: two 16-row tiles x 4 K quarters.
+UOCR_DEV long long dn_cost(const DecodeArgs& a, const SlotTable&, int slot) {
+    return (slot >= a.S && a.int8) ? 1 : 2;  // bf16 blocks are twice the bytes
 }
 
-template <bool kI8, int NJ, int NQ>
-UOCR_DEV void dn_rows_t(const DecodeArgs& a, const SlotTable& tb, int slot, int blk, int q0, uint32_t item_s,
-                        uint32_t hoff, int lane, int warp) {
-    constexpr int I = NJ * 128;
-    constexpr uint32_t rowb = kI8 ? I : 2 * I;
-    constexpr int RW = kW2Rows / kCW;  // rows per warp
-    const uint32_t sc_s = item_s + (uint32_t)kW2Rows * rowb;  // int8 scales [32][NJ]
-    const uint32_t h_s = item_s + hoff;
-    const int base = tb.base[slot];
-    float4 hr[NQ][NJ];
-#pragma unroll
-    for (int q = 0; q < NQ; ++q) {
-        const uint32_t hrow = h_s + 4u * (uint32_t)(q0 + q) * I;
-#pragma unroll
-        for (int j = 0; j < NJ; ++j) hr[q][j] = lds_f128(hrow + 16u * (lane + 32 * j));
-    }
-    float v[RW * NQ];
-#pragma unroll
-    for (int rr = 0; rr < RW; ++rr) {
-        const int r = warp * RW + rr;
-        uint32_t w[NJ][kI8 ? 1 : 2];
-        lds_row<kI8, NJ>(item_s + (uint32_t)r * rowb, lane, w);
-        float acc[NQ][2];
-#pragma unroll
-        for (int q = 0; q < NQ; ++q) acc[q][0] = acc[q][1] = 0.0f;
-#pragma unroll
-        for (int j = 0; j < NJ; ++j) {
-            float f[4];
-            unpack4<kI8>(w[j], f);
-            if (kI8) {
-                const float s = lds_f32(sc_s + 4u * (r * NJ + j));
-#pragma unroll
-                for (int q = 0; q < NQ; ++q) acc[q][j & 1] = __fmaf_rn(s, dot4(f, hr[q][j], 0.0f), acc[q][j & 1]);
-            } else {
-#pragma unroll
-                for (int q = 0; q < NQ; ++q) acc[q][j & 1] = dot4(f, hr[q][j], acc[q][j & 1]);
-            }
-        }
-#pragma unroll
-        for (int q = 0; q < NQ; ++q) v[rr * NQ + q] = __fadd_rn(acc[q][0], acc[q][1]);
-    }
-    warp_sum_n<RW * NQ>(v);
-    // lane (rr * NQ + q) stores row rr of token q
-    if (lane < RW * NQ) {
-        float y = v[0];
-#pragma unroll
-        for (int i = 1; i < RW * NQ; ++i)
-            if (lane == i) y = v[i];
-        const int rr = lane / NQ, q = lane % NQ;
-        a.y[(size_t)(base + q0 + q) * a.H + blk * kW2Rows + warp * RW + rr] = y;
-    }
-}
+struct DnSmem {
+    float red[kRedBufs][kCW][16][8];
+};
 
-template <bool kI8, int NJ>
-UOCR_DEV void dn_item_t(const DecodeArgs& a, const SlotTable& tb, int slot, int blk, uint32_t item_s, uint32_t hoff,
-                        int lane, int warp) {
-    const int cnt = tb.count[slot];
-    int q0 = 0;
-    for (; q0 + 2 <= cnt; q0 += 2) dn_rows_t<kI8, NJ, 2>(a, tb, slot, blk, q0, item_s, hoff, lane, warp);
-    if (q0 < cnt) dn_rows_t<kI8, NJ, 1>(a, tb, slot, blk, q0, item_s, hoff, lane, warp);
-}
-
-// Any I multiple of 128 (h re-read from shared memory per chunk).
-template <bool kI8>
-UOCR_DEV void dn_item_any(const DecodeArgs& a, const SlotTable& tb, int slot, int blk, const unsigned char* item,
-                          uint32_t hoff, int lane, int warp) {
-    const int I = a.I, NJ = I / 128, RW = kW2Rows / kCW;
-    const size_t rowb = kI8 ? I : 2 * (size_t)I;
-    const float* sc = reinterpret_cast<const float*>(item + kW2Rows * rowb);
-    const float* hs = reinterpret_cast<const float*>(item + hoff);
-    const int cnt = tb.count[slot], base = tb.base[slot];
-    for (int q = 0; q < cnt; ++q) {
-        for (int rr = 0; rr < RW; ++rr) {
-            const int r = warp * RW + rr;
-            const unsigned char* wr = item + r * rowb;
-            float acc = 0.0f;
-            for (int j = 0; j < NJ; ++j) {
-                const int k = 4 * (lane + 32 * j);
-                const float4 hv = *reinterpret_cast<const float4*>(hs + (size_t)q * I + k);
-                uint32_t w[2];
-                if (kI8) {
-                    w[0] = *reinterpret_cast<const uint32_t*>(wr + k);
-                } else {
-                    const uint2 w2 = *reinterpret_cast<const uint2*>(wr + 2 * k);
-                    w[0] = w2.x; w[1] = w2.y;
-                }
-                float f[4];
-                unpack4<kI8>(w, f);
-                acc = kI8 ? __fmaf_rn(sc[r * NJ + j], dot4(f, hv, 0.0f), acc) : dot4(f, hv, acc);
-            }
-            float v[1] = {acc};
-            warp_sum_n<1>(v);
-            if (lane == 0) a.y[(size_t)(base + q) * a.H + blk * kW2Rows + r] = v[0];
-        }
-    }
-}
-
-UOCR_DEV void dn_item(const DecodeArgs& a, const SlotTable& tb, int slot, int blk, const unsigned char* item,
-                      uint32_t hoff, int lane, int warp) {
-    const bool i8 = slot >= a.S && a.int8;
-    const int NJ = a.I / 128;
-    const uint32_t it_s = smem_addr(item);
-    if (i8) {
-        if (NJ == 7) dn_item_t<true, 7>(a, tb, slot, blk, it_s, hoff, lane, warp);
-        else if (NJ == 1) dn_item_t<true, 1>(a, tb, slot, blk, it_s, hoff, lane, warp);
-        else dn_item_any<true>(a, tb, slot, blk, item, hoff, lane, warp);
-    } else {
-        if (NJ == 7) dn_item_t<false, 7>(a, tb, slot, blk, it_s, hoff, lane, warp);
-        else if (NJ == 1) dn_item_t<false, 1>(a, tb, slot, blk, it_s, hoff, lane, warp);
-        else dn_item_any<false>(a, tb, slot, blk, item, hoff, lane, warp);
-    }
+// y[slot row][blk * 32 + row] for the slot's tokens, from the partial tiles.
+UOCR_DEV void dn_finish(const DecodeArgs& a, const SlotTable& tb, int slot, int blk, const float (&red)[kCW][16][8],
+                        int tid) {
+    const int row = tid >> 3, n = tid & 7;
+    if (n >= tb.count[slot]) return;
+    const int tile = row >> 4, r16 = row & 15;
+    float y = 0.0f;
+#pragma unroll
+    for (int q = 0; q < 4; ++q) y += red[tile * 4 + q][r16][n];
+    a.y[(size_t)(tb.base[slot] + n) * a.H + blk * kW2Rows + row] = y;
 }
 
 // Rows [r0, r0 + 4) are complete over all slots: lane (t, r) sums token t's shared rows, then its
@@ -749,24 +781,40 @@ UOCR_DEV void combine_rows(const DecodeArgs& a, int r0, int lane) {
     a.out[(size_t)t * a.H + r] = acc;
 }
 
+// K3 warps keep the current run's h fragments in registers for I up to 128 * kK3RegS8 (int8)
+// and 64 * kK3RegBf16 (bf16).
+constexpr int kK3RegS8 = 8, kK3RegBf16 = 14;
+
+template <bool kI8L>
 __global__ void __launch_bounds__(kThreads3, 1)
-decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t off_meta, uint32_t off_ring) {
+decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t off_meta, uint32_t off_dn,
+                   uint32_t off_hf, uint32_t off_hd, uint32_t off_sig, uint32_t off_ring) {
     extern __shared__ __align__(16) unsigned char smem[];
     __shared__ int abort_flag;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* done = full + kK3Desc;
-    uint64_t* empty = done + kK3Desc;
+    uint64_t* done = full + kK3Desc;     // consumers: the item's y rows are written
+    uint64_t* freed = done + kK3Desc;    // consumers: the item's ring bytes are no longer read
+    uint64_t* empty = freed + kK3Desc;   // publisher: the descriptor is no longer read
+    uint64_t* redbar = empty + kK3Desc;     // [kRedBufs]
+    uint64_t* hbar = redbar + kRedBufs;     // [2]: the run's h staged by all warps
     SlotTable* tb = reinterpret_cast<SlotTable*>(smem + off_tbl);
     ItemMeta* meta = reinterpret_cast<ItemMeta*>(smem + off_meta);
+    DnSmem* ds = reinterpret_cast<DnSmem*>(smem + off_dn);
+    float* hf = reinterpret_cast<float*>(smem + off_hf);
+    uint32_t* hd = reinterpret_cast<uint32_t*>(smem + off_hd);
+    float* hsig = reinterpret_cast<float*>(smem + off_sig);
     unsigned char* ring = smem + off_ring;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int nblk = a.H / kW2Rows;
+    const int nblk = a.H / kW2Rows, ldh = a.I + 4;
     if (tid == 0) {
         for (int s = 0; s < kK3Desc; ++s) {
             mbar_init(&full[s], 1);
             mbar_init(&done[s], kCW);
+            mbar_init(&freed[s], kCW);
             mbar_init(&empty[s], 1);
         }
+        for (int s = 0; s < kRedBufs; ++s) mbar_init(&redbar[s], kCW);
+        for (int s = 0; s < 2; ++s) mbar_init(&hbar[s], kCW);
         abort_flag = 0;
         fence_mbar_init();
         pdl_launch_dependents();  // the next layer's kernel waits for this grid itself
@@ -776,11 +824,12 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
 
     if (warp == kCW) {
         // ---------------- producer ----------------
-        // Items are placed back to back in the ring (wrapping to 0 when one does not fit) and
-        // retire in order; an item may be placed once the descriptor it reuses is free and no
-        // in-flight item overlaps its bytes.
+        // Items are placed back to back in the ring (wrapping to 0 when one does not fit). Ring
+        // bytes retire in order as the consumers finish their products (`freed`); descriptors
+        // retire in order as the publisher finishes with them (`empty`). An item may be placed
+        // once its descriptor is free and no item still being read overlaps its bytes.
         uint32_t lo_b[kK3Desc], hi_b[kK3Desc];  // byte range of descriptor d's item
-        int n = 0, oldest = 0;
+        int n = 0, oldest = 0, oldest_desc = 0;
         uint32_t head = 0;
         bool ok = true;
         pdl_wait_prior_grid();  // h and the routing table come from K2
@@ -797,25 +846,35 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
             const bool i8 = slot >= a.S && a.int8;
             const uint32_t wbytes = (uint32_t)w2_block_bytes(a.I, a.G, i8);
             const uint32_t hoff = (wbytes + 15u) & ~15u;
-            const uint32_t hbytes = (uint32_t)tb->count[slot] * a.I * 4;
-            const uint32_t need = hoff + hbytes;
             for (int blk = j0; blk < j1 && ok; ++blk) {
+                const uint32_t hbytes = blk == j0 ? (uint32_t)tb->count[slot] * a.I * 4 : 0u;  // run start
+                const uint32_t need = hoff + hbytes;
                 if (head + need > ring_bytes) head = 0;
-                // retire items until this one's descriptor is free and its bytes do not overlap
+                // retire ring bytes until this item's do not overlap any still being read
                 while (oldest < n) {
-                    bool clash = n - oldest >= kK3Desc;
+                    bool clash = false;
                     for (int m = oldest; m < n && !clash; ++m) {
                         const int d = m % kK3Desc;
                         clash = head < hi_b[d] && lo_b[d] < head + need;
                     }
                     if (!clash) break;
-                    if (!mbar_wait_warp(&empty[oldest % kK3Desc], (oldest / kK3Desc) & 1, &abort_flag,
+                    if (!mbar_wait_warp(&freed[oldest % kK3Desc], (oldest / kK3Desc) & 1, &abort_flag,
                                         &a.ctl->status)) {
                         ok = false;
                         break;
                     }
                     ++oldest;
                 }
+                // and the descriptor: item n reuses item n - kK3Desc's
+                while (ok && n - oldest_desc >= kK3Desc) {
+                    if (!mbar_wait_warp(&empty[oldest_desc % kK3Desc], (oldest_desc / kK3Desc) & 1, &abort_flag,
+                                        &a.ctl->status))
+                        ok = false;
+                    ++oldest_desc;
+                }
+                // a retired descriptor's bytes were freed before it: never wait on that `freed`
+                // phase again (its barrier may complete again for a later item)
+                oldest = max(oldest, oldest_desc);
                 if (!ok) break;
                 const int d = n % kK3Desc;
                 lo_b[d] = head;
@@ -830,10 +889,10 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
                     meta[d].slot = slot;
                     meta[d].blk = blk;
                     meta[d].off = head;
-                    meta[d].hoff = hoff;
+                    meta[d].hoff = hbytes ? hoff : 0u;  // 0: no h with this item
                     mbar_arrive_expect_tx(&full[d], wbytes + hbytes);
                     bulk_g2s(ring + head, wsrc, wbytes, &full[d]);
-                    bulk_g2s(ring + head + hoff, a.h + (size_t)tb->base[slot] * a.I, hbytes, &full[d]);
+                    if (hbytes) bulk_g2s(ring + head + hoff, a.h + (size_t)tb->base[slot] * a.I, hbytes, &full[d]);
                     unsigned long long* tr = trace_rec(a, 1, n);
                     if (tr) tr[4] = global_timer_ns();
                 }
@@ -886,23 +945,112 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
         }
     } else {
         // ---------------- consumers ----------------
+        const uint32_t hf_s = smem_addr(hf), hd_s = smem_addr(hd);
+        int runs = 0;
+        const int tile = warp >> 2, q = warp & 3;
+        const int n8 = a.I / 128, n16 = a.I / 64;  // k-steps per warp (s8 32-wide, bf16 16-wide)
+        const bool reg8 = n8 <= kK3RegS8, reg16 = n16 <= kK3RegBf16;
+        FragS8<kK3RegS8> f8;
+        FragBf16<kK3RegBf16> f16;
+        // As in K2: item n's products, then item n-1 is finished (y rows written, `done`
+        // arrived for the publisher), then item n's partial tile buffer is released.
+        int pend_slot = -1, pend_blk = 0, pend_n = 0, pend_d = 0;
+        bool ok = true;
+        auto finish_pending = [&]() {
+            const int b = pend_n % kRedBufs;
+            ok = mbar_wait_warp(&redbar[b], (pend_n / kRedBufs) & 1, &abort_flag, &a.ctl->status);
+            if (!ok) return;
+            dn_finish(a, *tb, pend_slot, pend_blk, ds->red[b], tid);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&done[pend_d]);
+        };
         for (int n = 0;; ++n) {
             const int d = n % kK3Desc;
             unsigned long long* tr = warp == 0 ? trace_rec(a, 1, n) : nullptr;
             if (tr && lane == 0) tr[0] = global_timer_ns();
-            if (!mbar_wait_warp(&full[d], (n / kK3Desc) & 1, &abort_flag, &a.ctl->status)) break;
+            if (!mbar_wait_warp(&full[d], (n / kK3Desc) & 1, &abort_flag, &a.ctl->status)) {
+                ok = false;
+                break;
+            }
             const int slot = meta[d].slot, blk = meta[d].blk;
-            if (slot >= 0) {
-                if (tr && lane == 0) tr[1] = global_timer_ns();
-                dn_item(a, *tb, slot, blk, ring + meta[d].off, meta[d].hoff, lane, warp);
+            if (slot < 0) {
+                if (pend_slot >= 0) finish_pending();
+                if (ok && lane == 0) mbar_arrive(&done[d]);
+                pend_slot = -1;
+                break;
+            }
+            if (tr && lane == 0) tr[1] = global_timer_ns();
+            const bool i8 = slot >= a.S && a.int8;
+            const uint32_t item_s = launder(smem_addr(ring + meta[d].off));
+            if (meta[d].hoff) {
+                // a run of this slot starts: every warp's products of the previous item must be
+                // done before the caches change (their partial tiles are all stored)
+                if (pend_slot >= 0 && !mbar_wait_warp(&redbar[pend_n % kRedBufs], (pend_n / kRedBufs) & 1,
+                                                      &abort_flag, &a.ctl->status)) {
+                    ok = false;
+                    break;
+                }
+                // stage its h rows (fp32, padded; rows >= count zero) and, for int8 weights, their digits
+                const float* hsrc = reinterpret_cast<const float*>(ring + meta[d].off + meta[d].hoff);
+                const int cnt = tb->count[slot];
+                for (int i = tid; i < kMaxB * (a.I / 4); i += kCW * 32) {
+                    const int qq = i / (a.I / 4), c4 = i % (a.I / 4);
+                    const float4 v = qq < cnt ? *reinterpret_cast<const float4*>(hsrc + (size_t)qq * a.I + 4 * c4)
+                                              : make_float4(0.f, 0.f, 0.f, 0.f);
+                    *reinterpret_cast<float4*>(hf + (size_t)qq * ldh + 4 * c4) = v;
+                }
                 __syncwarp();
-                if (tr && lane == 0) {
-                    tr[2] = global_timer_ns();
-                    tr[3] = ((unsigned long long)slot << 32) | (unsigned)blk;
+                if (lane == 0) mbar_arrive(&hbar[runs & 1]);
+                if (!mbar_wait_warp(&hbar[runs & 1], (runs >> 1) & 1, &abort_flag, &a.ctl->status)) {
+                    ok = false;
+                    break;
+                }
+                ++runs;
+                if (i8) {
+                    stage_digits(hf, ldh, a.I, cnt, hd, hsig, warp, lane, kCW);
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&hbar[runs & 1]);
+                    if (!mbar_wait_warp(&hbar[runs & 1], (runs >> 1) & 1, &abort_flag, &a.ctl->status)) {
+                        ok = false;
+                        break;
+                    }
+                    ++runs;
+                    if (kI8L && reg8) load_frag_s8<kK3RegS8>(f8, hd_s, hsig, a.I / 128, q * n8, n8, lane);
+                } else if (!kI8L && reg16) {
+                    load_frag_bf16<kK3RegBf16>(f16, hf_s, ldh, q * n16, n16, lane);
                 }
             }
-            if (lane == 0) mbar_arrive(&done[d]);
-            if (slot < 0) break;
+            float acc[4] = {0.f, 0.f, 0.f, 0.f};
+            if (i8) {
+                const uint32_t rowb = (uint32_t)packed_row_bytes(a.I, true);
+                const int NG = a.I / 128;
+                const uint32_t rows = item_s + (uint32_t)tile * 16 * rowb, sc = item_s + kW2Rows * rowb;
+                if (kI8L && reg8) mma_tile_s8_reg<kK3RegS8>(rows, rowb, tile * 16, sc, NG, q * n8, n8, f8, lane, acc);
+                else mma_tile_s8(rows, rowb, tile * 16, sc, NG, q * n8, q * n8 + n8, hd_s, hsig, lane, acc);
+            } else {
+                const uint32_t rowb = (uint32_t)packed_row_bytes(a.I, false);
+                const uint32_t rows = item_s + (uint32_t)tile * 16 * rowb;
+                if (!kI8L && reg16) mma_tile_bf16_reg<kK3RegBf16>(rows, rowb, q * n16, n16, f16, lane, acc);
+                else mma_tile_bf16(rows, rowb, q * n16, q * n16 + n16, hf_s, ldh, lane, acc);
+            }
+            fence_regs(acc);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&freed[d]);  // the item's ring bytes are no longer read
+            store_partial(ds->red[n % kRedBufs], warp, lane, acc);
+            if (pend_slot >= 0) {
+                finish_pending();
+                if (!ok) break;
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&redbar[n % kRedBufs]);
+            if (tr && lane == 0) {
+                tr[2] = global_timer_ns();
+                tr[3] = ((unsigned long long)slot << 32) | (unsigned)blk;
+            }
+            pend_slot = slot;
+            pend_blk = blk;
+            pend_n = n;
+            pend_d = d;
         }
     }
 }
@@ -948,36 +1096,49 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
         const size_t off_tbl = 256;
         const size_t off_route = off_tbl + up(sizeof(SlotTable), 128);
         const size_t off_meta = off_route + up(sizeof(RouteSmem), 128);
-        const size_t off_xs = off_meta + up(sizeof(ItemMeta) * 8, 128);
-        const size_t off_stages = up(off_xs + sizeof(float) * a.B * a.H, 128);
+        const size_t off_gu = off_meta + up(sizeof(ItemMeta) * 8, 128);
+        const size_t off_xf = off_gu + up(sizeof(GuSmem), 128);
+        const size_t off_xd = off_xf + up(sizeof(float) * kMaxB * (a.H + 4), 128);
+        const size_t xd_bytes = a.int8 ? (size_t)(a.H / 32) * 3 * 32 * 8 : 0;
+        const size_t off_sig = off_xd + up(xd_bytes, 128);
+        const size_t off_stages = up(off_sig + sizeof(float) * kMaxB * (a.H / 128), 128);
         if ((size_t)max_smem < off_stages + 2 * (size_t)stage_bytes) return cudaErrorInvalidConfiguration;
         int nst = (int)std::min<size_t>(8, ((size_t)max_smem - off_stages) / stage_bytes);
         const size_t smem = off_stages + (size_t)nst * stage_bytes;
-        err = ensure_smem_optin(reinterpret_cast<const void*>(decode_gate_up_kernel), smem);
+        const void* k2 = a.int8 ? reinterpret_cast<const void*>(decode_gate_up_kernel<true>)
+                                : reinterpret_cast<const void*>(decode_gate_up_kernel<false>);
+        err = ensure_smem_optin(k2, smem);
         if (err != cudaSuccess) return err;
-        uint32_t ot = (uint32_t)off_tbl, orr = (uint32_t)off_route, om = (uint32_t)off_meta, ox = (uint32_t)off_xs,
-                 os = (uint32_t)off_stages;
-        void* args[] = {&a, &nst, &stage_bytes, &ot, &orr, &om, &ox, &os};
-        err = launch_pdl(reinterpret_cast<const void*>(decode_gate_up_kernel), dim3(sms), dim3(kThreads), smem, st,
-                         args);
+        uint32_t o[8] = {(uint32_t)off_tbl, (uint32_t)off_route, (uint32_t)off_meta, (uint32_t)off_gu,
+                         (uint32_t)off_xf,  (uint32_t)off_xd,    (uint32_t)off_sig,  (uint32_t)off_stages};
+        void* args[] = {&a, &nst, &stage_bytes, &o[0], &o[1], &o[2], &o[3], &o[4], &o[5], &o[6], &o[7]};
+        err = launch_pdl(k2, dim3(sms), dim3(kThreads), smem, st, args);
         if (err != cudaSuccess) return err;
     }
     // ---- K3: the rest of shared memory is the item ring
     {
-        const size_t off_tbl = 256;
+        const size_t off_tbl = 512;  // 4 x kK3Desc + kRedBufs + 2 mbarriers before it
         const size_t off_meta = off_tbl + up(sizeof(SlotTable), 128);
-        const size_t off_ring = off_meta + up(sizeof(ItemMeta) * kK3Desc, 128);
+        const size_t off_dn = off_meta + up(sizeof(ItemMeta) * kK3Desc, 128);
+        const size_t off_hf = off_dn + up(sizeof(DnSmem), 128);
+        const size_t off_hd = off_hf + up(sizeof(float) * kMaxB * (a.I + 4), 128);
+        const size_t hd_bytes = a.int8 ? (size_t)(a.I / 32) * 3 * 32 * 8 : 0;
+        const size_t off_sig = off_hd + up(hd_bytes, 128);
+        const size_t off_ring = up(off_sig + sizeof(float) * kMaxB * (a.I / 128), 128);
         const size_t max_item =
             up(std::max(w2_block_bytes(a.I, a.G, false), a.int8 ? w2_block_bytes(a.I, a.G, true) : size_t(0)), 16) +
             (size_t)kMaxB * a.I * 4;
-        if ((size_t)max_smem < off_ring + 2 * max_item) return cudaErrorInvalidConfiguration;
+        if ((size_t)max_smem < off_ring + max_item) return cudaErrorInvalidConfiguration;
         uint32_t ring_bytes = (uint32_t)(((size_t)max_smem - off_ring) & ~size_t(127));
         const size_t smem = off_ring + ring_bytes;
-        err = ensure_smem_optin(reinterpret_cast<const void*>(decode_down_kernel), smem);
+        const void* k3 = a.int8 ? reinterpret_cast<const void*>(decode_down_kernel<true>)
+                                : reinterpret_cast<const void*>(decode_down_kernel<false>);
+        err = ensure_smem_optin(k3, smem);
         if (err != cudaSuccess) return err;
-        uint32_t ot = (uint32_t)off_tbl, om = (uint32_t)off_meta, orr = (uint32_t)off_ring;
-        void* args[] = {&a, &ring_bytes, &ot, &om, &orr};
-        err = launch_pdl(reinterpret_cast<const void*>(decode_down_kernel), dim3(sms), dim3(kThreads3), smem, st, args);
+        uint32_t o[7] = {(uint32_t)off_tbl, (uint32_t)off_meta, (uint32_t)off_dn, (uint32_t)off_hf,
+                         (uint32_t)off_hd,  (uint32_t)off_sig,  (uint32_t)off_ring};
+        void* args[] = {&a, &ring_bytes, &o[0], &o[1], &o[2], &o[3], &o[4], &o[5], &o[6]};
+        err = launch_pdl(k3, dim3(sms), dim3(kThreads3), smem, st, args);
         if (err != cudaSuccess) return err;
     }
     return cudaGetLastError();

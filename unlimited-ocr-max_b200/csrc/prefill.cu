@@ -166,8 +166,9 @@ __global__ void __launch_bounds__(256) prefill_dequant_w13_kernel(const unsigned
     const long r = (pr >> 4) * 8 + (pr & 7);  // gate/up row within the expert
     const long b16 = r >> 4, j = r & 15;      // int8 block of 16 row pairs, row within it
     const unsigned char* blk = w + (size_t)(e * (I / 16) + b16) * blk_bytes;
-    const unsigned char* src = blk + (size_t)(is_up ? 16 + j : j) * H + k;
-    const float* sc = reinterpret_cast<const float*>(blk + 32 * (size_t)H) + (is_up ? 16 : 0) * (H / G) + j * (H / G);
+    const size_t rowb = packed_row_bytes(H, true);
+    const unsigned char* src = blk + (size_t)(is_up ? 16 + j : j) * rowb + k;
+    const float* sc = reinterpret_cast<const float*>(blk + 32 * rowb) + (is_up ? 16 : 0) * (H / G) + j * (H / G);
     const uint2 v = *reinterpret_cast<const uint2*>(src);
     float f[8];
     unpack_s8x8(v.x, v.y, f);
@@ -186,8 +187,9 @@ __global__ void __launch_bounds__(256) prefill_dequant_w2_kernel(const unsigned 
     const int k = (int)(i - row * I);
     const unsigned char* blk = w + (size_t)(row / kW2Rows) * blk_bytes;
     const int j = (int)(row % kW2Rows);
-    const uint2 v = *reinterpret_cast<const uint2*>(blk + (size_t)j * I + k);
-    const float* sc = reinterpret_cast<const float*>(blk + (size_t)kW2Rows * I) + j * (I / G);
+    const size_t rowb = packed_row_bytes(I, true);
+    const uint2 v = *reinterpret_cast<const uint2*>(blk + (size_t)j * rowb + k);
+    const float* sc = reinterpret_cast<const float*>(blk + (size_t)kW2Rows * rowb) + j * (I / G);
     float f[8];
     unpack_s8x8(v.x, v.y, f);
     uint16_t o[8];
@@ -449,12 +451,14 @@ static PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
     return fn;
 }
 
-// 2-D bf16 [rows, cols] row-major, box {64, box_rows}, 128-byte swizzle, zero fill out of bounds.
-static bool make_map_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows) {
+// 2-D bf16 [rows, cols] with a row stride of `ld` elements, box {64, box_rows}, 128-byte
+// swizzle, zero fill out of bounds.
+static bool make_map_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint64_t cols, uint32_t box_rows,
+                          uint64_t ld) {
     auto fn = encode_fn();
     if (!fn) return false;
     const cuuint64_t dims[2] = {cols, rows};
-    const cuuint64_t strides[1] = {cols * 2};
+    const cuuint64_t strides[1] = {ld * 2};
     const cuuint32_t box[2] = {64, box_rows};
     const cuuint32_t estr[2] = {1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
@@ -557,14 +561,17 @@ cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& 
     // upper bound of m-tiles (the plan holds the exact count on the device)
     const int max_mtiles = (kT + 127) / 128 + E + S * ((T + 127) / 128);
     CUtensorMap mA1, mB1, mBs1, mA2, mB2, mBs2;
-    if (!make_map_bf16(&mA1, xperm, (uint64_t)kT + T, H, kBM) ||
-        !make_map_bf16(&mB1, w13, (uint64_t)E * 2 * I, H, kBN) ||
-        !make_map_bf16(&mA2, h, (uint64_t)kT + (uint64_t)S * T, I, kBM) ||
-        !make_map_bf16(&mB2, w2, (uint64_t)E * H, I, kBN))
+    // packed bf16 weights have padded rows (layout.h); the int8 path's dequantized copies do not
+    const uint64_t ld13 = a.int8 ? H : packed_row_bytes(H, false) / 2;
+    const uint64_t ld2 = a.int8 ? I : packed_row_bytes(I, false) / 2;
+    if (!make_map_bf16(&mA1, xperm, (uint64_t)kT + T, H, kBM, H) ||
+        !make_map_bf16(&mB1, w13, (uint64_t)E * 2 * I, H, kBN, ld13) ||
+        !make_map_bf16(&mA2, h, (uint64_t)kT + (uint64_t)S * T, I, kBM, I) ||
+        !make_map_bf16(&mB2, w2, (uint64_t)E * H, I, kBN, ld2))
         return cudaErrorInvalidValue;
     if (S > 0) {
-        if (!make_map_bf16(&mBs1, a.w13_shared, (uint64_t)S * 2 * I, H, kBN) ||
-            !make_map_bf16(&mBs2, a.w2_shared, (uint64_t)S * H, I, kBN))
+        if (!make_map_bf16(&mBs1, a.w13_shared, (uint64_t)S * 2 * I, H, kBN, packed_row_bytes(H, false) / 2) ||
+            !make_map_bf16(&mBs2, a.w2_shared, (uint64_t)S * H, I, kBN, packed_row_bytes(I, false) / 2))
             return cudaErrorInvalidValue;
     } else {
         mBs1 = mB1;  // no shared groups in the plan: never read

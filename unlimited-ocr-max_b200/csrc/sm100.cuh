@@ -62,14 +62,14 @@ UOCR_DEV bool mbar_wait(uint64_t* bar, uint32_t parity, uint32_t* status) {
     return true;
 }
 
-// Whole-warp bounded wait (every lane calls it; the result is warp-uniform). Polls with a short
-// sleep between tries so waiting warps leave the issue slots to the working ones; the global
-// timer is read every 32 polls. `abort_flag` (optional) ends the wait early.
+// Whole-warp bounded wait (every lane calls it; the result is warp-uniform). mbarrier.try_wait
+// itself suspends the warp until the phase completes or a hardware time slice ends, so the
+// loop does not sleep; the global timer is read every 32 polls. `abort_flag` (optional) ends
+// the wait early.
 UOCR_DEV bool mbar_wait_warp(uint64_t* bar, uint32_t parity, volatile int* abort_flag, uint32_t* status) {
     if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
     uint64_t t0 = 0;
     for (uint32_t spin = 1;; ++spin) {
-        __nanosleep(40);
         if (__all_sync(0xffffffffu, mbar_try_wait(bar, parity))) return true;
         if ((spin & 31) == 0) {
             int give_up = 0;

@@ -156,7 +156,7 @@ class UocrMoE:
         if tuple(sg.shape) != (S * I, H) or tuple(su.shape) != (S * I, H) or tuple(sd.shape) != (H, S * I):
             raise ValueError("shared_experts: projections do not match shared_experts_dim")
         t["w13s"] = torch.empty(L.uocr_moe_w13_bytes(S, I, H, G, 0) // 2, dtype=torch.bfloat16, device=dev)
-        t["w2s"] = torch.empty((S, H, I), dtype=torch.bfloat16, device=dev)
+        t["w2s"] = torch.empty(L.uocr_moe_w2_bytes(S, H, I, G, 0) // 2, dtype=torch.bfloat16, device=dev)
         check(L.uocr_moe_pack_shared(sg.data_ptr(), su.data_ptr(), sd.data_ptr(), S, I, H,
                                      t["w13s"].data_ptr(), t["w2s"].data_ptr(), stream))
         torch.cuda.current_stream(dev).synchronize()
