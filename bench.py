@@ -52,9 +52,11 @@ def parse():
     p.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
     p.add_argument("--settle", type=float, default=1.5,
                    help="seconds of untimed replays before timing, while the clock sampler runs")
-    p.add_argument("--workload", choices=["decode", "prefill"], default="decode",
+    p.add_argument("--workload", choices=["decode", "prefill", "ep"], default="decode",
                    help="decode: configs[1]/[3] int8 B=8 decode stack (the headline); "
-                        "prefill: configs[2] bf16 prefill of 4096 tokens")
+                        "prefill: configs[2] bf16 prefill of 4096 tokens; "
+                        "ep: configs[4] expert-parallel prefill of --ep-tokens over the ranks")
+    p.add_argument("--ep-tokens", type=int, default=65536, help="EP prefill tokens over all ranks (configs[4])")
     p.add_argument("--tokens", type=int, default=4096, help="prefill tokens (configs[2]: 4096)")
     return p.parse_args()
 
@@ -467,6 +469,76 @@ def run_prefill(args, torch, uocr, synth, dist, world, rank, device):
     print(json.dumps(line), flush=True)
 
 
+def run_ep(args, torch, uocr, synth, dist, world, rank, device):
+    """bf16 MoE over --ep-tokens tokens split evenly over the ranks, routed experts
+    sharded (64 / N per GPU), Zipf(1.1) expert bias, NCCL all-to-all dispatch / combine."""
+    ep_mod = importlib.import_module(f"{PKG}.ep")
+    T_all = args.ep_tokens
+    if T_all % world:
+        raise SystemExit(f"--ep-tokens {T_all} does not split over {world} ranks")
+    T = T_all // world
+    cfg = uocr.MoEConfig()
+    st = synth.layer_state(cfg, 5000, device=device)
+    moe = ep_mod.ExpertParallelMoE(cfg, device=device).load_state_dict(st)
+    del st
+    moe.bias = synth.skew_bias(E, 5001, zipf_s=1.1, device=device)
+    x = synth.hidden_states(T_all, H, 5002, device=device)[rank * T:(rank + 1) * T].contiguous()
+    torch.cuda.empty_cache()
+    for _ in range(max(args.warmup, 3)):
+        out = moe(x)
+    torch.cuda.synchronize()
+    sampler = ClockSampler(physical_gpu_index(int(os.environ.get("LOCAL_RANK", "0"))))
+    sampler.start()
+    dist.barrier()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(args.steps):
+        out = moe(x)
+    b.record()
+    torch.cuda.synchronize()
+    clocks = sampler.stop()
+    ms = a.elapsed_time(b) / args.steps
+    t = torch.tensor([ms], device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    ms = float(t.item())
+    # per-rank expert load and exchanged bytes of one step
+    ids, wts = moe._route(x)
+    plan = ep_mod.plan_dispatch(ids, wts, world, moe.e_local)
+    sent = torch.tensor([sum(plan.send_counts) - plan.send_counts[rank]], dtype=torch.int64, device=device)
+    load = torch.bincount(ids.flatten().long(), minlength=E).to(torch.int64)
+    dist.all_reduce(sent)
+    dist.all_reduce(load)
+    finite = bool(torch.isfinite(out).all())
+    tc, tc_src = measured_tc_peak()
+    flop = PREFILL_FLOP_PER_TOKEN * T_all
+    tflops = flop / (ms * 1e-3) / 1e12
+    per_rank = load.view(world, -1).sum(1).tolist()
+    if rank != 0:
+        return
+    remote_rows = int(sent.item())
+    print(json.dumps({
+        "metric": "MoE-layer tokens/s (expert-parallel prefill, bf16)",
+        "value": T_all / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+        "vs_baseline": None, "dtype": "bf16 operands, fp32 accumulate (fp32 in/out)",
+        "data": "synthetic (seeded N(0,0.02)->bf16 weights; hidden N(0,1) RMS-normalised; Zipf(1.1) expert bias)",
+        "config": {"workload": f"configs[4] expert-parallel prefill, {T_all} tokens over {world} GPU(s)",
+                   "tokens_per_rank": T, "experts_per_rank": moe.e_local, "hidden": H, "moe_intermediate": I,
+                   "top_k": TOPK, "shared": S, "parallelism": f"ep{world} (routed experts) x dp{world} (tokens, shared)",
+                   "expert_rows_per_rank": per_rank,
+                   "remote_rows": remote_rows,
+                   "all_to_all_bytes_per_step": remote_rows * (H * 2 + 2 * TOPK * 4) + remote_rows * H * 4},
+        "roofline": {"bound": "tensor", "achieved": tflops / world, "peak": tc, "unit": "TFLOP/s per GPU",
+                     "frac": tflops / world / tc, "peak_source": tc_src + " (burst)",
+                     "scope": "whole EP layer (route, plan, all-to-all, experts, all-to-all, combine, shared)",
+                     "algorithmic_flop_per_step": flop, "traffic": None},
+        "e2e": None,
+        "clocks": clocks,
+        "outputs_finite": finite,
+    }), flush=True)
+
+
 def run_ours(args):
     import torch
 
@@ -474,9 +546,14 @@ def run_ours(args):
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     dist = None
-    if world > 1:
+    if world > 1 or args.workload == "ep":
         import torch.distributed as dist
 
+        if world == 1:  # a one-rank group for the expert-parallel path
+            os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+            os.environ.setdefault("MASTER_PORT", "29531")
+            os.environ.setdefault("RANK", "0")
+            os.environ.setdefault("WORLD_SIZE", "1")
         torch.cuda.set_device(local)
         dist.init_process_group("nccl", timeout=timedelta(seconds=180), device_id=torch.device("cuda", local))
     device = torch.device("cuda", local)
@@ -484,6 +561,11 @@ def run_ours(args):
     uocr = importlib.import_module(PKG)
     synth = importlib.import_module(f"{PKG}.synth")
     uocr.load()
+    if args.workload == "ep":
+        run_ep(args, torch, uocr, synth, dist, world, rank, device)
+        dist.barrier()
+        dist.destroy_process_group()
+        return
     if args.workload == "prefill":
         run_prefill(args, torch, uocr, synth, dist, world, rank, device)
         if dist:

@@ -174,6 +174,26 @@ UOCR_API int uocr_moe_prefill(const uocr_moe_layer* L, const float* x, int64_t T
                               float* out, int32_t* ids_out, float* wts_out,
                               void* workspace, size_t workspace_bytes, uocr_stream_t stream);
 
+/* Expert-parallel pieces (no counterpart in the reference, which runs on one device; they serve
+ * the expert-parallel prefill of configs[4]: tokens routed on their own GPU, rows exchanged with
+ * NCCL all-to-all, experts computed where they live).
+ *
+ * uocr_moe_ep_experts: the routed experts of L (typically a slice of E_local experts) applied to
+ * N received bf16 rows: out[n] = sum_s weight[n, s] * expert_{expert_local[n, s]}(rows[n]),
+ * s < L->top_k, entries with expert_local < 0 skipped; expert products as in uocr_moe_prefill.
+ * L's shared experts are not applied. */
+UOCR_API size_t uocr_moe_ep_experts_workspace_bytes(const uocr_moe_layer* L, int64_t N);
+UOCR_API int uocr_moe_ep_experts(const uocr_moe_layer* L, const uint16_t* rows, int64_t N,
+                                 const int32_t* expert_local, const float* weight, float* out,
+                                 void* workspace, size_t workspace_bytes, uocr_stream_t stream);
+
+/* The shared experts of L alone over x [T, H] fp32 (bf16 products, fp32 out): out = shared(x),
+ * or out += shared(x) with accumulate != 0. */
+UOCR_API size_t uocr_moe_shared_workspace_bytes(const uocr_moe_layer* L, int64_t T);
+UOCR_API int uocr_moe_shared_forward(const uocr_moe_layer* L, const float* x, int64_t T, float* out,
+                                     int accumulate, void* workspace, size_t workspace_bytes,
+                                     uocr_stream_t stream);
+
 /* Decode step without a caller workspace. No counterpart in the reference: added for callers
  * that cannot allocate device memory (a plugin host that passes an operator only its inputs
  * and outputs, or a runtime whose device memory is reserved up front). Same computation as

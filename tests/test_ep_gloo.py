@@ -1,0 +1,104 @@
+"""Expert-parallel bookkeeping on CPU ranks (gloo, world size 2): the dispatch plan, the count
+and row exchanges and the per-token sum of partials, with the expert compute done by a float64
+restatement of the layer on the receiving rank. The gathered outputs of both ranks must equal
+the single-process float64 layer (routing from the bit-exact fp32 oracle) to the prefill
+tolerance (the rows travel as bf16, as in the CUDA path)."""
+
+from __future__ import annotations
+
+import importlib
+import os
+import socket
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+ROOT = Path(__file__).resolve().parents[1]
+H, I, E, K, S = 256, 128, 8, 6, 2
+T_TOTAL = 48
+
+
+def _free_port() -> int:
+    with socket.socket() as s:
+        s.bind(("127.0.0.1", 0))
+        return s.getsockname()[1]
+
+
+def _setup():
+    sys.path.insert(0, str(ROOT))
+    from oracle import moe_oracle as o
+
+    cfg = o.MoEConfig(hidden=H, inter=I, n_routed=E, n_shared=S, top_k=K)
+    w = o.synth_weights(cfg, 11, std=0.05)
+    x = o.synth_hidden(T_TOTAL, H, 12)
+    return o, cfg, w, x
+
+
+def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        ep = importlib.import_module("unlimited-ocr-max_b200.ep")
+        o, cfg, w, x = _setup()
+        e_local = E // world
+        t_local = T_TOTAL // world
+        xl = torch.from_numpy(x[rank * t_local:(rank + 1) * t_local].copy())
+        st = {n: o.bf16_to_f32(getattr(w, n)).astype(np.float64) for n in ("gate", "up", "down")}
+        sg, su, sd = (o.bf16_to_f32(a).astype(np.float64) for a in (w.shared_gate, w.shared_up, w.shared_down))
+        silu = lambda a: a / (1.0 + np.exp(-a))  # noqa: E731
+
+        def route(xt):
+            r = o.route_fp32(xt.numpy(), w.router, None, K)
+            return torch.from_numpy(r.ids), torch.from_numpy(r.weights)
+
+        def local_experts(rows, meta_e, meta_w):
+            xr = rows.float().numpy().astype(np.float64)
+            out = np.zeros_like(xr)
+            for n in range(xr.shape[0]):
+                for s in range(K):
+                    e = int(meta_e[n, s])
+                    if e < 0:
+                        continue
+                    g = rank * e_local + e
+                    hcol = silu(st["gate"][g] @ xr[n]) * (st["up"][g] @ xr[n])
+                    out[n] += float(meta_w[n, s]) * (st["down"][g] @ hcol)
+            return torch.from_numpy(out.astype(np.float32))
+
+        def shared(xt, out):
+            xf = xt.numpy().astype(np.float64)
+            out += torch.from_numpy(((silu(xf @ sg.T) * (xf @ su.T)) @ sd.T).astype(np.float32))
+
+        got = ep.ep_forward(xl, route, local_experts, shared, world, e_local)
+        np.save(os.path.join(out_dir, f"rank{rank}.npy"), got.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_plan_dispatch_rows_and_metadata():
+    ep = importlib.import_module("unlimited-ocr-max_b200.ep")
+    ids = torch.tensor([[0, 5, 1, 7, 2, 3], [4, 5, 6, 7, 0, 1], [0, 1, 2, 3, 4, 5]], dtype=torch.int32)
+    wts = torch.arange(18, dtype=torch.float32).view(3, 6) / 100
+    plan = ep.plan_dispatch(ids, wts, 2, 4)
+    assert plan.send_counts == [3, 3]  # every token has experts on both ranks
+    assert plan.order.tolist() == [0, 1, 2, 0, 1, 2]
+    # token 0 on rank 1: experts 5 and 7 -> local 1 and 3 in slots 1 and 3
+    assert plan.meta_expert[3].tolist() == [-1, 1, -1, 3, -1, -1]
+    assert torch.equal(plan.meta_weight[3], torch.tensor([0, 0.01, 0, 0.03, 0, 0]))
+    one = ep.plan_dispatch(torch.tensor([[0, 1, 2, 3, 0, 1]], dtype=torch.int32), wts[:1], 2, 4)
+    assert one.send_counts == [1, 0]
+
+
+def test_ep_forward_two_gloo_ranks(tmp_path):
+    world = 2
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    got = np.concatenate([np.load(tmp_path / f"rank{r}.npy") for r in range(world)])
+    o, cfg, w, x = _setup()
+    r = o.route_fp32(x, w.router, None, K)
+    ref = o.moe_layer_fp64(cfg, w, x, r.ids, r.weights)
+    assert np.max(np.abs(got - ref)) <= 2e-2
+    assert o.rel_l2(got, ref) <= 1e-2

@@ -6,7 +6,8 @@ not a Python identifier). Public surface:
 * ``MoEConfig``, ``UocrMoE`` -- the reference's ``MoE`` module surface (decoder.py:517-667);
 * ``ops`` -- the reference's custom ops ``moe_bf16_qmv``, ``moe_int8_qmv``,
   ``int8_dequant_expert``, ``dense_bf16_qmv`` and the gate ``route``;
-* ``weights`` -- checkpoint-name stacking and int8 detection (weight_adapters.py);
+* ``ep`` -- ``ExpertParallelMoE``, the prefill with routed experts sharded over GPUs;
+* ``synth`` -- seeded synthetic weights and activations of the benchmark configs;
 * ``build`` -- compiles ``libuocr_moe.so`` in-tree.
 """
 

@@ -366,6 +366,7 @@ int uocr_moe_prefill(const uocr_moe_layer* L, const float* x, int64_t T, const f
     uocr::PrefillArgs a{};
     a.T = (int)T; a.H = L->hidden; a.I = L->inter; a.E = L->n_routed; a.S = L->n_shared; a.topk = L->top_k;
     a.G = L->int8 ? L->group : 128; a.int8 = L->int8;
+    a.route = 1; a.use_shared = 1; a.accumulate = 0;
     a.x = x; a.router = L->router; a.bias = bias;
     a.ids = ids_out ? ids_out : reinterpret_cast<int32_t*>(ws + d.ids);
     a.wts = wts_out ? wts_out : reinterpret_cast<float*>(ws + d.wts);
@@ -373,6 +374,79 @@ int uocr_moe_prefill(const uocr_moe_layer* L, const float* x, int64_t T, const f
     a.w13_shared = L->w13_shared; a.w2_shared = L->w2_shared;
     a.out = out;
     return cuda_status(uocr::launch_prefill(a, ws, d, S(stream)), "moe_prefill: launch");
+}
+
+// expert-parallel pieces
+// ---------------------------------------------------------------------------------------
+
+size_t uocr_moe_ep_experts_workspace_bytes(const uocr_moe_layer* L, int64_t N) {
+    if (!L || N < 1 || N > (int64_t(1) << 24)) return 0;
+    return uocr::prefill_layout((int)N, L->hidden, L->inter, L->n_routed, 0, L->top_k, L->int8 != 0).total;
+}
+
+int uocr_moe_ep_experts(const uocr_moe_layer* L, const uint16_t* rows, int64_t N, const int32_t* expert_local,
+                        const float* weight, float* out, void* workspace, size_t workspace_bytes,
+                        uocr_stream_t stream) {
+    int rc = check_layer(L, "moe_ep_experts");
+    if (rc) return rc;
+    if (N < 0 || N > (int64_t(1) << 24)) return fail(UOCR_EINVAL, "moe_ep_experts: N=%lld outside 0..2^24", (long long)N);
+    if (N == 0) return ok();
+    if ((int64_t)L->top_k * N >= (int64_t(1) << 31)) return fail(UOCR_EUNSUPPORTED, "moe_ep_experts: too many rows");
+    if (L->hidden % 256) return fail(UOCR_EUNSUPPORTED, "moe_ep_experts: hidden=%d must be a multiple of 256", L->hidden);
+    if (!rows || !expert_local || !weight || !out || !workspace) return fail(UOCR_EINVAL, "moe_ep_experts: null pointer");
+    if (!a16(rows) || !a16(out)) return fail(UOCR_EINVAL, "moe_ep_experts: rows and out must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(workspace) & 255)
+        return fail(UOCR_EINVAL, "moe_ep_experts: workspace must be 256-byte aligned");
+    const uocr::PrefillLayout d =
+        uocr::prefill_layout((int)N, L->hidden, L->inter, L->n_routed, 0, L->top_k, L->int8 != 0);
+    if (workspace_bytes < d.total)
+        return fail(UOCR_EINVAL, "moe_ep_experts: workspace of %zu bytes, need %zu", workspace_bytes, d.total);
+    char* ws = reinterpret_cast<char*>(workspace);
+    uocr::PrefillArgs a{};
+    a.T = (int)N; a.H = L->hidden; a.I = L->inter; a.E = L->n_routed; a.S = 0; a.topk = L->top_k;
+    a.G = L->int8 ? L->group : 128; a.int8 = L->int8;
+    a.route = 0; a.use_shared = 0; a.accumulate = 0;
+    a.x_bf16 = rows;
+    a.ids = const_cast<int32_t*>(expert_local);
+    a.wts = const_cast<float*>(weight);
+    a.w13 = L->w13; a.w2 = L->w2;
+    a.out = out;
+    return cuda_status(uocr::launch_prefill(a, ws, d, S(stream)), "moe_ep_experts: launch");
+}
+
+size_t uocr_moe_shared_workspace_bytes(const uocr_moe_layer* L, int64_t T) {
+    if (!L || T < 1 || T > (int64_t(1) << 24)) return 0;
+    return uocr::prefill_layout((int)T, L->hidden, L->inter, L->n_routed, L->n_shared, 0, false).total;
+}
+
+int uocr_moe_shared_forward(const uocr_moe_layer* L, const float* x, int64_t T, float* out, int accumulate,
+                            void* workspace, size_t workspace_bytes, uocr_stream_t stream) {
+    if (!L) return fail(UOCR_EINVAL, "moe_shared_forward: null layer");
+    if (T < 0 || T > (int64_t(1) << 24)) return fail(UOCR_EINVAL, "moe_shared_forward: T=%lld outside 0..2^24", (long long)T);
+    if (T == 0) return ok();
+    if (L->n_shared < 1 || L->n_shared > uocr::kDecodeMaxShared)
+        return fail(UOCR_EUNSUPPORTED, "moe_shared_forward: n_shared=%d outside 1..8", L->n_shared);
+    if (L->hidden < 256 || L->hidden % 256 || L->inter < 128 || L->inter % 128)
+        return fail(UOCR_EUNSUPPORTED, "moe_shared_forward: hidden must be a multiple of 256, inter of 128");
+    if (!L->w13_shared || !L->w2_shared || !x || !out || !workspace) return fail(UOCR_EINVAL, "moe_shared_forward: null pointer");
+    if (!a16(x) || !a16(out) || !a16(L->w13_shared) || !a16(L->w2_shared))
+        return fail(UOCR_EINVAL, "moe_shared_forward: pointers must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(workspace) & 255)
+        return fail(UOCR_EINVAL, "moe_shared_forward: workspace must be 256-byte aligned");
+    const uocr::PrefillLayout d = uocr::prefill_layout((int)T, L->hidden, L->inter, L->n_routed, L->n_shared, 0, false);
+    if (workspace_bytes < d.total)
+        return fail(UOCR_EINVAL, "moe_shared_forward: workspace of %zu bytes, need %zu", workspace_bytes, d.total);
+    char* ws = reinterpret_cast<char*>(workspace);
+    uocr::PrefillArgs a{};
+    // no routed entries: the routed tensor maps are sized over the shared weights and never read
+    a.T = (int)T; a.H = L->hidden; a.I = L->inter; a.E = L->n_shared; a.S = L->n_shared; a.topk = 0;
+    a.G = 128; a.int8 = 0;
+    a.route = 0; a.use_shared = 1; a.accumulate = accumulate != 0;
+    a.x = x;
+    a.w13 = L->w13_shared; a.w2 = L->w2_shared;  // no routed groups: the routed maps are never read
+    a.w13_shared = L->w13_shared; a.w2_shared = L->w2_shared;
+    a.out = out;
+    return cuda_status(uocr::launch_prefill(a, ws, d, S(stream)), "moe_shared_forward: launch");
 }
 
 int uocr_moe_decode_set_trace(void* device_buffer, size_t bytes) {

@@ -91,7 +91,11 @@ struct PrefillPlan {
 
 struct PrefillArgs {
     int T, H, I, E, S, topk, G, int8;
-    const float* x;  // [T, H]
+    int route;       // 1: route x here (ids/wts are outputs); 0: ids/wts given, id < 0 = no expert
+    int use_shared;  // add the S shared experts
+    int accumulate;  // out += instead of out =
+    const float* x;  // [T, H] fp32 (or null with x_bf16)
+    const uint16_t* x_bf16;  // [T, H] bf16 rows given directly (or null)
     const uint16_t* router;
     const float* bias;
     int32_t* ids;  // [T, topk]
@@ -104,7 +108,7 @@ struct PrefillArgs {
 };
 // Byte offsets of the prefill workspace regions (status word first).
 struct PrefillLayout {
-    size_t status, ids, wts, chunk_counts, chunk_base, plan1, plan2, dest, src_tok, xperm, h, y, w13, w2, total;
+    size_t status, n_valid, ids, wts, chunk_counts, chunk_base, plan1, plan2, dest, src_tok, xperm, h, y, w13, w2, total;
 };
 PrefillLayout prefill_layout(int T, int H, int I, int E, int S, int topk, bool int8);
 cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& d, cudaStream_t st);

@@ -43,7 +43,7 @@ __global__ void __launch_bounds__(kChunk) prefill_hist_kernel(const int32_t* __r
     if (threadIdx.x < 64) hist[threadIdx.x] = 0;
     __syncthreads();
     const int q = blockIdx.x * kChunk + threadIdx.x;
-    if (q < n) atomicAdd(&hist[clamp_expert(ids[q], E)], 1);
+    if (q < n && ids[q] >= 0) atomicAdd(&hist[clamp_expert(ids[q], E)], 1);  // < 0: no expert for the entry
     __syncthreads();
     if (threadIdx.x < 64) chunk_counts[blockIdx.x * 64 + threadIdx.x] = hist[threadIdx.x];
 }
@@ -52,7 +52,7 @@ __global__ void __launch_bounds__(kChunk) prefill_hist_kernel(const int32_t* __r
 __global__ void __launch_bounds__(64) prefill_scan_kernel(const int* __restrict__ chunk_counts, int nchunks, int E,
                                                           int S, int T, int topk, int* __restrict__ chunk_base,
                                                           PrefillPlan* __restrict__ plan1,
-                                                          PrefillPlan* __restrict__ plan2) {
+                                                          PrefillPlan* __restrict__ plan2, int* __restrict__ n_valid) {
     __shared__ int total[64];
     __shared__ int base[65];
     const int e = threadIdx.x;
@@ -68,6 +68,7 @@ __global__ void __launch_bounds__(64) prefill_scan_kernel(const int* __restrict_
             acc += total[i];
         }
         base[64] = acc;
+        *n_valid = acc;  // routed entries with an expert: rows [0, acc) of the permuted A
     }
     __syncthreads();
     if (e < E) {
@@ -114,7 +115,7 @@ __global__ void __launch_bounds__(kChunk) prefill_scatter_kernel(const int32_t* 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i < (kChunk / 32) * 64; i += kChunk) (&wcount[0][0])[i] = 0;
     __syncthreads();
-    const int e = q < n ? clamp_expert(ids[q], E) : -1;
+    const int e = (q < n && ids[q] >= 0) ? clamp_expert(ids[q], E) : -1;
     const unsigned same = __match_any_sync(0xffffffffu, e);
     const int rank_in_warp = __popc(same & ((1u << lane) - 1u));
     if (e >= 0 && rank_in_warp == 0) wcount[warp][e] = __popc(same);
@@ -125,19 +126,31 @@ __global__ void __launch_bounds__(kChunk) prefill_scatter_kernel(const int32_t* 
         const int p = chunk_base[blockIdx.x * 64 + e] + before + rank_in_warp;
         dest[q] = p;
         src_tok[p] = q / topk;
+    } else if (q < n) {
+        dest[q] = -1;
     }
 }
 
-// xperm[p] = bf16(x[src_tok[p]]) for p < kT; xperm[kT + t] = bf16(x[t]). One warp per row.
-__global__ void __launch_bounds__(256) prefill_gather_kernel(const float* __restrict__ x, int T, int H, int kT,
+// xperm[p] = bf16(x[src_tok[p]]) for p < n_valid; with shared experts also xperm[kT + t] =
+// bf16(x[t]). x is fp32 (converted) or already bf16 (copied). One warp per row.
+__global__ void __launch_bounds__(256) prefill_gather_kernel(const float* __restrict__ x, const uint16_t* __restrict__ xb,
+                                                             int T, int H, int kT, int shared,
+                                                             const int* __restrict__ n_valid,
                                                              const int* __restrict__ src_tok,
                                                              uint16_t* __restrict__ xperm) {
     const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
     const int lane = threadIdx.x & 31;
-    if (row >= kT + T) return;
+    if (row >= kT + (shared ? T : 0)) return;
+    if (row < kT && row >= *n_valid) return;
     const int t = row < kT ? src_tok[row] : row - kT;
-    const float* src = x + (size_t)t * H;
     uint16_t* dst = xperm + (size_t)row * H;
+    if (xb) {
+        const uint16_t* src = xb + (size_t)t * H;
+        for (int k = lane * 8; k < H; k += 256)
+            *reinterpret_cast<uint4*>(dst + k) = *reinterpret_cast<const uint4*>(src + k);
+        return;
+    }
+    const float* src = x + (size_t)t * H;
     for (int k = lane * 8; k < H; k += 256) {
         const float4 a = *reinterpret_cast<const float4*>(src + k);
         const float4 b = *reinterpret_cast<const float4*>(src + k + 4);
@@ -198,17 +211,21 @@ __global__ void __launch_bounds__(256) prefill_dequant_w2_kernel(const unsigned 
     *reinterpret_cast<uint4*>(out + i) = *reinterpret_cast<const uint4*>(o);
 }
 
-// out[t][j] = sum_s w[t,s] * y[dest[t*k+s]][j] + sum_q y[kT + q*T + t][j]
+// out[t][j] (+)= sum_s w[t,s] * y[dest[t*k+s]][j] (entries without an expert skipped)
+//              + sum_q y[kT + q*T + t][j]                     (S shared experts)
 __global__ void __launch_bounds__(256) prefill_combine_kernel(const float* __restrict__ y, const float* __restrict__ wts,
                                                               const int* __restrict__ dest, int T, int H, int topk,
-                                                              int S, float* __restrict__ out) {
+                                                              int S, int accumulate, float* __restrict__ out) {
     const int t = blockIdx.x;
     const int kT = topk * T;
     for (int j = threadIdx.x * 4; j < H; j += blockDim.x * 4) {
         float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (accumulate) acc = *reinterpret_cast<const float4*>(out + (size_t)t * H + j);
         for (int s = 0; s < topk; ++s) {
+            const int d = dest[t * topk + s];
+            if (d < 0) continue;
             const float w = wts[t * topk + s];
-            const float4 v = *reinterpret_cast<const float4*>(y + (size_t)dest[t * topk + s] * H + j);
+            const float4 v = *reinterpret_cast<const float4*>(y + (size_t)d * H + j);
             acc.x = __fmaf_rn(w, v.x, acc.x);
             acc.y = __fmaf_rn(w, v.y, acc.y);
             acc.z = __fmaf_rn(w, v.z, acc.z);
@@ -497,11 +514,12 @@ PrefillLayout prefill_layout(int T, int H, int I, int E, int S, int topk, bool i
     const size_t kT = (size_t)topk * T;
     const size_t nchunks = (kT + kChunk - 1) / kChunk;
     size_t off = 0;
-    d.status = off; off += 256;
+    d.status = off; off += 128;
+    d.n_valid = off; off += 128;
     d.ids = off; off += al(sizeof(int32_t) * kT);
     d.wts = off; off += al(sizeof(float) * kT);
-    d.chunk_counts = off; off += al(sizeof(int) * nchunks * 64);
-    d.chunk_base = off; off += al(sizeof(int) * nchunks * 64);
+    d.chunk_counts = off; off += al(sizeof(int) * (nchunks ? nchunks : 1) * 64);
+    d.chunk_base = off; off += al(sizeof(int) * (nchunks ? nchunks : 1) * 64);
     d.plan1 = off; off += al(sizeof(PrefillPlan));
     d.plan2 = off; off += al(sizeof(PrefillPlan));
     d.dest = off; off += al(sizeof(int) * kT);
@@ -519,7 +537,8 @@ PrefillLayout prefill_layout(int T, int H, int I, int E, int S, int topk, bool i
 }
 
 cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& d, cudaStream_t st) {
-    const int T = a.T, H = a.H, I = a.I, E = a.E, S = a.S, k = a.topk;
+    const int T = a.T, H = a.H, I = a.I, E = a.E, k = a.topk;
+    const int S = a.use_shared ? a.S : 0;  // shared-expert groups in the GEMMs
     const int kT = k * T;
     const int nchunks = (kT + kChunk - 1) / kChunk;
     int32_t* ids = a.ids;
@@ -530,23 +549,29 @@ cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& 
     PrefillPlan* plan2 = reinterpret_cast<PrefillPlan*>(ws + d.plan2);
     int* dest = reinterpret_cast<int*>(ws + d.dest);
     int* src_tok = reinterpret_cast<int*>(ws + d.src_tok);
+    int* n_valid = reinterpret_cast<int*>(ws + d.n_valid);
     uint16_t* xperm = reinterpret_cast<uint16_t*>(ws + d.xperm);
     uint16_t* h = reinterpret_cast<uint16_t*>(ws + d.h);
     float* y = reinterpret_cast<float*>(ws + d.y);
     uint32_t* status = reinterpret_cast<uint32_t*>(ws + d.status);
 
-    cudaError_t err = launch_route(a.x, T, H, a.router, E, a.bias, k, ids, wts, st);
-    if (err != cudaSuccess) return err;
-    prefill_hist_kernel<<<nchunks, kChunk, 0, st>>>(ids, kT, E, chunk_counts);
-    prefill_scan_kernel<<<1, 64, 0, st>>>(chunk_counts, nchunks, E, S, T, k, chunk_base, plan1, plan2);
-    prefill_scatter_kernel<<<nchunks, kChunk, 0, st>>>(ids, kT, E, k, chunk_base, dest, src_tok);
-    prefill_gather_kernel<<<(kT + T + 7) / 8, 256, 0, st>>>(a.x, T, H, kT, src_tok, xperm);
+    cudaError_t err = cudaSuccess;
+    if (a.route && k > 0) {
+        err = launch_route(a.x, T, H, a.router, E, a.bias, k, ids, wts, st);
+        if (err != cudaSuccess) return err;
+    }
+    if (nchunks > 0) prefill_hist_kernel<<<nchunks, kChunk, 0, st>>>(ids, kT, E, chunk_counts);
+    prefill_scan_kernel<<<1, 64, 0, st>>>(chunk_counts, nchunks, E, S, T, k, chunk_base, plan1, plan2, n_valid);
+    if (nchunks > 0) prefill_scatter_kernel<<<nchunks, kChunk, 0, st>>>(ids, kT, E, k, chunk_base, dest, src_tok);
+    const int grows = kT + (S ? T : 0);
+    if (grows > 0)
+        prefill_gather_kernel<<<(grows + 7) / 8, 256, 0, st>>>(a.x, a.x_bf16, T, H, kT, S > 0, n_valid, src_tok, xperm);
     err = cudaGetLastError();
     if (err != cudaSuccess) return err;
 
     const void* w13 = a.w13;
     const void* w2 = a.w2;
-    if (a.int8) {
+    if (a.int8 && k > 0) {
         uint16_t* w13d = reinterpret_cast<uint16_t*>(ws + d.w13);
         uint16_t* w2d = reinterpret_cast<uint16_t*>(ws + d.w2);
         const long n13 = (long)E * 2 * I * H, n2 = (long)E * H * I;
@@ -559,7 +584,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& 
         w2 = w2d;
     }
     // upper bound of m-tiles (the plan holds the exact count on the device)
-    const int max_mtiles = (kT + 127) / 128 + E + S * ((T + 127) / 128);
+    const int max_mtiles = (kT + 127) / 128 + (k > 0 ? E : 0) + S * ((T + 127) / 128);
     CUtensorMap mA1, mB1, mBs1, mA2, mB2, mBs2;
     // packed bf16 weights have padded rows (layout.h); the int8 path's dequantized copies do not
     const uint64_t ld13 = a.int8 ? H : packed_row_bytes(H, false) / 2;
@@ -582,7 +607,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& 
     if (err != cudaSuccess) return err;
     err = launch_gemm(kEpiF32, mA2, mB2, mBs2, plan2, H / kBN, I / kBK, H, y, H, max_mtiles * (H / kBN), status, st);
     if (err != cudaSuccess) return err;
-    prefill_combine_kernel<<<T, 256, 0, st>>>(y, wts, dest, T, H, k, S, a.out);
+    prefill_combine_kernel<<<T, 256, 0, st>>>(y, wts, dest, T, H, k, S, a.accumulate, a.out);
     return cudaGetLastError();
 }
 

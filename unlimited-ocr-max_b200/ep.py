@@ -1,0 +1,192 @@
+"""Expert-parallel prefill of the MoE sublayer over P GPUs of one node.
+
+The reference runs the MoE on one device; this is the B200 build's extension for large token
+batches. Every rank holds T / P tokens, the replicated gate and shared experts, and E / P routed
+experts (contiguous: rank r owns experts [r E/P, (r+1) E/P)). One forward:
+
+1. route the rank's tokens (the bit-exact gate, ``uocr_moe_route``);
+2. plan: one row per (token, destination rank) that holds at least one of its k experts, rows
+   ordered by destination rank, then token; each row carries, per slot, the expert's local index
+   on that rank (or -1) and its routing weight;
+3. exchange counts, then rows (bf16) and metadata, with ``all_to_all_single`` (NCCL over
+   NVLink);
+4. each rank applies its local experts to the rows it received, pre-weighted and summed per
+   row (``uocr_moe_ep_experts``: the prefill's permute + tcgen05 grouped GEMMs);
+5. exchange the fp32 partial rows back; each token sums its partials in destination-rank order
+   (deterministic), then adds its shared experts (``uocr_moe_shared_forward``, data-parallel).
+
+The bookkeeping (2, 3, 5) is plain torch and also runs on CPU ranks (gloo) for tests; the
+compute steps are CUDA only (``ExpertParallelMoE``).
+"""
+
+from __future__ import annotations
+
+import ctypes
+from dataclasses import dataclass
+from typing import Callable, Mapping
+
+import torch
+import torch.distributed as dist
+
+from . import ops
+from ._lib import check, load
+from .moe import MoEConfig, UocrMoE
+
+__all__ = ["DispatchPlan", "plan_dispatch", "exchange_counts", "exchange_rows", "sum_partials", "ep_forward",
+           "ExpertParallelMoE"]
+
+
+@dataclass
+class DispatchPlan:
+    order: torch.Tensor        # [Ns] token of each send row (rows grouped by destination rank)
+    send_counts: list[int]     # rows per destination rank
+    meta_expert: torch.Tensor  # [Ns, k] int32: local expert index on the destination, -1 for none
+    meta_weight: torch.Tensor  # [Ns, k] fp32 routing weight of the slot
+
+
+def plan_dispatch(ids: torch.Tensor, wts: torch.Tensor, world: int, e_local: int) -> DispatchPlan:
+    """Rows to send: one per (token, destination rank) with at least one expert there."""
+    dest = torch.div(ids.long(), e_local, rounding_mode="floor")  # [T, k]
+    orders, counts, metas_e, metas_w = [], [], [], []
+    for p in range(world):
+        on_p = dest == p
+        tok = torch.nonzero(on_p.any(dim=1), as_tuple=False).flatten()
+        orders.append(tok)
+        counts.append(int(tok.numel()))
+        sel = on_p[tok]
+        metas_e.append(torch.where(sel, ids[tok].long() - p * e_local, torch.full_like(ids[tok].long(), -1)).int())
+        metas_w.append(torch.where(sel, wts[tok], torch.zeros_like(wts[tok])))
+    return DispatchPlan(torch.cat(orders), counts, torch.cat(metas_e), torch.cat(metas_w))
+
+
+def exchange_counts(send_counts: list[int], device, group=None) -> list[int]:
+    world = len(send_counts)
+    send = torch.tensor(send_counts, dtype=torch.int64, device=device)
+    recv = torch.empty(world, dtype=torch.int64, device=device)
+    dist.all_to_all_single(recv, send, group=group)
+    return [int(v) for v in recv.tolist()]
+
+
+def exchange_rows(t: torch.Tensor, send_counts: list[int], recv_counts: list[int], group=None) -> torch.Tensor:
+    """all_to_all_single of the rows of ``t`` (rank p gets send_counts[p] rows, in order)."""
+    out = torch.empty((sum(recv_counts),) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
+    dist.all_to_all_single(out, t.contiguous(), output_split_sizes=recv_counts, input_split_sizes=send_counts,
+                           group=group)
+    return out
+
+
+def sum_partials(T: int, H: int, plan: DispatchPlan, partial: torch.Tensor) -> torch.Tensor:
+    """out[t] = sum over destination ranks p (ascending) of the partial row of (t, p); every rank
+    sends each token at most one row, so each step indexes distinct tokens (no atomics)."""
+    out = torch.zeros((T, H), dtype=torch.float32, device=partial.device)
+    r0 = 0
+    for c in plan.send_counts:
+        if c:
+            out.index_add_(0, plan.order[r0:r0 + c], partial[r0:r0 + c])
+        r0 += c
+    return out
+
+
+def ep_forward(x: torch.Tensor, route: Callable, local_experts: Callable, shared: Callable, world: int,
+               e_local: int, group=None) -> torch.Tensor:
+    """One expert-parallel MoE forward of this rank's tokens x [T, H] fp32.
+
+    route(x) -> (ids [T,k] int32 global, wts [T,k] fp32); local_experts(rows bf16 [N,H], meta_e,
+    meta_w) -> fp32 [N,H]; shared(x, out) adds the shared experts into out in place.
+    """
+    T, H = x.shape
+    ids, wts = route(x)
+    plan = plan_dispatch(ids, wts, world, e_local)
+    recv_counts = exchange_counts(plan.send_counts, x.device, group)
+    rows = x.index_select(0, plan.order).to(torch.bfloat16)
+    meta = torch.cat([plan.meta_expert, plan.meta_weight.view(torch.int32)], dim=1)  # one exchange
+    rows_in = exchange_rows(rows, plan.send_counts, recv_counts, group)
+    meta_in = exchange_rows(meta, plan.send_counts, recv_counts, group)
+    k = ids.shape[1]
+    part_in = local_experts(rows_in, meta_in[:, :k].contiguous(), meta_in[:, k:].contiguous().view(torch.float32))
+    part = exchange_rows(part_in, recv_counts, plan.send_counts, group)
+    out = sum_partials(T, H, plan, part)
+    shared(x, out)
+    return out
+
+
+class ExpertParallelMoE:
+    """The MoE sublayer with its routed experts sharded over the ranks of ``group``.
+
+    Construct on every rank after ``torch.distributed`` is initialised (backend "nccl"), load the
+    full reference state dict (every rank keeps only its slice of the routed experts), then call
+    with the rank's tokens.
+    """
+
+    def __init__(self, config: MoEConfig, *, group=None, device: str | torch.device = "cuda") -> None:
+        self.config = config
+        self.group = group
+        self.rank = dist.get_rank(group)
+        self.world = dist.get_world_size(group)
+        E = config.n_routed_experts
+        if E % self.world:
+            raise ValueError(f"ExpertParallelMoE: {E} experts do not split over {self.world} ranks")
+        self.e_local = E // self.world
+        if self.e_local < config.num_experts_per_tok:
+            raise ValueError("ExpertParallelMoE: fewer local experts than experts per token")
+        self.device = torch.device(device)
+        if self.device.type != "cuda":
+            raise ValueError("ExpertParallelMoE runs on CUDA devices only")
+        local_cfg = MoEConfig(**{**config.__dict__, "n_routed_experts": self.e_local})
+        self.local = UocrMoE(local_cfg, device=self.device)
+        self.router: torch.Tensor | None = None
+        self.bias: torch.Tensor | None = None
+        self._ws: dict[str, torch.Tensor] = {}
+
+    def load_state_dict(self, state: Mapping[str, torch.Tensor]) -> "ExpertParallelMoE":
+        e0, n = self.rank * self.e_local, self.e_local
+        local = {}
+        for name, t in state.items():
+            if name.startswith("experts."):
+                t = t[e0:e0 + n]
+            elif name == "gate.gate_score.weight":
+                self.router = t.to(self.device, torch.bfloat16).contiguous()
+                t = t[e0:e0 + n]  # unused by the local module (routing uses the full gate)
+            local[name] = t
+        self.local.load_state_dict(local)
+        return self
+
+    def _workspace(self, name: str, nbytes: int) -> torch.Tensor:
+        ws = self._ws.get(name)
+        if ws is None or ws.numel() < nbytes:
+            ws = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)
+            self._ws[name] = ws
+        return ws
+
+    def _route(self, x: torch.Tensor):
+        return ops.route(x, self.router, self.bias, self.config.num_experts_per_tok)
+
+    def _local_experts(self, rows: torch.Tensor, meta_e: torch.Tensor, meta_w: torch.Tensor) -> torch.Tensor:
+        N, H = rows.shape
+        out = torch.empty((N, H), dtype=torch.float32, device=self.device)
+        if N == 0:
+            return out
+        L = load()
+        lay = ctypes.byref(self.local.layer)
+        ws = self._workspace("ep", L.uocr_moe_ep_experts_workspace_bytes(lay, N))
+        check(L.uocr_moe_ep_experts(lay, rows.view(torch.int16).data_ptr(), N, meta_e.data_ptr(), meta_w.data_ptr(),
+                                    out.data_ptr(), ws.data_ptr(), ws.numel(),
+                                    torch.cuda.current_stream(self.device).cuda_stream))
+        return out
+
+    def _shared(self, x: torch.Tensor, out: torch.Tensor) -> None:
+        T = x.shape[0]
+        if T == 0:
+            return
+        L = load()
+        lay = ctypes.byref(self.local.layer)
+        ws = self._workspace("shared", L.uocr_moe_shared_workspace_bytes(lay, T))
+        check(L.uocr_moe_shared_forward(lay, x.data_ptr(), T, out.data_ptr(), 1, ws.data_ptr(), ws.numel(),
+                                        torch.cuda.current_stream(self.device).cuda_stream))
+
+    def __call__(self, x: torch.Tensor) -> torch.Tensor:
+        """The MoE over this rank's tokens x [T, H] fp32 (a collective: every rank calls it)."""
+        if not x.is_cuda or x.dtype != torch.float32 or x.dim() != 2 or x.shape[1] != self.config.hidden_size:
+            raise ValueError("ExpertParallelMoE: x must be a CUDA fp32 [T, hidden] tensor")
+        return ep_forward(x.contiguous(), self._route, self._local_experts, self._shared, self.world, self.e_local,
+                          self.group)
