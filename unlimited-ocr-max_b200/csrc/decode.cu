@@ -1,12 +1,14 @@
 // Decode-step MoE sublayer (MoE.decode_rows, unlimited_ocr_max/decoder.py:641-655) for B <= 8
-// tokens: two persistent kernels chained by programmatic dependent launch (PDL), each
-// streaming its weights from HBM once.
+// tokens: three kernels chained by programmatic dependent launch (PDL); K2 and K3 are persistent
+// and stream their weights from HBM once.
 //
-//   K2 route + gate/up   every CTA routes the step itself (fp32 logits in the oracle's order,
-//              softmax, top-k: bit-exact and identical in every CTA, so no grid-wide exchange)
-//              while its producer already streams shared-expert blocks; the routing groups the
-//              step by expert ("slots": 0..S-1 the shared experts, S+u the u-th distinct routed
-//              expert in ascending id), each slot owning contiguous rows of the h and y scratch.
+//   K1 logits            one small CTA per routed expert: the fp32 router logits of the B tokens
+//              in the oracle's order (router row fetched before the dependency wait).
+//   K2 route + gate/up   every CTA finishes the routing itself from K1's logits (softmax, top-k:
+//              bit-exact and identical in every CTA, so no grid-wide exchange) while its
+//              producer already streams shared-expert blocks; the routing groups the step by
+//              expert ("slots": 0..S-1 the shared experts, S+u the u-th distinct routed expert in
+//              ascending id), each slot owning contiguous rows of the h and y scratch.
 //              Items (slot, block of 8 or 16 row pairs) -> h[slot row][n] = silu(g) * u.
 //   K3 down + combine    items (slot, 32 output rows) -> y[slot row][j]; a publisher warp counts
 //              finished 4-row groups (a self-resetting counter per group) and the one that
@@ -128,7 +130,7 @@ UOCR_DEV void mma_tile_s8(uint32_t rows_s, uint32_t rowb, int row0, uint32_t sc_
         }
         const float slo = lds_f32(sc_s + 4u * ((row0 + g) * NG + grp));
         const float shi = lds_f32(sc_s + 4u * ((row0 + g + 8) * NG + grp));
-        const float sg0 = sig[(2 * t) * NG + grp], sg1 = sig[(2 * t + 1) * NG + grp];
+        const float sg0 = sig[2 * t], sg1 = sig[2 * t + 1];
         acc[0] = __fmaf_rn(undigit(c[0][0], c[1][0], c[2][0]), slo * sg0, acc[0]);
         acc[1] = __fmaf_rn(undigit(c[0][1], c[1][1], c[2][1]), slo * sg1, acc[1]);
         acc[2] = __fmaf_rn(undigit(c[0][2], c[1][2], c[2][2]), shi * sg0, acc[2]);
@@ -160,24 +162,23 @@ UOCR_DEV void mma_tile_bf16(uint32_t rows_s, uint32_t rowb, int s0, int s1, uint
 // product) and the products run back to back.
 template <int MAXS>
 struct FragS8 {
-    uint2 b[MAXS][3];    // digits d0..d2 of the warp's columns (lane: column g, bytes 8t..8t+7)
-    float sg[MAXS][2];   // digit scale of columns 2t, 2t+1 in the k-step's group
+    uint2 b[MAXS][3];  // digits d0..d2 of the warp's columns (lane: column g, bytes 8t..8t+7)
+    float sg[2];       // digit scale of columns 2t, 2t+1
 };
 
 template <int MAXS>
-UOCR_DEV void load_frag_s8(FragS8<MAXS>& f, uint32_t xd_s, const float* sig, int NG, int s0, int n, int lane) {
+UOCR_DEV void load_frag_s8(FragS8<MAXS>& f, uint32_t xd_s, const float* sig, int s0, int n, int lane) {
     const int t = lane & 3;
-    const uint32_t sig_s = smem_addr(sig);
 #pragma unroll
     for (int i = 0; i < MAXS; ++i) {
         if (i < n) {
             const int s = s0 + i;
 #pragma unroll
             for (int d = 0; d < 3; ++d) f.b[i][d] = lds_u64(xd_s + 8u * ((s * 3 + d) * 32 + lane));
-            f.sg[i][0] = lds_f32(sig_s + 4u * ((2 * t) * NG + (s >> 2)));
-            f.sg[i][1] = lds_f32(sig_s + 4u * ((2 * t + 1) * NG + (s >> 2)));
         }
     }
+    f.sg[0] = lds_f32(smem_addr(sig) + 8u * t);
+    f.sg[1] = lds_f32(smem_addr(sig) + 8u * t + 4u);
 }
 
 // s8 tile product over the warp's k-steps with register-resident digits (see mma_tile_s8).
@@ -203,10 +204,10 @@ UOCR_DEV void mma_tile_s8_reg(uint32_t rows_s, uint32_t rowb, int row0, uint32_t
                 for (int d = 0; d < 3; ++d)
 #pragma unroll
                     for (int j = 0; j < 4; ++j) v[d][j] = c[0][d][j] + c[1][d][j];
-                acc[0] = __fmaf_rn(undigit(v[0][0], v[1][0], v[2][0]), slo * f.sg[i][0], acc[0]);
-                acc[1] = __fmaf_rn(undigit(v[0][1], v[1][1], v[2][1]), slo * f.sg[i][1], acc[1]);
-                acc[2] = __fmaf_rn(undigit(v[0][2], v[1][2], v[2][2]), shi * f.sg[i][0], acc[2]);
-                acc[3] = __fmaf_rn(undigit(v[0][3], v[1][3], v[2][3]), shi * f.sg[i][1], acc[3]);
+                acc[0] = __fmaf_rn(undigit(v[0][0], v[1][0], v[2][0]), slo * f.sg[0], acc[0]);
+                acc[1] = __fmaf_rn(undigit(v[0][1], v[1][1], v[2][1]), slo * f.sg[1], acc[1]);
+                acc[2] = __fmaf_rn(undigit(v[0][2], v[1][2], v[2][2]), shi * f.sg[0], acc[2]);
+                acc[3] = __fmaf_rn(undigit(v[0][3], v[1][3], v[2][3]), shi * f.sg[1], acc[3]);
 #pragma unroll
                 for (int h = 0; h < 2; ++h)
 #pragma unroll
@@ -256,29 +257,35 @@ UOCR_DEV void mma_tile_bf16_reg(uint32_t rows_s, uint32_t rowb, int s0, int n, c
     for (int j = 0; j < 4; ++j) acc[j] += (c[0][0][j] + c[1][0][j]) + (c[0][1][j] + c[1][1][j]) + (c[0][2][j] + c[1][2][j]);
 }
 
-// Activations of up to 8 columns (rows of xf, stride ldx; rows >= valid read as zero) as int8
-// digits in fragment order: one warp per (column, 128-group), a lane per 4 values.
-UOCR_DEV void stage_digits(const float* xf, int ldx, int K, int valid, uint32_t* xd, float* sig, int warp, int lane,
-                           int nwarps) {
-    const int NG = K / 128;
-    for (int u = warp; u < kMaxB * NG; u += nwarps) {
-        const int col = u / NG, grp = u % NG;
-        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (col < valid) v = *reinterpret_cast<const float4*>(xf + (size_t)col * ldx + grp * 128 + 4 * lane);
-        float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
+// Activations of 8 columns (rows of xf, stride ldx; rows >= valid are zero) as int8 digits in
+// fragment order, one power-of-two scale per column: warp w converts column w (kCW >= 8 warps).
+UOCR_DEV void stage_digits(const float* xf, int ldx, int K, int valid, uint32_t* xd, float* sig, int warp, int lane) {
+    if (warp >= kMaxB) return;
+    const int col = warp;
+    const float* row = xf + (size_t)col * ldx;
+    const bool live = col < valid;
+    float m = 0.0f;
+    for (int k = 4 * lane; k < K; k += 128) {
+        if (live) {
+            const float4 v = *reinterpret_cast<const float4*>(row + k);
+            m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+        }
+    }
 #pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-        float sg, inv;
-        digit_scale(m, sg, inv);
-        if (lane == 0) sig[col * NG + grp] = sg;
+    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    float sg, inv;
+    digit_scale(m, sg, inv);
+    if (lane == 0) sig[col] = sg;
+    for (int k = 4 * lane; k < K; k += 128) {
+        const float4 v = live ? *reinterpret_cast<const float4*>(row + k) : make_float4(0.f, 0.f, 0.f, 0.f);
         int d[4][3];
         to_digits(v.x, inv, d[0][0], d[0][1], d[0][2]);
         to_digits(v.y, inv, d[1][0], d[1][1], d[1][2]);
         to_digits(v.z, inv, d[2][0], d[2][1], d[2][2]);
         to_digits(v.w, inv, d[3][0], d[3][1], d[3][2]);
-        // values k = 128 grp + 4 lane .. + 3: k-step 4 grp + lane / 8, bytes 4 (lane % 8) of it,
-        // i.e. fragment lane 4 col + (lane % 8) / 2, half lane % 2
-        const int s = grp * 4 + (lane >> 3), fl = 4 * col + ((lane & 7) >> 1), half = lane & 1;
+        // values k..k+3 sit in k-step k / 32 at bytes k % 32: fragment lane 4 col + (k % 32) / 8,
+        // half (k % 8) / 4
+        const int s = k >> 5, fl = 4 * col + ((k & 31) >> 3), half = (k & 7) >> 2;
 #pragma unroll
         for (int q = 0; q < 3; ++q)
             xd[((s * 3 + q) * 32 + fl) * 2 + half] = pack_s8x4(d[0][q], d[1][q], d[2][q], d[3][q]);
@@ -298,67 +305,36 @@ struct RouteSmem {
     unsigned used[2];
 };
 
-// MoEGate (decoder.py:500-514) for the B tokens of xs, in the oracle's fp32 order: logit =
-// 8 segments of H/8, each an fma chain in ascending k from +0, summed in ascending order, +
-// bias; softmax with this build's exponential and a fixed butterfly sum; top-k by (p desc,
-// index asc). Warp w computes segment w of every expert for every token (lane: experts lane
-// and lane + 32). `part` is >= 8 * kMaxB * 64 floats of scratch. Then the slot table: routed
-// slot u is the u-th used expert; its rows start after the shared experts' S * B rows.
-// CTA 0 also writes ids / wts and the global RouteTable (read by K3).
-UOCR_DEV void cta_route(const DecodeArgs& a, const float* xs, int ldx, float* part, RouteSmem* rs, SlotTable* tb,
-                       int tid) {
+// The rest of MoEGate (decoder.py:500-514) for the B tokens, after K1's logits: softmax with
+// this build's exponential and a fixed butterfly sum, top-k by (p desc, index asc), identical
+// in every CTA. Then the slot table: routed slot u is the u-th used expert; its rows start after
+// the shared experts' S * B rows. CTA 0 also writes ids / wts and the global RouteTable (read
+// by K3). The tokens are staged into xs on the way (rows B..7 zero) for the activation digits.
+UOCR_DEV void cta_route(const DecodeArgs& a, float* xs, int ldx, RouteSmem* rs, SlotTable* tb, int tid,
+                        unsigned long long* ev) {
     const int warp = tid >> 5, lane = tid & 31;
-    const int H = a.H, L = H / 8, B = a.B, E = a.E, k = a.topk;
-    {
-        const int s = warp;
-        float acc[2][kMaxB];
+    const int H = a.H, B = a.B, E = a.E, k = a.topk;
+    unsigned long long* rv = a.trace ? trace_rec(a, 0, a.trace_items / 2 - 2) : nullptr;  // diagnostics
+    pdl_wait_prior_grid();  // the logits (K1), and through K1 the previous layer's output x
+    if (ev && tid == 0) ev[1] = global_timer_ns();
+    // the logits, and the tokens (for the activation digits): every load of a batch issued before its stores
+    for (int i = tid; i < B * 64; i += kCW * 32) rs->logits[i >> 6][i & 63] = __ldcg(a.logits + i);
+    for (int i0 = 0; i0 < kMaxB * (H / 4); i0 += 10 * kCW * 32) {
+        float4 v[10];
 #pragma unroll
-        for (int t = 0; t < kMaxB; ++t) acc[0][t] = acc[1][t] = 0.0f;
-        const bool v0 = lane < E, v1 = lane + 32 < E;
-        const uint16_t* w0 = a.router + (size_t)(v0 ? lane : 0) * H + s * L;
-        const uint16_t* w1 = a.router + (size_t)(v1 ? lane + 32 : 0) * H + s * L;
-        const uint32_t xs_s = smem_addr(xs) + 4u * (uint32_t)(s * L);
-        for (int kk = 0; kk < L; kk += 8) {
-            float f0[8], f1[8];
-            unpack_bf16x8(ldg_nc_v4(w0 + kk), f0);
-            unpack_bf16x8(ldg_nc_v4(w1 + kk), f1);
-#pragma unroll
-            for (int t = 0; t < kMaxB; ++t) {
-                if (t < B) {
-                    const uint32_t xr = xs_s + 4u * (uint32_t)(t * ldx + kk);
-                    const float4 xa = lds_f128(xr), xb = lds_f128(xr + 16);
-                    const float x8[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-                    float u0 = acc[0][t], u1 = acc[1][t];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        u0 = __fmaf_rn(f0[i], x8[i], u0);
-                        u1 = __fmaf_rn(f1[i], x8[i], u1);
-                    }
-                    acc[0][t] = u0;
-                    acc[1][t] = u1;
-                }
-            }
+        for (int j = 0; j < 10; ++j) {
+            const int i = i0 + j * kCW * 32 + tid;
+            v[j] = (i < kMaxB * (H / 4) && i / (H / 4) < B) ? __ldcg(reinterpret_cast<const float4*>(a.x) + i)
+                                                            : make_float4(0.f, 0.f, 0.f, 0.f);
         }
 #pragma unroll
-        for (int t = 0; t < kMaxB; ++t) {
-            if (t < B) {
-                part[(s * kMaxB + t) * 64 + lane] = acc[0][t];
-                part[(s * kMaxB + t) * 64 + lane + 32] = acc[1][t];
-            }
+        for (int j = 0; j < 10; ++j) {
+            const int i = i0 + j * kCW * 32 + tid;
+            if (i < kMaxB * (H / 4)) *reinterpret_cast<float4*>(xs + (size_t)(i / (H / 4)) * ldx + 4 * (i % (H / 4))) = v[j];
         }
     }
     named_bar_sync(kBarConsumers, kCW * 32);
-    for (int i = tid; i < B * 64; i += kCW * 32) {
-        const int t = i >> 6, e = i & 63;
-        if (e < E) {
-            float total = part[t * 64 + e];
-#pragma unroll
-            for (int s = 1; s < 8; ++s) total = __fadd_rn(total, part[(s * kMaxB + t) * 64 + e]);
-            if (a.bias) total = __fadd_rn(total, a.bias[e]);
-            rs->logits[t][e] = total;
-        }
-    }
-    named_bar_sync(kBarConsumers, kCW * 32);
+    if (rv && tid == 0) rv[0] = global_timer_ns();
     // softmax + top-k: warp b serves token b
     if (warp < B) {
         const int b = warp;
@@ -398,6 +374,7 @@ UOCR_DEV void cta_route(const DecodeArgs& a, const float* xs, int ldx, float* pa
         }
     }
     named_bar_sync(kBarConsumers, kCW * 32);
+    if (rv && tid == 0) rv[3] = global_timer_ns();
     // group by expert (threads 0..63 = experts)
     const int kB = k * B;
     int c = 0;
@@ -408,6 +385,7 @@ UOCR_DEV void cta_route(const DecodeArgs& a, const float* xs, int ldx, float* pa
         if (lane == 0) rs->used[warp] = bal;
     }
     named_bar_sync(kBarConsumers, kCW * 32);
+    if (rv && tid == 0) rv[4] = global_timer_ns();
     const unsigned long long used = (unsigned long long)rs->used[0] | ((unsigned long long)rs->used[1] << 32);
     RouteTable* g = a.table;
     const bool pub = blockIdx.x == 0;  // CTA 0 publishes the table for K3
@@ -445,6 +423,7 @@ UOCR_DEV void cta_route(const DecodeArgs& a, const float* xs, int ldx, float* pa
         if (pub) g->U = __popcll(used);
     }
     named_bar_sync(kBarConsumers, kCW * 32);
+    if (rv && tid == 0) rv[5] = global_timer_ns();
     if (pub && tid < B) {
         // token tid's routed rows in ascending expert id (the combine's order)
         int ord[kDecodeMaxTopk];
@@ -461,9 +440,8 @@ UOCR_DEV void cta_route(const DecodeArgs& a, const float* xs, int ldx, float* pa
             g->tok_w[tid][s] = rs->wts[tid * k + ord[s]];
         }
     }
-    // `part` lives in a stage buffer the producer fills next with the async proxy
-    fence_proxy_async_smem();
     named_bar_sync(kBarConsumers, kCW * 32);
+    if (rv && tid == 0) rv[6] = global_timer_ns();
 }
 
 // Weighted static partition: the items of slots [first, last) in order, item cost c(slot);
@@ -487,6 +465,76 @@ UOCR_DEV void slot_range(long long pre, long long c, int n, const Partition& p, 
     long long s1 = b <= 0 ? 0 : (b + c - 1) / c;
     j0 = (int)(s0 < n ? s0 : n);
     j1 = (int)(s1 < n ? s1 : n);
+}
+
+// ======================================================================================
+// K1: router logits
+// ======================================================================================
+// CTA e computes expert e's logits for the B tokens: thread (segment s, token t) runs the
+// oracle's chain over segment s (fma in ascending k from +0); the 8 segment sums are added in
+// ascending order, then the bias. The router row is fetched before the dependency wait; the
+// CTA is small (64 threads, 256 B of shared memory) so it fits beside the other kernels' CTAs.
+constexpr int kLogitSteps = 20;  // 8-element steps per segment held in registers (H <= 1280)
+
+__global__ void __launch_bounds__(64)
+decode_logits_kernel(DecodeArgs a) {
+    __shared__ float part[8][kMaxB];
+    const int e = blockIdx.x, s = threadIdx.x >> 3, t = threadIdx.x & 7;
+    const int H = a.H, L = H / 8, nit = L / 8;
+    const uint16_t* w = a.router + (size_t)e * H + s * L;
+    uint4 r[kLogitSteps];
+#pragma unroll
+    for (int i = 0; i < kLogitSteps; ++i)
+        if (i < nit) r[i] = ldg_nc_v4(w + 8 * i);
+    pdl_launch_dependents();  // K2 launches now; it waits for this grid before it reads the logits
+    pdl_wait_prior_grid();    // x is the previous layer's output
+    float acc = 0.0f;
+    if (t < a.B) {
+        const float* x = a.x + (size_t)t * H + s * L;
+        if (nit <= kLogitSteps) {
+#pragma unroll
+            for (int half = 0; half < 2; ++half) {
+                constexpr int kHalf = kLogitSteps / 2;
+                float4 xv[2 * kHalf];  // this half's 8-element steps of x, all loads issued first
+#pragma unroll
+                for (int i = 0; i < kHalf; ++i) {
+                    const int q = half * kHalf + i;
+                    if (q < nit) {
+                        xv[2 * i] = __ldcg(reinterpret_cast<const float4*>(x + 8 * q));
+                        xv[2 * i + 1] = __ldcg(reinterpret_cast<const float4*>(x + 8 * q + 4));
+                    }
+                }
+#pragma unroll
+                for (int i = 0; i < kHalf; ++i) {
+                    const int q = half * kHalf + i;
+                    if (q < nit) {
+                        float f[8];
+                        unpack_bf16x8(r[q], f);
+                        const float x8[8] = {xv[2 * i].x,     xv[2 * i].y,     xv[2 * i].z,     xv[2 * i].w,
+                                             xv[2 * i + 1].x, xv[2 * i + 1].y, xv[2 * i + 1].z, xv[2 * i + 1].w};
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) acc = __fmaf_rn(f[j], x8[j], acc);
+                    }
+                }
+            }
+        } else {
+            for (int kk = 0; kk < L; kk += 8) {
+                float f[8];
+                unpack_bf16x8(ldg_nc_v4(w + kk), f);
+#pragma unroll
+                for (int j = 0; j < 8; ++j) acc = __fmaf_rn(f[j], __ldcg(x + kk + j), acc);
+            }
+        }
+    }
+    part[s][t] = acc;
+    __syncthreads();
+    if (s == 0 && t < a.B) {
+        float total = part[0][t];
+#pragma unroll
+        for (int q = 1; q < 8; ++q) total = __fadd_rn(total, part[q][t]);
+        if (a.bias) total = __fadd_rn(total, a.bias[e]);
+        a.logits[t * 64 + e] = total;
+    }
 }
 
 // ======================================================================================
@@ -587,6 +635,10 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
     unsigned char* stages = smem + off_stages;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int ldx = a.H + 4;
+    // diagnostics: kernel-level events of this CTA (start, consumers past the dependency wait,
+    // routed, fragments loaded, consumers done)
+    unsigned long long* ev = a.trace ? trace_rec(a, 0, a.trace_items / 2 - 1) : nullptr;
+    if (ev && tid == 0) ev[0] = global_timer_ns();
     if (tid == 0) {
         for (int s = 0; s < nst; ++s) {
             mbar_init(&full[s], 1);
@@ -613,8 +665,6 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             }
         };
         auto issue = [&](int slot, int blk) {
-            // the last stage doubles as the routing scratch until the table is ready
-            if (round == 0 && st == nst - 1) wait_table();
             if (ok && round > 0 && !mbar_wait_warp(&empty[st], (round - 1) & 1, &abort_flag, &a.ctl->status))
                 ok = false;
             if (!ok) return;
@@ -669,28 +719,23 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
         __syncwarp();
     } else {
         // ---------------- consumers: route, stage the digits, then the items ----------------
-        // the tokens (complete once the previous layer's grid is); rows B..7 stay zero
-        pdl_wait_prior_grid();
-        for (int i = tid; i < kMaxB * (a.H / 4); i += kCW * 32) {
-            const int t = i / (a.H / 4), c4 = i % (a.H / 4);
-            const float4 v = t < a.B ? __ldcg(reinterpret_cast<const float4*>(a.x) + i) : make_float4(0.f, 0.f, 0.f, 0.f);
-            *reinterpret_cast<float4*>(xf + (size_t)t * ldx + 4 * c4) = v;
-        }
-        named_bar_sync(kBarConsumers, kCW * 32);
-        cta_route(a, xf, ldx, reinterpret_cast<float*>(stages + (size_t)(nst - 1) * stage_bytes), rs, tb, tid);
+        cta_route(a, xf, ldx, rs, tb, tid, ev);
         if (tid == 0) mbar_arrive(table_ready);
+        if (ev && tid == 0) ev[2] = global_timer_ns();
         if (a.int8) {
-            stage_digits(xf, ldx, a.H, a.B, xd, xsig, warp, lane, kCW);
+            stage_digits(xf, ldx, a.H, a.B, xd, xsig, warp, lane);
             named_bar_sync(kBarConsumers, kCW * 32);
         }
+        if (ev && tid == 0) ev[5] = global_timer_ns();
         const uint32_t xf_s = smem_addr(xf), xd_s = smem_addr(xd);
         // this warp's activation fragments, fixed for the CTA
         const int nks = a.H / 128;
         const bool reg = nks <= kK2RegSteps;
         FragS8<kK2RegSteps> f8;
         FragBf16<kK2RegSteps> f16;
-        if (kI8L && reg) load_frag_s8<kK2RegSteps>(f8, xd_s, xsig, nks, (warp & 3) * nks, nks, lane);
+        if (kI8L && reg) load_frag_s8<kK2RegSteps>(f8, xd_s, xsig, (warp & 3) * nks, nks, lane);
         if (!kI8L && reg) load_frag_bf16<kK2RegSteps>(f16, xf_s, ldx, warp * nks, nks, lane);
+        if (ev && tid == 0) ev[3] = global_timer_ns();
         // Item n: products, stage release, partial tile stored; then item n-1 is finished (its
         // partial tiles are complete once every warp has arrived) and item n's buffer released.
         int pend_slot = -1, pend_blk = 0, pend_n = 0;
@@ -737,6 +782,7 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             pend_n = n;
         }
         if (ok && pend_slot >= 0) finish_pending();
+        if (ev && tid == 0) ev[4] = global_timer_ns();
     }
 }
 
@@ -767,18 +813,42 @@ UOCR_DEV void dn_finish(const DecodeArgs& a, const SlotTable& tb, int slot, int 
     a.y[(size_t)(tb.base[slot] + n) * a.H + blk * kW2Rows + row] = y;
 }
 
-// Rows [r0, r0 + 4) are complete over all slots: lane (t, r) sums token t's shared rows, then its
-// routed rows in ascending expert id (w * y). (The token lists come from the global table.)
-UOCR_DEV void combine_rows(const DecodeArgs& a, int r0, int lane) {
-    const int t = lane >> 2, r = r0 + (lane & 3);
+// Completed 4-row groups g[0..ng) (each complete over all slots): lane (t, r) sums, for every
+// group, token t's shared rows, then its routed rows in ascending expert id (w * y). trow/tw are
+// token t's routed rows and weights (from K2's table, held by the lane). Four groups at a time,
+// every load issued before the sums.
+UOCR_DEV void combine_groups(const DecodeArgs& a, const int* g, int ng, const int (&trow)[kDecodeMaxTopk],
+                             const float (&tw)[kDecodeMaxTopk], int lane) {
+    const int t = lane >> 2;
     if (t >= a.B) return;
-    float acc = 0.0f;
-    for (int q = 0; q < a.S; ++q) acc = __fadd_rn(acc, __ldcg(a.y + (size_t)(q * a.B + t) * a.H + r));
-    for (int s = 0; s < a.topk; ++s) {
-        const int row = __ldcg(&a.table->tok_row[t][s]);
-        acc = __fmaf_rn(__ldcg(&a.table->tok_w[t][s]), __ldcg(a.y + (size_t)row * a.H + r), acc);
+    for (int b = 0; b < ng; b += 4) {
+        float ys[4][kDecodeMaxShared], yr[4][kDecodeMaxTopk];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (b + i < ng) {
+                const int r = g[b + i] * 4 + (lane & 3);
+#pragma unroll
+                for (int q = 0; q < kDecodeMaxShared; ++q)
+                    if (q < a.S) ys[i][q] = __ldcg(a.y + (size_t)(q * a.B + t) * a.H + r);
+#pragma unroll
+                for (int s = 0; s < kDecodeMaxTopk; ++s)
+                    if (s < a.topk) yr[i][s] = __ldcg(a.y + (size_t)trow[s] * a.H + r);
+            }
+        }
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            if (b + i < ng) {
+                float acc = 0.0f;
+#pragma unroll
+                for (int q = 0; q < kDecodeMaxShared; ++q)
+                    if (q < a.S) acc = __fadd_rn(acc, ys[i][q]);
+#pragma unroll
+                for (int s = 0; s < kDecodeMaxTopk; ++s)
+                    if (s < a.topk) acc = __fmaf_rn(tw[s], yr[i][s], acc);
+                a.out[(size_t)t * a.H + g[b + i] * 4 + (lane & 3)] = acc;
+            }
+        }
     }
-    a.out[(size_t)t * a.H + r] = acc;
 }
 
 // K3 warps keep the current run's h fragments in registers for I up to 128 * kK3RegS8 (int8)
@@ -806,6 +876,8 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
     unsigned char* ring = smem + off_ring;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int nblk = a.H / kW2Rows, ldh = a.I + 4;
+    unsigned long long* ev = a.trace ? trace_rec(a, 1, a.trace_items / 2 - 1) : nullptr;
+    if (ev && tid == 0) ev[0] = global_timer_ns();
     if (tid == 0) {
         for (int s = 0; s < kK3Desc; ++s) {
             mbar_init(&full[s], 1);
@@ -833,6 +905,7 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
         uint32_t head = 0;
         bool ok = true;
         pdl_wait_prior_grid();  // h and the routing table come from K2
+        if (ev && lane == 0) ev[1] = global_timer_ns();
         load_routed_slots(tb, a, lane);
         auto items = [&](int) { return nblk; };
         auto cost = [&](int s) { return dn_cost(a, *tb, s); };
@@ -919,30 +992,56 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
         __syncwarp();
     } else if (warp == kCW + 1) {
         // ---------------- publisher: count finished row groups, combine completed ones ----------------
-        // One fence per item publishes the consumers' y rows (ordered before it by the done
-        // barrier) device-wide before they are counted.
+        // One fence per batch of finished items publishes the consumers' y rows (ordered before
+        // it by the done barriers) device-wide before they are counted.
         pdl_wait_prior_grid();
         const unsigned nslot_all = (unsigned)(a.S + __ldcg(&a.table->U));
-        for (int m = 0;; ++m) {
-            const int d = m % kK3Desc;
-            if (!mbar_wait_warp(&done[d], (m / kK3Desc) & 1, &abort_flag, &a.ctl->status)) break;
-            const int slot = meta[d].slot, blk = meta[d].blk;
-            if (slot < 0) break;
-            __threadfence();
-            const bool last = lane < kCW && atomicAdd(&a.row_done[blk * kCW + lane], 1u) == nslot_all - 1;
-            unsigned mask = __ballot_sync(0xffffffffu, last);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[d]);
-            if (mask) __threadfence();
-            while (mask) {
-                const int w = __ffs(mask) - 1;
-                mask &= mask - 1;
-                const int g = blk * kCW + w;
-                combine_rows(a, g * 4, lane);
-                __syncwarp();
-                if (lane == 0) a.row_done[g] = 0;  // counters are left zeroed for the next launch
+        int trow[kDecodeMaxTopk];
+        float tw[kDecodeMaxTopk];
+        {
+            const int t = min(lane >> 2, a.B - 1);
+#pragma unroll
+            for (int s = 0; s < kDecodeMaxTopk; ++s) {
+                trow[s] = s < a.topk ? __ldcg(&a.table->tok_row[t][s]) : 0;
+                tw[s] = s < a.topk ? __ldcg(&a.table->tok_w[t][s]) : 0.0f;
             }
         }
+        constexpr int kBatch = 4;  // items per fence at most
+        int groups[kBatch * kCW];
+        bool end = false;
+        for (int m = 0; !end;) {
+            if (!mbar_wait_warp(&done[m % kK3Desc], (m / kK3Desc) & 1, &abort_flag, &a.ctl->status)) break;
+            int c = 1;  // further finished items, without waiting
+            while (c < kBatch && __all_sync(0xffffffffu, mbar_try_wait(&done[(m + c) % kK3Desc], ((m + c) / kK3Desc) & 1)))
+                ++c;
+            __threadfence();
+            int ng = 0;
+            for (int j = 0; j < c; ++j) {
+                const int d = (m + j) % kK3Desc;
+                const int slot = meta[d].slot, blk = meta[d].blk;
+                if (slot < 0) {
+                    end = true;
+                    break;
+                }
+                const bool last = lane < kCW && atomicAdd(&a.row_done[blk * kCW + lane], 1u) == nslot_all - 1;
+                unsigned mask = __ballot_sync(0xffffffffu, last);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[d]);
+                while (mask) {
+                    groups[ng++] = blk * kCW + __ffs(mask) - 1;
+                    mask &= mask - 1;
+                }
+            }
+            if (ng) {
+                __threadfence();
+                combine_groups(a, groups, ng, trow, tw, lane);
+                __syncwarp();
+                if (lane < ng) a.row_done[groups[lane]] = 0;  // counters are left zeroed for the next launch
+                for (int i = lane + 32; i < ng; i += 32) a.row_done[groups[i]] = 0;
+            }
+            m += c;
+        }
+        if (ev && lane == 0) ev[3] = global_timer_ns();
     } else {
         // ---------------- consumers ----------------
         const uint32_t hf_s = smem_addr(hf), hd_s = smem_addr(hd);
@@ -1007,7 +1106,7 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
                 }
                 ++runs;
                 if (i8) {
-                    stage_digits(hf, ldh, a.I, cnt, hd, hsig, warp, lane, kCW);
+                    stage_digits(hf, ldh, a.I, cnt, hd, hsig, warp, lane);
                     __syncwarp();
                     if (lane == 0) mbar_arrive(&hbar[runs & 1]);
                     if (!mbar_wait_warp(&hbar[runs & 1], (runs >> 1) & 1, &abort_flag, &a.ctl->status)) {
@@ -1015,7 +1114,7 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
                         break;
                     }
                     ++runs;
-                    if (kI8L && reg8) load_frag_s8<kK3RegS8>(f8, hd_s, hsig, a.I / 128, q * n8, n8, lane);
+                    if (kI8L && reg8) load_frag_s8<kK3RegS8>(f8, hd_s, hsig, q * n8, n8, lane);
                 } else if (!kI8L && reg16) {
                     load_frag_bf16<kK3RegBf16>(f16, hf_s, ldh, q * n16, n16, lane);
                 }
@@ -1052,6 +1151,7 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
             pend_n = n;
             pend_d = d;
         }
+        if (ev && tid == 0) ev[2] = global_timer_ns();
     }
 }
 
@@ -1079,20 +1179,28 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
     int dev = 0, max_smem = 0, sms = 0;
     cudaError_t err = cudaGetDevice(&dev);
     if (err != cudaSuccess) return err;
+    int sm_smem = 0;
     cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
+    cudaDeviceGetAttribute(&sm_smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    max_smem -= 1024;  // the kernels' static shared memory (a few words) comes out of the same budget
+    // K2 / K3 leave room on their SM for their own static shared memory (a few words) and their
+    // reservation, and for one K1 CTA (256 B + reservation), so K1 can start beside them
+    max_smem = std::min(max_smem - 1024, sm_smem - 1024 - 1024 - (1024 + 256));
     if (g_decode_trace) {
         a.trace = g_decode_trace;
         a.trace_items = (int)(g_decode_trace_bytes / (sizeof(unsigned long long) * 8 * (size_t)sms)) & ~1;
     }
 
-    // ---- K2: route + gate/up; a stage holds one w13 block (the last one also the routing scratch)
+    // ---- K1: logits, one CTA per routed expert
+    {
+        void* args[] = {&a};
+        err = launch_pdl(reinterpret_cast<const void*>(decode_logits_kernel), dim3(a.E), dim3(64), 0, st, args);
+        if (err != cudaSuccess) return err;
+    }
+    // ---- K2: route + gate/up; a stage holds one w13 block
     {
         uint32_t stage_bytes = (uint32_t)up(
-            std::max({w13_block_bytes(a.H, a.G, false), a.int8 ? w13_block_bytes(a.H, a.G, true) : size_t(0),
-                      sizeof(float) * 8 * kMaxB * 64}),
-            128);
+            std::max(w13_block_bytes(a.H, a.G, false), a.int8 ? w13_block_bytes(a.H, a.G, true) : size_t(0)), 128);
         const size_t off_tbl = 256;
         const size_t off_route = off_tbl + up(sizeof(SlotTable), 128);
         const size_t off_meta = off_route + up(sizeof(RouteSmem), 128);

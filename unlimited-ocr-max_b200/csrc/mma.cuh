@@ -5,9 +5,9 @@
 // unpack and multiply-add work.
 //
 // Exact activations. fp32 activations are given to the s8 product as three int8 digits per
-// value with a power-of-two scale per (token, 128-group): v = sigma * (d0 + d1 / 128 + d2 / 128^2),
-// |d| <= 64, accumulated in int32 (exact) and recombined in fp32 after each group, before the
-// group's weight scale; the representation error is below 2^-21 of the group's largest value.
+// value with a power-of-two scale per token: v = sigma * (d0 + d1 / 128 + d2 / 128^2), |d| <= 64,
+// accumulated in int32 (exact) and recombined in fp32 after each 128-group, before the group's
+// weight scale; the representation error is below 2^-21 of the token's largest value.
 // To the bf16 product they are given as three bf16 terms v = t0 + t1 + t2 (t0 = bf16(v),
 // t1 = bf16(v - t0), t2 = bf16(v - t0 - t1)), exact to ~2^-24.
 //
