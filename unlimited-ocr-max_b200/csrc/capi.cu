@@ -269,7 +269,7 @@ int uocr_moe_route(const float* x, int64_t T, int64_t H, const uint16_t* router,
 namespace {
 
 struct DecodeLayout {
-    size_t ctl, row_done, logits, table, ids, wts, h, y, total;
+    size_t ctl, logits, table, ids, wts, h, y, total;
 };
 
 DecodeLayout decode_layout(const uocr_moe_layer* L, int64_t B) {
@@ -277,7 +277,6 @@ DecodeLayout decode_layout(const uocr_moe_layer* L, int64_t B) {
     const size_t pairs = (size_t)(L->top_k + L->n_shared) * (size_t)B;
     size_t off = 0;
     d.ctl = off; off += align256(sizeof(uocr::DecodeCtl));
-    d.row_done = off; off += align256(sizeof(uint32_t) * (size_t)(L->hidden / 4));
     d.logits = off; off += align256(sizeof(float) * 8 * 64);
     d.table = off; off += align256(sizeof(uocr::RouteTable));
     d.ids = off; off += align256(sizeof(int32_t) * (size_t)B * L->top_k);
@@ -340,7 +339,6 @@ int uocr_moe_decode(const uocr_moe_layer* L, const float* x, int64_t B, const fl
     a.wts = wts_out ? wts_out : reinterpret_cast<float*>(ws + d.wts);
     a.w13 = L->w13; a.w2 = L->w2;
     a.w13_shared = L->w13_shared; a.w2_shared = L->w2_shared;
-    a.row_done = reinterpret_cast<uint32_t*>(ws + d.row_done);
     a.h = reinterpret_cast<float*>(ws + d.h);
     a.y = reinterpret_cast<float*>(ws + d.y);
     a.out = out;

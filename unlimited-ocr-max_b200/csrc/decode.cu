@@ -10,9 +10,9 @@
 //              expert ("slots": 0..S-1 the shared experts, S+u the u-th distinct routed expert in
 //              ascending id), each slot owning contiguous rows of the h and y scratch.
 //              Items (slot, block of 8 or 16 row pairs) -> h[slot row][n] = silu(g) * u.
-//   K3 down + combine    items (slot, 32 output rows) -> y[slot row][j]; a publisher warp counts
-//              finished 4-row groups (a self-resetting counter per group) and the one that
-//              completes a group sums it over each token's slots in a fixed order: out[t][j].
+//   K3 down + combine    items (slot, 32 output rows) -> y[slot row][j]; then a grid barrier
+//              (K3's CTAs, one per SM, are all resident) and every CTA sums its 1/grid slice of
+//              the B x H outputs over each token's slots in a fixed order: out[t][j].
 // A slot's arithmetic uses only its own token rows, and each output sums a token's slots in
 // ascending order, so every output row is bitwise independent of the batch.
 //
@@ -40,7 +40,6 @@ constexpr int kThreads = (kCW + 1) * 32;     // + producer warp
 constexpr int kMaxB = 8;
 constexpr int kMaxSlotsSm = 72;              // shared (<= 8) + routed (<= 64)
 constexpr int kK3Desc = 8;                   // K3 items in flight (descriptor ring)
-constexpr int kThreads3 = kThreads + 32;     // K3: + publisher warp
 constexpr uint32_t kBarConsumers = 1;        // named barrier of the 8 consumer warps
 
 // Slots of this step in shared memory: rows [0, S) the shared experts, [S, S+U) routed.
@@ -486,8 +485,12 @@ decode_logits_kernel(DecodeArgs a) {
 #pragma unroll
     for (int i = 0; i < kLogitSteps; ++i)
         if (i < nit) r[i] = ldg_nc_v4(w + 8 * i);
+    // diagnostics: start, past the dependency wait, done
+    unsigned long long* ev = a.trace ? trace_rec(a, 1, a.trace_items / 2 - 2) : nullptr;
+    if (ev && threadIdx.x == 0) ev[0] = global_timer_ns();
     pdl_launch_dependents();  // K2 launches now; it waits for this grid before it reads the logits
     pdl_wait_prior_grid();    // x is the previous layer's output
+    if (ev && threadIdx.x == 0) ev[1] = global_timer_ns();
     float acc = 0.0f;
     if (t < a.B) {
         const float* x = a.x + (size_t)t * H + s * L;
@@ -535,6 +538,7 @@ decode_logits_kernel(DecodeArgs a) {
         if (a.bias) total = __fadd_rn(total, a.bias[e]);
         a.logits[t * 64 + e] = total;
     }
+    if (ev && threadIdx.x == 0) ev[2] = global_timer_ns();
 }
 
 // ======================================================================================
@@ -813,41 +817,31 @@ UOCR_DEV void dn_finish(const DecodeArgs& a, const SlotTable& tb, int slot, int 
     a.y[(size_t)(tb.base[slot] + n) * a.H + blk * kW2Rows + row] = y;
 }
 
-// Completed 4-row groups g[0..ng) (each complete over all slots): lane (t, r) sums, for every
-// group, token t's shared rows, then its routed rows in ascending expert id (w * y). trow/tw are
-// token t's routed rows and weights (from K2's table, held by the lane). Four groups at a time,
-// every load issued before the sums.
-UOCR_DEV void combine_groups(const DecodeArgs& a, const int* g, int ng, const int (&trow)[kDecodeMaxTopk],
-                             const float (&tw)[kDecodeMaxTopk], int lane) {
-    const int t = lane >> 2;
-    if (t >= a.B) return;
-    for (int b = 0; b < ng; b += 4) {
-        float ys[4][kDecodeMaxShared], yr[4][kDecodeMaxTopk];
+// This CTA's share of the outputs, after every CTA's items (grid barrier): out[t][j] for the
+// flat indices [lo, hi) of the B x H output, one per thread: token t's shared rows in order,
+// then its routed rows in ascending expert id (w * y), from the slot table's row lists.
+UOCR_DEV void combine_slice(const DecodeArgs& a, const int (&trow)[kMaxB][kDecodeMaxTopk],
+                            const float (&tw)[kMaxB][kDecodeMaxTopk], int tid) {
+    const int total = a.B * a.H;
+    const int lo = (int)((long long)total * blockIdx.x / gridDim.x);
+    const int hi = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
+    for (int o = lo + tid; o < hi; o += blockDim.x) {
+        const int t = o / a.H, j = o - t * a.H;
+        float ys[kDecodeMaxShared], yr[kDecodeMaxTopk];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            if (b + i < ng) {
-                const int r = g[b + i] * 4 + (lane & 3);
+        for (int q = 0; q < kDecodeMaxShared; ++q)
+            if (q < a.S) ys[q] = __ldcg(a.y + (size_t)(q * a.B + t) * a.H + j);
 #pragma unroll
-                for (int q = 0; q < kDecodeMaxShared; ++q)
-                    if (q < a.S) ys[i][q] = __ldcg(a.y + (size_t)(q * a.B + t) * a.H + r);
+        for (int s = 0; s < kDecodeMaxTopk; ++s)
+            if (s < a.topk) yr[s] = __ldcg(a.y + (size_t)trow[t][s] * a.H + j);
+        float acc = 0.0f;
 #pragma unroll
-                for (int s = 0; s < kDecodeMaxTopk; ++s)
-                    if (s < a.topk) yr[i][s] = __ldcg(a.y + (size_t)trow[s] * a.H + r);
-            }
-        }
+        for (int q = 0; q < kDecodeMaxShared; ++q)
+            if (q < a.S) acc = __fadd_rn(acc, ys[q]);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            if (b + i < ng) {
-                float acc = 0.0f;
-#pragma unroll
-                for (int q = 0; q < kDecodeMaxShared; ++q)
-                    if (q < a.S) acc = __fadd_rn(acc, ys[i][q]);
-#pragma unroll
-                for (int s = 0; s < kDecodeMaxTopk; ++s)
-                    if (s < a.topk) acc = __fmaf_rn(tw[s], yr[i][s], acc);
-                a.out[(size_t)t * a.H + g[b + i] * 4 + (lane & 3)] = acc;
-            }
-        }
+        for (int s = 0; s < kDecodeMaxTopk; ++s)
+            if (s < a.topk) acc = __fmaf_rn(tw[t][s], yr[s], acc);
+        a.out[o] = acc;
     }
 }
 
@@ -856,15 +850,16 @@ UOCR_DEV void combine_groups(const DecodeArgs& a, const int* g, int ng, const in
 constexpr int kK3RegS8 = 8, kK3RegBf16 = 14;
 
 template <bool kI8L>
-__global__ void __launch_bounds__(kThreads3, 1)
+__global__ void __launch_bounds__(kThreads, 1)
 decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t off_meta, uint32_t off_dn,
                    uint32_t off_hf, uint32_t off_hd, uint32_t off_sig, uint32_t off_ring) {
     extern __shared__ __align__(16) unsigned char smem[];
-    __shared__ int abort_flag;
+    __shared__ int abort_flag, bar_ok;
+    __shared__ int trow[kMaxB][kDecodeMaxTopk];
+    __shared__ float tw[kMaxB][kDecodeMaxTopk];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* done = full + kK3Desc;     // consumers: the item's y rows are written
-    uint64_t* freed = done + kK3Desc;    // consumers: the item's ring bytes are no longer read
-    uint64_t* empty = freed + kK3Desc;   // publisher: the descriptor is no longer read
+    uint64_t* freed = full + kK3Desc;    // consumers: the item's ring bytes are no longer read
+    uint64_t* empty = freed + kK3Desc;   // consumers: the item is finished, its descriptor free
     uint64_t* redbar = empty + kK3Desc;     // [kRedBufs]
     uint64_t* hbar = redbar + kRedBufs;     // [2]: the run's h staged by all warps
     SlotTable* tb = reinterpret_cast<SlotTable*>(smem + off_tbl);
@@ -881,9 +876,8 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
     if (tid == 0) {
         for (int s = 0; s < kK3Desc; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&done[s], kCW);
             mbar_init(&freed[s], kCW);
-            mbar_init(&empty[s], 1);
+            mbar_init(&empty[s], kCW);
         }
         for (int s = 0; s < kRedBufs; ++s) mbar_init(&redbar[s], kCW);
         for (int s = 0; s < 2; ++s) mbar_init(&hbar[s], kCW);
@@ -898,7 +892,7 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
         // ---------------- producer ----------------
         // Items are placed back to back in the ring (wrapping to 0 when one does not fit). Ring
         // bytes retire in order as the consumers finish their products (`freed`); descriptors
-        // retire in order as the publisher finishes with them (`empty`). An item may be placed
+        // retire in order as the consumers finish the items (`empty`). An item may be placed
         // once its descriptor is free and no item still being read overlaps its bytes.
         uint32_t lo_b[kK3Desc], hi_b[kK3Desc];  // byte range of descriptor d's item
         int n = 0, oldest = 0, oldest_desc = 0;
@@ -990,58 +984,6 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
             }
         }
         __syncwarp();
-    } else if (warp == kCW + 1) {
-        // ---------------- publisher: count finished row groups, combine completed ones ----------------
-        // One fence per batch of finished items publishes the consumers' y rows (ordered before
-        // it by the done barriers) device-wide before they are counted.
-        pdl_wait_prior_grid();
-        const unsigned nslot_all = (unsigned)(a.S + __ldcg(&a.table->U));
-        int trow[kDecodeMaxTopk];
-        float tw[kDecodeMaxTopk];
-        {
-            const int t = min(lane >> 2, a.B - 1);
-#pragma unroll
-            for (int s = 0; s < kDecodeMaxTopk; ++s) {
-                trow[s] = s < a.topk ? __ldcg(&a.table->tok_row[t][s]) : 0;
-                tw[s] = s < a.topk ? __ldcg(&a.table->tok_w[t][s]) : 0.0f;
-            }
-        }
-        constexpr int kBatch = 4;  // items per fence at most
-        int groups[kBatch * kCW];
-        bool end = false;
-        for (int m = 0; !end;) {
-            if (!mbar_wait_warp(&done[m % kK3Desc], (m / kK3Desc) & 1, &abort_flag, &a.ctl->status)) break;
-            int c = 1;  // further finished items, without waiting
-            while (c < kBatch && __all_sync(0xffffffffu, mbar_try_wait(&done[(m + c) % kK3Desc], ((m + c) / kK3Desc) & 1)))
-                ++c;
-            __threadfence();
-            int ng = 0;
-            for (int j = 0; j < c; ++j) {
-                const int d = (m + j) % kK3Desc;
-                const int slot = meta[d].slot, blk = meta[d].blk;
-                if (slot < 0) {
-                    end = true;
-                    break;
-                }
-                const bool last = lane < kCW && atomicAdd(&a.row_done[blk * kCW + lane], 1u) == nslot_all - 1;
-                unsigned mask = __ballot_sync(0xffffffffu, last);
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[d]);
-                while (mask) {
-                    groups[ng++] = blk * kCW + __ffs(mask) - 1;
-                    mask &= mask - 1;
-                }
-            }
-            if (ng) {
-                __threadfence();
-                combine_groups(a, groups, ng, trow, tw, lane);
-                __syncwarp();
-                if (lane < ng) a.row_done[groups[lane]] = 0;  // counters are left zeroed for the next launch
-                for (int i = lane + 32; i < ng; i += 32) a.row_done[groups[i]] = 0;
-            }
-            m += c;
-        }
-        if (ev && lane == 0) ev[3] = global_timer_ns();
     } else {
         // ---------------- consumers ----------------
         const uint32_t hf_s = smem_addr(hf), hd_s = smem_addr(hd);
@@ -1051,8 +993,8 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
         const bool reg8 = n8 <= kK3RegS8, reg16 = n16 <= kK3RegBf16;
         FragS8<kK3RegS8> f8;
         FragBf16<kK3RegBf16> f16;
-        // As in K2: item n's products, then item n-1 is finished (y rows written, `done`
-        // arrived for the publisher), then item n's partial tile buffer is released.
+        // As in K2: item n's products, then item n-1 is finished (y rows written, its descriptor
+        // released), then item n's partial tile buffer is released.
         int pend_slot = -1, pend_blk = 0, pend_n = 0, pend_d = 0;
         bool ok = true;
         auto finish_pending = [&]() {
@@ -1061,7 +1003,7 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
             if (!ok) return;
             dn_finish(a, *tb, pend_slot, pend_blk, ds->red[b], tid);
             __syncwarp();
-            if (lane == 0) mbar_arrive(&done[pend_d]);
+            if (lane == 0) mbar_arrive(&empty[pend_d]);
         };
         for (int n = 0;; ++n) {
             const int d = n % kK3Desc;
@@ -1074,7 +1016,6 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
             const int slot = meta[d].slot, blk = meta[d].blk;
             if (slot < 0) {
                 if (pend_slot >= 0) finish_pending();
-                if (ok && lane == 0) mbar_arrive(&done[d]);
                 pend_slot = -1;
                 break;
             }
@@ -1153,6 +1094,18 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
         }
         if (ev && tid == 0) ev[2] = global_timer_ns();
     }
+
+    // ---------------- combine: every CTA's y rows are written (grid barrier) ----------------
+    pdl_wait_prior_grid();  // the routing table (K2); already complete for the producer
+    const int tk = tid / kDecodeMaxTopk, ts = tid % kDecodeMaxTopk;
+    if (tk < kMaxB) {
+        const bool v = tk < a.B && ts < a.topk;
+        trow[tk][ts] = v ? __ldcg(&a.table->tok_row[tk][ts]) : 0;
+        tw[tk][ts] = v ? __ldcg(&a.table->tok_w[tk][ts]) : 0.0f;
+    }
+    const bool ok = grid_barrier(&a.ctl->bar_count, &a.ctl->bar_epoch, &a.ctl->status, &bar_ok);
+    if (ev && tid == 0) ev[3] = global_timer_ns();
+    if (ok && !abort_flag && __ldcg(&a.ctl->status) == 0) combine_slice(a, trow, tw, tid);
 }
 
 // ======================================================================================
@@ -1225,7 +1178,7 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
     }
     // ---- K3: the rest of shared memory is the item ring
     {
-        const size_t off_tbl = 512;  // 4 x kK3Desc + kRedBufs + 2 mbarriers before it
+        const size_t off_tbl = 512;  // 3 x kK3Desc + kRedBufs + 2 mbarriers before it
         const size_t off_meta = off_tbl + up(sizeof(SlotTable), 128);
         const size_t off_dn = off_meta + up(sizeof(ItemMeta) * kK3Desc, 128);
         const size_t off_hf = off_dn + up(sizeof(DnSmem), 128);
@@ -1246,7 +1199,7 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
         uint32_t o[7] = {(uint32_t)off_tbl, (uint32_t)off_meta, (uint32_t)off_dn, (uint32_t)off_hf,
                          (uint32_t)off_hd,  (uint32_t)off_sig,  (uint32_t)off_ring};
         void* args[] = {&a, &ring_bytes, &o[0], &o[1], &o[2], &o[3], &o[4], &o[5], &o[6]};
-        err = launch_pdl(k3, dim3(sms), dim3(kThreads3), smem, st, args);
+        err = launch_pdl(k3, dim3(sms), dim3(kThreads), smem, st, args);
         if (err != cudaSuccess) return err;
     }
     return cudaGetLastError();

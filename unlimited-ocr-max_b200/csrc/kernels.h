@@ -26,8 +26,9 @@ cudaError_t launch_route(const float* x, int T, int H, const uint16_t* wg, int E
 // launch leaves it zeroed again except `status`, which is sticky until read.
 struct DecodeCtl {
     uint32_t status;
-    uint32_t route_done;  // route-kernel CTAs finished (the last one resets it)
-    uint32_t pad[62];
+    uint32_t bar_count;   // K3 grid barrier: CTAs arrived (the last one resets it)
+    uint32_t bar_epoch;   // K3 grid barrier: completed barriers (advanced by the last arrival)
+    uint32_t pad[61];
 };
 constexpr int kDecodeMaxShared = 8;
 constexpr int kDecodeMaxTopk = 8;
@@ -63,7 +64,6 @@ struct DecodeArgs {
     float* y;       // [(k+S)*B, H], slot-contiguous rows
     float* out;     // [B, H]
     DecodeCtl* ctl;
-    uint32_t* row_done;  // [H/4] combine counters (self-resetting)
     float* logits;       // [8][64]
     RouteTable* table;
     unsigned long long* trace;  // optional per-CTA item timeline (diagnostics), null = off

@@ -140,6 +140,45 @@ UOCR_DEV bool wait_counter_geq(const uint32_t* p, uint32_t target, uint32_t* sta
     return true;
 }
 
+// Spin until *p != old (gpu-scope acquire), at most kWaitBudgetNs.
+UOCR_DEV bool wait_word_ne(const uint32_t* p, uint32_t old, uint32_t* status) {
+    if (ld_acquire_gpu(p) != old) return true;
+    const uint64_t t0 = global_timer_ns();
+    while (ld_acquire_gpu(p) == old) {
+        __nanosleep(32);
+        if (global_timer_ns() - t0 > kWaitBudgetNs) {
+            set_status(status, kStatusWaitTimeout);
+            return false;
+        }
+    }
+    return true;
+}
+
+// Barrier over every CTA of a grid whose CTAs are all resident at once (a persistent launch of
+// one CTA per SM). count / epoch are device words, zero-filled once: the last CTA to arrive
+// resets count and advances epoch, which the others wait for. Every CTA must arrive (also after
+// an error of its own) or the others give up after kWaitBudgetNs. Returns false on a timeout.
+// All threads of the CTA call it.
+UOCR_DEV bool grid_barrier(uint32_t* count, uint32_t* epoch, uint32_t* status, int* ok_smem) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const uint32_t e0 = ld_acquire_gpu(epoch);
+        __threadfence();  // this CTA's writes (ordered before it by __syncthreads) before the arrival
+        bool ok = true;
+        if (atomicAdd(count, 1u) == gridDim.x - 1) {
+            atomicExch(count, 0u);
+            __threadfence();
+            atomicAdd(epoch, 1u);
+        } else {
+            ok = wait_word_ne(epoch, e0, status);
+        }
+        __threadfence();
+        *ok_smem = ok;
+    }
+    __syncthreads();
+    return *ok_smem != 0;
+}
+
 // ---- named barriers (a subset of the CTA's warps) ----------------------------------------
 UOCR_DEV void named_bar_sync(uint32_t id, uint32_t threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
