@@ -155,107 +155,6 @@ UOCR_DEV void mma_tile_bf16(uint32_t rows_s, uint32_t rowb, int s0, int s1, uint
     }
 }
 
-// ---- register-resident activation fragments ----------------------------------------------
-// A warp that always covers the same k-steps [s0, s0 + n) keeps their activation fragments in
-// registers; an item then only loads its weight fragments (all of them before the first
-// product) and the products run back to back.
-template <int MAXS>
-struct FragS8 {
-    uint2 b[MAXS][3];  // digits d0..d2 of the warp's columns (lane: column g, bytes 8t..8t+7)
-    float sg[2];       // digit scale of columns 2t, 2t+1
-};
-
-template <int MAXS>
-UOCR_DEV void load_frag_s8(FragS8<MAXS>& f, uint32_t xd_s, const float* sig, int s0, int n, int lane) {
-    const int t = lane & 3;
-#pragma unroll
-    for (int i = 0; i < MAXS; ++i) {
-        if (i < n) {
-            const int s = s0 + i;
-#pragma unroll
-            for (int d = 0; d < 3; ++d) f.b[i][d] = lds_u64(xd_s + 8u * ((s * 3 + d) * 32 + lane));
-        }
-    }
-    f.sg[0] = lds_f32(smem_addr(sig) + 8u * t);
-    f.sg[1] = lds_f32(smem_addr(sig) + 8u * t + 4u);
-}
-
-// s8 tile product over the warp's k-steps with register-resident digits (see mma_tile_s8).
-template <int MAXS>
-UOCR_DEV void mma_tile_s8_reg(uint32_t rows_s, uint32_t rowb, int row0, uint32_t sc_s, int NG, int s0, int n,
-                              const FragS8<MAXS>& f, int lane, float (&acc)[4]) {
-    const int g = lane >> 2;
-    const uint32_t ra = rows_s + (uint32_t)g * rowb + 8u * (lane & 3), rb = ra + 8u * rowb;
-    const uint32_t sa = sc_s + 4u * ((row0 + g) * NG), sb = sc_s + 4u * ((row0 + g + 8) * NG);
-    // even and odd k-steps accumulate separately: six independent product chains in flight
-    int c[2][3][4] = {};
-#pragma unroll
-    for (int i = 0; i < MAXS; ++i) {
-        if (i < n) {
-            const int s = s0 + i;
-            const uint2 A0 = lds_u64_nv(ra + 32u * s), A1 = lds_u64_nv(rb + 32u * s);
-#pragma unroll
-            for (int d = 0; d < 3; ++d) mma_s8(c[i & 1][d], A0.x, A1.x, A0.y, A1.y, f.b[i][d].x, f.b[i][d].y);
-            if (i == n - 1 || ((s + 1) & 3) == 0) {  // the k-step closes a 128-group
-                const float slo = lds_f32_nv(sa + 4u * (s >> 2)), shi = lds_f32_nv(sb + 4u * (s >> 2));
-                int v[3][4];
-#pragma unroll
-                for (int d = 0; d < 3; ++d)
-#pragma unroll
-                    for (int j = 0; j < 4; ++j) v[d][j] = c[0][d][j] + c[1][d][j];
-                acc[0] = __fmaf_rn(undigit(v[0][0], v[1][0], v[2][0]), slo * f.sg[0], acc[0]);
-                acc[1] = __fmaf_rn(undigit(v[0][1], v[1][1], v[2][1]), slo * f.sg[1], acc[1]);
-                acc[2] = __fmaf_rn(undigit(v[0][2], v[1][2], v[2][2]), shi * f.sg[0], acc[2]);
-                acc[3] = __fmaf_rn(undigit(v[0][3], v[1][3], v[2][3]), shi * f.sg[1], acc[3]);
-#pragma unroll
-                for (int h = 0; h < 2; ++h)
-#pragma unroll
-                    for (int d = 0; d < 3; ++d) c[h][d][0] = c[h][d][1] = c[h][d][2] = c[h][d][3] = 0;
-            }
-        }
-    }
-}
-
-template <int MAXS>
-struct FragBf16 {
-    uint2 b[MAXS][3];  // bf16 terms t0..t2 of the warp's column (lane: column g, values 4t..4t+3)
-};
-
-template <int MAXS>
-UOCR_DEV void load_frag_bf16(FragBf16<MAXS>& f, uint32_t xf_s, int ldx, int s0, int n, int lane) {
-    const uint32_t xa = xf_s + 4u * ((uint32_t)(lane >> 2) * ldx + 4 * (lane & 3));
-#pragma unroll
-    for (int i = 0; i < MAXS; ++i) {
-        if (i < n) {
-            const float4 v = lds_f128(xa + 64u * (s0 + i));
-            uint32_t b0[3], b1[3];
-            bf16_terms(v.x, v.y, b0[0], b0[1], b0[2]);
-            bf16_terms(v.z, v.w, b1[0], b1[1], b1[2]);
-#pragma unroll
-            for (int q = 0; q < 3; ++q) f.b[i][q] = make_uint2(b0[q], b1[q]);
-        }
-    }
-}
-
-// bf16 tile product over the warp's k-steps with register-resident terms; one accumulator per
-// term keeps three independent chains in flight.
-template <int MAXS>
-UOCR_DEV void mma_tile_bf16_reg(uint32_t rows_s, uint32_t rowb, int s0, int n, const FragBf16<MAXS>& f, int lane,
-                                float (&acc)[4]) {
-    const uint32_t ra = rows_s + (uint32_t)(lane >> 2) * rowb + 8u * (lane & 3), rb = ra + 8u * rowb;
-    float c[2][3][4] = {};  // (k-step parity, term): six independent chains
-#pragma unroll
-    for (int i = 0; i < MAXS; ++i) {
-        if (i < n) {
-            const uint2 A0 = lds_u64_nv(ra + 32u * (s0 + i)), A1 = lds_u64_nv(rb + 32u * (s0 + i));
-#pragma unroll
-            for (int q = 0; q < 3; ++q) mma_bf16(c[i & 1][q], A0.x, A1.x, A0.y, A1.y, f.b[i][q].x, f.b[i][q].y);
-        }
-    }
-#pragma unroll
-    for (int j = 0; j < 4; ++j) acc[j] += (c[0][0][j] + c[1][0][j]) + (c[0][1][j] + c[1][1][j]) + (c[0][2][j] + c[1][2][j]);
-}
-
 // Activations of 8 columns (rows of xf, stride ldx; rows >= valid are zero) as int8 digits in
 // fragment order, one power-of-two scale per column: warp w converts column w (kCW >= 8 warps).
 UOCR_DEV void stage_digits(const float* xf, int ldx, int K, int valid, uint32_t* xd, float* sig, int warp, int lane) {
@@ -560,28 +459,22 @@ struct GuSmem {
     float red[kRedBufs][kCW][16][8];
 };
 
-// Activation fragments a K2 warp keeps in registers: its k-steps of x are fixed for the CTA.
-// Layers up to H = 128 * kK2RegSteps use them; larger ones read the fragments from shared memory.
-constexpr int kK2RegSteps = 10;
-
 // The warp's partial tile of one item. int8 blocks: tile warp / 4 (gate, up), K quarter
 // warp % 4 (H / 128 k-steps of 32); bf16 blocks: K eighth `warp` (H / 128 k-steps of 16).
-template <bool kI8L>
+// The activation fragments are read from shared memory in the loop: a compact loop runs
+// faster here than one unrolled over register-held fragments (instruction fetch dominates).
 UOCR_DEV void gu_partial(const DecodeArgs& a, bool i8, uint32_t stage_s, uint32_t xf_s, int ldx, uint32_t xd_s,
-                         const float* xsig, const FragS8<kK2RegSteps>& f8, const FragBf16<kK2RegSteps>& f16,
-                         bool reg, int lane, int warp, float (&acc)[4]) {
+                         const float* xsig, int lane, int warp, float (&acc)[4]) {
     acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
     const int n = a.H / 128;  // k-steps per warp, both kinds
     if (i8) {
         const uint32_t rowb = (uint32_t)packed_row_bytes(a.H, true);
         const int tile = warp >> 2, s0 = (warp & 3) * n;
         const uint32_t rows = stage_s + (uint32_t)tile * 16 * rowb, sc = stage_s + 32 * rowb;
-        if (kI8L && reg) mma_tile_s8_reg<kK2RegSteps>(rows, rowb, tile * 16, sc, n, s0, n, f8, lane, acc);
-        else mma_tile_s8(rows, rowb, tile * 16, sc, n, s0, s0 + n, xd_s, xsig, lane, acc);
+        mma_tile_s8(rows, rowb, tile * 16, sc, n, s0, s0 + n, xd_s, xsig, lane, acc);
     } else {
         const uint32_t rowb = (uint32_t)packed_row_bytes(a.H, false);
-        if (!kI8L && reg) mma_tile_bf16_reg<kK2RegSteps>(stage_s, rowb, warp * n, n, f16, lane, acc);
-        else mma_tile_bf16(stage_s, rowb, warp * n, warp * n + n, xf_s, ldx, lane, acc);
+        mma_tile_bf16(stage_s, rowb, warp * n, warp * n + n, xf_s, ldx, lane, acc);
     }
 }
 
@@ -618,7 +511,6 @@ UOCR_DEV void gu_finish(const DecodeArgs& a, const SlotTable& tb, bool i8, int s
     if (pos >= 0) a.h[(size_t)(tb.base[slot] + pos) * a.I + blk * P + p] = silu(g) * u;
 }
 
-template <bool kI8L>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl, uint32_t off_route,
                       uint32_t off_meta, uint32_t off_gu, uint32_t off_xf, uint32_t off_xd, uint32_t off_sig,
@@ -733,12 +625,6 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
         if (ev && tid == 0) ev[5] = global_timer_ns();
         const uint32_t xf_s = smem_addr(xf), xd_s = smem_addr(xd);
         // this warp's activation fragments, fixed for the CTA
-        const int nks = a.H / 128;
-        const bool reg = nks <= kK2RegSteps;
-        FragS8<kK2RegSteps> f8;
-        FragBf16<kK2RegSteps> f16;
-        if (kI8L && reg) load_frag_s8<kK2RegSteps>(f8, xd_s, xsig, (warp & 3) * nks, nks, lane);
-        if (!kI8L && reg) load_frag_bf16<kK2RegSteps>(f16, xf_s, ldx, warp * nks, nks, lane);
         if (ev && tid == 0) ev[3] = global_timer_ns();
         // Item n: products, stage release, partial tile stored; then item n-1 is finished (its
         // partial tiles are complete once every warp has arrived) and item n's buffer released.
@@ -763,7 +649,7 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             const bool i8 = slot >= a.S && a.int8;
             const uint32_t stage_s = launder(smem_addr(stages + (size_t)st * stage_bytes));
             float acc[4];
-            gu_partial<kI8L>(a, i8, stage_s, xf_s, ldx, xd_s, xsig, f8, f16, reg, lane, warp, acc);
+            gu_partial(a, i8, stage_s, xf_s, ldx, xd_s, xsig, lane, warp, acc);
             fence_regs(acc);
             __syncwarp();
             if (tr && lane == 0) tr[5] = global_timer_ns();
@@ -845,11 +731,6 @@ UOCR_DEV void combine_slice(const DecodeArgs& a, const int (&trow)[kMaxB][kDecod
     }
 }
 
-// K3 warps keep the current run's h fragments in registers for I up to 128 * kK3RegS8 (int8)
-// and 64 * kK3RegBf16 (bf16).
-constexpr int kK3RegS8 = 8, kK3RegBf16 = 14;
-
-template <bool kI8L>
 __global__ void __launch_bounds__(kThreads, 1)
 decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t off_meta, uint32_t off_dn,
                    uint32_t off_hf, uint32_t off_hd, uint32_t off_sig, uint32_t off_ring) {
@@ -990,9 +871,6 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
         int runs = 0;
         const int tile = warp >> 2, q = warp & 3;
         const int n8 = a.I / 128, n16 = a.I / 64;  // k-steps per warp (s8 32-wide, bf16 16-wide)
-        const bool reg8 = n8 <= kK3RegS8, reg16 = n16 <= kK3RegBf16;
-        FragS8<kK3RegS8> f8;
-        FragBf16<kK3RegBf16> f16;
         // As in K2: item n's products, then item n-1 is finished (y rows written, its descriptor
         // released), then item n's partial tile buffer is released.
         int pend_slot = -1, pend_blk = 0, pend_n = 0, pend_d = 0;
@@ -1055,9 +933,6 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
                         break;
                     }
                     ++runs;
-                    if (kI8L && reg8) load_frag_s8<kK3RegS8>(f8, hd_s, hsig, q * n8, n8, lane);
-                } else if (!kI8L && reg16) {
-                    load_frag_bf16<kK3RegBf16>(f16, hf_s, ldh, q * n16, n16, lane);
                 }
             }
             float acc[4] = {0.f, 0.f, 0.f, 0.f};
@@ -1065,16 +940,15 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
                 const uint32_t rowb = (uint32_t)packed_row_bytes(a.I, true);
                 const int NG = a.I / 128;
                 const uint32_t rows = item_s + (uint32_t)tile * 16 * rowb, sc = item_s + kW2Rows * rowb;
-                if (kI8L && reg8) mma_tile_s8_reg<kK3RegS8>(rows, rowb, tile * 16, sc, NG, q * n8, n8, f8, lane, acc);
-                else mma_tile_s8(rows, rowb, tile * 16, sc, NG, q * n8, q * n8 + n8, hd_s, hsig, lane, acc);
+                mma_tile_s8(rows, rowb, tile * 16, sc, NG, q * n8, q * n8 + n8, hd_s, hsig, lane, acc);
             } else {
                 const uint32_t rowb = (uint32_t)packed_row_bytes(a.I, false);
                 const uint32_t rows = item_s + (uint32_t)tile * 16 * rowb;
-                if (!kI8L && reg16) mma_tile_bf16_reg<kK3RegBf16>(rows, rowb, q * n16, n16, f16, lane, acc);
-                else mma_tile_bf16(rows, rowb, q * n16, q * n16 + n16, hf_s, ldh, lane, acc);
+                mma_tile_bf16(rows, rowb, q * n16, q * n16 + n16, hf_s, ldh, lane, acc);
             }
             fence_regs(acc);
             __syncwarp();
+            if (tr && lane == 0) tr[5] = global_timer_ns();
             if (lane == 0) mbar_arrive(&freed[d]);  // the item's ring bytes are no longer read
             store_partial(ds->red[n % kRedBufs], warp, lane, acc);
             if (pend_slot >= 0) {
@@ -1084,6 +958,7 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
             __syncwarp();
             if (lane == 0) mbar_arrive(&redbar[n % kRedBufs]);
             if (tr && lane == 0) {
+                tr[6] = global_timer_ns();
                 tr[2] = global_timer_ns();
                 tr[3] = ((unsigned long long)slot << 32) | (unsigned)blk;
             }
@@ -1166,8 +1041,7 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
         if ((size_t)max_smem < off_stages + 2 * (size_t)stage_bytes) return cudaErrorInvalidConfiguration;
         int nst = (int)std::min<size_t>(8, ((size_t)max_smem - off_stages) / stage_bytes);
         const size_t smem = off_stages + (size_t)nst * stage_bytes;
-        const void* k2 = a.int8 ? reinterpret_cast<const void*>(decode_gate_up_kernel<true>)
-                                : reinterpret_cast<const void*>(decode_gate_up_kernel<false>);
+        const void* k2 = reinterpret_cast<const void*>(decode_gate_up_kernel);
         err = ensure_smem_optin(k2, smem);
         if (err != cudaSuccess) return err;
         uint32_t o[8] = {(uint32_t)off_tbl, (uint32_t)off_route, (uint32_t)off_meta, (uint32_t)off_gu,
@@ -1192,8 +1066,7 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
         if ((size_t)max_smem < off_ring + max_item) return cudaErrorInvalidConfiguration;
         uint32_t ring_bytes = (uint32_t)(((size_t)max_smem - off_ring) & ~size_t(127));
         const size_t smem = off_ring + ring_bytes;
-        const void* k3 = a.int8 ? reinterpret_cast<const void*>(decode_down_kernel<true>)
-                                : reinterpret_cast<const void*>(decode_down_kernel<false>);
+        const void* k3 = reinterpret_cast<const void*>(decode_down_kernel);
         err = ensure_smem_optin(k3, smem);
         if (err != cudaSuccess) return err;
         uint32_t o[7] = {(uint32_t)off_tbl, (uint32_t)off_meta, (uint32_t)off_dn, (uint32_t)off_hf,
