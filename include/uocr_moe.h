@@ -105,7 +105,6 @@ typedef struct uocr_moe_layer {
     int32_t int8;       /* 1: routed stacks int8 with fp32 scales inside the blocks; 0: bf16 */
     int32_t reserved;
     const uint16_t* router;     /* bf16 [E, H]  (gate.gate_score.weight) */
-    const uint16_t* router_seg; /* the router re-laid out for the decode step (uocr_moe_pack_router) */
     const void* w13;            /* routed gate|up blocks (uocr_moe_pack_w13) */
     const void* w2;             /* routed down blocks (uocr_moe_pack_w2) */
     const uint16_t* w13_shared; /* shared gate|up as S bf16 experts (uocr_moe_pack_shared) */
@@ -135,12 +134,6 @@ UOCR_API int uocr_moe_pack_w13(const void* gate, const void* up, const float* ga
 /* Pack experts.down_proj [E, H, I] (+ int8 _scales [E, H, I/G]) into w2_out. */
 UOCR_API int uocr_moe_pack_w2(const void* down, const float* down_scales, int64_t E, int64_t H, int64_t I,
                               int64_t group, int int8, void* w2_out, uocr_stream_t stream);
-
-/* Re-lay out the router [E, H] bf16 (E <= 64, H a multiple of 64) for the decode step's gate:
- * [8 segments][H/64 steps][64 experts][8] bf16, experts >= E zero-filled; router_seg_out holds
- * 64 * H bf16. The routing arithmetic (and its bits) is unchanged; only the loads coalesce. */
-UOCR_API int uocr_moe_pack_router(const uint16_t* router, int64_t E, int64_t H, uint16_t* router_seg_out,
-                                  uocr_stream_t stream);
 
 /* Pack the shared experts (shared_experts.{gate,up,down}_proj.weight as [S*I, H], [S*I, H],
  * [H, S*I] in plain [out, in] order) into w13_shared (uocr_moe_w13_bytes(S, I, H, 128, 0)

@@ -34,7 +34,6 @@ class UocrMoeLayer(ctypes.Structure):
         ("int8", ctypes.c_int32),
         ("reserved", ctypes.c_int32),
         ("router", P),
-        ("router_seg", P),
         ("w13", P),
         ("w2", P),
         ("w13_shared", P),
@@ -55,7 +54,6 @@ SIGNATURES: dict[str, tuple] = {
     "uocr_moe_pack_w13": (I32, [P, P, P, P, I64, I64, I64, I64, I32, P, P]),
     "uocr_moe_pack_w2": (I32, [P, P, I64, I64, I64, I64, I32, P, P]),
     "uocr_moe_pack_shared": (I32, [P, P, P, I64, I64, I64, P, P, P]),
-    "uocr_moe_pack_router": (I32, [P, I64, I64, P, P]),
     "uocr_moe_route": (I32, [P, I64, I64, P, I64, P, I64, P, P, P]),
     "uocr_moe_decode_workspace_bytes": (SZ, [ctypes.POINTER(UocrMoeLayer), I64]),
     "uocr_moe_decode": (I32, [ctypes.POINTER(UocrMoeLayer), P, I64, P, P, P, P, P, SZ, P]),

@@ -78,7 +78,7 @@ extern "C" {
 
 const char* uocr_last_error(void) { return g_last_error.c_str(); }
 
-int uocr_abi_version(void) { return 3; }
+int uocr_abi_version(void) { return 4; }
 
 // ---------------------------------------------------------------------------------------
 // reference op shims
@@ -217,14 +217,6 @@ int uocr_moe_pack_w2(const void* down, const float* down_scales, int64_t E, int6
                        "pack_w2: launch");
 }
 
-int uocr_moe_pack_router(const uint16_t* router, int64_t E, int64_t H, uint16_t* out, uocr_stream_t stream) {
-    if (E < 1 || E > 64) return fail(UOCR_EUNSUPPORTED, "pack_router: %lld experts; this build routes 1..64", (long long)E);
-    if (H < 64 || H % 64) return fail(UOCR_EINVAL, "pack_router: hidden=%lld must be a positive multiple of 64", (long long)H);
-    if (!router || !out) return fail(UOCR_EINVAL, "pack_router: null pointer");
-    if (!a16(router) || !a16(out)) return fail(UOCR_EINVAL, "pack_router: pointers must be 16-byte aligned");
-    return cuda_status(uocr::launch_pack_router(router, (int)E, (int)H, out, S(stream)), "pack_router: launch");
-}
-
 int uocr_moe_pack_shared(const uint16_t* gate, const uint16_t* up, const uint16_t* down, int64_t S_, int64_t I,
                          int64_t H, uint16_t* w13_out, uint16_t* w2_out, uocr_stream_t stream) {
     if (S_ < 1 || I < 1 || H < 1) return fail(UOCR_EINVAL, "pack_shared: empty");
@@ -321,8 +313,6 @@ int uocr_moe_decode(const uocr_moe_layer* L, const float* x, int64_t B, const fl
     if (B < 1 || B > 8) return fail(UOCR_EINVAL, "moe_decode: B=%lld outside 1..8 (use moe_prefill)", (long long)B);
     if (L->n_shared > uocr::kDecodeMaxShared) return fail(UOCR_EUNSUPPORTED, "moe_decode: more than 8 shared experts");
     if (L->hidden > 8192 || L->inter > 8192) return fail(UOCR_EUNSUPPORTED, "moe_decode: hidden/inter above 8192");
-    if (!L->router_seg || !a16(L->router_seg))
-        return fail(UOCR_EINVAL, "moe_decode: the layer needs router_seg (uocr_moe_pack_router), 16-byte aligned");
     if (!x || !out || !workspace) return fail(UOCR_EINVAL, "moe_decode: null pointer");
     if (!a16(x) || !a16(out)) return fail(UOCR_EINVAL, "moe_decode: x and out must be 16-byte aligned");
     if (bias && (reinterpret_cast<uintptr_t>(bias) & 3)) return fail(UOCR_EINVAL, "moe_decode: bias must be 4-byte aligned");
@@ -334,7 +324,7 @@ int uocr_moe_decode(const uocr_moe_layer* L, const float* x, int64_t B, const fl
     uocr::DecodeArgs a{};
     a.B = (int)B; a.H = L->hidden; a.I = L->inter; a.E = L->n_routed; a.S = L->n_shared; a.topk = L->top_k;
     a.G = L->int8 ? L->group : 128; a.int8 = L->int8;
-    a.x = x; a.router = L->router; a.router_seg = L->router_seg; a.bias = bias;
+    a.x = x; a.router = L->router; a.bias = bias;
     a.ids = ids_out ? ids_out : reinterpret_cast<int32_t*>(ws + d.ids);
     a.wts = wts_out ? wts_out : reinterpret_cast<float*>(ws + d.wts);
     a.w13 = L->w13; a.w2 = L->w2;

@@ -52,7 +52,6 @@ struct DecodeArgs {
     int B, H, I, E, S, topk, G, int8;
     const float* x;
     const uint16_t* router;
-    const uint16_t* router_seg;  // router in segment-chain order (uocr_moe_pack_router)
     const float* bias;
     int32_t* ids;
     float* wts;
@@ -119,7 +118,6 @@ cudaError_t launch_pack_w13(const void* gate, const void* up, const float* gs, c
                             int G, bool int8, void* out, cudaStream_t st);
 cudaError_t launch_pack_w2(const void* down, const float* ds, int E, int H, int I, int G, bool int8, void* out,
                            cudaStream_t st);
-cudaError_t launch_pack_router(const uint16_t* router, int E, int H, uint16_t* out, cudaStream_t st);
 cudaError_t launch_pack_shared(const uint16_t* gate, const uint16_t* up, const uint16_t* down, long S, long I, long H,
                                uint16_t* w13, uint16_t* w2, cudaStream_t st);
 

@@ -89,23 +89,4 @@ cudaError_t launch_pack_shared(const uint16_t* gate, const uint16_t* up, const u
     return cudaGetLastError();
 }
 
-// router [E, H] -> [8 segments][H / 64 steps][64 experts][8] bf16 (experts >= E zero): the decode
-// routing's lane e reads step `it` of segment s of expert e as 16 contiguous bytes, and the 32
-// lanes of a warp read 512 contiguous bytes.
-__global__ void pack_router_kernel(const uint16_t* __restrict__ router, int E, int H, uint16_t* __restrict__ out) {
-    const int L = H / 8, steps = L / 8;
-    const long n = (long)8 * steps * 64;  // 16-byte chunks
-    for (long c = (long)blockIdx.x * blockDim.x + threadIdx.x; c < n; c += (long)gridDim.x * blockDim.x) {
-        const int e = (int)(c % 64), it = (int)((c / 64) % steps), seg = (int)(c / (64 * steps));
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (e < E) v = *reinterpret_cast<const uint4*>(router + (size_t)e * H + seg * L + it * 8);
-        reinterpret_cast<uint4*>(out)[c] = v;
-    }
-}
-
-cudaError_t launch_pack_router(const uint16_t* router, int E, int H, uint16_t* out, cudaStream_t st) {
-    pack_router_kernel<<<64, 256, 0, st>>>(router, E, H, out);
-    return cudaGetLastError();
-}
-
 }  // namespace uocr

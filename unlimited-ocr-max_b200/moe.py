@@ -130,14 +130,12 @@ class UocrMoE:
         if router.dtype != torch.bfloat16 or tuple(router.shape) != (E, H):
             raise ValueError(f"gate.gate_score.weight: expected bf16 [{E}, {H}], got {router.dtype} {tuple(router.shape)}")
         t = {"router": router.to(dev).contiguous()}
-        t["router_seg"] = torch.empty(64 * H, dtype=torch.bfloat16, device=dev)
         wdt = torch.int8 if cfg.int8_experts else torch.bfloat16
         gate = on_dev("experts.gate_proj", wdt, (E, I, H))
         up = on_dev("experts.up_proj", wdt, (E, I, H))
         G = INT8_GROUP_SIZE
         L = load()
         stream = torch.cuda.current_stream(dev).cuda_stream
-        check(L.uocr_moe_pack_router(t["router"].data_ptr(), E, H, t["router_seg"].data_ptr(), stream))
         i8 = int(cfg.int8_experts)
         scales = {}
         if cfg.int8_experts:
@@ -167,7 +165,6 @@ class UocrMoE:
         lay.hidden, lay.inter, lay.n_routed, lay.n_shared = H, I, E, S
         lay.top_k, lay.group, lay.int8 = cfg.num_experts_per_tok, INT8_GROUP_SIZE, int(cfg.int8_experts)
         lay.router = t["router"].data_ptr()
-        lay.router_seg = t["router_seg"].data_ptr()
         lay.w13, lay.w2 = t["w13"].data_ptr(), t["w2"].data_ptr()
         lay.w13_shared, lay.w2_shared = t["w13s"].data_ptr(), t["w2s"].data_ptr()
         self._layer = lay
