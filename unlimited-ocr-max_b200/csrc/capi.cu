@@ -261,7 +261,7 @@ int uocr_moe_route(const float* x, int64_t T, int64_t H, const uint16_t* router,
 namespace {
 
 struct DecodeLayout {
-    size_t ctl, logits, table, ids, wts, h, y, total;
+    size_t ctl, logits, xdig, xsig, table, ids, wts, h, y, total;
 };
 
 DecodeLayout decode_layout(const uocr_moe_layer* L, int64_t B) {
@@ -269,7 +269,9 @@ DecodeLayout decode_layout(const uocr_moe_layer* L, int64_t B) {
     const size_t pairs = (size_t)(L->top_k + L->n_shared) * (size_t)B;
     size_t off = 0;
     d.ctl = off; off += align256(sizeof(uocr::DecodeCtl));
-    d.logits = off; off += align256(sizeof(float) * 8 * 64);
+    d.logits = off; off += align256(sizeof(float) * 8 * 64 * 8);
+    d.xdig = off; off += align256((size_t)L->hidden * 24);
+    d.xsig = off; off += align256(sizeof(float) * 8 * (size_t)(L->hidden / 128));
     d.table = off; off += align256(sizeof(uocr::RouteTable));
     d.ids = off; off += align256(sizeof(int32_t) * (size_t)B * L->top_k);
     d.wts = off; off += align256(sizeof(float) * (size_t)B * L->top_k);
@@ -334,6 +336,8 @@ int uocr_moe_decode(const uocr_moe_layer* L, const float* x, int64_t B, const fl
     a.out = out;
     a.ctl = reinterpret_cast<uocr::DecodeCtl*>(ws + d.ctl);
     a.logits = reinterpret_cast<float*>(ws + d.logits);
+    a.xdig = reinterpret_cast<uint32_t*>(ws + d.xdig);
+    a.xsig = reinterpret_cast<float*>(ws + d.xsig);
     a.table = reinterpret_cast<uocr::RouteTable*>(ws + d.table);
     return cuda_status(uocr::launch_decode_layer(a, S(stream)), "moe_decode: launch");
 }

@@ -129,7 +129,7 @@ UOCR_DEV void mma_tile_s8(uint32_t rows_s, uint32_t rowb, int row0, uint32_t sc_
         }
         const float slo = lds_f32(sc_s + 4u * ((row0 + g) * NG + grp));
         const float shi = lds_f32(sc_s + 4u * ((row0 + g + 8) * NG + grp));
-        const float sg0 = sig[2 * t], sg1 = sig[2 * t + 1];
+        const float sg0 = sig[2 * t * NG + grp], sg1 = sig[(2 * t + 1) * NG + grp];
         acc[0] = __fmaf_rn(undigit(c[0][0], c[1][0], c[2][0]), slo * sg0, acc[0]);
         acc[1] = __fmaf_rn(undigit(c[0][1], c[1][1], c[2][1]), slo * sg1, acc[1]);
         acc[2] = __fmaf_rn(undigit(c[0][2], c[1][2], c[2][2]), shi * sg0, acc[2]);
@@ -155,38 +155,45 @@ UOCR_DEV void mma_tile_bf16(uint32_t rows_s, uint32_t rowb, int s0, int s1, uint
     }
 }
 
-// Activations of 8 columns (rows of xf, stride ldx; rows >= valid are zero) as int8 digits in
-// fragment order, one power-of-two scale per column: warp w converts column w (kCW >= 8 warps).
-UOCR_DEV void stage_digits(const float* xf, int ldx, int K, int valid, uint32_t* xd, float* sig, int warp, int lane) {
-    if (warp >= kMaxB) return;
-    const int col = warp;
-    const float* row = xf + (size_t)col * ldx;
-    const bool live = col < valid;
-    float m = 0.0f;
-    for (int k = 4 * lane; k < K; k += 128) {
-        if (live) {
-            const float4 v = *reinterpret_cast<const float4*>(row + k);
-            m = fmaxf(m, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
-        }
-    }
+// Digits of one 128-value group of one column: lane L holds values [4L, 4L + 4) of the group.
+// Returns the group's scale (warp-uniform) and the lane's three digit words.
+UOCR_DEV float group_digits(float4 v, uint32_t (&w)[3]) {
+    float m = fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w)));
 #pragma unroll
     for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
     float sg, inv;
     digit_scale(m, sg, inv);
-    if (lane == 0) sig[col] = sg;
-    for (int k = 4 * lane; k < K; k += 128) {
-        const float4 v = live ? *reinterpret_cast<const float4*>(row + k) : make_float4(0.f, 0.f, 0.f, 0.f);
-        int d[4][3];
-        to_digits(v.x, inv, d[0][0], d[0][1], d[0][2]);
-        to_digits(v.y, inv, d[1][0], d[1][1], d[1][2]);
-        to_digits(v.z, inv, d[2][0], d[2][1], d[2][2]);
-        to_digits(v.w, inv, d[3][0], d[3][1], d[3][2]);
-        // values k..k+3 sit in k-step k / 32 at bytes k % 32: fragment lane 4 col + (k % 32) / 8,
-        // half (k % 8) / 4
-        const int s = k >> 5, fl = 4 * col + ((k & 31) >> 3), half = (k & 7) >> 2;
+    int d[4][3];
+    to_digits(v.x, inv, d[0][0], d[0][1], d[0][2]);
+    to_digits(v.y, inv, d[1][0], d[1][1], d[1][2]);
+    to_digits(v.z, inv, d[2][0], d[2][1], d[2][2]);
+    to_digits(v.w, inv, d[3][0], d[3][1], d[3][2]);
 #pragma unroll
-        for (int q = 0; q < 3; ++q)
-            xd[((s * 3 + q) * 32 + fl) * 2 + half] = pack_s8x4(d[0][q], d[1][q], d[2][q], d[3][q]);
+    for (int q = 0; q < 3; ++q) w[q] = pack_s8x4(d[0][q], d[1][q], d[2][q], d[3][q]);
+    return sg;
+}
+// Index (in 32-bit words) of digit q of values k..k+3 (k a multiple of 4) of column col in the
+// fragment-ordered digit buffer: k-step k / 32, fragment lane 4 col + (k % 32) / 8, half (k % 8) / 4.
+UOCR_DEV int digit_word(int k, int col, int q) {
+    return (((k >> 5) * 3 + q) * 32 + 4 * col + ((k & 31) >> 3)) * 2 + ((k & 7) >> 2);
+}
+
+// Activations of 8 columns (rows of xf, stride ldx; rows >= valid are zero) as int8 digits in
+// fragment order, one power-of-two scale per column and 128-group (sig[col * K/128 + g]):
+// warp w converts column w (kCW >= 8 warps).
+UOCR_DEV void stage_digits(const float* xf, int ldx, int K, int valid, uint32_t* xd, float* sig, int warp, int lane) {
+    if (warp >= kMaxB) return;
+    const int col = warp, NG = K / 128;
+    const float* row = xf + (size_t)col * ldx;
+    const bool live = col < valid;
+    for (int g = 0; g < NG; ++g) {
+        const int k = 128 * g + 4 * lane;
+        const float4 v = live ? *reinterpret_cast<const float4*>(row + k) : make_float4(0.f, 0.f, 0.f, 0.f);
+        uint32_t w[3];
+        const float sg = group_digits(v, w);
+        if (lane == 0) sig[col * NG + g] = sg;
+#pragma unroll
+        for (int q = 0; q < 3; ++q) xd[digit_word(k, col, q)] = w[q];
     }
 }
 
@@ -196,43 +203,61 @@ UOCR_DEV void stage_digits(const float* xf, int ldx, int K, int valid, uint32_t*
 // Scratch of the step's routing in shared memory.
 struct RouteSmem {
     float logits[kMaxB][64];
+    float bias[64];
+    unsigned long long mask[64];  // entries (token * k + r) routed to expert e
     int ids[kMaxB * kDecodeMaxTopk];
     float wts[kMaxB * kDecodeMaxTopk];
-    int cnt[64];
     int rowof[kMaxB * kDecodeMaxTopk];
     unsigned used[2];
+    int wsum[2];
 };
 
-// The rest of MoEGate (decoder.py:500-514) for the B tokens, after K1's logits: softmax with
-// this build's exponential and a fixed butterfly sum, top-k by (p desc, index asc), identical
-// in every CTA. Then the slot table: routed slot u is the u-th used expert; its rows start after
-// the shared experts' S * B rows. CTA 0 also writes ids / wts and the global RouteTable (read
-// by K3). The tokens are staged into xs on the way (rows B..7 zero) for the activation digits.
-UOCR_DEV void cta_route(const DecodeArgs& a, float* xs, int ldx, RouteSmem* rs, SlotTable* tb, int tid,
+// The rest of MoEGate (decoder.py:500-514) for the B tokens, from K1's partials: logit = the 8
+// segment partials added in ascending order, + bias; softmax with this build's exponential and
+// a fixed butterfly sum; top-k by (p desc, index asc) — identical in every CTA. Then the slot
+// table: routed slot u is the u-th used expert; its rows start after the shared experts' S * B
+// rows, its entries in token order. CTA 0 also writes ids / wts and the global RouteTable (read
+// by K3). The inputs arrive by bulk copies on `inb`: the partials into `part` (the last stage
+// buffer, which the producer fills only after the table is ready), the digits and their scales
+// (int8 layers), and the token rows into xs (rows B..7 zero).
+UOCR_DEV void cta_route(const DecodeArgs& a, float* xs, int ldx, uint32_t* xd, float* xsig, float* part,
+                        uint64_t* inb, volatile int* abort_flag, RouteSmem* rs, SlotTable* tb, int tid,
                         unsigned long long* ev) {
     const int warp = tid >> 5, lane = tid & 31;
-    const int H = a.H, B = a.B, E = a.E, k = a.topk;
+    const int H = a.H, B = a.B, E = a.E, k = a.topk, kB = k * B;
     unsigned long long* rv = a.trace ? trace_rec(a, 0, a.trace_items / 2 - 2) : nullptr;  // diagnostics
-    pdl_wait_prior_grid();  // the logits (K1), and through K1 the previous layer's output x
+    // before the wait: this call's inputs that no kernel of the step writes, and scratch resets
+    if (tid < 64) {
+        rs->bias[tid] = a.bias && tid < E ? a.bias[tid] : 0.0f;
+        rs->mask[tid] = 0ull;
+    }
+    for (int i = tid; i < 64 * kMaxB; i += kCW * 32) tb->pos[a.S + i / kMaxB][i % kMaxB] = -1;
+    pdl_wait_prior_grid();  // K1's partials and digits; through K1, the previous layer's output x
     if (ev && tid == 0) ev[1] = global_timer_ns();
-    // the logits, and the tokens (for the activation digits): every load of a batch issued before its stores
-    for (int i = tid; i < B * 64; i += kCW * 32) rs->logits[i >> 6][i & 63] = __ldcg(a.logits + i);
-    for (int i0 = 0; i0 < kMaxB * (H / 4); i0 += 10 * kCW * 32) {
-        float4 v[10];
-#pragma unroll
-        for (int j = 0; j < 10; ++j) {
-            const int i = i0 + j * kCW * 32 + tid;
-            v[j] = (i < kMaxB * (H / 4) && i / (H / 4) < B) ? __ldcg(reinterpret_cast<const float4*>(a.x) + i)
-                                                            : make_float4(0.f, 0.f, 0.f, 0.f);
-        }
-#pragma unroll
-        for (int j = 0; j < 10; ++j) {
-            const int i = i0 + j * kCW * 32 + tid;
-            if (i < kMaxB * (H / 4)) *reinterpret_cast<float4*>(xs + (size_t)(i / (H / 4)) * ldx + 4 * (i % (H / 4))) = v[j];
-        }
+    if (warp == 0) {
+        const uint32_t pbytes = (uint32_t)B * 64 * 8 * 4;
+        const uint32_t dbytes = a.int8 ? (uint32_t)H * 24 : 0u, sbytes = a.int8 ? 8u * (H / 128) * 4 : 0u;
+        if (lane == 0) mbar_arrive_expect_tx(inb, pbytes + dbytes + sbytes + (uint32_t)B * H * 4);
+        __syncwarp();
+        if (lane == 0) bulk_g2s(part, a.logits, pbytes, inb);
+        if (lane == 1 && dbytes) bulk_g2s(xd, a.xdig, dbytes, inb);
+        if (lane == 2 && sbytes) bulk_g2s(xsig, a.xsig, sbytes, inb);
+        if (lane >= 8 && lane < 8 + B) bulk_g2s(xs + (size_t)(lane - 8) * ldx, a.x + (size_t)(lane - 8) * H, H * 4, inb);
+    }
+    for (int i = B * (H / 4) + tid; i < kMaxB * (H / 4); i += kCW * 32)
+        *reinterpret_cast<float4*>(xs + (size_t)(i / (H / 4)) * ldx + 4 * (i % (H / 4))) = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (!mbar_wait_warp(inb, 0, abort_flag, &a.ctl->status)) *abort_flag = 1;
+    if (rv && tid == 0) rv[0] = global_timer_ns();
+    for (int i = tid; i < B * 64; i += kCW * 32) {
+        const float4 p0 = *reinterpret_cast<const float4*>(part + 8 * i);
+        const float4 p1 = *reinterpret_cast<const float4*>(part + 8 * i + 4);
+        float total = __fadd_rn(__fadd_rn(__fadd_rn(p0.x, p0.y), p0.z), p0.w);
+        total = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(total, p1.x), p1.y), p1.z), p1.w);
+        if (a.bias) total = __fadd_rn(total, rs->bias[i & 63]);
+        rs->logits[i >> 6][i & 63] = total;
     }
     named_bar_sync(kBarConsumers, kCW * 32);
-    if (rv && tid == 0) rv[0] = global_timer_ns();
+    if (rv && tid == 0) rv[3] = global_timer_ns();
     // softmax + top-k: warp b serves token b
     if (warp < B) {
         const int b = warp;
@@ -247,21 +272,17 @@ UOCR_DEV void cta_route(const DecodeArgs& a, float* xs, int ldx, RouteSmem* rs, 
         float sum = __fadd_rn(e0, e1);
 #pragma unroll
         for (int off = 16; off >= 1; off >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, off));
-        float p0 = v0 ? __fdiv_rn(e0, sum) : -1.0f;
-        float p1 = v1 ? __fdiv_rn(e1, sum) : -1.0f;
+        // keys: bits of p + 1 (p >= 0, so the order of the keys is the order of p); 0 = no candidate
+        uint32_t k0 = v0 ? __float_as_uint(__fdiv_rn(e0, sum)) + 1u : 0u;
+        uint32_t k1 = v1 ? __float_as_uint(__fdiv_rn(e1, sum)) + 1u : 0u;
         for (int rr = 0; rr < k; ++rr) {
-            float bp = p0;
-            int bi = lane;
-            if (p1 > bp) { bp = p1; bi = lane + 32; }
-#pragma unroll
-            for (int off = 16; off >= 1; off >>= 1) {
-                const float op = __shfl_xor_sync(0xffffffffu, bp, off);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-                if (op > bp || (op == bp && oi < bi)) { bp = op; bi = oi; }
-            }
-            if (bi == lane) p0 = -2.0f;
-            if (bi == lane + 32) p1 = -2.0f;
+            const uint32_t mk = __reduce_max_sync(0xffffffffu, max(k0, k1));
+            const unsigned b0 = __ballot_sync(0xffffffffu, k0 == mk), b1 = __ballot_sync(0xffffffffu, k1 == mk);
+            const int bi = b0 ? __ffs(b0) - 1 : 31 + __ffs(b1);  // the lowest index of the largest p
+            if (bi == lane) k0 = 0u;
+            if (bi == lane + 32) k1 = 0u;
             if (lane == 0) {
+                const float bp = __uint_as_float(mk - 1u);
                 rs->ids[b * k + rr] = bi;
                 rs->wts[b * k + rr] = bp;
                 if (blockIdx.x == 0) {
@@ -272,41 +293,33 @@ UOCR_DEV void cta_route(const DecodeArgs& a, float* xs, int ldx, RouteSmem* rs, 
         }
     }
     named_bar_sync(kBarConsumers, kCW * 32);
-    if (rv && tid == 0) rv[3] = global_timer_ns();
-    // group by expert (threads 0..63 = experts)
-    const int kB = k * B;
-    int c = 0;
-    if (tid < 64) {
-        for (int q = 0; q < kB; ++q) c += (rs->ids[q] == tid);
-        rs->cnt[tid] = c;
+    if (rv && tid == 0) rv[4] = global_timer_ns();
+    // group by expert: entry q = token * k + r sets bit q of its expert's mask
+    if (tid < kB) atomicOr(&rs->mask[rs->ids[tid]], 1ull << tid);
+    named_bar_sync(kBarConsumers, kCW * 32);
+    unsigned long long m = 0ull;
+    int c = 0, incl = 0;
+    if (tid < 64) {  // warps 0, 1: expert tid
+        m = rs->mask[tid];
+        c = __popcll(m);
+        incl = c;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, off);
+            if (lane >= off) incl += v;
+        }
         const unsigned bal = __ballot_sync(0xffffffffu, c > 0);
         if (lane == 0) rs->used[warp] = bal;
+        if (lane == 31) rs->wsum[warp] = incl;
     }
     named_bar_sync(kBarConsumers, kCW * 32);
-    if (rv && tid == 0) rv[4] = global_timer_ns();
     const unsigned long long used = (unsigned long long)rs->used[0] | ((unsigned long long)rs->used[1] << 32);
     RouteTable* g = a.table;
     const bool pub = blockIdx.x == 0;  // CTA 0 publishes the table for K3
     if (tid < 64 && c > 0) {
         const int u = __popcll(used & ((1ull << tid) - 1ull));
         const int row = a.S + u;
-        int base = a.S * B;
-        for (int e = 0; e < tid; ++e) base += rs->cnt[e];
-        int n = 0;
-        for (int t = 0; t < kMaxB; ++t) tb->pos[row][t] = -1;
-        for (int q = 0; q < kB; ++q) {
-            if (rs->ids[q] == tid) {
-                tb->pos[row][q / k] = (signed char)n;
-                tb->token[row][n] = q / k;
-                tb->weight[row][n] = rs->wts[q];
-                rs->rowof[q] = base + n;
-                if (pub) {
-                    g->token[u][n] = q / k;
-                    g->weight[u][n] = rs->wts[q];
-                }
-                ++n;
-            }
-        }
+        const int base = a.S * B + (incl - c) + (warp == 1 ? rs->wsum[0] : 0);
         tb->expert[row] = tid;
         tb->count[row] = c;
         tb->base[row] = base;
@@ -314,6 +327,18 @@ UOCR_DEV void cta_route(const DecodeArgs& a, float* xs, int ldx, RouteSmem* rs, 
             g->expert[u] = tid;
             g->count[u] = c;
             g->base[u] = base;
+        }
+        int n = 0;
+        for (unsigned long long mm = m; mm; mm &= mm - 1ull, ++n) {
+            const int q = __ffsll((long long)mm) - 1, t = q / k;
+            tb->pos[row][t] = (signed char)n;
+            tb->token[row][n] = t;
+            tb->weight[row][n] = rs->wts[q];
+            rs->rowof[q] = base + n;
+            if (pub) {
+                g->token[u][n] = t;
+                g->weight[u][n] = rs->wts[q];
+            }
         }
     }
     if (tid == 0) {
@@ -338,6 +363,8 @@ UOCR_DEV void cta_route(const DecodeArgs& a, float* xs, int ldx, RouteSmem* rs, 
             g->tok_w[tid][s] = rs->wts[tid * k + ord[s]];
         }
     }
+    // `part` lives in a stage buffer the producer fills next with the async proxy
+    fence_proxy_async_smem();
     named_bar_sync(kBarConsumers, kCW * 32);
     if (rv && tid == 0) rv[6] = global_timer_ns();
 }
@@ -366,78 +393,89 @@ UOCR_DEV void slot_range(long long pre, long long c, int n, const Partition& p, 
 }
 
 // ======================================================================================
-// K1: router logits
+// K1: router logit partials and the activation digits
 // ======================================================================================
-// CTA e computes expert e's logits for the B tokens: thread (segment s, token t) runs the
-// oracle's chain over segment s (fma in ascending k from +0); the 8 segment sums are added in
-// ascending order, then the bias. The router row is fetched before the dependency wait; the
-// CTA is small (64 threads, 256 B of shared memory) so it fits beside the other kernels' CTAs.
+// One warp per CTA. CTAs [0, 8E): expert e = c / 8, segment s = c % 8; lane t < B runs the
+// oracle's chain for token t over segment s (fma in ascending k from +0) and writes the
+// partial sum part[t][e][s]; K2 adds the 8 partials in ascending order plus the bias. The
+// router segment is fetched before the dependency wait. CTAs [8E, 8E + 8 H/128): column
+// t = d / (H/128), group g = d % (H/128): the int8 digits of x[t][128g, 128g + 128) in K2's
+// fragment order plus the group's scale (zero digits for t >= B). Small CTAs (no shared
+// memory) so several start beside the previous layer's K3 on every SM.
 constexpr int kLogitSteps = 20;  // 8-element steps per segment held in registers (H <= 1280)
 
-__global__ void __launch_bounds__(64)
+__global__ void __launch_bounds__(32)
 decode_logits_kernel(DecodeArgs a) {
-    __shared__ float part[8][kMaxB];
-    const int e = blockIdx.x, s = threadIdx.x >> 3, t = threadIdx.x & 7;
-    const int H = a.H, L = H / 8, nit = L / 8;
-    const uint16_t* w = a.router + (size_t)e * H + s * L;
-    uint4 r[kLogitSteps];
-#pragma unroll
-    for (int i = 0; i < kLogitSteps; ++i)
-        if (i < nit) r[i] = ldg_nc_v4(w + 8 * i);
+    const int c = blockIdx.x, lane = threadIdx.x;
+    const int H = a.H;
     // diagnostics: start, past the dependency wait, done
-    unsigned long long* ev = a.trace ? trace_rec(a, 1, a.trace_items / 2 - 2) : nullptr;
-    if (ev && threadIdx.x == 0) ev[0] = global_timer_ns();
-    pdl_launch_dependents();  // K2 launches now; it waits for this grid before it reads the logits
-    pdl_wait_prior_grid();    // x is the previous layer's output
-    if (ev && threadIdx.x == 0) ev[1] = global_timer_ns();
-    float acc = 0.0f;
-    if (t < a.B) {
-        const float* x = a.x + (size_t)t * H + s * L;
-        if (nit <= kLogitSteps) {
+    unsigned long long* ev = a.trace && c < 64 ? trace_rec(a, 1, a.trace_items / 2 - 2) : nullptr;
+    if (ev && lane == 0) ev[0] = global_timer_ns();
+    if (c < a.E * 8) {
+        const int e = c >> 3, s = c & 7, L = H / 8, nit = L / 8;
+        const uint16_t* w = a.router + (size_t)e * H + s * L;
+        uint4 r[kLogitSteps];
+        if (lane < a.B) {
 #pragma unroll
-            for (int half = 0; half < 2; ++half) {
-                constexpr int kHalf = kLogitSteps / 2;
-                float4 xv[2 * kHalf];  // this half's 8-element steps of x, all loads issued first
-#pragma unroll
-                for (int i = 0; i < kHalf; ++i) {
-                    const int q = half * kHalf + i;
-                    if (q < nit) {
-                        xv[2 * i] = __ldcg(reinterpret_cast<const float4*>(x + 8 * q));
-                        xv[2 * i + 1] = __ldcg(reinterpret_cast<const float4*>(x + 8 * q + 4));
-                    }
-                }
-#pragma unroll
-                for (int i = 0; i < kHalf; ++i) {
-                    const int q = half * kHalf + i;
-                    if (q < nit) {
-                        float f[8];
-                        unpack_bf16x8(r[q], f);
-                        const float x8[8] = {xv[2 * i].x,     xv[2 * i].y,     xv[2 * i].z,     xv[2 * i].w,
-                                             xv[2 * i + 1].x, xv[2 * i + 1].y, xv[2 * i + 1].z, xv[2 * i + 1].w};
-#pragma unroll
-                        for (int j = 0; j < 8; ++j) acc = __fmaf_rn(f[j], x8[j], acc);
-                    }
-                }
-            }
-        } else {
-            for (int kk = 0; kk < L; kk += 8) {
-                float f[8];
-                unpack_bf16x8(ldg_nc_v4(w + kk), f);
-#pragma unroll
-                for (int j = 0; j < 8; ++j) acc = __fmaf_rn(f[j], __ldcg(x + kk + j), acc);
-            }
+            for (int i = 0; i < kLogitSteps; ++i)
+                if (i < nit) r[i] = ldg_nc_v4(w + 8 * i);
         }
-    }
-    part[s][t] = acc;
-    __syncthreads();
-    if (s == 0 && t < a.B) {
-        float total = part[0][t];
+        pdl_launch_dependents();  // K2 launches now; it waits for this grid before it reads the partials
+        pdl_wait_prior_grid();    // x is the previous layer's output
+        if (ev && lane == 0) ev[1] = global_timer_ns();
+        float acc = 0.0f;
+        if (lane < a.B) {
+            const float* x = a.x + (size_t)lane * H + s * L;
+            if (nit <= kLogitSteps) {
 #pragma unroll
-        for (int q = 1; q < 8; ++q) total = __fadd_rn(total, part[q][t]);
-        if (a.bias) total = __fadd_rn(total, a.bias[e]);
-        a.logits[t * 64 + e] = total;
+                for (int half = 0; half < 2; ++half) {
+                    constexpr int kHalf = kLogitSteps / 2;
+                    float4 xv[2 * kHalf];  // this half's 8-element steps of x, all loads issued first
+#pragma unroll
+                    for (int i = 0; i < kHalf; ++i) {
+                        const int q = half * kHalf + i;
+                        if (q < nit) {
+                            xv[2 * i] = __ldcg(reinterpret_cast<const float4*>(x + 8 * q));
+                            xv[2 * i + 1] = __ldcg(reinterpret_cast<const float4*>(x + 8 * q + 4));
+                        }
+                    }
+#pragma unroll
+                    for (int i = 0; i < kHalf; ++i) {
+                        const int q = half * kHalf + i;
+                        if (q < nit) {
+                            float f[8];
+                            unpack_bf16x8(r[q], f);
+                            const float x8[8] = {xv[2 * i].x,     xv[2 * i].y,     xv[2 * i].z,     xv[2 * i].w,
+                                                 xv[2 * i + 1].x, xv[2 * i + 1].y, xv[2 * i + 1].z, xv[2 * i + 1].w};
+#pragma unroll
+                            for (int j = 0; j < 8; ++j) acc = __fmaf_rn(f[j], x8[j], acc);
+                        }
+                    }
+                }
+            } else {
+                for (int kk = 0; kk < L; kk += 8) {
+                    float f[8];
+                    unpack_bf16x8(ldg_nc_v4(w + kk), f);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc = __fmaf_rn(f[j], __ldcg(x + kk + j), acc);
+                }
+            }
+            a.logits[((size_t)lane * 64 + e) * 8 + s] = acc;
+        }
+    } else {
+        const int d = c - a.E * 8, NG = H / 128, t = d / NG, g = d % NG;
+        pdl_launch_dependents();
+        pdl_wait_prior_grid();
+        const int k = 128 * g + 4 * lane;
+        const float4 v = t < a.B ? __ldcg(reinterpret_cast<const float4*>(a.x + (size_t)t * H + k))
+                                 : make_float4(0.f, 0.f, 0.f, 0.f);
+        uint32_t w[3];
+        const float sg = group_digits(v, w);
+        if (lane == 0) a.xsig[t * NG + g] = sg;
+#pragma unroll
+        for (int q = 0; q < 3; ++q) a.xdig[digit_word(k, t, q)] = w[q];
     }
-    if (ev && threadIdx.x == 0) ev[2] = global_timer_ns();
+    if (ev && lane == 0) ev[2] = global_timer_ns();
 }
 
 // ======================================================================================
@@ -521,6 +559,7 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
     uint64_t* empty = full + nst;
     uint64_t* table_ready = empty + nst;
     uint64_t* redbar = table_ready + 1;  // [kRedBufs]: all warps' partial tiles of an item are stored
+    uint64_t* inb = redbar + kRedBufs;   // the routing's inputs have arrived
     SlotTable* tb = reinterpret_cast<SlotTable*>(smem + off_tbl);
     RouteSmem* rs = reinterpret_cast<RouteSmem*>(smem + off_route);
     ItemMeta* meta = reinterpret_cast<ItemMeta*>(smem + off_meta);
@@ -542,6 +581,7 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
         }
         mbar_init(table_ready, 1);
         for (int b = 0; b < kRedBufs; ++b) mbar_init(&redbar[b], kCW);
+        mbar_init(inb, 1);
         abort_flag = 0;
         fence_mbar_init();
         pdl_launch_dependents();  // K3 launches early; it waits for this grid before it reads h
@@ -561,6 +601,8 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             }
         };
         auto issue = [&](int slot, int blk) {
+            // the last stage holds the routing's logit partials until the table is ready
+            if (round == 0 && st == nst - 1) wait_table();
             if (ok && round > 0 && !mbar_wait_warp(&empty[st], (round - 1) & 1, &abort_flag, &a.ctl->status))
                 ok = false;
             if (!ok) return;
@@ -615,14 +657,10 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
         __syncwarp();
     } else {
         // ---------------- consumers: route, stage the digits, then the items ----------------
-        cta_route(a, xf, ldx, rs, tb, tid, ev);
+        cta_route(a, xf, ldx, xd, xsig, reinterpret_cast<float*>(stages + (size_t)(nst - 1) * stage_bytes), inb,
+                  &abort_flag, rs, tb, tid, ev);
         if (tid == 0) mbar_arrive(table_ready);
-        if (ev && tid == 0) ev[2] = global_timer_ns();
-        if (a.int8) {
-            stage_digits(xf, ldx, a.H, a.B, xd, xsig, warp, lane);
-            named_bar_sync(kBarConsumers, kCW * 32);
-        }
-        if (ev && tid == 0) ev[5] = global_timer_ns();
+        if (ev && tid == 0) ev[2] = ev[5] = global_timer_ns();
         const uint32_t xf_s = smem_addr(xf), xd_s = smem_addr(xd);
         // this warp's activation fragments, fixed for the CTA
         if (ev && tid == 0) ev[3] = global_timer_ns();
@@ -1011,24 +1049,29 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
     cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaDeviceGetAttribute(&sm_smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    // K2 / K3 leave room on their SM for their own static shared memory (a few words) and their
-    // reservation, and for one K1 CTA (256 B + reservation), so K1 can start beside them
-    max_smem = std::min(max_smem - 1024, sm_smem - 1024 - 1024 - (1024 + 256));
+    // K2 / K3 leave room on their SM for their own static shared memory (< 1 KB) and their
+    // reservation, and for K1's CTAs (no shared memory, 1 KB reservation each), so K1 can start
+    // beside them
+    const int k1_ctas = a.E * 8 + kMaxB * (a.H / 128);
+    const int k1_per_sm = (k1_ctas + sms - 1) / sms;
+    max_smem = std::min(max_smem - 1024, sm_smem - 1024 - 1024 - 1024 * k1_per_sm);
     if (g_decode_trace) {
         a.trace = g_decode_trace;
         a.trace_items = (int)(g_decode_trace_bytes / (sizeof(unsigned long long) * 8 * (size_t)sms)) & ~1;
     }
 
-    // ---- K1: logits, one CTA per routed expert
+    // ---- K1: logit partials (one CTA per expert and segment) and the activation digits
     {
         void* args[] = {&a};
-        err = launch_pdl(reinterpret_cast<const void*>(decode_logits_kernel), dim3(a.E), dim3(64), 0, st, args);
+        err = launch_pdl(reinterpret_cast<const void*>(decode_logits_kernel), dim3(k1_ctas), dim3(32), 0, st, args);
         if (err != cudaSuccess) return err;
     }
     // ---- K2: route + gate/up; a stage holds one w13 block
     {
         uint32_t stage_bytes = (uint32_t)up(
-            std::max(w13_block_bytes(a.H, a.G, false), a.int8 ? w13_block_bytes(a.H, a.G, true) : size_t(0)), 128);
+            std::max({w13_block_bytes(a.H, a.G, false), a.int8 ? w13_block_bytes(a.H, a.G, true) : size_t(0),
+                      sizeof(float) * kMaxB * 64 * 8}),  // the last stage first holds the logit partials
+            128);
         const size_t off_tbl = 256;
         const size_t off_route = off_tbl + up(sizeof(SlotTable), 128);
         const size_t off_meta = off_route + up(sizeof(RouteSmem), 128);

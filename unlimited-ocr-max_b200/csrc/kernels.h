@@ -63,7 +63,9 @@ struct DecodeArgs {
     float* y;       // [(k+S)*B, H], slot-contiguous rows
     float* out;     // [B, H]
     DecodeCtl* ctl;
-    float* logits;       // [8][64]
+    float* logits;       // [8][64][8] router logit partials (token, expert, segment)
+    uint32_t* xdig;      // [H / 32][3][32][2] words: x as int8 digits in fragment order (K1 -> K2)
+    float* xsig;         // [8][H / 128] scales of the digit groups
     RouteTable* table;
     unsigned long long* trace;  // optional per-CTA item timeline (diagnostics), null = off
     int trace_items;            // items recorded per CTA
