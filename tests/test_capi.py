@@ -133,14 +133,17 @@ def test_config_validation(uocr):
 
 
 def test_packed_sizes_and_refusals(uocr):
-    """Packed block sizes follow the layout; bad packing calls are refused on the host."""
+    """Packed item sizes follow the layout; bad packing calls are refused on the host."""
     L = uocr.load()
-    # every packed row carries 16 bytes of padding; int8 w13: per block of 16 row pairs
-    # 32 rows of (H + 16) bytes + 2*16*(H/128) fp32 scales
-    assert L.uocr_moe_w13_bytes(64, 896, 1280, 128, 1) == 64 * (896 // 16) * (32 * (1280 + 16) + 2 * 16 * 10 * 4)
-    assert L.uocr_moe_w13_bytes(64, 896, 1280, 128, 0) == 64 * (896 // 8) * 16 * (2 * 1280 + 16)
-    assert L.uocr_moe_w2_bytes(64, 1280, 896, 128, 1) == 64 * (1280 // 32) * (32 * (896 + 16) + 32 * 7 * 4)
-    assert L.uocr_moe_w2_bytes(64, 1280, 896, 128, 0) == 64 * 1280 * (2 * 896 + 16)
+    # items: atoms of 128 rows x 128 bytes (+ int8 scales, one fp32 per row and atom); gate|up
+    # row blocks of 64 pairs with 2 atoms per item, down row blocks of 128 rows (int8: 1 atom)
+    atom = 128 * 128
+    assert L.uocr_moe_w13_bytes(64, 896, 1280, 128, 1) == 64 * 14 * 5 * (2 * atom + 2 * 128 * 4)
+    assert L.uocr_moe_w13_bytes(64, 896, 1280, 128, 0) == 64 * 14 * 10 * 2 * atom
+    assert L.uocr_moe_w2_bytes(64, 1280, 896, 128, 1) == 64 * 10 * 7 * (atom + 128 * 4)
+    assert L.uocr_moe_w2_bytes(64, 1280, 896, 128, 0) == 64 * 10 * 7 * 2 * atom
+    assert L.uocr_moe_w13_bytes(64, 896, 1280, 128, 0) == 64 * 2 * 896 * 1280 * 2  # bf16: no padding
+    assert L.uocr_moe_w13_bytes(64, 896, 1152, 128, 1) == 0  # int8 gate|up needs H % 256
     assert L.uocr_moe_w13_bytes(64, 896, 1280, 64, 1) == 0  # only the checkpoint's G = 128
     rc = L.uocr_moe_pack_w13(None, None, None, None, 4, 100, 256, 128, 0, None, None)
     assert rc == 1 and b"pack_w13" in L.uocr_last_error()

@@ -1,7 +1,9 @@
-"""The packed weight blocks (uocr_moe_pack_w13 / _w2 / _shared) byte for byte against a numpy
-statement of the layout: every row followed by 16 zero bytes; w13 blocks of P row pairs
-[gate P rows | up P rows | int8: gate scales | up scales] (P = 8 bf16, 16 int8); w2 blocks of
-32 rows [rows | int8: scales]."""
+"""The packed weight items (uocr_moe_pack_w13 / _w2 / _shared) byte for byte against a numpy
+statement of the layout: row blocks of 128 rows; an item is `atoms` K ranges of 128 bytes per
+row, each a [128 rows][128 B] atom with the 16-byte chunks of row r permuted c -> c ^ (r % 8)
+(128-byte swizzle), then for int8 the fp32 scales [atom][row]. gate|up row blocks hold 64 pairs
+interleaved by 8 (rows 16i..16i+7 gate, 16i+8..16i+15 up), 2 atoms per item; down row blocks
+hold 128 output rows, 1 (int8) or 2 (bf16) atoms per item."""
 
 from __future__ import annotations
 
@@ -13,22 +15,43 @@ pytestmark = pytest.mark.gpu
 DEV = "cuda"
 
 
-PAD = 16
+def swizzle(atom: np.ndarray) -> bytes:
+    """[R, 128] uint8 -> the 128-byte-swizzled atom."""
+    R = atom.shape[0]
+    chunks = atom.reshape(R, 8, 16)
+    out = np.empty_like(chunks)
+    dst = np.arange(8)[None, :] ^ (np.arange(R) % 8)[:, None]
+    out[np.arange(R)[:, None], dst] = chunks
+    return out.tobytes()
 
 
-def padded(rows: np.ndarray) -> bytes:
-    return b"".join(r.tobytes() + bytes(PAD) for r in rows)
+def items(rows: np.ndarray, scales, atoms: int) -> bytes:
+    """rows: [128, K] (int8 or uint16) of one row block; scales [128, K/128] fp32 or None."""
+    raw = rows.view(np.uint8).reshape(128, -1)
+    out = bytearray()
+    per_item = atoms * 128
+    for i0 in range(0, raw.shape[1], per_item):
+        for a in range(atoms):
+            out += swizzle(np.ascontiguousarray(raw[:, i0 + a * 128:i0 + (a + 1) * 128]))
+        if scales is not None:
+            g0 = i0 // 128  # int8: one byte per element, so byte offset / 128 = group
+            for a in range(atoms):
+                out += np.ascontiguousarray(scales[:, g0 + a]).astype(np.float32).tobytes()
+    return bytes(out)
 
 
-def w13_ref(gate: np.ndarray, up: np.ndarray, gs, us, P: int) -> bytes:
+def w13_ref(gate: np.ndarray, up: np.ndarray, gs, us) -> bytes:
     E, I, H = gate.shape
+    r = np.arange(128)
+    pair = (r >> 4) * 8 + (r & 7)
+    is_up = (r & 15) >= 8
     out = bytearray()
     for e in range(E):
-        for b in range(I // P):
-            rows = slice(b * P, (b + 1) * P)
-            out += padded(gate[e, rows]) + padded(up[e, rows])
-            if gs is not None:
-                out += gs[e, rows].tobytes() + us[e, rows].tobytes()
+        for rb in range(I // 64):
+            p = 64 * rb + pair
+            rows = np.where(is_up[:, None], up[e, p], gate[e, p])
+            sc = None if gs is None else np.where(is_up[:, None], us[e, p], gs[e, p])
+            out += items(rows, sc, 2)
     return bytes(out)
 
 
@@ -36,11 +59,9 @@ def w2_ref(down: np.ndarray, ds) -> bytes:
     E, H, I = down.shape
     out = bytearray()
     for e in range(E):
-        for b in range(H // 32):
-            rows = slice(b * 32, (b + 1) * 32)
-            out += padded(down[e, rows])
-            if ds is not None:
-                out += ds[e, rows].tobytes()
+        for rb in range(H // 128):
+            j = slice(128 * rb, 128 * rb + 128)
+            out += items(down[e, j], None if ds is None else ds[e, j], 1 if ds is not None else 2)
     return bytes(out)
 
 
@@ -71,8 +92,7 @@ def test_pack_routed_blocks(uocr, int8):
                                o13.data_ptr(), st) == 0, L.uocr_last_error()
     assert L.uocr_moe_pack_w2(td.data_ptr(), ptr(tds), E, H, I, G, int(int8), o2.data_ptr(), st) == 0
     torch.cuda.synchronize()
-    P = 16 if int8 else 8
-    assert o13.cpu().numpy().tobytes() == w13_ref(gate, up, gs, us, P)
+    assert o13.cpu().numpy().tobytes() == w13_ref(gate, up, gs, us)
     assert o2.cpu().numpy().tobytes() == w2_ref(down, ds)
 
 
@@ -88,6 +108,6 @@ def test_pack_shared_blocks(uocr):
     assert L.uocr_moe_pack_shared(dev(gate).data_ptr(), dev(up).data_ptr(), dev(down).data_ptr(), S, I, H,
                                   o13.data_ptr(), o2.data_ptr(), torch.cuda.current_stream().cuda_stream) == 0
     torch.cuda.synchronize()
-    assert o13.cpu().numpy().tobytes() == w13_ref(gate.reshape(S, I, H), up.reshape(S, I, H), None, None, 8)
+    assert o13.cpu().numpy().tobytes() == w13_ref(gate.reshape(S, I, H), up.reshape(S, I, H), None, None)
     want2 = np.stack([down[:, q * I:(q + 1) * I] for q in range(S)])
-    assert o2.cpu().numpy().tobytes() == padded(want2.reshape(S * H, I))
+    assert o2.cpu().numpy().tobytes() == w2_ref(want2, None)

@@ -171,58 +171,71 @@ int uocr_dense_bf16_qmv(float* out, int64_t out_rows, int64_t out_cols, const fl
 // packing
 // ---------------------------------------------------------------------------------------
 
-static int check_pack(const char* who, int64_t E, int64_t N, int64_t K, int64_t G, int int8) {
-    if (E < 1 || N < 1 || K < 1) return fail(UOCR_EINVAL, "%s: empty stack", who);
-    if (K % 128) return fail(UOCR_EINVAL, "%s: K=%lld is not a multiple of 128", who, (long long)K);
+static int check_pack(const char* who, int64_t E, int64_t G, int int8) {
+    if (E < 1) return fail(UOCR_EINVAL, "%s: empty stack", who);
     if (int8 && (G != 128)) return fail(UOCR_EUNSUPPORTED, "%s: int8 group size %lld (this build packs G = 128)", who, (long long)G);
     return ok();
 }
+static bool a16p(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+// gate|up: I a multiple of 64 (row blocks of 64 pairs); H a multiple of 256 (int8) / 128 (bf16)
+static bool w13_dims_ok(int64_t I, int64_t H, int int8) {
+    return I >= 64 && I % 64 == 0 && H >= 128 && H % (int8 ? 256 : 128) == 0 && I <= INT32_MAX && H <= INT32_MAX;
+}
+// down: H a multiple of 128 (row blocks), I a multiple of 128
+static bool w2_dims_ok(int64_t H, int64_t I) {
+    return H >= 128 && H % 128 == 0 && I >= 128 && I % 128 == 0 && I <= INT32_MAX && H <= INT32_MAX;
+}
 
 size_t uocr_moe_w13_bytes(int64_t E, int64_t I, int64_t H, int64_t group, int int8) {
-    if (E < 1 || I < 16 || H < 128 || I % 16 || H % 128 || (int8 && group != 128)) return 0;
-    return (size_t)E * uocr::w13_expert_bytes((int)I, (int)H, (int)(int8 ? group : 128), int8 != 0);
+    if (E < 1 || !w13_dims_ok(I, H, int8) || (int8 && group != 128)) return 0;
+    return (size_t)E * uocr::w13_expert_bytes((int)I, (int)H, int8 != 0);
 }
 
 size_t uocr_moe_w2_bytes(int64_t E, int64_t H, int64_t I, int64_t group, int int8) {
-    if (E < 1 || I < 128 || H < 32 || I % 128 || H % 32 || (int8 && group != 128)) return 0;
-    return (size_t)E * uocr::w2_expert_bytes((int)H, (int)I, (int)(int8 ? group : 128), int8 != 0);
+    if (E < 1 || !w2_dims_ok(H, I) || (int8 && group != 128)) return 0;
+    return (size_t)E * uocr::w2_expert_bytes((int)H, (int)I, int8 != 0);
 }
 
 int uocr_moe_pack_w13(const void* gate, const void* up, const float* gate_scales, const float* up_scales, int64_t E,
                       int64_t I, int64_t H, int64_t group, int int8, void* w13_out, uocr_stream_t stream) {
-    int rc = check_pack("pack_w13", E, I, H, group, int8);
+    int rc = check_pack("pack_w13", E, group, int8);
     if (rc) return rc;
-    if (I % 16) return fail(UOCR_EINVAL, "pack_w13: I=%lld is not a multiple of 16", (long long)I);
+    if (!w13_dims_ok(I, H, int8))
+        return fail(UOCR_EINVAL, "pack_w13: I=%lld must be a multiple of 64 and H=%lld of %d", (long long)I,
+                    (long long)H, int8 ? 256 : 128);
     if (!gate || !up || !w13_out || (int8 && (!gate_scales || !up_scales)))
         return fail(UOCR_EINVAL, "pack_w13: null pointer");
-    if ((reinterpret_cast<uintptr_t>(gate) | reinterpret_cast<uintptr_t>(up) | reinterpret_cast<uintptr_t>(w13_out) |
-         reinterpret_cast<uintptr_t>(gate_scales) | reinterpret_cast<uintptr_t>(up_scales)) & 3)
-        return fail(UOCR_EINVAL, "pack_w13: pointers must be 4-byte aligned");
-    return cuda_status(uocr::launch_pack_w13(gate, up, gate_scales, up_scales, (int)E, (int)I, (int)H,
-                                             int8 ? (int)group : 128, int8 != 0, w13_out, S(stream)),
+    if (!a16p(gate) || !a16p(up) || !a16p(w13_out) || ((reinterpret_cast<uintptr_t>(gate_scales) |
+                                                        reinterpret_cast<uintptr_t>(up_scales)) & 3))
+        return fail(UOCR_EINVAL, "pack_w13: weights and output must be 16-byte aligned, scales 4-byte aligned");
+    return cuda_status(uocr::launch_pack_w13(gate, up, gate_scales, up_scales, (int)E, (int)I, (int)H, int8 != 0,
+                                             (long)(I * H), (long)H, w13_out, S(stream)),
                        "pack_w13: launch");
 }
 
 int uocr_moe_pack_w2(const void* down, const float* down_scales, int64_t E, int64_t H, int64_t I, int64_t group,
                      int int8, void* w2_out, uocr_stream_t stream) {
-    int rc = check_pack("pack_w2", E, H, I, group, int8);
+    int rc = check_pack("pack_w2", E, group, int8);
     if (rc) return rc;
-    if (H % 32) return fail(UOCR_EINVAL, "pack_w2: H=%lld is not a multiple of 32", (long long)H);
+    if (!w2_dims_ok(H, I))
+        return fail(UOCR_EINVAL, "pack_w2: H=%lld and I=%lld must be multiples of 128", (long long)H, (long long)I);
     if (!down || !w2_out || (int8 && !down_scales)) return fail(UOCR_EINVAL, "pack_w2: null pointer");
-    if ((reinterpret_cast<uintptr_t>(down) | reinterpret_cast<uintptr_t>(w2_out) |
-         reinterpret_cast<uintptr_t>(down_scales)) & 3)
-        return fail(UOCR_EINVAL, "pack_w2: pointers must be 4-byte aligned");
-    return cuda_status(uocr::launch_pack_w2(down, down_scales, (int)E, (int)H, (int)I, int8 ? (int)group : 128,
-                                            int8 != 0, w2_out, S(stream)),
+    if (!a16p(down) || !a16p(w2_out) || (reinterpret_cast<uintptr_t>(down_scales) & 3))
+        return fail(UOCR_EINVAL, "pack_w2: weights and output must be 16-byte aligned, scales 4-byte aligned");
+    return cuda_status(uocr::launch_pack_w2(down, down_scales, (int)E, (int)H, (int)I, int8 != 0, (long)(H * I),
+                                            (long)I, w2_out, S(stream)),
                        "pack_w2: launch");
 }
 
 int uocr_moe_pack_shared(const uint16_t* gate, const uint16_t* up, const uint16_t* down, int64_t S_, int64_t I,
                          int64_t H, uint16_t* w13_out, uint16_t* w2_out, uocr_stream_t stream) {
     if (S_ < 1 || I < 1 || H < 1) return fail(UOCR_EINVAL, "pack_shared: empty");
-    if (I % 128) return fail(UOCR_EINVAL, "pack_shared: I=%lld is not a multiple of 128", (long long)I);
-    if (H % 128) return fail(UOCR_EINVAL, "pack_shared: H=%lld is not a multiple of 128", (long long)H);
+    if (!w13_dims_ok(I, H, 0) || !w2_dims_ok(H, I))
+        return fail(UOCR_EINVAL, "pack_shared: I=%lld and H=%lld must be multiples of 128", (long long)I, (long long)H);
     if (!gate || !up || !down || !w13_out || !w2_out) return fail(UOCR_EINVAL, "pack_shared: null pointer");
+    if (!a16p(gate) || !a16p(up) || !a16p(down) || !a16p(w13_out) || !a16p(w2_out))
+        return fail(UOCR_EINVAL, "pack_shared: pointers must be 16-byte aligned");
     return cuda_status(uocr::launch_pack_shared(gate, up, down, S_, I, H, w13_out, w2_out, S(stream)),
                        "pack_shared: launch");
 }
@@ -261,7 +274,7 @@ int uocr_moe_route(const float* x, int64_t T, int64_t H, const uint16_t* router,
 namespace {
 
 struct DecodeLayout {
-    size_t ctl, logits, xdig, xsig, table, ids, wts, h, y, total;
+    size_t ctl, logits, xd, xb, xsig, table, ids, wts, h, y, total;
 };
 
 DecodeLayout decode_layout(const uocr_moe_layer* L, int64_t B) {
@@ -270,7 +283,8 @@ DecodeLayout decode_layout(const uocr_moe_layer* L, int64_t B) {
     size_t off = 0;
     d.ctl = off; off += align256(sizeof(uocr::DecodeCtl));
     d.logits = off; off += align256(sizeof(float) * 8 * 64 * 8);
-    d.xdig = off; off += align256((size_t)L->hidden * 24);
+    d.xd = off; off += align256((size_t)L->hidden * 32);
+    d.xb = off; off += align256((size_t)L->hidden * 32);
     d.xsig = off; off += align256(sizeof(float) * 8 * (size_t)(L->hidden / 128));
     d.table = off; off += align256(sizeof(uocr::RouteTable));
     d.ids = off; off += align256(sizeof(int32_t) * (size_t)B * L->top_k);
@@ -292,6 +306,8 @@ int check_layer(const uocr_moe_layer* L, const char* who) {
     if (L->top_k < 1 || L->top_k > L->n_routed) return fail(UOCR_EINVAL, "%s: top_k=%d outside [1, E]", who, L->top_k);
     if (L->int8 && L->group != 128)
         return fail(UOCR_EUNSUPPORTED, "%s: int8 experts need the checkpoint's group size 128", who);
+    if (L->int8 && L->hidden % 256)
+        return fail(UOCR_EUNSUPPORTED, "%s: int8 experts need hidden=%d to be a multiple of 256", who, L->hidden);
     if (L->top_k > uocr::kDecodeMaxTopk)
         return fail(UOCR_EUNSUPPORTED, "%s: top_k=%d above %d", who, L->top_k, uocr::kDecodeMaxTopk);
     if (!L->router || !L->w13 || !L->w2) return fail(UOCR_EINVAL, "%s: null weight pointer", who);
@@ -336,7 +352,8 @@ int uocr_moe_decode(const uocr_moe_layer* L, const float* x, int64_t B, const fl
     a.out = out;
     a.ctl = reinterpret_cast<uocr::DecodeCtl*>(ws + d.ctl);
     a.logits = reinterpret_cast<float*>(ws + d.logits);
-    a.xdig = reinterpret_cast<uint32_t*>(ws + d.xdig);
+    a.xd = reinterpret_cast<unsigned char*>(ws + d.xd);
+    a.xb = reinterpret_cast<unsigned char*>(ws + d.xb);
     a.xsig = reinterpret_cast<float*>(ws + d.xsig);
     a.table = reinterpret_cast<uocr::RouteTable*>(ws + d.table);
     return cuda_status(uocr::launch_decode_layer(a, S(stream)), "moe_decode: launch");
@@ -467,7 +484,8 @@ int uocr_moe_device_status(const void* workspace, uocr_stream_t stream) {
     if (status) {
         // sticky until read: clear it so the next failure is reported afresh
         cudaMemset(const_cast<void*>(workspace), 0, sizeof status);
-        return fail(UOCR_EDEVICE, "device_status: a device-side wait gave up (code %u)", status);
+        return fail(UOCR_EDEVICE, "device_status: a device-side check failed (code %u: %s)", status,
+                    status == 1 ? "a bounded wait gave up" : status == 2 ? "shared memory misaligned" : "unknown");
     }
     return ok();
 }

@@ -13,6 +13,7 @@ namespace uocr {
 enum DeviceStatus : uint32_t {
     kStatusOk = 0,
     kStatusWaitTimeout = 1,  // a spin/mbarrier wait exceeded its iteration budget
+    kStatusMisaligned = 2,   // a kernel's shared-memory window was not aligned as its operands need
 };
 
 UOCR_DEV void set_status(uint32_t* status, uint32_t code) {

@@ -1,27 +1,34 @@
 // Decode-step MoE sublayer (MoE.decode_rows, unlimited_ocr_max/decoder.py:641-655) for B <= 8
 // tokens: three kernels chained by programmatic dependent launch (PDL); K2 and K3 are persistent
-// and stream their weights from HBM once.
+// (one CTA per SM) and stream their weights from HBM once, through the tcgen05 tensor cores.
 //
-//   K1 logits            one small CTA per routed expert: the fp32 router logits of the B tokens
-//              in the oracle's order (router row fetched before the dependency wait).
-//   K2 route + gate/up   every CTA finishes the routing itself from K1's logits (softmax, top-k:
-//              bit-exact and identical in every CTA, so no grid-wide exchange) while its
-//              producer already streams shared-expert blocks; the routing groups the step by
+//   K1 logits + operands   one warp per CTA: the fp32 router logit partials of (expert,
+//              segment) in the oracle's order, and the tokens as tensor-core B operands
+//              (int8 digits, bf16 terms) in the swizzled shared-memory image.
+//   K2 route + gate/up     every CTA finishes the routing itself from K1's partials (softmax,
+//              top-k: bit-exact and identical in every CTA, so no grid-wide exchange) while its
+//              producer already streams shared-expert items; the routing groups the step by
 //              expert ("slots": 0..S-1 the shared experts, S+u the u-th distinct routed expert in
 //              ascending id), each slot owning contiguous rows of the h and y scratch.
-//              Items (slot, block of 8 or 16 row pairs) -> h[slot row][n] = silu(g) * u.
-//   K3 down + combine    items (slot, 32 output rows) -> y[slot row][j]; then a grid barrier
-//              (K3's CTAs, one per SM, are all resident) and every CTA sums its 1/grid slice of
-//              the B x H outputs over each token's slots in a fixed order: out[t][j].
-// A slot's arithmetic uses only its own token rows, and each output sums a token's slots in
-// ascending order, so every output row is bitwise independent of the batch.
+//              Units (slot, row block of 64 gate|up pairs) -> h[slot row][pair] = silu(g) * u.
+//   K3 down + combine      units (slot, row block of 128 output rows) -> y[slot row][j]; then a
+//              grid barrier and every CTA sums its 1/grid slice of the B x H outputs over each
+//              token's slots in a fixed order: out[t][j].
 //
-// One producer warp copies each item with a single cp.async.bulk (the weights are repacked so
-// an item is one contiguous block, layout.h; K3 adds one copy of the slot's h rows) into
-// shared memory; all 8 consumer warps work on the same item, each on its own rows, with the
-// tokens' activations held in registers. A bulk copy costs ~0.2 us to issue, so blocks of
-// 28-58 KB are what keeps 100+ KB in flight per SM. Work is split over the CTAs by a static
-// partition weighted by each item's cost (bytes and tokens).
+// Inside K2 / K3 (9 warps): warp 8 copies each item (a row block's weights over one K range,
+// layout.h) with one cp.async.bulk into shared memory; warp 0 issues the item's tcgen05.mma
+// (M = 128 weight rows, N = 32: three int8 digit planes x 8 tokens, or N = 16: two bf16 terms x
+// 8 tokens; accumulators in TMEM); warps 4-7 read the accumulators back (tcgen05.ld: one TMEM
+// lane per weight row), apply the int8 group scales and finish the row block; in K3 warps 1-3
+// convert each slot's h rows into the B operand. Work is split over the CTAs by a static
+// partition of the units weighted by their bytes.
+//
+// Exact activations: an fp32 value v is given to the int8 MMA as three int8 digits with a
+// power-of-two scale per (token, 128-group), v = sigma (d0 + d1/128 + d2/128^2), |d| <= 64, the
+// int32 sums recombined in fp32 per group before the weight scale (error < 2^-21 of the group's
+// largest value); to the bf16 MMA as two bf16 terms v = t0 + t1 (t0 = bf16(v), t1 = bf16(v - t0)).
+// Every output element is its own dot product, so every output row is bitwise independent of
+// the batch it rides in.
 //
 // Every device-side wait is bounded (sm100.cuh, kWaitBudgetNs): on expiry the waiter records a
 // status code in the workspace and the kernel winds down without writing its output.
@@ -30,17 +37,23 @@
 #include "common.cuh"
 #include "kernels.h"
 #include "layout.h"
-#include "mma.cuh"
+#include "digits.cuh"
 #include "sm100.cuh"
 
 namespace uocr {
 
-constexpr int kCW = 8;                       // consumer warps (K2 and K3)
-constexpr int kThreads = (kCW + 1) * 32;     // + producer warp
+constexpr int kThreads = 9 * 32;             // K2, K3: MMA warp 0, stagers 1-3, epilogue 4-7, producer 8
+constexpr int kCW = 8;                       // warps 0-7 (K2's routing)
 constexpr int kMaxB = 8;
 constexpr int kMaxSlotsSm = 72;              // shared (<= 8) + routed (<= 64)
 constexpr int kK3Desc = 8;                   // K3 items in flight (descriptor ring)
-constexpr uint32_t kBarConsumers = 1;        // named barrier of the 8 consumer warps
+constexpr uint32_t kBarConsumers = 1;        // named barrier of warps 0-7
+constexpr int kAccSlots = 4;                 // TMEM accumulators of 32 columns
+constexpr uint32_t kTmemCols = 128;
+constexpr int kDigitAtomBytes = 32 * 128;    // int8 B operand atom: 3 digit planes x 8 tokens + 8 pad rows
+constexpr int kTermAtomBytes = 16 * 128;     // bf16 B operand atom: 2 terms x 8 tokens
+constexpr uint32_t kIdescS8 = umma_idesc_s8(128, 32);
+constexpr uint32_t kIdescBf16 = umma_idesc_bf16(128, 16);
 
 // Slots of this step in shared memory: rows [0, S) the shared experts, [S, S+U) routed.
 struct SlotTable {
@@ -55,10 +68,21 @@ struct SlotTable {
 };
 
 struct ItemMeta {
-    int slot;  // < 0: end of the work
-    int blk;
-    uint32_t off;  // K3: byte offset of the item in the ring
-    uint32_t hoff; // K3: offset of the h rows from `off`
+    int slot;       // < 0: end of the work
+    int rb;         // row block
+    int ki;         // item (K range) within the row block
+    uint32_t off;   // K3: byte offset of the item in the ring
+    uint32_t hoff;  // K3: offset of the slot's h rows from `off` (0: none)
+};
+
+// One TMEM accumulator's description, written by the MMA warp, read by the epilogue.
+struct AccMeta {
+    int slot;   // < 0: end of the work
+    int rb;
+    int gi;     // int8: the 128-group of the accumulator
+    int flags;  // bit 0: int8 (one group), bit 1: the row block's last accumulator
+    float sig[kMaxB];       // K3 int8: digit scales of the slot's entries for the group
+    float scl[kRowBlock];   // int8: weight scales of the 128 rows for the group
 };
 
 // The shared-expert slots (known from the shape alone).
@@ -96,65 +120,14 @@ UOCR_DEV void load_routed_slots(SlotTable* tb, const DecodeArgs& a, int lane) {
     __syncwarp();
 }
 
-// Diagnostics timeline: per CTA `items` records of 8 words
-// {consumer wait start, data ready, done, slot<<32|block, producer issue, 0, 0, 0} (global-timer ns).
+// Diagnostics timeline: per CTA `items` records of 8 words (global-timer ns); item n of K2 / K3:
+// {MMA warp wait start, data ready, MMAs issued, slot<<32|rb<<16|ki, producer issue, 0, 0, 0}.
 UOCR_DEV unsigned long long* trace_rec(const DecodeArgs& a, int half, int n) {
     if (!a.trace || n >= a.trace_items / 2) return nullptr;
     return a.trace + ((size_t)blockIdx.x * a.trace_items + (size_t)half * (a.trace_items / 2) + n) * 8;
 }
 
-// ---- tensor-core tile products (mma.cuh) -------------------------------------------------
-// Rows live in shared memory with a stride of `rowb` bytes; a k-step is 32 bytes of a row.
-// Lane (g, t) loads 8 bytes at 8t of rows g and g + 8 of the 16-row tile starting at `rows_s`.
-//
-// s8 weights, int8-digit activations: k-steps [s0, s1) of the tile; digits `xd_s` in fragment
-// order ([k-step][digit][lane] x 8 bytes), their scales sig[col * NG + group]; per-row weight
-// scales at sc_s + 4 * (row * NG + group) for the tile's rows row0 + g, row0 + g + 8. Adds the
-// fp32 products to acc (C layout: (g, 2t), (g, 2t + 1), (g + 8, 2t), (g + 8, 2t + 1)).
-UOCR_DEV void mma_tile_s8(uint32_t rows_s, uint32_t rowb, int row0, uint32_t sc_s, int NG, int s0, int s1,
-                          uint32_t xd_s, const float* sig, int lane, float (&acc)[4]) {
-    const int g = lane >> 2, t = lane & 3;
-    const uint32_t ra = rows_s + (uint32_t)g * rowb + 8u * t, rb = ra + 8u * rowb;
-    for (int s = s0; s < s1;) {
-        const int grp = s >> 2;
-        const int se = min(s1, (grp + 1) << 2);
-        int c[3][4] = {{0, 0, 0, 0}, {0, 0, 0, 0}, {0, 0, 0, 0}};
-        for (; s < se; ++s) {
-            const uint2 A0 = lds_u64(ra + 32u * s), A1 = lds_u64(rb + 32u * s);
-#pragma unroll
-            for (int d = 0; d < 3; ++d) {
-                const uint2 Bd = lds_u64(xd_s + 8u * ((s * 3 + d) * 32 + lane));
-                mma_s8(c[d], A0.x, A1.x, A0.y, A1.y, Bd.x, Bd.y);
-            }
-        }
-        const float slo = lds_f32(sc_s + 4u * ((row0 + g) * NG + grp));
-        const float shi = lds_f32(sc_s + 4u * ((row0 + g + 8) * NG + grp));
-        const float sg0 = sig[2 * t * NG + grp], sg1 = sig[(2 * t + 1) * NG + grp];
-        acc[0] = __fmaf_rn(undigit(c[0][0], c[1][0], c[2][0]), slo * sg0, acc[0]);
-        acc[1] = __fmaf_rn(undigit(c[0][1], c[1][1], c[2][1]), slo * sg1, acc[1]);
-        acc[2] = __fmaf_rn(undigit(c[0][2], c[1][2], c[2][2]), shi * sg0, acc[2]);
-        acc[3] = __fmaf_rn(undigit(c[0][3], c[1][3], c[2][3]), shi * sg1, acc[3]);
-    }
-}
-
-// bf16 weights, fp32 activations xf (column n = row n of xf, stride ldx floats) split into
-// three bf16 terms on the fly: k-steps [s0, s1) (16 values each).
-UOCR_DEV void mma_tile_bf16(uint32_t rows_s, uint32_t rowb, int s0, int s1, uint32_t xf_s, int ldx, int lane,
-                            float (&acc)[4]) {
-    const int g = lane >> 2, t = lane & 3;
-    const uint32_t ra = rows_s + (uint32_t)g * rowb + 8u * t, rb = ra + 8u * rowb;
-    const uint32_t xa = xf_s + 4u * ((uint32_t)g * ldx + 4 * t);
-    for (int s = s0; s < s1; ++s) {
-        const uint2 A0 = lds_u64(ra + 32u * s), A1 = lds_u64(rb + 32u * s);
-        const float4 v = lds_f128(xa + 64u * s);
-        uint32_t b0[3], b1[3];
-        bf16_terms(v.x, v.y, b0[0], b0[1], b0[2]);
-        bf16_terms(v.z, v.w, b1[0], b1[1], b1[2]);
-#pragma unroll
-        for (int q = 0; q < 3; ++q) mma_bf16(acc, A0.x, A1.x, A0.y, A1.y, b0[q], b1[q]);
-    }
-}
-
+// ---- B operands ----------------------------------------------------------------------------
 // Digits of one 128-value group of one column: lane L holds values [4L, 4L + 4) of the group.
 // Returns the group's scale (warp-uniform) and the lane's three digit words.
 UOCR_DEV float group_digits(float4 v, uint32_t (&w)[3]) {
@@ -172,33 +145,29 @@ UOCR_DEV float group_digits(float4 v, uint32_t (&w)[3]) {
     for (int q = 0; q < 3; ++q) w[q] = pack_s8x4(d[0][q], d[1][q], d[2][q], d[3][q]);
     return sg;
 }
-// Index (in 32-bit words) of digit q of values k..k+3 (k a multiple of 4) of column col in the
-// fragment-ordered digit buffer: k-step k / 32, fragment lane 4 col + (k % 32) / 8, half (k % 8) / 4.
-UOCR_DEV int digit_word(int k, int col, int q) {
-    return (((k >> 5) * 3 + q) * 32 + 4 * col + ((k & 31) >> 3)) * 2 + ((k & 7) >> 2);
-}
-
-// Activations of 8 columns (rows of xf, stride ldx; rows >= valid are zero) as int8 digits in
-// fragment order, one power-of-two scale per column and 128-group (sig[col * K/128 + g]):
-// warp w converts column w (kCW >= 8 warps).
-UOCR_DEV void stage_digits(const float* xf, int ldx, int K, int valid, uint32_t* xd, float* sig, int warp, int lane) {
-    if (warp >= kMaxB) return;
-    const int col = warp, NG = K / 128;
-    const float* row = xf + (size_t)col * ldx;
-    const bool live = col < valid;
-    for (int g = 0; g < NG; ++g) {
-        const int k = 128 * g + 4 * lane;
-        const float4 v = live ? *reinterpret_cast<const float4*>(row + k) : make_float4(0.f, 0.f, 0.f, 0.f);
-        uint32_t w[3];
-        const float sg = group_digits(v, w);
-        if (lane == 0) sig[col * NG + g] = sg;
+// int8 operand image [group][32 rows][128 B] (swizzled): digit plane p of column t is row 8p + t.
+// Lane L's words of group g, column t.
+UOCR_DEV void put_digits(unsigned char* img, int g, int t, int lane, const uint32_t (&w)[3]) {
 #pragma unroll
-        for (int q = 0; q < 3; ++q) xd[digit_word(k, col, q)] = w[q];
-    }
+    for (int p = 0; p < 3; ++p)
+        *reinterpret_cast<uint32_t*>(img + (size_t)g * kDigitAtomBytes + atom_offset(8 * p + t, 4 * lane)) = w[p];
+}
+// bf16 operand image [64-element atom][16 rows][128 B] (swizzled): term q of column t is row
+// 8q + t. Lane L's values [4L, 4L + 4) of 128-element chunk g of column t (atom 2g + L / 16).
+UOCR_DEV void put_terms(unsigned char* img, int g, int t, int lane, float4 v) {
+    const __nv_bfloat162 a0 = __floats2bfloat162_rn(v.x, v.y), a1 = __floats2bfloat162_rn(v.z, v.w);
+    const __nv_bfloat162 b0 = __floats2bfloat162_rn(v.x - __low2float(a0), v.y - __high2float(a0));
+    const __nv_bfloat162 b1 = __floats2bfloat162_rn(v.z - __low2float(a1), v.w - __high2float(a1));
+    unsigned char* atom = img + (size_t)(2 * g + (lane >> 4)) * kTermAtomBytes;
+    const int c = 8 * (lane & 15);
+    *reinterpret_cast<uint2*>(atom + atom_offset(t, c)) =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&a0), *reinterpret_cast<const uint32_t*>(&a1));
+    *reinterpret_cast<uint2*>(atom + atom_offset(8 + t, c)) =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&b0), *reinterpret_cast<const uint32_t*>(&b1));
 }
 
 // ======================================================================================
-// routing inside a CTA (the 8 consumer warps of K2)
+// routing inside a CTA (warps 0-7 of K2)
 // ======================================================================================
 // Scratch of the step's routing in shared memory.
 struct RouteSmem {
@@ -218,9 +187,8 @@ struct RouteSmem {
 // table: routed slot u is the u-th used expert; its rows start after the shared experts' S * B
 // rows, its entries in token order. CTA 0 also writes ids / wts and the global RouteTable (read
 // by K3). The inputs arrive by bulk copies on `inb`: the partials into `part` (the last stage
-// buffer, which the producer fills only after the table is ready), the digits and their scales
-// (int8 layers), and the token rows into xs (rows B..7 zero).
-UOCR_DEV void cta_route(const DecodeArgs& a, float* xs, int ldx, uint32_t* xd, float* xsig, float* part,
+// buffer, which the producer fills only after the table is ready) and K1's operand images.
+UOCR_DEV void cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* xb, float* xsig, float* part,
                         uint64_t* inb, volatile int* abort_flag, RouteSmem* rs, SlotTable* tb, int tid,
                         unsigned long long* ev) {
     const int warp = tid >> 5, lane = tid & 31;
@@ -232,20 +200,18 @@ UOCR_DEV void cta_route(const DecodeArgs& a, float* xs, int ldx, uint32_t* xd, f
         rs->mask[tid] = 0ull;
     }
     for (int i = tid; i < 64 * kMaxB; i += kCW * 32) tb->pos[a.S + i / kMaxB][i % kMaxB] = -1;
-    pdl_wait_prior_grid();  // K1's partials and digits; through K1, the previous layer's output x
+    pdl_wait_prior_grid();  // K1's partials and operands
     if (ev && tid == 0) ev[1] = global_timer_ns();
     if (warp == 0) {
-        const uint32_t pbytes = (uint32_t)B * 64 * 8 * 4;
-        const uint32_t dbytes = a.int8 ? (uint32_t)H * 24 : 0u, sbytes = a.int8 ? 8u * (H / 128) * 4 : 0u;
-        if (lane == 0) mbar_arrive_expect_tx(inb, pbytes + dbytes + sbytes + (uint32_t)B * H * 4);
+        const uint32_t pbytes = (uint32_t)B * 64 * 8 * 4, img = (uint32_t)H * 32;
+        const uint32_t dbytes = a.int8 ? img : 0u, sbytes = a.int8 ? 8u * (H / 128) * 4 : 0u;
+        if (lane == 0) mbar_arrive_expect_tx(inb, pbytes + dbytes + sbytes + img);
         __syncwarp();
         if (lane == 0) bulk_g2s(part, a.logits, pbytes, inb);
-        if (lane == 1 && dbytes) bulk_g2s(xd, a.xdig, dbytes, inb);
-        if (lane == 2 && sbytes) bulk_g2s(xsig, a.xsig, sbytes, inb);
-        if (lane >= 8 && lane < 8 + B) bulk_g2s(xs + (size_t)(lane - 8) * ldx, a.x + (size_t)(lane - 8) * H, H * 4, inb);
+        if (lane == 1) bulk_g2s(xb, a.xb, img, inb);
+        if (lane == 2 && dbytes) bulk_g2s(xd, a.xd, dbytes, inb);
+        if (lane == 3 && sbytes) bulk_g2s(xsig, a.xsig, sbytes, inb);
     }
-    for (int i = B * (H / 4) + tid; i < kMaxB * (H / 4); i += kCW * 32)
-        *reinterpret_cast<float4*>(xs + (size_t)(i / (H / 4)) * ldx + 4 * (i % (H / 4))) = make_float4(0.f, 0.f, 0.f, 0.f);
     if (!mbar_wait_warp(inb, 0, abort_flag, &a.ctl->status)) *abort_flag = 1;
     if (rv && tid == 0) rv[0] = global_timer_ns();
     for (int i = tid; i < B * 64; i += kCW * 32) {
@@ -369,21 +335,21 @@ UOCR_DEV void cta_route(const DecodeArgs& a, float* xs, int ldx, uint32_t* xd, f
     if (rv && tid == 0) rv[6] = global_timer_ns();
 }
 
-// Weighted static partition: the items of slots [first, last) in order, item cost c(slot);
-// this CTA takes the items whose cost prefix starts in [lo, hi) of the total.
+// Weighted static partition: the units of slots [first, last) in order, unit cost c(slot);
+// this CTA takes the units whose cost prefix starts in [lo, hi) of the total.
 struct Partition {
     long long lo, hi;
 };
-template <class CostFn, class ItemsFn>
-UOCR_DEV Partition cta_share(int first, int last, CostFn cost, ItemsFn items) {
+template <class CostFn, class UnitsFn>
+UOCR_DEV Partition cta_share(int first, int last, CostFn cost, UnitsFn units) {
     long long total = 0;
-    for (int s = first; s < last; ++s) total += (long long)items(s) * cost(s);
+    for (int s = first; s < last; ++s) total += (long long)units(s) * cost(s);
     Partition p;
     p.lo = total * blockIdx.x / gridDim.x;
     p.hi = total * (blockIdx.x + 1) / gridDim.x;
     return p;
 }
-// Items j of slot s (cost prefix before the slot `pre`, cost c) that start in [lo, hi).
+// Units j of slot s (cost prefix before the slot `pre`, cost c) that start in [lo, hi).
 UOCR_DEV void slot_range(long long pre, long long c, int n, const Partition& p, int& j0, int& j1) {
     long long a = p.lo - pre, b = p.hi - pre;
     long long s0 = a <= 0 ? 0 : (a + c - 1) / c;
@@ -393,15 +359,15 @@ UOCR_DEV void slot_range(long long pre, long long c, int n, const Partition& p, 
 }
 
 // ======================================================================================
-// K1: router logit partials and the activation digits
+// K1: router logit partials and the tokens as B operands
 // ======================================================================================
 // One warp per CTA. CTAs [0, 8E): expert e = c / 8, segment s = c % 8; lane t < B runs the
 // oracle's chain for token t over segment s (fma in ascending k from +0) and writes the
 // partial sum part[t][e][s]; K2 adds the 8 partials in ascending order plus the bias. The
 // router segment is fetched before the dependency wait. CTAs [8E, 8E + 8 H/128): column
-// t = d / (H/128), group g = d % (H/128): the int8 digits of x[t][128g, 128g + 128) in K2's
-// fragment order plus the group's scale (zero digits for t >= B). Small CTAs (no shared
-// memory) so several start beside the previous layer's K3 on every SM.
+// t = d / (H/128), group g = d % (H/128): x[t][128g, 128g + 128) as int8 digits (+ the group's
+// scale) and as two bf16 terms, in K2's operand images (zeros for t >= B). Small CTAs (no
+// shared memory) so several start beside the previous layer's K3 on every SM.
 constexpr int kLogitSteps = 20;  // 8-element steps per segment held in registers (H <= 1280)
 
 __global__ void __launch_bounds__(32)
@@ -469,127 +435,164 @@ decode_logits_kernel(DecodeArgs a) {
         const int k = 128 * g + 4 * lane;
         const float4 v = t < a.B ? __ldcg(reinterpret_cast<const float4*>(a.x + (size_t)t * H + k))
                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-        uint32_t w[3];
-        const float sg = group_digits(v, w);
-        if (lane == 0) a.xsig[t * NG + g] = sg;
-#pragma unroll
-        for (int q = 0; q < 3; ++q) a.xdig[digit_word(k, t, q)] = w[q];
+        put_terms(a.xb, g, t, lane, v);
+        if (a.int8) {
+            uint32_t w[3];
+            const float sg = group_digits(v, w);
+            if (lane == 0) a.xsig[t * NG + g] = sg;
+            put_digits(a.xd, g, t, lane, w);
+            *reinterpret_cast<uint32_t*>(a.xd + (size_t)g * kDigitAtomBytes + atom_offset(24 + t, 4 * lane)) = 0u;
+        }
     }
     if (ev && lane == 0) ev[2] = global_timer_ns();
 }
 
 // ======================================================================================
-// K2: route + gate/up + SwiGLU
+// the MMA warp and the epilogue warps (K2 and K3)
 // ======================================================================================
-// Items: (slot, block) with I / P blocks per slot, P = 16 row pairs for int8 stacks and 8 for
-// bf16 (one packed block, layout.h). Shared slots first (streamed while the CTA routes), then
-// routed slots. In an item all 8 consumer warps split the block's K range: int8 blocks are two
-// 16-row tiles (gate, up) x 4 K quarters, bf16 blocks one tile [8 gate | 8 up rows] x 8 K
-// eighths; the partial sums meet in shared memory and the SwiGLU is applied per (pair, token).
-UOCR_DEV int gu_pairs(const DecodeArgs& a, int slot) { return (slot >= a.S && a.int8) ? 16 : 8; }
-// relative cost of one item (its bytes dominate; tokens ride along in the tensor-core product)
-UOCR_DEV long long gu_cost(const DecodeArgs& a, const SlotTable&, int) { return 1; }
-
-// Partial tiles of items n, n-1, n-2: item n's finish runs after item n+1's products, and a
-// warp releases item n's buffer only after that finish.
-constexpr int kRedBufs = 3;
-struct GuSmem {
-    float red[kRedBufs][kCW][16][8];
+// Shared state of the tensor-core pipeline of one CTA.
+struct Pipe {
+    uint64_t* tfull;   // [kAccSlots]: description written (1 arrival) + MMAs complete (commit)
+    uint64_t* tfree;   // [kAccSlots]: the 4 epilogue warps have read the accumulator
+    AccMeta* acc;      // [kAccSlots]
+    uint32_t tmem;     // TMEM base (kTmemCols columns)
+    int c;             // accumulators handed out (MMA warp)
+    volatile int* abort_flag;
+    uint32_t* status;
 };
 
-// The warp's partial tile of one item. int8 blocks: tile warp / 4 (gate, up), K quarter
-// warp % 4 (H / 128 k-steps of 32); bf16 blocks: K eighth `warp` (H / 128 k-steps of 16).
-// The activation fragments are read from shared memory in the loop: a compact loop runs
-// faster here than one unrolled over register-held fragments (instruction fetch dominates).
-UOCR_DEV void gu_partial(const DecodeArgs& a, bool i8, uint32_t stage_s, uint32_t xf_s, int ldx, uint32_t xd_s,
-                         const float* xsig, int lane, int warp, float (&acc)[4]) {
-    acc[0] = acc[1] = acc[2] = acc[3] = 0.0f;
-    const int n = a.H / 128;  // k-steps per warp, both kinds
-    if (i8) {
-        const uint32_t rowb = (uint32_t)packed_row_bytes(a.H, true);
-        const int tile = warp >> 2, s0 = (warp & 3) * n;
-        const uint32_t rows = stage_s + (uint32_t)tile * 16 * rowb, sc = stage_s + 32 * rowb;
-        mma_tile_s8(rows, rowb, tile * 16, sc, n, s0, s0 + n, xd_s, xsig, lane, acc);
-    } else {
-        const uint32_t rowb = (uint32_t)packed_row_bytes(a.H, false);
-        mma_tile_bf16(stage_s, rowb, warp * n, warp * n + n, xf_s, ldx, lane, acc);
+// MMA warp: take the next accumulator slot (waiting until the epilogue has read it), publish
+// its description; returns its index, or -1 on a timeout. `scl` (int8) = the 128 row scales,
+// `sig` (K3 int8) = the group's 8 column scales.
+UOCR_DEV int acquire_acc(Pipe& p, int slot, int rb, int gi, int flags, const float* scl, const float* sig, int lane) {
+    const int j = p.c % kAccSlots;
+    if (p.c >= kAccSlots && !mbar_wait_warp(&p.tfree[j], ((p.c / kAccSlots) - 1) & 1, p.abort_flag, p.status))
+        return -1;
+    AccMeta& m = p.acc[j];
+    if (lane == 0) {
+        m.slot = slot;
+        m.rb = rb;
+        m.gi = gi;
+        m.flags = flags;
     }
+    if (scl)
+        for (int i = lane; i < kRowBlock; i += 32) m.scl[i] = scl[i];
+    if (sig && lane < kMaxB) m.sig[lane] = sig[lane];
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&p.tfull[j]);  // the description (release); the MMAs' commit is the second arrival
+    tc_fence_after();                          // the epilogue's TMEM reads precede this warp's next MMAs
+    ++p.c;
+    return j;
 }
 
-UOCR_DEV void store_partial(float (&red)[kCW][16][8], int warp, int lane, const float (&acc)[4]) {
-    const int g = lane >> 2, t = lane & 3;
-    *reinterpret_cast<float2*>(&red[warp][g][2 * t]) = make_float2(acc[0], acc[1]);
-    *reinterpret_cast<float2*>(&red[warp][g + 8][2 * t]) = make_float2(acc[2], acc[3]);
+// Epilogue warp (TMEM lane quarter q = warp % 4, row = 32 q + lane): waits for accumulator c,
+// reads it and its description; returns false at the end of the work or on a timeout.
+struct AccRead {
+    int slot, rb, gi, flags;
+    float scl, sig[kMaxB];
+    uint32_t v[32];
+};
+UOCR_DEV bool read_acc(Pipe& p, int c, int q, int lane, bool want_sig, AccRead& r) {
+    const int j = c % kAccSlots;
+    if (!mbar_wait_warp(&p.tfull[j], (c / kAccSlots) & 1, p.abort_flag, p.status)) return false;
+    const AccMeta& m = p.acc[j];
+    r.slot = m.slot;
+    if (r.slot < 0) return false;
+    r.rb = m.rb;
+    r.gi = m.gi;
+    r.flags = m.flags;
+    r.scl = (r.flags & 1) ? m.scl[32 * q + lane] : 0.0f;
+    if (want_sig) {
+#pragma unroll
+        for (int t = 0; t < kMaxB; ++t) r.sig[t] = m.sig[t];
+    }
+    tc_fence_after();
+    tmem_ld_32x32b_x32(p.tmem + ((uint32_t)(32 * q) << 16) + 32u * j, r.v);
+    tmem_wait_ld();
+    tc_fence_before();
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&p.tfree[j]);
+    return true;
 }
 
-// h[slot row][blk * P + p] = silu(g) * u for the slot's tokens, from the partial tiles.
-UOCR_DEV void gu_finish(const DecodeArgs& a, const SlotTable& tb, bool i8, int slot, int blk,
-                        const float (&red)[kCW][16][8], int tid) {
-    const int p = tid >> 3, n = tid & 7;
-    float g = 0.0f, u = 0.0f;
-    int P;
-    if (i8) {
-        P = 16;
-        if (p >= 16) return;
+// int8 accumulator -> acc[t] += undigit(planes) * (row scale * column scale), fixed order
+UOCR_DEV void fold_s8(const AccRead& r, const float* colsig, float (&acc)[kMaxB]) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q) {
-            g += red[q][p][n];
-            u += red[4 + q][p][n];
-        }
-    } else {
-        P = 8;
-        if (p >= 8) return;
+    for (int t = 0; t < kMaxB; ++t)
+        acc[t] = __fmaf_rn(undigit((int)r.v[t], (int)r.v[8 + t], (int)r.v[16 + t]), __fmul_rn(r.scl, colsig[t]),
+                           acc[t]);
+}
+// bf16 accumulator (the whole row block): acc[t] = term-0 column + term-1 column
+UOCR_DEV void fold_bf16(const AccRead& r, float (&acc)[kMaxB]) {
 #pragma unroll
-        for (int w = 0; w < kCW; ++w) {
-            g += red[w][p][n];
-            u += red[w][8 + p][n];
-        }
-    }
-    const int pos = tb.pos[slot][n];
-    if (pos >= 0) a.h[(size_t)(tb.base[slot] + pos) * a.I + blk * P + p] = silu(g) * u;
+    for (int t = 0; t < kMaxB; ++t) acc[t] = __fadd_rn(__uint_as_float(r.v[t]), __uint_as_float(r.v[8 + t]));
+}
+
+// ======================================================================================
+// K2: route + gate/up + SwiGLU
+// ======================================================================================
+// Units (slot, row block): w13_items(H) items of 2 atoms each. Shared slots first (streamed
+// while the CTA routes), then the routed slots.
+UOCR_DEV long long gu_unit_cost(const DecodeArgs& a, int slot) {
+    const bool i8 = slot >= a.S && a.int8;
+    return (long long)w13_items(a.H, i8) * (long long)w13_item_bytes(i8);
 }
 
 __global__ void __launch_bounds__(kThreads, 1)
 decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl, uint32_t off_route,
-                      uint32_t off_meta, uint32_t off_gu, uint32_t off_xf, uint32_t off_xd, uint32_t off_sig,
+                      uint32_t off_meta, uint32_t off_acc, uint32_t off_xd, uint32_t off_xb, uint32_t off_sig,
                       uint32_t off_stages) {
-    extern __shared__ __align__(16) unsigned char smem[];
+    extern __shared__ __align__(1024) unsigned char smem[];
     __shared__ int abort_flag;
+    __shared__ uint32_t tmem_base;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + nst;
+    uint64_t* empty = full + nst;         // the MMAs reading the stage are complete
     uint64_t* table_ready = empty + nst;
-    uint64_t* redbar = table_ready + 1;  // [kRedBufs]: all warps' partial tiles of an item are stored
-    uint64_t* inb = redbar + kRedBufs;   // the routing's inputs have arrived
+    uint64_t* inb = table_ready + 1;      // the routing's inputs have arrived
+    uint64_t* tfull = inb + 1;            // [kAccSlots]
+    uint64_t* tfree = tfull + kAccSlots;  // [kAccSlots]
+    uint64_t* mdone = tfree + kAccSlots;  // the MMA warp's drain
     SlotTable* tb = reinterpret_cast<SlotTable*>(smem + off_tbl);
     RouteSmem* rs = reinterpret_cast<RouteSmem*>(smem + off_route);
     ItemMeta* meta = reinterpret_cast<ItemMeta*>(smem + off_meta);
-    GuSmem* gs = reinterpret_cast<GuSmem*>(smem + off_gu);
-    float* xf = reinterpret_cast<float*>(smem + off_xf);
-    uint32_t* xd = reinterpret_cast<uint32_t*>(smem + off_xd);
+    AccMeta* accm = reinterpret_cast<AccMeta*>(smem + off_acc);
+    unsigned char* xd = smem + off_xd;
+    unsigned char* xb = smem + off_xb;
     float* xsig = reinterpret_cast<float*>(smem + off_sig);
     unsigned char* stages = smem + off_stages;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int ldx = a.H + 4;
-    // diagnostics: kernel-level events of this CTA (start, consumers past the dependency wait,
-    // routed, fragments loaded, consumers done)
+    // diagnostics: kernel-level events of this CTA (start, past the dependency wait, routed,
+    // MMA warp done, epilogue done)
     unsigned long long* ev = a.trace ? trace_rec(a, 0, a.trace_items / 2 - 1) : nullptr;
     if (ev && tid == 0) ev[0] = global_timer_ns();
+    if (smem_addr(smem) & 1023u) {  // the swizzled operands need 1024-byte alignment (same in every CTA)
+        if (tid == 0) set_status(&a.ctl->status, kStatusMisaligned);
+        return;
+    }
     if (tid == 0) {
         for (int s = 0; s < nst; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], kCW);
+            mbar_init(&empty[s], 1);
         }
         mbar_init(table_ready, 1);
-        for (int b = 0; b < kRedBufs; ++b) mbar_init(&redbar[b], kCW);
         mbar_init(inb, 1);
+        for (int j = 0; j < kAccSlots; ++j) {
+            mbar_init(&tfull[j], 2);
+            mbar_init(&tfree[j], 4);
+        }
+        mbar_init(mdone, 1);
         abort_flag = 0;
         fence_mbar_init();
         pdl_launch_dependents();  // K3 launches early; it waits for this grid before it reads h
     }
+    if (warp == 0) tmem_alloc(&tmem_base, kTmemCols);
     load_shared_slots(tb, a, tid, blockDim.x);
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
+    Pipe pipe{tfull, tfree, accm, tmem_base, 0, &abort_flag, &a.ctl->status};
 
-    if (warp == kCW) {
+    if (warp == 8) {
         // ---------------- producer: one bulk copy per item ----------------
         int n = 0, st = 0;
         uint32_t round = 0;
@@ -600,7 +603,7 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                 routed = true;
             }
         };
-        auto issue = [&](int slot, int blk) {
+        auto issue = [&](int slot, int rb, int ki) {
             // the last stage holds the routing's logit partials until the table is ready
             if (round == 0 && st == nst - 1) wait_table();
             if (ok && round > 0 && !mbar_wait_warp(&empty[st], (round - 1) & 1, &abort_flag, &a.ctl->status))
@@ -608,15 +611,16 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             if (!ok) return;
             if (lane == 0) {
                 const bool i8 = slot >= a.S && a.int8;
-                const uint32_t bytes = (uint32_t)w13_block_bytes(a.H, a.G, i8);
+                const uint32_t bytes = (uint32_t)w13_item_bytes(i8);
                 const unsigned char* src =
                     slot < a.S ? reinterpret_cast<const unsigned char*>(a.w13_shared) +
-                                     (size_t)tb->expert[slot] * w13_expert_bytes(a.I, a.H, a.G, false)
+                                     (size_t)tb->expert[slot] * w13_expert_bytes(a.I, a.H, false)
                                : reinterpret_cast<const unsigned char*>(a.w13) +
-                                     (size_t)tb->expert[slot] * w13_expert_bytes(a.I, a.H, a.G, i8);
-                src += (size_t)blk * bytes;
+                                     (size_t)tb->expert[slot] * w13_expert_bytes(a.I, a.H, i8);
+                src += ((size_t)rb * w13_items(a.H, i8) + ki) * bytes;
                 meta[st].slot = slot;
-                meta[st].blk = blk;
+                meta[st].rb = rb;
+                meta[st].ki = ki;
                 mbar_arrive_expect_tx(&full[st], bytes);
                 bulk_g2s(stages + (size_t)st * stage_bytes, src, bytes, &full[st]);
                 unsigned long long* tr = trace_rec(a, 0, n);
@@ -631,16 +635,18 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             if (!ok) break;
             const int first = phase == 0 ? 0 : a.S;
             const int last = phase == 0 ? a.S : tb->nslot;
-            auto items = [&](int s) { return a.I / gu_pairs(a, s); };
-            auto cost = [&](int s) { return gu_cost(a, *tb, s); };
-            const Partition p = cta_share(first, last, cost, items);
+            auto units = [&](int) { return a.I / 64; };
+            auto cost = [&](int s) { return gu_unit_cost(a, s); };
+            const Partition p = cta_share(first, last, cost, units);
             long long pre = 0;
             for (int s = first; s < last && ok; ++s) {
                 const long long c = cost(s);
                 int j0, j1;
-                slot_range(pre, c, items(s), p, j0, j1);
-                for (int j = j0; j < j1 && ok; ++j) issue(s, j);
-                pre += (long long)items(s) * c;
+                slot_range(pre, c, units(s), p, j0, j1);
+                const int nk = w13_items(a.H, s >= a.S && a.int8);
+                for (int rb = j0; rb < j1 && ok; ++rb)
+                    for (int ki = 0; ki < nk && ok; ++ki) issue(s, rb, ki);
+                pre += (long long)units(s) * c;
             }
         }
         if (lane == 0) {
@@ -656,92 +662,135 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
         }
         __syncwarp();
     } else {
-        // ---------------- consumers: route, stage the digits, then the items ----------------
-        cta_route(a, xf, ldx, xd, xsig, reinterpret_cast<float*>(stages + (size_t)(nst - 1) * stage_bytes), inb,
+        // ---------------- warps 0-7: route; then MMA (warp 0) and epilogue (warps 4-7) ----------------
+        cta_route(a, xd, xb, xsig, reinterpret_cast<float*>(stages + (size_t)(nst - 1) * stage_bytes), inb,
                   &abort_flag, rs, tb, tid, ev);
         if (tid == 0) mbar_arrive(table_ready);
-        if (ev && tid == 0) ev[2] = ev[5] = global_timer_ns();
-        const uint32_t xf_s = smem_addr(xf), xd_s = smem_addr(xd);
-        // this warp's activation fragments, fixed for the CTA
-        if (ev && tid == 0) ev[3] = global_timer_ns();
-        // Item n: products, stage release, partial tile stored; then item n-1 is finished (its
-        // partial tiles are complete once every warp has arrived) and item n's buffer released.
-        int pend_slot = -1, pend_blk = 0, pend_n = 0;
-        bool pend_i8 = false, ok = true;
-        auto finish_pending = [&]() {
-            const int b = pend_n % kRedBufs;
-            ok = mbar_wait_warp(&redbar[b], (pend_n / kRedBufs) & 1, &abort_flag, &a.ctl->status);
-            if (ok) gu_finish(a, *tb, pend_i8, pend_slot, pend_blk, gs->red[b], tid);
-        };
-        for (int n = 0;; ++n) {
-            const int st = n % nst;
-            unsigned long long* tr = warp == 0 ? trace_rec(a, 0, n) : nullptr;
-            if (tr && lane == 0) tr[0] = global_timer_ns();
-            if (!mbar_wait_warp(&full[st], (n / nst) & 1, &abort_flag, &a.ctl->status)) {
-                ok = false;
-                break;
+        if (ev && tid == 0) ev[2] = global_timer_ns();
+        if (warp == 0) {
+            const uint32_t xd_s = smem_addr(xd), xb_s = smem_addr(xb);
+            const int nk8 = w13_items(a.H, true), nk16 = w13_items(a.H, false);
+            bool ok = true;
+            int cur = 0;
+            for (int n = 0;; ++n) {
+                const int st = n % nst;
+                unsigned long long* tr = trace_rec(a, 0, n);
+                if (tr && lane == 0) tr[0] = global_timer_ns();
+                if (!mbar_wait_warp(&full[st], (n / nst) & 1, &abort_flag, &a.ctl->status)) {
+                    ok = false;
+                    break;
+                }
+                const int slot = meta[st].slot;
+                if (slot < 0) break;
+                if (tr && lane == 0) tr[1] = global_timer_ns();
+                const int rb = meta[st].rb, ki = meta[st].ki;
+                const bool i8 = slot >= a.S && a.int8;
+                unsigned char* item = stages + (size_t)st * stage_bytes;
+                const uint32_t item_s = smem_addr(item);
+                if (i8) {
+                    const float* scl = reinterpret_cast<const float*>(item + 2 * kAtomBytes);
+                    for (int g = 0; g < 2 && ok; ++g) {
+                        const int gi = ki * 2 + g;
+                        const int j = acquire_acc(pipe, slot, rb, gi, 1 | (ki == nk8 - 1 && g == 1 ? 2 : 0),
+                                                  scl + g * kRowBlock, nullptr, lane);
+                        if (j < 0) {
+                            ok = false;
+                            break;
+                        }
+                        if (lane == 0) {
+#pragma unroll
+                            for (int s = 0; s < 4; ++s)
+                                umma_i8(pipe.tmem + 32u * j, umma_desc_sw128(item_s + g * kAtomBytes + 32 * s),
+                                        umma_desc_sw128(xd_s + gi * kDigitAtomBytes + 32 * s), kIdescS8, s > 0);
+                            umma_commit(&tfull[j]);
+                        }
+                        __syncwarp();
+                    }
+                    if (!ok) break;
+                } else {
+                    if (ki == 0) {
+                        cur = acquire_acc(pipe, slot, rb, 0, 2, nullptr, nullptr, lane);
+                        if (cur < 0) {
+                            ok = false;
+                            break;
+                        }
+                    }
+                    if (lane == 0) {
+#pragma unroll
+                        for (int at = 0; at < 2; ++at)
+#pragma unroll
+                            for (int s = 0; s < 4; ++s)
+                                umma_f16(pipe.tmem + 32u * cur, umma_desc_sw128(item_s + at * kAtomBytes + 32 * s),
+                                         umma_desc_sw128(xb_s + (2 * ki + at) * kTermAtomBytes + 32 * s), kIdescBf16,
+                                         (ki | at | s) != 0);
+                        if (ki == nk16 - 1) umma_commit(&tfull[cur]);
+                    }
+                    __syncwarp();
+                }
+                if (lane == 0) umma_commit(&empty[st]);  // the stage is free once these MMAs complete
+                if (tr && lane == 0) {
+                    tr[2] = global_timer_ns();
+                    tr[3] = ((unsigned long long)slot << 32) | ((unsigned)rb << 16) | (unsigned)ki;
+                }
+                __syncwarp();
             }
-            const int slot = meta[st].slot, blk = meta[st].blk;
-            if (slot < 0) break;
-            if (tr && lane == 0) tr[1] = global_timer_ns();
-            const bool i8 = slot >= a.S && a.int8;
-            const uint32_t stage_s = launder(smem_addr(stages + (size_t)st * stage_bytes));
-            float acc[4];
-            gu_partial(a, i8, stage_s, xf_s, ldx, xd_s, xsig, lane, warp, acc);
-            fence_regs(acc);
+            if (ok) {
+                const int j = acquire_acc(pipe, -1, 0, 0, 0, nullptr, nullptr, lane);  // end marker
+                if (j >= 0 && lane == 0) mbar_arrive(&tfull[j]);
+            } else if (lane == 0) {
+                abort_flag = 1;
+            }
+            if (lane == 0) {  // every MMA complete before TMEM is released
+                umma_commit(mdone);
+                mbar_wait(mdone, 0, &a.ctl->status);
+            }
             __syncwarp();
-            if (tr && lane == 0) tr[5] = global_timer_ns();
-            if (lane == 0) mbar_arrive(&empty[st]);  // the stage is free once the warp's products are done
-            store_partial(gs->red[n % kRedBufs], warp, lane, acc);
-            if (pend_slot >= 0) {
-                finish_pending();
-                if (!ok) break;
+            if (ev && lane == 0) ev[3] = global_timer_ns();
+        } else if (warp >= 4) {
+            const int q = warp & 3, row = 32 * q + lane;
+            float acc[kMaxB];
+#pragma unroll
+            for (int t = 0; t < kMaxB; ++t) acc[t] = 0.0f;
+            for (int c = 0;; ++c) {
+                AccRead r;
+                if (!read_acc(pipe, c, q, lane, false, r)) break;
+                if (r.flags & 1) {
+                    float colsig[kMaxB];
+#pragma unroll
+                    for (int t = 0; t < kMaxB; ++t) colsig[t] = xsig[t * (a.H / 128) + r.gi];
+                    fold_s8(r, colsig, acc);
+                } else {
+                    fold_bf16(r, acc);
+                }
+                if (r.flags & 2) {
+                    // SwiGLU: gate row (lane % 16 < 8) with the up row 8 lanes up; h for the slot's tokens
+                    const bool gate = (lane & 15) < 8;
+                    const int pair = 64 * r.rb + 8 * (row >> 4) + (row & 7);
+                    const int base = tb->base[r.slot];
+#pragma unroll
+                    for (int t = 0; t < kMaxB; ++t) {
+                        const float u = __shfl_xor_sync(0xffffffffu, acc[t], 8);
+                        const int pos = tb->pos[r.slot][t];
+                        if (gate && pos >= 0) a.h[(size_t)(base + pos) * a.I + pair] = silu(acc[t]) * u;
+                        acc[t] = 0.0f;
+                    }
+                }
             }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&redbar[n % kRedBufs]);
-            if (tr && lane == 0) {
-                tr[6] = global_timer_ns();
-                tr[2] = global_timer_ns();
-                tr[3] = ((unsigned long long)slot << 32) | (unsigned)blk;
-            }
-            pend_slot = slot;
-            pend_blk = blk;
-            pend_i8 = i8;
-            pend_n = n;
+            if (ev && tid == 128) ev[4] = global_timer_ns();
         }
-        if (ok && pend_slot >= 0) finish_pending();
-        if (ev && tid == 0) ev[4] = global_timer_ns();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
     }
 }
 
 // ======================================================================================
-// K3: down + combine
+// K3: down projection + combine
 // ======================================================================================
-// Items: (slot, 32-row block) with H / 32 blocks per slot, each one bulk copy of its weight
-// block; the first item of each run of a slot in this CTA also carries the slot's h rows. At a
-// run's start the consumers stage those rows (fp32, padded) and, for int8 weights, their digits.
-// All 8 warps split each item: two 16-row tiles x 4 K quarters.
-UOCR_DEV long long dn_cost(const DecodeArgs& a, const SlotTable&, int slot) {
-    return (slot >= a.S && a.int8) ? 1 : 2;  // bf16 blocks are twice the bytes
-}
-
-struct DnSmem {
-    float red[kRedBufs][kCW][16][8];
-};
-
-// y[slot row][blk * 32 + row] for the slot's tokens, from the partial tiles.
-UOCR_DEV void dn_finish(const DecodeArgs& a, const SlotTable& tb, int slot, int blk, const float (&red)[kCW][16][8],
-                        int tid) {
-    const int row = tid >> 3, n = tid & 7;
-    if (n >= tb.count[slot]) return;
-    const int tile = row >> 4, r16 = row & 15;
-    float y = 0.0f;
-#pragma unroll
-    for (int q = 0; q < 4; ++q) y += red[tile * 4 + q][r16][n];
-    a.y[(size_t)(tb.base[slot] + n) * a.H + blk * kW2Rows + row] = y;
-}
-
-// This CTA's share of the outputs, after every CTA's items (grid barrier): out[t][j] for the
+// This CTA's share of the outputs, after every CTA's units (grid barrier): out[t][j] for the
 // flat indices [lo, hi) of the B x H output, one per thread: token t's shared rows in order,
 // then its routed rows in ascending expert id (w * y), from the slot table's row lists.
 UOCR_DEV void combine_slice(const DecodeArgs& a, const int (&trow)[kMaxB][kDecodeMaxTopk],
@@ -769,132 +818,184 @@ UOCR_DEV void combine_slice(const DecodeArgs& a, const int (&trow)[kMaxB][kDecod
     }
 }
 
+// Units (slot, row block of 128 output rows): w2_items(I) items.
+UOCR_DEV long long dn_unit_cost(const DecodeArgs& a, int slot) {
+    const bool i8 = slot >= a.S && a.int8;
+    return (long long)w2_items(a.I, i8) * (long long)w2_item_bytes(i8);
+}
+
+// A slot run's operand image (int8 [I/128 groups][32 rows][128 B] or bf16 [I/64 atoms][16 rows]
+// [128 B], both I * 32 bytes) is double-buffered: run r uses buffer r % 2.
 __global__ void __launch_bounds__(kThreads, 1)
-decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t off_meta, uint32_t off_dn,
-                   uint32_t off_hf, uint32_t off_hd, uint32_t off_sig, uint32_t off_ring) {
-    extern __shared__ __align__(16) unsigned char smem[];
-    __shared__ int abort_flag, bar_ok;
+decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t off_meta, uint32_t off_acc,
+                   uint32_t off_hb, uint32_t off_hsig, uint32_t off_ring) {
+    extern __shared__ __align__(1024) unsigned char smem[];
+    __shared__ int abort_flag, bar_ok, hdesc[2];
+    __shared__ uint32_t tmem_base;
     __shared__ int trow[kMaxB][kDecodeMaxTopk];
     __shared__ float tw[kMaxB][kDecodeMaxTopk];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* freed = full + kK3Desc;    // consumers: the item's ring bytes are no longer read
-    uint64_t* empty = freed + kK3Desc;   // consumers: the item is finished, its descriptor free
-    uint64_t* redbar = empty + kK3Desc;     // [kRedBufs]
-    uint64_t* hbar = redbar + kRedBufs;     // [2]: the run's h staged by all warps
+    uint64_t* freed = full + kK3Desc;      // the MMAs reading the item's ring bytes are complete
+    uint64_t* empty = freed + kK3Desc;     // the MMA warp is done with the descriptor
+    uint64_t* tfull = empty + kK3Desc;     // [kAccSlots]
+    uint64_t* tfree = tfull + kAccSlots;   // [kAccSlots]
+    uint64_t* hload = tfree + kAccSlots;   // [2]: a run's first item is issued (producer)
+    uint64_t* hready = hload + 2;          // [2]: the run's operand image is staged (3 stager warps)
+    uint64_t* bfree = hready + 2;          // [2]: the MMAs reading the image are complete
+    uint64_t* mdone = bfree + 2;
     SlotTable* tb = reinterpret_cast<SlotTable*>(smem + off_tbl);
     ItemMeta* meta = reinterpret_cast<ItemMeta*>(smem + off_meta);
-    DnSmem* ds = reinterpret_cast<DnSmem*>(smem + off_dn);
-    float* hf = reinterpret_cast<float*>(smem + off_hf);
-    uint32_t* hd = reinterpret_cast<uint32_t*>(smem + off_hd);
-    float* hsig = reinterpret_cast<float*>(smem + off_sig);
+    AccMeta* accm = reinterpret_cast<AccMeta*>(smem + off_acc);
+    unsigned char* hb = smem + off_hb;
+    float* hsig = reinterpret_cast<float*>(smem + off_hsig);  // [2][8][I / 128]
     unsigned char* ring = smem + off_ring;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int nblk = a.H / kW2Rows, ldh = a.I + 4;
+    const int NG3 = a.I / 128;
+    const uint32_t img_bytes = (uint32_t)a.I * 32;
     unsigned long long* ev = a.trace ? trace_rec(a, 1, a.trace_items / 2 - 1) : nullptr;
     if (ev && tid == 0) ev[0] = global_timer_ns();
+    if (smem_addr(smem) & 1023u) {  // as in K2: every CTA returns, so none waits at the grid barrier
+        if (tid == 0) set_status(&a.ctl->status, kStatusMisaligned);
+        return;
+    }
     if (tid == 0) {
         for (int s = 0; s < kK3Desc; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&freed[s], kCW);
-            mbar_init(&empty[s], kCW);
+            mbar_init(&freed[s], 1);
+            mbar_init(&empty[s], 1);
         }
-        for (int s = 0; s < kRedBufs; ++s) mbar_init(&redbar[s], kCW);
-        for (int s = 0; s < 2; ++s) mbar_init(&hbar[s], kCW);
+        for (int j = 0; j < kAccSlots; ++j) {
+            mbar_init(&tfull[j], 2);
+            mbar_init(&tfree[j], 4);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&hload[b], 1);
+            mbar_init(&hready[b], 3);
+            mbar_init(&bfree[b], 1);
+        }
+        mbar_init(mdone, 1);
         abort_flag = 0;
         fence_mbar_init();
         pdl_launch_dependents();  // the next layer's kernel waits for this grid itself
     }
+    if (warp == 0) tmem_alloc(&tmem_base, kTmemCols);
     load_shared_slots(tb, a, tid, blockDim.x);
+    tc_fence_before();
     __syncthreads();
+    tc_fence_after();
+    Pipe pipe{tfull, tfree, accm, tmem_base, 0, &abort_flag, &a.ctl->status};
 
-    if (warp == kCW) {
+    if (warp == 8) {
         // ---------------- producer ----------------
-        // Items are placed back to back in the ring (wrapping to 0 when one does not fit). Ring
-        // bytes retire in order as the consumers finish their products (`freed`); descriptors
-        // retire in order as the consumers finish the items (`empty`). An item may be placed
-        // once its descriptor is free and no item still being read overlaps its bytes.
+        // Items are placed back to back in the ring at 1024-byte boundaries (wrapping to 0 when
+        // one does not fit); the first item of a slot's run carries the slot's h rows. Ring
+        // bytes retire in order as the MMAs reading them complete (`freed`); descriptors retire
+        // as the MMA warp finishes with them (`empty`). Run r + 2 starts only after run r's
+        // operand image is staged (its buffer and hdesc slot are reused).
         uint32_t lo_b[kK3Desc], hi_b[kK3Desc];  // byte range of descriptor d's item
-        int n = 0, oldest = 0, oldest_desc = 0;
+        int n = 0, oldest = 0, oldest_desc = 0, runs = 0;
         uint32_t head = 0;
         bool ok = true;
         pdl_wait_prior_grid();  // h and the routing table come from K2
         if (ev && lane == 0) ev[1] = global_timer_ns();
         load_routed_slots(tb, a, lane);
-        auto items = [&](int) { return nblk; };
-        auto cost = [&](int s) { return dn_cost(a, *tb, s); };
-        const Partition p = cta_share(0, tb->nslot, cost, items);
+        auto units = [&](int) { return a.H / kRowBlock; };
+        auto cost = [&](int s) { return dn_unit_cost(a, s); };
+        const Partition p = cta_share(0, tb->nslot, cost, units);
         long long pre = 0;
         for (int slot = 0; slot < tb->nslot && ok; ++slot) {
             const long long c = cost(slot);
             int j0, j1;
-            slot_range(pre, c, nblk, p, j0, j1);
-            pre += (long long)nblk * c;
+            slot_range(pre, c, units(slot), p, j0, j1);
+            pre += (long long)units(slot) * c;
             const bool i8 = slot >= a.S && a.int8;
-            const uint32_t wbytes = (uint32_t)w2_block_bytes(a.I, a.G, i8);
+            const int nk = w2_items(a.I, i8);
+            const uint32_t wbytes = (uint32_t)w2_item_bytes(i8);
             const uint32_t hoff = (wbytes + 15u) & ~15u;
-            for (int blk = j0; blk < j1 && ok; ++blk) {
-                const uint32_t hbytes = blk == j0 ? (uint32_t)tb->count[slot] * a.I * 4 : 0u;  // run start
-                const uint32_t need = hoff + hbytes;
-                if (head + need > ring_bytes) head = 0;
-                // retire ring bytes until this item's do not overlap any still being read
-                while (oldest < n) {
-                    bool clash = false;
-                    for (int m = oldest; m < n && !clash; ++m) {
-                        const int d = m % kK3Desc;
-                        clash = head < hi_b[d] && lo_b[d] < head + need;
-                    }
-                    if (!clash) break;
-                    if (!mbar_wait_warp(&freed[oldest % kK3Desc], (oldest / kK3Desc) & 1, &abort_flag,
-                                        &a.ctl->status)) {
+            for (int rb = j0; rb < j1 && ok; ++rb) {
+                for (int ki = 0; ki < nk && ok; ++ki) {
+                    const bool run_start = rb == j0 && ki == 0;
+                    const uint32_t hbytes = run_start ? (uint32_t)tb->count[slot] * a.I * 4 : 0u;
+                    const uint32_t need = hoff + hbytes;
+                    if (run_start && runs >= 2 &&
+                        !mbar_wait_warp(&hready[runs & 1], ((runs - 2) >> 1) & 1, &abort_flag, &a.ctl->status)) {
                         ok = false;
                         break;
                     }
-                    ++oldest;
+                    head = (head + 1023u) & ~1023u;
+                    if (head + need > ring_bytes) head = 0;
+                    // retire ring bytes until this item's do not overlap any still being read
+                    while (oldest < n) {
+                        bool clash = false;
+                        for (int m = oldest; m < n && !clash; ++m) {
+                            const int d = m % kK3Desc;
+                            clash = head < hi_b[d] && lo_b[d] < head + need;
+                        }
+                        if (!clash) break;
+                        if (!mbar_wait_warp(&freed[oldest % kK3Desc], (oldest / kK3Desc) & 1, &abort_flag,
+                                            &a.ctl->status)) {
+                            ok = false;
+                            break;
+                        }
+                        ++oldest;
+                    }
+                    // and the descriptor: item n reuses item n - kK3Desc's
+                    while (ok && n - oldest_desc >= kK3Desc) {
+                        if (!mbar_wait_warp(&empty[oldest_desc % kK3Desc], (oldest_desc / kK3Desc) & 1, &abort_flag,
+                                            &a.ctl->status))
+                            ok = false;
+                        ++oldest_desc;
+                    }
+                    // a retired descriptor's bytes were freed before it: never wait on that `freed`
+                    // phase again (its barrier may complete again for a later item)
+                    oldest = max(oldest, oldest_desc);
+                    if (!ok) break;
+                    const int d = n % kK3Desc;
+                    lo_b[d] = head;
+                    hi_b[d] = head + need;
+                    if (lane == 0) {
+                        const unsigned char* wsrc =
+                            slot < a.S ? reinterpret_cast<const unsigned char*>(a.w2_shared) +
+                                             (size_t)tb->expert[slot] * w2_expert_bytes(a.H, a.I, false)
+                                       : reinterpret_cast<const unsigned char*>(a.w2) +
+                                             (size_t)tb->expert[slot] * w2_expert_bytes(a.H, a.I, i8);
+                        wsrc += ((size_t)rb * nk + ki) * wbytes;
+                        meta[d].slot = slot;
+                        meta[d].rb = rb;
+                        meta[d].ki = ki;
+                        meta[d].off = head;
+                        meta[d].hoff = hbytes ? hoff : 0u;
+                        mbar_arrive_expect_tx(&full[d], wbytes + hbytes);
+                        bulk_g2s(ring + head, wsrc, wbytes, &full[d]);
+                        if (hbytes) {
+                            bulk_g2s(ring + head + hoff, a.h + (size_t)tb->base[slot] * a.I, hbytes, &full[d]);
+                            hdesc[runs & 1] = n;
+                            mbar_arrive(&hload[runs & 1]);
+                        }
+                        unsigned long long* tr = trace_rec(a, 1, n);
+                        if (tr) tr[4] = global_timer_ns();
+                    }
+                    __syncwarp();
+                    if (hbytes) ++runs;
+                    head += need;
+                    ++n;
                 }
-                // and the descriptor: item n reuses item n - kK3Desc's
-                while (ok && n - oldest_desc >= kK3Desc) {
-                    if (!mbar_wait_warp(&empty[oldest_desc % kK3Desc], (oldest_desc / kK3Desc) & 1, &abort_flag,
-                                        &a.ctl->status))
-                        ok = false;
-                    ++oldest_desc;
-                }
-                // a retired descriptor's bytes were freed before it: never wait on that `freed`
-                // phase again (its barrier may complete again for a later item)
-                oldest = max(oldest, oldest_desc);
-                if (!ok) break;
-                const int d = n % kK3Desc;
-                lo_b[d] = head;
-                hi_b[d] = head + need;
-                if (lane == 0) {
-                    const unsigned char* wsrc =
-                        slot < a.S ? reinterpret_cast<const unsigned char*>(a.w2_shared) +
-                                         (size_t)tb->expert[slot] * w2_expert_bytes(a.H, a.I, a.G, false)
-                                   : reinterpret_cast<const unsigned char*>(a.w2) +
-                                         (size_t)tb->expert[slot] * w2_expert_bytes(a.H, a.I, a.G, i8);
-                    wsrc += (size_t)blk * wbytes;
-                    meta[d].slot = slot;
-                    meta[d].blk = blk;
-                    meta[d].off = head;
-                    meta[d].hoff = hbytes ? hoff : 0u;  // 0: no h with this item
-                    mbar_arrive_expect_tx(&full[d], wbytes + hbytes);
-                    bulk_g2s(ring + head, wsrc, wbytes, &full[d]);
-                    if (hbytes) bulk_g2s(ring + head + hoff, a.h + (size_t)tb->base[slot] * a.I, hbytes, &full[d]);
-                    unsigned long long* tr = trace_rec(a, 1, n);
-                    if (tr) tr[4] = global_timer_ns();
-                }
-                __syncwarp();
-                head += need;
-                ++n;
             }
         }
         if (lane == 0) {
             if (ok) {
-                // end marker in the next descriptor once it is free
+                // end markers: the next descriptor once it is free, and the stagers' next run
                 if (n >= kK3Desc && !mbar_wait(&empty[n % kK3Desc], ((n / kK3Desc) - 1) & 1, &a.ctl->status)) {
                     ok = false;
                 } else {
                     meta[n % kK3Desc].slot = -1;
                     mbar_arrive(&full[n % kK3Desc]);
+                }
+                if (ok && (runs < 2 || mbar_wait(&hready[runs & 1], ((runs - 2) >> 1) & 1, &a.ctl->status))) {
+                    hdesc[runs & 1] = -1;
+                    mbar_arrive(&hload[runs & 1]);
+                } else {
+                    ok = false;
                 }
             }
             if (!ok) {
@@ -903,109 +1004,151 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
             }
         }
         __syncwarp();
-    } else {
-        // ---------------- consumers ----------------
-        const uint32_t hf_s = smem_addr(hf), hd_s = smem_addr(hd);
-        int runs = 0;
-        const int tile = warp >> 2, q = warp & 3;
-        const int n8 = a.I / 128, n16 = a.I / 64;  // k-steps per warp (s8 32-wide, bf16 16-wide)
-        // As in K2: item n's products, then item n-1 is finished (y rows written, its descriptor
-        // released), then item n's partial tile buffer is released.
-        int pend_slot = -1, pend_blk = 0, pend_n = 0, pend_d = 0;
+    } else if (warp == 0) {
+        // ---------------- MMA warp ----------------
         bool ok = true;
-        auto finish_pending = [&]() {
-            const int b = pend_n % kRedBufs;
-            ok = mbar_wait_warp(&redbar[b], (pend_n / kRedBufs) & 1, &abort_flag, &a.ctl->status);
-            if (!ok) return;
-            dn_finish(a, *tb, pend_slot, pend_blk, ds->red[b], tid);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&empty[pend_d]);
-        };
+        int cur = 0, runs = 0, b = 0;
+        const uint32_t hb_s = smem_addr(hb);
         for (int n = 0;; ++n) {
             const int d = n % kK3Desc;
-            unsigned long long* tr = warp == 0 ? trace_rec(a, 1, n) : nullptr;
+            unsigned long long* tr = trace_rec(a, 1, n);
             if (tr && lane == 0) tr[0] = global_timer_ns();
             if (!mbar_wait_warp(&full[d], (n / kK3Desc) & 1, &abort_flag, &a.ctl->status)) {
                 ok = false;
                 break;
             }
-            const int slot = meta[d].slot, blk = meta[d].blk;
-            if (slot < 0) {
-                if (pend_slot >= 0) finish_pending();
-                pend_slot = -1;
-                break;
-            }
+            const int slot = meta[d].slot;
+            if (slot < 0) break;
             if (tr && lane == 0) tr[1] = global_timer_ns();
-            const bool i8 = slot >= a.S && a.int8;
-            const uint32_t item_s = launder(smem_addr(ring + meta[d].off));
+            const int rb = meta[d].rb, ki = meta[d].ki;
             if (meta[d].hoff) {
-                // a run of this slot starts: every warp's products of the previous item must be
-                // done before the caches change (their partial tiles are all stored)
-                if (pend_slot >= 0 && !mbar_wait_warp(&redbar[pend_n % kRedBufs], (pend_n / kRedBufs) & 1,
-                                                      &abort_flag, &a.ctl->status)) {
-                    ok = false;
-                    break;
-                }
-                // stage its h rows (fp32, padded; rows >= count zero) and, for int8 weights, their digits
-                const float* hsrc = reinterpret_cast<const float*>(ring + meta[d].off + meta[d].hoff);
-                const int cnt = tb->count[slot];
-                for (int i = tid; i < kMaxB * (a.I / 4); i += kCW * 32) {
-                    const int qq = i / (a.I / 4), c4 = i % (a.I / 4);
-                    const float4 v = qq < cnt ? *reinterpret_cast<const float4*>(hsrc + (size_t)qq * a.I + 4 * c4)
-                                              : make_float4(0.f, 0.f, 0.f, 0.f);
-                    *reinterpret_cast<float4*>(hf + (size_t)qq * ldh + 4 * c4) = v;
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&hbar[runs & 1]);
-                if (!mbar_wait_warp(&hbar[runs & 1], (runs >> 1) & 1, &abort_flag, &a.ctl->status)) {
+                // a run starts: the previous run's image is free once its MMAs complete
+                if (runs > 0 && lane == 0) umma_commit(&bfree[(runs - 1) & 1]);
+                b = runs & 1;
+                if (!mbar_wait_warp(&hready[b], (runs >> 1) & 1, &abort_flag, &a.ctl->status)) {
                     ok = false;
                     break;
                 }
                 ++runs;
-                if (i8) {
-                    stage_digits(hf, ldh, a.I, cnt, hd, hsig, warp, lane);
-                    __syncwarp();
-                    if (lane == 0) mbar_arrive(&hbar[runs & 1]);
-                    if (!mbar_wait_warp(&hbar[runs & 1], (runs >> 1) & 1, &abort_flag, &a.ctl->status)) {
+            }
+            const bool i8 = slot >= a.S && a.int8;
+            const int nk = w2_items(a.I, i8);
+            unsigned char* item = ring + meta[d].off;
+            const uint32_t item_s = smem_addr(item), img_s = hb_s + (uint32_t)b * img_bytes;
+            if (i8) {
+                float sig[kMaxB];
+#pragma unroll
+                for (int t = 0; t < kMaxB; ++t) sig[t] = hsig[(b * kMaxB + t) * NG3 + ki];
+                const int j = acquire_acc(pipe, slot, rb, ki, 1 | (ki == nk - 1 ? 2 : 0),
+                                          reinterpret_cast<const float*>(item + kAtomBytes), sig, lane);
+                if (j < 0) {
+                    ok = false;
+                    break;
+                }
+                if (lane == 0) {
+#pragma unroll
+                    for (int s = 0; s < 4; ++s)
+                        umma_i8(pipe.tmem + 32u * j, umma_desc_sw128(item_s + 32 * s),
+                                umma_desc_sw128(img_s + ki * kDigitAtomBytes + 32 * s), kIdescS8, s > 0);
+                    umma_commit(&tfull[j]);
+                }
+            } else {
+                if (ki == 0) {
+                    cur = acquire_acc(pipe, slot, rb, 0, 2, nullptr, nullptr, lane);
+                    if (cur < 0) {
                         ok = false;
                         break;
                     }
-                    ++runs;
+                }
+                if (lane == 0) {
+#pragma unroll
+                    for (int at = 0; at < 2; ++at)
+#pragma unroll
+                        for (int s = 0; s < 4; ++s)
+                            umma_f16(pipe.tmem + 32u * cur, umma_desc_sw128(item_s + at * kAtomBytes + 32 * s),
+                                     umma_desc_sw128(img_s + (2 * ki + at) * kTermAtomBytes + 32 * s), kIdescBf16,
+                                     (ki | at | s) != 0);
+                    if (ki == nk - 1) umma_commit(&tfull[cur]);
                 }
             }
-            float acc[4] = {0.f, 0.f, 0.f, 0.f};
-            if (i8) {
-                const uint32_t rowb = (uint32_t)packed_row_bytes(a.I, true);
-                const int NG = a.I / 128;
-                const uint32_t rows = item_s + (uint32_t)tile * 16 * rowb, sc = item_s + kW2Rows * rowb;
-                mma_tile_s8(rows, rowb, tile * 16, sc, NG, q * n8, q * n8 + n8, hd_s, hsig, lane, acc);
-            } else {
-                const uint32_t rowb = (uint32_t)packed_row_bytes(a.I, false);
-                const uint32_t rows = item_s + (uint32_t)tile * 16 * rowb;
-                mma_tile_bf16(rows, rowb, q * n16, q * n16 + n16, hf_s, ldh, lane, acc);
+            if (lane == 0) {
+                umma_commit(&freed[d]);  // the item's ring bytes are free once these MMAs complete
+                mbar_arrive(&empty[d]);  // the descriptor is no longer read
             }
-            fence_regs(acc);
-            __syncwarp();
-            if (tr && lane == 0) tr[5] = global_timer_ns();
-            if (lane == 0) mbar_arrive(&freed[d]);  // the item's ring bytes are no longer read
-            store_partial(ds->red[n % kRedBufs], warp, lane, acc);
-            if (pend_slot >= 0) {
-                finish_pending();
-                if (!ok) break;
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&redbar[n % kRedBufs]);
             if (tr && lane == 0) {
-                tr[6] = global_timer_ns();
                 tr[2] = global_timer_ns();
-                tr[3] = ((unsigned long long)slot << 32) | (unsigned)blk;
+                tr[3] = ((unsigned long long)slot << 32) | ((unsigned)rb << 16) | (unsigned)ki;
             }
-            pend_slot = slot;
-            pend_blk = blk;
-            pend_n = n;
-            pend_d = d;
+            __syncwarp();
         }
-        if (ev && tid == 0) ev[2] = global_timer_ns();
+        if (ok) {
+            const int j = acquire_acc(pipe, -1, 0, 0, 0, nullptr, nullptr, lane);  // end marker
+            if (j >= 0 && lane == 0) mbar_arrive(&tfull[j]);
+        } else if (lane == 0) {
+            abort_flag = 1;
+        }
+        if (lane == 0) {
+            umma_commit(mdone);
+            mbar_wait(mdone, 0, &a.ctl->status);
+        }
+        __syncwarp();
+    } else if (warp <= 3) {
+        // ---------------- stagers: a run's h rows -> its operand image ----------------
+        for (int r = 0;; ++r) {
+            const int b = r & 1;
+            if (!mbar_wait_warp(&hload[b], (r >> 1) & 1, &abort_flag, &a.ctl->status)) break;
+            const int n = hdesc[b];
+            if (n < 0) break;
+            const int d = n % kK3Desc;
+            if (!mbar_wait_warp(&full[d], (n / kK3Desc) & 1, &abort_flag, &a.ctl->status)) break;
+            if (r >= 2 && !mbar_wait_warp(&bfree[b], ((r - 2) >> 1) & 1, &abort_flag, &a.ctl->status)) break;
+            const int slot = meta[d].slot, cnt = tb->count[slot];
+            const bool i8 = slot >= a.S && a.int8;
+            const float* h = reinterpret_cast<const float*>(ring + meta[d].off + meta[d].hoff);
+            unsigned char* img = hb + (size_t)b * img_bytes;
+            for (int task = warp - 1; task < cnt * NG3; task += 3) {
+                const int e = task / NG3, g = task - e * NG3;
+                const float4 v = *reinterpret_cast<const float4*>(h + (size_t)e * a.I + 128 * g + 4 * lane);
+                if (i8) {
+                    uint32_t w[3];
+                    const float sg = group_digits(v, w);
+                    if (lane == 0) hsig[(b * kMaxB + e) * NG3 + g] = sg;
+                    put_digits(img, g, e, lane, w);
+                } else {
+                    put_terms(img, g, e, lane, v);
+                }
+            }
+            fence_proxy_async_smem();  // generic writes of the image, read next by the tensor cores
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&hready[b]);
+        }
+    } else {
+        // ---------------- epilogue ----------------
+        const int q = warp & 3, row = 32 * q + lane;
+        float acc[kMaxB];
+#pragma unroll
+        for (int t = 0; t < kMaxB; ++t) acc[t] = 0.0f;
+        for (int c = 0;; ++c) {
+            AccRead r;
+            if (!read_acc(pipe, c, q, lane, true, r)) break;
+            if (r.flags & 1) fold_s8(r, r.sig, acc);
+            else fold_bf16(r, acc);
+            if (r.flags & 2) {
+                const int cnt = tb->count[r.slot], base = tb->base[r.slot];
+#pragma unroll
+                for (int t = 0; t < kMaxB; ++t) {
+                    if (t < cnt) a.y[(size_t)(base + t) * a.H + kRowBlock * r.rb + row] = acc[t];
+                    acc[t] = 0.0f;
+                }
+            }
+        }
+        if (ev && tid == 128) ev[2] = global_timer_ns();
+    }
+    tc_fence_before();
+    __syncthreads();
+    if (warp == 0) {
+        tc_fence_after();
+        tmem_dealloc(tmem_base, kTmemCols);
     }
 
     // ---------------- combine: every CTA's y rows are written (grid barrier) ----------------
@@ -1051,70 +1194,68 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     // K2 / K3 leave room on their SM for their own static shared memory (< 1 KB) and their
     // reservation, and for K1's CTAs (no shared memory, 1 KB reservation each), so K1 can start
-    // beside them
+    // beside them. The dynamic region is 1024-byte aligned (the swizzled operands).
     const int k1_ctas = a.E * 8 + kMaxB * (a.H / 128);
     const int k1_per_sm = (k1_ctas + sms - 1) / sms;
     max_smem = std::min(max_smem - 1024, sm_smem - 1024 - 1024 - 1024 * k1_per_sm);
+    max_smem &= ~1023;
     if (g_decode_trace) {
         a.trace = g_decode_trace;
         a.trace_items = (int)(g_decode_trace_bytes / (sizeof(unsigned long long) * 8 * (size_t)sms)) & ~1;
     }
 
-    // ---- K1: logit partials (one CTA per expert and segment) and the activation digits
+    // ---- K1: logit partials (one CTA per expert and segment) and the B operand images
     {
         void* args[] = {&a};
         err = launch_pdl(reinterpret_cast<const void*>(decode_logits_kernel), dim3(k1_ctas), dim3(32), 0, st, args);
         if (err != cudaSuccess) return err;
     }
-    // ---- K2: route + gate/up; a stage holds one w13 block
+    // ---- K2: route + gate/up; a stage holds one w13 item (the last one first the logit partials)
     {
-        uint32_t stage_bytes = (uint32_t)up(
-            std::max({w13_block_bytes(a.H, a.G, false), a.int8 ? w13_block_bytes(a.H, a.G, true) : size_t(0),
-                      sizeof(float) * kMaxB * 64 * 8}),  // the last stage first holds the logit partials
-            128);
+        const uint32_t stage_bytes = (uint32_t)up(
+            std::max({w13_item_bytes(false), a.int8 ? w13_item_bytes(true) : size_t(0),
+                      sizeof(float) * kMaxB * 64 * 8}),
+            1024);
         const size_t off_tbl = 256;
         const size_t off_route = off_tbl + up(sizeof(SlotTable), 128);
         const size_t off_meta = off_route + up(sizeof(RouteSmem), 128);
-        const size_t off_gu = off_meta + up(sizeof(ItemMeta) * 8, 128);
-        const size_t off_xf = off_gu + up(sizeof(GuSmem), 128);
-        const size_t off_xd = off_xf + up(sizeof(float) * kMaxB * (a.H + 4), 128);
-        const size_t xd_bytes = a.int8 ? (size_t)(a.H / 32) * 3 * 32 * 8 : 0;
-        const size_t off_sig = off_xd + up(xd_bytes, 128);
-        const size_t off_stages = up(off_sig + sizeof(float) * kMaxB * (a.H / 128), 128);
+        const size_t off_acc = off_meta + up(sizeof(ItemMeta) * 8, 128);
+        const size_t off_sig = off_acc + up(sizeof(AccMeta) * kAccSlots, 128);
+        const size_t off_xb = up(off_sig + sizeof(float) * kMaxB * (a.H / 128), 1024);
+        const size_t off_xd = off_xb + (size_t)a.H * 32;
+        const size_t off_stages = off_xd + (a.int8 ? (size_t)a.H * 32 : 0);
         if ((size_t)max_smem < off_stages + 2 * (size_t)stage_bytes) return cudaErrorInvalidConfiguration;
         int nst = (int)std::min<size_t>(8, ((size_t)max_smem - off_stages) / stage_bytes);
         const size_t smem = off_stages + (size_t)nst * stage_bytes;
         const void* k2 = reinterpret_cast<const void*>(decode_gate_up_kernel);
         err = ensure_smem_optin(k2, smem);
         if (err != cudaSuccess) return err;
-        uint32_t o[8] = {(uint32_t)off_tbl, (uint32_t)off_route, (uint32_t)off_meta, (uint32_t)off_gu,
-                         (uint32_t)off_xf,  (uint32_t)off_xd,    (uint32_t)off_sig,  (uint32_t)off_stages};
-        void* args[] = {&a, &nst, &stage_bytes, &o[0], &o[1], &o[2], &o[3], &o[4], &o[5], &o[6], &o[7]};
+        uint32_t o[8] = {(uint32_t)off_tbl, (uint32_t)off_route, (uint32_t)off_meta, (uint32_t)off_acc,
+                         (uint32_t)off_xd,  (uint32_t)off_xb,    (uint32_t)off_sig,  (uint32_t)off_stages};
+        uint32_t sb = stage_bytes;
+        void* args[] = {&a, &nst, &sb, &o[0], &o[1], &o[2], &o[3], &o[4], &o[5], &o[6], &o[7]};
         err = launch_pdl(k2, dim3(sms), dim3(kThreads), smem, st, args);
         if (err != cudaSuccess) return err;
     }
-    // ---- K3: the rest of shared memory is the item ring
+    // ---- K3: two operand images for slot runs, the rest of shared memory is the item ring
     {
-        const size_t off_tbl = 512;  // 3 x kK3Desc + kRedBufs + 2 mbarriers before it
+        const size_t off_tbl = 512;  // 3 x kK3Desc + 2 x kAccSlots + 7 mbarriers before it
         const size_t off_meta = off_tbl + up(sizeof(SlotTable), 128);
-        const size_t off_dn = off_meta + up(sizeof(ItemMeta) * kK3Desc, 128);
-        const size_t off_hf = off_dn + up(sizeof(DnSmem), 128);
-        const size_t off_hd = off_hf + up(sizeof(float) * kMaxB * (a.I + 4), 128);
-        const size_t hd_bytes = a.int8 ? (size_t)(a.I / 32) * 3 * 32 * 8 : 0;
-        const size_t off_sig = off_hd + up(hd_bytes, 128);
-        const size_t off_ring = up(off_sig + sizeof(float) * kMaxB * (a.I / 128), 128);
+        const size_t off_acc = off_meta + up(sizeof(ItemMeta) * kK3Desc, 128);
+        const size_t off_hsig = off_acc + up(sizeof(AccMeta) * kAccSlots, 128);
+        const size_t off_hb = up(off_hsig + sizeof(float) * 2 * kMaxB * (a.I / 128), 1024);
+        const size_t off_ring = off_hb + 2 * (size_t)a.I * 32;
         const size_t max_item =
-            up(std::max(w2_block_bytes(a.I, a.G, false), a.int8 ? w2_block_bytes(a.I, a.G, true) : size_t(0)), 16) +
-            (size_t)kMaxB * a.I * 4;
-        if ((size_t)max_smem < off_ring + max_item) return cudaErrorInvalidConfiguration;
-        uint32_t ring_bytes = (uint32_t)(((size_t)max_smem - off_ring) & ~size_t(127));
+            up(std::max(w2_item_bytes(false), a.int8 ? w2_item_bytes(true) : size_t(0)), 16) + (size_t)kMaxB * a.I * 4;
+        if ((size_t)max_smem < off_ring + max_item + 1024) return cudaErrorInvalidConfiguration;
+        uint32_t ring_bytes = (uint32_t)(((size_t)max_smem - off_ring) & ~size_t(1023));
         const size_t smem = off_ring + ring_bytes;
         const void* k3 = reinterpret_cast<const void*>(decode_down_kernel);
         err = ensure_smem_optin(k3, smem);
         if (err != cudaSuccess) return err;
-        uint32_t o[7] = {(uint32_t)off_tbl, (uint32_t)off_meta, (uint32_t)off_dn, (uint32_t)off_hf,
-                         (uint32_t)off_hd,  (uint32_t)off_sig,  (uint32_t)off_ring};
-        void* args[] = {&a, &ring_bytes, &o[0], &o[1], &o[2], &o[3], &o[4], &o[5], &o[6]};
+        uint32_t o[6] = {(uint32_t)off_tbl, (uint32_t)off_meta, (uint32_t)off_acc,
+                         (uint32_t)off_hb,  (uint32_t)off_hsig, (uint32_t)off_ring};
+        void* args[] = {&a, &ring_bytes, &o[0], &o[1], &o[2], &o[3], &o[4], &o[5]};
         err = launch_pdl(k3, dim3(sms), dim3(kThreads), smem, st, args);
         if (err != cudaSuccess) return err;
     }

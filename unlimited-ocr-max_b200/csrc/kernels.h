@@ -64,7 +64,8 @@ struct DecodeArgs {
     float* out;     // [B, H]
     DecodeCtl* ctl;
     float* logits;       // [8][64][8] router logit partials (token, expert, segment)
-    uint32_t* xdig;      // [H / 32][3][32][2] words: x as int8 digits in fragment order (K1 -> K2)
+    unsigned char* xd;   // [H / 128][32 rows][128 B]: x as int8 digit planes, the MMA B operand image (K1 -> K2)
+    unsigned char* xb;   // [H / 64][16 rows][128 B]: x as two bf16 terms, the MMA B operand image
     float* xsig;         // [8][H / 128] scales of the digit groups
     RouteTable* table;
     unsigned long long* trace;  // optional per-CTA item timeline (diagnostics), null = off
@@ -115,11 +116,11 @@ struct PrefillLayout {
 PrefillLayout prefill_layout(int T, int H, int I, int E, int S, int topk, bool int8);
 cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& d, cudaStream_t st);
 
-// pack.cu
+// pack.cu: source rows at (e * estride + row * ld) elements
 cudaError_t launch_pack_w13(const void* gate, const void* up, const float* gs, const float* us, int E, int I, int H,
-                            int G, bool int8, void* out, cudaStream_t st);
-cudaError_t launch_pack_w2(const void* down, const float* ds, int E, int H, int I, int G, bool int8, void* out,
-                           cudaStream_t st);
+                            bool int8, long estride, long ld, void* out, cudaStream_t st);
+cudaError_t launch_pack_w2(const void* down, const float* ds, int E, int H, int I, bool int8, long estride, long ld,
+                           void* out, cudaStream_t st);
 cudaError_t launch_pack_shared(const uint16_t* gate, const uint16_t* up, const uint16_t* down, long S, long I, long H,
                                uint16_t* w13, uint16_t* w2, cudaStream_t st);
 

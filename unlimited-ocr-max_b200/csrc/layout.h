@@ -1,21 +1,26 @@
-// Packed expert-weight layouts (host and device). Weights are repacked once at load into
-// contiguous blocks sized for one bulk copy each: a decode work item is exactly one block, so
-// the streaming kernels issue one large copy per item instead of one per row and scale run.
-// Every packed row is followed by 16 bytes of padding: rows of a block then start on different
-// shared-memory banks, so the tensor-core fragment loads (8 rows x 8 bytes per lane group) are
-// conflict-free.
+// Packed expert-weight layouts (host and device). Weights are repacked once at load into the
+// shared-memory image the tcgen05 tensor cores read: K-major rows in 128-byte-swizzle atoms.
 //
-// gate|up "w13", per expert, I / P blocks of P row pairs (P = 8 for bf16, 16 for int8):
-//     [gate rows pP .. pP+P-1 | up rows pP .. pP+P-1          (2P rows of row_bytes)
-//      | int8 only: gate scales (P x H/G fp32) | up scales (P x H/G fp32)]
-//   For bf16 this is the [E*2I, H] row matrix (row stride H + 8 elements) with gate and up rows
-//   interleaved in groups of 8: the prefill GEMM reads it through a 2-D tensor map (a 256-row
-//   tile = 128 gate + 128 up rows, paired column c <-> c + 8 within every 16).
-// down "w2", per expert, H / 32 blocks of 32 rows:
-//     [rows (32 rows of row_bytes) | int8 only: scales (32 x I/G fp32)]
-//   For bf16 this is the [E*H, I] row matrix with row stride I + 8 elements.
-// Shared experts (always bf16): w13_shared as bf16 w13 with S pseudo-experts (shared expert q
-// owns intermediate rows [qI, (q+1)I) of the checkpoint's shared MLP); w2_shared as bf16 w2.
+// Atom: R rows x 128 bytes of one K range (128 int8 or 64 bf16 elements); byte c of row r sits at
+//     r * 128 + (((c / 16) ^ (r % 8)) * 16) + c % 16
+// (the 128-byte swizzle, 8-row groups 1024 bytes apart), so a block copied verbatim to a
+// 1024-byte-aligned shared-memory address is a valid SWIZZLE_128B K-major MMA operand.
+//
+// Row block: 128 rows (the MMA's M). Item: the row block's atoms over one K range plus, for
+// int8, their fp32 scales [atom][128 rows] (one 128-element group per int8 atom):
+//     [atom 0: 128 rows x 128 B][atom 1]...[int8: scales of atom 0 (128 fp32)][atom 1]...
+// A decode work item is exactly one item: one bulk copy.
+//
+// gate|up "w13", per expert I/64 row blocks of 64 row pairs, rows interleaved in groups of 8
+// (rows 16i..16i+7 = gate pairs 8i..8i+7, rows 16i+8..16i+15 = the matching up pairs), each
+// row block H / item_k items of 2 atoms (int8: K 256 = 2 groups; bf16: K 128).
+// down "w2", per expert H/128 row blocks of 128 output rows, each I/128 items (int8: 1 atom =
+// 1 group; bf16: 2 atoms).
+// For bf16 the items of a row block are its atoms back to back, so the whole stack is the 4-D
+// array [row block][K / 64 atoms][128 rows][128 B]: the prefill GEMM reads 256-row tiles of it
+// through a 4-D tensor map (two consecutive row blocks, one atom) without swizzling.
+// Shared experts (always bf16): w13_shared / w2_shared in the bf16 layouts with S pseudo-experts
+// (shared expert q owns intermediate rows [qI, (q+1)I) of the checkpoint's shared MLP).
 #pragma once
 
 #include <stddef.h>
@@ -23,26 +28,34 @@
 
 namespace uocr {
 
-constexpr int kW2Rows = 32;   // rows per down block
-constexpr int kRowPad = 16;   // bytes after every packed row
+constexpr int kRowBlock = 128;    // rows of a row block
+constexpr int kAtomRowBytes = 128;
+constexpr int kAtomBytes = kRowBlock * kAtomRowBytes;  // 16 KB
 
-// bytes of one packed row of K elements
-__host__ __device__ inline size_t packed_row_bytes(int K, bool int8) {
-    return (size_t)K * (int8 ? 1 : 2) + kRowPad;
+// byte offset of (row r, byte c) inside an atom
+__host__ __device__ inline uint32_t atom_offset(int r, int c) {
+    return (uint32_t)r * 128u + ((((uint32_t)c >> 4) ^ ((uint32_t)r & 7u)) << 4) + ((uint32_t)c & 15u);
 }
-__host__ __device__ inline int w13_pairs(bool int8) { return int8 ? 16 : 8; }
-__host__ __device__ inline size_t w13_block_bytes(int H, int G, bool int8) {
-    const size_t P = (size_t)w13_pairs(int8);
-    return 2 * P * packed_row_bytes(H, int8) + (int8 ? 2 * P * (size_t)(H / G) * 4 : 0);
+
+__host__ __device__ inline int w13_atoms() { return 2; }
+__host__ __device__ inline int w2_atoms(bool int8) { return int8 ? 1 : 2; }
+// K elements of one atom
+__host__ __device__ inline int atom_k(bool int8) { return int8 ? 128 : 64; }
+__host__ __device__ inline size_t item_bytes(int atoms, bool int8) {
+    return (size_t)atoms * kAtomBytes + (int8 ? (size_t)atoms * kRowBlock * 4 : 0);
 }
-__host__ __device__ inline size_t w13_expert_bytes(int I, int H, int G, bool int8) {
-    return (size_t)(I / w13_pairs(int8)) * w13_block_bytes(H, G, int8);
+// items per row block, and item bytes, of the gate|up and down stacks
+__host__ __device__ inline int w13_items(int H, bool int8) { return H / (w13_atoms() * atom_k(int8)); }
+__host__ __device__ inline int w2_items(int I, bool int8) { return I / (w2_atoms(int8) * atom_k(int8)); }
+__host__ __device__ inline size_t w13_item_bytes(bool int8) { return item_bytes(w13_atoms(), int8); }
+__host__ __device__ inline size_t w2_item_bytes(bool int8) { return item_bytes(w2_atoms(int8), int8); }
+__host__ __device__ inline size_t w13_expert_bytes(int I, int H, bool int8) {
+    return (size_t)(I / 64) * w13_items(H, int8) * w13_item_bytes(int8);
 }
-__host__ __device__ inline size_t w2_block_bytes(int I, int G, bool int8) {
-    return (size_t)kW2Rows * packed_row_bytes(I, int8) + (int8 ? (size_t)kW2Rows * (I / G) * 4 : 0);
+__host__ __device__ inline size_t w2_expert_bytes(int H, int I, bool int8) {
+    return (size_t)(H / kRowBlock) * w2_items(I, int8) * w2_item_bytes(int8);
 }
-__host__ __device__ inline size_t w2_expert_bytes(int H, int I, int G, bool int8) {
-    return (size_t)(H / kW2Rows) * w2_block_bytes(I, G, int8);
-}
+// row of the gate|up row block holding gate (up = 0) or up (up = 1) pair p (0..63)
+__host__ __device__ inline int w13_block_row(int p, int up) { return (p >> 3) * 16 + up * 8 + (p & 7); }
 
 }  // namespace uocr

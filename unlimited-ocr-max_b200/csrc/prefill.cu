@@ -163,52 +163,36 @@ __global__ void __launch_bounds__(256) prefill_gather_kernel(const float* __rest
     }
 }
 
-// int8 gate|up blocks (layout.h) -> the bf16 gate|up row matrix (8-row interleave): each bf16
-// element is bf16_rne(f32(q) * scale), int8_dequant_expert's bits (kernels/moe_int8.mojo:330-340).
-// Thread: 8 consecutive elements of one bf16 row.
-__global__ void __launch_bounds__(256) prefill_dequant_w13_kernel(const unsigned char* __restrict__ w, long rows, int I,
-                                                                  int H, int G, size_t blk_bytes,
-                                                                  uint16_t* __restrict__ out) {
-    const long i = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 8;
-    if (i >= rows * H) return;
-    const long prow = i / H;  // bf16 packed row: 16-row groups of 8 gate then 8 up rows
-    const int k = (int)(i - prow * H);
-    const long per_e = 2L * I;
-    const long e = prow / per_e, pr = prow - e * per_e;
-    const bool is_up = (pr & 15) >= 8;
-    const long r = (pr >> 4) * 8 + (pr & 7);  // gate/up row within the expert
-    const long b16 = r >> 4, j = r & 15;      // int8 block of 16 row pairs, row within it
-    const unsigned char* blk = w + (size_t)(e * (I / 16) + b16) * blk_bytes;
-    const size_t rowb = packed_row_bytes(H, true);
-    const unsigned char* src = blk + (size_t)(is_up ? 16 + j : j) * rowb + k;
-    const float* sc = reinterpret_cast<const float*>(blk + 32 * rowb) + (is_up ? 16 : 0) * (H / G) + j * (H / G);
-    const uint2 v = *reinterpret_cast<const uint2*>(src);
-    float f[8];
-    unpack_s8x8(v.x, v.y, f);
-    uint16_t o[8];
+// int8 items (layout.h) -> the bf16 row-block layout [row block][K / 64 atoms][128 rows][128 B]:
+// each bf16 element is bf16_rne(f32(q) * scale), int8_dequant_expert's bits
+// (kernels/moe_int8.mojo:330-340). Thread: 16 elements of one row (one 16-byte int8 chunk ->
+// two 16-byte bf16 chunks). `atoms` int8 atoms per item (w13: 2, w2: 1).
+__global__ void __launch_bounds__(256) prefill_dequant_kernel(const unsigned char* __restrict__ w, long nrb, int K,
+                                                              int atoms, unsigned char* __restrict__ out) {
+    const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+    const long per_rb = (long)kRowBlock * (K / 16);
+    if (i >= nrb * per_rb) return;
+    const long rb = i / per_rb;
+    const int rem = (int)(i - rb * per_rb), r = rem / (K / 16), k = 16 * (rem - r * (K / 16));
+    const int ik = atoms * 128, ki = k / ik, a = (k % ik) / 128, c = k % 128;
+    const unsigned char* item = w + ((size_t)rb * (K / ik) + ki) * item_bytes(atoms, true);
+    const uint4 v = *reinterpret_cast<const uint4*>(item + (size_t)a * kAtomBytes + atom_offset(r, c));
+    const float sc = reinterpret_cast<const float*>(item + (size_t)atoms * kAtomBytes)[a * kRowBlock + r];
+    float f0[8], f1[8];
+    unpack_s8x8(v.x, v.y, f0);
+    unpack_s8x8(v.z, v.w, f1);
+    uint32_t o[8];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) o[q] = f32_to_bf16_rne(__fmul_rn(f[q], sc[(k + q) / G]));
-    *reinterpret_cast<uint4*>(out + i) = *reinterpret_cast<const uint4*>(o);
-}
-
-// int8 down blocks (32 rows + scales) -> bf16 [E*H, I].
-__global__ void __launch_bounds__(256) prefill_dequant_w2_kernel(const unsigned char* __restrict__ w, long rows, int I,
-                                                                 int G, size_t blk_bytes, uint16_t* __restrict__ out) {
-    const long i = ((long)blockIdx.x * blockDim.x + threadIdx.x) * 8;
-    if (i >= rows * I) return;
-    const long row = i / I;  // e * H + j
-    const int k = (int)(i - row * I);
-    const unsigned char* blk = w + (size_t)(row / kW2Rows) * blk_bytes;
-    const int j = (int)(row % kW2Rows);
-    const size_t rowb = packed_row_bytes(I, true);
-    const uint2 v = *reinterpret_cast<const uint2*>(blk + (size_t)j * rowb + k);
-    const float* sc = reinterpret_cast<const float*>(blk + (size_t)kW2Rows * rowb) + j * (I / G);
-    float f[8];
-    unpack_s8x8(v.x, v.y, f);
-    uint16_t o[8];
-#pragma unroll
-    for (int q = 0; q < 8; ++q) o[q] = f32_to_bf16_rne(__fmul_rn(f[q], sc[(k + q) / G]));
-    *reinterpret_cast<uint4*>(out + i) = *reinterpret_cast<const uint4*>(o);
+    for (int q = 0; q < 4; ++q) {
+        o[q] = (uint32_t)f32_to_bf16_rne(__fmul_rn(f0[2 * q], sc)) |
+               ((uint32_t)f32_to_bf16_rne(__fmul_rn(f0[2 * q + 1], sc)) << 16);
+        o[4 + q] = (uint32_t)f32_to_bf16_rne(__fmul_rn(f1[2 * q], sc)) |
+                   ((uint32_t)f32_to_bf16_rne(__fmul_rn(f1[2 * q + 1], sc)) << 16);
+    }
+    unsigned char* dst = out + ((size_t)rb * (K / 64) + k / 64) * kAtomBytes;
+    const int c2 = (k % 64) * 2;
+    *reinterpret_cast<uint4*>(dst + atom_offset(r, c2)) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(dst + atom_offset(r, c2 + 16)) = make_uint4(o[4], o[5], o[6], o[7]);
 }
 
 // out[t][j] (+)= sum_s w[t,s] * y[dest[t*k+s]][j] (entries without an expert skipped)
@@ -338,7 +322,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                     if (round > 0 && !gwait(&gs->empty[s], (round - 1) & 1, abort_flag, status)) break;
                     mbar_arrive_expect_tx(&gs->full[s], kATile + kBTile);
                     tma_load_2d(sA + s * kATile, &tmA, kt * kBK, a_row, &gs->full[s]);
-                    tma_load_2d(sB + s * kBTile, mb, kt * kBK, b_row, &gs->full[s]);
+                    tma_load_4d(sB + s * kBTile, mb, 0, 0, kt, b_row / kRowBlock, &gs->full[s]);
                     if (++s == kGStages) { s = 0; ++round; }
                 }
             }
@@ -483,6 +467,21 @@ static bool make_map_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint6
               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
+// The bf16 row-block weights (layout.h) as the 4-D array [nrb][K / 64][128 rows][64 elements],
+// box {64, 128, 1, 2}: 256 rows (two consecutive row blocks) of one 64-element atom, already
+// swizzled in memory, so copied without swizzling into a 1024-byte-aligned tile.
+static bool make_map_bf16_blocks(CUtensorMap* m, const void* base, uint64_t nrb, uint64_t K) {
+    auto fn = encode_fn();
+    if (!fn) return false;
+    const cuuint64_t dims[4] = {64, 128, K / 64, nrb};
+    const cuuint64_t strides[3] = {128, (cuuint64_t)kAtomBytes, (cuuint64_t)(K / 64) * kAtomBytes};
+    const cuuint32_t box[4] = {64, 128, 1, 2};
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
+              CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+}
+
 size_t gemm_smem_bytes() {
     return 1024 + kGStages * (kATile + kBTile) + 256 + sizeof(PrefillPlan);
 }
@@ -572,31 +571,28 @@ cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& 
     const void* w13 = a.w13;
     const void* w2 = a.w2;
     if (a.int8 && k > 0) {
-        uint16_t* w13d = reinterpret_cast<uint16_t*>(ws + d.w13);
-        uint16_t* w2d = reinterpret_cast<uint16_t*>(ws + d.w2);
-        const long n13 = (long)E * 2 * I * H, n2 = (long)E * H * I;
-        prefill_dequant_w13_kernel<<<(unsigned)((n13 / 8 + 255) / 256), 256, 0, st>>>(
-            reinterpret_cast<const unsigned char*>(a.w13), (long)E * 2 * I, I, H, a.G, w13_block_bytes(H, a.G, true),
-            w13d);
-        prefill_dequant_w2_kernel<<<(unsigned)((n2 / 8 + 255) / 256), 256, 0, st>>>(
-            reinterpret_cast<const unsigned char*>(a.w2), (long)E * H, I, a.G, w2_block_bytes(I, a.G, true), w2d);
+        unsigned char* w13d = reinterpret_cast<unsigned char*>(ws + d.w13);
+        unsigned char* w2d = reinterpret_cast<unsigned char*>(ws + d.w2);
+        const long nrb13 = (long)E * (2 * I / kRowBlock), nrb2 = (long)E * (H / kRowBlock);
+        const long n13 = nrb13 * kRowBlock * (H / 16), n2 = nrb2 * kRowBlock * (I / 16);
+        prefill_dequant_kernel<<<(unsigned)((n13 + 255) / 256), 256, 0, st>>>(
+            reinterpret_cast<const unsigned char*>(a.w13), nrb13, H, w13_atoms(), w13d);
+        prefill_dequant_kernel<<<(unsigned)((n2 + 255) / 256), 256, 0, st>>>(
+            reinterpret_cast<const unsigned char*>(a.w2), nrb2, I, w2_atoms(true), w2d);
         w13 = w13d;
         w2 = w2d;
     }
     // upper bound of m-tiles (the plan holds the exact count on the device)
     const int max_mtiles = (kT + 127) / 128 + (k > 0 ? E : 0) + S * ((T + 127) / 128);
     CUtensorMap mA1, mB1, mBs1, mA2, mB2, mBs2;
-    // packed bf16 weights have padded rows (layout.h); the int8 path's dequantized copies do not
-    const uint64_t ld13 = a.int8 ? H : packed_row_bytes(H, false) / 2;
-    const uint64_t ld2 = a.int8 ? I : packed_row_bytes(I, false) / 2;
     if (!make_map_bf16(&mA1, xperm, (uint64_t)kT + T, H, kBM, H) ||
-        !make_map_bf16(&mB1, w13, (uint64_t)E * 2 * I, H, kBN, ld13) ||
+        !make_map_bf16_blocks(&mB1, w13, (uint64_t)E * 2 * I / kRowBlock, H) ||
         !make_map_bf16(&mA2, h, (uint64_t)kT + (uint64_t)S * T, I, kBM, I) ||
-        !make_map_bf16(&mB2, w2, (uint64_t)E * H, I, kBN, ld2))
+        !make_map_bf16_blocks(&mB2, w2, (uint64_t)E * H / kRowBlock, I))
         return cudaErrorInvalidValue;
     if (S > 0) {
-        if (!make_map_bf16(&mBs1, a.w13_shared, (uint64_t)S * 2 * I, H, kBN, packed_row_bytes(H, false) / 2) ||
-            !make_map_bf16(&mBs2, a.w2_shared, (uint64_t)S * H, I, kBN, packed_row_bytes(I, false) / 2))
+        if (!make_map_bf16_blocks(&mBs1, a.w13_shared, (uint64_t)S * 2 * I / kRowBlock, H) ||
+            !make_map_bf16_blocks(&mBs2, a.w2_shared, (uint64_t)S * H / kRowBlock, I))
             return cudaErrorInvalidValue;
     } else {
         mBs1 = mB1;  // no shared groups in the plan: never read
