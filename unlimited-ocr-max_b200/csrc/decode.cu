@@ -34,6 +34,8 @@
 // status code in the workspace and the kernel winds down without writing its output.
 #include <algorithm>
 
+#include <cuda_bf16.h>
+
 #include "common.cuh"
 #include "kernels.h"
 #include "layout.h"
