@@ -31,11 +31,12 @@ def items(rows: np.ndarray, scales, atoms: int) -> bytes:
     out = bytearray()
     per_item = atoms * 128
     for i0 in range(0, raw.shape[1], per_item):
-        for a in range(atoms):
+        here = min(atoms, (raw.shape[1] - i0) // 128)  # the last item may be shorter
+        for a in range(here):
             out += swizzle(np.ascontiguousarray(raw[:, i0 + a * 128:i0 + (a + 1) * 128]))
         if scales is not None:
             g0 = i0 // 128  # int8: one byte per element, so byte offset / 128 = group
-            for a in range(atoms):
+            for a in range(here):
                 out += np.ascontiguousarray(scales[:, g0 + a]).astype(np.float32).tobytes()
     return bytes(out)
 
@@ -61,14 +62,14 @@ def w2_ref(down: np.ndarray, ds) -> bytes:
     for e in range(E):
         for rb in range(H // 128):
             j = slice(128 * rb, 128 * rb + 128)
-            out += items(down[e, j], None if ds is None else ds[e, j], 1 if ds is not None else 2)
+            out += items(down[e, j], None if ds is None else ds[e, j], 2)
     return bytes(out)
 
 
 @pytest.mark.parametrize("int8", [False, True])
 def test_pack_routed_blocks(uocr, int8):
     L = uocr.load()
-    E, I, H, G = 3, 128, 256, 128
+    E, I, H, G = 3, 384, 256, 128  # I / 128 = 3: the down rows' last int8 item holds one group
     rng = np.random.default_rng(3)
     if int8:
         gate, up = (rng.integers(-127, 128, (E, I, H), dtype=np.int8) for _ in range(2))

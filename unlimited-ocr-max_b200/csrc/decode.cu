@@ -50,8 +50,9 @@ constexpr int kMaxB = 8;
 constexpr int kMaxSlotsSm = 72;              // shared (<= 8) + routed (<= 64)
 constexpr int kK3Desc = 8;                   // K3 items in flight (descriptor ring)
 constexpr uint32_t kBarConsumers = 1;        // named barrier of warps 0-7
-constexpr int kAccSlots = 4;                 // TMEM accumulators of 32 columns
-constexpr uint32_t kTmemCols = 128;
+constexpr int kAccSlots = 4;                 // TMEM accumulators of 64 columns
+constexpr uint32_t kAccCols = 64;
+constexpr uint32_t kTmemCols = kAccSlots * kAccCols;
 constexpr int kDigitAtomBytes = 32 * 128;    // int8 B operand atom: 3 digit planes x 8 tokens + 8 pad rows
 constexpr int kTermAtomBytes = 16 * 128;     // bf16 B operand atom: 2 terms x 8 tokens
 constexpr uint32_t kIdescS8 = umma_idesc_s8(128, 32);
@@ -77,14 +78,16 @@ struct ItemMeta {
     uint32_t hoff;  // K3: offset of the slot's h rows from `off` (0: none)
 };
 
-// One TMEM accumulator's description, written by the MMA warp, read by the epilogue.
+// One TMEM accumulator's description, written by the MMA warp, read by the epilogue. An
+// accumulator is 64 TMEM columns: int8 = up to two 128-groups (columns 0-31, 32-63; three digit
+// planes x 8 tokens + 8 unused each), bf16 = two terms x 8 tokens (columns 0-15).
 struct AccMeta {
     int slot;   // < 0: end of the work
     int rb;
-    int gi;     // int8: the 128-group of the accumulator
-    int flags;  // bit 0: int8 (one group), bit 1: the row block's last accumulator
-    float sig[kMaxB];       // K3 int8: digit scales of the slot's entries for the group
-    float scl[kRowBlock];   // int8: weight scales of the 128 rows for the group
+    int gi;     // int8: the 128-group of columns 0-31 (columns 32-63: gi + 1)
+    int flags;  // bit 0: int8, bit 1: the row block's last accumulator, bit 2: int8 with two groups
+    float sig[2][kMaxB];       // K3 int8: digit scales of the slot's entries for each group
+    float scl[2][kRowBlock];   // int8: weight scales of the 128 rows for each group
 };
 
 // The shared-expert slots (known from the shape alone).
@@ -337,27 +340,40 @@ UOCR_DEV void cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* x
     if (rv && tid == 0) rv[6] = global_timer_ns();
 }
 
-// Weighted static partition: the units of slots [first, last) in order, unit cost c(slot);
-// this CTA takes the units whose cost prefix starts in [lo, hi) of the total.
-struct Partition {
-    long long lo, hi;
-};
-template <class CostFn, class UnitsFn>
-UOCR_DEV Partition cta_share(int first, int last, CostFn cost, UnitsFn units) {
-    long long total = 0;
-    for (int s = first; s < last; ++s) total += (long long)units(s) * cost(s);
-    Partition p;
-    p.lo = total * blockIdx.x / gridDim.x;
-    p.hi = total * (blockIdx.x + 1) / gridDim.x;
-    return p;
+// Static partitions of work units over the CTAs (costs in 512-byte units). All intermediate
+// values fit 32-bit integers for the decode sizes (<= 1008 units of cost <= 640, G <= 1024);
+// the one ratio is a double division (64-bit integer division is slow on the device).
+// n equal units: CTA c takes [ceil(n c / G), ceil(n (c + 1) / G)).
+UOCR_DEV void even_units(int n, int c, int G, int& j0, int& j1) {
+    j0 = (n * c + G - 1) / G;
+    j1 = (n * (c + 1) + G - 1) / G;
 }
-// Units j of slot s (cost prefix before the slot `pre`, cost c) that start in [lo, hi).
-UOCR_DEV void slot_range(long long pre, long long c, int n, const Partition& p, int& j0, int& j1) {
-    long long a = p.lo - pre, b = p.hi - pre;
-    long long s0 = a <= 0 ? 0 : (a + c - 1) / c;
-    long long s1 = b <= 0 ? 0 : (b + c - 1) / c;
-    j0 = (int)(s0 < n ? s0 : n);
-    j1 = (int)(s1 < n ? s1 : n);
+// The second of two phases of equal-cost units (n0 of cost u0 already split by even_units, then
+// n1 of cost u1): CTA c's quota of the second phase is max(0, total / G - p0(c)) (p0 = its
+// first-phase cost); the quotas' prefix, scaled to n1, gives contiguous ranges (neighbours
+// evaluate the same expression on the same integer prefix). One warp.
+UOCR_DEV void routed_units(int n0, int u0, int n1, int u1, int lane, int& j0, int& j1) {
+    const int G = gridDim.x, me = blockIdx.x;
+    const int T = n0 * u0 + n1 * u1;
+    auto quota = [&](int c) {
+        int a0, a1;
+        even_units(n0, c, G, a0, a1);
+        return max(0, T - G * (a1 - a0) * u0);
+    };
+    long long before = 0, total = 0;
+    for (int c = lane; c < G; c += 32) {
+        const int q = quota(c);
+        total += q;
+        if (c < me) before += q;
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+        total += __shfl_xor_sync(0xffffffffu, total, off);
+        before += __shfl_xor_sync(0xffffffffu, before, off);
+    }
+    auto bound = [&](long long pre) { return total > 0 ? (int)((double)n1 * (double)pre / (double)total) : 0; };
+    j0 = bound(before);
+    j1 = me == G - 1 ? n1 : bound(before + quota(me));
 }
 
 // ======================================================================================
@@ -463,10 +479,10 @@ struct Pipe {
     uint32_t* status;
 };
 
-// MMA warp: take the next accumulator slot (waiting until the epilogue has read it), publish
-// its description; returns its index, or -1 on a timeout. `scl` (int8) = the 128 row scales,
-// `sig` (K3 int8) = the group's 8 column scales.
-UOCR_DEV int acquire_acc(Pipe& p, int slot, int rb, int gi, int flags, const float* scl, const float* sig, int lane) {
+// MMA warp: take the next accumulator slot (waiting until the epilogue has read it) and write
+// its description; returns its index, or -1 on a timeout. publish_acc makes the description
+// visible (the first of tfull's two arrivals; the MMAs' commit is the second).
+UOCR_DEV int acquire_acc(Pipe& p, int slot, int rb, int gi, int flags, int lane) {
     const int j = p.c % kAccSlots;
     if (p.c >= kAccSlots && !mbar_wait_warp(&p.tfree[j], ((p.c / kAccSlots) - 1) & 1, p.abort_flag, p.status))
         return -1;
@@ -477,22 +493,27 @@ UOCR_DEV int acquire_acc(Pipe& p, int slot, int rb, int gi, int flags, const flo
         m.gi = gi;
         m.flags = flags;
     }
-    if (scl)
-        for (int i = lane; i < kRowBlock; i += 32) m.scl[i] = scl[i];
-    if (sig && lane < kMaxB) m.sig[lane] = sig[lane];
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&p.tfull[j]);  // the description (release); the MMAs' commit is the second arrival
-    tc_fence_after();                          // the epilogue's TMEM reads precede this warp's next MMAs
+    tc_fence_after();  // the epilogue's TMEM reads precede this warp's next MMAs
     ++p.c;
     return j;
+}
+// int8 scales of one group into the description: 128 row scales (one float4 per lane) and,
+// for K3, the 8 column scales.
+UOCR_DEV void acc_scales(Pipe& p, int j, int g, const float* scl, const float* sig, int lane) {
+    reinterpret_cast<float4*>(p.acc[j].scl[g])[lane] = reinterpret_cast<const float4*>(scl)[lane];
+    if (sig && lane < kMaxB) p.acc[j].sig[g][lane] = sig[lane];
+}
+UOCR_DEV void publish_acc(Pipe& p, int j, int lane) {
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&p.tfull[j]);  // release: the description above
 }
 
 // Epilogue warp (TMEM lane quarter q = warp % 4, row = 32 q + lane): waits for accumulator c,
 // reads it and its description; returns false at the end of the work or on a timeout.
 struct AccRead {
     int slot, rb, gi, flags;
-    float scl, sig[kMaxB];
-    uint32_t v[32];
+    float scl[2], sig[2][kMaxB];
+    uint32_t v[2][32];
 };
 UOCR_DEV bool read_acc(Pipe& p, int c, int q, int lane, bool want_sig, AccRead& r) {
     const int j = c % kAccSlots;
@@ -503,13 +524,20 @@ UOCR_DEV bool read_acc(Pipe& p, int c, int q, int lane, bool want_sig, AccRead& 
     r.rb = m.rb;
     r.gi = m.gi;
     r.flags = m.flags;
-    r.scl = (r.flags & 1) ? m.scl[32 * q + lane] : 0.0f;
-    if (want_sig) {
-#pragma unroll
-        for (int t = 0; t < kMaxB; ++t) r.sig[t] = m.sig[t];
-    }
+    const int ng = (r.flags & 4) ? 2 : 1;
     tc_fence_after();
-    tmem_ld_32x32b_x32(p.tmem + ((uint32_t)(32 * q) << 16) + 32u * j, r.v);
+    const uint32_t taddr = p.tmem + ((uint32_t)(32 * q) << 16) + kAccCols * j;
+    tmem_ld_32x32b_x32(taddr, r.v[0]);
+    if (ng == 2) tmem_ld_32x32b_x32(taddr + 32, r.v[1]);
+    if (r.flags & 1) {
+        for (int g = 0; g < ng; ++g) {
+            r.scl[g] = m.scl[g][32 * q + lane];
+            if (want_sig) {
+#pragma unroll
+                for (int t = 0; t < kMaxB; ++t) r.sig[g][t] = m.sig[g][t];
+            }
+        }
+    }
     tmem_wait_ld();
     tc_fence_before();
     __syncwarp();
@@ -517,29 +545,24 @@ UOCR_DEV bool read_acc(Pipe& p, int c, int q, int lane, bool want_sig, AccRead& 
     return true;
 }
 
-// int8 accumulator -> acc[t] += undigit(planes) * (row scale * column scale), fixed order
-UOCR_DEV void fold_s8(const AccRead& r, const float* colsig, float (&acc)[kMaxB]) {
+// int8 group g of an accumulator -> acc[t] += undigit(planes) * (row scale * column scale)
+UOCR_DEV void fold_s8(const AccRead& r, int g, const float* colsig, float (&acc)[kMaxB]) {
 #pragma unroll
     for (int t = 0; t < kMaxB; ++t)
-        acc[t] = __fmaf_rn(undigit((int)r.v[t], (int)r.v[8 + t], (int)r.v[16 + t]), __fmul_rn(r.scl, colsig[t]),
-                           acc[t]);
+        acc[t] = __fmaf_rn(undigit((int)r.v[g][t], (int)r.v[g][8 + t], (int)r.v[g][16 + t]),
+                           __fmul_rn(r.scl[g], colsig[t]), acc[t]);
 }
 // bf16 accumulator (the whole row block): acc[t] = term-0 column + term-1 column
 UOCR_DEV void fold_bf16(const AccRead& r, float (&acc)[kMaxB]) {
 #pragma unroll
-    for (int t = 0; t < kMaxB; ++t) acc[t] = __fadd_rn(__uint_as_float(r.v[t]), __uint_as_float(r.v[8 + t]));
+    for (int t = 0; t < kMaxB; ++t) acc[t] = __fadd_rn(__uint_as_float(r.v[0][t]), __uint_as_float(r.v[0][8 + t]));
 }
 
 // ======================================================================================
 // K2: route + gate/up + SwiGLU
 // ======================================================================================
-// Units (slot, row block): w13_items(H) items of 2 atoms each. Shared slots first (streamed
-// while the CTA routes), then the routed slots.
-UOCR_DEV long long gu_unit_cost(const DecodeArgs& a, int slot) {
-    const bool i8 = slot >= a.S && a.int8;
-    return (long long)w13_items(a.H, i8) * (long long)w13_item_bytes(i8);
-}
-
+// Units (slot, row block of 64 gate|up pairs): w13_items(H) items of 2 atoms each. Shared slots
+// first (streamed while the CTA routes), then the routed slots.
 __global__ void __launch_bounds__(kThreads, 1)
 decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl, uint32_t off_route,
                       uint32_t off_meta, uint32_t off_acc, uint32_t off_xd, uint32_t off_xb, uint32_t off_sig,
@@ -632,24 +655,22 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             ++n;
             if (++st == nst) { st = 0; ++round; }
         };
-        for (int phase = 0; phase < 2 && ok; ++phase) {
-            if (phase == 1) wait_table();
-            if (!ok) break;
-            const int first = phase == 0 ? 0 : a.S;
-            const int last = phase == 0 ? a.S : tb->nslot;
-            auto units = [&](int) { return a.I / 64; };
-            auto cost = [&](int s) { return gu_unit_cost(a, s); };
-            const Partition p = cta_share(first, last, cost, units);
-            long long pre = 0;
-            for (int s = first; s < last && ok; ++s) {
-                const long long c = cost(s);
-                int j0, j1;
-                slot_range(pre, c, units(s), p, j0, j1);
-                const int nk = w13_items(a.H, s >= a.S && a.int8);
-                for (int rb = j0; rb < j1 && ok; ++rb)
-                    for (int ki = 0; ki < nk && ok; ++ki) issue(s, rb, ki);
-                pre += (long long)units(s) * c;
-            }
+        // units (slot, row block of 64 pairs): the shared experts' first (streamed while the
+        // CTA routes), then the routed ones, balanced against each CTA's shared share
+        const int per = a.I / 64;
+        auto issue_units = [&](int slot0, int j0, int j1, bool i8) {
+            const int nk = w13_items(a.H, i8);
+            for (int j = j0; j < j1 && ok; ++j)
+                for (int ki = 0; ki < nk && ok; ++ki) issue(slot0 + j / per, j % per, ki);
+        };
+        auto unit_cost = [&](bool i8) { return (int)((size_t)w13_items(a.H, i8) * w13_item_bytes(i8) / 512); };
+        int j0, j1;
+        even_units(a.S * per, blockIdx.x, gridDim.x, j0, j1);
+        issue_units(0, j0, j1, false);
+        wait_table();
+        if (ok) {
+            routed_units(a.S * per, unit_cost(false), (tb->nslot - a.S) * per, unit_cost(a.int8 != 0), lane, j0, j1);
+            issue_units(a.S, j0, j1, a.int8 != 0);
         }
         if (lane == 0) {
             if (!ok) {
@@ -690,39 +711,42 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                 unsigned char* item = stages + (size_t)st * stage_bytes;
                 const uint32_t item_s = smem_addr(item);
                 if (i8) {
+                    // both groups of the item in one accumulator (columns 0-31, 32-63)
                     const float* scl = reinterpret_cast<const float*>(item + 2 * kAtomBytes);
-                    for (int g = 0; g < 2 && ok; ++g) {
-                        const int gi = ki * 2 + g;
-                        const int j = acquire_acc(pipe, slot, rb, gi, 1 | (ki == nk8 - 1 && g == 1 ? 2 : 0),
-                                                  scl + g * kRowBlock, nullptr, lane);
-                        if (j < 0) {
-                            ok = false;
-                            break;
-                        }
-                        if (lane == 0) {
+                    const int j = acquire_acc(pipe, slot, rb, 2 * ki, 1 | 4 | (ki == nk8 - 1 ? 2 : 0), lane);
+                    if (j < 0) {
+                        ok = false;
+                        break;
+                    }
+                    acc_scales(pipe, j, 0, scl, nullptr, lane);
+                    acc_scales(pipe, j, 1, scl + kRowBlock, nullptr, lane);
+                    publish_acc(pipe, j, lane);
+                    if (lane == 0) {
+#pragma unroll
+                        for (int g = 0; g < 2; ++g)
 #pragma unroll
                             for (int s = 0; s < 4; ++s)
-                                umma_i8(pipe.tmem + 32u * j, umma_desc_sw128(item_s + g * kAtomBytes + 32 * s),
-                                        umma_desc_sw128(xd_s + gi * kDigitAtomBytes + 32 * s), kIdescS8, s > 0);
-                            umma_commit(&tfull[j]);
-                        }
-                        __syncwarp();
+                                umma_i8(pipe.tmem + kAccCols * j + 32u * g,
+                                        umma_desc_sw128(item_s + g * kAtomBytes + 32 * s),
+                                        umma_desc_sw128(xd_s + (2 * ki + g) * kDigitAtomBytes + 32 * s), kIdescS8, s > 0);
+                        umma_commit(&tfull[j]);
                     }
-                    if (!ok) break;
+                    __syncwarp();
                 } else {
                     if (ki == 0) {
-                        cur = acquire_acc(pipe, slot, rb, 0, 2, nullptr, nullptr, lane);
+                        cur = acquire_acc(pipe, slot, rb, 0, 2, lane);
                         if (cur < 0) {
                             ok = false;
                             break;
                         }
+                        publish_acc(pipe, cur, lane);
                     }
                     if (lane == 0) {
 #pragma unroll
                         for (int at = 0; at < 2; ++at)
 #pragma unroll
                             for (int s = 0; s < 4; ++s)
-                                umma_f16(pipe.tmem + 32u * cur, umma_desc_sw128(item_s + at * kAtomBytes + 32 * s),
+                                umma_f16(pipe.tmem + kAccCols * cur, umma_desc_sw128(item_s + at * kAtomBytes + 32 * s),
                                          umma_desc_sw128(xb_s + (2 * ki + at) * kTermAtomBytes + 32 * s), kIdescBf16,
                                          (ki | at | s) != 0);
                         if (ki == nk16 - 1) umma_commit(&tfull[cur]);
@@ -737,8 +761,11 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                 __syncwarp();
             }
             if (ok) {
-                const int j = acquire_acc(pipe, -1, 0, 0, 0, nullptr, nullptr, lane);  // end marker
-                if (j >= 0 && lane == 0) mbar_arrive(&tfull[j]);
+                const int j = acquire_acc(pipe, -1, 0, 0, 0, lane);  // end marker
+                if (j >= 0) {
+                    publish_acc(pipe, j, lane);
+                    if (lane == 0) mbar_arrive(&tfull[j]);
+                }
             } else if (lane == 0) {
                 abort_flag = 1;
             }
@@ -757,10 +784,12 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                 AccRead r;
                 if (!read_acc(pipe, c, q, lane, false, r)) break;
                 if (r.flags & 1) {
-                    float colsig[kMaxB];
+                    for (int g = 0; g < ((r.flags & 4) ? 2 : 1); ++g) {
+                        float colsig[kMaxB];
 #pragma unroll
-                    for (int t = 0; t < kMaxB; ++t) colsig[t] = xsig[t * (a.H / 128) + r.gi];
-                    fold_s8(r, colsig, acc);
+                        for (int t = 0; t < kMaxB; ++t) colsig[t] = xsig[t * (a.H / 128) + r.gi + g];
+                        fold_s8(r, g, colsig, acc);
+                    }
                 } else {
                     fold_bf16(r, acc);
                 }
@@ -820,14 +849,9 @@ UOCR_DEV void combine_slice(const DecodeArgs& a, const int (&trow)[kMaxB][kDecod
     }
 }
 
-// Units (slot, row block of 128 output rows): w2_items(I) items.
-UOCR_DEV long long dn_unit_cost(const DecodeArgs& a, int slot) {
-    const bool i8 = slot >= a.S && a.int8;
-    return (long long)w2_items(a.I, i8) * (long long)w2_item_bytes(i8);
-}
-
-// A slot run's operand image (int8 [I/128 groups][32 rows][128 B] or bf16 [I/64 atoms][16 rows]
-// [128 B], both I * 32 bytes) is double-buffered: run r uses buffer r % 2.
+// Units (slot, row block of 128 output rows): w2_items(I) items. A slot run's operand image
+// (int8 [I/128 groups][32 rows][128 B] or bf16 [I/64 atoms][16 rows][128 B], both I * 32
+// bytes) is double-buffered: run r uses buffer r % 2.
 __global__ void __launch_bounds__(kThreads, 1)
 decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t off_meta, uint32_t off_acc,
                    uint32_t off_hb, uint32_t off_hsig, uint32_t off_ring) {
@@ -842,7 +866,7 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
     uint64_t* tfull = empty + kK3Desc;     // [kAccSlots]
     uint64_t* tfree = tfull + kAccSlots;   // [kAccSlots]
     uint64_t* hload = tfree + kAccSlots;   // [2]: a run's first item is issued (producer)
-    uint64_t* hready = hload + 2;          // [2]: the run's operand image is staged (3 stager warps)
+    uint64_t* hready = hload + 2;          // [2]: the run's operand image is staged (7 arrivals)
     uint64_t* bfree = hready + 2;          // [2]: the MMAs reading the image are complete
     uint64_t* mdone = bfree + 2;
     SlotTable* tb = reinterpret_cast<SlotTable*>(smem + off_tbl);
@@ -872,7 +896,7 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&hload[b], 1);
-            mbar_init(&hready[b], 3);
+            mbar_init(&hready[b], 7);
             mbar_init(&bfree[b], 1);
         }
         mbar_init(mdone, 1);
@@ -901,89 +925,93 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
         pdl_wait_prior_grid();  // h and the routing table come from K2
         if (ev && lane == 0) ev[1] = global_timer_ns();
         load_routed_slots(tb, a, lane);
-        auto units = [&](int) { return a.H / kRowBlock; };
-        auto cost = [&](int s) { return dn_unit_cost(a, s); };
-        const Partition p = cta_share(0, tb->nslot, cost, units);
-        long long pre = 0;
-        for (int slot = 0; slot < tb->nslot && ok; ++slot) {
-            const long long c = cost(slot);
-            int j0, j1;
-            slot_range(pre, c, units(slot), p, j0, j1);
-            pre += (long long)units(slot) * c;
+        if (ev && lane == 0) ev[4] = global_timer_ns();
+        // units (slot, row block of 128 rows): the shared experts' split evenly, then the routed
+        // ones balanced against each CTA's shared share
+        const int nrb = a.H / kRowBlock;
+        auto unit_cost = [&](bool i8) { return (int)(w2_rb_bytes(a.I, i8) / 512); };
+        int s0, s1, r0, r1;
+        even_units(a.S * nrb, blockIdx.x, gridDim.x, s0, s1);
+        routed_units(a.S * nrb, unit_cost(false), (tb->nslot - a.S) * nrb, unit_cost(a.int8 != 0), lane, r0, r1);
+        if (ev && lane == 0) ev[5] = global_timer_ns();
+        int prev_slot = -1;
+        auto issue_unit = [&](int slot, int rb) {
             const bool i8 = slot >= a.S && a.int8;
             const int nk = w2_items(a.I, i8);
-            const uint32_t wbytes = (uint32_t)w2_item_bytes(i8);
-            const uint32_t hoff = (wbytes + 15u) & ~15u;
-            for (int rb = j0; rb < j1 && ok; ++rb) {
-                for (int ki = 0; ki < nk && ok; ++ki) {
-                    const bool run_start = rb == j0 && ki == 0;
-                    const uint32_t hbytes = run_start ? (uint32_t)tb->count[slot] * a.I * 4 : 0u;
-                    const uint32_t need = hoff + hbytes;
-                    if (run_start && runs >= 2 &&
-                        !mbar_wait_warp(&hready[runs & 1], ((runs - 2) >> 1) & 1, &abort_flag, &a.ctl->status)) {
+            const bool new_run = slot != prev_slot;
+            prev_slot = slot;
+            for (int ki = 0; ki < nk && ok; ++ki) {
+                const uint32_t wbytes = (uint32_t)item_bytes(w2_item_atoms(a.I, i8, ki), i8);
+                const uint32_t hoff = (wbytes + 15u) & ~15u;
+                const bool run_start = new_run && ki == 0;
+                const uint32_t hbytes = run_start ? (uint32_t)tb->count[slot] * a.I * 4 : 0u;
+                const uint32_t need = hoff + hbytes;
+                if (run_start && runs >= 2 &&
+                    !mbar_wait_warp(&hready[runs & 1], ((runs - 2) >> 1) & 1, &abort_flag, &a.ctl->status)) {
+                    ok = false;
+                    break;
+                }
+                head = (head + 1023u) & ~1023u;
+                if (head + need > ring_bytes) head = 0;
+                // retire ring bytes until this item's do not overlap any still being read
+                while (oldest < n) {
+                    bool clash = false;
+                    for (int m = oldest; m < n && !clash; ++m) {
+                        const int d = m % kK3Desc;
+                        clash = head < hi_b[d] && lo_b[d] < head + need;
+                    }
+                    if (!clash) break;
+                    if (!mbar_wait_warp(&freed[oldest % kK3Desc], (oldest / kK3Desc) & 1, &abort_flag,
+                                        &a.ctl->status)) {
                         ok = false;
                         break;
                     }
-                    head = (head + 1023u) & ~1023u;
-                    if (head + need > ring_bytes) head = 0;
-                    // retire ring bytes until this item's do not overlap any still being read
-                    while (oldest < n) {
-                        bool clash = false;
-                        for (int m = oldest; m < n && !clash; ++m) {
-                            const int d = m % kK3Desc;
-                            clash = head < hi_b[d] && lo_b[d] < head + need;
-                        }
-                        if (!clash) break;
-                        if (!mbar_wait_warp(&freed[oldest % kK3Desc], (oldest / kK3Desc) & 1, &abort_flag,
-                                            &a.ctl->status)) {
-                            ok = false;
-                            break;
-                        }
-                        ++oldest;
-                    }
-                    // and the descriptor: item n reuses item n - kK3Desc's
-                    while (ok && n - oldest_desc >= kK3Desc) {
-                        if (!mbar_wait_warp(&empty[oldest_desc % kK3Desc], (oldest_desc / kK3Desc) & 1, &abort_flag,
-                                            &a.ctl->status))
-                            ok = false;
-                        ++oldest_desc;
-                    }
-                    // a retired descriptor's bytes were freed before it: never wait on that `freed`
-                    // phase again (its barrier may complete again for a later item)
-                    oldest = max(oldest, oldest_desc);
-                    if (!ok) break;
-                    const int d = n % kK3Desc;
-                    lo_b[d] = head;
-                    hi_b[d] = head + need;
-                    if (lane == 0) {
-                        const unsigned char* wsrc =
-                            slot < a.S ? reinterpret_cast<const unsigned char*>(a.w2_shared) +
-                                             (size_t)tb->expert[slot] * w2_expert_bytes(a.H, a.I, false)
-                                       : reinterpret_cast<const unsigned char*>(a.w2) +
-                                             (size_t)tb->expert[slot] * w2_expert_bytes(a.H, a.I, i8);
-                        wsrc += ((size_t)rb * nk + ki) * wbytes;
-                        meta[d].slot = slot;
-                        meta[d].rb = rb;
-                        meta[d].ki = ki;
-                        meta[d].off = head;
-                        meta[d].hoff = hbytes ? hoff : 0u;
-                        mbar_arrive_expect_tx(&full[d], wbytes + hbytes);
-                        bulk_g2s(ring + head, wsrc, wbytes, &full[d]);
-                        if (hbytes) {
-                            bulk_g2s(ring + head + hoff, a.h + (size_t)tb->base[slot] * a.I, hbytes, &full[d]);
-                            hdesc[runs & 1] = n;
-                            mbar_arrive(&hload[runs & 1]);
-                        }
-                        unsigned long long* tr = trace_rec(a, 1, n);
-                        if (tr) tr[4] = global_timer_ns();
-                    }
-                    __syncwarp();
-                    if (hbytes) ++runs;
-                    head += need;
-                    ++n;
+                    ++oldest;
                 }
+                // and the descriptor: item n reuses item n - kK3Desc's
+                while (ok && n - oldest_desc >= kK3Desc) {
+                    if (!mbar_wait_warp(&empty[oldest_desc % kK3Desc], (oldest_desc / kK3Desc) & 1, &abort_flag,
+                                        &a.ctl->status))
+                        ok = false;
+                    ++oldest_desc;
+                }
+                // a retired descriptor's bytes were freed before it: never wait on that `freed`
+                // phase again (its barrier may complete again for a later item)
+                oldest = max(oldest, oldest_desc);
+                if (!ok) break;
+                const int d = n % kK3Desc;
+                lo_b[d] = head;
+                hi_b[d] = head + need;
+                if (lane == 0) {
+                    const unsigned char* wsrc =
+                        slot < a.S ? reinterpret_cast<const unsigned char*>(a.w2_shared) +
+                                         (size_t)tb->expert[slot] * w2_expert_bytes(a.H, a.I, false)
+                                   : reinterpret_cast<const unsigned char*>(a.w2) +
+                                         (size_t)tb->expert[slot] * w2_expert_bytes(a.H, a.I, i8);
+                    wsrc += (size_t)rb * w2_rb_bytes(a.I, i8) + w2_item_offset(i8, ki);
+                    meta[d].slot = slot;
+                    meta[d].rb = rb;
+                    meta[d].ki = ki;
+                    meta[d].off = head;
+                    meta[d].hoff = hbytes ? hoff : 0u;
+                    mbar_arrive_expect_tx(&full[d], wbytes + hbytes);
+                    bulk_g2s(ring + head, wsrc, wbytes, &full[d]);
+                    if (hbytes) {
+                        bulk_g2s(ring + head + hoff, a.h + (size_t)tb->base[slot] * a.I, hbytes, &full[d]);
+                        hdesc[runs & 1] = n;
+                        mbar_arrive(&hload[runs & 1]);
+                    }
+                    unsigned long long* tr = trace_rec(a, 1, n);
+                    if (tr) tr[4] = global_timer_ns();
+                }
+                __syncwarp();
+                if (hbytes) ++runs;
+                head += need;
+                ++n;
             }
-        }
+        };
+        for (int j = s0; j < s1 && ok; ++j) issue_unit(j / nrb, j % nrb);
+        for (int j = r0; j < r1 && ok; ++j) issue_unit(a.S + j / nrb, j % nrb);
         if (lane == 0) {
             if (ok) {
                 // end markers: the next descriptor once it is free, and the stagers' next run
@@ -1038,36 +1066,44 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
             unsigned char* item = ring + meta[d].off;
             const uint32_t item_s = smem_addr(item), img_s = hb_s + (uint32_t)b * img_bytes;
             if (i8) {
-                float sig[kMaxB];
-#pragma unroll
-                for (int t = 0; t < kMaxB; ++t) sig[t] = hsig[(b * kMaxB + t) * NG3 + ki];
-                const int j = acquire_acc(pipe, slot, rb, ki, 1 | (ki == nk - 1 ? 2 : 0),
-                                          reinterpret_cast<const float*>(item + kAtomBytes), sig, lane);
+                // the item's one or two groups in one accumulator (columns 0-31, 32-63)
+                const int at = w2_item_atoms(a.I, true, ki);
+                const int j = acquire_acc(pipe, slot, rb, 2 * ki, 1 | (at == 2 ? 4 : 0) | (ki == nk - 1 ? 2 : 0), lane);
                 if (j < 0) {
                     ok = false;
                     break;
                 }
-                if (lane == 0) {
+                const float* scl = reinterpret_cast<const float*>(item + at * kAtomBytes);
+                for (int g = 0; g < at; ++g) {
+                    float sig[kMaxB];
 #pragma unroll
-                    for (int s = 0; s < 4; ++s)
-                        umma_i8(pipe.tmem + 32u * j, umma_desc_sw128(item_s + 32 * s),
-                                umma_desc_sw128(img_s + ki * kDigitAtomBytes + 32 * s), kIdescS8, s > 0);
+                    for (int t = 0; t < kMaxB; ++t) sig[t] = hsig[(b * kMaxB + t) * NG3 + 2 * ki + g];
+                    acc_scales(pipe, j, g, scl + g * kRowBlock, sig, lane);
+                }
+                publish_acc(pipe, j, lane);
+                if (lane == 0) {
+                    for (int g = 0; g < at; ++g)
+#pragma unroll
+                        for (int s = 0; s < 4; ++s)
+                            umma_i8(pipe.tmem + kAccCols * j + 32u * g, umma_desc_sw128(item_s + g * kAtomBytes + 32 * s),
+                                    umma_desc_sw128(img_s + (2 * ki + g) * kDigitAtomBytes + 32 * s), kIdescS8, s > 0);
                     umma_commit(&tfull[j]);
                 }
             } else {
                 if (ki == 0) {
-                    cur = acquire_acc(pipe, slot, rb, 0, 2, nullptr, nullptr, lane);
+                    cur = acquire_acc(pipe, slot, rb, 0, 2, lane);
                     if (cur < 0) {
                         ok = false;
                         break;
                     }
+                    publish_acc(pipe, cur, lane);
                 }
                 if (lane == 0) {
 #pragma unroll
                     for (int at = 0; at < 2; ++at)
 #pragma unroll
                         for (int s = 0; s < 4; ++s)
-                            umma_f16(pipe.tmem + 32u * cur, umma_desc_sw128(item_s + at * kAtomBytes + 32 * s),
+                            umma_f16(pipe.tmem + kAccCols * cur, umma_desc_sw128(item_s + at * kAtomBytes + 32 * s),
                                      umma_desc_sw128(img_s + (2 * ki + at) * kTermAtomBytes + 32 * s), kIdescBf16,
                                      (ki | at | s) != 0);
                     if (ki == nk - 1) umma_commit(&tfull[cur]);
@@ -1084,8 +1120,11 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
             __syncwarp();
         }
         if (ok) {
-            const int j = acquire_acc(pipe, -1, 0, 0, 0, nullptr, nullptr, lane);  // end marker
-            if (j >= 0 && lane == 0) mbar_arrive(&tfull[j]);
+            const int j = acquire_acc(pipe, -1, 0, 0, 0, lane);  // end marker
+            if (j >= 0) {
+                publish_acc(pipe, j, lane);
+                if (lane == 0) mbar_arrive(&tfull[j]);
+            }
         } else if (lane == 0) {
             abort_flag = 1;
         }
@@ -1094,57 +1133,90 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
             mbar_wait(mdone, 0, &a.ctl->status);
         }
         __syncwarp();
-    } else if (warp <= 3) {
-        // ---------------- stagers: a run's h rows -> its operand image ----------------
-        for (int r = 0;; ++r) {
+    } else {
+        // ---------------- stagers (warps 1-3, and 4-7 for the first run) and epilogue (4-7) ----------------
+        // A run's h rows -> its operand image: `nw` warps (rank 0..nw-1) share the (entry, group)
+        // tasks; hready completes after 7 arrivals (3 stager warps add 4 from rank 0).
+        // diagnostics: runs 0 and 1 of stager rank 0 {hload, data, image free, staged}
+        unsigned long long* sv = a.trace ? trace_rec(a, 1, a.trace_items / 2 - 3) : nullptr;
+        auto stage = [&](int r, int nw, int rank) -> bool {
             const int b = r & 1;
-            if (!mbar_wait_warp(&hload[b], (r >> 1) & 1, &abort_flag, &a.ctl->status)) break;
+            unsigned long long* tv = sv && rank == 0 && lane == 0 && r < 2 ? sv + 4 * r : nullptr;
+            if (!mbar_wait_warp(&hload[b], (r >> 1) & 1, &abort_flag, &a.ctl->status)) return false;
+            if (tv) tv[0] = global_timer_ns();
             const int n = hdesc[b];
-            if (n < 0) break;
+            if (n < 0) return false;
             const int d = n % kK3Desc;
-            if (!mbar_wait_warp(&full[d], (n / kK3Desc) & 1, &abort_flag, &a.ctl->status)) break;
-            if (r >= 2 && !mbar_wait_warp(&bfree[b], ((r - 2) >> 1) & 1, &abort_flag, &a.ctl->status)) break;
+            if (!mbar_wait_warp(&full[d], (n / kK3Desc) & 1, &abort_flag, &a.ctl->status)) return false;
+            if (tv) tv[1] = global_timer_ns();
+            if (r >= 2 && !mbar_wait_warp(&bfree[b], ((r - 2) >> 1) & 1, &abort_flag, &a.ctl->status)) return false;
+            if (tv) tv[2] = global_timer_ns();
             const int slot = meta[d].slot, cnt = tb->count[slot];
             const bool i8 = slot >= a.S && a.int8;
             const float* h = reinterpret_cast<const float*>(ring + meta[d].off + meta[d].hoff);
             unsigned char* img = hb + (size_t)b * img_bytes;
-            for (int task = warp - 1; task < cnt * NG3; task += 3) {
-                const int e = task / NG3, g = task - e * NG3;
-                const float4 v = *reinterpret_cast<const float4*>(h + (size_t)e * a.I + 128 * g + 4 * lane);
-                if (i8) {
-                    uint32_t w[3];
-                    const float sg = group_digits(v, w);
-                    if (lane == 0) hsig[(b * kMaxB + e) * NG3 + g] = sg;
-                    put_digits(img, g, e, lane, w);
-                } else {
-                    put_terms(img, g, e, lane, v);
+            const int ntask = cnt * NG3;
+            for (int t0 = rank; t0 < ntask; t0 += 4 * nw) {
+                float4 v[4];  // four tasks' loads issued before any of their stores
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int task = t0 + u * nw;
+                    if (task < ntask) {
+                        const int e = task / NG3, g = task - e * NG3;
+                        v[u] = *reinterpret_cast<const float4*>(h + (size_t)e * a.I + 128 * g + 4 * lane);
+                    }
+                }
+#pragma unroll
+                for (int u = 0; u < 4; ++u) {
+                    const int task = t0 + u * nw;
+                    if (task < ntask) {
+                        const int e = task / NG3, g = task - e * NG3;
+                        if (i8) {
+                            uint32_t w[3];
+                            const float sg = group_digits(v[u], w);
+                            if (lane == 0) hsig[(b * kMaxB + e) * NG3 + g] = sg;
+                            put_digits(img, g, e, lane, w);
+                        } else {
+                            put_terms(img, g, e, lane, v[u]);
+                        }
+                    }
                 }
             }
             fence_proxy_async_smem();  // generic writes of the image, read next by the tensor cores
             __syncwarp();
-            if (lane == 0) mbar_arrive(&hready[b]);
-        }
-    } else {
-        // ---------------- epilogue ----------------
-        const int q = warp & 3, row = 32 * q + lane;
-        float acc[kMaxB];
+            if (lane == 0) mbar_arrive_cnt(&hready[b], nw == 3 && rank == 0 ? 5u : 1u);
+            if (tv) tv[3] = global_timer_ns();
+            return true;
+        };
+        bool more = stage(0, 7, warp - 1);
+        if (warp <= 3) {
+            for (int r = 1; more; ++r) more = stage(r, 3, warp - 1);
+        } else {
+            // ---------------- epilogue ----------------
+            const int q = warp & 3, row = 32 * q + lane;
+            float acc[kMaxB];
 #pragma unroll
-        for (int t = 0; t < kMaxB; ++t) acc[t] = 0.0f;
-        for (int c = 0;; ++c) {
-            AccRead r;
-            if (!read_acc(pipe, c, q, lane, true, r)) break;
-            if (r.flags & 1) fold_s8(r, r.sig, acc);
-            else fold_bf16(r, acc);
-            if (r.flags & 2) {
-                const int cnt = tb->count[r.slot], base = tb->base[r.slot];
+            for (int t = 0; t < kMaxB; ++t) acc[t] = 0.0f;
+            for (int c = 0;; ++c) {
+                AccRead r;
+                if (!read_acc(pipe, c, q, lane, true, r)) break;
+                if (r.flags & 1) {
+                    fold_s8(r, 0, r.sig[0], acc);
+                    if (r.flags & 4) fold_s8(r, 1, r.sig[1], acc);
+                } else {
+                    fold_bf16(r, acc);
+                }
+                if (r.flags & 2) {
+                    const int cnt = tb->count[r.slot], base = tb->base[r.slot];
 #pragma unroll
-                for (int t = 0; t < kMaxB; ++t) {
-                    if (t < cnt) a.y[(size_t)(base + t) * a.H + kRowBlock * r.rb + row] = acc[t];
-                    acc[t] = 0.0f;
+                    for (int t = 0; t < kMaxB; ++t) {
+                        if (t < cnt) a.y[(size_t)(base + t) * a.H + kRowBlock * r.rb + row] = acc[t];
+                        acc[t] = 0.0f;
+                    }
                 }
             }
+            if (ev && tid == 128) ev[2] = global_timer_ns();
         }
-        if (ev && tid == 128) ev[2] = global_timer_ns();
     }
     tc_fence_before();
     __syncthreads();
@@ -1248,7 +1320,8 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
         const size_t off_hb = up(off_hsig + sizeof(float) * 2 * kMaxB * (a.I / 128), 1024);
         const size_t off_ring = off_hb + 2 * (size_t)a.I * 32;
         const size_t max_item =
-            up(std::max(w2_item_bytes(false), a.int8 ? w2_item_bytes(true) : size_t(0)), 16) + (size_t)kMaxB * a.I * 4;
+            up(std::max(item_bytes(kW2Atoms, false), a.int8 ? item_bytes(kW2Atoms, true) : size_t(0)), 16) +
+            (size_t)kMaxB * a.I * 4;
         if ((size_t)max_smem < off_ring + max_item + 1024) return cudaErrorInvalidConfiguration;
         uint32_t ring_bytes = (uint32_t)(((size_t)max_smem - off_ring) & ~size_t(1023));
         const size_t smem = off_ring + ring_bytes;

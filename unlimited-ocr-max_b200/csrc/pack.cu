@@ -61,12 +61,12 @@ __global__ void pack_w2_kernel(const char* down, const float* ds, int H, int I, 
                                bool int8, char* out) {
     const int nk = w2_items(I, int8);
     const int rb = blockIdx.x / nk, ki = blockIdx.x - rb * nk, e = blockIdx.y;
-    const size_t ib = w2_item_bytes(int8);
-    char* dst = out + (size_t)e * w2_expert_bytes(H, I, int8) + ((size_t)rb * nk + ki) * ib;
+    char* dst = out + (size_t)e * w2_expert_bytes(H, I, int8) + (size_t)rb * w2_rb_bytes(I, int8) +
+                w2_item_offset(int8, ki);
     auto row_ptr = [&](int r) { return down + ((size_t)e * estride + (size_t)(kRowBlock * rb + r) * ld) * esz; };
     auto scale_ptr = [&](int r) { return ds + ((size_t)e * H + kRowBlock * rb + r) * (I / 128); };
-    const int atoms = w2_atoms(int8);
-    pack_item(dst, atoms, atom_k(int8), esz, ki * atoms * atom_k(int8), int8, row_ptr, scale_ptr);
+    pack_item(dst, w2_item_atoms(I, int8, ki), atom_k(int8), esz, ki * kW2Atoms * atom_k(int8), int8, row_ptr,
+              scale_ptr);
 }
 
 cudaError_t launch_pack_w2(const void* down, const float* ds, int E, int H, int I, bool int8, long estride, long ld,

@@ -174,10 +174,14 @@ __global__ void __launch_bounds__(256) prefill_dequant_kernel(const unsigned cha
     if (i >= nrb * per_rb) return;
     const long rb = i / per_rb;
     const int rem = (int)(i - rb * per_rb), r = rem / (K / 16), k = 16 * (rem - r * (K / 16));
+    // items of `atoms` atoms of 128 elements, the last one possibly shorter (layout.h)
     const int ik = atoms * 128, ki = k / ik, a = (k % ik) / 128, c = k % 128;
-    const unsigned char* item = w + ((size_t)rb * (K / ik) + ki) * item_bytes(atoms, true);
+    const int nitems = (K / 128 + atoms - 1) / atoms, left = K / 128 - ki * atoms;
+    const int here = left < atoms ? left : atoms;  // atoms of this item
+    const size_t rb_bytes = (size_t)(nitems - 1) * item_bytes(atoms, true) + item_bytes((K / 128) - (nitems - 1) * atoms, true);
+    const unsigned char* item = w + (size_t)rb * rb_bytes + (size_t)ki * item_bytes(atoms, true);
     const uint4 v = *reinterpret_cast<const uint4*>(item + (size_t)a * kAtomBytes + atom_offset(r, c));
-    const float sc = reinterpret_cast<const float*>(item + (size_t)atoms * kAtomBytes)[a * kRowBlock + r];
+    const float sc = reinterpret_cast<const float*>(item + (size_t)here * kAtomBytes)[a * kRowBlock + r];
     float f0[8], f1[8];
     unpack_s8x8(v.x, v.y, f0);
     unpack_s8x8(v.z, v.w, f1);
@@ -578,7 +582,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& 
         prefill_dequant_kernel<<<(unsigned)((n13 + 255) / 256), 256, 0, st>>>(
             reinterpret_cast<const unsigned char*>(a.w13), nrb13, H, w13_atoms(), w13d);
         prefill_dequant_kernel<<<(unsigned)((n2 + 255) / 256), 256, 0, st>>>(
-            reinterpret_cast<const unsigned char*>(a.w2), nrb2, I, w2_atoms(true), w2d);
+            reinterpret_cast<const unsigned char*>(a.w2), nrb2, I, kW2Atoms, w2d);
         w13 = w13d;
         w2 = w2d;
     }
