@@ -105,20 +105,16 @@ UOCR_DEV void load_shared_slots(SlotTable* tb, const DecodeArgs& a, int tid, int
     if (tid == 0) tb->nslot = a.S;
 }
 
-// The routed slots, from K2's table in global memory (K3, after the dependency wait; one warp).
+// The routed slots' experts and rows, from K2's table in global memory (K3, after the
+// dependency wait; one warp; the combine reads the table's per-token row lists itself).
 UOCR_DEV void load_routed_slots(SlotTable* tb, const DecodeArgs& a, int lane) {
     const RouteTable* g = a.table;
     const int U = __ldcg(&g->U);
     for (int u = lane; u < U; u += 32) {
-        const int row = a.S + u;
-        tb->expert[row] = __ldcg(&g->expert[u]);
-        tb->count[row] = __ldcg(&g->count[u]);
-        tb->base[row] = __ldcg(&g->base[u]);
-#pragma unroll
-        for (int q = 0; q < kMaxB; ++q) {
-            tb->token[row][q] = __ldcg(&g->token[u][q]);
-            tb->weight[row][q] = __ldcg(&g->weight[u][q]);
-        }
+        const int e = __ldcg(&g->expert[u]), n = __ldcg(&g->count[u]), b = __ldcg(&g->base[u]);
+        tb->expert[a.S + u] = e;
+        tb->count[a.S + u] = n;
+        tb->base[a.S + u] = b;
     }
     __syncwarp();
     if (lane == 0) tb->nslot = a.S + U;
@@ -351,29 +347,22 @@ UOCR_DEV void even_units(int n, int c, int G, int& j0, int& j1) {
 // The second of two phases of equal-cost units (n0 of cost u0 already split by even_units, then
 // n1 of cost u1): CTA c's quota of the second phase is max(0, total / G - p0(c)) (p0 = its
 // first-phase cost); the quotas' prefix, scaled to n1, gives contiguous ranges (neighbours
-// evaluate the same expression on the same integer prefix). One warp.
-UOCR_DEV void routed_units(int n0, int u0, int n1, int u1, int lane, int& j0, int& j1) {
-    const int G = gridDim.x, me = blockIdx.x;
-    const int T = n0 * u0 + n1 * u1;
-    auto quota = [&](int c) {
-        int a0, a1;
-        even_units(n0, c, G, a0, a1);
-        return max(0, T - G * (a1 - a0) * u0);
+// evaluate the same expression on the same integer prefix). A CTA's first-phase count is
+// floor(n0 / G) or one more, and the counts of CTAs [0, c) sum to ceil(n0 c / G), so the prefix
+// has a closed form.
+UOCR_DEV void routed_units(int n0, int u0, int n1, int u1, int& j0, int& j1) {
+    const int G = gridDim.x, c = blockIdx.x;
+    const long long T = (long long)n0 * u0 + (long long)n1 * u1;
+    const int lo = n0 / G;
+    const long long q_lo = max(0LL, T - (long long)G * u0 * lo), q_hi = max(0LL, T - (long long)G * u0 * (lo + 1));
+    auto before = [&](int cc) {  // quota of CTAs [0, cc)
+        const long long hi_cnt = (((long long)n0 * cc + G - 1) / G) - (long long)cc * lo;
+        return hi_cnt * q_hi + ((long long)cc - hi_cnt) * q_lo;
     };
-    long long before = 0, total = 0;
-    for (int c = lane; c < G; c += 32) {
-        const int q = quota(c);
-        total += q;
-        if (c < me) before += q;
-    }
-#pragma unroll
-    for (int off = 16; off >= 1; off >>= 1) {
-        total += __shfl_xor_sync(0xffffffffu, total, off);
-        before += __shfl_xor_sync(0xffffffffu, before, off);
-    }
+    const long long total = before(G);
     auto bound = [&](long long pre) { return total > 0 ? (int)((double)n1 * (double)pre / (double)total) : 0; };
-    j0 = bound(before);
-    j1 = me == G - 1 ? n1 : bound(before + quota(me));
+    j0 = bound(before(c));
+    j1 = c == G - 1 ? n1 : bound(before(c + 1));
 }
 
 // ======================================================================================
@@ -669,7 +658,7 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
         issue_units(0, j0, j1, false);
         wait_table();
         if (ok) {
-            routed_units(a.S * per, unit_cost(false), (tb->nslot - a.S) * per, unit_cost(a.int8 != 0), lane, j0, j1);
+            routed_units(a.S * per, unit_cost(false), (tb->nslot - a.S) * per, unit_cost(a.int8 != 0), j0, j1);
             issue_units(a.S, j0, j1, a.int8 != 0);
         }
         if (lane == 0) {
@@ -932,7 +921,7 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
         auto unit_cost = [&](bool i8) { return (int)(w2_rb_bytes(a.I, i8) / 512); };
         int s0, s1, r0, r1;
         even_units(a.S * nrb, blockIdx.x, gridDim.x, s0, s1);
-        routed_units(a.S * nrb, unit_cost(false), (tb->nslot - a.S) * nrb, unit_cost(a.int8 != 0), lane, r0, r1);
+        routed_units(a.S * nrb, unit_cost(false), (tb->nslot - a.S) * nrb, unit_cost(a.int8 != 0), r0, r1);
         if (ev && lane == 0) ev[5] = global_timer_ns();
         int prev_slot = -1;
         auto issue_unit = [&](int slot, int rb) {
