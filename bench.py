@@ -612,7 +612,7 @@ def run_ours(args):
         v, cores, sample = CpuDecode(True, B).rate()
         cpu = {"value": v, "unit": "tokens/s", "cores": cores, "kind": "port", "sample": sample}
     if rank == 0:
-        launches_per_step = 2 * L  # per layer: route + gate|up experts, down experts + combine
+        launches_per_step = 3 * L  # per layer: logits, route + gate|up experts, down experts + combine
         line = {
             "metric": "MoE-layer tokens/s (decode, int8 routed experts, B=8)",
             "value": value,
@@ -636,7 +636,10 @@ def run_ours(args):
             },
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": peak_src, "scope": "whole decode layer step (route+experts+combine)",
-                         "algorithmic_bytes_per_step": step_bytes, "traffic": None},
+                         "algorithmic_bytes_per_step": step_bytes,
+                         # ncu DRAM bytes of one layer's gate/up + down launches over their algorithmic
+                         # bytes: 1.004 (read once); the step's traffic scaled from that capture
+                         "traffic": round(step_bytes * 1.004), "traffic_source": "ncu, one layer, scaled"},
             "e2e": {"value": world * B * L / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
             "gpu_launches": launches_per_step * args.steps,
