@@ -57,6 +57,9 @@ def parse():
                         "prefill: configs[2] bf16 prefill of 4096 tokens; "
                         "ep: configs[4] expert-parallel prefill of --ep-tokens over the ranks")
     p.add_argument("--ep-tokens", type=int, default=65536, help="EP prefill tokens over all ranks (configs[4])")
+    p.add_argument("--ep-placement", choices=["balanced", "contiguous"], default="balanced",
+                   help="EP expert->rank map: balanced from the routed loads of a calibration batch (another "
+                        "seed of the same distribution), or contiguous ranges")
     p.add_argument("--tokens", type=int, default=4096, help="prefill tokens (configs[2]: 4096)")
     return p.parse_args()
 
@@ -471,7 +474,9 @@ def run_prefill(args, torch, uocr, synth, dist, world, rank, device):
 
 def run_ep(args, torch, uocr, synth, dist, world, rank, device):
     """bf16 MoE over --ep-tokens tokens split evenly over the ranks, routed experts
-    sharded (64 / N per GPU), Zipf(1.1) expert bias, NCCL all-to-all dispatch / combine."""
+    sharded (64 / N per GPU), Zipf(1.1) expert bias, NCCL all-to-all dispatch / combine. The
+    expert->rank map is balanced on the routed loads of a calibration batch drawn from another
+    seed (the measured batch is not seen), unless --ep-placement contiguous."""
     ep_mod = importlib.import_module(f"{PKG}.ep")
     T_all = args.ep_tokens
     if T_all % world:
@@ -479,9 +484,19 @@ def run_ep(args, torch, uocr, synth, dist, world, rank, device):
     T = T_all // world
     cfg = uocr.MoEConfig()
     st = synth.layer_state(cfg, 5000, device=device)
-    moe = ep_mod.ExpertParallelMoE(cfg, device=device).load_state_dict(st)
+    bias = synth.skew_bias(E, 5001, zipf_s=1.1, device=device)
+    placement = None
+    if args.ep_placement == "balanced":
+        xc = synth.hidden_states(T_all, H, 5003, device=device)[rank * T:(rank + 1) * T].contiguous()
+        router = st["gate.gate_score.weight"].to(device, torch.bfloat16).contiguous()
+        ids_c, _ = uocr.ops.route(xc, router, bias, TOPK)
+        calib = torch.bincount(ids_c.flatten().long(), minlength=E).to(torch.int64)
+        dist.all_reduce(calib)
+        placement = ep_mod.balanced_placement(calib.cpu(), world)
+        del xc, ids_c
+    moe = ep_mod.ExpertParallelMoE(cfg, device=device, placement=placement).load_state_dict(st)
     del st
-    moe.bias = synth.skew_bias(E, 5001, zipf_s=1.1, device=device)
+    moe.bias = bias
     x = synth.hidden_states(T_all, H, 5002, device=device)[rank * T:(rank + 1) * T].contiguous()
     torch.cuda.empty_cache()
     for _ in range(max(args.warmup, 3)):
@@ -504,7 +519,7 @@ def run_ep(args, torch, uocr, synth, dist, world, rank, device):
     ms = float(t.item())
     # per-rank expert load and exchanged bytes of one step
     ids, wts = moe._route(x)
-    plan = ep_mod.plan_dispatch(ids, wts, world, moe.e_local)
+    plan = ep_mod.plan_dispatch(ids, wts, world, moe.placement)
     sent = torch.tensor([sum(plan.send_counts) - plan.send_counts[rank]], dtype=torch.int64, device=device)
     load = torch.bincount(ids.flatten().long(), minlength=E).to(torch.int64)
     dist.all_reduce(sent)
@@ -513,7 +528,7 @@ def run_ep(args, torch, uocr, synth, dist, world, rank, device):
     tc, tc_src = measured_tc_peak()
     flop = PREFILL_FLOP_PER_TOKEN * T_all
     tflops = flop / (ms * 1e-3) / 1e12
-    per_rank = load.view(world, -1).sum(1).tolist()
+    per_rank = [int(load[ex].sum()) for ex in moe.placement.experts]
     if rank != 0:
         return
     remote_rows = int(sent.item())
@@ -526,7 +541,7 @@ def run_ep(args, torch, uocr, synth, dist, world, rank, device):
         "config": {"workload": f"configs[4] expert-parallel prefill, {T_all} tokens over {world} GPU(s)",
                    "tokens_per_rank": T, "experts_per_rank": moe.e_local, "hidden": H, "moe_intermediate": I,
                    "top_k": TOPK, "shared": S, "parallelism": f"ep{world} (routed experts) x dp{world} (tokens, shared)",
-                   "expert_rows_per_rank": per_rank,
+                   "expert_placement": args.ep_placement, "expert_rows_per_rank": per_rank,
                    "remote_rows": remote_rows,
                    "all_to_all_bytes_per_step": remote_rows * (H * 2 + 2 * TOPK * 4) + remote_rows * H * 4},
         "roofline": {"bound": "tensor", "achieved": tflops / world, "peak": tc, "unit": "TFLOP/s per GPU",

@@ -39,13 +39,21 @@ def _setup():
     return o, cfg, w, x
 
 
-def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
+def _placement(ep, world: int, kind: str):
+    if kind == "contiguous":
+        return E // world
+    # balanced from a skewed histogram: the hot experts 0 and 1 land on different ranks
+    return ep.balanced_placement([90, 80, 10, 10, 5, 5, 1, 1], world)
+
+
+def _worker(rank: int, world: int, port: int, out_dir: str, kind: str) -> None:
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
     dist.init_process_group("gloo", rank=rank, world_size=world)
     try:
         ep = importlib.import_module("unlimited-ocr-max_b200.ep")
         o, cfg, w, x = _setup()
-        e_local = E // world
+        placement = _placement(ep, world, kind)
+        experts = ep.contiguous_placement(E, world).experts if kind == "contiguous" else placement.experts
         t_local = T_TOTAL // world
         xl = torch.from_numpy(x[rank * t_local:(rank + 1) * t_local].copy())
         st = {n: o.bf16_to_f32(getattr(w, n)).astype(np.float64) for n in ("gate", "up", "down")}
@@ -64,7 +72,7 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
                     e = int(meta_e[n, s])
                     if e < 0:
                         continue
-                    g = rank * e_local + e
+                    g = experts[rank][e]
                     hcol = silu(st["gate"][g] @ xr[n]) * (st["up"][g] @ xr[n])
                     out[n] += float(meta_w[n, s]) * (st["down"][g] @ hcol)
             return torch.from_numpy(out.astype(np.float32))
@@ -73,7 +81,7 @@ def _worker(rank: int, world: int, port: int, out_dir: str) -> None:
             xf = xt.numpy().astype(np.float64)
             out += torch.from_numpy(((silu(xf @ sg.T) * (xf @ su.T)) @ sd.T).astype(np.float32))
 
-        got = ep.ep_forward(xl, route, local_experts, shared, world, e_local)
+        got = ep.ep_forward(xl, route, local_experts, shared, world, placement)
         np.save(os.path.join(out_dir, f"rank{rank}.npy"), got.numpy())
     finally:
         dist.destroy_process_group()
@@ -93,9 +101,36 @@ def test_plan_dispatch_rows_and_metadata():
     assert one.send_counts == [1, 0]
 
 
-def test_ep_forward_two_gloo_ranks(tmp_path):
+def test_balanced_placement():
+    ep = importlib.import_module("unlimited-ocr-max_b200.ep")
+    pl = ep.balanced_placement([90, 80, 10, 10, 5, 5, 1, 1], 2)
+    assert pl.experts == [[0, 3, 6, 7], [1, 2, 4, 5]]  # loads 102 and 100
+    owner, local = pl.owner_local()
+    assert owner.tolist() == [0, 1, 1, 0, 1, 1, 0, 0] and local.tolist() == [0, 0, 1, 1, 2, 3, 2, 3]
+    # Zipf-skewed loads over 64 experts on 4 ranks: expert 0 alone exceeds the mean rank load,
+    # so the best any placement can do is expert 0 plus the 15 lightest; the greedy rule gets
+    # that, where contiguous ranges put the whole head on rank 0
+    load = [int(1e6 / (e + 1) ** 1.1) for e in range(64)]
+    worst = max(sum(load[e] for e in v) for v in ep.balanced_placement(load, 4).experts)
+    assert worst == load[0] + sum(sorted(load)[:15])
+    assert max(sum(load[16 * p:16 * p + 16]) for p in range(4)) > 2 * worst
+    with pytest.raises(ValueError):
+        ep.balanced_placement([1] * 7, 2)
+
+
+def test_plan_dispatch_with_placement():
+    ep = importlib.import_module("unlimited-ocr-max_b200.ep")
+    pl = ep.ExpertPlacement([[0, 2, 4, 6], [1, 3, 5, 7]])
+    ids = torch.tensor([[0, 5, 1, 7, 2, 3]], dtype=torch.int32)
+    plan = ep.plan_dispatch(ids, torch.ones(1, 6), 2, pl)
+    assert plan.send_counts == [1, 1]
+    assert plan.meta_expert.tolist() == [[0, -1, -1, -1, 1, -1], [-1, 2, 0, 3, -1, 1]]
+
+
+@pytest.mark.parametrize("kind", ["contiguous", "balanced"])
+def test_ep_forward_two_gloo_ranks(tmp_path, kind):
     world = 2
-    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path)), nprocs=world, join=True)
+    mp.spawn(_worker, args=(world, _free_port(), str(tmp_path), kind), nprocs=world, join=True)
     got = np.concatenate([np.load(tmp_path / f"rank{r}.npy") for r in range(world)])
     o, cfg, w, x = _setup()
     r = o.route_fp32(x, w.router, None, K)

@@ -100,7 +100,7 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _ep_worker(rank: int, world: int, port: int, T: int, out_dir: str) -> None:
+def _ep_worker(rank: int, world: int, port: int, T: int, out_dir: str, kind: str) -> None:
     import sys
 
     sys.path.insert(0, str(ROOT))
@@ -114,7 +114,11 @@ def _ep_worker(rank: int, world: int, port: int, T: int, out_dir: str) -> None:
         uocr = importlib.import_module("unlimited-ocr-max_b200")
         ep = importlib.import_module("unlimited-ocr-max_b200.ep")
         cfg, w = full_layer(o, False, 4)
-        m = ep.ExpertParallelMoE(uocr.MoEConfig(), device=f"cuda:{rank}").load_state_dict(to_state(w, cfg, False))
+        placement = None
+        if kind == "strided":  # every world-th expert, in descending order: local != global index
+            placement = ep.ExpertPlacement([list(range(63 - p, -1, -world)) for p in range(world)])
+        m = ep.ExpertParallelMoE(uocr.MoEConfig(), device=f"cuda:{rank}", placement=placement)
+        m.load_state_dict(to_state(w, cfg, False))
         bias = np.random.default_rng(8).standard_normal(64).astype(np.float32)
         m.bias = torch.from_numpy(bias).to(f"cuda:{rank}")
         x = o.synth_hidden(T * world, cfg.hidden, 9)[rank * T:(rank + 1) * T]
@@ -125,12 +129,13 @@ def _ep_worker(rank: int, world: int, port: int, T: int, out_dir: str) -> None:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("kind", ["contiguous", "strided"])
 @pytest.mark.parametrize("world", [1, 2])
-def test_expert_parallel_moe(oracle, tmp_path, world):
+def test_expert_parallel_moe(oracle, tmp_path, world, kind):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
     T = 512
-    mp.spawn(_ep_worker, args=(world, _free_port(), T, str(tmp_path)), nprocs=world, join=True)
+    mp.spawn(_ep_worker, args=(world, _free_port(), T, str(tmp_path), kind), nprocs=world, join=True)
     got = np.concatenate([np.load(tmp_path / f"ep{r}.npy") for r in range(world)])
     cfg, w = full_layer(oracle, False, 4)
     bias = np.random.default_rng(8).standard_normal(64).astype(np.float32)

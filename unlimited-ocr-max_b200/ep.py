@@ -2,7 +2,10 @@
 
 The reference runs the MoE on one device; this is the B200 build's extension for large token
 batches. Every rank holds T / P tokens, the replicated gate and shared experts, and E / P routed
-experts (contiguous: rank r owns experts [r E/P, (r+1) E/P)). One forward:
+experts, placed by an ``ExpertPlacement``: contiguous ranges by default (rank r owns experts
+[r E/P, (r+1) E/P)), or balanced from measured expert loads (``balanced_placement``: a skewed
+gate sends most rows to a few experts, and the rank holding them sets the step time). One
+forward:
 
 1. route the rank's tokens (the bit-exact gate, ``uocr_moe_route``);
 2. plan: one row per (token, destination rank) that holds at least one of its k experts, rows
@@ -22,7 +25,7 @@ compute steps are CUDA only (``ExpertParallelMoE``).
 from __future__ import annotations
 
 import ctypes
-from dataclasses import dataclass
+from dataclasses import dataclass, field
 from typing import Callable, Mapping
 
 import torch
@@ -32,8 +35,71 @@ from . import ops
 from ._lib import check, load
 from .moe import MoEConfig, UocrMoE
 
-__all__ = ["DispatchPlan", "plan_dispatch", "exchange_counts", "exchange_rows", "sum_partials", "ep_forward",
-           "ExpertParallelMoE"]
+__all__ = ["ExpertPlacement", "contiguous_placement", "balanced_placement", "DispatchPlan", "plan_dispatch",
+           "exchange_counts", "exchange_rows", "sum_partials", "ep_forward", "ExpertParallelMoE"]
+
+
+@dataclass
+class ExpertPlacement:
+    """Which rank holds each routed expert: rank p holds ``experts[p]`` (global ids, the same
+    number on every rank) as its local experts 0, 1, ... in that order."""
+
+    experts: list[list[int]]
+    _maps: dict = field(default_factory=dict, repr=False, compare=False)
+
+    @property
+    def world(self) -> int:
+        return len(self.experts)
+
+    @property
+    def e_local(self) -> int:
+        return len(self.experts[0])
+
+    def owner_local(self, device=None) -> tuple[torch.Tensor, torch.Tensor]:
+        """[E] int64 owner rank and [E] int64 local index of every expert (cached per device)."""
+        key = str(torch.device(device) if device is not None else "cpu")
+        if key not in self._maps:
+            E = sum(len(v) for v in self.experts)
+            owner = torch.empty(E, dtype=torch.int64)
+            local = torch.empty(E, dtype=torch.int64)
+            for p, ex in enumerate(self.experts):
+                owner[ex] = p
+                local[ex] = torch.arange(len(ex))
+            self._maps[key] = (owner.to(device), local.to(device))
+        return self._maps[key]
+
+
+def contiguous_placement(E: int, world: int) -> ExpertPlacement:
+    if E % world:
+        raise ValueError(f"{E} experts do not split over {world} ranks")
+    n = E // world
+    return ExpertPlacement([list(range(p * n, (p + 1) * n)) for p in range(world)])
+
+
+def balanced_placement(load, world: int) -> ExpertPlacement:
+    """E / world experts per rank with the routed rows (``load[e]``, e.g. a histogram of past
+    routing decisions) spread as evenly as the greedy longest-first rule does it: experts by
+    descending load (ties: lower id first) each go to the rank with the least load so far among
+    those with room (ties: lower rank). Deterministic, so every rank computes the same map."""
+    load = [int(v) for v in (load.tolist() if isinstance(load, torch.Tensor) else load)]
+    E = len(load)
+    if E % world:
+        raise ValueError(f"{E} experts do not split over {world} ranks")
+    cap = E // world
+    sums, experts = [0] * world, [[] for _ in range(world)]
+    for e in sorted(range(E), key=lambda e: (-load[e], e)):
+        p = min((q for q in range(world) if len(experts[q]) < cap), key=lambda q: (sums[q], q))
+        experts[p].append(e)
+        sums[p] += load[e]
+    return ExpertPlacement([sorted(v) for v in experts])
+
+
+def _as_placement(placement, world: int) -> ExpertPlacement:
+    if isinstance(placement, ExpertPlacement):
+        if placement.world != world:
+            raise ValueError(f"placement for {placement.world} ranks used with {world}")
+        return placement
+    return contiguous_placement(int(placement) * world, world)  # an int: experts per rank, contiguous
 
 
 @dataclass
@@ -44,9 +110,12 @@ class DispatchPlan:
     meta_weight: torch.Tensor  # [Ns, k] fp32 routing weight of the slot
 
 
-def plan_dispatch(ids: torch.Tensor, wts: torch.Tensor, world: int, e_local: int) -> DispatchPlan:
-    """Rows to send: one per (token, destination rank) with at least one expert there."""
-    dest = torch.div(ids.long(), e_local, rounding_mode="floor")  # [T, k]
+def plan_dispatch(ids: torch.Tensor, wts: torch.Tensor, world: int, placement) -> DispatchPlan:
+    """Rows to send: one per (token, destination rank) with at least one expert there.
+    ``placement``: an ExpertPlacement, or an int (experts per rank, contiguous ranges)."""
+    owner, local = _as_placement(placement, world).owner_local(ids.device)
+    dest = owner[ids.long()]  # [T, k]
+    loc = local[ids.long()]
     orders, counts, metas_e, metas_w = [], [], [], []
     for p in range(world):
         on_p = dest == p
@@ -54,7 +123,7 @@ def plan_dispatch(ids: torch.Tensor, wts: torch.Tensor, world: int, e_local: int
         orders.append(tok)
         counts.append(int(tok.numel()))
         sel = on_p[tok]
-        metas_e.append(torch.where(sel, ids[tok].long() - p * e_local, torch.full_like(ids[tok].long(), -1)).int())
+        metas_e.append(torch.where(sel, loc[tok], torch.full_like(loc[tok], -1)).int())
         metas_w.append(torch.where(sel, wts[tok], torch.zeros_like(wts[tok])))
     return DispatchPlan(torch.cat(orders), counts, torch.cat(metas_e), torch.cat(metas_w))
 
@@ -88,15 +157,16 @@ def sum_partials(T: int, H: int, plan: DispatchPlan, partial: torch.Tensor) -> t
 
 
 def ep_forward(x: torch.Tensor, route: Callable, local_experts: Callable, shared: Callable, world: int,
-               e_local: int, group=None) -> torch.Tensor:
+               placement, group=None) -> torch.Tensor:
     """One expert-parallel MoE forward of this rank's tokens x [T, H] fp32.
 
     route(x) -> (ids [T,k] int32 global, wts [T,k] fp32); local_experts(rows bf16 [N,H], meta_e,
-    meta_w) -> fp32 [N,H]; shared(x, out) adds the shared experts into out in place.
+    meta_w) -> fp32 [N,H] (meta_e: local expert indices); shared(x, out) adds the shared experts
+    into out in place. placement: as for plan_dispatch.
     """
     T, H = x.shape
     ids, wts = route(x)
-    plan = plan_dispatch(ids, wts, world, e_local)
+    plan = plan_dispatch(ids, wts, world, placement)
     recv_counts = exchange_counts(plan.send_counts, x.device, group)
     rows = x.index_select(0, plan.order).to(torch.bfloat16)
     meta = torch.cat([plan.meta_expert, plan.meta_weight.view(torch.int32)], dim=1)  # one exchange
@@ -113,12 +183,13 @@ def ep_forward(x: torch.Tensor, route: Callable, local_experts: Callable, shared
 class ExpertParallelMoE:
     """The MoE sublayer with its routed experts sharded over the ranks of ``group``.
 
-    Construct on every rank after ``torch.distributed`` is initialised (backend "nccl"), load the
-    full reference state dict (every rank keeps only its slice of the routed experts), then call
-    with the rank's tokens.
+    Construct on every rank after ``torch.distributed`` is initialised (backend "nccl"), with the
+    same ``placement`` everywhere (default: contiguous ranges), load the full reference state dict
+    (every rank keeps only its own routed experts), then call with the rank's tokens.
     """
 
-    def __init__(self, config: MoEConfig, *, group=None, device: str | torch.device = "cuda") -> None:
+    def __init__(self, config: MoEConfig, *, group=None, device: str | torch.device = "cuda",
+                 placement: ExpertPlacement | None = None) -> None:
         self.config = config
         self.group = group
         self.rank = dist.get_rank(group)
@@ -126,6 +197,12 @@ class ExpertParallelMoE:
         E = config.n_routed_experts
         if E % self.world:
             raise ValueError(f"ExpertParallelMoE: {E} experts do not split over {self.world} ranks")
+        if placement is None:
+            placement = contiguous_placement(E, self.world)
+        if placement.world != self.world or sorted(e for v in placement.experts for e in v) != list(range(E)) or \
+                any(len(v) != E // self.world for v in placement.experts):
+            raise ValueError("ExpertParallelMoE: placement must give every rank E / world distinct experts")
+        self.placement = placement
         self.e_local = E // self.world
         if self.e_local < config.num_experts_per_tok:
             raise ValueError("ExpertParallelMoE: fewer local experts than experts per token")
@@ -139,14 +216,14 @@ class ExpertParallelMoE:
         self._ws: dict[str, torch.Tensor] = {}
 
     def load_state_dict(self, state: Mapping[str, torch.Tensor]) -> "ExpertParallelMoE":
-        e0, n = self.rank * self.e_local, self.e_local
+        mine = torch.tensor(self.placement.experts[self.rank], dtype=torch.int64)
         local = {}
         for name, t in state.items():
             if name.startswith("experts."):
-                t = t[e0:e0 + n]
+                t = t.index_select(0, mine.to(t.device))
             elif name == "gate.gate_score.weight":
                 self.router = t.to(self.device, torch.bfloat16).contiguous()
-                t = t[e0:e0 + n]  # unused by the local module (routing uses the full gate)
+                t = t[:self.e_local]  # unused by the local module (routing uses the full gate)
             local[name] = t
         self.local.load_state_dict(local)
         return self
@@ -188,5 +265,5 @@ class ExpertParallelMoE:
         """The MoE over this rank's tokens x [T, H] fp32 (a collective: every rank calls it)."""
         if not x.is_cuda or x.dtype != torch.float32 or x.dim() != 2 or x.shape[1] != self.config.hidden_size:
             raise ValueError("ExpertParallelMoE: x must be a CUDA fp32 [T, hidden] tensor")
-        return ep_forward(x.contiguous(), self._route, self._local_experts, self._shared, self.world, self.e_local,
-                          self.group)
+        return ep_forward(x.contiguous(), self._route, self._local_experts, self._shared, self.world,
+                          self.placement, self.group)
