@@ -187,6 +187,29 @@ UOCR_API int uocr_moe_ep_experts(const uocr_moe_layer* L, const uint16_t* rows, 
                                  const int32_t* expert_local, const float* weight, float* out,
                                  void* workspace, size_t workspace_bytes, uocr_stream_t stream);
 
+/* uocr_moe_ep_dispatch: the dispatch plan and row gather of T local tokens routed to ids/wts
+ * [T, top_k] (global expert ids, id < 0 = none), for `world` <= 8 ranks with expert e held by rank
+ * owner[e] as its local expert local[e] (device int32 [E]). One row per (token, rank holding at
+ * least one of its experts), ordered by rank, then token (the row order of the torch bookkeeping
+ * in ep.py, bit for bit). Outputs, device memory:
+ *   send_counts int64 [world]      rows per destination rank;
+ *   rows   bf16  [T * world, H]    x rounded to bf16 (nearest even), first sum(send_counts) used;
+ *   meta   int32 [T * world, 2k]   per row the local expert of each slot (-1: another rank's or
+ *                                  none), then the slot's routing weight as fp32 bits (0 for -1);
+ *   inv    int32 [world, T]        row of (rank p, token t), -1 if t sends p nothing.
+ * Two launches; no host synchronisation. */
+UOCR_API size_t uocr_moe_ep_dispatch_workspace_bytes(int64_t T, int64_t world);
+UOCR_API int uocr_moe_ep_dispatch(const float* x, int64_t T, int64_t H, const int32_t* ids, const float* wts,
+                                  int64_t top_k, const int32_t* owner, const int32_t* local, int64_t E,
+                                  int64_t world, int64_t* send_counts, uint16_t* rows, int32_t* meta,
+                                  int32_t* inv, void* workspace, size_t workspace_bytes, uocr_stream_t stream);
+
+/* uocr_moe_ep_combine: out[t] = (sum over ranks p ascending, from +0, of partials[inv[p, t]] for
+ * inv >= 0) + add[t] (when add is not null): the partial rows come back in the dispatch's row
+ * order; `add` is typically the shared experts' output. fp32 throughout. */
+UOCR_API int uocr_moe_ep_combine(const float* partials, int64_t n_rows, const int32_t* inv, int64_t T,
+                                 int64_t world, int64_t H, const float* add, float* out, uocr_stream_t stream);
+
 /* The shared experts of L alone over x [T, H] fp32 (bf16 products, fp32 out): out = shared(x),
  * or out += shared(x) with accumulate != 0. */
 UOCR_API size_t uocr_moe_shared_workspace_bytes(const uocr_moe_layer* L, int64_t T);

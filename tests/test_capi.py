@@ -149,3 +149,19 @@ def test_packed_sizes_and_refusals(uocr):
     assert rc == 1 and b"pack_w13" in L.uocr_last_error()
     rc = L.uocr_moe_pack_w2(None, None, 4, 256, 896, 64, 1, None, None)
     assert rc == 4 and b"group size" in L.uocr_last_error()
+
+
+def test_ep_dispatch_combine_refusals(uocr):
+    """Argument checks of the expert-parallel bookkeeping entry points (no device work)."""
+    lib = uocr.load()
+    err = lambda: lib.uocr_last_error().decode()  # noqa: E731
+    assert lib.uocr_moe_ep_dispatch_workspace_bytes(16384, 4) > 16384
+    assert lib.uocr_moe_ep_dispatch_workspace_bytes(16, 9) == 0
+    args = [None, 16, 1280, None, None, 6, None, None, 64]
+    assert lib.uocr_moe_ep_dispatch(*args, 9, None, None, None, None, None, 0, None) == 4 and "world=9" in err()
+    assert lib.uocr_moe_ep_dispatch(None, 16, 1284, None, None, 6, None, None, 64, 2, None, None, None, None, None, 0,
+                                    None) == 1 and "multiple of 8" in err()
+    assert lib.uocr_moe_ep_dispatch(*args, 2, None, None, None, None, None, 0, None) == 1 and "null" in err()
+    assert lib.uocr_moe_ep_combine(None, 4, None, 16, 0, 1280, None, None, None) == 4 and "world=0" in err()
+    assert lib.uocr_moe_ep_combine(None, 4, None, 16, 2, 1280, None, None, None) == 1 and "null" in err()
+    assert lib.uocr_moe_ep_combine(None, 0, None, 0, 2, 1280, None, None, None) == 0

@@ -125,6 +125,9 @@ def test_plan_dispatch_with_placement():
     plan = ep.plan_dispatch(ids, torch.ones(1, 6), 2, pl)
     assert plan.send_counts == [1, 1]
     assert plan.meta_expert.tolist() == [[0, -1, -1, -1, 1, -1], [-1, 2, 0, 3, -1, 1]]
+    # id -1 (no expert) sends nothing, to no rank
+    none = ep.plan_dispatch(torch.tensor([[-1, -1, 1, 3, -1, 5]], dtype=torch.int32), torch.ones(1, 6), 2, pl)
+    assert none.send_counts == [0, 1] and none.meta_expert.tolist() == [[-1, -1, 0, 1, -1, 2]]
 
 
 @pytest.mark.parametrize("kind", ["contiguous", "balanced"])

@@ -1,7 +1,9 @@
 """GPU parity of the expert-parallel pieces through the C ABI: uocr_moe_ep_experts (local experts
 over received bf16 rows, entries without a local expert skipped), uocr_moe_shared_forward, and
 ExpertParallelMoE end to end (one NCCL rank on one GPU; two ranks when two GPUs are visible),
-against the float64 layer fed the bit-exact routing, at the prefill tolerance."""
+against the float64 layer fed the bit-exact routing, at the prefill tolerance. The dispatch and
+combine kernels (uocr_moe_ep_dispatch / uocr_moe_ep_combine) must reproduce the torch
+bookkeeping of ep.py bit for bit, and so must the whole device path."""
 
 from __future__ import annotations
 
@@ -71,6 +73,81 @@ def test_ep_experts_vs_fp64(uocr, oracle):
     _check(oracle, out.cpu().numpy(), ref)
 
 
+def _random_routing(rng, T, k, E, none_frac=0.1):
+    ids = np.stack([rng.permutation(E)[:k] for _ in range(T)]).astype(np.int32) if T else np.zeros((0, k), np.int32)
+    ids[rng.random((T, k)) < none_frac] = -1
+    wts = rng.random((T, k)).astype(np.float32)
+    return ids, wts
+
+
+def _dispatch(L, x, ids, wts, placement, world):
+    T, H = x.shape
+    k = ids.shape[1]
+    owner, local = (t.int().to(DEV).contiguous() for t in placement.owner_local())
+    send = torch.full((world,), -7, dtype=torch.int64, device=DEV)
+    rows = torch.zeros((max(T * world, 1), H), dtype=torch.bfloat16, device=DEV)
+    meta = torch.zeros((max(T * world, 1), 2 * k), dtype=torch.int32, device=DEV)
+    inv = torch.zeros((world, max(T, 1)), dtype=torch.int32, device=DEV)
+    ws = torch.zeros(max(L.uocr_moe_ep_dispatch_workspace_bytes(T, world), 1), dtype=torch.uint8, device=DEV)
+    rc = L.uocr_moe_ep_dispatch(x.data_ptr(), T, H, ids.data_ptr(), wts.data_ptr(), k, owner.data_ptr(),
+                                local.data_ptr(), owner.numel(), world, send.data_ptr(),
+                                rows.view(torch.int16).data_ptr(), meta.data_ptr(), inv.data_ptr(), ws.data_ptr(),
+                                ws.numel(), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, L.uocr_last_error()
+    return send, rows, meta, inv
+
+
+@pytest.mark.parametrize("world,T", [(1, 300), (2, 1), (2, 257), (3, 1000), (4, 4096), (8, 513), (4, 0)])
+def test_ep_dispatch_matches_torch_plan(uocr, world, T):
+    ep = importlib.import_module("unlimited-ocr-max_b200.ep")
+    L = uocr.load()
+    rng = np.random.default_rng(world * 1000 + T)
+    E, k, H = 64, 6, 1280
+    perm = rng.permutation(E)
+    placement = ep.ExpertPlacement([sorted(perm[p::world].tolist()) for p in range(world)])
+    ids_np, wts_np = _random_routing(rng, T, k, E)
+    ids, wts = torch.from_numpy(ids_np).to(DEV), torch.from_numpy(wts_np).to(DEV)
+    x = torch.from_numpy(rng.standard_normal((T, H)).astype(np.float32) * 3).to(DEV)
+    send, rows, meta, inv = _dispatch(L, x, ids, wts, placement, world)
+    plan = ep.plan_dispatch(ids.cpu(), wts.cpu(), world, placement)
+    assert send.cpu().tolist() == plan.send_counts
+    ns = sum(plan.send_counts)
+    assert torch.equal(rows[:ns].cpu().view(torch.int16), x.cpu()[plan.order].to(torch.bfloat16).view(torch.int16))
+    assert torch.equal(meta[:ns, :k].cpu(), plan.meta_expert)
+    assert torch.equal(meta[:ns, k:].cpu(), plan.meta_weight.view(torch.int32))
+    want_inv = torch.full((world, T), -1, dtype=torch.int32)
+    r0 = 0
+    for p, c in enumerate(plan.send_counts):
+        want_inv[p, plan.order[r0:r0 + c]] = torch.arange(r0, r0 + c, dtype=torch.int32)
+        r0 += c
+    assert torch.equal(inv[:, :T].cpu(), want_inv)
+
+
+@pytest.mark.parametrize("with_add", [False, True])
+def test_ep_combine_matches_sum_partials(uocr, with_add):
+    ep = importlib.import_module("unlimited-ocr-max_b200.ep")
+    L = uocr.load()
+    rng = np.random.default_rng(3)
+    world, T, E, k, H = 4, 777, 64, 6, 1280
+    placement = ep.balanced_placement(rng.integers(0, 1000, E), world)
+    ids_np, wts_np = _random_routing(rng, T, k, E, 0.3)
+    ids, wts = torch.from_numpy(ids_np).to(DEV), torch.from_numpy(wts_np).to(DEV)
+    x = torch.from_numpy(rng.standard_normal((T, H)).astype(np.float32)).to(DEV)
+    send, rows, meta, inv = _dispatch(L, x, ids, wts, placement, world)
+    plan = ep.plan_dispatch(ids.cpu(), wts.cpu(), world, placement)
+    ns = sum(plan.send_counts)
+    part = torch.from_numpy(rng.standard_normal((ns, H)).astype(np.float32)).to(DEV)
+    add = torch.from_numpy(rng.standard_normal((T, H)).astype(np.float32)).to(DEV) if with_add else None
+    out = torch.full((T, H), float("nan"), device=DEV)
+    rc = L.uocr_moe_ep_combine(part.data_ptr(), ns, inv.data_ptr(), T, world, H, 0 if add is None else add.data_ptr(),
+                               out.data_ptr(), torch.cuda.current_stream().cuda_stream)
+    assert rc == 0, L.uocr_last_error()
+    want = ep.sum_partials(T, H, plan, part.cpu())
+    if add is not None:
+        want = want + add.cpu()
+    assert torch.equal(out.cpu(), want)
+
+
 @pytest.mark.parametrize("accumulate", [0, 1])
 def test_shared_forward_vs_fp64(uocr, oracle, accumulate):
     cfg, w, moe = _layer(uocr, oracle)
@@ -117,12 +194,17 @@ def _ep_worker(rank: int, world: int, port: int, T: int, out_dir: str, kind: str
         placement = None
         if kind == "strided":  # every world-th expert, in descending order: local != global index
             placement = ep.ExpertPlacement([list(range(63 - p, -1, -world)) for p in range(world)])
-        m = ep.ExpertParallelMoE(uocr.MoEConfig(), device=f"cuda:{rank}", placement=placement)
+        m = ep.ExpertParallelMoE(uocr.MoEConfig(), device=f"cuda:{rank}", placement=placement,
+                                 overlap_shared=kind != "strided")
         m.load_state_dict(to_state(w, cfg, False))
         bias = np.random.default_rng(8).standard_normal(64).astype(np.float32)
         m.bias = torch.from_numpy(bias).to(f"cuda:{rank}")
         x = o.synth_hidden(T * world, cfg.hidden, 9)[rank * T:(rank + 1) * T]
-        got = m(torch.from_numpy(x).to(f"cuda:{rank}"))
+        xd = torch.from_numpy(x).to(f"cuda:{rank}")
+        got = m(xd)
+        # the device bookkeeping reproduces the torch bookkeeping bit for bit
+        assert torch.equal(got, m.forward_reference(xd))
+        assert torch.equal(got, m(xd))
         np.save(os.path.join(out_dir, f"ep{rank}.npy"), got.cpu().numpy())
         dist.barrier()
     finally:

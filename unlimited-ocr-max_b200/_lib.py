@@ -63,6 +63,9 @@ SIGNATURES: dict[str, tuple] = {
     "uocr_moe_ep_experts": (I32, [ctypes.POINTER(UocrMoeLayer), P, I64, P, P, P, P, SZ, P]),
     "uocr_moe_shared_workspace_bytes": (SZ, [ctypes.POINTER(UocrMoeLayer), I64]),
     "uocr_moe_shared_forward": (I32, [ctypes.POINTER(UocrMoeLayer), P, I64, P, I32, P, SZ, P]),
+    "uocr_moe_ep_dispatch_workspace_bytes": (SZ, [I64, I64]),
+    "uocr_moe_ep_dispatch": (I32, [P, I64, I64, P, P, I64, P, P, I64, I64, P, P, P, P, P, SZ, P]),
+    "uocr_moe_ep_combine": (I32, [P, I64, P, I64, I64, I64, P, P, P]),
     "uocr_moe_device_status": (I32, [P, P]),
     "uocr_moe_decode_set_trace": (I32, [P, SZ]),
     "uocr_moe_decode_noalloc_max_bytes": (SZ, []),

@@ -433,6 +433,57 @@ int uocr_moe_ep_experts(const uocr_moe_layer* L, const uint16_t* rows, int64_t N
     return cuda_status(uocr::launch_prefill(a, ws, d, S(stream)), "moe_ep_experts: launch");
 }
 
+size_t uocr_moe_ep_dispatch_workspace_bytes(int64_t T, int64_t world) {
+    if (T < 1 || T > (int64_t(1) << 24) || world < 1 || world > uocr::kEpMaxWorld) return 0;
+    return uocr::ep_dispatch_workspace_bytes((int)T, (int)world);
+}
+
+int uocr_moe_ep_dispatch(const float* x, int64_t T, int64_t H, const int32_t* ids, const float* wts, int64_t top_k,
+                         const int32_t* owner, const int32_t* local, int64_t E, int64_t world, int64_t* send_counts,
+                         uint16_t* rows, int32_t* meta, int32_t* inv, void* workspace, size_t workspace_bytes,
+                         uocr_stream_t stream) {
+    if (T < 0 || T > (int64_t(1) << 24)) return fail(UOCR_EINVAL, "moe_ep_dispatch: T=%lld outside 0..2^24", (long long)T);
+    if (world < 1 || world > uocr::kEpMaxWorld)
+        return fail(UOCR_EUNSUPPORTED, "moe_ep_dispatch: world=%lld outside 1..%d", (long long)world, uocr::kEpMaxWorld);
+    if (H < 8 || H % 8) return fail(UOCR_EINVAL, "moe_ep_dispatch: hidden=%lld must be a positive multiple of 8", (long long)H);
+    if (top_k < 1 || top_k > 64) return fail(UOCR_EINVAL, "moe_ep_dispatch: top_k=%lld outside 1..64", (long long)top_k);
+    if (E < 1 || E > 4096) return fail(UOCR_EINVAL, "moe_ep_dispatch: E=%lld outside 1..4096", (long long)E);
+    if (T * world * H >= (int64_t(1) << 40)) return fail(UOCR_EUNSUPPORTED, "moe_ep_dispatch: too many rows");
+    if (!send_counts) return fail(UOCR_EINVAL, "moe_ep_dispatch: null pointer");
+    if (T == 0) {
+        cudaError_t err = cudaMemsetAsync(send_counts, 0, sizeof(int64_t) * world, S(stream));
+        return cuda_status(err, "moe_ep_dispatch: clear counts");
+    }
+    if (!x || !ids || !wts || !owner || !local || !rows || !meta || !inv || !workspace)
+        return fail(UOCR_EINVAL, "moe_ep_dispatch: null pointer");
+    if (!a16(x) || !a16(rows)) return fail(UOCR_EINVAL, "moe_ep_dispatch: x and rows must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(workspace) & 255)
+        return fail(UOCR_EINVAL, "moe_ep_dispatch: workspace must be 256-byte aligned");
+    const size_t need = uocr::ep_dispatch_workspace_bytes((int)T, (int)world);
+    if (workspace_bytes < need)
+        return fail(UOCR_EINVAL, "moe_ep_dispatch: workspace of %zu bytes, need %zu", workspace_bytes, need);
+    return cuda_status(uocr::launch_ep_dispatch(x, (int)T, (int)H, ids, wts, (int)top_k, owner, local, (int)E,
+                                                (int)world, reinterpret_cast<long long*>(send_counts), rows, meta,
+                                                inv, workspace, S(stream)),
+                       "moe_ep_dispatch: launch");
+}
+
+int uocr_moe_ep_combine(const float* partials, int64_t n_rows, const int32_t* inv, int64_t T, int64_t world,
+                        int64_t H, const float* add, float* out, uocr_stream_t stream) {
+    if (T < 0 || T > (int64_t(1) << 24)) return fail(UOCR_EINVAL, "moe_ep_combine: T=%lld outside 0..2^24", (long long)T);
+    if (world < 1 || world > uocr::kEpMaxWorld)
+        return fail(UOCR_EUNSUPPORTED, "moe_ep_combine: world=%lld outside 1..%d", (long long)world, uocr::kEpMaxWorld);
+    if (H < 4 || H % 4) return fail(UOCR_EINVAL, "moe_ep_combine: hidden=%lld must be a positive multiple of 4", (long long)H);
+    if (n_rows < 0) return fail(UOCR_EINVAL, "moe_ep_combine: negative row count");
+    if (T == 0) return ok();
+    if (!inv || !out || (n_rows > 0 && !partials)) return fail(UOCR_EINVAL, "moe_ep_combine: null pointer");
+    if (!a16(out) || (partials && !a16(partials)) || (add && !a16(add)))
+        return fail(UOCR_EINVAL, "moe_ep_combine: partials, add and out must be 16-byte aligned");
+    return cuda_status(uocr::launch_ep_combine(partials, (long long)n_rows, inv, (int)T, (int)world, (int)H, add, out,
+                                               S(stream)),
+                       "moe_ep_combine: launch");
+}
+
 size_t uocr_moe_shared_workspace_bytes(const uocr_moe_layer* L, int64_t T) {
     if (!L || T < 1 || T > (int64_t(1) << 24)) return 0;
     return uocr::prefill_layout((int)T, L->hidden, L->inter, L->n_routed, L->n_shared, 0, false).total;

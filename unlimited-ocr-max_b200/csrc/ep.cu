@@ -1,0 +1,197 @@
+// Expert-parallel bookkeeping on the device: the dispatch plan with the bf16 row gather, and
+// the combine of the returned partial rows. The reference runs the MoE on one device; these
+// serve the B200 build's expert-parallel prefill (ep.py). The row order (destination rank,
+// then token) and the sum order of the combine (ascending source rank, from +0, then the
+// shared-expert term) are the ones ep.py's plan_dispatch / sum_partials state, bit for bit.
+//
+// Dispatch, two launches over chunks of kChunk tokens:
+//   count:  per token the bit mask of ranks that own one of its experts; per chunk and rank the
+//           number of tokens with that bit (warp ballots).
+//   gather: each CTA sums the chunk counts of all chunks (rank totals, hence each rank's first
+//           row) and of the chunks before it, ranks its tokens per destination with ballot
+//           prefixes, writes inv / meta, then copies its rows x fp32 -> bf16 (round to nearest
+//           even) with 16-byte stores. CTA 0 writes the per-rank row counts.
+// HBM bytes: x read once per destination (the re-reads of a token's row hit L2), rows written
+// once: about T * H * 4 + rows * H * 2.
+#include "common.cuh"
+#include "kernels.h"
+
+#include <cuda_bf16.h>
+
+namespace uocr {
+
+namespace {
+
+constexpr int kChunk = 256;  // tokens per CTA (one per thread)
+
+__global__ void __launch_bounds__(kChunk)
+ep_count_kernel(const int32_t* __restrict__ ids, int T, int k, const int32_t* __restrict__ owner, int E, int world,
+                uint8_t* __restrict__ mask_out, int32_t* __restrict__ counts) {
+    __shared__ int wcount[kChunk / 32][kEpMaxWorld];
+    const int t = blockIdx.x * kChunk + threadIdx.x;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    unsigned mask = 0;
+    if (t < T) {
+        for (int s = 0; s < k; ++s) {
+            const int e = ids[(size_t)t * k + s];
+            const int o = (e >= 0 && e < E) ? owner[e] : -1;
+            if (o >= 0 && o < world) mask |= 1u << o;
+        }
+        mask_out[t] = (uint8_t)mask;
+    }
+    for (int p = 0; p < world; ++p) {
+        const unsigned b = __ballot_sync(0xffffffffu, (mask >> p) & 1u);
+        if (lane == 0) wcount[warp][p] = __popc(b);
+    }
+    __syncthreads();
+    if (threadIdx.x < world) {
+        int c = 0;
+        for (int w = 0; w < kChunk / 32; ++w) c += wcount[w][threadIdx.x];
+        counts[(size_t)blockIdx.x * world + threadIdx.x] = c;
+    }
+}
+
+__global__ void __launch_bounds__(kChunk)
+ep_gather_kernel(const float* __restrict__ x, int T, int H, const int32_t* __restrict__ ids,
+                 const float* __restrict__ wts, int k, const int32_t* __restrict__ owner,
+                 const int32_t* __restrict__ local, int E, int world, const uint8_t* __restrict__ masks,
+                 const int32_t* __restrict__ counts, int nchunks, long long* __restrict__ send_counts,
+                 __nv_bfloat16* __restrict__ rows, int32_t* __restrict__ meta, int32_t* __restrict__ inv) {
+    __shared__ int total[kEpMaxWorld], before[kEpMaxWorld], first[kEpMaxWorld];
+    __shared__ int wpre[kChunk / 32][kEpMaxWorld];
+    __shared__ int list_row[kChunk * kEpMaxWorld];
+    __shared__ int list_tok[kChunk * kEpMaxWorld];
+    __shared__ int nlist;
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int chunk = blockIdx.x;
+
+    // warp p: rank p's total over all chunks and over the chunks before this one
+    if (warp < world) {
+        int tot = 0, bef = 0;
+        for (int c = lane; c < nchunks; c += 32) {
+            const int v = counts[(size_t)c * world + warp];
+            tot += v;
+            if (c < chunk) bef += v;
+        }
+        for (int off = 16; off >= 1; off >>= 1) {
+            tot += __shfl_xor_sync(0xffffffffu, tot, off);
+            bef += __shfl_xor_sync(0xffffffffu, bef, off);
+        }
+        if (lane == 0) {
+            total[warp] = tot;
+            before[warp] = bef;
+        }
+    }
+    const int t = chunk * kChunk + threadIdx.x;
+    const unsigned mask = t < T ? masks[t] : 0u;
+    for (int p = 0; p < world; ++p) {
+        const unsigned b = __ballot_sync(0xffffffffu, (mask >> p) & 1u);
+        if (lane == 0) wpre[warp][p] = __popc(b);
+    }
+    if (threadIdx.x == 0) nlist = 0;
+    __syncthreads();
+    if (threadIdx.x < world) {
+        int f = 0;
+        for (int q = 0; q < (int)threadIdx.x; ++q) f += total[q];
+        first[threadIdx.x] = f + before[threadIdx.x];
+        if (chunk == 0) send_counts[threadIdx.x] = total[threadIdx.x];
+    }
+    __syncthreads();
+    for (int p = 0; p < world; ++p) {
+        const unsigned b = __ballot_sync(0xffffffffu, (mask >> p) & 1u);
+        if (t < T) {
+            int row = -1;
+            if ((mask >> p) & 1u) {
+                int pre = 0;
+                for (int w = 0; w < warp; ++w) pre += wpre[w][p];
+                row = first[p] + pre + __popc(b & ((1u << lane) - 1u));
+                int32_t* m = meta + (size_t)row * 2 * k;
+                for (int s = 0; s < k; ++s) {
+                    const int e = ids[(size_t)t * k + s];
+                    const bool mine = e >= 0 && e < E && owner[e] == p;
+                    m[s] = mine ? local[e] : -1;
+                    m[k + s] = mine ? __float_as_int(wts[(size_t)t * k + s]) : 0;
+                }
+                const int slot = atomicAdd(&nlist, 1);
+                list_row[slot] = row;
+                list_tok[slot] = t;
+            }
+            inv[(size_t)p * T + t] = row;
+        }
+    }
+    __syncthreads();
+    // rows: 8 elements (two float4 loads, one 16-byte store) per item
+    const int per_row = H / 8, n = nlist;
+    for (int i = threadIdx.x; i < n * per_row; i += kChunk) {
+        const int r = i / per_row, c = i - r * per_row;
+        const float* src = x + (size_t)list_tok[r] * H + 8 * c;
+        const float4 a = *reinterpret_cast<const float4*>(src);
+        const float4 b = *reinterpret_cast<const float4*>(src + 4);
+        __nv_bfloat162 o[4] = {__floats2bfloat162_rn(a.x, a.y), __floats2bfloat162_rn(a.z, a.w),
+                               __floats2bfloat162_rn(b.x, b.y), __floats2bfloat162_rn(b.z, b.w)};
+        *reinterpret_cast<uint4*>(rows + (size_t)list_row[r] * H + 8 * c) = *reinterpret_cast<uint4*>(o);
+    }
+}
+
+// out[t] = sum over ranks p ascending of partials[inv[p][t]] (rows with inv < 0 skipped; the sum
+// starts from +0), then + add[t] when given. One thread per 4 columns of a token.
+__global__ void ep_combine_kernel(const float* __restrict__ part, long long nrows, const int32_t* __restrict__ inv,
+                                  int T, int world, int H, const float* __restrict__ add, float* __restrict__ out) {
+    const int H4 = H / 4;
+    const long long n = (long long)T * H4;
+    for (long long i = blockIdx.x * (long long)blockDim.x + threadIdx.x; i < n; i += (long long)gridDim.x * blockDim.x) {
+        const int t = (int)(i / H4), c = (int)(i - (long long)t * H4);
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int p = 0; p < world; ++p) {
+            const int r = inv[(size_t)p * T + t];
+            if (r < 0 || r >= nrows) continue;
+            const float4 v = *reinterpret_cast<const float4*>(part + (size_t)r * H + 4 * c);
+            acc.x = __fadd_rn(acc.x, v.x);
+            acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z);
+            acc.w = __fadd_rn(acc.w, v.w);
+        }
+        if (add) {
+            const float4 v = *reinterpret_cast<const float4*>(add + (size_t)t * H + 4 * c);
+            acc.x = __fadd_rn(acc.x, v.x);
+            acc.y = __fadd_rn(acc.y, v.y);
+            acc.z = __fadd_rn(acc.z, v.z);
+            acc.w = __fadd_rn(acc.w, v.w);
+        }
+        *reinterpret_cast<float4*>(out + (size_t)t * H + 4 * c) = acc;
+    }
+}
+
+}  // namespace
+
+size_t ep_dispatch_workspace_bytes(int T, int world) {
+    const size_t nchunks = ((size_t)T + kChunk - 1) / kChunk;
+    return (((size_t)T + 255) & ~(size_t)255) + nchunks * world * sizeof(int32_t);
+}
+
+cudaError_t launch_ep_dispatch(const float* x, int T, int H, const int32_t* ids, const float* wts, int k,
+                               const int32_t* owner, const int32_t* local, int E, int world, long long* send_counts,
+                               uint16_t* rows, int32_t* meta, int32_t* inv, void* ws, cudaStream_t st) {
+    const int nchunks = (T + kChunk - 1) / kChunk;
+    uint8_t* masks = reinterpret_cast<uint8_t*>(ws);
+    int32_t* counts = reinterpret_cast<int32_t*>(masks + (((size_t)T + 255) & ~(size_t)255));
+    ep_count_kernel<<<nchunks, kChunk, 0, st>>>(ids, T, k, owner, E, world, masks, counts);
+    cudaError_t err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    ep_gather_kernel<<<nchunks, kChunk, 0, st>>>(x, T, H, ids, wts, k, owner, local, E, world, masks, counts, nchunks,
+                                                 send_counts, reinterpret_cast<__nv_bfloat16*>(rows), meta, inv);
+    return cudaGetLastError();
+}
+
+cudaError_t launch_ep_combine(const float* part, long long nrows, const int32_t* inv, int T, int world, int H,
+                              const float* add, float* out, cudaStream_t st) {
+    const long long n = (long long)T * (H / 4);
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    long long blocks = (n + 255) / 256;
+    if (blocks > (long long)sms * 8) blocks = (long long)sms * 8;
+    ep_combine_kernel<<<(unsigned)blocks, 256, 0, st>>>(part, nrows, inv, T, world, H, add, out);
+    return cudaGetLastError();
+}
+
+}  // namespace uocr

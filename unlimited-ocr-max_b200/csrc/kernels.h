@@ -116,6 +116,15 @@ struct PrefillLayout {
 PrefillLayout prefill_layout(int T, int H, int I, int E, int S, int topk, bool int8);
 cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& d, cudaStream_t st);
 
+// ep.cu: expert-parallel dispatch plan + bf16 row gather, and the combine of partial rows
+constexpr int kEpMaxWorld = 8;
+size_t ep_dispatch_workspace_bytes(int T, int world);
+cudaError_t launch_ep_dispatch(const float* x, int T, int H, const int32_t* ids, const float* wts, int k,
+                               const int32_t* owner, const int32_t* local, int E, int world, long long* send_counts,
+                               uint16_t* rows, int32_t* meta, int32_t* inv, void* ws, cudaStream_t st);
+cudaError_t launch_ep_combine(const float* part, long long nrows, const int32_t* inv, int T, int world, int H,
+                              const float* add, float* out, cudaStream_t st);
+
 // pack.cu: source rows at (e * estride + row * ld) elements
 cudaError_t launch_pack_w13(const void* gate, const void* up, const float* gs, const float* us, int E, int I, int H,
                             bool int8, long estride, long ld, void* out, cudaStream_t st);

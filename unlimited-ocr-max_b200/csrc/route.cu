@@ -9,71 +9,98 @@
 //            (s_l = e_l + e_{l+32}, then xor 16, 8, 4, 2, 1); p_j = e_j / sum (IEEE div);
 //   top-k:   k rounds of argmax by (p desc, index asc).
 //
-// One CTA serves kTT tokens with 512 threads = 64 experts x 8 segments: thread (j, s)
-// streams router row j's segment s once and fma-chains it against all kTT tokens, whose
-// rows sit in shared memory padded so the 8 segments' reads fall in distinct banks.
+// One CTA serves kTT = 16 tokens with 256 threads (8 tokens and 128 threads for a large H). Thread (eg, s, tg) owns router rows
+// j = eg + 16e (e = 0..3) over segment s and fma-chains them against the 8 tokens of token
+// group tg: per 8 K elements it loads 4 x 16 B of router rows (L2) and 16 float4 of token rows
+// from shared memory (each address shared by the 16 lanes of a half-warp, a broadcast) for 256
+// FMAs. Lanes 0-15 = eg, lane bit 4 = low bit of s, warp = (tg, s >> 1). Two CTAs per SM.
+// The FMA floor is T * 64 * H FMAs over 148 SMs x 128 FMA/clock.
 #include "common.cuh"
 #include "kernels.h"
 
 namespace uocr {
 
-constexpr int kRouteThreads = 512;
-
-template <int kTT>
-__global__ void __launch_bounds__(kRouteThreads)
+// kTG token groups of 8 (2; 1 when the hidden size leaves too little shared memory)
+template <int kTG>
+__global__ void __launch_bounds__(128 * kTG, 2)
 route_kernel(const float* __restrict__ x, int T, int H, const uint16_t* __restrict__ wg, int E,
              const float* __restrict__ bias, int topk, int32_t* __restrict__ ids_out, float* __restrict__ wts_out) {
+    constexpr int kTT = 8 * kTG;
+    constexpr int kRouteThreads = 128 * kTG;
     extern __shared__ float smem[];
     const int L = H / 8;     // segment length (multiple of 8)
     const int LP = L + 4;    // padded segment stride in floats
-    float* xs = smem;                         // [kTT][8][LP]
-    float* segs = xs + kTT * 8 * LP;          // [kTT][64][8]
-    float* logits = segs + kTT * 64 * 8;      // [kTT][64]
+    float* xs = smem;                         // [kTT][8][LP]; reused as segs [kTT][64][8]
+    float* segs = smem;
+    const int region = kTT * 8 * LP > kTT * 64 * 8 ? kTT * 8 * LP : kTT * 64 * 8;
+    float* logits = smem + region;            // [kTT][64]
 
     const int tid = threadIdx.x;
     const int t0 = blockIdx.x * kTT;
 
-    // stage the token rows (zeros past T)
-    for (int i = tid; i < kTT * H; i += kRouteThreads) {
-        const int t = i / H, k = i - t * H;
-        const int s = k / L, kk = k - s * L;
-        xs[(t * 8 + s) * LP + kk] = (t0 + t < T) ? x[(size_t)(t0 + t) * H + k] : 0.0f;
+    // stage the token rows (zeros past T), 16-byte loads
+    const int H4 = H / 4, L4 = L / 4;
+    for (int i = tid; i < kTT * H4; i += kRouteThreads) {
+        const int t = i / H4, k4 = i - t * H4;
+        const int s = k4 / L4, kk4 = k4 - s * L4;
+        const float4 v = (t0 + t < T) ? *reinterpret_cast<const float4*>(x + (size_t)(t0 + t) * H + 4 * k4)
+                                      : make_float4(0.f, 0.f, 0.f, 0.f);
+        *reinterpret_cast<float4*>(xs + (t * 8 + s) * LP + 4 * kk4) = v;
     }
     __syncthreads();
 
-    const int j = tid >> 3;
-    const int s = tid & 7;
-    if (j < E) {
-        float acc[kTT];
+    const int lane = tid & 31, warp = tid >> 5;
+    const int eg = lane & 15;
+    const int s = ((warp & 3) << 1) | (lane >> 4);
+    const int tg = warp >> 2;
+    float acc[4][8];
 #pragma unroll
-        for (int t = 0; t < kTT; ++t) acc[t] = 0.0f;
-        const uint16_t* wrow = wg + (size_t)j * H + s * L;
-        const float* xseg = xs + s * LP;
-        for (int kk = 0; kk < L; kk += 8) {
-            float wf[8];
-            unpack_bf16x8(*reinterpret_cast<const uint4*>(wrow + kk), wf);
+    for (int e = 0; e < 4; ++e)
 #pragma unroll
-            for (int t = 0; t < kTT; ++t) {
-                const float4 xa = *reinterpret_cast<const float4*>(xseg + t * 8 * LP + kk);
-                const float4 xb = *reinterpret_cast<const float4*>(xseg + t * 8 * LP + kk + 4);
-                float a = acc[t];
-                a = __fmaf_rn(wf[0], xa.x, a);
-                a = __fmaf_rn(wf[1], xa.y, a);
-                a = __fmaf_rn(wf[2], xa.z, a);
-                a = __fmaf_rn(wf[3], xa.w, a);
-                a = __fmaf_rn(wf[4], xb.x, a);
-                a = __fmaf_rn(wf[5], xb.y, a);
-                a = __fmaf_rn(wf[6], xb.z, a);
-                a = __fmaf_rn(wf[7], xb.w, a);
-                acc[t] = a;
+        for (int t = 0; t < 8; ++t) acc[e][t] = 0.0f;
+    const float* xseg = xs + (tg * 8 * 8 + s) * LP;  // token tg*8 + t at xseg + t * 8 * LP
+    for (int kk = 0; kk < L; kk += 8) {
+        float wf[4][8];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+            const int j = eg + 16 * e;
+            if (j < E) {
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(wg + (size_t)j * H + s * L + kk), wf[e]);
+            } else {
+#pragma unroll
+                for (int q = 0; q < 8; ++q) wf[e][q] = 0.0f;
             }
         }
 #pragma unroll
-        for (int t = 0; t < kTT; ++t) segs[(t * 64 + j) * 8 + s] = acc[t];
+        for (int t = 0; t < 8; ++t) {
+            const float4 xa = *reinterpret_cast<const float4*>(xseg + t * 8 * LP + kk);
+            const float4 xb = *reinterpret_cast<const float4*>(xseg + t * 8 * LP + kk + 4);
+#pragma unroll
+            for (int e = 0; e < 4; ++e) {
+                float a = acc[e][t];
+                a = __fmaf_rn(wf[e][0], xa.x, a);
+                a = __fmaf_rn(wf[e][1], xa.y, a);
+                a = __fmaf_rn(wf[e][2], xa.z, a);
+                a = __fmaf_rn(wf[e][3], xa.w, a);
+                a = __fmaf_rn(wf[e][4], xb.x, a);
+                a = __fmaf_rn(wf[e][5], xb.y, a);
+                a = __fmaf_rn(wf[e][6], xb.z, a);
+                a = __fmaf_rn(wf[e][7], xb.w, a);
+                acc[e][t] = a;
+            }
+        }
+    }
+    __syncthreads();  // token rows consumed: the region becomes segs
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+        const int j = eg + 16 * e;
+#pragma unroll
+        for (int t = 0; t < 8; ++t) segs[((tg * 8 + t) * 64 + j) * 8 + s] = acc[e][t];
     }
     __syncthreads();
-    if (s == 0 && j < E) {
-        for (int t = 0; t < kTT; ++t) {
+    for (int i = tid; i < kTT * 64; i += kRouteThreads) {
+        const int t = i >> 6, j = i & 63;
+        if (j < E) {
             const float* sg = segs + (t * 64 + j) * 8;
             float total = sg[0];
 #pragma unroll
@@ -84,10 +111,8 @@ route_kernel(const float* __restrict__ x, int T, int H, const uint16_t* __restri
     }
     __syncthreads();
 
-    // softmax + top-k: warp w serves token w of the tile
-    const int warp = tid >> 5, lane = tid & 31;
-    if (warp < kTT && t0 + warp < T) {
-        const int t = warp;
+    // softmax + top-k: warp w serves tokens w and w + 8 of the tile
+    for (int t = warp; t < kTT && t0 + t < T; t += kRouteThreads / 32) {
         const bool v0 = lane < E, v1 = lane + 32 < E;
         const float l0 = v0 ? logits[t * 64 + lane] : -INFINITY;
         const float l1 = v1 ? logits[t * 64 + lane + 32] : -INFINITY;
@@ -125,17 +150,29 @@ route_kernel(const float* __restrict__ x, int T, int H, const uint16_t* __restri
 
 size_t route_smem_bytes(int tt, int H) {
     const int LP = H / 8 + 4;
-    return sizeof(float) * ((size_t)tt * 8 * LP + (size_t)tt * 64 * 8 + (size_t)tt * 64);
+    size_t region = (size_t)tt * 8 * LP;                    // token rows
+    if (region < (size_t)tt * 64 * 8) region = (size_t)tt * 64 * 8;  // or the segment partials
+    return sizeof(float) * (region + (size_t)tt * 64);
 }
 
 cudaError_t launch_route(const float* x, int T, int H, const uint16_t* wg, int E, const float* bias, int topk,
                          int32_t* ids, float* wts, cudaStream_t st) {
     if (T <= 0) return cudaSuccess;
-    constexpr int TT = 8;
-    const size_t smem = route_smem_bytes(TT, H);
-    cudaError_t err = ensure_smem_optin(reinterpret_cast<const void*>(route_kernel<TT>), smem);
+    int dev = 0, optin = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err == cudaSuccess) err = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     if (err != cudaSuccess) return err;
-    route_kernel<TT><<<(T + TT - 1) / TT, kRouteThreads, smem, st>>>(x, T, H, wg, E, bias, topk, ids, wts);
+    if (route_smem_bytes(16, H) <= (size_t)optin / 2) {
+        const size_t smem = route_smem_bytes(16, H);
+        err = ensure_smem_optin(reinterpret_cast<const void*>(route_kernel<2>), smem);
+        if (err != cudaSuccess) return err;
+        route_kernel<2><<<(T + 15) / 16, 256, smem, st>>>(x, T, H, wg, E, bias, topk, ids, wts);
+    } else {
+        const size_t smem = route_smem_bytes(8, H);
+        err = ensure_smem_optin(reinterpret_cast<const void*>(route_kernel<1>), smem);
+        if (err != cudaSuccess) return err;
+        route_kernel<1><<<(T + 7) / 8, 128, smem, st>>>(x, T, H, wg, E, bias, topk, ids, wts);
+    }
     return cudaGetLastError();
 }
 

@@ -16,10 +16,16 @@ forward:
 4. each rank applies its local experts to the rows it received, pre-weighted and summed per
    row (``uocr_moe_ep_experts``: the prefill's permute + tcgen05 grouped GEMMs);
 5. exchange the fp32 partial rows back; each token sums its partials in destination-rank order
-   (deterministic), then adds its shared experts (``uocr_moe_shared_forward``, data-parallel).
+   (deterministic), then adds the sum of its shared experts (``uocr_moe_shared_forward``,
+   data-parallel): out = (partial_0 + partial_1 + ...) + (shared_0 + shared_1).
 
-The bookkeeping (2, 3, 5) is plain torch and also runs on CPU ranks (gloo) for tests; the
-compute steps are CUDA only (``ExpertParallelMoE``).
+``ep_forward`` states the bookkeeping (2, 3, 5) in plain torch; it runs on CPU ranks (gloo) in
+the tests and is the reference the device path is checked against. ``ExpertParallelMoE`` runs
+CUDA only: the plan and the bf16 row gather are one library call (``uocr_moe_ep_dispatch``, no
+host round trip but the one D2H read of the exchanged row counts), the per-token sum of the
+partials is another (``uocr_moe_ep_combine``), and the shared experts run on a side stream while
+the rows are exchanged and the routed experts computed; the result is bit-identical to
+``ep_forward`` with the same compute steps.
 """
 
 from __future__ import annotations
@@ -114,8 +120,10 @@ def plan_dispatch(ids: torch.Tensor, wts: torch.Tensor, world: int, placement) -
     """Rows to send: one per (token, destination rank) with at least one expert there.
     ``placement``: an ExpertPlacement, or an int (experts per rank, contiguous ranges)."""
     owner, local = _as_placement(placement, world).owner_local(ids.device)
-    dest = owner[ids.long()]  # [T, k]
-    loc = local[ids.long()]
+    valid = ids >= 0  # id < 0: no expert in the slot
+    idx = torch.where(valid, ids.long(), torch.zeros_like(ids.long()))
+    dest = torch.where(valid, owner[idx], torch.full_like(idx, -1))  # [T, k]
+    loc = local[idx]
     orders, counts, metas_e, metas_w = [], [], [], []
     for p in range(world):
         on_p = dest == p
@@ -161,8 +169,8 @@ def ep_forward(x: torch.Tensor, route: Callable, local_experts: Callable, shared
     """One expert-parallel MoE forward of this rank's tokens x [T, H] fp32.
 
     route(x) -> (ids [T,k] int32 global, wts [T,k] fp32); local_experts(rows bf16 [N,H], meta_e,
-    meta_w) -> fp32 [N,H] (meta_e: local expert indices); shared(x, out) adds the shared experts
-    into out in place. placement: as for plan_dispatch.
+    meta_w) -> fp32 [N,H] (meta_e: local expert indices); shared(x, buf) adds the shared experts
+    into buf in place (given zeros). placement: as for plan_dispatch.
     """
     T, H = x.shape
     ids, wts = route(x)
@@ -176,8 +184,9 @@ def ep_forward(x: torch.Tensor, route: Callable, local_experts: Callable, shared
     part_in = local_experts(rows_in, meta_in[:, :k].contiguous(), meta_in[:, k:].contiguous().view(torch.float32))
     part = exchange_rows(part_in, recv_counts, plan.send_counts, group)
     out = sum_partials(T, H, plan, part)
-    shared(x, out)
-    return out
+    sh = torch.zeros_like(out)
+    shared(x, sh)
+    return out.add_(sh)  # routed + shared, the shared experts summed on their own first
 
 
 class ExpertParallelMoE:
@@ -189,7 +198,7 @@ class ExpertParallelMoE:
     """
 
     def __init__(self, config: MoEConfig, *, group=None, device: str | torch.device = "cuda",
-                 placement: ExpertPlacement | None = None) -> None:
+                 placement: ExpertPlacement | None = None, overlap_shared: bool = True) -> None:
         self.config = config
         self.group = group
         self.rank = dist.get_rank(group)
@@ -203,6 +212,7 @@ class ExpertParallelMoE:
                 any(len(v) != E // self.world for v in placement.experts):
             raise ValueError("ExpertParallelMoE: placement must give every rank E / world distinct experts")
         self.placement = placement
+        self.overlap_shared = overlap_shared
         self.e_local = E // self.world
         if self.e_local < config.num_experts_per_tok:
             raise ValueError("ExpertParallelMoE: fewer local experts than experts per token")
@@ -214,6 +224,10 @@ class ExpertParallelMoE:
         self.router: torch.Tensor | None = None
         self.bias: torch.Tensor | None = None
         self._ws: dict[str, torch.Tensor] = {}
+        self._bufs: dict[str, torch.Tensor] = {}
+        owner, local = placement.owner_local(self.device)
+        self._owner, self._local = owner.int().contiguous(), local.int().contiguous()
+        self._side = torch.cuda.Stream(self.device)
 
     def load_state_dict(self, state: Mapping[str, torch.Tensor]) -> "ExpertParallelMoE":
         mine = torch.tensor(self.placement.experts[self.rank], dtype=torch.int64)
@@ -235,6 +249,41 @@ class ExpertParallelMoE:
             self._ws[name] = ws
         return ws
 
+    def _buf(self, name: str, shape: tuple, dtype: torch.dtype) -> torch.Tensor:
+        """A persistent buffer (reused across calls: the stream order keeps uses apart)."""
+        n = 1
+        for d in shape:
+            n *= d
+        b = self._bufs.get(name)
+        if b is None or b.dtype != dtype or b.numel() < n:
+            b = torch.empty(max(n, 1), dtype=dtype, device=self.device)
+            self._bufs[name] = b
+        return b[:n].view(shape)
+
+    def _dispatch(self, x: torch.Tensor, ids: torch.Tensor, wts: torch.Tensor):
+        """(send_counts int64 [world] on the device, rows bf16, meta int32 [.., 2k], inv int32 [world, T])."""
+        T, H = x.shape
+        k, W = ids.shape[1], self.world
+        send = self._buf("send", (W,), torch.int64)
+        rows = self._buf("rows", (T * W, H), torch.bfloat16)
+        meta = self._buf("meta", (T * W, 2 * k), torch.int32)
+        inv = self._buf("inv", (W, T), torch.int32)
+        L = load()
+        ws = self._workspace("dispatch", L.uocr_moe_ep_dispatch_workspace_bytes(T, W))
+        check(L.uocr_moe_ep_dispatch(x.data_ptr(), T, H, ids.data_ptr(), wts.data_ptr(), k, self._owner.data_ptr(),
+                                     self._local.data_ptr(), self.config.n_routed_experts, W, send.data_ptr(),
+                                     rows.view(torch.int16).data_ptr(), meta.data_ptr(), inv.data_ptr(),
+                                     ws.data_ptr(), ws.numel(), torch.cuda.current_stream(self.device).cuda_stream))
+        return send, rows, meta, inv
+
+    def _combine(self, part: torch.Tensor, inv: torch.Tensor, add: torch.Tensor | None, T: int) -> torch.Tensor:
+        H = self.config.hidden_size
+        out = torch.empty((T, H), dtype=torch.float32, device=self.device)
+        check(load().uocr_moe_ep_combine(part.data_ptr(), part.shape[0], inv.data_ptr(), T, self.world, H,
+                                         0 if add is None else add.data_ptr(), out.data_ptr(),
+                                         torch.cuda.current_stream(self.device).cuda_stream))
+        return out
+
     def _route(self, x: torch.Tensor):
         return ops.route(x, self.router, self.bias, self.config.num_experts_per_tok)
 
@@ -251,19 +300,48 @@ class ExpertParallelMoE:
                                     torch.cuda.current_stream(self.device).cuda_stream))
         return out
 
-    def _shared(self, x: torch.Tensor, out: torch.Tensor) -> None:
+    def _shared(self, x: torch.Tensor, out: torch.Tensor, accumulate: int = 1) -> None:
         T = x.shape[0]
         if T == 0:
             return
         L = load()
         lay = ctypes.byref(self.local.layer)
         ws = self._workspace("shared", L.uocr_moe_shared_workspace_bytes(lay, T))
-        check(L.uocr_moe_shared_forward(lay, x.data_ptr(), T, out.data_ptr(), 1, ws.data_ptr(), ws.numel(),
+        check(L.uocr_moe_shared_forward(lay, x.data_ptr(), T, out.data_ptr(), accumulate, ws.data_ptr(), ws.numel(),
                                         torch.cuda.current_stream(self.device).cuda_stream))
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         """The MoE over this rank's tokens x [T, H] fp32 (a collective: every rank calls it)."""
         if not x.is_cuda or x.dtype != torch.float32 or x.dim() != 2 or x.shape[1] != self.config.hidden_size:
             raise ValueError("ExpertParallelMoE: x must be a CUDA fp32 [T, hidden] tensor")
+        x = x.contiguous()
+        T, H = x.shape
+        k, W, g = self.config.num_experts_per_tok, self.world, self.group
+        cur = torch.cuda.current_stream(self.device)
+        sh = self._buf("shared_out", (T, H), torch.float32)
+        if self.overlap_shared:
+            self._side.wait_stream(cur)
+            with torch.cuda.stream(self._side):
+                self._shared(x, sh, accumulate=0)
+        else:
+            self._shared(x, sh, accumulate=0)
+        ids, wts = self._route(x)
+        send, rows, meta, inv = self._dispatch(x, ids, wts)
+        recv = torch.empty_like(send)
+        dist.all_to_all_single(recv, send, group=g)
+        counts = torch.cat([send, recv]).tolist()  # the one host synchronisation
+        sc, rc = counts[:W], counts[W:]
+        ns = sum(sc)
+        rows_in = exchange_rows(rows[:ns], sc, rc, g)
+        meta_in = exchange_rows(meta[:ns], sc, rc, g)
+        part_in = self._local_experts(rows_in, meta_in[:, :k].contiguous(),
+                                      meta_in[:, k:].contiguous().view(torch.float32))
+        part = exchange_rows(part_in, rc, sc, g)
+        if self.overlap_shared:
+            cur.wait_stream(self._side)
+        return self._combine(part, inv, sh if T else None, T)
+
+    def forward_reference(self, x: torch.Tensor) -> torch.Tensor:
+        """The same layer through the torch bookkeeping of ``ep_forward`` (the device path's check)."""
         return ep_forward(x.contiguous(), self._route, self._local_experts, self._shared, self.world,
                           self.placement, self.group)
