@@ -4,13 +4,15 @@
 // then token) and the sum order of the combine (ascending source rank, from +0, then the
 // shared-expert term) are the ones ep.py's plan_dispatch / sum_partials state, bit for bit.
 //
-// Dispatch, two launches over chunks of kChunk tokens:
-//   count:  per token the bit mask of ranks that own one of its experts; per chunk and rank the
-//           number of tokens with that bit (warp ballots).
-//   gather: each CTA sums the chunk counts of all chunks (rank totals, hence each rank's first
-//           row) and of the chunks before it, ranks its tokens per destination with ballot
-//           prefixes, writes inv / meta, then copies its rows x fp32 -> bf16 (round to nearest
-//           even) with 16-byte stores. CTA 0 writes the per-rank row counts.
+// Dispatch, three launches:
+//   count:  (chunks of kChunk tokens) per token the bit mask of ranks that own one of its
+//           experts; per chunk and rank the number of tokens with that bit (warp ballots).
+//   plan:   (chunks) each CTA sums the chunk counts of all chunks (rank totals, hence each
+//           rank's first row) and of the chunks before it, ranks its tokens per destination with
+//           ballot prefixes and writes inv, meta and the row -> token map. CTA 0 writes the
+//           per-rank row counts.
+//   copy:   (8 SM-widths of CTAs, a warp per row) rows x fp32 -> bf16 (round to nearest even),
+//           16-byte stores.
 // HBM bytes: x read once per destination (the re-reads of a token's row hit L2), rows written
 // once: about T * H * 4 + rows * H * 2.
 #include "common.cuh"
@@ -52,16 +54,13 @@ ep_count_kernel(const int32_t* __restrict__ ids, int T, int k, const int32_t* __
 }
 
 __global__ void __launch_bounds__(kChunk)
-ep_gather_kernel(const float* __restrict__ x, int T, int H, const int32_t* __restrict__ ids,
+ep_plan_kernel(int T, const int32_t* __restrict__ ids,
                  const float* __restrict__ wts, int k, const int32_t* __restrict__ owner,
                  const int32_t* __restrict__ local, int E, int world, const uint8_t* __restrict__ masks,
                  const int32_t* __restrict__ counts, int nchunks, long long* __restrict__ send_counts,
-                 __nv_bfloat16* __restrict__ rows, int32_t* __restrict__ meta, int32_t* __restrict__ inv) {
+                 int32_t* __restrict__ order, int32_t* __restrict__ meta, int32_t* __restrict__ inv) {
     __shared__ int total[kEpMaxWorld], before[kEpMaxWorld], first[kEpMaxWorld];
     __shared__ int wpre[kChunk / 32][kEpMaxWorld];
-    __shared__ int list_row[kChunk * kEpMaxWorld];
-    __shared__ int list_tok[kChunk * kEpMaxWorld];
-    __shared__ int nlist;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int chunk = blockIdx.x;
 
@@ -88,7 +87,6 @@ ep_gather_kernel(const float* __restrict__ x, int T, int H, const int32_t* __res
         const unsigned b = __ballot_sync(0xffffffffu, (mask >> p) & 1u);
         if (lane == 0) wpre[warp][p] = __popc(b);
     }
-    if (threadIdx.x == 0) nlist = 0;
     __syncthreads();
     if (threadIdx.x < world) {
         int f = 0;
@@ -112,24 +110,46 @@ ep_gather_kernel(const float* __restrict__ x, int T, int H, const int32_t* __res
                     m[s] = mine ? local[e] : -1;
                     m[k + s] = mine ? __float_as_int(wts[(size_t)t * k + s]) : 0;
                 }
-                const int slot = atomicAdd(&nlist, 1);
-                list_row[slot] = row;
-                list_tok[slot] = t;
+                order[row] = t;
             }
             inv[(size_t)p * T + t] = row;
         }
     }
-    __syncthreads();
-    // rows: 8 elements (two float4 loads, one 16-byte store) per item
-    const int per_row = H / 8, n = nlist;
-    for (int i = threadIdx.x; i < n * per_row; i += kChunk) {
-        const int r = i / per_row, c = i - r * per_row;
-        const float* src = x + (size_t)list_tok[r] * H + 8 * c;
-        const float4 a = *reinterpret_cast<const float4*>(src);
-        const float4 b = *reinterpret_cast<const float4*>(src + 4);
-        __nv_bfloat162 o[4] = {__floats2bfloat162_rn(a.x, a.y), __floats2bfloat162_rn(a.z, a.w),
-                               __floats2bfloat162_rn(b.x, b.y), __floats2bfloat162_rn(b.z, b.w)};
-        *reinterpret_cast<uint4*>(rows + (size_t)list_row[r] * H + 8 * c) = *reinterpret_cast<uint4*>(o);
+}
+
+// rows[r] = bf16(x[order[r]]) for r < the total row count: one warp per row at a time, 8
+// elements (two float4 loads, one 16-byte store) per lane step, the loads of a lane's steps
+// issued together.
+__global__ void __launch_bounds__(256)
+ep_copy_rows_kernel(const float* __restrict__ x, int H, const long long* __restrict__ send_counts, int world,
+                    const int32_t* __restrict__ order, __nv_bfloat16* __restrict__ rows) {
+    long long n = 0;
+    for (int p = 0; p < world; ++p) n += send_counts[p];
+    const int lane = threadIdx.x & 31;
+    const int per_row = H / 8;
+    for (long long r = blockIdx.x * 8LL + (threadIdx.x >> 5); r < n; r += gridDim.x * 8LL) {
+        const float* src = x + (size_t)order[r] * H;
+        __nv_bfloat16* dst = rows + (size_t)r * H;
+        for (int c0 = 0; c0 < per_row; c0 += 32 * 4) {
+            float4 a[4], b[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int c = c0 + u * 32 + lane;
+                if (c < per_row) {
+                    a[u] = *reinterpret_cast<const float4*>(src + 8 * c);
+                    b[u] = *reinterpret_cast<const float4*>(src + 8 * c + 4);
+                }
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                const int c = c0 + u * 32 + lane;
+                if (c < per_row) {
+                    __nv_bfloat162 o[4] = {__floats2bfloat162_rn(a[u].x, a[u].y), __floats2bfloat162_rn(a[u].z, a[u].w),
+                                           __floats2bfloat162_rn(b[u].x, b[u].y), __floats2bfloat162_rn(b[u].z, b[u].w)};
+                    *reinterpret_cast<uint4*>(dst + 8 * c) = *reinterpret_cast<uint4*>(o);
+                }
+            }
+        }
     }
 }
 
@@ -164,9 +184,11 @@ __global__ void ep_combine_kernel(const float* __restrict__ part, long long nrow
 
 }  // namespace
 
+static size_t align256(size_t v) { return (v + 255) & ~(size_t)255; }
+
 size_t ep_dispatch_workspace_bytes(int T, int world) {
     const size_t nchunks = ((size_t)T + kChunk - 1) / kChunk;
-    return (((size_t)T + 255) & ~(size_t)255) + nchunks * world * sizeof(int32_t);
+    return align256((size_t)T) + align256(nchunks * world * sizeof(int32_t)) + (size_t)T * world * sizeof(int32_t);
 }
 
 cudaError_t launch_ep_dispatch(const float* x, int T, int H, const int32_t* ids, const float* wts, int k,
@@ -174,12 +196,23 @@ cudaError_t launch_ep_dispatch(const float* x, int T, int H, const int32_t* ids,
                                uint16_t* rows, int32_t* meta, int32_t* inv, void* ws, cudaStream_t st) {
     const int nchunks = (T + kChunk - 1) / kChunk;
     uint8_t* masks = reinterpret_cast<uint8_t*>(ws);
-    int32_t* counts = reinterpret_cast<int32_t*>(masks + (((size_t)T + 255) & ~(size_t)255));
+    int32_t* counts = reinterpret_cast<int32_t*>(masks + align256((size_t)T));
+    int32_t* order = reinterpret_cast<int32_t*>(reinterpret_cast<char*>(counts) +
+                                                align256((size_t)nchunks * world * sizeof(int32_t)));
     ep_count_kernel<<<nchunks, kChunk, 0, st>>>(ids, T, k, owner, E, world, masks, counts);
     cudaError_t err = cudaGetLastError();
     if (err != cudaSuccess) return err;
-    ep_gather_kernel<<<nchunks, kChunk, 0, st>>>(x, T, H, ids, wts, k, owner, local, E, world, masks, counts, nchunks,
-                                                 send_counts, reinterpret_cast<__nv_bfloat16*>(rows), meta, inv);
+    ep_plan_kernel<<<nchunks, kChunk, 0, st>>>(T, ids, wts, k, owner, local, E, world, masks, counts, nchunks,
+                                               send_counts, order, meta, inv);
+    err = cudaGetLastError();
+    if (err != cudaSuccess) return err;
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    const long long max_rows = (long long)T * world;
+    long long blocks = (max_rows + 7) / 8;
+    if (blocks > (long long)sms * 8) blocks = (long long)sms * 8;
+    ep_copy_rows_kernel<<<(unsigned)blocks, 256, 0, st>>>(x, H, send_counts, world, order,
+                                                          reinterpret_cast<__nv_bfloat16*>(rows));
     return cudaGetLastError();
 }
 

@@ -241,6 +241,18 @@ constexpr int kGemmThreads = 192;           // producer, MMA, 4 epilogue warps
 constexpr uint32_t kTmemCols = 512;         // two 256-column accumulators
 
 enum GemmEpi : int { kEpiSwiGLU = 0, kEpiF32 = 1 };
+constexpr uint32_t kPlanBytes = (sizeof(PrefillPlan) + 127) & ~127u;
+
+// byte offset of 16-byte chunk `ch` of row `row` in a 32 x 128-byte staging buffer
+UOCR_DEV uint32_t stage_off(int row, int ch) { return (uint32_t)row * 128u + ((uint32_t)(ch ^ (row & 7)) << 4); }
+UOCR_DEV void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
+    asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
+}
+UOCR_DEV uint4 ld_shared_v4(uint32_t addr) {
+    uint4 v;
+    asm volatile("ld.shared.v4.b32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w) : "r"(addr) : "memory");
+    return v;
+}
 
 struct GemmSmem {
     uint64_t full[kGStages], empty[kGStages], tfull[2], tempty[2], done;
@@ -282,6 +294,8 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     uint8_t* sB = smem + kGStages * kATile;
     GemmSmem* gs = reinterpret_cast<GemmSmem*>(smem + kGStages * (kATile + kBTile));
     PrefillPlan* P = reinterpret_cast<PrefillPlan*>(reinterpret_cast<uint8_t*>(gs) + 256);
+    // epilogue staging: 4 KB per epilogue warp (32 rows x 128 B, 16-byte chunks XOR-swizzled by row)
+    const uint32_t stage_base = smem_addr(reinterpret_cast<uint8_t*>(P) + kPlanBytes);
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     volatile int* abort_flag = &gs->abort_flag;
 
@@ -377,7 +391,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     } else {
         // ---------------- epilogue: warps 2..5 own TMEM lanes 32*(warp%4) .. +31 ----------------
         const int quarter = warp & 3;
-        const int row_in_tile = quarter * 32 + lane;
+        const uint32_t stage = stage_base + (uint32_t)(warp - 2) * 4096u;
         int acc = 0;
         uint32_t around = 0;
         for (int tile = blockIdx.x; tile < total; tile += gridDim.x) {
@@ -387,13 +401,14 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             if (!mbar_wait_warp(&gs->tfull[acc], around & 1, abort_flag, status)) break;
             tc_fence_after();
             const int rows_valid = min(kBM, G.rows - mloc * kBM);
-            const bool live = row_in_tile < rows_valid;
-            const size_t out_row = (size_t)G.out_base + (size_t)mloc * kBM + row_in_tile;
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)acc * kBN;
             if (kEpi == kEpiSwiGLU) {
                 // tile columns in groups of 16: 8 gate rows then the same 8 up rows, so columns
                 // [32c, 32c + 32) give h columns [16c, 16c + 16) of this tile's 128
-                uint16_t* h = reinterpret_cast<uint16_t*>(out) + out_row * out_ld + (size_t)n * (kBN / 2);
+                // rows leave through the warp's staging buffer: 32 rows x 128 B (four chunks of
+                // 16 h columns), then 16-byte stores of 4 whole 128-byte row segments each
+                const size_t tile_row0 = (size_t)G.out_base + (size_t)mloc * kBM + quarter * 32;
+                uint16_t* h0 = reinterpret_cast<uint16_t*>(out) + (size_t)n * (kBN / 2);
 #pragma unroll 1
                 for (int c = 0; c < kBN / 32; ++c) {
                     uint32_t r[32];
@@ -407,24 +422,42 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
                         const float u0 = __uint_as_float(r[c0 + 8]), u1 = __uint_as_float(r[c0 + 9]);
                         pk[i] = (uint32_t)f32_to_bf16_rne(silu(g0) * u0) | ((uint32_t)f32_to_bf16_rne(silu(g1) * u1) << 16);
                     }
-                    if (live) {
-                        *reinterpret_cast<uint4*>(h + c * 16) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                        *reinterpret_cast<uint4*>(h + c * 16 + 8) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                    const int q = 2 * (c & 3);
+                    st_shared_v4(stage + stage_off(lane, q), pk[0], pk[1], pk[2], pk[3]);
+                    st_shared_v4(stage + stage_off(lane, q + 1), pk[4], pk[5], pk[6], pk[7]);
+                    if ((c & 3) == 3) {
+                        __syncwarp();
+                        const int cg = c >> 2;  // 64 h columns per flush
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const int row = i * 4 + (lane >> 3), ch = lane & 7;
+                            const uint4 v = ld_shared_v4(stage + stage_off(row, ch));
+                            if (quarter * 32 + row < rows_valid)
+                                *reinterpret_cast<uint4*>(h0 + (tile_row0 + row) * out_ld + cg * 64 + ch * 8) = v;
+                        }
+                        __syncwarp();
                     }
                 }
             } else {
-                float* y = reinterpret_cast<float*>(out) + out_row * out_ld + (size_t)n * kBN;
+                const size_t tile_row0 = (size_t)G.out_base + (size_t)mloc * kBM + quarter * 32;
+                float* y0 = reinterpret_cast<float*>(out) + (size_t)n * kBN;
 #pragma unroll 1
                 for (int c = 0; c < kBN / 32; ++c) {
                     uint32_t r[32];
                     tmem_ld_32x32b_x32(taddr + c * 32, r);
                     tmem_wait_ld();
-                    if (live) {
 #pragma unroll
-                        for (int v = 0; v < 8; ++v)
-                            *reinterpret_cast<uint4*>(y + c * 32 + v * 4) =
-                                make_uint4(r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+                    for (int v = 0; v < 8; ++v)
+                        st_shared_v4(stage + stage_off(lane, v), r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
+                    __syncwarp();
+#pragma unroll
+                    for (int i = 0; i < 8; ++i) {
+                        const int row = i * 4 + (lane >> 3), ch = lane & 7;
+                        const uint4 v = ld_shared_v4(stage + stage_off(row, ch));
+                        if (quarter * 32 + row < rows_valid)
+                            *reinterpret_cast<uint4*>(y0 + (tile_row0 + row) * out_ld + c * 32 + ch * 4) = v;
                     }
+                    __syncwarp();
                 }
             }
             tc_fence_before();
@@ -487,7 +520,7 @@ static bool make_map_bf16_blocks(CUtensorMap* m, const void* base, uint64_t nrb,
 }
 
 size_t gemm_smem_bytes() {
-    return 1024 + kGStages * (kATile + kBTile) + 256 + sizeof(PrefillPlan);
+    return 1024 + kGStages * (kATile + kBTile) + 256 + kPlanBytes + 4 * 4096;
 }
 
 static cudaError_t launch_gemm(int epi, const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& Bs,

@@ -20,6 +20,40 @@
 
 namespace uocr {
 
+// Softmax over the token's logits (lane l holds experts l and l + 32, v0 / v1 = they exist) and
+// greedy top-k by (probability desc, index asc); lane 0 writes ids / weights.
+__device__ __forceinline__ void softmax_topk_warp(float l0, float l1, bool v0, bool v1, int topk, int lane,
+                                                  int32_t* __restrict__ ids_row, float* __restrict__ wts_row) {
+    float m = fmaxf(l0, l1);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
+    const float e0 = v0 ? uocr_exp(__fsub_rn(l0, m)) : 0.0f;
+    const float e1 = v1 ? uocr_exp(__fsub_rn(l1, m)) : 0.0f;
+    float sum = __fadd_rn(e0, e1);
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, off));
+    float p0 = v0 ? __fdiv_rn(e0, sum) : -1.0f;
+    float p1 = v1 ? __fdiv_rn(e1, sum) : -1.0f;
+    for (int r = 0; r < topk; ++r) {
+        // lane-local best: lower index (lane) wins a tie with lane + 32
+        float bp = p0;
+        int bi = lane;
+        if (p1 > bp) { bp = p1; bi = lane + 32; }
+#pragma unroll
+        for (int off = 16; off >= 1; off >>= 1) {
+            const float op = __shfl_xor_sync(0xffffffffu, bp, off);
+            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+            if (op > bp || (op == bp && oi < bi)) { bp = op; bi = oi; }
+        }
+        if (bi == lane) p0 = -2.0f;
+        if (bi == lane + 32) p1 = -2.0f;
+        if (lane == 0) {
+            ids_row[r] = bi;
+            wts_row[r] = bp;
+        }
+    }
+}
+
 // kTG token groups of 8 (2; 1 when the hidden size leaves too little shared memory)
 template <int kTG>
 __global__ void __launch_bounds__(128 * kTG, 2)
@@ -38,15 +72,18 @@ route_kernel(const float* __restrict__ x, int T, int H, const uint16_t* __restri
     const int tid = threadIdx.x;
     const int t0 = blockIdx.x * kTT;
 
-    // stage the token rows (zeros past T), 16-byte loads
+    // stage the token rows (zeros past T): 16-byte cp.async copies, all in flight at once
     const int H4 = H / 4, L4 = L / 4;
     for (int i = tid; i < kTT * H4; i += kRouteThreads) {
         const int t = i / H4, k4 = i - t * H4;
         const int s = k4 / L4, kk4 = k4 - s * L4;
-        const float4 v = (t0 + t < T) ? *reinterpret_cast<const float4*>(x + (size_t)(t0 + t) * H + 4 * k4)
-                                      : make_float4(0.f, 0.f, 0.f, 0.f);
-        *reinterpret_cast<float4*>(xs + (t * 8 + s) * LP + 4 * kk4) = v;
+        const bool live = t0 + t < T;
+        const float* src = live ? x + (size_t)(t0 + t) * H + 4 * k4 : x;
+        const uint32_t dst = (uint32_t)__cvta_generic_to_shared(xs + (t * 8 + s) * LP + 4 * kk4);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(dst), "l"(src), "r"(live ? 16 : 0)
+                     : "memory");
     }
+    asm volatile("cp.async.wait_all;\n" ::: "memory");
     __syncthreads();
 
     const int lane = tid & 31, warp = tid >> 5;
@@ -116,36 +153,136 @@ route_kernel(const float* __restrict__ x, int T, int H, const uint16_t* __restri
         const bool v0 = lane < E, v1 = lane + 32 < E;
         const float l0 = v0 ? logits[t * 64 + lane] : -INFINITY;
         const float l1 = v1 ? logits[t * 64 + lane + 32] : -INFINITY;
-        float m = fmaxf(l0, l1);
+        softmax_topk_warp(l0, l1, v0, v1, topk, lane, ids_out + (size_t)(t0 + t) * topk, wts_out + (size_t)(t0 + t) * topk);
+    }
+}
+
+// Persistent variant for hidden sizes whose router fits in shared memory (H <= 1336): the CTA
+// stages the whole router once, rows padded by 16 bytes (a warp's 32 rows at one K offset fall in
+// distinct banks), then walks tiles of kRT tokens. Warp w owns segment s = w; lane l owns experts
+// l and l + 32, for the tile's kRT tokens (8 chains). Token rows arrive by cp.async one tile
+// ahead (issued after the barrier that retires the buffer's previous tile); the segment partials
+// of a tile go to one of two buffers, and after the next barrier warp t < kRT finishes token t
+// (sum of the 8 partials, bias, softmax, top-k) while the others compute. One barrier per tile.
+constexpr int kRT = 4;
+
+UOCR_DEV void route_stage_tokens(const float* __restrict__ x, int T, int H, int t0, float* dst, int tid) {
+    const int H4 = H / 4;
+    for (int i = tid; i < kRT * H4; i += 256) {
+        const int t = i / H4;
+        const bool live = t0 + t < T;
+        const float* src = live ? x + (size_t)(t0 + t) * H + 4 * (i - t * H4) : x;
+        const uint32_t d = (uint32_t)__cvta_generic_to_shared(dst + 4 * i);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(live ? 16 : 0) : "memory");
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+}
+
+__global__ void __launch_bounds__(256, 1)
+route_smem_kernel(const float* __restrict__ x, int T, int H, const uint16_t* __restrict__ wg, int E,
+                  const float* __restrict__ bias, int topk, int32_t* __restrict__ ids_out, float* __restrict__ wts_out) {
+    extern __shared__ __align__(16) unsigned char rsm[];
+    const int RS = H + 8;  // router row stride in bf16 elements
+    uint16_t* wr = reinterpret_cast<uint16_t*>(rsm);                            // [64][RS]
+    float* xs = reinterpret_cast<float*>(rsm + (size_t)64 * RS * 2);            // [2][kRT][H]
+    float* segs = xs + 2 * kRT * H;                                             // [2][kRT][64][8]
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int L = H / 8;
+    const int ntiles = (T + kRT - 1) / kRT;
+
+    // router rows (zeros for j >= E), 16-byte copies
+    const int H8 = H / 8;
+    for (int i = tid; i < 64 * H8; i += 256) {
+        const int j = i / H8, c = i - j * H8;
+        const bool live = j < E;
+        const uint16_t* src = live ? wg + (size_t)j * H + 8 * c : wg;
+        const uint32_t d = (uint32_t)__cvta_generic_to_shared(wr + (size_t)j * RS + 8 * c);
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(live ? 16 : 0) : "memory");
+    }
+    asm volatile("cp.async.commit_group;\n" ::: "memory");
+    int tile = blockIdx.x;
+    if (tile < ntiles) route_stage_tokens(x, T, H, tile * kRT, xs, tid);
+
+    const int s = warp;
+    const uint16_t* w0 = wr + (size_t)lane * RS + s * L;
+    const uint16_t* w1 = wr + (size_t)(lane + 32) * RS + s * L;
+    int buf = 0, prev_t0 = -1;
+    for (; tile < ntiles; tile += gridDim.x, buf ^= 1) {
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+        // this tile's token rows (and, first time, the router) are in place; every warp is done
+        // with the other token buffer and has written the previous tile's partials
+        __syncthreads();
+        const int next = tile + gridDim.x;
+        if (next < ntiles) route_stage_tokens(x, T, H, next * kRT, xs + (buf ^ 1) * kRT * H, tid);
+        // finish the previous tile
+        if (prev_t0 >= 0 && warp < kRT && prev_t0 + warp < T) {
+            const float* sg = segs + ((buf ^ 1) * kRT + warp) * 64 * 8;
+            const bool v0 = lane < E, v1 = lane + 32 < E;
+            float l0 = sg[lane * 8], l1 = sg[(lane + 32) * 8];
 #pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, off));
-        const float e0 = v0 ? uocr_exp(__fsub_rn(l0, m)) : 0.0f;
-        const float e1 = v1 ? uocr_exp(__fsub_rn(l1, m)) : 0.0f;
-        float sum = __fadd_rn(e0, e1);
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, off));
-        float p0 = v0 ? __fdiv_rn(e0, sum) : -1.0f;
-        float p1 = v1 ? __fdiv_rn(e1, sum) : -1.0f;
-        const size_t row = (size_t)(t0 + t) * topk;
-        for (int r = 0; r < topk; ++r) {
-            // lane-local best: lower index (lane) wins a tie with lane + 32
-            float bp = p0;
-            int bi = lane;
-            if (p1 > bp) { bp = p1; bi = lane + 32; }
-#pragma unroll
-            for (int off = 16; off >= 1; off >>= 1) {
-                const float op = __shfl_xor_sync(0xffffffffu, bp, off);
-                const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-                if (op > bp || (op == bp && oi < bi)) { bp = op; bi = oi; }
+            for (int q = 1; q < 8; ++q) {
+                l0 = __fadd_rn(l0, sg[lane * 8 + q]);
+                l1 = __fadd_rn(l1, sg[(lane + 32) * 8 + q]);
             }
-            if (bi == lane) p0 = -2.0f;
-            if (bi == lane + 32) p1 = -2.0f;
-            if (lane == 0) {
-                ids_out[row + r] = bi;
-                wts_out[row + r] = bp;
+            if (bias) {
+                if (v0) l0 = __fadd_rn(l0, bias[lane]);
+                if (v1) l1 = __fadd_rn(l1, bias[lane + 32]);
+            }
+            softmax_topk_warp(v0 ? l0 : -INFINITY, v1 ? l1 : -INFINITY, v0, v1, topk, lane,
+                              ids_out + (size_t)(prev_t0 + warp) * topk, wts_out + (size_t)(prev_t0 + warp) * topk);
+        }
+        const float* xt = xs + buf * kRT * H + s * L;
+        float acc0[kRT], acc1[kRT];
+#pragma unroll
+        for (int t = 0; t < kRT; ++t) acc0[t] = acc1[t] = 0.0f;
+        for (int kk = 0; kk < L; kk += 8) {
+            float a[8], b[8];
+            unpack_bf16x8(*reinterpret_cast<const uint4*>(w0 + kk), a);
+            unpack_bf16x8(*reinterpret_cast<const uint4*>(w1 + kk), b);
+#pragma unroll
+            for (int t = 0; t < kRT; ++t) {
+                const float4 xa = *reinterpret_cast<const float4*>(xt + t * H + kk);
+                const float4 xb = *reinterpret_cast<const float4*>(xt + t * H + kk + 4);
+                const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+                float u = acc0[t], v = acc1[t];
+#pragma unroll
+                for (int q = 0; q < 8; ++q) {
+                    u = __fmaf_rn(a[q], xv[q], u);
+                    v = __fmaf_rn(b[q], xv[q], v);
+                }
+                acc0[t] = u;
+                acc1[t] = v;
             }
         }
+        float* so = segs + buf * kRT * 64 * 8;
+#pragma unroll
+        for (int t = 0; t < kRT; ++t) {
+            so[(t * 64 + lane) * 8 + s] = acc0[t];
+            so[(t * 64 + lane + 32) * 8 + s] = acc1[t];
+        }
+        prev_t0 = tile * kRT;
     }
+    __syncthreads();
+    if (prev_t0 >= 0 && warp < kRT && prev_t0 + warp < T) {
+        const float* sg = segs + ((buf ^ 1) * kRT + warp) * 64 * 8;
+        const bool v0 = lane < E, v1 = lane + 32 < E;
+        float l0 = sg[lane * 8], l1 = sg[(lane + 32) * 8];
+#pragma unroll
+        for (int q = 1; q < 8; ++q) {
+            l0 = __fadd_rn(l0, sg[lane * 8 + q]);
+            l1 = __fadd_rn(l1, sg[(lane + 32) * 8 + q]);
+        }
+        if (bias) {
+            if (v0) l0 = __fadd_rn(l0, bias[lane]);
+            if (v1) l1 = __fadd_rn(l1, bias[lane + 32]);
+        }
+        softmax_topk_warp(v0 ? l0 : -INFINITY, v1 ? l1 : -INFINITY, v0, v1, topk, lane,
+                          ids_out + (size_t)(prev_t0 + warp) * topk, wts_out + (size_t)(prev_t0 + warp) * topk);
+    }
+}
+
+size_t route_persistent_smem_bytes(int H) {
+    return (size_t)64 * (H + 8) * 2 + (size_t)2 * kRT * H * 4 + (size_t)2 * kRT * 64 * 8 * 4;
 }
 
 size_t route_smem_bytes(int tt, int H) {
@@ -162,7 +299,16 @@ cudaError_t launch_route(const float* x, int T, int H, const uint16_t* wg, int E
     cudaError_t err = cudaGetDevice(&dev);
     if (err == cudaSuccess) err = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     if (err != cudaSuccess) return err;
-    if (route_smem_bytes(16, H) <= (size_t)optin / 2) {
+    const size_t psmem = route_persistent_smem_bytes(H);
+    if (psmem <= (size_t)optin) {
+        int sms = 148;
+        err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        if (err != cudaSuccess) return err;
+        err = ensure_smem_optin(reinterpret_cast<const void*>(route_smem_kernel), psmem);
+        if (err != cudaSuccess) return err;
+        const int ntiles = (T + kRT - 1) / kRT;
+        route_smem_kernel<<<ntiles < sms ? ntiles : sms, 256, psmem, st>>>(x, T, H, wg, E, bias, topk, ids, wts);
+    } else if (route_smem_bytes(16, H) <= (size_t)optin / 2) {
         const size_t smem = route_smem_bytes(16, H);
         err = ensure_smem_optin(reinterpret_cast<const void*>(route_kernel<2>), smem);
         if (err != cudaSuccess) return err;

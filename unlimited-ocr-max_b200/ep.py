@@ -24,8 +24,8 @@ the tests and is the reference the device path is checked against. ``ExpertParal
 CUDA only: the plan and the bf16 row gather are one library call (``uocr_moe_ep_dispatch``, no
 host round trip but the one D2H read of the exchanged row counts), the per-token sum of the
 partials is another (``uocr_moe_ep_combine``), and the shared experts run on a side stream while
-the rows are exchanged and the routed experts computed; the result is bit-identical to
-``ep_forward`` with the same compute steps.
+the rows are exchanged; the result is bit-identical to ``ep_forward`` with the same compute
+steps.
 """
 
 from __future__ import annotations
@@ -319,14 +319,15 @@ class ExpertParallelMoE:
         k, W, g = self.config.num_experts_per_tok, self.world, self.group
         cur = torch.cuda.current_stream(self.device)
         sh = self._buf("shared_out", (T, H), torch.float32)
+        ids, wts = self._route(x)
+        send, rows, meta, inv = self._dispatch(x, ids, wts)
+        # the shared experts overlap the exchanges (NCCL leaves most SMs free) or run in line
         if self.overlap_shared:
             self._side.wait_stream(cur)
             with torch.cuda.stream(self._side):
                 self._shared(x, sh, accumulate=0)
         else:
             self._shared(x, sh, accumulate=0)
-        ids, wts = self._route(x)
-        send, rows, meta, inv = self._dispatch(x, ids, wts)
         recv = torch.empty_like(send)
         dist.all_to_all_single(recv, send, group=g)
         counts = torch.cat([send, recv]).tolist()  # the one host synchronisation
