@@ -26,6 +26,11 @@
 #include <mutex>
 
 #include "common.cuh"
+
+#include <cuda_bf16.h>
+
+#include <cstdlib>
+#include <cstring>
 #include "kernels.h"
 #include "layout.h"
 #include "sm100.cuh"
@@ -283,6 +288,74 @@ UOCR_DEV bool gwait(uint64_t* bar, uint32_t parity, volatile int* abort_flag, ui
     return true;
 }
 
+// Epilogue of one 128 x kBN accumulator (TMEM columns from `taddr`, this warp's 32 lanes): the
+// SwiGLU pairs to bf16 h, or the fp32 y, for the tile's rows below rows_valid.
+// SiLU for the GEMM1 epilogue: a / (1 + e^-a) with the fast exponential and division intrinsics
+// (h is rounded to bf16 right after; the limits hold: e^-a = inf gives -0, e^-a = 0 gives a).
+UOCR_DEV float silu_fast(float a) { return __fdividef(a, 1.0f + __expf(-a)); }
+
+// Epilogue of one 128 x kBN accumulator (TMEM columns from `taddr`, this warp's 32 lanes): the
+// SwiGLU pairs to bf16 h, or the fp32 y, for the tile's rows below rows_valid. The TMEM load of
+// chunk c + 1 is in flight while chunk c is processed. Rows leave through the warp's staging
+// buffer (32 rows x 128 B, chunks XOR-swizzled by row) as 16-byte stores covering 4 whole
+// 128-byte row segments per instruction.
+template <int kEpi>
+UOCR_DEV void gemm_epilogue_tile(uint32_t taddr, const PrefillGroup& G, int mloc, int n, int rows_valid, void* out,
+                                 int out_ld, uint32_t stage, int quarter, int lane) {
+    constexpr int kChunks = kBN / 32;
+    const size_t tile_row0 = (size_t)G.out_base + (size_t)mloc * kBM + quarter * 32;
+    uint32_t r[2][32];
+    tmem_ld_32x32b_x32(taddr, r[0]);
+#pragma unroll
+    for (int c = 0; c < kChunks; ++c) {
+        tmem_wait_ld_tie(r[c & 1]);
+        if (c + 1 < kChunks) tmem_ld_32x32b_x32(taddr + (c + 1) * 32, r[(c + 1) & 1]);
+        const uint32_t* rc = r[c & 1];
+        if (kEpi == kEpiSwiGLU) {
+            // tile columns in groups of 16: 8 gate rows then the same 8 up rows, so columns
+            // [32c, 32c + 32) give h columns [16c, 16c + 16) of this tile's 128
+            uint32_t pk[8];
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int c0 = (2 * i) / 8 * 16 + (2 * i) % 8;  // gate column of h column 2i
+                const float g0 = __uint_as_float(rc[c0]), g1 = __uint_as_float(rc[c0 + 1]);
+                const float u0 = __uint_as_float(rc[c0 + 8]), u1 = __uint_as_float(rc[c0 + 9]);
+                const __nv_bfloat162 hv = __floats2bfloat162_rn(silu_fast(g0) * u0, silu_fast(g1) * u1);
+                pk[i] = *reinterpret_cast<const uint32_t*>(&hv);
+            }
+            const int q = 2 * (c & 3);
+            st_shared_v4(stage + stage_off(lane, q), pk[0], pk[1], pk[2], pk[3]);
+            st_shared_v4(stage + stage_off(lane, q + 1), pk[4], pk[5], pk[6], pk[7]);
+            if ((c & 3) == 3) {
+                __syncwarp();
+                uint16_t* h0 = reinterpret_cast<uint16_t*>(out) + (size_t)n * (kBN / 2) + (c >> 2) * 64;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int row = i * 4 + (lane >> 3), ch = lane & 7;
+                    const uint4 v = ld_shared_v4(stage + stage_off(row, ch));
+                    if (quarter * 32 + row < rows_valid)
+                        *reinterpret_cast<uint4*>(h0 + (tile_row0 + row) * out_ld + ch * 8) = v;
+                }
+                __syncwarp();
+            }
+        } else {
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+                st_shared_v4(stage + stage_off(lane, v), rc[4 * v], rc[4 * v + 1], rc[4 * v + 2], rc[4 * v + 3]);
+            __syncwarp();
+            float* y0 = reinterpret_cast<float*>(out) + (size_t)n * kBN + c * 32;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const int row = i * 4 + (lane >> 3), ch = lane & 7;
+                const uint4 v = ld_shared_v4(stage + stage_off(row, ch));
+                if (quarter * 32 + row < rows_valid)
+                    *reinterpret_cast<uint4*>(y0 + (tile_row0 + row) * out_ld + ch * 4) = v;
+            }
+            __syncwarp();
+        }
+    }
+}
+
 template <int kEpi>
 __global__ void __launch_bounds__(kGemmThreads, 1)
 grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
@@ -402,64 +475,7 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
             tc_fence_after();
             const int rows_valid = min(kBM, G.rows - mloc * kBM);
             const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)acc * kBN;
-            if (kEpi == kEpiSwiGLU) {
-                // tile columns in groups of 16: 8 gate rows then the same 8 up rows, so columns
-                // [32c, 32c + 32) give h columns [16c, 16c + 16) of this tile's 128
-                // rows leave through the warp's staging buffer: 32 rows x 128 B (four chunks of
-                // 16 h columns), then 16-byte stores of 4 whole 128-byte row segments each
-                const size_t tile_row0 = (size_t)G.out_base + (size_t)mloc * kBM + quarter * 32;
-                uint16_t* h0 = reinterpret_cast<uint16_t*>(out) + (size_t)n * (kBN / 2);
-#pragma unroll 1
-                for (int c = 0; c < kBN / 32; ++c) {
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(taddr + c * 32, r);
-                    tmem_wait_ld();
-                    uint32_t pk[8];
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const int c0 = (2 * i) / 8 * 16 + (2 * i) % 8;  // gate column of h column 2i
-                        const float g0 = __uint_as_float(r[c0]), g1 = __uint_as_float(r[c0 + 1]);
-                        const float u0 = __uint_as_float(r[c0 + 8]), u1 = __uint_as_float(r[c0 + 9]);
-                        pk[i] = (uint32_t)f32_to_bf16_rne(silu(g0) * u0) | ((uint32_t)f32_to_bf16_rne(silu(g1) * u1) << 16);
-                    }
-                    const int q = 2 * (c & 3);
-                    st_shared_v4(stage + stage_off(lane, q), pk[0], pk[1], pk[2], pk[3]);
-                    st_shared_v4(stage + stage_off(lane, q + 1), pk[4], pk[5], pk[6], pk[7]);
-                    if ((c & 3) == 3) {
-                        __syncwarp();
-                        const int cg = c >> 2;  // 64 h columns per flush
-#pragma unroll
-                        for (int i = 0; i < 8; ++i) {
-                            const int row = i * 4 + (lane >> 3), ch = lane & 7;
-                            const uint4 v = ld_shared_v4(stage + stage_off(row, ch));
-                            if (quarter * 32 + row < rows_valid)
-                                *reinterpret_cast<uint4*>(h0 + (tile_row0 + row) * out_ld + cg * 64 + ch * 8) = v;
-                        }
-                        __syncwarp();
-                    }
-                }
-            } else {
-                const size_t tile_row0 = (size_t)G.out_base + (size_t)mloc * kBM + quarter * 32;
-                float* y0 = reinterpret_cast<float*>(out) + (size_t)n * kBN;
-#pragma unroll 1
-                for (int c = 0; c < kBN / 32; ++c) {
-                    uint32_t r[32];
-                    tmem_ld_32x32b_x32(taddr + c * 32, r);
-                    tmem_wait_ld();
-#pragma unroll
-                    for (int v = 0; v < 8; ++v)
-                        st_shared_v4(stage + stage_off(lane, v), r[4 * v], r[4 * v + 1], r[4 * v + 2], r[4 * v + 3]);
-                    __syncwarp();
-#pragma unroll
-                    for (int i = 0; i < 8; ++i) {
-                        const int row = i * 4 + (lane >> 3), ch = lane & 7;
-                        const uint4 v = ld_shared_v4(stage + stage_off(row, ch));
-                        if (quarter * 32 + row < rows_valid)
-                            *reinterpret_cast<uint4*>(y0 + (tile_row0 + row) * out_ld + c * 32 + ch * 4) = v;
-                    }
-                    __syncwarp();
-                }
-            }
+            gemm_epilogue_tile<kEpi>(taddr, G, mloc, n, rows_valid, out, out_ld, stage, quarter, lane);
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive(&gs->tempty[acc]);
@@ -470,6 +486,182 @@ grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_consta
     if (warp == 1) {
         tc_fence_after();
         tmem_dealloc(tmem_base, kTmemCols);
+    }
+}
+
+// ---- CTA-pair variant: 256 x 256 tiles on tcgen05.mma.cta_group::2 -------------------------
+// A cluster of two CTAs computes a pair tile: m-tiles 2p (CTA 0) and 2p + 1 (CTA 1) of one group
+// against a 256-column slice of its weights. Each CTA stages its own 128 A rows and its half
+// (128 rows) of the B slice per K step, 32 KB instead of the single-CTA kernel's 48 KB for the
+// same flops per CTA, so six stages fit. Both CTAs' TMA loads complete on CTA 0's `full`
+// barrier (CTA 0 expects the bytes of both); CTA 0's MMA thread issues the pair MMAs and
+// commits to the `empty` / `tfull` barriers of both CTAs. Each CTA drains its own accumulator
+// (its 128 rows, all 256 columns) and arrives on CTA 0's `tempty` (8 arrivals: 4 warps x 2
+// CTAs). A group with an odd number of m-tiles leaves the second CTA of its last pair tile
+// without rows: it computes and discards them. Every wait is bounded; every path reaches the
+// closing cluster barrier.
+constexpr int kPStages = 6;
+constexpr uint32_t kBHalfTile = 128 * kBK * 2;  // 16 KB
+
+struct PairSmem {
+    uint64_t full[kPStages], empty[kPStages], tfull[2], tempty[2], done;
+    uint32_t tmem_base;
+    int abort_flag;
+    int pair_prefix[kPrefillMaxGroups + 1];
+};
+
+UOCR_DEV void pair_decode_tile(const int* pp, int NT, int tile, int& g, int& mp, int& n) {
+    const int pt = tile / NT;
+    n = tile - pt * NT;
+    g = 0;
+    while (pp[g + 1] <= pt) ++g;
+    mp = pt - pp[g];
+}
+
+template <int kEpi>
+__global__ void __launch_bounds__(kGemmThreads, 1)
+grouped_gemm_pair_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                         const __grid_constant__ CUtensorMap tmBs, const PrefillPlan* __restrict__ plan_g, int NT,
+                         int KT, int b_rows_per_group, void* __restrict__ out, int out_ld, uint32_t* status) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* sA = smem;
+    uint8_t* sB = smem + kPStages * kATile;
+    PairSmem* ps = reinterpret_cast<PairSmem*>(smem + kPStages * (kATile + kBHalfTile));
+    PrefillPlan* P = reinterpret_cast<PrefillPlan*>(reinterpret_cast<uint8_t*>(ps) + ((sizeof(PairSmem) + 127) & ~127u));
+    const uint32_t stage_base = smem_addr(reinterpret_cast<uint8_t*>(P) + kPlanBytes);
+    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+    const uint32_t rank = cluster_ctarank();
+    const bool leader = rank == 0;
+    const int cid = blockIdx.x >> 1, ncl = gridDim.x >> 1;
+    volatile int* abort_flag = &ps->abort_flag;
+
+    for (int i = tid; i < (int)(sizeof(PrefillPlan) / 4); i += blockDim.x)
+        reinterpret_cast<int*>(P)[i] = reinterpret_cast<const int*>(plan_g)[i];
+    __syncthreads();
+    if (tid == 0) {
+        for (int st = 0; st < kPStages; ++st) {
+            mbar_init(&ps->full[st], 1);
+            mbar_init(&ps->empty[st], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&ps->tfull[a], 1);
+            mbar_init(&ps->tempty[a], 8);
+        }
+        mbar_init(&ps->done, 1);
+        ps->abort_flag = 0;
+        ps->pair_prefix[0] = 0;
+        for (int g = 0; g < P->ngroups; ++g)
+            ps->pair_prefix[g + 1] = ps->pair_prefix[g] + (P->mtile_prefix[g + 1] - P->mtile_prefix[g] + 1) / 2;
+        fence_mbar_init();
+        tma_prefetch_desc(&tmA);
+        tma_prefetch_desc(&tmB);
+        tma_prefetch_desc(&tmBs);
+    }
+    if (warp == 1) tmem_alloc_pair(&ps->tmem_base, kTmemCols);
+    tc_fence_before();
+    __syncthreads();
+    cluster_sync_all();  // both CTAs' barriers are initialised before any cross-CTA arrival
+    tc_fence_after();
+    const uint32_t tmem_base = ps->tmem_base;
+    const int total = ps->pair_prefix[P->ngroups] * NT;
+
+    if (warp == 0) {
+        if (lane == 0) {
+            // ---------------- TMA producer (both CTAs) ----------------
+            int s = 0;
+            uint32_t round = 0;
+            for (int tile = cid; tile < total && !*abort_flag; tile += ncl) {
+                int g, mp, n;
+                pair_decode_tile(ps->pair_prefix, NT, tile, g, mp, n);
+                const PrefillGroup& G = P->g[g];
+                const int a_row = G.a_base + (2 * mp + (int)rank) * kBM;
+                const int b_rb = (G.wrow0 * b_rows_per_group + n * kBN) / kRowBlock + (int)rank;
+                const CUtensorMap* mb = G.shared ? &tmBs : &tmB;
+                bool ok = true;
+                for (int kt = 0; kt < KT; ++kt) {
+                    if (round > 0 && !gwait(&ps->empty[s], (round - 1) & 1, abort_flag, status)) { ok = false; break; }
+                    if (leader) mbar_arrive_expect_tx(&ps->full[s], 2 * (kATile + kBHalfTile));
+                    const uint32_t lf = mapa_shared(smem_addr(&ps->full[s]), 0);
+                    tma_load_2d_pair(sA + s * kATile, &tmA, kt * kBK, a_row, lf);
+                    tma_load_4d_pair(sB + s * kBHalfTile, mb, 0, 0, kt, b_rb, lf);
+                    if (++s == kPStages) { s = 0; ++round; }
+                }
+                if (!ok) break;
+            }
+            if (leader) {
+                // every copy counted on CTA 0's barriers (both CTAs') has landed before exit
+                for (int i = 0; i < kPStages; ++i) {
+                    int ss = s - 1 - i;
+                    uint32_t rr = round;
+                    if (ss < 0) { ss += kPStages; if (rr == 0) break; --rr; }
+                    mbar_wait(&ps->full[ss], rr & 1, status);
+                }
+            }
+        }
+        __syncwarp();
+    } else if (warp == 1) {
+        if (leader && lane == 0) {
+            // ---------------- pair MMA issuer (CTA 0) ----------------
+            constexpr uint32_t idesc = umma_idesc_bf16(2 * kBM, kBN);
+            int s = 0, acc = 0;
+            uint32_t round = 0, around = 0;
+            bool issued = false;
+            for (int tile = cid; tile < total && !*abort_flag; tile += ncl) {
+                if (around > 0 && !gwait(&ps->tempty[acc], (around - 1) & 1, abort_flag, status)) break;
+                tc_fence_after();
+                const uint32_t tmem_d = tmem_base + (uint32_t)acc * kBN;
+                bool ok = true;
+                for (int kt = 0; kt < KT; ++kt) {
+                    if (!gwait(&ps->full[s], round & 1, abort_flag, status)) { ok = false; break; }
+                    tc_fence_after();
+                    const uint64_t ad = umma_desc_sw128(smem_addr(sA + s * kATile));
+                    const uint64_t bd = umma_desc_sw128(smem_addr(sB + s * kBHalfTile));
+#pragma unroll
+                    for (int kk = 0; kk < kBK / 16; ++kk)
+                        umma_f16_pair(tmem_d, ad + 2 * kk, bd + 2 * kk, idesc, (kt | kk) != 0 ? 1u : 0u);
+                    issued = true;
+                    umma_commit_pair_both(&ps->empty[s]);
+                    if (++s == kPStages) { s = 0; ++round; }
+                }
+                if (!ok) break;
+                umma_commit_pair_both(&ps->tfull[acc]);
+                if (++acc == 2) { acc = 0; ++around; }
+            }
+            if (issued) {
+                // every pair MMA has completed before either CTA releases its TMEM
+                umma_commit_pair_own(&ps->done);
+                mbar_wait(&ps->done, 0, status);
+            }
+        }
+        __syncwarp();
+    } else {
+        // ---------------- epilogue (both CTAs): warps 2..5 own TMEM lanes 32*(warp%4) .. +31 ----
+        const int quarter = warp & 3;
+        const uint32_t stage = stage_base + (uint32_t)(warp - 2) * 4096u;
+        int acc = 0;
+        uint32_t around = 0;
+        for (int tile = cid; tile < total; tile += ncl) {
+            int g, mp, n;
+            pair_decode_tile(ps->pair_prefix, NT, tile, g, mp, n);
+            const PrefillGroup& G = P->g[g];
+            const int mloc = 2 * mp + (int)rank;
+            if (!mbar_wait_warp(&ps->tfull[acc], around & 1, abort_flag, status)) break;
+            tc_fence_after();
+            const int rows_valid = min(kBM, G.rows - mloc * kBM);  // <= 0: the pair's empty half
+            const uint32_t taddr = tmem_base + ((uint32_t)(quarter * 32) << 16) + (uint32_t)acc * kBN;
+            gemm_epilogue_tile<kEpi>(taddr, G, mloc, n, rows_valid, out, out_ld, stage, quarter, lane);
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_addr(&ps->tempty[acc]), 0));
+            if (++acc == 2) { acc = 0; ++around; }
+        }
+    }
+    __syncthreads();
+    cluster_sync_all();  // no cross-CTA arrival or MMA write is pending past this point
+    if (warp == 1) {
+        tc_fence_after();
+        tmem_dealloc_pair(tmem_base, kTmemCols);
     }
 }
 
@@ -507,12 +699,12 @@ static bool make_map_bf16(CUtensorMap* m, const void* base, uint64_t rows, uint6
 // The bf16 row-block weights (layout.h) as the 4-D array [nrb][K / 64][128 rows][64 elements],
 // box {64, 128, 1, 2}: 256 rows (two consecutive row blocks) of one 64-element atom, already
 // swizzled in memory, so copied without swizzling into a 1024-byte-aligned tile.
-static bool make_map_bf16_blocks(CUtensorMap* m, const void* base, uint64_t nrb, uint64_t K) {
+static bool make_map_bf16_blocks(CUtensorMap* m, const void* base, uint64_t nrb, uint64_t K, uint32_t box_blocks = 2) {
     auto fn = encode_fn();
     if (!fn) return false;
     const cuuint64_t dims[4] = {64, 128, K / 64, nrb};
     const cuuint64_t strides[3] = {128, (cuuint64_t)kAtomBytes, (cuuint64_t)(K / 64) * kAtomBytes};
-    const cuuint32_t box[4] = {64, 128, 1, 2};
+    const cuuint32_t box[4] = {64, 128, 1, box_blocks};
     const cuuint32_t estr[4] = {1, 1, 1, 1};
     return fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 4, const_cast<void*>(base), dims, strides, box, estr,
               CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
@@ -542,6 +734,69 @@ static cudaError_t launch_gemm(int epi, const CUtensorMap& A, const CUtensorMap&
         grouped_gemm_kernel<kEpiF32><<<grid, kGemmThreads, smem, st>>>(A, B, Bs, plan, NT, KT, b_rows_per_group, out,
                                                                       out_ld, status);
     return cudaGetLastError();
+}
+
+size_t gemm_pair_smem_bytes() {
+    return 1024 + kPStages * (kATile + kBHalfTile) + ((sizeof(PairSmem) + 127) & ~127u) + kPlanBytes + 4 * 4096;
+}
+
+// Pair-tile launch: clusters of 2 CTAs, as many clusters as fit at once (one CTA per SM).
+static cudaError_t launch_gemm_pair(int epi, const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& Bs,
+                                    const PrefillPlan* plan, int NT, int KT, int b_rows_per_group, void* out,
+                                    int out_ld, int max_pair_tiles, uint32_t* status, cudaStream_t st) {
+    const size_t smem = gemm_pair_smem_bytes();
+    const void* fn = epi == kEpiSwiGLU ? reinterpret_cast<const void*>(grouped_gemm_pair_kernel<kEpiSwiGLU>)
+                                       : reinterpret_cast<const void*>(grouped_gemm_pair_kernel<kEpiF32>);
+    cudaError_t err = ensure_smem_optin(fn, smem);
+    if (err != cudaSuccess) return err;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = 2;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cudaLaunchConfig_t cfg = {};
+    cfg.blockDim = dim3(kGemmThreads);
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = st;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    static int max_clusters = 0;  // per process: the device and kernel shape do not change
+    if (max_clusters == 0) {
+        int dev = 0, sms = 148;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+        cfg.gridDim = dim3((unsigned)(sms & ~1));
+        int n = 0;
+        err = cudaOccupancyMaxActiveClusters(&n, fn, &cfg);
+        if (err != cudaSuccess) return err;
+        if (n < 1) return cudaErrorInvalidConfiguration;
+        max_clusters = n;
+    }
+    const int clusters = std::max(1, std::min(max_clusters, max_pair_tiles));
+    cfg.gridDim = dim3((unsigned)(2 * clusters));
+    if (epi == kEpiSwiGLU)
+        err = cudaLaunchKernelEx(&cfg, grouped_gemm_pair_kernel<kEpiSwiGLU>, A, B, Bs, plan, NT, KT, b_rows_per_group,
+                                 out, out_ld, status);
+    else
+        err = cudaLaunchKernelEx(&cfg, grouped_gemm_pair_kernel<kEpiF32>, A, B, Bs, plan, NT, KT, b_rows_per_group, out,
+                                 out_ld, status);
+    if (err != cudaSuccess) return err;
+    return cudaGetLastError();
+}
+
+// Which grouped GEMM runs: the pair kernel when the groups are deep enough that an odd last
+// m-tile per group wastes little (on average at least kPairMinRows rows per group), else the
+// single-CTA kernel. UOCR_PREFILL_GEMM=pair|single overrides (diagnostics).
+constexpr int kPairMinRows = 384;
+static bool use_pair_gemm(long rows, int groups) {
+    static int mode = -1;
+    if (mode < 0) {
+        const char* e = getenv("UOCR_PREFILL_GEMM");
+        mode = (e && strcmp(e, "pair") == 0) ? 1 : (e && strcmp(e, "single") == 0) ? 2 : 0;
+    }
+    if (mode == 1) return true;
+    if (mode == 2) return false;
+    return groups > 0 && rows >= (long)kPairMinRows * groups;
 }
 
 PrefillLayout prefill_layout(int T, int H, int I, int E, int S, int topk, bool int8) {
@@ -635,11 +890,35 @@ cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& 
         mBs1 = mB1;  // no shared groups in the plan: never read
         mBs2 = mB2;
     }
-    err = launch_gemm(kEpiSwiGLU, mA1, mB1, mBs1, plan1, (2 * I) / kBN, H / kBK, 2 * I, h, I, max_mtiles * ((2 * I) / kBN),
-                      status, st);
-    if (err != cudaSuccess) return err;
-    err = launch_gemm(kEpiF32, mA2, mB2, mBs2, plan2, H / kBN, I / kBK, H, y, H, max_mtiles * (H / kBN), status, st);
-    if (err != cudaSuccess) return err;
+    const int groups = (k > 0 ? E : 0) + S;
+    if (use_pair_gemm((long)kT + (long)S * T, groups)) {
+        // B slices of 128 rows (one row block) per CTA
+        CUtensorMap pB1, pBs1, pB2, pBs2;
+        if (!make_map_bf16_blocks(&pB1, w13, (uint64_t)E * 2 * I / kRowBlock, H, 1) ||
+            !make_map_bf16_blocks(&pB2, w2, (uint64_t)E * H / kRowBlock, I, 1))
+            return cudaErrorInvalidValue;
+        if (S > 0) {
+            if (!make_map_bf16_blocks(&pBs1, a.w13_shared, (uint64_t)S * 2 * I / kRowBlock, H, 1) ||
+                !make_map_bf16_blocks(&pBs2, a.w2_shared, (uint64_t)S * H / kRowBlock, I, 1))
+                return cudaErrorInvalidValue;
+        } else {
+            pBs1 = pB1;
+            pBs2 = pB2;
+        }
+        const int max_pairs = max_mtiles;  // pair tiles <= m-tiles
+        err = launch_gemm_pair(kEpiSwiGLU, mA1, pB1, pBs1, plan1, (2 * I) / kBN, H / kBK, 2 * I, h, I,
+                               max_pairs * ((2 * I) / kBN), status, st);
+        if (err != cudaSuccess) return err;
+        err = launch_gemm_pair(kEpiF32, mA2, pB2, pBs2, plan2, H / kBN, I / kBK, H, y, H, max_pairs * (H / kBN), status,
+                               st);
+        if (err != cudaSuccess) return err;
+    } else {
+        err = launch_gemm(kEpiSwiGLU, mA1, mB1, mBs1, plan1, (2 * I) / kBN, H / kBK, 2 * I, h, I,
+                          max_mtiles * ((2 * I) / kBN), status, st);
+        if (err != cudaSuccess) return err;
+        err = launch_gemm(kEpiF32, mA2, mB2, mBs2, plan2, H / kBN, I / kBK, H, y, H, max_mtiles * (H / kBN), status, st);
+        if (err != cudaSuccess) return err;
+    }
     prefill_combine_kernel<<<T, 256, 0, st>>>(y, wts, dest, T, H, k, S, a.accumulate, a.out);
     return cudaGetLastError();
 }

@@ -285,6 +285,93 @@ UOCR_DEV void tmem_ld_32x32b_x32(uint32_t taddr, uint32_t (&r)[32]) {
         : "r"(taddr));
 }
 UOCR_DEV void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
+// tcgen05.wait::ld that also marks r[] as written by it, so no use of the loaded registers can be
+// scheduled before the wait (needed when a later tcgen05.ld is issued before r[] is consumed)
+UOCR_DEV void tmem_wait_ld_tie(uint32_t (&r)[32]) {
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[0]), "+r"(r[1]), "+r"(r[2]), "+r"(r[3]), "+r"(r[4]), "+r"(r[5]), "+r"(r[6]), "+r"(r[7]),
+                   "+r"(r[8]), "+r"(r[9]), "+r"(r[10]), "+r"(r[11]), "+r"(r[12]), "+r"(r[13]), "+r"(r[14]), "+r"(r[15])
+                 :
+                 : "memory");
+    asm volatile("tcgen05.wait::ld.sync.aligned;"
+                 : "+r"(r[16]), "+r"(r[17]), "+r"(r[18]), "+r"(r[19]), "+r"(r[20]), "+r"(r[21]), "+r"(r[22]),
+                   "+r"(r[23]), "+r"(r[24]), "+r"(r[25]), "+r"(r[26]), "+r"(r[27]), "+r"(r[28]), "+r"(r[29]),
+                   "+r"(r[30]), "+r"(r[31])
+                 :
+                 : "memory");
+}
+
+// ---- CTA pairs (clusters of 2) for tcgen05 cta_group::2 -------------------------------------
+UOCR_DEV uint32_t cluster_ctarank() {
+    uint32_t r;
+    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+    return r;
+}
+// every thread of both CTAs of the cluster: release own prior writes, acquire the peer's
+UOCR_DEV void cluster_sync_all() {
+    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+// the shared::cluster address of the object at own shared address `a` in CTA `rank`
+UOCR_DEV uint32_t mapa_shared(uint32_t a, uint32_t rank) {
+    uint32_t r;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(a), "r"(rank));
+    return r;
+}
+// arrive (release at cluster scope) on an mbarrier given by its shared::cluster address
+UOCR_DEV void mbar_arrive_cluster(uint32_t cluster_addr) {
+    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+// TMA tile loads into own shared memory whose completion is counted on the pair leader's
+// mbarrier (`mbar`: a shared::cluster address in CTA 0 of the pair)
+UOCR_DEV void tma_load_2d_pair(void* dst, const void* tmap, int c0, int c1, uint32_t mbar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+        "[%4];" ::"r"(smem_addr(dst)),
+        "l"(tmap), "r"(c0), "r"(c1), "r"(mbar)
+        : "memory");
+}
+UOCR_DEV void tma_load_4d_pair(void* dst, const void* tmap, int c0, int c1, int c2, int c3, uint32_t mbar) {
+    asm volatile(
+        "cp.async.bulk.tensor.4d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, "
+        "%5}], [%6];" ::"r"(smem_addr(dst)),
+        "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(mbar)
+        : "memory");
+}
+// TMEM for a CTA pair: one warp of each CTA (the same warp index) allocates / frees the same
+// columns in both CTAs' tensor memory
+UOCR_DEV void tmem_alloc_pair(uint32_t* smem_dst, uint32_t ncols) {
+    asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_addr(smem_dst)),
+                 "r"(ncols)
+                 : "memory");
+    asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+UOCR_DEV void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+    asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+// Pair MMA, issued by one thread of CTA 0: D (M = 256: rows 0-127 in CTA 0's TMEM, 128-255 in
+// CTA 1's) (+)= A (128 rows from each CTA's shared memory at the descriptor's address) x B (N/2
+// rows from each CTA's shared memory)^T, kind::f16.
+UOCR_DEV void umma_f16_pair(uint32_t tmem_d, uint64_t adesc, uint64_t bdesc, uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}" ::"r"(tmem_d),
+        "l"(adesc), "l"(bdesc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+// Arrive on own mbarrier `bar` once every pair MMA issued so far by this thread has completed.
+UOCR_DEV void umma_commit_pair_own(uint64_t* bar) {
+    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_addr(bar))
+                 : "memory");
+}
+// Arrive on the mbarrier at own shared address `bar` in both CTAs of the pair (mask 0b11) once
+// every pair MMA issued so far by this thread has completed.
+UOCR_DEV void umma_commit_pair_both(uint64_t* bar) {
+    asm volatile(
+        "{\n\t.reg .b16 m;\n\tmov.b16 m, 3;\n\t"
+        "tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.multicast::cluster.b64 [%0], m;\n\t}" ::"r"(
+            smem_addr(bar))
+        : "memory");
+}
 
 // ---- programmatic dependent launch ---------------------------------------------------------
 UOCR_DEV void pdl_wait_prior_grid() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
