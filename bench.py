@@ -57,6 +57,8 @@ def parse():
                         "prefill: configs[2] bf16 prefill of 4096 tokens; "
                         "ep: configs[4] expert-parallel prefill of --ep-tokens over the ranks")
     p.add_argument("--ep-tokens", type=int, default=65536, help="EP prefill tokens over all ranks (configs[4])")
+    p.add_argument("--ep-phases", action="store_true",
+                   help="EP: add per-phase device times of rank 0 (after the timed region) to the JSON line")
     p.add_argument("--ep-placement", choices=["balanced", "contiguous"], default="balanced",
                    help="EP expert->rank map: balanced from the routed loads of a calibration batch (another "
                         "seed of the same distribution), or contiguous ranges")
@@ -517,6 +519,7 @@ def run_ep(args, torch, uocr, synth, dist, world, rank, device):
     t = torch.tensor([ms], device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
+    phases = moe.profile_phases(x, 10) if args.ep_phases else None
     # per-rank expert load and exchanged bytes of one step
     ids, wts = moe._route(x)
     plan = ep_mod.plan_dispatch(ids, wts, world, moe.placement)
@@ -551,6 +554,7 @@ def run_ep(args, torch, uocr, synth, dist, world, rank, device):
         "e2e": None,
         "clocks": clocks,
         "outputs_finite": finite,
+        **({"phases_ms_rank0": phases} if phases is not None else {}),
     }), flush=True)
 
 

@@ -205,6 +205,9 @@ def _ep_worker(rank: int, world: int, port: int, T: int, out_dir: str, kind: str
         # the device bookkeeping reproduces the torch bookkeeping bit for bit
         assert torch.equal(got, m.forward_reference(xd))
         assert torch.equal(got, m(xd))
+        ph = m.profile_phases(xd, 2)
+        assert list(ph) == ["route", "dispatch", "counts", "exchange_rows", "experts", "exchange_back", "shared_wait",
+                            "combine"] and all(v >= 0 for v in ph.values())
         np.save(os.path.join(out_dir, f"ep{rank}.npy"), got.cpu().numpy())
         dist.barrier()
     finally:

@@ -235,6 +235,7 @@ route_smem_kernel(const float* __restrict__ x, int T, int H, const uint16_t* __r
         float acc0[kRT], acc1[kRT];
 #pragma unroll
         for (int t = 0; t < kRT; ++t) acc0[t] = acc1[t] = 0.0f;
+#pragma unroll 4
         for (int kk = 0; kk < L; kk += 8) {
             float a[8], b[8];
             unpack_bf16x8(*reinterpret_cast<const uint4*>(w0 + kk), a);

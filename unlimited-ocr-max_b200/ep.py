@@ -145,7 +145,10 @@ def exchange_counts(send_counts: list[int], device, group=None) -> list[int]:
 
 
 def exchange_rows(t: torch.Tensor, send_counts: list[int], recv_counts: list[int], group=None) -> torch.Tensor:
-    """all_to_all_single of the rows of ``t`` (rank p gets send_counts[p] rows, in order)."""
+    """all_to_all_single of the rows of ``t`` (rank p gets send_counts[p] rows, in order); with one
+    rank the rows stay where they are."""
+    if len(send_counts) == 1:
+        return t
     out = torch.empty((sum(recv_counts),) + tuple(t.shape[1:]), dtype=t.dtype, device=t.device)
     dist.all_to_all_single(out, t.contiguous(), output_split_sizes=recv_counts, input_split_sizes=send_counts,
                            group=group)
@@ -225,6 +228,7 @@ class ExpertParallelMoE:
         self.bias: torch.Tensor | None = None
         self._ws: dict[str, torch.Tensor] = {}
         self._bufs: dict[str, torch.Tensor] = {}
+        self._phase_events: list | None = None
         owner, local = placement.owner_local(self.device)
         self._owner, self._local = owner.int().contiguous(), local.int().contiguous()
         self._side = torch.cuda.Stream(self.device)
@@ -318,9 +322,13 @@ class ExpertParallelMoE:
         T, H = x.shape
         k, W, g = self.config.num_experts_per_tok, self.world, self.group
         cur = torch.cuda.current_stream(self.device)
+        mark = self._mark
+        mark("start")
         sh = self._buf("shared_out", (T, H), torch.float32)
         ids, wts = self._route(x)
+        mark("route")
         send, rows, meta, inv = self._dispatch(x, ids, wts)
+        mark("dispatch")
         # the shared experts overlap the exchanges (NCCL leaves most SMs free) or run in line
         if self.overlap_shared:
             self._side.wait_stream(cur)
@@ -333,14 +341,42 @@ class ExpertParallelMoE:
         counts = torch.cat([send, recv]).tolist()  # the one host synchronisation
         sc, rc = counts[:W], counts[W:]
         ns = sum(sc)
+        mark("counts")
         rows_in = exchange_rows(rows[:ns], sc, rc, g)
         meta_in = exchange_rows(meta[:ns], sc, rc, g)
+        mark("exchange_rows")
         part_in = self._local_experts(rows_in, meta_in[:, :k].contiguous(),
                                       meta_in[:, k:].contiguous().view(torch.float32))
+        mark("experts")
         part = exchange_rows(part_in, rc, sc, g)
+        mark("exchange_back")
         if self.overlap_shared:
             cur.wait_stream(self._side)
-        return self._combine(part, inv, sh if T else None, T)
+        mark("shared_wait")
+        out = self._combine(part, inv, sh if T else None, T)
+        mark("combine")
+        return out
+
+    def _mark(self, name: str) -> None:
+        if self._phase_events is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record(torch.cuda.current_stream(self.device))
+            self._phase_events.append((name, ev))
+
+    def profile_phases(self, x: torch.Tensor, steps: int = 10) -> dict[str, float]:
+        """Mean device time (ms) between the phase boundaries of ``steps`` calls on this rank's
+        main stream: route, dispatch, counts (exchange + the host read), exchange_rows,
+        experts, exchange_back, shared_wait (the side stream's shared experts not yet done),
+        combine. A collective: every rank calls it."""
+        acc: dict[str, float] = {}
+        for _ in range(steps):
+            self._phase_events = []
+            self(x)
+            torch.cuda.synchronize(self.device)
+            evs, self._phase_events = self._phase_events, None
+            for (_, a), (name, b) in zip(evs, evs[1:]):
+                acc[name] = acc.get(name, 0.0) + a.elapsed_time(b) / steps
+        return {k: round(v, 4) for k, v in acc.items()}
 
     def forward_reference(self, x: torch.Tensor) -> torch.Tensor:
         """The same layer through the torch bookkeeping of ``ep_forward`` (the device path's check)."""
