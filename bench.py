@@ -155,13 +155,17 @@ def build_stack(uocr, synth, int8: bool, layers: int, B: int, device, seed0: int
     import torch
 
     cfg = uocr.MoEConfig(int8_experts=int8)
-    mods, xs, outs, ids, wts = [], [], [], [], []
+    mods, ids, wts = [], [], []
+    # every layer's input and output are slices of one [L, B, H] buffer each, so the end-to-end
+    # timing moves a step's inputs and results with one copy each way
+    x_all = torch.empty((layers, B, H), dtype=torch.float32, device=device)
+    out_all = torch.empty((layers, B, H), dtype=torch.float32, device=device)
+    xs, outs = list(x_all.unbind(0)), list(out_all.unbind(0))
     for l in range(layers):
         st = synth.layer_state(cfg, seed0 + l, device=device)
         mods.append(uocr.UocrMoE(cfg, device=device).load_state_dict(st))
         del st
-        xs.append(synth.hidden_states(B, H, seed0 + 100 + l, device=device))
-        outs.append(torch.empty((B, H), dtype=torch.float32, device=device))
+        xs[l].copy_(synth.hidden_states(B, H, seed0 + 100 + l, device=device))
         ids.append(torch.empty((B, TOPK), dtype=torch.int32, device=device))
         wts.append(torch.empty((B, TOPK), dtype=torch.float32, device=device))
     torch.cuda.empty_cache()
@@ -216,17 +220,32 @@ def algorithmic_bytes(torch, ids_list, int8: bool, B: int) -> int:
     return total
 
 
+def _stacked(ts):
+    """The [L, ...] tensor whose slices ``ts`` are, if they are consecutive slices of one buffer."""
+    base = ts[0]._base
+    if base is not None and base.is_contiguous() and base.shape[0] == len(ts) and all(
+            t._base is base and t.data_ptr() == base[i].data_ptr() for i, t in enumerate(ts)):
+        return base
+    return None
+
+
 def time_e2e(torch, g, xs, outs, steps, warmup):
     """Public API end to end: H2D of every layer's input from pinned host memory, the step,
-    D2H of every layer's output, all inside the timed region."""
-    xh = [x.cpu().pin_memory() for x in xs]
-    oh = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in outs]
+    D2H of every layer's output, all inside the timed region (one copy each way when the
+    layers' inputs / outputs are slices of one buffer)."""
+    groups = []
+    for ts in (xs, outs):
+        st = _stacked(ts)
+        groups.append([st] if st is not None else list(ts))
+    xd, od = groups
+    xh = [x.cpu().pin_memory() for x in xd]
+    oh = [torch.empty(o.shape, dtype=o.dtype).pin_memory() for o in od]
 
     def one():
-        for h, d in zip(xh, xs):
+        for h, d in zip(xh, xd):
             d.copy_(h, non_blocking=True)
         g.replay()
-        for h, d in zip(oh, outs):
+        for h, d in zip(oh, od):
             h.copy_(d, non_blocking=True)
 
     for _ in range(warmup):
