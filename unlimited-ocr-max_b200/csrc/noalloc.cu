@@ -31,7 +31,8 @@
 namespace {
 
 // 1 MiB. The production layer (top_k 6, 2 shared experts, B = 8, inter 896, hidden 1280)
-// needs 557 KiB: (6 + 2) * 8 pairs of (896 + 1280) fp32 values, routing data and status.
+// needs 647 KiB: (6 + 2) * 8 pairs of (896 + 1280) fp32 values, the router logit partials, the
+// tokens' MMA operand images, routing data and status.
 constexpr size_t kNoAllocScratchBytes = size_t(1) << 20;
 
 static __device__ __align__(256) unsigned char g_noalloc_scratch[kNoAllocScratchBytes];
