@@ -247,7 +247,7 @@ def test_dense_bf16_qmv(uocr, oracle, m):
 @pytest.mark.parametrize("E,H", [(64, 1280), (8, 256), (64, 1536), (40, 2048)])
 @pytest.mark.parametrize("with_bias", [False, True])
 def test_route_bit_exact(uocr, oracle, T, E, H, with_bias):
-    """H <= 1336: the persistent kernel with the router in shared memory (T = 597 leaves 149
+    """H <= 1280: the persistent kernel with the router in shared memory (T = 597 leaves 149
     4-token tiles over 148 CTAs, 4096 wraps each CTA's token double buffer many times); 1536 and
     2048: the register-blocked kernels (16- and 8-token CTAs)."""
     rng = np.random.default_rng(T + E)

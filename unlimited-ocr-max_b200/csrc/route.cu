@@ -17,6 +17,7 @@
 // The FMA floor is T * 64 * H FMAs over 148 SMs x 128 FMA/clock.
 #include "common.cuh"
 #include "kernels.h"
+#include "sm100.cuh"
 
 namespace uocr {
 
@@ -34,22 +35,19 @@ __device__ __forceinline__ void softmax_topk_warp(float l0, float l1, bool v0, b
     for (int off = 16; off >= 1; off >>= 1) sum = __fadd_rn(sum, __shfl_xor_sync(0xffffffffu, sum, off));
     float p0 = v0 ? __fdiv_rn(e0, sum) : -1.0f;
     float p1 = v1 ? __fdiv_rn(e1, sum) : -1.0f;
+    // Each round: the largest probability, then the lowest expert index holding it. The
+    // probabilities are >= +0, so their bit patterns order as signed integers; the taken (-2)
+    // and absent (-1) entries are negative and never win while a valid one is left.
     for (int r = 0; r < topk; ++r) {
-        // lane-local best: lower index (lane) wins a tie with lane + 32
-        float bp = p0;
-        int bi = lane;
-        if (p1 > bp) { bp = p1; bi = lane + 32; }
-#pragma unroll
-        for (int off = 16; off >= 1; off >>= 1) {
-            const float op = __shfl_xor_sync(0xffffffffu, bp, off);
-            const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-            if (op > bp || (op == bp && oi < bi)) { bp = op; bi = oi; }
-        }
+        const int b0 = __float_as_int(p0), b1 = __float_as_int(p1);
+        const int m = __reduce_max_sync(0xffffffffu, b0 > b1 ? b0 : b1);
+        const int cand = b0 == m ? lane : (b1 == m ? lane + 32 : 64);
+        const int bi = __reduce_min_sync(0xffffffffu, cand);
         if (bi == lane) p0 = -2.0f;
         if (bi == lane + 32) p1 = -2.0f;
         if (lane == 0) {
             ids_row[r] = bi;
-            wts_row[r] = bp;
+            wts_row[r] = __int_as_float(m);
         }
     }
 }
@@ -157,18 +155,22 @@ route_kernel(const float* __restrict__ x, int T, int H, const uint16_t* __restri
     }
 }
 
-// Persistent variant for hidden sizes whose router fits in shared memory (H <= 1336): the CTA
+// Persistent variant for hidden sizes whose router fits in shared memory (H <= 1280 among multiples of 64): the CTA
 // stages the whole router once, rows padded by 16 bytes (a warp's 32 rows at one K offset fall in
-// distinct banks), then walks tiles of kRT tokens. Warp w owns segment s = w; lane l owns experts
-// l and l + 32, for the tile's kRT tokens (8 chains). Token rows arrive by cp.async one tile
-// ahead (issued after the barrier that retires the buffer's previous tile); the segment partials
-// of a tile go to one of two buffers, and after the next barrier warp t < kRT finishes token t
-// (sum of the 8 partials, bias, softmax, top-k) while the others compute. One barrier per tile.
+// distinct banks), then walks tiles of kRT tokens. Eight FMA warps: warp w owns segment s = w,
+// lane l experts l and l + 32, for the tile's kRT tokens (8 chains); token rows arrive by
+// cp.async one tile ahead (issued after the FMA warps' barrier that retires the buffer's previous
+// tile). Two finishing warps take each tile's segment partials from one of two buffers (handed
+// over by mbarriers) and finish tokens 2w' and 2w' + 1 (sum of the 8 partials, bias, softmax,
+// top-k), so the FMA warps never wait for a softmax. Every mbarrier wait is bounded.
 constexpr int kRT = 4;
+constexpr int kRouteFmaThreads = 256;
+constexpr int kRouteSmemThreads = kRouteFmaThreads + 64;
+constexpr uint32_t kRouteWaitPolls = 1u << 24;  // far beyond any legitimate wait; never hangs
 
 UOCR_DEV void route_stage_tokens(const float* __restrict__ x, int T, int H, int t0, float* dst, int tid) {
     const int H4 = H / 4;
-    for (int i = tid; i < kRT * H4; i += 256) {
+    for (int i = tid; i < kRT * H4; i += kRouteFmaThreads) {
         const int t = i / H4;
         const bool live = t0 + t < T;
         const float* src = live ? x + (size_t)(t0 + t) * H + 4 * (i - t * H4) : x;
@@ -178,10 +180,33 @@ UOCR_DEV void route_stage_tokens(const float* __restrict__ x, int T, int H, int 
     asm volatile("cp.async.commit_group;\n" ::: "memory");
 }
 
-__global__ void __launch_bounds__(256, 1)
+UOCR_DEV void route_wait(uint64_t* bar, uint32_t parity) {
+    for (uint32_t i = 0; i < kRouteWaitPolls && !mbar_try_wait(bar, parity); ++i) {
+    }
+}
+
+// Softmax + greedy top-k of one token from its [64][8] segment partials (the finishing warps).
+UOCR_DEV void route_finish_token(const float* sg, int E, const float* __restrict__ bias, int topk, int lane,
+                                 int32_t* __restrict__ ids_row, float* __restrict__ wts_row) {
+    const bool v0 = lane < E, v1 = lane + 32 < E;
+    float l0 = sg[lane * 8], l1 = sg[(lane + 32) * 8];
+#pragma unroll
+    for (int q = 1; q < 8; ++q) {
+        l0 = __fadd_rn(l0, sg[lane * 8 + q]);
+        l1 = __fadd_rn(l1, sg[(lane + 32) * 8 + q]);
+    }
+    if (bias) {
+        if (v0) l0 = __fadd_rn(l0, bias[lane]);
+        if (v1) l1 = __fadd_rn(l1, bias[lane + 32]);
+    }
+    softmax_topk_warp(v0 ? l0 : -INFINITY, v1 ? l1 : -INFINITY, v0, v1, topk, lane, ids_row, wts_row);
+}
+
+__global__ void __launch_bounds__(kRouteSmemThreads, 1)
 route_smem_kernel(const float* __restrict__ x, int T, int H, const uint16_t* __restrict__ wg, int E,
                   const float* __restrict__ bias, int topk, int32_t* __restrict__ ids_out, float* __restrict__ wts_out) {
     extern __shared__ __align__(16) unsigned char rsm[];
+    __shared__ uint64_t segs_full[2], segs_free[2];
     const int RS = H + 8;  // router row stride in bf16 elements
     uint16_t* wr = reinterpret_cast<uint16_t*>(rsm);                            // [64][RS]
     float* xs = reinterpret_cast<float*>(rsm + (size_t)64 * RS * 2);            // [2][kRT][H]
@@ -190,95 +215,93 @@ route_smem_kernel(const float* __restrict__ x, int T, int H, const uint16_t* __r
     const int L = H / 8;
     const int ntiles = (T + kRT - 1) / kRT;
 
-    // router rows (zeros for j >= E), 16-byte copies
-    const int H8 = H / 8;
-    for (int i = tid; i < 64 * H8; i += 256) {
-        const int j = i / H8, c = i - j * H8;
-        const bool live = j < E;
-        const uint16_t* src = live ? wg + (size_t)j * H + 8 * c : wg;
-        const uint32_t d = (uint32_t)__cvta_generic_to_shared(wr + (size_t)j * RS + 8 * c);
-        asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(live ? 16 : 0) : "memory");
-    }
-    asm volatile("cp.async.commit_group;\n" ::: "memory");
-    int tile = blockIdx.x;
-    if (tile < ntiles) route_stage_tokens(x, T, H, tile * kRT, xs, tid);
-
-    const int s = warp;
-    const uint16_t* w0 = wr + (size_t)lane * RS + s * L;
-    const uint16_t* w1 = wr + (size_t)(lane + 32) * RS + s * L;
-    int buf = 0, prev_t0 = -1;
-    for (; tile < ntiles; tile += gridDim.x, buf ^= 1) {
-        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
-        // this tile's token rows (and, first time, the router) are in place; every warp is done
-        // with the other token buffer and has written the previous tile's partials
-        __syncthreads();
-        const int next = tile + gridDim.x;
-        if (next < ntiles) route_stage_tokens(x, T, H, next * kRT, xs + (buf ^ 1) * kRT * H, tid);
-        // finish the previous tile
-        if (prev_t0 >= 0 && warp < kRT && prev_t0 + warp < T) {
-            const float* sg = segs + ((buf ^ 1) * kRT + warp) * 64 * 8;
-            const bool v0 = lane < E, v1 = lane + 32 < E;
-            float l0 = sg[lane * 8], l1 = sg[(lane + 32) * 8];
-#pragma unroll
-            for (int q = 1; q < 8; ++q) {
-                l0 = __fadd_rn(l0, sg[lane * 8 + q]);
-                l1 = __fadd_rn(l1, sg[(lane + 32) * 8 + q]);
-            }
-            if (bias) {
-                if (v0) l0 = __fadd_rn(l0, bias[lane]);
-                if (v1) l1 = __fadd_rn(l1, bias[lane + 32]);
-            }
-            softmax_topk_warp(v0 ? l0 : -INFINITY, v1 ? l1 : -INFINITY, v0, v1, topk, lane,
-                              ids_out + (size_t)(prev_t0 + warp) * topk, wts_out + (size_t)(prev_t0 + warp) * topk);
+    if (tid == 0) {
+        for (int i = 0; i < 2; ++i) {
+            mbar_init(&segs_full[i], kRouteFmaThreads);
+            mbar_init(&segs_free[i], 64);
         }
-        const float* xt = xs + buf * kRT * H + s * L;
-        float acc0[kRT], acc1[kRT];
+        fence_mbar_init();
+    }
+    if (tid < kRouteFmaThreads) {
+        // router rows (zeros for j >= E), 16-byte copies, and the first tile's token rows
+        const int H8 = H / 8;
+        for (int i = tid; i < 64 * H8; i += kRouteFmaThreads) {
+            const int j = i / H8, c = i - j * H8;
+            const bool live = j < E;
+            const uint16_t* src = live ? wg + (size_t)j * H + 8 * c : wg;
+            const uint32_t d = (uint32_t)__cvta_generic_to_shared(wr + (size_t)j * RS + 8 * c);
+            asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(d), "l"(src), "r"(live ? 16 : 0)
+                         : "memory");
+        }
+        asm volatile("cp.async.commit_group;\n" ::: "memory");
+        if ((int)blockIdx.x < ntiles) route_stage_tokens(x, T, H, blockIdx.x * kRT, xs, tid);
+    }
+    __syncthreads();  // barrier initialisation visible to all warps
+
+    if (tid < kRouteFmaThreads) {
+        const int s = warp;
+        const uint16_t* w0 = wr + (size_t)lane * RS + s * L;
+        const uint16_t* w1 = wr + (size_t)(lane + 32) * RS + s * L;
+        int it = 0;
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+            const int buf = it & 1;
+            asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+            // this tile's token rows (and, first time, the router) are in place; every FMA warp is
+            // done with the other token buffer
+            named_bar_sync(1, kRouteFmaThreads);
+            const int next = tile + gridDim.x;
+            if (next < ntiles) route_stage_tokens(x, T, H, next * kRT, xs + (buf ^ 1) * kRT * H, tid);
+            const float* xt = xs + buf * kRT * H + s * L;
+            float acc0[kRT], acc1[kRT];
 #pragma unroll
-        for (int t = 0; t < kRT; ++t) acc0[t] = acc1[t] = 0.0f;
+            for (int t = 0; t < kRT; ++t) acc0[t] = acc1[t] = 0.0f;
 #pragma unroll 4
-        for (int kk = 0; kk < L; kk += 8) {
-            float a[8], b[8];
-            unpack_bf16x8(*reinterpret_cast<const uint4*>(w0 + kk), a);
-            unpack_bf16x8(*reinterpret_cast<const uint4*>(w1 + kk), b);
+            for (int kk = 0; kk < L; kk += 8) {
+                float a[8], b[8];
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(w0 + kk), a);
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(w1 + kk), b);
+#pragma unroll
+                for (int t = 0; t < kRT; ++t) {
+                    const float4 xa = *reinterpret_cast<const float4*>(xt + t * H + kk);
+                    const float4 xb = *reinterpret_cast<const float4*>(xt + t * H + kk + 4);
+                    const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
+                    float u = acc0[t], v = acc1[t];
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {
+                        u = __fmaf_rn(a[q], xv[q], u);
+                        v = __fmaf_rn(b[q], xv[q], v);
+                    }
+                    acc0[t] = u;
+                    acc1[t] = v;
+                }
+            }
+            // the finishing warps are done with this buffer's previous tile (two tiles ago)
+            if (it >= 2) route_wait(&segs_free[buf], ((it >> 1) - 1) & 1);
+            float* so = segs + buf * kRT * 64 * 8;
 #pragma unroll
             for (int t = 0; t < kRT; ++t) {
-                const float4 xa = *reinterpret_cast<const float4*>(xt + t * H + kk);
-                const float4 xb = *reinterpret_cast<const float4*>(xt + t * H + kk + 4);
-                const float xv[8] = {xa.x, xa.y, xa.z, xa.w, xb.x, xb.y, xb.z, xb.w};
-                float u = acc0[t], v = acc1[t];
-#pragma unroll
-                for (int q = 0; q < 8; ++q) {
-                    u = __fmaf_rn(a[q], xv[q], u);
-                    v = __fmaf_rn(b[q], xv[q], v);
-                }
-                acc0[t] = u;
-                acc1[t] = v;
+                so[(t * 64 + lane) * 8 + s] = acc0[t];
+                so[(t * 64 + lane + 32) * 8 + s] = acc1[t];
             }
+            mbar_arrive(&segs_full[buf]);
         }
-        float* so = segs + buf * kRT * 64 * 8;
-#pragma unroll
-        for (int t = 0; t < kRT; ++t) {
-            so[(t * 64 + lane) * 8 + s] = acc0[t];
-            so[(t * 64 + lane + 32) * 8 + s] = acc1[t];
+        asm volatile("cp.async.wait_group 0;\n" ::: "memory");
+    } else {
+        const int fw = warp - kRouteFmaThreads / 32;  // 0 or 1: tokens 2fw, 2fw + 1 of each tile
+        int it = 0;
+        for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
+            const int buf = it & 1;
+            route_wait(&segs_full[buf], (it >> 1) & 1);
+            const float* sb = segs + buf * kRT * 64 * 8;
+#pragma unroll 1
+            for (int u = 0; u < 2; ++u) {
+                const int t = 2 * fw + u, tok = tile * kRT + t;
+                if (tok < T)
+                    route_finish_token(sb + t * 64 * 8, E, bias, topk, lane, ids_out + (size_t)tok * topk,
+                                       wts_out + (size_t)tok * topk);
+            }
+            mbar_arrive(&segs_free[buf]);
         }
-        prev_t0 = tile * kRT;
-    }
-    __syncthreads();
-    if (prev_t0 >= 0 && warp < kRT && prev_t0 + warp < T) {
-        const float* sg = segs + ((buf ^ 1) * kRT + warp) * 64 * 8;
-        const bool v0 = lane < E, v1 = lane + 32 < E;
-        float l0 = sg[lane * 8], l1 = sg[(lane + 32) * 8];
-#pragma unroll
-        for (int q = 1; q < 8; ++q) {
-            l0 = __fadd_rn(l0, sg[lane * 8 + q]);
-            l1 = __fadd_rn(l1, sg[(lane + 32) * 8 + q]);
-        }
-        if (bias) {
-            if (v0) l0 = __fadd_rn(l0, bias[lane]);
-            if (v1) l1 = __fadd_rn(l1, bias[lane + 32]);
-        }
-        softmax_topk_warp(v0 ? l0 : -INFINITY, v1 ? l1 : -INFINITY, v0, v1, topk, lane,
-                          ids_out + (size_t)(prev_t0 + warp) * topk, wts_out + (size_t)(prev_t0 + warp) * topk);
     }
 }
 
@@ -301,14 +324,15 @@ cudaError_t launch_route(const float* x, int T, int H, const uint16_t* wg, int E
     if (err == cudaSuccess) err = cudaDeviceGetAttribute(&optin, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     if (err != cudaSuccess) return err;
     const size_t psmem = route_persistent_smem_bytes(H);
-    if (psmem <= (size_t)optin) {
+    if (psmem + 64 <= (size_t)optin) {  // + the kernel's static mbarriers
         int sms = 148;
         err = cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
         if (err != cudaSuccess) return err;
         err = ensure_smem_optin(reinterpret_cast<const void*>(route_smem_kernel), psmem);
         if (err != cudaSuccess) return err;
         const int ntiles = (T + kRT - 1) / kRT;
-        route_smem_kernel<<<ntiles < sms ? ntiles : sms, 256, psmem, st>>>(x, T, H, wg, E, bias, topk, ids, wts);
+        route_smem_kernel<<<ntiles < sms ? ntiles : sms, kRouteSmemThreads, psmem, st>>>(x, T, H, wg, E, bias, topk,
+                                                                                          ids, wts);
     } else if (route_smem_bytes(16, H) <= (size_t)optin / 2) {
         const size_t smem = route_smem_bytes(16, H);
         err = ensure_smem_optin(reinterpret_cast<const void*>(route_kernel<2>), smem);
