@@ -57,6 +57,8 @@ def parse():
                         "prefill: configs[2] bf16 prefill of 4096 tokens; "
                         "ep: configs[4] expert-parallel prefill of --ep-tokens over the ranks")
     p.add_argument("--ep-tokens", type=int, default=65536, help="EP prefill tokens over all ranks (configs[4])")
+    p.add_argument("--ep-overlap", choices=["on", "off"], default="on",
+                   help="EP: run the shared experts on a side stream during the exchanges (on) or in line (off)")
     p.add_argument("--ep-phases", action="store_true",
                    help="EP: add per-phase device times of rank 0 (after the timed region) to the JSON line")
     p.add_argument("--ep-placement", choices=["balanced", "contiguous"], default="balanced",
@@ -515,7 +517,8 @@ def run_ep(args, torch, uocr, synth, dist, world, rank, device):
         dist.all_reduce(calib)
         placement = ep_mod.balanced_placement(calib.cpu(), world)
         del xc, ids_c
-    moe = ep_mod.ExpertParallelMoE(cfg, device=device, placement=placement).load_state_dict(st)
+    moe = ep_mod.ExpertParallelMoE(cfg, device=device, placement=placement,
+                                   overlap_shared=args.ep_overlap == "on").load_state_dict(st)
     del st
     moe.bias = bias
     x = synth.hidden_states(T_all, H, 5002, device=device)[rank * T:(rank + 1) * T].contiguous()
@@ -563,7 +566,8 @@ def run_ep(args, torch, uocr, synth, dist, world, rank, device):
         "config": {"workload": f"configs[4] expert-parallel prefill, {T_all} tokens over {world} GPU(s)",
                    "tokens_per_rank": T, "experts_per_rank": moe.e_local, "hidden": H, "moe_intermediate": I,
                    "top_k": TOPK, "shared": S, "parallelism": f"ep{world} (routed experts) x dp{world} (tokens, shared)",
-                   "expert_placement": args.ep_placement, "expert_rows_per_rank": per_rank,
+                   "expert_placement": args.ep_placement, "shared_overlap": args.ep_overlap,
+                   "expert_rows_per_rank": per_rank,
                    "remote_rows": remote_rows,
                    "all_to_all_bytes_per_step": remote_rows * (H * 2 + 2 * TOPK * 4) + remote_rows * H * 4},
         "roofline": {"bound": "tensor", "achieved": tflops / world, "peak": tc, "unit": "TFLOP/s per GPU",
