@@ -96,7 +96,7 @@ UOCR_API int uocr_dense_bf16_qmv(float* out, int64_t out_rows, int64_t out_cols,
 /* One layer's device-resident weights, in this library's packed layout (uocr_moe_pack_w13,
  * uocr_moe_pack_w2, uocr_moe_pack_shared). Plain pointers, caller-owned. */
 typedef struct uocr_moe_layer {
-    int32_t hidden;     /* H (1280), multiple of 128 */
+    int32_t hidden;     /* H (1280), multiple of 128 (of 256 with int8 experts) */
     int32_t inter;      /* I, moe_intermediate_size (896); multiple of 128 */
     int32_t n_routed;   /* E (64), <= 64 */
     int32_t n_shared;   /* S (2): shared_experts_dim = S * I */
@@ -112,16 +112,18 @@ typedef struct uocr_moe_layer {
 } uocr_moe_layer;
 
 /* Packed layouts (the reference keeps the checkpoint's [E, N, K] stacks, decoder.py:305-313;
- * this library re-lays them out once at load so that one decode work item is one contiguous
- * block):
- *   every packed row of K elements is followed by 16 bytes of padding;
- *   w13: per expert, I/P blocks of P row pairs (P = 8 bf16, 16 int8):
- *        [gate rows (P x H) | up rows (P x H) | int8: gate scales (P x H/G fp32) | up scales]
- *        (for bf16: the [E*2I, H] matrix, row stride H + 8, gate and up rows interleaved in
- *        groups of 8);
- *   w2:  per expert, H/32 blocks of 32 rows: [rows (32 x I) | int8: scales (32 x I/G fp32)]
- *        (for bf16: the [E*H, I] matrix, row stride I + 8).
- * Sizes in bytes for E experts: */
+ * this library re-lays them out once at load into the shared-memory image the tensor cores
+ * read, so that one decode work item is one contiguous block):
+ *   atom: 128 rows x 128 bytes of one K range (128 int8 or 64 bf16 elements), byte c of row r
+ *         at r * 128 + ((c / 16) ^ (r % 8)) * 16 + c % 16 (the 128-byte swizzle);
+ *   item: a row block's atoms over one K range, then for int8 their fp32 scales
+ *         [atom][128 rows] (one 128-element group per int8 atom);
+ *   w13: per expert, I/64 row blocks of 64 gate/up row pairs (rows 16i..16i+7 gate rows of
+ *        pairs 8i..8i+7, rows 16i+8..16i+15 the matching up rows), each row block H/256
+ *        (int8) or H/128 (bf16) items of 2 atoms;
+ *   w2:  per expert, H/128 row blocks of 128 output rows, each ceil(I/256) (int8, the last
+ *        item one atom when I/128 is odd) or I/128 (bf16) items of up to 2 atoms.
+ * Sizes in bytes for E experts (0 for unsupported shapes): */
 UOCR_API size_t uocr_moe_w13_bytes(int64_t E, int64_t I, int64_t H, int64_t group, int int8);
 UOCR_API size_t uocr_moe_w2_bytes(int64_t E, int64_t H, int64_t I, int64_t group, int int8);
 
@@ -211,7 +213,8 @@ UOCR_API int uocr_moe_ep_combine(const float* partials, int64_t n_rows, const in
                                  int64_t world, int64_t H, const float* add, float* out, uocr_stream_t stream);
 
 /* The shared experts of L alone over x [T, H] fp32 (bf16 products, fp32 out): out = shared(x),
- * or out += shared(x) with accumulate != 0. */
+ * or out += shared(x) with accumulate != 0. Meant to run beside the expert-parallel exchanges:
+ * its GEMMs leave 16 SMs free for concurrent kernels (NCCL's). */
 UOCR_API size_t uocr_moe_shared_workspace_bytes(const uocr_moe_layer* L, int64_t T);
 UOCR_API int uocr_moe_shared_forward(const uocr_moe_layer* L, const float* x, int64_t T, float* out,
                                      int accumulate, void* workspace, size_t workspace_bytes,

@@ -512,6 +512,12 @@ int uocr_moe_shared_forward(const uocr_moe_layer* L, const float* x, int64_t T, 
     a.T = (int)T; a.H = L->hidden; a.I = L->inter; a.E = L->n_shared; a.S = L->n_shared; a.topk = 0;
     a.G = 128; a.int8 = 0;
     a.route = 0; a.use_shared = 1; a.accumulate = accumulate != 0;
+    // this entry point serves the expert-parallel layer, where it runs beside NCCL's exchange
+    // kernels: its GEMMs leave 16 SMs free so those kernels are not queued behind them
+    int dev = 0, sms = 0;
+    if (cudaGetDevice(&dev) == cudaSuccess && cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) ==
+                                                  cudaSuccess && sms > 32)
+        a.max_ctas = sms - 16;
     a.x = x;
     a.w13 = L->w13_shared; a.w2 = L->w2_shared;  // no routed groups: the routed maps are never read
     a.w13_shared = L->w13_shared; a.w2_shared = L->w2_shared;

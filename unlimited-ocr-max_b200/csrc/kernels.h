@@ -97,6 +97,7 @@ struct PrefillArgs {
     int route;       // 1: route x here (ids/wts are outputs); 0: ids/wts given, id < 0 = no expert
     int use_shared;  // add the S shared experts
     int accumulate;  // out += instead of out =
+    int max_ctas;    // 0: the GEMMs take one CTA per SM; > 0: at most this many (SMs left to concurrent kernels)
     const float* x;  // [T, H] fp32 (or null with x_bf16)
     const uint16_t* x_bf16;  // [T, H] bf16 rows given directly (or null)
     const uint16_t* router;

@@ -717,7 +717,7 @@ size_t gemm_smem_bytes() {
 
 static cudaError_t launch_gemm(int epi, const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& Bs,
                                const PrefillPlan* plan, int NT, int KT, int b_rows_per_group, void* out, int out_ld,
-                               int max_tiles, uint32_t* status, cudaStream_t st) {
+                               int max_tiles, int max_ctas, uint32_t* status, cudaStream_t st) {
     int dev = 0, sms = 0;
     cudaGetDevice(&dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -726,7 +726,8 @@ static cudaError_t launch_gemm(int epi, const CUtensorMap& A, const CUtensorMap&
                                        : reinterpret_cast<const void*>(grouped_gemm_kernel<kEpiF32>);
     cudaError_t err = ensure_smem_optin(fn, smem);
     if (err != cudaSuccess) return err;
-    const int grid = std::max(1, std::min(sms, max_tiles));
+    int grid = std::max(1, std::min(sms, max_tiles));
+    if (max_ctas > 0) grid = std::min(grid, max_ctas);
     if (epi == kEpiSwiGLU)
         grouped_gemm_kernel<kEpiSwiGLU><<<grid, kGemmThreads, smem, st>>>(A, B, Bs, plan, NT, KT, b_rows_per_group, out,
                                                                          out_ld, status);
@@ -743,7 +744,7 @@ size_t gemm_pair_smem_bytes() {
 // Pair-tile launch: clusters of 2 CTAs, as many clusters as fit at once (one CTA per SM).
 static cudaError_t launch_gemm_pair(int epi, const CUtensorMap& A, const CUtensorMap& B, const CUtensorMap& Bs,
                                     const PrefillPlan* plan, int NT, int KT, int b_rows_per_group, void* out,
-                                    int out_ld, int max_pair_tiles, uint32_t* status, cudaStream_t st) {
+                                    int out_ld, int max_pair_tiles, int max_ctas, uint32_t* status, cudaStream_t st) {
     const size_t smem = gemm_pair_smem_bytes();
     const void* fn = epi == kEpiSwiGLU ? reinterpret_cast<const void*>(grouped_gemm_pair_kernel<kEpiSwiGLU>)
                                        : reinterpret_cast<const void*>(grouped_gemm_pair_kernel<kEpiF32>);
@@ -772,7 +773,8 @@ static cudaError_t launch_gemm_pair(int epi, const CUtensorMap& A, const CUtenso
         if (n < 1) return cudaErrorInvalidConfiguration;
         max_clusters = n;
     }
-    const int clusters = std::max(1, std::min(max_clusters, max_pair_tiles));
+    int clusters = std::max(1, std::min(max_clusters, max_pair_tiles));
+    if (max_ctas > 0) clusters = std::max(1, std::min(clusters, max_ctas / 2));
     cfg.gridDim = dim3((unsigned)(2 * clusters));
     if (epi == kEpiSwiGLU)
         err = cudaLaunchKernelEx(&cfg, grouped_gemm_pair_kernel<kEpiSwiGLU>, A, B, Bs, plan, NT, KT, b_rows_per_group,
@@ -907,16 +909,17 @@ cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& 
         }
         const int max_pairs = max_mtiles;  // pair tiles <= m-tiles
         err = launch_gemm_pair(kEpiSwiGLU, mA1, pB1, pBs1, plan1, (2 * I) / kBN, H / kBK, 2 * I, h, I,
-                               max_pairs * ((2 * I) / kBN), status, st);
+                               max_pairs * ((2 * I) / kBN), a.max_ctas, status, st);
         if (err != cudaSuccess) return err;
-        err = launch_gemm_pair(kEpiF32, mA2, pB2, pBs2, plan2, H / kBN, I / kBK, H, y, H, max_pairs * (H / kBN), status,
-                               st);
+        err = launch_gemm_pair(kEpiF32, mA2, pB2, pBs2, plan2, H / kBN, I / kBK, H, y, H, max_pairs * (H / kBN),
+                               a.max_ctas, status, st);
         if (err != cudaSuccess) return err;
     } else {
         err = launch_gemm(kEpiSwiGLU, mA1, mB1, mBs1, plan1, (2 * I) / kBN, H / kBK, 2 * I, h, I,
-                          max_mtiles * ((2 * I) / kBN), status, st);
+                          max_mtiles * ((2 * I) / kBN), a.max_ctas, status, st);
         if (err != cudaSuccess) return err;
-        err = launch_gemm(kEpiF32, mA2, mB2, mBs2, plan2, H / kBN, I / kBK, H, y, H, max_mtiles * (H / kBN), status, st);
+        err = launch_gemm(kEpiF32, mA2, mB2, mBs2, plan2, H / kBN, I / kBK, H, y, H, max_mtiles * (H / kBN), a.max_ctas,
+                          status, st);
         if (err != cudaSuccess) return err;
     }
     prefill_combine_kernel<<<T, 256, 0, st>>>(y, wts, dest, T, H, k, S, a.accumulate, a.out);
