@@ -78,7 +78,7 @@ extern "C" {
 
 const char* uocr_last_error(void) { return g_last_error.c_str(); }
 
-int uocr_abi_version(void) { return 4; }
+int uocr_abi_version(void) { return 5; }
 
 // ---------------------------------------------------------------------------------------
 // reference op shims
