@@ -1,6 +1,6 @@
-"""Expert-parallel bookkeeping on CPU ranks (gloo, world size 2): the dispatch plan, the count
+"""Expert-parallel bookkeeping on CPU ranks (gloo, world sizes 2 and 4): the dispatch plan, the count
 and row exchanges and the per-token sum of partials, with the expert compute done by a float64
-restatement of the layer on the receiving rank. The gathered outputs of both ranks must equal
+restatement of the layer on the receiving rank. The gathered outputs of all ranks must equal
 the single-process float64 layer (routing from the bit-exact fp32 oracle) to the prefill
 tolerance (the rows travel as bf16, as in the CUDA path)."""
 
@@ -130,9 +130,8 @@ def test_plan_dispatch_with_placement():
     assert none.send_counts == [0, 1] and none.meta_expert.tolist() == [[-1, -1, 0, 1, -1, 2]]
 
 
-@pytest.mark.parametrize("kind", ["contiguous", "balanced"])
-def test_ep_forward_two_gloo_ranks(tmp_path, kind):
-    world = 2
+@pytest.mark.parametrize("world,kind", [(2, "contiguous"), (2, "balanced"), (4, "balanced")])
+def test_ep_forward_gloo_ranks(tmp_path, world, kind):
     mp.spawn(_worker, args=(world, _free_port(), str(tmp_path), kind), nprocs=world, join=True)
     got = np.concatenate([np.load(tmp_path / f"rank{r}.npy") for r in range(world)])
     o, cfg, w, x = _setup()
