@@ -139,3 +139,22 @@ def test_ep_forward_gloo_ranks(tmp_path, world, kind):
     ref = o.moe_layer_fp64(cfg, w, x, r.ids, r.weights)
     assert np.max(np.abs(got - ref)) <= 2e-2
     assert o.rel_l2(got, ref) <= 1e-2
+
+
+def test_expert_parallel_module_refuses_bad_placements_and_cpu():
+    """Checked on the host before any device work (a one-rank gloo group)."""
+    ep = importlib.import_module("unlimited-ocr-max_b200.ep")
+    uocr = importlib.import_module("unlimited-ocr-max_b200")
+    dist.init_process_group("gloo", rank=0, world_size=1, init_method=f"tcp://127.0.0.1:{_free_port()}")
+    try:
+        cfg = uocr.MoEConfig()
+        bad = [ep.ExpertPlacement([list(range(63))]),                  # an expert missing
+               ep.ExpertPlacement([list(range(64)) + [0]]),            # an expert twice
+               ep.ExpertPlacement([list(range(32)), list(range(32, 64))])]  # placed for 2 ranks
+        for pl in bad:
+            with pytest.raises(ValueError, match="placement"):
+                ep.ExpertParallelMoE(cfg, device="cpu", placement=pl)
+        with pytest.raises(ValueError, match="CUDA"):
+            ep.ExpertParallelMoE(cfg, device="cpu")
+    finally:
+        dist.destroy_process_group()
