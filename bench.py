@@ -50,6 +50,9 @@ def parse():
     p.add_argument("--layers", type=int, default=11)
     p.add_argument("--no-sub", action="store_true", help="skip the ride-along sub-configs")
     p.add_argument("--no-cpu", action="store_true", help="skip the cpu_baseline leg")
+    p.add_argument("--no-ep", action="store_true",
+                   help="skip the configs[4] expert-parallel prefill that rides along in every decode line")
+    p.add_argument("--ep-steps", type=int, default=10, help="timed steps of the expert-parallel ride-along")
     p.add_argument("--settle", type=float, default=1.5,
                    help="seconds of untimed replays before timing, while the clock sampler runs")
     p.add_argument("--workload", choices=["decode", "prefill", "ep"], default="decode",
@@ -355,8 +358,10 @@ def prefill_row(torch, uocr, synth, int8, T, steps, warmup, dist, device, seed):
     tc, _ = measured_tc_peak()
     tflops = PREFILL_FLOP_PER_TOKEN * T / (ms * 1e-3) / 1e12
     counts = torch.bincount(ids.flatten().long(), minlength=E)
+    moe.check_status()
     row = {"value": T / (ms * 1e-3), "unit": "tokens/s", "tokens": T, "ms_per_layer": ms, "tflops": tflops,
-           "tc_frac": tflops / tc, "max_expert_rows": int(counts.max()), "experts_used": int((counts > 0).sum())}
+           "tc_frac": tflops / tc, "max_expert_rows": int(counts.max()), "experts_used": int((counts > 0).sum()),
+           "near_ties": near_ties(torch, x, moe._tensors["router"], moe.bias)}
     del moe, x, out, ids, wts
     torch.cuda.empty_cache()
     return row
@@ -495,11 +500,13 @@ def run_prefill(args, torch, uocr, synth, dist, world, rank, device):
     print(json.dumps(line), flush=True)
 
 
-def run_ep(args, torch, uocr, synth, dist, world, rank, device):
+def ep_measure(args, torch, uocr, synth, dist, world, rank, device, steps: int, warmup: int, phases: bool,
+               sampler=None) -> dict | None:
     """bf16 MoE over --ep-tokens tokens split evenly over the ranks, routed experts
-    sharded (64 / N per GPU), Zipf(1.1) expert bias, NCCL all-to-all dispatch / combine. The
+    sharded (64 / N per GPU), Zipf(1.1) expert bias, all-to-all dispatch / combine. The
     expert->rank map is balanced on the routed loads of a calibration batch drawn from another
-    seed (the measured batch is not seen), unless --ep-placement contiguous."""
+    seed (the measured batch is not seen), unless --ep-placement contiguous. A collective: every
+    rank calls it; rank 0 gets the metrics, the others None."""
     ep_mod = importlib.import_module(f"{PKG}.ep")
     T_all = args.ep_tokens
     if T_all % world:
@@ -523,61 +530,133 @@ def run_ep(args, torch, uocr, synth, dist, world, rank, device):
     moe.bias = bias
     x = synth.hidden_states(T_all, H, 5002, device=device)[rank * T:(rank + 1) * T].contiguous()
     torch.cuda.empty_cache()
-    for _ in range(max(args.warmup, 3)):
+    for _ in range(max(warmup, 3)):
         out = moe(x)
     torch.cuda.synchronize()
-    sampler = ClockSampler(physical_gpu_index(int(os.environ.get("LOCAL_RANK", "0"))))
-    sampler.start()
+    if sampler:
+        sampler.start()
     dist.barrier()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     a.record()
-    for _ in range(args.steps):
+    for _ in range(steps):
         out = moe(x)
     b.record()
     torch.cuda.synchronize()
-    clocks = sampler.stop()
-    ms = a.elapsed_time(b) / args.steps
+    clocks = sampler.stop() if sampler else None
+    ms = a.elapsed_time(b) / steps
     t = torch.tensor([ms], device=device)
     dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms = float(t.item())
-    phases = moe.profile_phases(x, 10) if args.ep_phases else None
-    # per-rank expert load and exchanged bytes of one step
+    moe.check_status()  # every device-side wait of the timed calls completed
+    ph = moe.profile_phases(x, 10) if phases else None
+    # per-rank expert load and the rows each rank sends to / receives from other ranks in one step
     ids, wts = moe._route(x)
     plan = ep_mod.plan_dispatch(ids, wts, world, moe.placement)
-    sent = torch.tensor([sum(plan.send_counts) - plan.send_counts[rank]], dtype=torch.int64, device=device)
+    sent_rank = sum(plan.send_counts) - plan.send_counts[rank]
+    counts = torch.tensor(plan.send_counts, dtype=torch.int64, device=device)
+    mat = [torch.zeros_like(counts) for _ in range(world)]
+    dist.all_gather(mat, counts)
+    recv_rank = int(sum(int(m[rank]) for m in mat)) - plan.send_counts[rank]
     load = torch.bincount(ids.flatten().long(), minlength=E).to(torch.int64)
-    dist.all_reduce(sent)
     dist.all_reduce(load)
+    near = near_ties(torch, x, moe.router, bias)
+    nt = torch.tensor([near], dtype=torch.int64, device=device)
+    dist.all_reduce(nt)
     finite = bool(torch.isfinite(out).all())
+    fin = torch.tensor([int(finite)], device=device)
+    dist.all_reduce(fin, op=dist.ReduceOp.MIN)
     tc, tc_src = measured_tc_peak()
     flop = PREFILL_FLOP_PER_TOKEN * T_all
     tflops = flop / (ms * 1e-3) / 1e12
     per_rank = [int(load[ex].sum()) for ex in moe.placement.experts]
+    del moe, x, out
+    torch.cuda.empty_cache()
+    if rank != 0:
+        return None
+    row_bytes = H * 2 + 2 * TOPK * 4  # a bf16 row and its slot metadata
+    part_bytes = moe_partial_bytes(H)
+    r = {
+        "value": T_all / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "tokens": T_all, "tokens_per_rank": T,
+        "ms_per_step": ms, "steps": steps, "tflops": tflops, "tc_frac_per_gpu": tflops / world / tc,
+        "tc_peak": tc, "tc_peak_source": tc_src + " (burst)",
+        "expert_placement": args.ep_placement, "shared_overlap": args.ep_overlap,
+        "expert_rows_per_rank": per_rank,
+        "rank0_remote_rows": {"sent": sent_rank, "received": recv_rank},
+        "rank0_exchange_bytes": {"dispatch": (sent_rank + recv_rank) * row_bytes,
+                                 "combine": (sent_rank + recv_rank) * part_bytes},
+        "routing": {"near_ties": int(nt.item()), "tokens": T_all, "margin": "6th-7th probability < 4 ulp"},
+        "outputs_finite": bool(fin.item()),
+        "clocks": clocks,
+    }
+    if ph is not None:
+        r["phases_ms_rank0"] = ph
+        xr, xb = ph.get("exchange_rows"), ph.get("exchange_back")
+        if world > 1 and xr and xb:
+            r["rank0_exchange_gbs"] = {"dispatch": r["rank0_exchange_bytes"]["dispatch"] / (xr * 1e-3) / 1e9,
+                                       "combine": r["rank0_exchange_bytes"]["combine"] / (xb * 1e-3) / 1e9}
+    return r
+
+
+def moe_partial_bytes(h: int) -> int:
+    """Bytes of one partial row sent back by the expert-parallel layer."""
+    ep_mod = importlib.import_module(f"{PKG}.ep")
+    return h * torch_dtype_size(ep_mod.PARTIAL_DTYPE)
+
+
+def torch_dtype_size(dt) -> int:
+    import torch
+
+    return torch.tensor([], dtype=dt).element_size()
+
+
+def near_ties(torch, x, router, bias) -> int:
+    """Tokens whose 6th and 7th routing probabilities (fp32 softmax of x @ router^T + bias, torch's
+    own order) lie within 4 ulp of each other: where a different fp32 summation order could pick a
+    different 6th expert (the reference's matmul order is not visible)."""
+    n = 0
+    for t0 in range(0, x.shape[0], 8192):
+        lg = x[t0:t0 + 8192] @ router.float().t()
+        if bias is not None:
+            lg = lg + bias
+        p = torch.softmax(lg, dim=1)
+        top = torch.topk(p, TOPK + 1, dim=1).values
+        p6, p7 = top[:, TOPK - 1], top[:, TOPK]
+        ulp = torch.nextafter(p6, torch.full_like(p6, float("inf"))) - p6
+        n += int(((p6 - p7) < 4 * ulp).sum())
+    return n
+
+
+def run_ep(args, torch, uocr, synth, dist, world, rank, device):
+    """--workload ep: configs[4] as the headline line."""
+    sampler = ClockSampler(physical_gpu_index(int(os.environ.get("LOCAL_RANK", "0"))))
+    r = ep_measure(args, torch, uocr, synth, dist, world, rank, device, args.steps, args.warmup, args.ep_phases,
+                   sampler)
     if rank != 0:
         return
-    remote_rows = int(sent.item())
     print(json.dumps({
         "metric": "MoE-layer tokens/s (expert-parallel prefill, bf16)",
-        "value": T_all / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-        "warmup": max(args.warmup, 3), "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
-        "vs_baseline": None, "dtype": "bf16 operands, fp32 accumulate (fp32 in/out)",
+        "value": r["value"], "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": r["ms_per_step"], "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "bf16 operands, fp32 accumulate (fp32 in/out)",
         "data": "synthetic (seeded N(0,0.02)->bf16 weights; hidden N(0,1) RMS-normalised; Zipf(1.1) expert bias)",
-        "config": {"workload": f"configs[4] expert-parallel prefill, {T_all} tokens over {world} GPU(s)",
-                   "tokens_per_rank": T, "experts_per_rank": moe.e_local, "hidden": H, "moe_intermediate": I,
-                   "top_k": TOPK, "shared": S, "parallelism": f"ep{world} (routed experts) x dp{world} (tokens, shared)",
-                   "expert_placement": args.ep_placement, "shared_overlap": args.ep_overlap,
-                   "expert_rows_per_rank": per_rank,
-                   "remote_rows": remote_rows,
-                   "all_to_all_bytes_per_step": remote_rows * (H * 2 + 2 * TOPK * 4) + remote_rows * H * 4},
-        "roofline": {"bound": "tensor", "achieved": tflops / world, "peak": tc, "unit": "TFLOP/s per GPU",
-                     "frac": tflops / world / tc, "peak_source": tc_src + " (burst)",
+        "config": {"workload": f"configs[4] expert-parallel prefill, {r['tokens']} tokens over {world} GPU(s)",
+                   "tokens_per_rank": r["tokens_per_rank"], "experts_per_rank": E // world, "hidden": H,
+                   "moe_intermediate": I, "top_k": TOPK, "shared": S,
+                   "parallelism": f"ep{world} (routed experts) x dp{world} (tokens, shared)",
+                   "expert_placement": r["expert_placement"], "shared_overlap": r["shared_overlap"],
+                   "expert_rows_per_rank": r["expert_rows_per_rank"], "rank0_remote_rows": r["rank0_remote_rows"],
+                   "rank0_exchange_bytes": r["rank0_exchange_bytes"]},
+        "roofline": {"bound": "tensor", "achieved": r["tflops"] / world, "peak": r["tc_peak"],
+                     "unit": "TFLOP/s per GPU", "frac": r["tc_frac_per_gpu"], "peak_source": r["tc_peak_source"],
                      "scope": "whole EP layer (route, plan, all-to-all, experts, all-to-all, combine, shared)",
-                     "algorithmic_flop_per_step": flop, "traffic": None},
+                     "algorithmic_flop_per_step": PREFILL_FLOP_PER_TOKEN * r["tokens"], "traffic": None},
         "e2e": None,
-        "clocks": clocks,
-        "outputs_finite": finite,
-        **({"phases_ms_rank0": phases} if phases is not None else {}),
+        "clocks": r["clocks"],
+        "routing": r["routing"],
+        "outputs_finite": r["outputs_finite"],
+        **({"phases_ms_rank0": r["phases_ms_rank0"]} if "phases_ms_rank0" in r else {}),
+        **({"rank0_exchange_gbs": r["rank0_exchange_gbs"]} if "rank0_exchange_gbs" in r else {}),
     }), flush=True)
 
 
@@ -588,7 +667,7 @@ def run_ours(args):
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
     dist = None
-    if world > 1 or args.workload == "ep":
+    if world > 1 or args.workload == "ep" or (args.workload == "decode" and not args.no_ep):
         import torch.distributed as dist
 
         if world == 1:  # a one-rank group for the expert-parallel path
@@ -620,6 +699,9 @@ def run_ours(args):
     sampler = ClockSampler(physical_gpu_index(local))
     g, ms, clocks = time_stack(torch, mods, xs, outs, ids, wts, args.steps, args.warmup, dist, sampler,
                                 settle_s=args.settle)
+    for m in mods:
+        m.check_status()  # every device-side wait of the timed steps completed (raises otherwise)
+    near = sum(near_ties(torch, x, m._tensors["router"], None) for m, x in zip(mods, xs))
     step_bytes = algorithmic_bytes(torch, ids, True, B)
     peak, peak_src = measured_peaks()
     achieved = step_bytes / (ms * 1e-3) / 1e9
@@ -649,6 +731,11 @@ def run_ours(args):
             r = prefill_row(torch, uocr, synth, int8, args.tokens, psteps, max(args.warmup // 4, 3), dist, device, 3000)
             r["value"] *= world
             subs[f"prefill_{'int8' if int8 else 'bf16'}_{args.tokens}"] = r
+    if not args.no_ep:
+        # configs[4] at this N: the expert-parallel prefill over the same ranks (a collective)
+        ep = ep_measure(args, torch, uocr, synth, dist, world, rank, device, args.ep_steps, 3, True)
+        if rank == 0:
+            subs[f"ep_prefill_{args.ep_tokens}"] = ep
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu:
         v, cores, sample = CpuDecode(True, B).rate()
@@ -687,6 +774,7 @@ def run_ours(args):
             "gpu_launches": launches_per_step * args.steps,
             "clocks": clocks,
             "cpu_baseline": cpu,
+            "routing": {"near_ties": near, "tokens": B * L, "margin": "6th-7th probability < 4 ulp"},
             "configs": subs,
             "outputs_finite": finite,
         }

@@ -35,7 +35,7 @@ def test_library_exports_every_declared_symbol(uocr):
 
     sigs = import_module("unlimited-ocr-max_b200._lib").SIGNATURES
     assert sorted(sigs) == header_functions()
-    assert lib.uocr_abi_version() == 5
+    assert lib.uocr_abi_version() == 6
 
 
 def test_only_the_c_abi_is_exported(uocr):

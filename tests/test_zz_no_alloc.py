@@ -56,3 +56,29 @@ def test_noalloc_refuses_what_does_not_fit(uocr):
     assert "scratch" in lib.uocr_last_error().decode()
     rc = lib.uocr_moe_decode_noalloc(ctypes.byref(moe.layer), x.data_ptr(), 9, None, x.data_ptr(), None)
     assert rc == 1
+
+
+def test_noalloc_reports_an_expired_wait_and_recovers(uocr):
+    """A caller without a workspace still learns of a device-side wait that gave up: the call
+    writes NaN over its output, uocr_moe_decode_noalloc_status returns UOCR_EDEVICE once (and
+    clears the array's status), and the next call gives the workspace entry point's bits."""
+    lib = uocr.load()
+    moe, synth = _layer(uocr, True, 41)
+    stream = torch.cuda.current_stream().cuda_stream
+    x = synth.hidden_states(8, 1280, 600, device=DEV)
+    want = moe.decode_rows(x)
+    got = torch.zeros_like(x)
+    assert lib.uocr_moe_decode_noalloc_status(stream) == 0, lib.uocr_last_error().decode()
+    assert lib.uocr_moe_test_barrier_extra(1) == 0  # the grid barrier waits for an arrival that never comes
+    try:
+        rc = lib.uocr_moe_decode_noalloc(ctypes.byref(moe.layer), x.data_ptr(), 8, None, got.data_ptr(), stream)
+    finally:
+        assert lib.uocr_moe_test_barrier_extra(0) == 0
+    assert rc == 0
+    assert lib.uocr_moe_decode_noalloc_status(stream) == 3
+    assert "bounded wait" in lib.uocr_last_error().decode()
+    assert torch.isnan(got).all()
+    assert lib.uocr_moe_decode_noalloc_status(stream) == 0  # read once: cleared
+    rc = lib.uocr_moe_decode_noalloc(ctypes.byref(moe.layer), x.data_ptr(), 8, None, got.data_ptr(), stream)
+    assert rc == 0 and lib.uocr_moe_decode_noalloc_status(stream) == 0
+    assert torch.equal(got, want)

@@ -70,6 +70,8 @@ SIGNATURES: dict[str, tuple] = {
     "uocr_moe_decode_set_trace": (I32, [P, SZ]),
     "uocr_moe_decode_noalloc_max_bytes": (SZ, []),
     "uocr_moe_decode_noalloc": (I32, [ctypes.POINTER(UocrMoeLayer), P, I64, P, P, P]),
+    "uocr_moe_decode_noalloc_status": (I32, [P]),
+    "uocr_moe_test_barrier_extra": (I32, [I32]),
 }
 
 _lock = threading.Lock()

@@ -47,6 +47,25 @@ namespace uocr {
 
 unsigned long long* g_decode_trace = nullptr;
 size_t g_decode_trace_bytes = 0;
+int g_decode_barrier_extra = 0;
+
+// Read a workspace's status word after `stream` finished; if it is set, clear it together with the
+// control words a failed call may have left behind (decode: DecodeCtl; prefill: its first 128
+// bytes are the status region, so the clear stays inside it). Returns the code read.
+int read_clear_status(const void* workspace, cudaStream_t stream, uint32_t* code) {
+    cudaError_t err = cudaStreamSynchronize(stream);
+    if (err != cudaSuccess) return fail(UOCR_ECUDA, "device_status: synchronize: %s", cudaGetErrorString(err));
+    *code = 0;
+    err = cudaMemcpy(code, workspace, sizeof *code, cudaMemcpyDeviceToHost);
+    if (err != cudaSuccess) return fail(UOCR_ECUDA, "device_status: read: %s", cudaGetErrorString(err));
+    if (*code) {
+        err = cudaMemset(const_cast<void*>(workspace), 0, kCtlClearBytes);
+        if (err != cudaSuccess) return fail(UOCR_ECUDA, "device_status: clear: %s", cudaGetErrorString(err));
+        return fail(UOCR_EDEVICE, "device_status: a device-side check failed (code %u: %s); cleared", *code,
+                    *code == 1 ? "a bounded wait gave up" : *code == 2 ? "shared memory misaligned" : "unknown");
+    }
+    return ok();
+}
 
 int set_error(int code, const char* msg) {
     g_last_error = msg;
@@ -78,7 +97,7 @@ extern "C" {
 
 const char* uocr_last_error(void) { return g_last_error.c_str(); }
 
-int uocr_abi_version(void) { return 5; }
+int uocr_abi_version(void) { return 6; }
 
 // ---------------------------------------------------------------------------------------
 // reference op shims
@@ -533,17 +552,13 @@ int uocr_moe_decode_set_trace(void* device_buffer, size_t bytes) {
 
 int uocr_moe_device_status(const void* workspace, uocr_stream_t stream) {
     if (!workspace) return fail(UOCR_EINVAL, "device_status: null workspace");
-    cudaError_t err = cudaStreamSynchronize(S(stream));
-    if (err != cudaSuccess) return cuda_status(err, "device_status: synchronize");
-    uint32_t status = 0;
-    err = cudaMemcpy(&status, workspace, sizeof status, cudaMemcpyDeviceToHost);
-    if (err != cudaSuccess) return cuda_status(err, "device_status: read");
-    if (status) {
-        // sticky until read: clear it so the next failure is reported afresh
-        cudaMemset(const_cast<void*>(workspace), 0, sizeof status);
-        return fail(UOCR_EDEVICE, "device_status: a device-side check failed (code %u: %s)", status,
-                    status == 1 ? "a bounded wait gave up" : status == 2 ? "shared memory misaligned" : "unknown");
-    }
+    uint32_t code = 0;
+    return uocr::read_clear_status(workspace, S(stream), &code);
+}
+
+int uocr_moe_test_barrier_extra(int extra) {
+    if (extra < 0 || extra > 1024) return fail(UOCR_EINVAL, "test_barrier_extra: %d outside 0..1024", extra);
+    uocr::g_decode_barrier_extra = extra;
     return ok();
 }
 

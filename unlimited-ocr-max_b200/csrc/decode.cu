@@ -31,7 +31,8 @@
 // the batch it rides in.
 //
 // Every device-side wait is bounded (sm100.cuh, kWaitBudgetNs): on expiry the waiter records a
-// status code in the workspace and the kernel winds down without writing its output.
+// status code, the kernel winds down, and the call writes NaN over its output instead of the
+// combine (DecodeCtl in kernels.h); the sticky status word tells the host (uocr_moe_device_status).
 #include <algorithm>
 
 #include <cuda_bf16.h>
@@ -190,8 +191,8 @@ struct RouteSmem {
 // by K3). The inputs arrive by bulk copies on `inb`: the partials into `part` (the last stage
 // buffer, which the producer fills only after the table is ready) and K1's operand images.
 UOCR_DEV void cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* xb, float* xsig, float* part,
-                        uint64_t* inb, volatile int* abort_flag, RouteSmem* rs, SlotTable* tb, int tid,
-                        unsigned long long* ev) {
+                        uint64_t* inb, volatile int* abort_flag, uint32_t* fail, RouteSmem* rs, SlotTable* tb,
+                        int tid, unsigned long long* ev) {
     const int warp = tid >> 5, lane = tid & 31;
     const int H = a.H, B = a.B, E = a.E, k = a.topk, kB = k * B;
     unsigned long long* rv = a.trace ? trace_rec(a, 0, a.trace_items / 2 - 2) : nullptr;  // diagnostics
@@ -213,7 +214,7 @@ UOCR_DEV void cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* x
         if (lane == 2 && dbytes) bulk_g2s(xd, a.xd, dbytes, inb);
         if (lane == 3 && sbytes) bulk_g2s(xsig, a.xsig, sbytes, inb);
     }
-    if (!mbar_wait_warp(inb, 0, abort_flag, &a.ctl->status)) *abort_flag = 1;
+    if (!mbar_wait_warp(inb, 0, abort_flag, fail)) *abort_flag = 1;
     if (rv && tid == 0) rv[0] = global_timer_ns();
     for (int i = tid; i < B * 64; i += kCW * 32) {
         const float4 p0 = *reinterpret_cast<const float4*>(part + 8 * i);
@@ -558,7 +559,8 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                       uint32_t off_stages) {
     extern __shared__ __align__(1024) unsigned char smem[];
     __shared__ int abort_flag;
-    __shared__ uint32_t tmem_base;
+    __shared__ uint32_t tmem_base, cta_fail;  // cta_fail: this CTA's failure code (published at exit)
+    uint32_t* fail = &cta_fail;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + nst;         // the MMAs reading the stage are complete
     uint64_t* table_ready = empty + nst;
@@ -580,7 +582,10 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
     unsigned long long* ev = a.trace ? trace_rec(a, 0, a.trace_items / 2 - 1) : nullptr;
     if (ev && tid == 0) ev[0] = global_timer_ns();
     if (smem_addr(smem) & 1023u) {  // the swizzled operands need 1024-byte alignment (same in every CTA)
-        if (tid == 0) set_status(&a.ctl->status, kStatusMisaligned);
+        if (tid == 0) {
+            set_status(&a.ctl->status, kStatusMisaligned);
+            atomicOr(&a.ctl->k2_fail, 1u);
+        }
         return;
     }
     if (tid == 0) {
@@ -596,6 +601,7 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
         }
         mbar_init(mdone, 1);
         abort_flag = 0;
+        cta_fail = 0;
         fence_mbar_init();
         pdl_launch_dependents();  // K3 launches early; it waits for this grid before it reads h
     }
@@ -604,7 +610,7 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    Pipe pipe{tfull, tfree, accm, tmem_base, 0, &abort_flag, &a.ctl->status};
+    Pipe pipe{tfull, tfree, accm, tmem_base, 0, &abort_flag, fail};
 
     if (warp == 8) {
         // ---------------- producer: one bulk copy per item ----------------
@@ -613,14 +619,14 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
         bool ok = true, routed = false;
         auto wait_table = [&]() {
             if (!routed) {
-                ok = mbar_wait_warp(table_ready, 0, &abort_flag, &a.ctl->status);
+                ok = mbar_wait_warp(table_ready, 0, &abort_flag, fail);
                 routed = true;
             }
         };
         auto issue = [&](int slot, int rb, int ki) {
             // the last stage holds the routing's logit partials until the table is ready
             if (round == 0 && st == nst - 1) wait_table();
-            if (ok && round > 0 && !mbar_wait_warp(&empty[st], (round - 1) & 1, &abort_flag, &a.ctl->status))
+            if (ok && round > 0 && !mbar_wait_warp(&empty[st], (round - 1) & 1, &abort_flag, fail))
                 ok = false;
             if (!ok) return;
             if (lane == 0) {
@@ -665,7 +671,7 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             if (!ok) {
                 abort_flag = 1;
                 for (int q = max(0, n - nst); q < n; ++q) mbar_wait(&full[q % nst], (q / nst) & 1, nullptr);
-            } else if (round == 0 || mbar_wait(&empty[st], (round - 1) & 1, &a.ctl->status)) {
+            } else if (round == 0 || mbar_wait(&empty[st], (round - 1) & 1, fail)) {
                 meta[st].slot = -1;  // end marker
                 mbar_arrive(&full[st]);
             } else {
@@ -676,7 +682,7 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
     } else {
         // ---------------- warps 0-7: route; then MMA (warp 0) and epilogue (warps 4-7) ----------------
         cta_route(a, xd, xb, xsig, reinterpret_cast<float*>(stages + (size_t)(nst - 1) * stage_bytes), inb,
-                  &abort_flag, rs, tb, tid, ev);
+                  &abort_flag, fail, rs, tb, tid, ev);
         if (tid == 0) mbar_arrive(table_ready);
         if (ev && tid == 0) ev[2] = global_timer_ns();
         if (warp == 0) {
@@ -688,7 +694,7 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                 const int st = n % nst;
                 unsigned long long* tr = trace_rec(a, 0, n);
                 if (tr && lane == 0) tr[0] = global_timer_ns();
-                if (!mbar_wait_warp(&full[st], (n / nst) & 1, &abort_flag, &a.ctl->status)) {
+                if (!mbar_wait_warp(&full[st], (n / nst) & 1, &abort_flag, fail)) {
                     ok = false;
                     break;
                 }
@@ -760,7 +766,7 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             }
             if (lane == 0) {  // every MMA complete before TMEM is released
                 umma_commit(mdone);
-                mbar_wait(mdone, 0, &a.ctl->status);
+                mbar_wait(mdone, 0, fail);
             }
             __syncwarp();
             if (ev && lane == 0) ev[3] = global_timer_ns();
@@ -805,6 +811,11 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
         tc_fence_after();
         tmem_dealloc(tmem_base, kTmemCols);
     }
+    // a failed CTA's h rows are incomplete: the down kernel learns it from k2_fail
+    if (tid == 0 && (cta_fail || abort_flag)) {
+        set_status(&a.ctl->status, cta_fail ? cta_fail : kStatusWaitTimeout);
+        atomicOr(&a.ctl->k2_fail, 1u);
+    }
 }
 
 // ======================================================================================
@@ -845,8 +856,9 @@ __global__ void __launch_bounds__(kThreads, 1)
 decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t off_meta, uint32_t off_acc,
                    uint32_t off_hb, uint32_t off_hsig, uint32_t off_ring) {
     extern __shared__ __align__(1024) unsigned char smem[];
-    __shared__ int abort_flag, bar_ok, hdesc[2];
-    __shared__ uint32_t tmem_base;
+    __shared__ int abort_flag, hdesc[2];
+    __shared__ uint32_t tmem_base, cta_fail, verdict;  // cta_fail: this CTA's failure code (published at exit)
+    uint32_t* fail = &cta_fail;
     __shared__ int trow[kMaxB][kDecodeMaxTopk];
     __shared__ float tw[kMaxB][kDecodeMaxTopk];
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
@@ -890,6 +902,7 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
         }
         mbar_init(mdone, 1);
         abort_flag = 0;
+        cta_fail = 0;
         fence_mbar_init();
         pdl_launch_dependents();  // the next layer's kernel waits for this grid itself
     }
@@ -898,7 +911,7 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    Pipe pipe{tfull, tfree, accm, tmem_base, 0, &abort_flag, &a.ctl->status};
+    Pipe pipe{tfull, tfree, accm, tmem_base, 0, &abort_flag, fail};
 
     if (warp == 8) {
         // ---------------- producer ----------------
@@ -936,7 +949,7 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
                 const uint32_t hbytes = run_start ? (uint32_t)tb->count[slot] * a.I * 4 : 0u;
                 const uint32_t need = hoff + hbytes;
                 if (run_start && runs >= 2 &&
-                    !mbar_wait_warp(&hready[runs & 1], ((runs - 2) >> 1) & 1, &abort_flag, &a.ctl->status)) {
+                    !mbar_wait_warp(&hready[runs & 1], ((runs - 2) >> 1) & 1, &abort_flag, fail)) {
                     ok = false;
                     break;
                 }
@@ -951,7 +964,7 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
                     }
                     if (!clash) break;
                     if (!mbar_wait_warp(&freed[oldest % kK3Desc], (oldest / kK3Desc) & 1, &abort_flag,
-                                        &a.ctl->status)) {
+                                        fail)) {
                         ok = false;
                         break;
                     }
@@ -960,7 +973,7 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
                 // and the descriptor: item n reuses item n - kK3Desc's
                 while (ok && n - oldest_desc >= kK3Desc) {
                     if (!mbar_wait_warp(&empty[oldest_desc % kK3Desc], (oldest_desc / kK3Desc) & 1, &abort_flag,
-                                        &a.ctl->status))
+                                        fail))
                         ok = false;
                     ++oldest_desc;
                 }
@@ -1004,13 +1017,13 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
         if (lane == 0) {
             if (ok) {
                 // end markers: the next descriptor once it is free, and the stagers' next run
-                if (n >= kK3Desc && !mbar_wait(&empty[n % kK3Desc], ((n / kK3Desc) - 1) & 1, &a.ctl->status)) {
+                if (n >= kK3Desc && !mbar_wait(&empty[n % kK3Desc], ((n / kK3Desc) - 1) & 1, fail)) {
                     ok = false;
                 } else {
                     meta[n % kK3Desc].slot = -1;
                     mbar_arrive(&full[n % kK3Desc]);
                 }
-                if (ok && (runs < 2 || mbar_wait(&hready[runs & 1], ((runs - 2) >> 1) & 1, &a.ctl->status))) {
+                if (ok && (runs < 2 || mbar_wait(&hready[runs & 1], ((runs - 2) >> 1) & 1, fail))) {
                     hdesc[runs & 1] = -1;
                     mbar_arrive(&hload[runs & 1]);
                 } else {
@@ -1032,7 +1045,7 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
             const int d = n % kK3Desc;
             unsigned long long* tr = trace_rec(a, 1, n);
             if (tr && lane == 0) tr[0] = global_timer_ns();
-            if (!mbar_wait_warp(&full[d], (n / kK3Desc) & 1, &abort_flag, &a.ctl->status)) {
+            if (!mbar_wait_warp(&full[d], (n / kK3Desc) & 1, &abort_flag, fail)) {
                 ok = false;
                 break;
             }
@@ -1044,7 +1057,7 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
                 // a run starts: the previous run's image is free once its MMAs complete
                 if (runs > 0 && lane == 0) umma_commit(&bfree[(runs - 1) & 1]);
                 b = runs & 1;
-                if (!mbar_wait_warp(&hready[b], (runs >> 1) & 1, &abort_flag, &a.ctl->status)) {
+                if (!mbar_wait_warp(&hready[b], (runs >> 1) & 1, &abort_flag, fail)) {
                     ok = false;
                     break;
                 }
@@ -1119,7 +1132,7 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
         }
         if (lane == 0) {
             umma_commit(mdone);
-            mbar_wait(mdone, 0, &a.ctl->status);
+            mbar_wait(mdone, 0, fail);
         }
         __syncwarp();
     } else {
@@ -1131,14 +1144,14 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
         auto stage = [&](int r, int nw, int rank) -> bool {
             const int b = r & 1;
             unsigned long long* tv = sv && rank == 0 && lane == 0 && r < 2 ? sv + 4 * r : nullptr;
-            if (!mbar_wait_warp(&hload[b], (r >> 1) & 1, &abort_flag, &a.ctl->status)) return false;
+            if (!mbar_wait_warp(&hload[b], (r >> 1) & 1, &abort_flag, fail)) return false;
             if (tv) tv[0] = global_timer_ns();
             const int n = hdesc[b];
             if (n < 0) return false;
             const int d = n % kK3Desc;
-            if (!mbar_wait_warp(&full[d], (n / kK3Desc) & 1, &abort_flag, &a.ctl->status)) return false;
+            if (!mbar_wait_warp(&full[d], (n / kK3Desc) & 1, &abort_flag, fail)) return false;
             if (tv) tv[1] = global_timer_ns();
-            if (r >= 2 && !mbar_wait_warp(&bfree[b], ((r - 2) >> 1) & 1, &abort_flag, &a.ctl->status)) return false;
+            if (r >= 2 && !mbar_wait_warp(&bfree[b], ((r - 2) >> 1) & 1, &abort_flag, fail)) return false;
             if (tv) tv[2] = global_timer_ns();
             const int slot = meta[d].slot, cnt = tb->count[slot];
             const bool i8 = slot >= a.S && a.int8;
@@ -1222,9 +1235,23 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
         trow[tk][ts] = v ? __ldcg(&a.table->tok_row[tk][ts]) : 0;
         tw[tk][ts] = v ? __ldcg(&a.table->tok_w[tk][ts]) : 0.0f;
     }
-    const bool ok = grid_barrier(&a.ctl->bar_count, &a.ctl->bar_epoch, &a.ctl->status, &bar_ok);
+    // the CTAs' failures (this one's, the gate/up kernel's) ride into the barrier: the combine runs
+    // only if nothing of this call failed, else every CTA writes NaN over its share of the output
+    const uint32_t mine = cta_fail | (abort_flag ? (uint32_t)kStatusWaitTimeout : 0u) |
+                          (__ldcg(&a.ctl->k2_fail) ? (uint32_t)kStatusWaitTimeout : 0u);
+    const uint32_t bad = grid_barrier_gather(&a.ctl->bar_count, &a.ctl->bar_epoch, &a.ctl->bar_fail, a.ctl->verdict,
+                                             &a.ctl->k2_fail, gridDim.x + (uint32_t)a.bar_extra, mine, fail,
+                                             &verdict);
     if (ev && tid == 0) ev[3] = global_timer_ns();
-    if (ok && !abort_flag && __ldcg(&a.ctl->status) == 0) combine_slice(a, trow, tw, tid);
+    if (bad == 0) {
+        combine_slice(a, trow, tw, tid);
+    } else {
+        const int total = a.B * a.H;
+        const int lo = (int)((long long)total * blockIdx.x / gridDim.x);
+        const int hi = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
+        for (int o = lo + tid; o < hi; o += blockDim.x) a.out[o] = __uint_as_float(0x7FC00000u);
+    }
+    if (tid == 0 && cta_fail) set_status(&a.ctl->status, cta_fail);
 }
 
 // ======================================================================================
@@ -1232,17 +1259,22 @@ decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t
 // ======================================================================================
 static size_t up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args) {
+// Launch with programmatic dependent launch allowed; `cooperative` adds the guarantee that every
+// CTA of the grid is resident at once (the launch fails instead of running a grid that does not fit).
+static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args,
+                              bool cooperative = false) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[1];
+    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
+    attr[1].id = cudaLaunchAttributeCooperative;
+    attr[1].val.cooperative = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    cfg.numAttrs = cooperative ? 2 : 1;
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
@@ -1266,6 +1298,7 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
         a.trace = g_decode_trace;
         a.trace_items = (int)(g_decode_trace_bytes / (sizeof(unsigned long long) * 8 * (size_t)sms)) & ~1;
     }
+    a.bar_extra = g_decode_barrier_extra;
 
     // ---- K1: logit partials (one CTA per expert and segment) and the B operand images
     {
@@ -1317,10 +1350,16 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
         const void* k3 = reinterpret_cast<const void*>(decode_down_kernel);
         err = ensure_smem_optin(k3, smem);
         if (err != cudaSuccess) return err;
+        // the grid barrier needs every CTA resident: one per SM must fit, and the launch is
+        // cooperative so that it is never run partly behind another stream's kernels
+        int per_sm = 0;
+        err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k3, kThreads, smem);
+        if (err != cudaSuccess) return err;
+        if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
         uint32_t o[6] = {(uint32_t)off_tbl, (uint32_t)off_meta, (uint32_t)off_acc,
                          (uint32_t)off_hb,  (uint32_t)off_hsig, (uint32_t)off_ring};
         void* args[] = {&a, &ring_bytes, &o[0], &o[1], &o[2], &o[3], &o[4], &o[5]};
-        err = launch_pdl(k3, dim3(sms), dim3(kThreads), smem, st, args);
+        err = launch_pdl(k3, dim3(sms), dim3(kThreads), smem, st, args, true);
         if (err != cudaSuccess) return err;
     }
     return cudaGetLastError();

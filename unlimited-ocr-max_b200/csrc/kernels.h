@@ -22,14 +22,28 @@ cudaError_t launch_route(const float* x, int T, int H, const uint16_t* wg, int E
                          int32_t* ids, float* wts, cudaStream_t st);
 
 // decode.cu
-// Control block at the start of a decode workspace. Zero-filled once by the caller; every
-// launch leaves it zeroed again except `status`, which is sticky until read.
+// Control block at the start of a decode workspace, zero-filled once by the caller.
+//   status     sticky: the code of the first device-side failure of any call on this workspace,
+//              until the host reads and clears it (uocr_moe_device_status). Only reported, never
+//              used to decide anything on the device.
+//   k2_fail    this call's gate/up kernel failed (set by its CTAs at exit, read by every down-kernel
+//              CTA after its dependency wait, cleared by the down kernel's last barrier arrival).
+//   bar_*      the down kernel's grid barrier: arrivals counted modulo the grid size (the last
+//              arrival of a round subtracts the grid size), completed rounds, and the failures the
+//              CTAs carried into it; verdict[e & 1] holds round e's failures for the waiters.
+// A call whose own kernels failed writes NaN to its whole output instead of the combine, so a
+// failure never leaves stale values that look like a result; later calls are unaffected.
 struct DecodeCtl {
     uint32_t status;
-    uint32_t bar_count;   // K3 grid barrier: CTAs arrived (the last one resets it)
-    uint32_t bar_epoch;   // K3 grid barrier: completed barriers (advanced by the last arrival)
-    uint32_t pad[61];
+    uint32_t bar_count;
+    uint32_t bar_epoch;
+    uint32_t k2_fail;
+    uint32_t bar_fail;
+    uint32_t verdict[2];
+    uint32_t pad[57];
 };
+// Words of the control block the host clears along with `status` (uocr_moe_device_status).
+constexpr size_t kCtlClearBytes = 7 * sizeof(uint32_t);
 constexpr int kDecodeMaxShared = 8;
 constexpr int kDecodeMaxTopk = 8;
 
@@ -70,10 +84,13 @@ struct DecodeArgs {
     RouteTable* table;
     unsigned long long* trace;  // optional per-CTA item timeline (diagnostics), null = off
     int trace_items;            // items recorded per CTA
+    int bar_extra;              // test hook: the down kernel's barrier waits for this many more arrivals
 };
 // diagnostics: the trace buffer the next decode launches record into (capi.cu)
 extern unsigned long long* g_decode_trace;
 extern size_t g_decode_trace_bytes;
+// test hook: extra arrivals the next decode launches' grid barrier waits for (capi.cu)
+extern int g_decode_barrier_extra;
 cudaError_t launch_decode_layer(const DecodeArgs& a, cudaStream_t st);
 
 // prefill.cu

@@ -12,10 +12,12 @@
 // The array is a file-scope __device__ variable: every GPU that loads the library holds
 // kNoAllocScratchBytes of it until the process exits. All calls on a device share it and it
 // keeps the previous call's contents, so two calls whose work overlaps on the GPU (different
-// streams without ordering between them) race on it. The kernel's control counters at the
-// start of the array are zero when the library is loaded (a __device__ array is zero-filled)
-// and every call leaves them zero again; every other scratch byte a call reads is written
-// earlier in the same call.
+// streams without ordering between them) race on it. The control block at the start of the
+// array is zero when the library is loaded (a __device__ array is zero-filled); a call's own
+// counters return to a state the next call accepts, and every other scratch byte a call reads
+// is written earlier in the same call. Its status word is sticky: a call whose device-side
+// bounded wait gave up writes NaN over its output and records the failure there, and
+// uocr_moe_decode_noalloc_status reads and clears it (later calls compute normally either way).
 //
 // The first call on each device looks up the array's device address (cudaGetSymbolAddress,
 // with that device current) and caches it; that first call should come before any stream
@@ -62,6 +64,7 @@ cudaError_t scratch_address(void** out) {
 
 namespace uocr {
 int set_error(int code, const char* msg);  // capi.cu: sets what uocr_last_error() reports
+int read_clear_status(const void* workspace, cudaStream_t stream, uint32_t* code);  // capi.cu
 }  // namespace uocr
 
 extern "C" UOCR_API size_t uocr_moe_decode_noalloc_max_bytes(void) { return kNoAllocScratchBytes; }
@@ -88,4 +91,15 @@ extern "C" UOCR_API int uocr_moe_decode_noalloc(const uocr_moe_layer* L, const f
     // The regular entry point with the in-library array as its workspace (it validates the
     // layer and keeps the routing in the workspace).
     return uocr_moe_decode(L, x, B, bias, out, nullptr, nullptr, base, kNoAllocScratchBytes, stream);
+}
+
+extern "C" UOCR_API int uocr_moe_decode_noalloc_status(uocr_stream_t stream) {
+    void* base = nullptr;
+    const cudaError_t err = scratch_address(&base);
+    if (err != cudaSuccess) {
+        const std::string m = std::string("moe_decode_noalloc_status: cudaGetSymbolAddress: ") + cudaGetErrorString(err);
+        return uocr::set_error(UOCR_ECUDA, m.c_str());
+    }
+    uint32_t code = 0;
+    return uocr::read_clear_status(base, reinterpret_cast<cudaStream_t>(stream), &code);
 }

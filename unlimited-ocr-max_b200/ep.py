@@ -246,6 +246,20 @@ class ExpertParallelMoE:
         self.local.load_state_dict(local)
         return self
 
+    def check_status(self) -> None:
+        """Synchronise and read (clearing) the device status of this rank's workspaces (the local
+        experts', the shared experts' and the local module's): raises :class:`UocrError` if a
+        device-side bounded wait gave up since the last check."""
+        from ._lib import check as _check
+
+        L = load()
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        for name in ("ep", "shared"):
+            ws = self._ws.get(name)
+            if ws is not None:
+                _check(L.uocr_moe_device_status(ws.data_ptr(), stream))
+        self.local.check_status()
+
     def _workspace(self, name: str, nbytes: int) -> torch.Tensor:
         ws = self._ws.get(name)
         if ws is None or ws.numel() < nbytes:

@@ -77,6 +77,16 @@ class MoEConfig:
         return self.n_shared_experts * self.moe_intermediate_size
 
 
+def _dtype_name(d) -> str | None:
+    """A dtype given as a torch dtype, a name, or an object with ``.name`` -> its bare name."""
+    if d is None:
+        return None
+    if isinstance(d, torch.dtype):
+        return str(d).removeprefix("torch.")
+    name = getattr(d, "name", d)
+    return str(name).removeprefix("torch.").lower()
+
+
 def _unkblock(w: torch.Tensor) -> torch.Tensor:
     """A shared-expert projection as ``[N, K]``: accepts the plain checkpoint form or the
     reference's K-blocked declaration ``[K/16, N, 16]`` (decoder.py:219-225)."""
@@ -89,8 +99,22 @@ def _unkblock(w: torch.Tensor) -> torch.Tensor:
 class UocrMoE:
     """64 routed experts, top-6, plus the shared experts (decoder.py:517-554)."""
 
-    def __init__(self, config: MoEConfig, *, device: str | torch.device = "cuda") -> None:
+    def __init__(self, config: MoEConfig, *, dtype=None, device: str | torch.device = "cuda",
+                 norm_router_dtype=None) -> None:
+        """``MoE(config, *, dtype, device, norm_router_dtype=None)`` (decoder.py:533-535).
+
+        ``dtype`` is the non-expert weights' dtype: bf16 (the checkpoint's), the only one this
+        build takes. ``norm_router_dtype`` is the dtype the router weight is held in: bf16, or
+        fp32 holding bf16 values exactly (the accelerator pipeline's upcast, pipeline.py:380-389);
+        either way the logits are fp32 sums of the same products. Both accept a torch dtype, a
+        name ("bfloat16"), or any object whose ``.name`` is one (a MAX ``DType``)."""
         self.config = config
+        if _dtype_name(dtype) not in (None, "bfloat16"):
+            raise ConfigError(f"UocrMoE: dtype {_dtype_name(dtype)} (this build holds the non-expert weights in bfloat16)")
+        if _dtype_name(norm_router_dtype) not in (None, "bfloat16", "float32"):
+            raise ConfigError(f"UocrMoE: norm_router_dtype {_dtype_name(norm_router_dtype)} (bfloat16 or float32)")
+        self.dtype = torch.bfloat16
+        self.norm_router_dtype = norm_router_dtype
         self.device = torch.device(device)
         if self.device.type != "cuda":
             raise ValueError("UocrMoE runs on a CUDA device only (no CPU path)")
@@ -170,6 +194,26 @@ class UocrMoE:
         self._layer = lay
         return self
 
+    @classmethod
+    def from_checkpoint(cls, checkpoint: Mapping[str, torch.Tensor], layer: int, config: MoEConfig | None = None,
+                        *, device: str | torch.device = "cuda") -> "UocrMoE":
+        """Decoder layer ``layer``'s MoE from checkpoint tensors named as in the model file
+        (``model.layers.{L}.mlp.experts.{E}.{proj}.weight`` [+ ``_scales``], ``...mlp.gate.weight``,
+        ``...mlp.shared_experts.{proj}.weight``): stacked and checked as the reference's weight
+        adapter does (``weights.moe_layer_state``), then packed. The int8 form is detected from
+        the checkpoint; ``config`` (default: the model's MoE fields) must agree with it."""
+        from .weights import WeightMappingError, moe_layer_state
+
+        cfg = config or MoEConfig()
+        state, int8 = moe_layer_state(checkpoint, layer, num_experts=cfg.n_routed_experts)
+        if config is None:
+            cfg = MoEConfig(int8_experts=int8)
+        elif cfg.int8_experts != int8:
+            raise WeightMappingError(
+                f"the checkpoint's experts are {'int8' if int8 else 'bfloat16'} but the config declares "
+                f"{'int8' if cfg.int8_experts else 'bfloat16'}")
+        return cls(cfg, device=device).load_state_dict(state)
+
     @property
     def layer(self) -> UocrMoeLayer:
         if self._layer is None:
@@ -194,9 +238,20 @@ class UocrMoE:
             raise ValueError(f"UocrMoE: x must be [rows, {self.config.hidden_size}], got {tuple(x.shape)}")
         return x.contiguous()
 
+    def check_status(self) -> None:
+        """Synchronise and read (clearing) the device status of every workspace of this layer:
+        raises :class:`UocrError` (code UOCR_EDEVICE) if a device-side bounded wait of any call
+        since the last check gave up. Such a call wrote NaN over its output instead of a result."""
+        L = load()
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        for ws in list(self._ws.values()):
+            check(L.uocr_moe_device_status(ws.data_ptr(), stream))
+
     def decode_rows(self, x: torch.Tensor, *, out: torch.Tensor | None = None, ids: torch.Tensor | None = None,
-                    wts: torch.Tensor | None = None) -> torch.Tensor:
-        """MoE.decode_rows (decoder.py:641-655): routed top-k + shared experts for B rows."""
+                    wts: torch.Tensor | None = None, check_status: bool = False) -> torch.Tensor:
+        """MoE.decode_rows (decoder.py:641-655): routed top-k + shared experts for B rows.
+        ``check_status=True`` synchronises after the call and raises if a device-side wait gave
+        up (otherwise such a failure shows as NaN output and in :meth:`check_status`)."""
         x = self._check_x(x)
         B = x.shape[0]
         if out is None:
@@ -215,6 +270,8 @@ class UocrMoE:
                 0 if self.bias is None else self.bias.data_ptr(), out[b0:b1].data_ptr(),
                 0 if ids is None else ids[b0:b1].data_ptr(), 0 if wts is None else wts[b0:b1].data_ptr(),
                 ws.data_ptr(), ws.numel(), stream))
+        if check_status:
+            self.check_status()
         return out
 
     def prefill_workspace(self, T: int) -> torch.Tensor:
@@ -248,8 +305,11 @@ class UocrMoE:
 
     def __call__(self, x: torch.Tensor) -> torch.Tensor:
         """MoE.__call__ (decoder.py:657-667): the MoE over ``x [T, H]``. Up to DECODE_MAX_B rows
-        run the decode kernels (exact fp32 products, one weight read per selected expert);
-        longer inputs run :meth:`prefill` when hidden_size is a multiple of 256."""
+        run the decode kernels (one weight read per selected expert; the activations enter the
+        tensor cores as three int8 digit planes per 128-group for int8 experts, exact to 2^-21 of
+        the group's largest value, and as two bf16 terms for bf16 weights, exact to about 2^-17
+        relative; fp32 accumulation); longer inputs run :meth:`prefill` (bf16 activations into
+        grouped bf16 GEMMs) when hidden_size is a multiple of 256."""
         if x.dim() == 2 and x.shape[0] > DECODE_MAX_B and self.config.hidden_size % 256 == 0:
             return self.prefill(x)
         return self.decode_rows(x)
