@@ -62,6 +62,8 @@ def parse():
     p.add_argument("--ep-tokens", type=int, default=65536, help="EP prefill tokens over all ranks (configs[4])")
     p.add_argument("--ep-overlap", choices=["on", "off"], default="on",
                    help="EP: run the shared experts on a side stream during the exchanges (on) or in line (off)")
+    p.add_argument("--ep-exchange", choices=["peer", "nccl"], default="peer",
+                   help="EP: peer-memory exchange (stores into the other GPUs' buffers) or the NCCL all-to-alls")
     p.add_argument("--ep-phases", action="store_true",
                    help="EP: add per-phase device times of rank 0 (after the timed region) to the JSON line")
     p.add_argument("--ep-placement", choices=["balanced", "contiguous"], default="balanced",
@@ -524,8 +526,8 @@ def ep_measure(args, torch, uocr, synth, dist, world, rank, device, steps: int, 
         dist.all_reduce(calib)
         placement = ep_mod.balanced_placement(calib.cpu(), world)
         del xc, ids_c
-    moe = ep_mod.ExpertParallelMoE(cfg, device=device, placement=placement,
-                                   overlap_shared=args.ep_overlap == "on").load_state_dict(st)
+    moe = ep_mod.ExpertParallelMoE(cfg, device=device, placement=placement, overlap_shared=args.ep_overlap == "on",
+                                   exchange=args.ep_exchange).load_state_dict(st)
     del st
     moe.bias = bias
     x = synth.hidden_states(T_all, H, 5002, device=device)[rank * T:(rank + 1) * T].contiguous()
@@ -566,6 +568,7 @@ def ep_measure(args, torch, uocr, synth, dist, world, rank, device, steps: int, 
     finite = bool(torch.isfinite(out).all())
     fin = torch.tensor([int(finite)], device=device)
     dist.all_reduce(fin, op=dist.ReduceOp.MIN)
+    moe.close()
     tc, tc_src = measured_tc_peak()
     flop = PREFILL_FLOP_PER_TOKEN * T_all
     tflops = flop / (ms * 1e-3) / 1e12
@@ -580,7 +583,7 @@ def ep_measure(args, torch, uocr, synth, dist, world, rank, device, steps: int, 
         "value": T_all / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "tokens": T_all, "tokens_per_rank": T,
         "ms_per_step": ms, "steps": steps, "tflops": tflops, "tc_frac_per_gpu": tflops / world / tc,
         "tc_peak": tc, "tc_peak_source": tc_src + " (burst)",
-        "expert_placement": args.ep_placement, "shared_overlap": args.ep_overlap,
+        "expert_placement": args.ep_placement, "shared_overlap": args.ep_overlap, "exchange": args.ep_exchange,
         "expert_rows_per_rank": per_rank,
         "rank0_remote_rows": {"sent": sent_rank, "received": recv_rank},
         "rank0_exchange_bytes": {"dispatch": (sent_rank + recv_rank) * row_bytes,
@@ -592,9 +595,11 @@ def ep_measure(args, torch, uocr, synth, dist, world, rank, device, steps: int, 
     if ph is not None:
         r["phases_ms_rank0"] = ph
         xr, xb = ph.get("exchange_rows"), ph.get("exchange_back")
-        if world > 1 and xr and xb:
+        if world > 1 and xr and xb:  # the NCCL exchanges: bytes in and out over their phase times
             r["rank0_exchange_gbs"] = {"dispatch": r["rank0_exchange_bytes"]["dispatch"] / (xr * 1e-3) / 1e9,
                                        "combine": r["rank0_exchange_bytes"]["combine"] / (xb * 1e-3) / 1e9}
+        elif world > 1 and ph.get("dispatch"):  # peer stores: the rows rank 0 sends, over its dispatch kernels
+            r["rank0_exchange_gbs"] = {"dispatch_sent": sent_rank * row_bytes / (ph["dispatch"] * 1e-3) / 1e9}
     return r
 
 

@@ -215,6 +215,51 @@ UOCR_API int uocr_moe_ep_dispatch(const float* x, int64_t T, int64_t H, const in
 UOCR_API int uocr_moe_ep_combine(const float* partials, int64_t n_rows, const int32_t* inv, int64_t T,
                                  int64_t world, int64_t H, const float* add, float* out, uocr_stream_t stream);
 
+/* ---- the expert-parallel exchange through peer memory (no counterpart in the reference) ----
+ * What ExpertParallelMoE runs: no all-to-all and no host synchronisation. Every rank allocates one
+ * exchange buffer of uocr_moe_ep_peer_buffer_bytes (zero-filled, 256-byte aligned, the same size on
+ * every rank) and maps every other rank's into its process (uocr_ipc_export / uocr_ipc_import).
+ * A forward on every rank, with the same increasing epoch:
+ *   1. uocr_moe_ep_peer_dispatch: the plan of uocr_moe_ep_dispatch, but every (token, destination)
+ *      row (bf16) and its slot metadata (local expert ids, weights) is stored straight into the
+ *      destination's buffer, slot `rank`; then the row count and the epoch are published there.
+ *      inv [world, T] receives each token's position in each destination's slot (-1: none).
+ *   2. uocr_moe_ep_peer_experts: waits (bounded) for every source's rows of this epoch, applies L's
+ *      routed experts (a slice of E_local experts, expert products as in uocr_moe_prefill) to the
+ *      received rows, and stores each row's weighted sum as bf16 straight back into its source's
+ *      buffer; then flags every source.
+ *   3. uocr_moe_ep_peer_combine: waits (bounded) for every expert rank's flag of this epoch, then
+ *      out[t] = (sum over ranks p ascending, from +0, of float(partial of (t, p))) + add[t].
+ * A wait that gives up (a rank that never comes: 20 s), or a received count above cap_tokens, sets
+ * the buffer's status (uocr_moe_device_status(buf[rank]) reports and clears it); the affected
+ * sources are flagged and their outputs, and every output while the status is set, are NaN. */
+#define UOCR_IPC_HANDLE_BYTES 64
+typedef struct uocr_ep_peers {
+    int32_t world;       /* ranks, 1..8 */
+    int32_t rank;        /* this process's rank */
+    int32_t cap_tokens;  /* tokens per rank the slots hold: at least every rank's T */
+    int32_t hidden;      /* H, multiple of 256 */
+    int32_t top_k;       /* k */
+    int32_t reserved;
+    uint64_t epoch;      /* this forward's number: 1, 2, ..., the same on every rank */
+    void* buf[8];        /* rank p's exchange buffer as mapped in this process (buf[rank]: its own) */
+} uocr_ep_peers;
+UOCR_API size_t uocr_moe_ep_peer_buffer_bytes(int64_t world, int64_t cap_tokens, int64_t hidden, int64_t top_k);
+UOCR_API size_t uocr_moe_ep_peer_workspace_bytes(const uocr_moe_layer* L, const uocr_ep_peers* P);
+UOCR_API int uocr_moe_ep_peer_dispatch(const uocr_ep_peers* P, const float* x, int64_t T, const int32_t* ids,
+                                       const float* wts, const int32_t* owner, const int32_t* local, int64_t E,
+                                       int32_t* inv, void* workspace, size_t workspace_bytes, uocr_stream_t stream);
+UOCR_API int uocr_moe_ep_peer_experts(const uocr_moe_layer* L, const uocr_ep_peers* P, void* workspace,
+                                      size_t workspace_bytes, uocr_stream_t stream);
+UOCR_API int uocr_moe_ep_peer_combine(const uocr_ep_peers* P, const int32_t* inv, int64_t T, const float* add,
+                                      float* out, uocr_stream_t stream);
+/* CUDA IPC for the exchange buffers: the handle (UOCR_IPC_HANDLE_BYTES) and offset of a device
+ * pointer inside its allocation, and the mapping of another process's (current device; peer
+ * access enabled on first use). Plain peer loads and stores only: no multicast object is made. */
+UOCR_API int uocr_ipc_export(const void* dev_ptr, void* handle_out, uint64_t* offset_out);
+UOCR_API int uocr_ipc_import(const void* handle, uint64_t offset, void** dev_ptr_out);
+UOCR_API int uocr_ipc_close(void* dev_ptr, uint64_t offset);
+
 /* The shared experts of L alone over x [T, H] fp32 (bf16 products, fp32 out): out = shared(x),
  * or out += shared(x) with accumulate != 0. Meant to run beside the expert-parallel exchanges:
  * its GEMMs leave 16 SMs free for concurrent kernels (NCCL's). */

@@ -1,9 +1,10 @@
 """GPU parity of the expert-parallel pieces through the C ABI: uocr_moe_ep_experts (local experts
 over received bf16 rows, entries without a local expert skipped), uocr_moe_shared_forward, and
-ExpertParallelMoE end to end (one NCCL rank on one GPU; two ranks when two GPUs are visible),
+ExpertParallelMoE end to end, with the peer-memory exchange and with the NCCL bookkeeping, on 1, 2,
+4 and 8 ranks (one process per GPU; the cases with more ranks than visible GPUs are skipped),
 against the float64 layer fed the bit-exact routing, at the prefill tolerance. The dispatch and
 combine kernels (uocr_moe_ep_dispatch / uocr_moe_ep_combine) must reproduce the torch
-bookkeeping of ep.py bit for bit, and so must the whole device path."""
+bookkeeping of ep.py bit for bit, and so must the whole device path of either exchange."""
 
 from __future__ import annotations
 
@@ -177,14 +178,21 @@ def _free_port() -> int:
         return s.getsockname()[1]
 
 
-def _ep_worker(rank: int, world: int, port: int, T: int, out_dir: str, kind: str) -> None:
+def _token_split(T: int, world: int, kind: str) -> list[int]:
+    """Tokens per rank: equal, or ragged (rank r has 37 r fewer)."""
+    return [T - 37 * r for r in range(world)] if kind == "ragged" else [T] * world
+
+
+def _ep_worker(rank: int, world: int, port: int, T: int, out_dir: str, kind: str, exchange: str) -> None:
     import sys
 
     sys.path.insert(0, str(ROOT))
     sys.path.insert(0, str(ROOT / "tests"))
     os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
     torch.cuda.set_device(rank)
     dist.init_process_group("nccl", rank=rank, world_size=world, device_id=torch.device("cuda", rank))
+    m = None
     try:
         from oracle import moe_oracle as o
 
@@ -195,35 +203,44 @@ def _ep_worker(rank: int, world: int, port: int, T: int, out_dir: str, kind: str
         if kind == "strided":  # every world-th expert, in descending order: local != global index
             placement = ep.ExpertPlacement([list(range(63 - p, -1, -world)) for p in range(world)])
         m = ep.ExpertParallelMoE(uocr.MoEConfig(), device=f"cuda:{rank}", placement=placement,
-                                 overlap_shared=kind != "strided")
+                                 overlap_shared=kind != "strided", exchange=exchange, timeout_s=120)
         m.load_state_dict(to_state(w, cfg, False))
         bias = np.random.default_rng(8).standard_normal(64).astype(np.float32)
         m.bias = torch.from_numpy(bias).to(f"cuda:{rank}")
-        x = o.synth_hidden(T * world, cfg.hidden, 9)[rank * T:(rank + 1) * T]
+        ts = _token_split(T, world, kind)
+        x = o.synth_hidden(sum(ts), cfg.hidden, 9)[sum(ts[:rank]):sum(ts[:rank + 1])]
         xd = torch.from_numpy(x).to(f"cuda:{rank}")
         got = m(xd)
-        # the device bookkeeping reproduces the torch bookkeeping bit for bit
+        # the device exchange reproduces the torch bookkeeping of ep_forward bit for bit
         assert torch.equal(got, m.forward_reference(xd))
         assert torch.equal(got, m(xd))
         ph = m.profile_phases(xd, 2)
-        assert list(ph) == ["route", "dispatch", "counts", "exchange_rows", "experts", "exchange_back", "shared_wait",
-                            "combine"] and all(v >= 0 for v in ph.values())
+        want = (["route", "dispatch", "experts", "shared_wait", "combine"] if exchange == "peer" else
+                ["route", "dispatch", "counts", "exchange_rows", "experts", "exchange_back", "shared_wait", "combine"])
+        assert list(ph) == want and all(v >= 0 for v in ph.values())
+        assert torch.equal(m(xd), got)  # after the phase calls (later epochs) still the same bits
+        m.check_status()
         np.save(os.path.join(out_dir, f"ep{rank}.npy"), got.cpu().numpy())
         dist.barrier()
     finally:
+        if m is not None:
+            m.close()
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("kind", ["contiguous", "strided"])
-@pytest.mark.parametrize("world", [1, 2])
-def test_expert_parallel_moe(oracle, tmp_path, world, kind):
+@pytest.mark.parametrize("exchange", ["peer", "nccl"])
+@pytest.mark.parametrize("kind", ["contiguous", "strided", "ragged"])
+@pytest.mark.parametrize("world", [1, 2, 4, 8])
+def test_expert_parallel_moe(oracle, tmp_path, world, kind, exchange):
     if torch.cuda.device_count() < world:
         pytest.skip(f"needs {world} GPUs")
+    if kind == "ragged" and world == 1:
+        pytest.skip("one rank: nothing to be ragged against")
     T = 512
-    mp.spawn(_ep_worker, args=(world, _free_port(), T, str(tmp_path), kind), nprocs=world, join=True)
+    mp.spawn(_ep_worker, args=(world, _free_port(), T, str(tmp_path), kind, exchange), nprocs=world, join=True)
     got = np.concatenate([np.load(tmp_path / f"ep{r}.npy") for r in range(world)])
     cfg, w = full_layer(oracle, False, 4)
     bias = np.random.default_rng(8).standard_normal(64).astype(np.float32)
-    x = oracle.synth_hidden(T * world, cfg.hidden, 9)
+    x = oracle.synth_hidden(sum(_token_split(T, world, kind)), cfg.hidden, 9)
     r = oracle.route_fp32(x, w.router, bias, 6)
     _check(oracle, got, oracle.moe_layer_fp64(cfg, w, x, r.ids, r.weights))

@@ -21,6 +21,21 @@ I64 = ctypes.c_int64
 SZ = ctypes.c_size_t
 
 
+class UocrEpPeers(ctypes.Structure):
+    """Mirror of ``struct uocr_ep_peers`` (include/uocr_moe.h)."""
+
+    _fields_ = [
+        ("world", ctypes.c_int32),
+        ("rank", ctypes.c_int32),
+        ("cap_tokens", ctypes.c_int32),
+        ("hidden", ctypes.c_int32),
+        ("top_k", ctypes.c_int32),
+        ("reserved", ctypes.c_int32),
+        ("epoch", ctypes.c_uint64),
+        ("buf", ctypes.c_void_p * 8),
+    ]
+
+
 class UocrMoeLayer(ctypes.Structure):
     """Mirror of ``struct uocr_moe_layer`` (include/uocr_moe.h)."""
 
@@ -71,6 +86,14 @@ SIGNATURES: dict[str, tuple] = {
     "uocr_moe_decode_noalloc_max_bytes": (SZ, []),
     "uocr_moe_decode_noalloc": (I32, [ctypes.POINTER(UocrMoeLayer), P, I64, P, P, P]),
     "uocr_moe_decode_noalloc_status": (I32, [P]),
+    "uocr_moe_ep_peer_buffer_bytes": (SZ, [I64, I64, I64, I64]),
+    "uocr_moe_ep_peer_workspace_bytes": (SZ, [ctypes.POINTER(UocrMoeLayer), ctypes.POINTER(UocrEpPeers)]),
+    "uocr_moe_ep_peer_dispatch": (I32, [ctypes.POINTER(UocrEpPeers), P, I64, P, P, P, P, I64, P, P, SZ, P]),
+    "uocr_moe_ep_peer_experts": (I32, [ctypes.POINTER(UocrMoeLayer), ctypes.POINTER(UocrEpPeers), P, SZ, P]),
+    "uocr_moe_ep_peer_combine": (I32, [ctypes.POINTER(UocrEpPeers), P, I64, P, P, P]),
+    "uocr_ipc_export": (I32, [P, P, ctypes.POINTER(ctypes.c_uint64)]),
+    "uocr_ipc_import": (I32, [P, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]),
+    "uocr_ipc_close": (I32, [P, ctypes.c_uint64]),
     "uocr_moe_test_barrier_extra": (I32, [I32]),
 }
 

@@ -2,9 +2,13 @@
 // reference ops' error messages, then kernel launches on the caller's stream.
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 #include <string>
 #include <unordered_map>
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
 
 #include "../../include/uocr_moe.h"
 #include "common.cuh"
@@ -62,7 +66,10 @@ int read_clear_status(const void* workspace, cudaStream_t stream, uint32_t* code
         err = cudaMemset(const_cast<void*>(workspace), 0, kCtlClearBytes);
         if (err != cudaSuccess) return fail(UOCR_ECUDA, "device_status: clear: %s", cudaGetErrorString(err));
         return fail(UOCR_EDEVICE, "device_status: a device-side check failed (code %u: %s); cleared", *code,
-                    *code == 1 ? "a bounded wait gave up" : *code == 2 ? "shared memory misaligned" : "unknown");
+                    *code == 1 ? "a bounded wait gave up"
+                    : *code == 2 ? "shared memory misaligned"
+                    : *code == 3 ? "an exchanged row count above the slot capacity"
+                                 : "unknown");
     }
     return ok();
 }
@@ -542,6 +549,176 @@ int uocr_moe_shared_forward(const uocr_moe_layer* L, const float* x, int64_t T, 
     a.w13_shared = L->w13_shared; a.w2_shared = L->w2_shared;
     a.out = out;
     return cuda_status(uocr::launch_prefill(a, ws, d, S(stream)), "moe_shared_forward: launch");
+}
+
+// ---------------------------------------------------------------------------------------
+// expert-parallel exchange through peer memory
+// ---------------------------------------------------------------------------------------
+
+static int check_peers(const uocr_ep_peers* P, const char* who) {
+    if (!P) return fail(UOCR_EINVAL, "%s: null peers", who);
+    if (P->world < 1 || P->world > uocr::kEpMaxWorld)
+        return fail(UOCR_EUNSUPPORTED, "%s: world=%d outside 1..%d", who, P->world, uocr::kEpMaxWorld);
+    if (P->rank < 0 || P->rank >= P->world) return fail(UOCR_EINVAL, "%s: rank=%d outside [0, world)", who, P->rank);
+    if (P->cap_tokens < 1 || P->cap_tokens > (1 << 22))
+        return fail(UOCR_EINVAL, "%s: cap_tokens=%d outside 1..2^22", who, P->cap_tokens);
+    if (P->hidden < 256 || P->hidden % 256 || P->hidden > 8192)
+        return fail(UOCR_EUNSUPPORTED, "%s: hidden=%d must be a multiple of 256 up to 8192", who, P->hidden);
+    if (P->top_k < 1 || P->top_k > uocr::kDecodeMaxTopk) return fail(UOCR_EINVAL, "%s: top_k=%d outside 1..8", who, P->top_k);
+    if (P->epoch < 1 || P->epoch > (1ull << 62)) return fail(UOCR_EINVAL, "%s: epoch must be 1..2^62", who);
+    if ((int64_t)P->world * P->cap_tokens * P->top_k >= (int64_t(1) << 31))
+        return fail(UOCR_EUNSUPPORTED, "%s: world * cap_tokens * top_k exceeds int32", who);
+    for (int q = 0; q < P->world; ++q)
+        if (!P->buf[q] || (reinterpret_cast<uintptr_t>(P->buf[q]) & 255))
+            return fail(UOCR_EINVAL, "%s: buf[%d] null or not 256-byte aligned", who, q);
+    return ok();
+}
+
+static uocr::EpPeers to_peers(const uocr_ep_peers* P) {
+    uocr::EpPeers e{};
+    e.world = P->world; e.rank = P->rank; e.cap = P->cap_tokens; e.H = P->hidden; e.k = P->top_k;
+    e.epoch = P->epoch;
+    for (int q = 0; q < P->world; ++q) e.buf[q] = reinterpret_cast<unsigned char*>(P->buf[q]);
+    return e;
+}
+
+static uocr::EpPeerScratch peer_scratch(const uocr_moe_layer* L, const uocr_ep_peers* P) {
+    const int rows = P->world * P->cap_tokens;
+    const size_t pre =
+        uocr::prefill_layout(rows, L->hidden, L->inter, L->n_routed, 0, L->top_k, L->int8 != 0).total;
+    return uocr::ep_peer_scratch(P->world, P->cap_tokens, L->hidden, L->inter, L->n_routed, L->top_k, L->int8 != 0,
+                                 pre);
+}
+
+size_t uocr_moe_ep_peer_buffer_bytes(int64_t world, int64_t cap_tokens, int64_t hidden, int64_t top_k) {
+    if (world < 1 || world > uocr::kEpMaxWorld || cap_tokens < 1 || cap_tokens > (1 << 22) || hidden < 8 ||
+        hidden > 8192 || top_k < 1 || top_k > uocr::kDecodeMaxTopk)
+        return 0;
+    return uocr::ep_peer_layout((int)world, (int)cap_tokens, (int)hidden, (int)top_k).total;
+}
+
+size_t uocr_moe_ep_peer_workspace_bytes(const uocr_moe_layer* L, const uocr_ep_peers* P) {
+    if (!L || !P || P->world < 1 || P->world > uocr::kEpMaxWorld || P->cap_tokens < 1) return 0;
+    return peer_scratch(L, P).total;
+}
+
+int uocr_moe_ep_peer_dispatch(const uocr_ep_peers* P, const float* x, int64_t T, const int32_t* ids,
+                              const float* wts, const int32_t* owner, const int32_t* local, int64_t E, int32_t* inv,
+                              void* workspace, size_t workspace_bytes, uocr_stream_t stream) {
+    int rc = check_peers(P, "moe_ep_peer_dispatch");
+    if (rc) return rc;
+    if (T < 0 || T > P->cap_tokens)
+        return fail(UOCR_EINVAL, "moe_ep_peer_dispatch: T=%lld outside 0..cap_tokens=%d", (long long)T, P->cap_tokens);
+    if (E < 1 || E > 4096) return fail(UOCR_EINVAL, "moe_ep_peer_dispatch: E=%lld outside 1..4096", (long long)E);
+    if ((T > 0 && (!x || !ids || !wts || !inv)) || !owner || !local || !workspace)
+        return fail(UOCR_EINVAL, "moe_ep_peer_dispatch: null pointer");
+    if (T > 0 && !a16(x)) return fail(UOCR_EINVAL, "moe_ep_peer_dispatch: x must be 16-byte aligned");
+    if (reinterpret_cast<uintptr_t>(workspace) & 255)
+        return fail(UOCR_EINVAL, "moe_ep_peer_dispatch: workspace must be 256-byte aligned");
+    // the dispatch part of the scratch does not depend on the layer: size it with a stand-in
+    const uocr::EpPeerScratch d = uocr::ep_peer_scratch(P->world, P->cap_tokens, P->hidden, 0, 0, P->top_k, false, 0);
+    if (workspace_bytes < d.prefill)
+        return fail(UOCR_EINVAL, "moe_ep_peer_dispatch: workspace of %zu bytes, need %zu", workspace_bytes, d.prefill);
+    return cuda_status(uocr::launch_ep_peer_dispatch(to_peers(P), x, (int)T, ids, wts, owner, local, (int)E, inv,
+                                                     reinterpret_cast<char*>(workspace), d, S(stream)),
+                       "moe_ep_peer_dispatch: launch");
+}
+
+int uocr_moe_ep_peer_experts(const uocr_moe_layer* L, const uocr_ep_peers* P, void* workspace, size_t workspace_bytes,
+                             uocr_stream_t stream) {
+    int rc = check_layer(L, "moe_ep_peer_experts");
+    if (rc) return rc;
+    rc = check_peers(P, "moe_ep_peer_experts");
+    if (rc) return rc;
+    if (P->hidden != L->hidden || P->top_k != L->top_k)
+        return fail(UOCR_EINVAL, "moe_ep_peer_experts: peers and layer disagree on hidden or top_k");
+    if (!workspace || (reinterpret_cast<uintptr_t>(workspace) & 255))
+        return fail(UOCR_EINVAL, "moe_ep_peer_experts: workspace null or not 256-byte aligned");
+    const uocr::EpPeerScratch d = peer_scratch(L, P);
+    if (workspace_bytes < d.total)
+        return fail(UOCR_EINVAL, "moe_ep_peer_experts: workspace of %zu bytes, need %zu", workspace_bytes, d.total);
+    const int rows = P->world * P->cap_tokens;
+    const uocr::EpPeerLayout X = uocr::ep_peer_layout(P->world, P->cap_tokens, P->hidden, P->top_k);
+    const uocr::EpPeers peers = to_peers(P);
+    char* ws = reinterpret_cast<char*>(workspace);
+    cudaError_t err = uocr::launch_ep_peer_wait(peers, ws, d, S(stream));
+    if (err != cudaSuccess) return cuda_status(err, "moe_ep_peer_experts: wait");
+    unsigned char* own = peers.buf[peers.rank];
+    uocr::PrefillArgs a{};
+    a.T = rows; a.H = L->hidden; a.I = L->inter; a.E = L->n_routed; a.S = 0; a.topk = L->top_k;
+    a.G = L->int8 ? L->group : 128; a.int8 = L->int8;
+    a.route = 0; a.use_shared = 0; a.accumulate = 0;
+    a.x_bf16 = reinterpret_cast<const uint16_t*>(own + X.rows);
+    a.ids = reinterpret_cast<int32_t*>(own + X.eid);
+    a.wts = reinterpret_cast<float*>(own + X.w);
+    a.w13 = L->w13; a.w2 = L->w2;
+    a.peers = &peers;
+    a.slot_counts = reinterpret_cast<const int*>(ws + d.hdr + uocr::kEpHdrSlotCounts);
+    a.slot_fail = reinterpret_cast<const int*>(ws + d.hdr + uocr::kEpHdrSlotFail);
+    a.done = reinterpret_cast<unsigned int*>(ws + d.hdr + uocr::kEpHdrDonePart);
+    a.status = reinterpret_cast<uint32_t*>(own + X.status);
+    const uocr::PrefillLayout pl =
+        uocr::prefill_layout(rows, L->hidden, L->inter, L->n_routed, 0, L->top_k, L->int8 != 0);
+    return cuda_status(uocr::launch_prefill(a, ws + d.prefill, pl, S(stream)), "moe_ep_peer_experts: launch");
+}
+
+int uocr_moe_ep_peer_combine(const uocr_ep_peers* P, const int32_t* inv, int64_t T, const float* add, float* out,
+                             uocr_stream_t stream) {
+    int rc = check_peers(P, "moe_ep_peer_combine");
+    if (rc) return rc;
+    if (T < 0 || T > P->cap_tokens)
+        return fail(UOCR_EINVAL, "moe_ep_peer_combine: T=%lld outside 0..cap_tokens=%d", (long long)T, P->cap_tokens);
+    if (T > 0 && (!inv || !out)) return fail(UOCR_EINVAL, "moe_ep_peer_combine: null pointer");
+    if ((out && !a16(out)) || (add && !a16(add)))
+        return fail(UOCR_EINVAL, "moe_ep_peer_combine: add and out must be 16-byte aligned");
+    return cuda_status(uocr::launch_ep_peer_combine(to_peers(P), inv, (int)T, add, out, S(stream)),
+                       "moe_ep_peer_combine: launch");
+}
+
+static PFN_cuMemGetAddressRange_v3020 address_range_fn() {
+    static PFN_cuMemGetAddressRange_v3020 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void* p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuMemGetAddressRange_v3020>(p);
+    });
+    return fn;
+}
+
+int uocr_ipc_export(const void* dev_ptr, void* handle_out, uint64_t* offset_out) {
+    if (!dev_ptr || !handle_out || !offset_out) return fail(UOCR_EINVAL, "ipc_export: null pointer");
+    auto range = address_range_fn();
+    if (!range) return fail(UOCR_ECUDA, "ipc_export: cuMemGetAddressRange unavailable");
+    CUdeviceptr base = 0;
+    size_t size = 0;
+    if (range(&base, &size, reinterpret_cast<CUdeviceptr>(dev_ptr)) != CUDA_SUCCESS)
+        return fail(UOCR_EINVAL, "ipc_export: not a device allocation");
+    cudaIpcMemHandle_t h;
+    cudaError_t err = cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base));
+    if (err != cudaSuccess) return cuda_status(err, "ipc_export: cudaIpcGetMemHandle");
+    static_assert(sizeof(h) == UOCR_IPC_HANDLE_BYTES, "IPC handle size");
+    memcpy(handle_out, &h, sizeof h);
+    *offset_out = reinterpret_cast<uint64_t>(dev_ptr) - (uint64_t)base;
+    return ok();
+}
+
+int uocr_ipc_import(const void* handle, uint64_t offset, void** dev_ptr_out) {
+    if (!handle || !dev_ptr_out) return fail(UOCR_EINVAL, "ipc_import: null pointer");
+    cudaIpcMemHandle_t h;
+    memcpy(&h, handle, sizeof h);
+    void* base = nullptr;
+    cudaError_t err = cudaIpcOpenMemHandle(&base, h, cudaIpcMemLazyEnablePeerAccess);
+    if (err != cudaSuccess) return cuda_status(err, "ipc_import: cudaIpcOpenMemHandle");
+    *dev_ptr_out = reinterpret_cast<char*>(base) + offset;
+    return ok();
+}
+
+int uocr_ipc_close(void* dev_ptr, uint64_t offset) {
+    if (!dev_ptr) return fail(UOCR_EINVAL, "ipc_close: null pointer");
+    return cuda_status(cudaIpcCloseMemHandle(reinterpret_cast<char*>(dev_ptr) - offset), "ipc_close");
 }
 
 int uocr_moe_decode_set_trace(void* device_buffer, size_t bytes) {

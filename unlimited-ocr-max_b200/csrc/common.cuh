@@ -14,6 +14,7 @@ enum DeviceStatus : uint32_t {
     kStatusOk = 0,
     kStatusWaitTimeout = 1,  // a spin/mbarrier wait exceeded its iteration budget
     kStatusMisaligned = 2,   // a kernel's shared-memory window was not aligned as its operands need
+    kStatusBadCount = 3,     // an exchanged row count above the receiving slot's capacity (expert-parallel)
 };
 
 UOCR_DEV void set_status(uint32_t* status, uint32_t code) {

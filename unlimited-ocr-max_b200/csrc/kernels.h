@@ -109,6 +109,8 @@ struct PrefillPlan {
     PrefillGroup g[kPrefillMaxGroups];
 };
 
+struct EpPeers;  // ep.cu
+
 struct PrefillArgs {
     int T, H, I, E, S, topk, G, int8;
     int route;       // 1: route x here (ids/wts are outputs); 0: ids/wts given, id < 0 = no expert
@@ -126,6 +128,14 @@ struct PrefillArgs {
     const uint16_t* w13_shared;
     const uint16_t* w2_shared;
     float* out;  // [T, H]
+    // expert-parallel peer mode (null peers: off): rows [q cap, q cap + slot_counts[q]) of the T = world
+    // cap rows are valid, the others skipped; instead of `out`, row q cap + r goes as bf16 to rank q's
+    // partial slot `rank`, row r, and each rank q's part_flag[rank] is set once all rows are stored
+    const EpPeers* peers;
+    const int* slot_counts;
+    const int* slot_fail;
+    unsigned int* done;    // local zero word, last-CTA detection of the partials kernel
+    uint32_t* status;      // null: the workspace's own status word
 };
 // Byte offsets of the prefill workspace regions (status word first).
 struct PrefillLayout {
@@ -142,6 +152,42 @@ cudaError_t launch_ep_dispatch(const float* x, int T, int H, const int32_t* ids,
                                uint16_t* rows, int32_t* meta, int32_t* inv, void* ws, cudaStream_t st);
 cudaError_t launch_ep_combine(const float* part, long long nrows, const int32_t* inv, int T, int world, int H,
                               const float* add, float* out, cudaStream_t st);
+
+// ep.cu: the exchange through peer memory. Every rank holds one exchange buffer of the same layout,
+// mapped into every other rank's process (CUDA IPC); a source rank stores its rows and slot
+// metadata straight into its slot of each destination's buffer, an expert rank stores the partial
+// rows straight back into its slot of each source's buffer, and per-source flags (the forward's
+// epoch, written with system-scope release after the data) order the two sides. No host
+// synchronisation, no intermediate copies.
+struct EpSig {  // per source rank q, in the destination's buffer (64 bytes)
+    unsigned long long disp_epoch;  // q's rows / metadata of this epoch are in slot q
+    unsigned long long disp_count;  // rows q sent here this epoch
+    unsigned long long part_flag;   // (epoch << 1) | fail: q's partial rows for this rank's slot-q rows
+    unsigned long long pad[5];
+};
+struct EpPeerLayout {
+    size_t status, sig, eid, w, rows, part, total;
+};
+EpPeerLayout ep_peer_layout(int world, int cap, int H, int k);
+struct EpPeers {
+    int world, rank, cap, H, k, pad;
+    unsigned long long epoch;
+    unsigned char* buf[kEpMaxWorld];  // rank p's exchange buffer as mapped in this process
+};
+// Local scratch of the peer path: a header (counters, slot counts), the dispatch plan, then the
+// expert products of up to world * cap received rows (prefill layout).
+struct EpPeerScratch {
+    size_t hdr, masks, chunk_counts, order, send_counts, prefill, total;
+};
+constexpr size_t kEpHdrDoneDispatch = 0, kEpHdrDonePart = 4, kEpHdrSlotCounts = 32, kEpHdrSlotFail = 64;
+EpPeerScratch ep_peer_scratch(int world, int cap, int H, int I, int E, int k, bool int8, size_t prefill_bytes);
+cudaError_t launch_ep_peer_dispatch(const EpPeers& P, const float* x, int T, const int32_t* ids, const float* wts,
+                                    const int32_t* owner, const int32_t* local, int E, int32_t* inv, char* ws,
+                                    const EpPeerScratch& d, cudaStream_t st);
+// wait for every source's dispatch of this epoch; slot counts and per-slot failures into the header
+cudaError_t launch_ep_peer_wait(const EpPeers& P, char* ws, const EpPeerScratch& d, cudaStream_t st);
+cudaError_t launch_ep_peer_combine(const EpPeers& P, const int32_t* inv, int T, const float* add, float* out,
+                                   cudaStream_t st);
 
 // pack.cu: source rows at (e * estride + row * ld) elements
 cudaError_t launch_pack_w13(const void* gate, const void* up, const float* gs, const float* us, int E, int I, int H,

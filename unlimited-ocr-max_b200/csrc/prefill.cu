@@ -42,13 +42,23 @@ namespace uocr {
 // ======================================================================================
 constexpr int kChunk = 256;  // entries per histogram chunk (one CTA, one thread each)
 
-__global__ void __launch_bounds__(kChunk) prefill_hist_kernel(const int32_t* __restrict__ ids, int n, int E,
+// Entry q (row q / topk) takes part: always, or (expert-parallel peer mode) when its row lies inside
+// the valid part of its source slot, rows [slot * cap, slot * cap + slot_counts[slot]).
+UOCR_DEV bool entry_in_slot(int q, int topk, const int* slot_counts, int cap) {
+    if (!slot_counts) return true;
+    const int row = q / topk;
+    return row - (row / cap) * cap < slot_counts[row / cap];
+}
+
+__global__ void __launch_bounds__(kChunk) prefill_hist_kernel(const int32_t* __restrict__ ids, int n, int E, int topk,
+                                                              const int* __restrict__ slot_counts, int cap,
                                                               int* __restrict__ chunk_counts) {
     __shared__ int hist[64];
     if (threadIdx.x < 64) hist[threadIdx.x] = 0;
     __syncthreads();
     const int q = blockIdx.x * kChunk + threadIdx.x;
-    if (q < n && ids[q] >= 0) atomicAdd(&hist[clamp_expert(ids[q], E)], 1);  // < 0: no expert for the entry
+    if (q < n && entry_in_slot(q, topk, slot_counts, cap) && ids[q] >= 0)
+        atomicAdd(&hist[clamp_expert(ids[q], E)], 1);  // < 0: no expert for the entry
     __syncthreads();
     if (threadIdx.x < 64) chunk_counts[blockIdx.x * 64 + threadIdx.x] = hist[threadIdx.x];
 }
@@ -113,14 +123,15 @@ __global__ void __launch_bounds__(64) prefill_scan_kernel(const int* __restrict_
 
 // Rank of each entry among the entries of its expert (stable in entry order) -> destination row.
 __global__ void __launch_bounds__(kChunk) prefill_scatter_kernel(const int32_t* __restrict__ ids, int n, int E,
-                                                                 int topk, const int* __restrict__ chunk_base,
+                                                                 int topk, const int* __restrict__ slot_counts,
+                                                                 int cap, const int* __restrict__ chunk_base,
                                                                  int* __restrict__ dest, int* __restrict__ src_tok) {
     __shared__ int wcount[kChunk / 32][64];
     const int q = blockIdx.x * kChunk + threadIdx.x;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     for (int i = threadIdx.x; i < (kChunk / 32) * 64; i += kChunk) (&wcount[0][0])[i] = 0;
     __syncthreads();
-    const int e = (q < n && ids[q] >= 0) ? clamp_expert(ids[q], E) : -1;
+    const int e = (q < n && entry_in_slot(q, topk, slot_counts, cap) && ids[q] >= 0) ? clamp_expert(ids[q], E) : -1;
     const unsigned same = __match_any_sync(0xffffffffu, e);
     const int rank_in_warp = __popc(same & ((1u << lane) - 1u));
     if (e >= 0 && rank_in_warp == 0) wcount[warp][e] = __popc(same);
@@ -232,6 +243,58 @@ __global__ void __launch_bounds__(256) prefill_combine_kernel(const float* __res
             acc.w = __fadd_rn(acc.w, v.w);
         }
         *reinterpret_cast<float4*>(out + (size_t)t * H + j) = acc;
+    }
+}
+
+// Expert-parallel peer mode: received row n = q * cap + r (source q, position r) of the valid part
+// of its slot -> bf16(sum_s w[n,s] * y[dest[n*k+s]]) (the same fp32 fma chain from +0 as
+// prefill_combine_kernel, then rounded to nearest even) stored straight into rank q's exchange
+// buffer, partial slot `rank`, row r. The grid's last CTA then sets every rank q's part_flag[rank]
+// to (epoch << 1) | fail, fail when slot q's rows were not processed (its wait failed, or its count
+// was refused) or a bounded wait of these products gave up (`status`).
+__global__ void __launch_bounds__(256) ep_partials_kernel(const float* __restrict__ y, const float* __restrict__ wts,
+                                                          const int* __restrict__ dest, int topk, EpPeers P,
+                                                          size_t part_off, size_t sig_off,
+                                                          const int* __restrict__ slot_counts,
+                                                          const int* __restrict__ slot_fail, const uint32_t* status,
+                                                          unsigned int* __restrict__ done) {
+    const int n = blockIdx.x, H = P.H;
+    const int q = n / P.cap, r = n - q * P.cap;
+    if (r < slot_counts[q]) {
+        uint16_t* dst = reinterpret_cast<uint16_t*>(P.buf[q] + part_off) + ((size_t)P.rank * P.cap + r) * H;
+        for (int j = threadIdx.x * 8; j < H; j += blockDim.x * 8) {
+            float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+            for (int s = 0; s < topk; ++s) {
+                const int d = dest[n * topk + s];
+                if (d < 0) continue;
+                const float w = wts[n * topk + s];
+                const float4 v0 = *reinterpret_cast<const float4*>(y + (size_t)d * H + j);
+                const float4 v1 = *reinterpret_cast<const float4*>(y + (size_t)d * H + j + 4);
+                const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc[i] = __fmaf_rn(w, v[i], acc[i]);
+            }
+            uint4 o;
+            o.x = (uint32_t)f32_to_bf16_rne(acc[0]) | ((uint32_t)f32_to_bf16_rne(acc[1]) << 16);
+            o.y = (uint32_t)f32_to_bf16_rne(acc[2]) | ((uint32_t)f32_to_bf16_rne(acc[3]) << 16);
+            o.z = (uint32_t)f32_to_bf16_rne(acc[4]) | ((uint32_t)f32_to_bf16_rne(acc[5]) << 16);
+            o.w = (uint32_t)f32_to_bf16_rne(acc[6]) | ((uint32_t)f32_to_bf16_rne(acc[7]) << 16);
+            *reinterpret_cast<uint4*>(dst + j) = o;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        if (atomicAdd(done, 1u) == gridDim.x - 1) {
+            *done = 0u;  // for the next call
+            __threadfence_system();
+            const unsigned long long any = *reinterpret_cast<const volatile uint32_t*>(status) != 0u ? 1ull : 0ull;
+            for (int p = 0; p < P.world; ++p) {
+                EpSig* sig = reinterpret_cast<EpSig*>(P.buf[p] + sig_off) + P.rank;
+                const unsigned long long f = any | (slot_fail[p] ? 1ull : 0ull);
+                st_release_sys_u64(&sig->part_flag, (P.epoch << 1) | f);
+            }
+        }
     }
 }
 
@@ -846,16 +909,19 @@ cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& 
     uint16_t* xperm = reinterpret_cast<uint16_t*>(ws + d.xperm);
     uint16_t* h = reinterpret_cast<uint16_t*>(ws + d.h);
     float* y = reinterpret_cast<float*>(ws + d.y);
-    uint32_t* status = reinterpret_cast<uint32_t*>(ws + d.status);
+    uint32_t* status = a.status ? a.status : reinterpret_cast<uint32_t*>(ws + d.status);
+    const int cap = a.peers ? a.peers->cap : 1;
+    const int* slots = a.peers ? a.slot_counts : nullptr;
 
     cudaError_t err = cudaSuccess;
     if (a.route && k > 0) {
         err = launch_route(a.x, T, H, a.router, E, a.bias, k, ids, wts, st);
         if (err != cudaSuccess) return err;
     }
-    if (nchunks > 0) prefill_hist_kernel<<<nchunks, kChunk, 0, st>>>(ids, kT, E, chunk_counts);
+    if (nchunks > 0) prefill_hist_kernel<<<nchunks, kChunk, 0, st>>>(ids, kT, E, k, slots, cap, chunk_counts);
     prefill_scan_kernel<<<1, 64, 0, st>>>(chunk_counts, nchunks, E, S, T, k, chunk_base, plan1, plan2, n_valid);
-    if (nchunks > 0) prefill_scatter_kernel<<<nchunks, kChunk, 0, st>>>(ids, kT, E, k, chunk_base, dest, src_tok);
+    if (nchunks > 0)
+        prefill_scatter_kernel<<<nchunks, kChunk, 0, st>>>(ids, kT, E, k, slots, cap, chunk_base, dest, src_tok);
     const int grows = kT + (S ? T : 0);
     if (grows > 0)
         prefill_gather_kernel<<<(grows + 7) / 8, 256, 0, st>>>(a.x, a.x_bf16, T, H, kT, S > 0, n_valid, src_tok, xperm);
@@ -921,6 +987,12 @@ cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& 
         err = launch_gemm(kEpiF32, mA2, mB2, mBs2, plan2, H / kBN, I / kBK, H, y, H, max_mtiles * (H / kBN), a.max_ctas,
                           status, st);
         if (err != cudaSuccess) return err;
+    }
+    if (a.peers) {
+        const EpPeerLayout L = ep_peer_layout(a.peers->world, a.peers->cap, a.peers->H, a.peers->k);
+        ep_partials_kernel<<<T, 160, 0, st>>>(y, wts, dest, k, *a.peers, L.part, L.sig, a.slot_counts, a.slot_fail,
+                                              status, a.done);
+        return cudaGetLastError();
     }
     prefill_combine_kernel<<<T, 256, 0, st>>>(y, wts, dest, T, H, k, S, a.accumulate, a.out);
     return cudaGetLastError();

@@ -22,6 +22,10 @@ UOCR_DEV uint64_t global_timer_ns() {
 // microseconds), far below a hang. After it the waiter records kStatusWaitTimeout and the
 // kernel winds down without touching the data it was waiting for.
 constexpr uint64_t kWaitBudgetNs = 200ull * 1000ull * 1000ull;
+// Budget of a wait on another GPU's expert-parallel exchange: the ranks' hosts enqueue their work
+// independently and may be far apart in time, so this is long; it only has to end a wait for a
+// rank that never comes.
+constexpr uint64_t kEpWaitBudgetNs = 20ull * 1000ull * 1000ull * 1000ull;
 
 // ---- mbarrier ------------------------------------------------------------------------------
 UOCR_DEV void mbar_init(uint64_t* bar, uint32_t count) {
@@ -131,6 +135,16 @@ UOCR_DEV uint32_t ld_acquire_gpu(const uint32_t* p) {
 UOCR_DEV void st_release_gpu(uint32_t* p, uint32_t v) {
     asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
 }
+// ---- flags shared with other GPUs (peer memory over NVLink): system-scope ordering --------------
+UOCR_DEV unsigned long long ld_acquire_sys_u64(const unsigned long long* p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+UOCR_DEV void st_release_sys_u64(unsigned long long* p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
 // Spin until *p >= target (gpu-scope acquire), at most kWaitBudgetNs.
 UOCR_DEV bool wait_counter_geq(const uint32_t* p, uint32_t target, uint32_t* status) {
     if (ld_acquire_gpu(p) >= target) return true;

@@ -11,38 +11,50 @@ forward:
 2. plan: one row per (token, destination rank) that holds at least one of its k experts, rows
    ordered by destination rank, then token; each row carries, per slot, the expert's local index
    on that rank (or -1) and its routing weight;
-3. exchange counts, then rows (bf16) and metadata, with ``all_to_all_single`` (NCCL over
-   NVLink);
+3. send the rows (bf16) and their metadata to the destination ranks;
 4. each rank applies its local experts to the rows it received, pre-weighted and summed per
-   row (``uocr_moe_ep_experts``: the prefill's permute + tcgen05 grouped GEMMs);
-5. exchange the fp32 partial rows back; each token sums its partials in destination-rank order
+   row (the prefill's permute + tcgen05 grouped GEMMs), rounded to bf16;
+5. send the partial rows back; each token sums its partials in destination-rank order
    (deterministic), then adds the sum of its shared experts (``uocr_moe_shared_forward``,
    data-parallel): out = (partial_0 + partial_1 + ...) + (shared_0 + shared_1).
 
-``ep_forward`` states the bookkeeping (2, 3, 5) in plain torch; it runs on CPU ranks (gloo) in
-the tests and is the reference the device path is checked against. ``ExpertParallelMoE`` runs
-CUDA only: the plan and the bf16 row gather are one library call (``uocr_moe_ep_dispatch``, no
-host round trip but the one D2H read of the exchanged row counts), the per-token sum of the
-partials is another (``uocr_moe_ep_combine``), and the shared experts run on a side stream while
-the rows are exchanged; the result is bit-identical to ``ep_forward`` with the same compute
-steps.
+``ExpertParallelMoE`` (exchange "peer", the default) does 2-5 in three library calls with no
+all-to-all and no host synchronisation: every rank maps every other rank's exchange buffer (CUDA
+IPC, plain peer loads and stores over NVLink, no multicast), the dispatch kernels store the rows
+and metadata straight into the destinations' slots, the expert products store the partial rows
+straight back, and per-source epoch flags written with system-scope release order the two sides
+(bounded device waits; a failure gives NaN outputs and a status that ``check_status`` raises).
+``ep_forward`` states the same bookkeeping in plain torch over ``torch.distributed`` collectives
+(the count table, ``all_to_all_single`` of rows, metadata and partials); it runs on CPU ranks
+(gloo) in the tests, serves exchange "nccl", and is the reference the peer path is checked
+against bit for bit. Its host-side exchanges take a timeout: a rank that does not take part in
+time, or a count table that cannot be right, raises :class:`ExchangeError` on every rank that
+sees it, after aborting the communicator, before any rows move.
 """
 
 from __future__ import annotations
 
 import ctypes
 from dataclasses import dataclass, field
+from datetime import timedelta
 from typing import Callable, Mapping
 
 import torch
 import torch.distributed as dist
 
 from . import ops
-from ._lib import check, load
+from ._lib import UocrEpPeers, check, load
 from .moe import MoEConfig, UocrMoE
 
 __all__ = ["ExpertPlacement", "contiguous_placement", "balanced_placement", "DispatchPlan", "plan_dispatch",
-           "exchange_counts", "exchange_rows", "sum_partials", "ep_forward", "ExpertParallelMoE"]
+           "ExchangeError", "count_table", "exchange_counts", "exchange_rows", "sum_partials", "ep_forward",
+           "ExpertParallelMoE", "PARTIAL_DTYPE"]
+
+#: dtype of the partial rows the expert ranks send back (half the bytes of fp32; the rounding is far
+#: inside the layer's tolerance)
+PARTIAL_DTYPE = torch.bfloat16
+#: default time a rank waits for the others at a host-side exchange
+DEFAULT_TIMEOUT_S = 120.0
 
 
 @dataclass
@@ -136,12 +148,61 @@ def plan_dispatch(ids: torch.Tensor, wts: torch.Tensor, world: int, placement) -
     return DispatchPlan(torch.cat(orders), counts, torch.cat(metas_e), torch.cat(metas_w))
 
 
-def exchange_counts(send_counts: list[int], device, group=None) -> list[int]:
-    world = len(send_counts)
-    send = torch.tensor(send_counts, dtype=torch.int64, device=device)
-    recv = torch.empty(world, dtype=torch.int64, device=device)
-    dist.all_to_all_single(recv, send, group=group)
-    return [int(v) for v in recv.tolist()]
+class ExchangeError(RuntimeError):
+    """An expert-parallel exchange failed on the host: a rank did not take part within the timeout,
+    or the exchanged row counts cannot be right. Raised on every rank that sees it."""
+
+
+def _abort(group) -> None:
+    """Abort the communicator (NCCL) so that no later collective waits on a rank that is gone."""
+    try:
+        dist.distributed_c10d._abort_process_group(group)
+    except Exception:  # noqa: BLE001 - gloo has no abort; the error below is what matters
+        pass
+
+
+def _wait(work, what: str, timeout_s: float | None, group) -> None:
+    """Wait for an async collective at most ``timeout_s`` seconds on the host (None: no limit)."""
+    if timeout_s is None:
+        work.wait()
+        return
+    try:
+        done = work.wait(timeout=timedelta(seconds=timeout_s))
+    except Exception as e:  # noqa: BLE001 - the backends raise RuntimeError on a timeout
+        _abort(group)
+        raise ExchangeError(f"{what}: not every rank took part within {timeout_s:g} s ({e})") from e
+    if done is False:
+        _abort(group)
+        raise ExchangeError(f"{what}: not every rank took part within {timeout_s:g} s")
+
+
+def count_table(send_counts: list[int], T: int, device, group=None, timeout_s: float | None = None) -> torch.Tensor:
+    """Every rank's row counts and token count, gathered (host tensor [world, world + 1]: row p is
+    rank p's rows to ranks 0..world-1, then its T). Every rank gets the same table and checks it the
+    same way, so a bad count is refused by every rank before any row moves: a count below 0 or above
+    the sender's token count (a rank sends each token at most one row per destination)."""
+    world = dist.get_world_size(group)
+    mine = torch.tensor([*send_counts, T], dtype=torch.int64, device=device)
+    parts = [torch.empty_like(mine) for _ in range(world)]
+    _wait(dist.all_gather(parts, mine, group=group, async_op=True), "row counts", timeout_s, group)
+    tab = torch.stack(parts).cpu()
+    if tab.shape != (world, world + 1):
+        raise ExchangeError(f"row counts: a rank sent {tab.shape[1] - 1} counts for {world} ranks")
+    for p in range(world):
+        tp = int(tab[p, world])
+        for q in range(world):
+            c = int(tab[p, q])
+            if c < 0 or c > tp:
+                raise ExchangeError(f"row counts: rank {p} announces {c} rows for rank {q} from {tp} tokens")
+    return tab
+
+
+def exchange_counts(send_counts: list[int], device, group=None, T: int | None = None,
+                    timeout_s: float | None = None) -> list[int]:
+    """The rows this rank receives from each rank (from the checked count table)."""
+    rank = dist.get_rank(group)
+    tab = count_table(send_counts, max(send_counts) if T is None else T, device, group, timeout_s)
+    return [int(v) for v in tab[:, rank].tolist()]
 
 
 def exchange_rows(t: torch.Tensor, send_counts: list[int], recv_counts: list[int], group=None) -> torch.Tensor:
@@ -162,30 +223,32 @@ def sum_partials(T: int, H: int, plan: DispatchPlan, partial: torch.Tensor) -> t
     r0 = 0
     for c in plan.send_counts:
         if c:
-            out.index_add_(0, plan.order[r0:r0 + c], partial[r0:r0 + c])
+            out.index_add_(0, plan.order[r0:r0 + c], partial[r0:r0 + c].float())
         r0 += c
     return out
 
 
 def ep_forward(x: torch.Tensor, route: Callable, local_experts: Callable, shared: Callable, world: int,
-               placement, group=None) -> torch.Tensor:
+               placement, group=None, timeout_s: float | None = DEFAULT_TIMEOUT_S) -> torch.Tensor:
     """One expert-parallel MoE forward of this rank's tokens x [T, H] fp32.
 
     route(x) -> (ids [T,k] int32 global, wts [T,k] fp32); local_experts(rows bf16 [N,H], meta_e,
-    meta_w) -> fp32 [N,H] (meta_e: local expert indices); shared(x, buf) adds the shared experts
-    into buf in place (given zeros). placement: as for plan_dispatch.
+    meta_w) -> fp32 [N,H] (meta_e: local expert indices), sent back rounded to PARTIAL_DTYPE;
+    shared(x, buf) adds the shared experts into buf in place (given zeros). placement: as for
+    plan_dispatch. The count exchange waits at most ``timeout_s`` (None: no limit) and refuses an
+    impossible count table (:class:`ExchangeError`) before any row moves.
     """
     T, H = x.shape
     ids, wts = route(x)
     plan = plan_dispatch(ids, wts, world, placement)
-    recv_counts = exchange_counts(plan.send_counts, x.device, group)
+    recv_counts = exchange_counts(plan.send_counts, x.device, group, T=T, timeout_s=timeout_s)
     rows = x.index_select(0, plan.order).to(torch.bfloat16)
     meta = torch.cat([plan.meta_expert, plan.meta_weight.view(torch.int32)], dim=1)  # one exchange
     rows_in = exchange_rows(rows, plan.send_counts, recv_counts, group)
     meta_in = exchange_rows(meta, plan.send_counts, recv_counts, group)
     k = ids.shape[1]
     part_in = local_experts(rows_in, meta_in[:, :k].contiguous(), meta_in[:, k:].contiguous().view(torch.float32))
-    part = exchange_rows(part_in, recv_counts, plan.send_counts, group)
+    part = exchange_rows(part_in.to(PARTIAL_DTYPE), recv_counts, plan.send_counts, group)
     out = sum_partials(T, H, plan, part)
     sh = torch.zeros_like(out)
     shared(x, sh)
@@ -201,7 +264,21 @@ class ExpertParallelMoE:
     """
 
     def __init__(self, config: MoEConfig, *, group=None, device: str | torch.device = "cuda",
-                 placement: ExpertPlacement | None = None, overlap_shared: bool = True) -> None:
+                 placement: ExpertPlacement | None = None, overlap_shared: bool = True, exchange: str = "peer",
+                 timeout_s: float | None = DEFAULT_TIMEOUT_S, max_tokens: int | None = None) -> None:
+        """``exchange``: "peer" (stores into the other ranks' memory, no host synchronisation; the
+        default) or "nccl" (``ep_forward``'s collectives, one host read of the count table).
+        ``timeout_s`` bounds every host-side wait on the other ranks (the set-up of the peer
+        buffers, the "nccl" count exchange): past it the communicator is aborted and
+        :class:`ExchangeError` raised. ``max_tokens``: the most tokens any rank passes in one call
+        (default: the largest T of the first call, agreed by all ranks)."""
+        if exchange not in ("peer", "nccl"):
+            raise ValueError(f"ExpertParallelMoE: exchange {exchange!r} (peer or nccl)")
+        self.exchange = exchange
+        self.timeout_s = timeout_s
+        self.max_tokens = max_tokens
+        self._peer: dict | None = None
+        self._epoch = 0
         self.config = config
         self.group = group
         self.rank = dist.get_rank(group)
@@ -258,7 +335,100 @@ class ExpertParallelMoE:
             ws = self._ws.get(name)
             if ws is not None:
                 _check(L.uocr_moe_device_status(ws.data_ptr(), stream))
+        if self._peer is not None:
+            _check(L.uocr_moe_device_status(self._peer["own"].data_ptr(), stream))
         self.local.check_status()
+
+    # ---- the peer exchange ------------------------------------------------------------------
+    def _setup_peers(self, T: int) -> None:
+        """Collective (every rank, at its first call): agree on the slot capacity, allocate this
+        rank's exchange buffer, and map every other rank's (CUDA IPC handles all-gathered)."""
+        L, g, W = load(), self.group, self.world
+        cap = torch.tensor([T if self.max_tokens is None else self.max_tokens], dtype=torch.int64, device=self.device)
+        _wait(dist.all_reduce(cap, op=dist.ReduceOp.MAX, group=g, async_op=True), "exchange set-up", self.timeout_s, g)
+        cap = int(cap.item())
+        H, k = self.config.hidden_size, self.config.num_experts_per_tok
+        nbytes = L.uocr_moe_ep_peer_buffer_bytes(W, cap, H, k)
+        if nbytes == 0:
+            raise ValueError(f"ExpertParallelMoE: no exchange buffer for {W} ranks x {cap} tokens")
+        own = torch.zeros(nbytes, dtype=torch.uint8, device=self.device)  # epochs and flags start at 0
+        torch.cuda.synchronize(self.device)
+        handle = (ctypes.c_ubyte * 64)()
+        off = ctypes.c_uint64()
+        check(L.uocr_ipc_export(own.data_ptr(), ctypes.cast(handle, ctypes.c_void_p), ctypes.byref(off)))
+        mine = torch.tensor(list(bytes(handle)) + list(int(off.value).to_bytes(8, "little")), dtype=torch.uint8,
+                            device=self.device)
+        parts = [torch.empty_like(mine) for _ in range(W)]
+        _wait(dist.all_gather(parts, mine, group=g, async_op=True), "exchange set-up", self.timeout_s, g)
+        P = UocrEpPeers()
+        P.world, P.rank, P.cap_tokens, P.hidden, P.top_k = W, self.rank, cap, H, k
+        imported = []
+        for q, t in enumerate(parts):
+            if q == self.rank:
+                P.buf[q] = own.data_ptr()
+                continue
+            b = bytes(t.cpu().tolist())
+            h = (ctypes.c_ubyte * 64).from_buffer_copy(b[:64])
+            o = int.from_bytes(b[64:], "little")
+            ptr = ctypes.c_void_p()
+            check(L.uocr_ipc_import(ctypes.cast(h, ctypes.c_void_p), o, ctypes.byref(ptr)))
+            P.buf[q] = ptr.value
+            imported.append((ptr.value, o))
+        _wait(dist.barrier(group=g, async_op=True), "exchange set-up", self.timeout_s, g)
+        self._peer = {"P": P, "own": own, "imported": imported, "cap": cap}
+
+    def close(self) -> None:
+        """Unmap the other ranks' exchange buffers (after the stream's work is done)."""
+        if self._peer is not None:
+            torch.cuda.synchronize(self.device)
+            L = load()
+            for ptr, o in self._peer["imported"]:
+                L.uocr_ipc_close(ptr, o)
+            self._peer = None
+
+    def _call_peer(self, x: torch.Tensor) -> torch.Tensor:
+        T, H = x.shape
+        if self._peer is None:
+            self._setup_peers(T)
+        pe = self._peer
+        if T > pe["cap"]:
+            raise ValueError(f"ExpertParallelMoE: {T} tokens, above the exchange capacity {pe['cap']} "
+                             "(construct with max_tokens)")
+        P = pe["P"]
+        self._epoch += 1
+        P.epoch = self._epoch
+        L = load()
+        lay = ctypes.byref(self.local.layer)
+        cur = torch.cuda.current_stream(self.device)
+        stream = cur.cuda_stream
+        mark = self._mark
+        mark("start")
+        sh = self._buf("shared_out", (T, H), torch.float32)
+        ids, wts = self._route(x)
+        mark("route")
+        inv = self._buf("inv", (self.world, T), torch.int32)
+        ws = self._workspace("peer", L.uocr_moe_ep_peer_workspace_bytes(lay, ctypes.byref(P)))
+        check(L.uocr_moe_ep_peer_dispatch(ctypes.byref(P), x.data_ptr(), T, ids.data_ptr(), wts.data_ptr(),
+                                          self._owner.data_ptr(), self._local.data_ptr(),
+                                          self.config.n_routed_experts, inv.data_ptr(), ws.data_ptr(), ws.numel(),
+                                          stream))
+        mark("dispatch")
+        if self.overlap_shared:
+            self._side.wait_stream(cur)
+            with torch.cuda.stream(self._side):
+                self._shared(x, sh, accumulate=0)
+        else:
+            self._shared(x, sh, accumulate=0)
+        check(L.uocr_moe_ep_peer_experts(lay, ctypes.byref(P), ws.data_ptr(), ws.numel(), stream))
+        mark("experts")
+        if self.overlap_shared:
+            cur.wait_stream(self._side)
+        mark("shared_wait")
+        out = torch.empty((T, H), dtype=torch.float32, device=self.device)
+        check(L.uocr_moe_ep_peer_combine(ctypes.byref(P), inv.data_ptr(), T, sh.data_ptr() if T else None,
+                                         out.data_ptr(), stream))
+        mark("combine")
+        return out
 
     def _workspace(self, name: str, nbytes: int) -> torch.Tensor:
         ws = self._ws.get(name)
@@ -333,6 +503,8 @@ class ExpertParallelMoE:
         if not x.is_cuda or x.dtype != torch.float32 or x.dim() != 2 or x.shape[1] != self.config.hidden_size:
             raise ValueError("ExpertParallelMoE: x must be a CUDA fp32 [T, hidden] tensor")
         x = x.contiguous()
+        if self.exchange == "peer":
+            return self._call_peer(x)
         T, H = x.shape
         k, W, g = self.config.num_experts_per_tok, self.world, self.group
         cur = torch.cuda.current_stream(self.device)
@@ -350,10 +522,8 @@ class ExpertParallelMoE:
                 self._shared(x, sh, accumulate=0)
         else:
             self._shared(x, sh, accumulate=0)
-        recv = torch.empty_like(send)
-        dist.all_to_all_single(recv, send, group=g)
-        counts = torch.cat([send, recv]).tolist()  # the one host synchronisation
-        sc, rc = counts[:W], counts[W:]
+        tab = count_table(send.tolist(), T, self.device, g, self.timeout_s)  # the one host synchronisation
+        sc, rc = tab[self.rank, :W].tolist(), tab[:, self.rank].tolist()
         ns = sum(sc)
         mark("counts")
         rows_in = exchange_rows(rows[:ns], sc, rc, g)
@@ -362,7 +532,7 @@ class ExpertParallelMoE:
         part_in = self._local_experts(rows_in, meta_in[:, :k].contiguous(),
                                       meta_in[:, k:].contiguous().view(torch.float32))
         mark("experts")
-        part = exchange_rows(part_in, rc, sc, g)
+        part = exchange_rows(part_in.to(PARTIAL_DTYPE), rc, sc, g).float()
         mark("exchange_back")
         if self.overlap_shared:
             cur.wait_stream(self._side)
@@ -379,9 +549,12 @@ class ExpertParallelMoE:
 
     def profile_phases(self, x: torch.Tensor, steps: int = 10) -> dict[str, float]:
         """Mean device time (ms) between the phase boundaries of ``steps`` calls on this rank's
-        main stream: route, dispatch, counts (exchange + the host read), exchange_rows,
-        experts, exchange_back, shared_wait (the side stream's shared experts not yet done),
-        combine. A collective: every rank calls it."""
+        main stream. Exchange "peer": route, dispatch (plan; rows and metadata stored into the
+        destinations), experts (wait for every source; expert products; partial rows stored back),
+        shared_wait (the side stream's shared experts not yet done), combine (wait for every expert
+        rank; sum). Exchange "nccl": route, dispatch, counts (count table + the host read),
+        exchange_rows, experts, exchange_back, shared_wait, combine. A collective: every rank
+        calls it."""
         acc: dict[str, float] = {}
         for _ in range(steps):
             self._phase_events = []
@@ -395,4 +568,4 @@ class ExpertParallelMoE:
     def forward_reference(self, x: torch.Tensor) -> torch.Tensor:
         """The same layer through the torch bookkeeping of ``ep_forward`` (the device path's check)."""
         return ep_forward(x.contiguous(), self._route, self._local_experts, self._shared, self.world,
-                          self.placement, self.group)
+                          self.placement, self.group, self.timeout_s)
