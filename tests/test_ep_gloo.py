@@ -158,3 +158,105 @@ def test_expert_parallel_module_refuses_bad_placements_and_cpu():
             ep.ExpertParallelMoE(cfg, device="cpu")
     finally:
         dist.destroy_process_group()
+
+
+# ---- failures injected on the host ----------------------------------------------------------------
+
+
+def _failure_worker(rank: int, world: int, port: int, out_dir: str, mode: str) -> None:
+    """mode "absent": rank world-1 never joins the forward (it leaves after a while); the others must
+    raise ExchangeError within their timeout. mode "count": rank 1 announces more rows for rank 0
+    than it has tokens; every rank must refuse the count table before any row moves."""
+    import json
+    import time
+
+    os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    ep = importlib.import_module("unlimited-ocr-max_b200.ep")
+    o, cfg, w, x = _setup()
+    t_local = T_TOTAL // world
+    xl = torch.from_numpy(x[rank * t_local:(rank + 1) * t_local].copy())
+    calls = {"rows": 0, "experts": 0}
+    real_exchange_rows = ep.exchange_rows
+
+    def counting_exchange_rows(*a, **k):
+        calls["rows"] += 1
+        return real_exchange_rows(*a, **k)
+
+    ep.exchange_rows = counting_exchange_rows
+    if mode == "count" and rank == 1:
+        real_plan = ep.plan_dispatch
+
+        def corrupt_plan(*a, **k):
+            plan = real_plan(*a, **k)
+            plan.send_counts[0] = t_local + 5  # more rows than this rank has tokens
+            return plan
+
+        ep.plan_dispatch = corrupt_plan
+
+    def route(xt):
+        r = o.route_fp32(xt.numpy(), w.router, None, K)
+        return torch.from_numpy(r.ids), torch.from_numpy(r.weights)
+
+    def local_experts(rows, meta_e, meta_w):
+        calls["experts"] += 1
+        return torch.zeros(rows.shape[0], H)
+
+    def shared(xt, out):
+        pass
+
+    result = {"rank": rank}
+    if mode == "absent" and rank == world - 1:
+        time.sleep(12)  # never takes part; leaves well after the others' timeout
+        result["absent"] = True
+    else:
+        t0 = time.time()
+        try:
+            ep.ep_forward(xl, route, local_experts, shared, world, E // world, timeout_s=3.0)
+            result["raised"] = None
+        except ep.ExchangeError as e:
+            result["raised"] = str(e)
+        result["seconds"] = time.time() - t0
+    result.update(calls)
+    with open(os.path.join(out_dir, f"fail{rank}.json"), "w") as f:
+        json.dump(result, f)
+    os._exit(0)  # no destroy_process_group: a peer may be gone
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_a_rank_that_never_posts_makes_the_others_raise_in_time(tmp_path, world):
+    import json
+
+    mp.spawn(_failure_worker, args=(world, _free_port(), str(tmp_path), "absent"), nprocs=world, join=True)
+    for r in range(world - 1):
+        res = json.loads((tmp_path / f"fail{r}.json").read_text())
+        assert res["raised"] and "not every rank took part within 3 s" in res["raised"], res
+        assert res["seconds"] < 10, res
+        assert res["rows"] == 0 and res["experts"] == 0, res  # nothing moved after the failed count exchange
+
+
+def test_a_corrupted_count_is_refused_by_every_rank_before_any_row_moves(tmp_path):
+    import json
+
+    world = 2
+    mp.spawn(_failure_worker, args=(world, _free_port(), str(tmp_path), "count"), nprocs=world, join=True)
+    for r in range(world):
+        res = json.loads((tmp_path / f"fail{r}.json").read_text())
+        assert res["raised"] and "rank 1 announces" in res["raised"] and "from 24 tokens" in res["raised"], res
+        assert res["rows"] == 0 and res["experts"] == 0, res
+
+
+def test_count_table_checks(tmp_path):
+    """The table a healthy step gathers passes; the receive counts are its columns."""
+    ep = importlib.import_module("unlimited-ocr-max_b200.ep")
+    dist.init_process_group("gloo", rank=0, world_size=1, init_method=f"tcp://127.0.0.1:{_free_port()}")
+    try:
+        tab = ep.count_table([7], 9, "cpu")
+        assert tab.tolist() == [[7, 9]]
+        assert ep.exchange_counts([7], "cpu", T=9) == [7]
+        with pytest.raises(ep.ExchangeError, match="announces 10 rows for rank 0 from 9 tokens"):
+            ep.count_table([10], 9, "cpu")
+        with pytest.raises(ep.ExchangeError, match="announces -1 rows"):
+            ep.count_table([-1], 9, "cpu")
+    finally:
+        dist.destroy_process_group()

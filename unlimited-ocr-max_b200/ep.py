@@ -154,10 +154,12 @@ class ExchangeError(RuntimeError):
 
 
 def _abort(group) -> None:
-    """Abort the communicator (NCCL) so that no later collective waits on a rank that is gone."""
+    """Abort the NCCL communicator so that no later collective waits on a rank that is gone (other
+    backends have no abort: their next collective times out on its own)."""
     try:
-        dist.distributed_c10d._abort_process_group(group)
-    except Exception:  # noqa: BLE001 - gloo has no abort; the error below is what matters
+        if dist.get_backend(group) == "nccl":
+            dist.distributed_c10d._abort_process_group(group)
+    except Exception:  # noqa: BLE001 - the ExchangeError raised next is what matters
         pass
 
 
