@@ -157,9 +157,10 @@ UOCR_API int uocr_moe_route(const float* x, int64_t T, int64_t H, const uint16_t
  * out [B, H] fp32 = routed top-k experts weighted by the router + shared experts.
  * ids_out / wts_out (nullable) receive the routing. `workspace` must hold
  * uocr_moe_decode_workspace_bytes(L, B) bytes (256-byte aligned), zero-filled once before its
- * first use. Every device-side wait is bounded: a call in which one gave up writes NaN over `out`
- * and sets the workspace's sticky status (uocr_moe_device_status reports it); later calls compute
- * normally. The down kernel is a cooperative launch (all its CTAs resident at once). */
+ * first use. Two launches: the router logits, then one persistent experts kernel (a cooperative
+ * launch: its CTAs, one per SM, wait on each other's units). Every device-side wait is bounded: a
+ * call in which one gave up writes NaN over `out` and sets the workspace's sticky status; until
+ * uocr_moe_device_status has read (and so cleared) it, later calls on that workspace write NaN too. */
 UOCR_API size_t uocr_moe_decode_workspace_bytes(const uocr_moe_layer* L, int64_t B);
 UOCR_API int uocr_moe_decode(const uocr_moe_layer* L, const float* x, int64_t B, const float* bias,
                     float* out, int32_t* ids_out, float* wts_out,
@@ -281,13 +282,14 @@ UOCR_API int uocr_moe_decode_noalloc(const uocr_moe_layer* L, const float* x, in
                                      const float* bias, float* out, uocr_stream_t stream);
 /* The in-library array's status on the current device, as uocr_moe_device_status reports a
  * workspace's: synchronises `stream`, returns UOCR_OK, or UOCR_EDEVICE once after a call whose
- * device-side wait gave up (that call wrote NaN over its output), and clears it. No counterpart
- * in the reference. */
+ * device-side wait gave up (that call, and every call until this read, wrote NaN over its output),
+ * and clears it. No counterpart in the reference. */
 UOCR_API int uocr_moe_decode_noalloc_status(uocr_stream_t stream);
 
 /* Diagnostics: record a per-CTA timeline of the work items of subsequent uocr_moe_decode
- * launches into `device_buffer` (zero-filled by the caller; per item 8 words: consumer wait
- * start, data ready, item done, slot/rows, producer issue time, all in global-timer ns).
+ * launches into `device_buffer` (zero-filled by the caller; per CTA two halves, gate/up items then
+ * down items, per item 8 words: MMA warp wait start, data ready, MMAs issued, slot/rows, producer
+ * issue time, all in global-timer ns; the last records of each half hold kernel-level events).
  * NULL turns recording off. Not thread-safe; for profiling only. No counterpart in the
  * reference (its profiler is server-level). */
 UOCR_API int uocr_moe_decode_set_trace(void* device_buffer, size_t bytes);
@@ -298,11 +300,11 @@ UOCR_API int uocr_moe_decode_set_trace(void* device_buffer, size_t bytes);
  * a failed call left behind). No counterpart in the reference, whose ops cannot time out. */
 UOCR_API int uocr_moe_device_status(const void* workspace, uocr_stream_t stream);
 
-/* Test hook (no counterpart in the reference): the grid barrier of the next decode launches waits
- * for `extra` arrivals that never come, so every one of its bounded waits runs out; used to check
- * that such a failure is reported (UOCR_EDEVICE, NaN output) and that the next call is correct.
- * 0 turns it off. Not thread-safe; for tests only. */
-UOCR_API int uocr_moe_test_barrier_extra(int extra);
+/* Test hook (no counterpart in the reference): the down phase of the next decode launches waits,
+ * per slot, for `extra` gate/up arrivals that never come, so its bounded waits run out; used to
+ * check that such a failure is reported (NaN output, UOCR_EDEVICE from the status read) and that
+ * calls after the status read are correct. 0 turns it off. Not thread-safe; for tests only. */
+UOCR_API int uocr_moe_test_wait_extra(int extra);
 
 #ifdef __cplusplus
 }

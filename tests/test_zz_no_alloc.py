@@ -69,11 +69,11 @@ def test_noalloc_reports_an_expired_wait_and_recovers(uocr):
     want = moe.decode_rows(x)
     got = torch.zeros_like(x)
     assert lib.uocr_moe_decode_noalloc_status(stream) == 0, lib.uocr_last_error().decode()
-    assert lib.uocr_moe_test_barrier_extra(1) == 0  # the grid barrier waits for an arrival that never comes
+    assert lib.uocr_moe_test_wait_extra(1) == 0  # the grid barrier waits for an arrival that never comes
     try:
         rc = lib.uocr_moe_decode_noalloc(ctypes.byref(moe.layer), x.data_ptr(), 8, None, got.data_ptr(), stream)
     finally:
-        assert lib.uocr_moe_test_barrier_extra(0) == 0
+        assert lib.uocr_moe_test_wait_extra(0) == 0
     assert rc == 0
     assert lib.uocr_moe_decode_noalloc_status(stream) == 3
     assert "bounded wait" in lib.uocr_last_error().decode()

@@ -94,7 +94,7 @@ SIGNATURES: dict[str, tuple] = {
     "uocr_ipc_export": (I32, [P, P, ctypes.POINTER(ctypes.c_uint64)]),
     "uocr_ipc_import": (I32, [P, ctypes.c_uint64, ctypes.POINTER(ctypes.c_void_p)]),
     "uocr_ipc_close": (I32, [P, ctypes.c_uint64]),
-    "uocr_moe_test_barrier_extra": (I32, [I32]),
+    "uocr_moe_test_wait_extra": (I32, [I32]),
 }
 
 _lock = threading.Lock()

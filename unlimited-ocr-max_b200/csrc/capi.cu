@@ -51,7 +51,7 @@ namespace uocr {
 
 unsigned long long* g_decode_trace = nullptr;
 size_t g_decode_trace_bytes = 0;
-int g_decode_barrier_extra = 0;
+int g_decode_wait_extra = 0;
 
 // Read a workspace's status word after `stream` finished; if it is set, clear it together with the
 // control words a failed call may have left behind (decode: DecodeCtl; prefill: its first 128
@@ -300,7 +300,7 @@ int uocr_moe_route(const float* x, int64_t T, int64_t H, const uint16_t* router,
 namespace {
 
 struct DecodeLayout {
-    size_t ctl, logits, xd, xb, xsig, table, ids, wts, h, y, total;
+    size_t ctl, logits, xd, xb, xsig, ids, wts, h, y, total;
 };
 
 DecodeLayout decode_layout(const uocr_moe_layer* L, int64_t B) {
@@ -312,7 +312,6 @@ DecodeLayout decode_layout(const uocr_moe_layer* L, int64_t B) {
     d.xd = off; off += align256((size_t)L->hidden * 32);
     d.xb = off; off += align256((size_t)L->hidden * 32);
     d.xsig = off; off += align256(sizeof(float) * 8 * (size_t)(L->hidden / 128));
-    d.table = off; off += align256(sizeof(uocr::RouteTable));
     d.ids = off; off += align256(sizeof(int32_t) * (size_t)B * L->top_k);
     d.wts = off; off += align256(sizeof(float) * (size_t)B * L->top_k);
     d.h = off; off += align256(sizeof(float) * pairs * (size_t)L->inter);
@@ -381,7 +380,6 @@ int uocr_moe_decode(const uocr_moe_layer* L, const float* x, int64_t B, const fl
     a.xd = reinterpret_cast<unsigned char*>(ws + d.xd);
     a.xb = reinterpret_cast<unsigned char*>(ws + d.xb);
     a.xsig = reinterpret_cast<float*>(ws + d.xsig);
-    a.table = reinterpret_cast<uocr::RouteTable*>(ws + d.table);
     return cuda_status(uocr::launch_decode_layer(a, S(stream)), "moe_decode: launch");
 }
 
@@ -733,9 +731,9 @@ int uocr_moe_device_status(const void* workspace, uocr_stream_t stream) {
     return uocr::read_clear_status(workspace, S(stream), &code);
 }
 
-int uocr_moe_test_barrier_extra(int extra) {
-    if (extra < 0 || extra > 1024) return fail(UOCR_EINVAL, "test_barrier_extra: %d outside 0..1024", extra);
-    uocr::g_decode_barrier_extra = extra;
+int uocr_moe_test_wait_extra(int extra) {
+    if (extra < 0 || extra > 1024) return fail(UOCR_EINVAL, "test_wait_extra: %d outside 0..1024", extra);
+    uocr::g_decode_wait_extra = extra;
     return ok();
 }
 

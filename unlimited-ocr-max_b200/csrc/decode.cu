@@ -45,11 +45,10 @@
 
 namespace uocr {
 
-constexpr int kThreads = 9 * 32;             // K2, K3: MMA warp 0, stagers 1-3, epilogue 4-7, producer 8
+constexpr int kThreads = 9 * 32;             // MMA warp 0, stagers 1-3, epilogue 4-7, producer 8
 constexpr int kCW = 8;                       // warps 0-7 (K2's routing)
 constexpr int kMaxB = 8;
 constexpr int kMaxSlotsSm = 72;              // shared (<= 8) + routed (<= 64)
-constexpr int kK3Desc = 8;                   // K3 items in flight (descriptor ring)
 constexpr uint32_t kBarConsumers = 1;        // named barrier of warps 0-7
 constexpr int kAccSlots = 4;                 // TMEM accumulators of 64 columns
 constexpr uint32_t kAccCols = 64;
@@ -72,11 +71,12 @@ struct SlotTable {
 };
 
 struct ItemMeta {
-    int slot;       // < 0: end of the work
-    int rb;         // row block
-    int ki;         // item (K range) within the row block
-    uint32_t off;   // K3: byte offset of the item in the ring
-    uint32_t hoff;  // K3: offset of the slot's h rows from `off` (0: none)
+    int slot;   // < 0: end of the work
+    int rb;     // row block (gate/up: 64 pairs; down: 128 output rows)
+    int ki;     // item (K range) within the row block
+    int phase;  // 0: gate/up, 1: down
+    int run;    // down: the slot run this item starts (its operand image), -1 for none
+    int pad[3];
 };
 
 // One TMEM accumulator's description, written by the MMA warp, read by the epilogue. An
@@ -86,7 +86,7 @@ struct AccMeta {
     int slot;   // < 0: end of the work
     int rb;
     int gi;     // int8: the 128-group of columns 0-31 (columns 32-63: gi + 1)
-    int flags;  // bit 0: int8, bit 1: the row block's last accumulator, bit 2: int8 with two groups
+    int flags;  // bit 0: int8, bit 1: the unit's last accumulator, bit 2: int8 with two groups, bit 3: down
     float sig[2][kMaxB];       // K3 int8: digit scales of the slot's entries for each group
     float scl[2][kRowBlock];   // int8: weight scales of the 128 rows for each group
 };
@@ -104,22 +104,6 @@ UOCR_DEV void load_shared_slots(SlotTable* tb, const DecodeArgs& a, int tid, int
         }
     }
     if (tid == 0) tb->nslot = a.S;
-}
-
-// The routed slots' experts and rows, from K2's table in global memory (K3, after the
-// dependency wait; one warp; the combine reads the table's per-token row lists itself).
-UOCR_DEV void load_routed_slots(SlotTable* tb, const DecodeArgs& a, int lane) {
-    const RouteTable* g = a.table;
-    const int U = __ldcg(&g->U);
-    for (int u = lane; u < U; u += 32) {
-        const int e = __ldcg(&g->expert[u]), n = __ldcg(&g->count[u]), b = __ldcg(&g->base[u]);
-        tb->expert[a.S + u] = e;
-        tb->count[a.S + u] = n;
-        tb->base[a.S + u] = b;
-    }
-    __syncwarp();
-    if (lane == 0) tb->nslot = a.S + U;
-    __syncwarp();
 }
 
 // Diagnostics timeline: per CTA `items` records of 8 words (global-timer ns); item n of K2 / K3:
@@ -183,16 +167,25 @@ struct RouteSmem {
     int wsum[2];
 };
 
+// Per token, its routed y rows in ascending expert id and their weights (the combine's order).
+struct CombineSmem {
+    int trow[kMaxB][kDecodeMaxTopk];
+    float tw[kMaxB][kDecodeMaxTopk];
+    int req[2];  // a column block this CTA's epilogue completed: (down unit end << 8) | (block + 1)
+};
+
 // The rest of MoEGate (decoder.py:500-514) for the B tokens, from K1's partials: logit = the 8
 // segment partials added in ascending order, + bias; softmax with this build's exponential and
 // a fixed butterfly sum; top-k by (p desc, index asc) — identical in every CTA. Then the slot
 // table: routed slot u is the u-th used expert; its rows start after the shared experts' S * B
-// rows, its entries in token order. CTA 0 also writes ids / wts and the global RouteTable (read
-// by K3). The inputs arrive by bulk copies on `inb`: the partials into `part` (the last stage
+// rows, its entries in token order; and each token's rows for the combine. CTA 0 also writes ids /
+// wts. The inputs arrive by bulk copies on `inb`: the partials into `part` (the last stage
 // buffer, which the producer fills only after the table is ready) and K1's operand images.
-UOCR_DEV void cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* xb, float* xsig, float* part,
+// Returns false (nothing routed) if the workspace holds an unread failure (`stale`) or the inputs
+// did not arrive in time.
+UOCR_DEV bool cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* xb, float* xsig, float* part,
                         uint64_t* inb, volatile int* abort_flag, uint32_t* fail, RouteSmem* rs, SlotTable* tb,
-                        int tid, unsigned long long* ev) {
+                        CombineSmem* cs, int* stale, int tid, unsigned long long* ev) {
     const int warp = tid >> 5, lane = tid & 31;
     const int H = a.H, B = a.B, E = a.E, k = a.topk, kB = k * B;
     unsigned long long* rv = a.trace ? trace_rec(a, 0, a.trace_items / 2 - 2) : nullptr;  // diagnostics
@@ -204,6 +197,11 @@ UOCR_DEV void cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* x
     for (int i = tid; i < 64 * kMaxB; i += kCW * 32) tb->pos[a.S + i / kMaxB][i % kMaxB] = -1;
     pdl_wait_prior_grid();  // K1's partials and operands
     if (ev && tid == 0) ev[1] = global_timer_ns();
+    // an unread failure of an earlier call leaves the counters unknown: this call only writes NaN
+    // until the host reads the status (which resets the control block)
+    if (tid == 0) *stale = __ldcg(&a.ctl->status) != 0u;
+    named_bar_sync(kBarConsumers, kCW * 32);
+    if (*stale) return false;
     if (warp == 0) {
         const uint32_t pbytes = (uint32_t)B * 64 * 8 * 4, img = (uint32_t)H * 32;
         const uint32_t dbytes = a.int8 ? img : 0u, sbytes = a.int8 ? 8u * (H / 128) * 4 : 0u;
@@ -215,6 +213,8 @@ UOCR_DEV void cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* x
         if (lane == 3 && sbytes) bulk_g2s(xsig, a.xsig, sbytes, inb);
     }
     if (!mbar_wait_warp(inb, 0, abort_flag, fail)) *abort_flag = 1;
+    named_bar_sync(kBarConsumers, kCW * 32);
+    if (*abort_flag) return false;
     if (rv && tid == 0) rv[0] = global_timer_ns();
     for (int i = tid; i < B * 64; i += kCW * 32) {
         const float4 p0 = *reinterpret_cast<const float4*>(part + 8 * i);
@@ -282,8 +282,6 @@ UOCR_DEV void cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* x
     }
     named_bar_sync(kBarConsumers, kCW * 32);
     const unsigned long long used = (unsigned long long)rs->used[0] | ((unsigned long long)rs->used[1] << 32);
-    RouteTable* g = a.table;
-    const bool pub = blockIdx.x == 0;  // CTA 0 publishes the table for K3
     if (tid < 64 && c > 0) {
         const int u = __popcll(used & ((1ull << tid) - 1ull));
         const int row = a.S + u;
@@ -291,11 +289,6 @@ UOCR_DEV void cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* x
         tb->expert[row] = tid;
         tb->count[row] = c;
         tb->base[row] = base;
-        if (pub) {
-            g->expert[u] = tid;
-            g->count[u] = c;
-            g->base[u] = base;
-        }
         int n = 0;
         for (unsigned long long mm = m; mm; mm &= mm - 1ull, ++n) {
             const int q = __ffsll((long long)mm) - 1, t = q / k;
@@ -303,19 +296,12 @@ UOCR_DEV void cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* x
             tb->token[row][n] = t;
             tb->weight[row][n] = rs->wts[q];
             rs->rowof[q] = base + n;
-            if (pub) {
-                g->token[u][n] = t;
-                g->weight[u][n] = rs->wts[q];
-            }
         }
     }
-    if (tid == 0) {
-        tb->nslot = a.S + __popcll(used);
-        if (pub) g->U = __popcll(used);
-    }
+    if (tid == 0) tb->nslot = a.S + __popcll(used);
     named_bar_sync(kBarConsumers, kCW * 32);
     if (rv && tid == 0) rv[5] = global_timer_ns();
-    if (pub && tid < B) {
+    if (tid < B) {
         // token tid's routed rows in ascending expert id (the combine's order)
         int ord[kDecodeMaxTopk];
         for (int s = 0; s < k; ++s) {
@@ -327,14 +313,15 @@ UOCR_DEV void cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* x
             ord[i] = s;
         }
         for (int s = 0; s < k; ++s) {
-            g->tok_row[tid][s] = rs->rowof[tid * k + ord[s]];
-            g->tok_w[tid][s] = rs->wts[tid * k + ord[s]];
+            cs->trow[tid][s] = rs->rowof[tid * k + ord[s]];
+            cs->tw[tid][s] = rs->wts[tid * k + ord[s]];
         }
     }
     // `part` lives in a stage buffer the producer fills next with the async proxy
     fence_proxy_async_smem();
     named_bar_sync(kBarConsumers, kCW * 32);
     if (rv && tid == 0) rv[6] = global_timer_ns();
+    return true;
 }
 
 // Static partitions of work units over the CTAs (costs in 512-byte units). All intermediate
@@ -549,43 +536,136 @@ UOCR_DEV void fold_bf16(const AccRead& r, float (&acc)[kMaxB]) {
 }
 
 // ======================================================================================
-// K2: route + gate/up + SwiGLU
+// the experts kernel: route, gate/up (phase A), down (phase B), combine
 // ======================================================================================
-// Units (slot, row block of 64 gate|up pairs): w13_items(H) items of 2 atoms each. Shared slots
-// first (streamed while the CTA routes), then the routed slots.
+// This CTA's work units of both phases: shared units first (known from the shape), then routed
+// units (known once the CTA has routed), each part a contiguous range of a static partition.
+struct Units {
+    int a_s0, a_s1, a_r0, a_r1;  // gate/up units (slot, 64 pairs): shared of S * I/64, routed of U * I/64
+    int b_s0, b_s1, b_r0, b_r1;  // down units (slot, 128 rows): shared of S * H/128, routed of U * H/128
+    int na, nb;                  // units in each phase
+};
+UOCR_DEV void unit_a(const Units& u, const DecodeArgs& a, int i, int& slot, int& rb) {
+    const int per = a.I / 64, ns = u.a_s1 - u.a_s0;
+    const int j = i < ns ? u.a_s0 + i : u.a_r0 + (i - ns);
+    slot = (i < ns ? 0 : a.S) + j / per;
+    rb = j % per;
+}
+UOCR_DEV void unit_b(const Units& u, const DecodeArgs& a, int i, int& slot, int& rb) {
+    const int nrb = a.H / kRowBlock, ns = u.b_s1 - u.b_s0;
+    const int j = i < ns ? u.b_s0 + i : u.b_r0 + (i - ns);
+    slot = (i < ns ? 0 : a.S) + j / nrb;
+    rb = j % nrb;
+}
+
+// out[t][128 rb + c] for the B tokens and the block's 128 columns by the 128 epilogue threads
+// (thread i: token i / 16, the 8 columns from 8 (i % 16)): the token's shared rows in order, then
+// its routed rows in ascending expert id (w * y), rows loaded 8 at a time; NaN when the call failed.
+UOCR_DEV void combine_block(const DecodeArgs& a, const CombineSmem* cs, int rb, bool failed, int i) {
+    const int t = i >> 4, c = kRowBlock * rb + 8 * (i & 15);
+    if (t >= a.B) return;
+    float acc[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) acc[j] = failed ? __uint_as_float(0x7FC00000u) : 0.0f;
+    const int nrows = a.S + a.topk;  // row r < S: shared row r; else routed row r - S
+    for (int r0 = 0; r0 < nrows && !failed; r0 += 8) {
+        float4 v[8][2];
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int r = r0 + u;
+            if (r < nrows) {
+                const int row = r < a.S ? r * a.B + t : cs->trow[t][r - a.S];
+                const float* src = a.y + (size_t)row * a.H + c;
+                v[u][0] = __ldcg(reinterpret_cast<const float4*>(src));
+                v[u][1] = __ldcg(reinterpret_cast<const float4*>(src + 4));
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 8; ++u) {
+            const int r = r0 + u;
+            if (r < nrows) {
+                const float e[8] = {v[u][0].x, v[u][0].y, v[u][0].z, v[u][0].w,
+                                    v[u][1].x, v[u][1].y, v[u][1].z, v[u][1].w};
+                if (r < a.S) {
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc[j] = __fadd_rn(acc[j], e[j]);
+                } else {
+                    const float w = cs->tw[t][r - a.S];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) acc[j] = __fmaf_rn(w, e[j], acc[j]);
+                }
+            }
+        }
+    }
+    float* o = a.out + (size_t)t * a.H + c;
+    *reinterpret_cast<float4*>(o) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+    *reinterpret_cast<float4*>(o + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
+}
+// The same block written NaN by one warp alone (a failure path: no loads).
+UOCR_DEV void nan_block(const DecodeArgs& a, int rb, int lane) {
+    const float nan = __uint_as_float(0x7FC00000u);
+    for (int t = 0; t < a.B; ++t)
+        *reinterpret_cast<float4*>(a.out + (size_t)t * a.H + kRowBlock * rb + 4 * lane) = make_float4(nan, nan, nan, nan);
+}
+// `n` more shares of combined column blocks (4 shares a block: one per epilogue warp); the share
+// that completes the call resets the call's words for the next call.
+UOCR_DEV void count_combined(const DecodeArgs& a, uint32_t n) {
+    __threadfence();
+    if (atomicAdd(&a.ctl->cdone, n) + n == 4u * (uint32_t)(a.H / kRowBlock)) {
+        for (int s = 0; s < 72; ++s) a.ctl->hdone[s] = 0u;
+        a.ctl->call_fail = 0u;
+        __threadfence();
+        atomicExch(&a.ctl->cdone, 0u);
+    }
+}
+
+// Persistent, one CTA per SM (a cooperative launch: CTAs wait on each other's units), 9 warps:
+// warp 8 streams items (one bulk copy each) into a ring of fixed stages, first the gate/up units
+// (phase A: shared ones while the CTA routes, then routed), then the down units (phase B); warp 0
+// issues their tcgen05 MMAs (B operand: the tokens' images from K1 in phase A, the slot run's h
+// image in phase B); warps 4-7 drain the accumulators: phase A -> h rows (SwiGLU) and a count per
+// slot; phase B -> y rows and a count per output column block, whose completing arrival has its
+// CTA combine the block. Warps 1-3 (phase B) turn each slot run's h rows, once every CTA's gate/up
+// units of that slot are counted, into the run's operand image. Warps 0-7 route first.
 __global__ void __launch_bounds__(kThreads, 1)
-decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl, uint32_t off_route,
-                      uint32_t off_meta, uint32_t off_acc, uint32_t off_xd, uint32_t off_xb, uint32_t off_sig,
-                      uint32_t off_stages) {
+decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl, uint32_t off_route,
+                      uint32_t off_meta, uint32_t off_acc, uint32_t off_cs, uint32_t off_sig, uint32_t off_hsig,
+                      uint32_t off_img, uint32_t off_stages) {
     extern __shared__ __align__(1024) unsigned char smem[];
-    __shared__ int abort_flag;
+    __shared__ int abort_flag, stale, routed;
     __shared__ uint32_t tmem_base, cta_fail;  // cta_fail: this CTA's failure code (published at exit)
+    __shared__ Units units;
     uint32_t* fail = &cta_fail;
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* empty = full + nst;         // the MMAs reading the stage are complete
+    uint64_t* empty = full + nst;          // the MMAs reading the stage are complete
     uint64_t* table_ready = empty + nst;
-    uint64_t* inb = table_ready + 1;      // the routing's inputs have arrived
-    uint64_t* tfull = inb + 1;            // [kAccSlots]
-    uint64_t* tfree = tfull + kAccSlots;  // [kAccSlots]
-    uint64_t* mdone = tfree + kAccSlots;  // the MMA warp's drain
+    uint64_t* inb = table_ready + 1;       // the routing's inputs have arrived
+    uint64_t* tfull = inb + 1;             // [kAccSlots]
+    uint64_t* tfree = tfull + kAccSlots;   // [kAccSlots]
+    uint64_t* mdone = tfree + kAccSlots;   // the MMA warp's drain
+    uint64_t* adone = mdone + 1;           // every gate/up MMA is complete (the image region is free)
+    uint64_t* hready = adone + 1;          // [2]: a run's image is staged (3 stager warps)
+    uint64_t* bfree = hready + 2;          // [2]: the MMAs reading a run's image are complete
+    uint64_t* ubar = bfree + 2;            // the 4 epilogue warps at a down unit's end
     SlotTable* tb = reinterpret_cast<SlotTable*>(smem + off_tbl);
     RouteSmem* rs = reinterpret_cast<RouteSmem*>(smem + off_route);
     ItemMeta* meta = reinterpret_cast<ItemMeta*>(smem + off_meta);
     AccMeta* accm = reinterpret_cast<AccMeta*>(smem + off_acc);
-    unsigned char* xd = smem + off_xd;
-    unsigned char* xb = smem + off_xb;
+    CombineSmem* cs = reinterpret_cast<CombineSmem*>(smem + off_cs);
     float* xsig = reinterpret_cast<float*>(smem + off_sig);
+    float* hsig = reinterpret_cast<float*>(smem + off_hsig);  // [2][8][I / 128]
+    unsigned char* xb = smem + off_img;                       // phase A: bf16 terms image
+    unsigned char* xd = smem + off_img + (size_t)a.H * 32;    // phase A: int8 digits image
+    unsigned char* hb = smem + off_img;                       // phase B: two run images of I * 32 bytes
     unsigned char* stages = smem + off_stages;
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    // diagnostics: kernel-level events of this CTA (start, past the dependency wait, routed,
-    // MMA warp done, epilogue done)
+    const int NG3 = a.I / 128, nrb = a.H / kRowBlock;
+    const uint32_t img_bytes = (uint32_t)a.I * 32;
+    const uint32_t hd_target = 4u * (uint32_t)(a.I / 64) + (uint32_t)a.hold_extra;
     unsigned long long* ev = a.trace ? trace_rec(a, 0, a.trace_items / 2 - 1) : nullptr;
     if (ev && tid == 0) ev[0] = global_timer_ns();
     if (smem_addr(smem) & 1023u) {  // the swizzled operands need 1024-byte alignment (same in every CTA)
-        if (tid == 0) {
-            set_status(&a.ctl->status, kStatusMisaligned);
-            atomicOr(&a.ctl->k2_fail, 1u);
-        }
+        if (tid == 0) set_status(&a.ctl->status, kStatusMisaligned);
         return;
     }
     if (tid == 0) {
@@ -600,10 +680,25 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             mbar_init(&tfree[j], 4);
         }
         mbar_init(mdone, 1);
+        mbar_init(adone, 1);
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&hready[b], 3);
+            mbar_init(&bfree[b], 1);
+        }
+        mbar_init(ubar, 4);
         abort_flag = 0;
+        stale = 0;
+        routed = 0;
         cta_fail = 0;
+        cs->req[0] = cs->req[1] = -1;
+        // the shared-expert units (known from the shape)
+        even_units(a.S * (a.I / 64), blockIdx.x, gridDim.x, units.a_s0, units.a_s1);
+        even_units(a.S * nrb, blockIdx.x, gridDim.x, units.b_s0, units.b_s1);
+        units.a_r0 = units.a_r1 = units.b_r0 = units.b_r1 = 0;
+        units.na = units.a_s1 - units.a_s0;
+        units.nb = 0;
         fence_mbar_init();
-        pdl_launch_dependents();  // K3 launches early; it waits for this grid before it reads h
+        pdl_launch_dependents();  // the next layer's first kernel launches early; it waits for this grid
     }
     if (warp == 0) tmem_alloc(&tmem_base, kTmemCols);
     load_shared_slots(tb, a, tid, blockDim.x);
@@ -613,59 +708,82 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
     Pipe pipe{tfull, tfree, accm, tmem_base, 0, &abort_flag, fail};
 
     if (warp == 8) {
-        // ---------------- producer: one bulk copy per item ----------------
+        // ---------------- producer: one bulk copy per item into the stage ring ----------------
         int n = 0, st = 0;
         uint32_t round = 0;
-        bool ok = true, routed = false;
+        bool ok = true, waited = false;
         auto wait_table = [&]() {
-            if (!routed) {
-                ok = mbar_wait_warp(table_ready, 0, &abort_flag, fail);
-                routed = true;
+            if (!waited) {
+                ok = mbar_wait_warp(table_ready, 0, &abort_flag, fail) && routed;
+                waited = true;
             }
         };
-        auto issue = [&](int slot, int rb, int ki) {
+        auto issue = [&](const unsigned char* src, uint32_t bytes, int slot, int rb, int ki, int phase, int run) {
             // the last stage holds the routing's logit partials until the table is ready
             if (round == 0 && st == nst - 1) wait_table();
-            if (ok && round > 0 && !mbar_wait_warp(&empty[st], (round - 1) & 1, &abort_flag, fail))
-                ok = false;
+            if (ok && round > 0 && !mbar_wait_warp(&empty[st], (round - 1) & 1, &abort_flag, fail)) ok = false;
             if (!ok) return;
             if (lane == 0) {
-                const bool i8 = slot >= a.S && a.int8;
-                const uint32_t bytes = (uint32_t)w13_item_bytes(i8);
-                const unsigned char* src =
-                    slot < a.S ? reinterpret_cast<const unsigned char*>(a.w13_shared) +
-                                     (size_t)tb->expert[slot] * w13_expert_bytes(a.I, a.H, false)
-                               : reinterpret_cast<const unsigned char*>(a.w13) +
-                                     (size_t)tb->expert[slot] * w13_expert_bytes(a.I, a.H, i8);
-                src += ((size_t)rb * w13_items(a.H, i8) + ki) * bytes;
                 meta[st].slot = slot;
                 meta[st].rb = rb;
                 meta[st].ki = ki;
+                meta[st].phase = phase;
+                meta[st].run = run;
                 mbar_arrive_expect_tx(&full[st], bytes);
                 bulk_g2s(stages + (size_t)st * stage_bytes, src, bytes, &full[st]);
-                unsigned long long* tr = trace_rec(a, 0, n);
+                unsigned long long* tr = trace_rec(a, phase, n);
                 if (tr) tr[4] = global_timer_ns();
             }
             __syncwarp();
             ++n;
-            if (++st == nst) { st = 0; ++round; }
+            if (++st == nst) {
+                st = 0;
+                ++round;
+            }
         };
-        // units (slot, row block of 64 pairs): the shared experts' first (streamed while the
-        // CTA routes), then the routed ones, balanced against each CTA's shared share
-        const int per = a.I / 64;
-        auto issue_units = [&](int slot0, int j0, int j1, bool i8) {
+        auto issue_a = [&](int slot, int rb) {
+            const bool i8 = slot >= a.S && a.int8;
+            const uint32_t bytes = (uint32_t)w13_item_bytes(i8);
+            const unsigned char* base =
+                slot < a.S ? reinterpret_cast<const unsigned char*>(a.w13_shared) +
+                                 (size_t)tb->expert[slot] * w13_expert_bytes(a.I, a.H, false)
+                           : reinterpret_cast<const unsigned char*>(a.w13) +
+                                 (size_t)tb->expert[slot] * w13_expert_bytes(a.I, a.H, i8);
             const int nk = w13_items(a.H, i8);
-            for (int j = j0; j < j1 && ok; ++j)
-                for (int ki = 0; ki < nk && ok; ++ki) issue(slot0 + j / per, j % per, ki);
+            for (int ki = 0; ki < nk && ok; ++ki)
+                issue(base + ((size_t)rb * nk + ki) * bytes, bytes, slot, rb, ki, 0, -1);
         };
-        auto unit_cost = [&](bool i8) { return (int)((size_t)w13_items(a.H, i8) * w13_item_bytes(i8) / 512); };
-        int j0, j1;
-        even_units(a.S * per, blockIdx.x, gridDim.x, j0, j1);
-        issue_units(0, j0, j1, false);
+        const int ns_a = units.a_s1 - units.a_s0;
+        for (int i = 0; i < ns_a && ok; ++i) {  // shared units: streamed while routing
+            int slot, rb;
+            unit_a(units, a, i, slot, rb);
+            issue_a(slot, rb);
+        }
         wait_table();
+        int runs = 0, prev = -1;
         if (ok) {
-            routed_units(a.S * per, unit_cost(false), (tb->nslot - a.S) * per, unit_cost(a.int8 != 0), j0, j1);
-            issue_units(a.S, j0, j1, a.int8 != 0);
+            for (int i = ns_a; i < units.na && ok; ++i) {
+                int slot, rb;
+                unit_a(units, a, i, slot, rb);
+                issue_a(slot, rb);
+            }
+            for (int i = 0; i < units.nb && ok; ++i) {
+                int slot, rb;
+                unit_b(units, a, i, slot, rb);
+                const bool i8 = slot >= a.S && a.int8;
+                const unsigned char* base =
+                    slot < a.S ? reinterpret_cast<const unsigned char*>(a.w2_shared) +
+                                     (size_t)tb->expert[slot] * w2_expert_bytes(a.H, a.I, false)
+                               : reinterpret_cast<const unsigned char*>(a.w2) +
+                                     (size_t)tb->expert[slot] * w2_expert_bytes(a.H, a.I, i8);
+                base += (size_t)rb * w2_rb_bytes(a.I, i8);
+                const int run = slot != prev ? runs++ : -1;
+                prev = slot;
+                const int nk = w2_items(a.I, i8);
+                for (int ki = 0; ki < nk && ok; ++ki)
+                    issue(base + w2_item_offset(i8, ki), (uint32_t)item_bytes(w2_item_atoms(a.I, i8, ki), i8), slot,
+                          rb, ki, 1, ki == 0 ? run : -1);
+            }
         }
         if (lane == 0) {
             if (!ok) {
@@ -680,74 +798,157 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
         }
         __syncwarp();
     } else {
-        // ---------------- warps 0-7: route; then MMA (warp 0) and epilogue (warps 4-7) ----------------
-        cta_route(a, xd, xb, xsig, reinterpret_cast<float*>(stages + (size_t)(nst - 1) * stage_bytes), inb,
-                  &abort_flag, fail, rs, tb, tid, ev);
-        if (tid == 0) mbar_arrive(table_ready);
+        // ---------------- warps 0-7: route; then MMA (0), stagers (1-3), epilogue (4-7) ----------------
+        const bool ok_route =
+            cta_route(a, xd, xb, xsig, reinterpret_cast<float*>(stages + (size_t)(nst - 1) * stage_bytes), inb,
+                      &abort_flag, fail, rs, tb, cs, &stale, tid, ev);
+        if (tid == 0) {
+            if (ok_route) {
+                // the routed units, balanced against each CTA's shared share
+                const int nu = tb->nslot - a.S;
+                routed_units(a.S * (a.I / 64), (int)((size_t)w13_items(a.H, false) * w13_item_bytes(false) / 512),
+                             nu * (a.I / 64),
+                             (int)((size_t)w13_items(a.H, a.int8 != 0) * w13_item_bytes(a.int8 != 0) / 512),
+                             units.a_r0, units.a_r1);
+                routed_units(a.S * nrb, (int)(w2_rb_bytes(a.I, false) / 512), nu * nrb,
+                             (int)(w2_rb_bytes(a.I, a.int8 != 0) / 512), units.b_r0, units.b_r1);
+                units.na = (units.a_s1 - units.a_s0) + (units.a_r1 - units.a_r0);
+                units.nb = (units.b_s1 - units.b_s0) + (units.b_r1 - units.b_r0);
+                routed = 1;
+            } else {
+                abort_flag = 1;
+            }
+            mbar_arrive(table_ready);
+        }
+        named_bar_sync(kBarConsumers, kCW * 32);
         if (ev && tid == 0) ev[2] = global_timer_ns();
         if (warp == 0) {
-            const uint32_t xd_s = smem_addr(xd), xb_s = smem_addr(xb);
+            // ---------------- MMA warp ----------------
+            const uint32_t xd_s = smem_addr(xd), xb_s = smem_addr(xb), hb_s = smem_addr(hb);
             const int nk8 = w13_items(a.H, true), nk16 = w13_items(a.H, false);
-            bool ok = true;
-            int cur = 0;
-            for (int n = 0;; ++n) {
+            bool ok = routed != 0, b_started = false;
+            int cur = 0, b = 0;
+            for (int n = 0; ok; ++n) {
                 const int st = n % nst;
-                unsigned long long* tr = trace_rec(a, 0, n);
-                if (tr && lane == 0) tr[0] = global_timer_ns();
+                const uint64_t t_wait = a.trace ? global_timer_ns() : 0;
                 if (!mbar_wait_warp(&full[st], (n / nst) & 1, &abort_flag, fail)) {
                     ok = false;
                     break;
                 }
                 const int slot = meta[st].slot;
                 if (slot < 0) break;
-                if (tr && lane == 0) tr[1] = global_timer_ns();
-                const int rb = meta[st].rb, ki = meta[st].ki;
+                const int rb = meta[st].rb, ki = meta[st].ki, phase = meta[st].phase, run = meta[st].run;
+                unsigned long long* tr = a.trace ? trace_rec(a, phase, n) : nullptr;
+                if (tr && lane == 0) {
+                    tr[0] = t_wait;
+                    tr[1] = global_timer_ns();
+                }
                 const bool i8 = slot >= a.S && a.int8;
                 unsigned char* item = stages + (size_t)st * stage_bytes;
                 const uint32_t item_s = smem_addr(item);
-                if (i8) {
-                    // both groups of the item in one accumulator (columns 0-31, 32-63)
-                    const float* scl = reinterpret_cast<const float*>(item + 2 * kAtomBytes);
-                    const int j = acquire_acc(pipe, slot, rb, 2 * ki, 1 | 4 | (ki == nk8 - 1 ? 2 : 0), lane);
-                    if (j < 0) {
-                        ok = false;
-                        break;
-                    }
-                    acc_scales(pipe, j, 0, scl, nullptr, lane);
-                    acc_scales(pipe, j, 1, scl + kRowBlock, nullptr, lane);
-                    publish_acc(pipe, j, lane);
-                    if (lane == 0) {
-#pragma unroll
-                        for (int g = 0; g < 2; ++g)
-#pragma unroll
-                            for (int s = 0; s < 4; ++s)
-                                umma_i8(pipe.tmem + kAccCols * j + 32u * g,
-                                        umma_desc_sw128(item_s + g * kAtomBytes + 32 * s),
-                                        umma_desc_sw128(xd_s + (2 * ki + g) * kDigitAtomBytes + 32 * s), kIdescS8, s > 0);
-                        umma_commit(&tfull[j]);
-                    }
-                    __syncwarp();
-                } else {
-                    if (ki == 0) {
-                        cur = acquire_acc(pipe, slot, rb, 0, 2, lane);
-                        if (cur < 0) {
+                if (phase == 0) {
+                    if (i8) {
+                        // both groups of the item in one accumulator (columns 0-31, 32-63)
+                        const float* scl = reinterpret_cast<const float*>(item + 2 * kAtomBytes);
+                        const int j = acquire_acc(pipe, slot, rb, 2 * ki, 1 | 4 | (ki == nk8 - 1 ? 2 : 0), lane);
+                        if (j < 0) {
                             ok = false;
                             break;
                         }
-                        publish_acc(pipe, cur, lane);
-                    }
-                    if (lane == 0) {
+                        acc_scales(pipe, j, 0, scl, nullptr, lane);
+                        acc_scales(pipe, j, 1, scl + kRowBlock, nullptr, lane);
+                        publish_acc(pipe, j, lane);
+                        if (lane == 0) {
 #pragma unroll
-                        for (int at = 0; at < 2; ++at)
+                            for (int g = 0; g < 2; ++g)
 #pragma unroll
-                            for (int s = 0; s < 4; ++s)
-                                umma_f16(pipe.tmem + kAccCols * cur, umma_desc_sw128(item_s + at * kAtomBytes + 32 * s),
-                                         umma_desc_sw128(xb_s + (2 * ki + at) * kTermAtomBytes + 32 * s), kIdescBf16,
-                                         (ki | at | s) != 0);
-                        if (ki == nk16 - 1) umma_commit(&tfull[cur]);
+                                for (int s = 0; s < 4; ++s)
+                                    umma_i8(pipe.tmem + kAccCols * j + 32u * g, umma_desc_sw128(item_s + g * kAtomBytes + 32 * s),
+                                            umma_desc_sw128(xd_s + (2 * ki + g) * kDigitAtomBytes + 32 * s), kIdescS8, s > 0);
+                            umma_commit(&tfull[j]);
+                        }
+                    } else {
+                        if (ki == 0) {
+                            cur = acquire_acc(pipe, slot, rb, 0, 2, lane);
+                            if (cur < 0) {
+                                ok = false;
+                                break;
+                            }
+                            publish_acc(pipe, cur, lane);
+                        }
+                        if (lane == 0) {
+#pragma unroll
+                            for (int at = 0; at < 2; ++at)
+#pragma unroll
+                                for (int s = 0; s < 4; ++s)
+                                    umma_f16(pipe.tmem + kAccCols * cur, umma_desc_sw128(item_s + at * kAtomBytes + 32 * s),
+                                             umma_desc_sw128(xb_s + (2 * ki + at) * kTermAtomBytes + 32 * s), kIdescBf16,
+                                             (ki | at | s) != 0);
+                            if (ki == nk16 - 1) umma_commit(&tfull[cur]);
+                        }
                     }
-                    __syncwarp();
+                } else {
+                    if (!b_started) {  // the image region may be restaged once every gate/up MMA is done
+                        if (lane == 0) umma_commit(adone);
+                        b_started = true;
+                    }
+                    if (run >= 0) {
+                        // a run starts: the previous run's image is free once its MMAs complete
+                        if (run > 0 && lane == 0) umma_commit(&bfree[(run - 1) & 1]);
+                        b = run & 1;
+                        if (!mbar_wait_warp(&hready[b], (run >> 1) & 1, &abort_flag, fail)) {
+                            ok = false;
+                            break;
+                        }
+                    }
+                    const int nk = w2_items(a.I, i8);
+                    const uint32_t img_s = hb_s + (uint32_t)b * img_bytes;
+                    if (i8) {
+                        const int at = w2_item_atoms(a.I, true, ki);
+                        const int j = acquire_acc(pipe, slot, rb, 2 * ki,
+                                                  8 | 1 | (at == 2 ? 4 : 0) | (ki == nk - 1 ? 2 : 0), lane);
+                        if (j < 0) {
+                            ok = false;
+                            break;
+                        }
+                        const float* scl = reinterpret_cast<const float*>(item + at * kAtomBytes);
+                        for (int g = 0; g < at; ++g) {
+                            float sig[kMaxB];
+#pragma unroll
+                            for (int t = 0; t < kMaxB; ++t) sig[t] = hsig[(b * kMaxB + t) * NG3 + 2 * ki + g];
+                            acc_scales(pipe, j, g, scl + g * kRowBlock, sig, lane);
+                        }
+                        publish_acc(pipe, j, lane);
+                        if (lane == 0) {
+                            for (int g = 0; g < at; ++g)
+#pragma unroll
+                                for (int s = 0; s < 4; ++s)
+                                    umma_i8(pipe.tmem + kAccCols * j + 32u * g, umma_desc_sw128(item_s + g * kAtomBytes + 32 * s),
+                                            umma_desc_sw128(img_s + (2 * ki + g) * kDigitAtomBytes + 32 * s), kIdescS8, s > 0);
+                            umma_commit(&tfull[j]);
+                        }
+                    } else {
+                        if (ki == 0) {
+                            cur = acquire_acc(pipe, slot, rb, 0, 8 | 2, lane);
+                            if (cur < 0) {
+                                ok = false;
+                                break;
+                            }
+                            publish_acc(pipe, cur, lane);
+                        }
+                        if (lane == 0) {
+#pragma unroll
+                            for (int at = 0; at < 2; ++at)
+#pragma unroll
+                                for (int s = 0; s < 4; ++s)
+                                    umma_f16(pipe.tmem + kAccCols * cur, umma_desc_sw128(item_s + at * kAtomBytes + 32 * s),
+                                             umma_desc_sw128(img_s + (2 * ki + at) * kTermAtomBytes + 32 * s), kIdescBf16,
+                                             (ki | at | s) != 0);
+                            if (ki == nk - 1) umma_commit(&tfull[cur]);
+                        }
+                    }
                 }
+                __syncwarp();
                 if (lane == 0) umma_commit(&empty[st]);  // the stage is free once these MMAs complete
                 if (tr && lane == 0) {
                     tr[2] = global_timer_ns();
@@ -764,41 +965,195 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             } else if (lane == 0) {
                 abort_flag = 1;
             }
-            if (lane == 0) {  // every MMA complete before TMEM is released
-                umma_commit(mdone);
+            if (lane == 0) {
+                if (!b_started) umma_commit(adone);
+                umma_commit(mdone);  // every MMA complete before TMEM is released
                 mbar_wait(mdone, 0, fail);
             }
             __syncwarp();
             if (ev && lane == 0) ev[3] = global_timer_ns();
-        } else if (warp >= 4) {
-            const int q = warp & 3, row = 32 * q + lane;
+        } else if (warp <= 3) {
+            // ---------------- stagers: each slot run's h rows -> its operand image ----------------
+            // runs in the producer's order; run r uses image r % 2; hready completes after 3 arrivals
+            const int rank = warp - 1;
+            unsigned long long* sv = a.trace ? trace_rec(a, 1, a.trace_items / 2 - 3) : nullptr;
+            int r = 0, prev = -1;
+            bool ok = routed != 0;
+            for (int i = 0; i < units.nb && ok; ++i) {
+                int slot, rb;
+                unit_b(units, a, i, slot, rb);
+                if (slot == prev) continue;
+                prev = slot;
+                const int b = r & 1;
+                unsigned long long* tv = sv && rank == 0 && lane == 0 && r < 2 ? sv + 4 * r : nullptr;
+                // the image region: free of gate/up MMAs (runs 0, 1), or of run r - 2's MMAs
+                if (r < 2) ok = mbar_wait_warp(adone, 0, &abort_flag, fail);
+                else ok = mbar_wait_warp(&bfree[b], ((r - 2) >> 1) & 1, &abort_flag, fail);
+                if (tv) tv[0] = global_timer_ns();
+                // every CTA's gate/up units of the slot are counted (their h rows written)
+                if (ok) {
+                    int done = 0;
+                    if (lane == 0) done = wait_counter_geq(&a.ctl->hdone[slot], hd_target, fail);
+                    ok = __shfl_sync(0xffffffffu, done, 0) != 0;
+                }
+                if (!ok) break;
+                if (tv) tv[1] = global_timer_ns();
+                const int cnt = tb->count[slot], base = tb->base[slot];
+                const bool i8 = slot >= a.S && a.int8;
+                unsigned char* img = hb + (size_t)b * img_bytes;
+                const int ntask = cnt * NG3;
+                for (int t0 = rank; t0 < ntask; t0 += 4 * 3) {
+                    float4 v[4];  // four tasks' loads issued before any of their stores
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int task = t0 + u * 3;
+                        if (task < ntask) {
+                            const int e = task / NG3, g = task - e * NG3;
+                            v[u] = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)(base + e) * a.I + 128 * g + 4 * lane));
+                        }
+                    }
+#pragma unroll
+                    for (int u = 0; u < 4; ++u) {
+                        const int task = t0 + u * 3;
+                        if (task < ntask) {
+                            const int e = task / NG3, g = task - e * NG3;
+                            if (i8) {
+                                uint32_t w[3];
+                                const float sg = group_digits(v[u], w);
+                                if (lane == 0) hsig[(b * kMaxB + e) * NG3 + g] = sg;
+                                put_digits(img, g, e, lane, w);
+                            } else {
+                                put_terms(img, g, e, lane, v[u]);
+                            }
+                        }
+                    }
+                }
+                fence_proxy_async_smem();  // generic writes of the image, read next by the tensor cores
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&hready[b]);
+                if (tv) tv[2] = global_timer_ns();
+                ++r;
+            }
+            if (!ok && lane == 0) abort_flag = 1;
+        } else {
+            // ---------------- epilogue (warps 4-7) ----------------
+            const int q = warp & 3, row = 32 * q + lane, ie = tid - 128;
             float acc[kMaxB];
 #pragma unroll
             for (int t = 0; t < kMaxB; ++t) acc[t] = 0.0f;
-            for (int c = 0;; ++c) {
+            int ia = 0, ib = 0;  // units of each phase counted so far (in the partition's order)
+            const uint32_t yd_target = 4u * (uint32_t)tb->nslot;
+            bool ok = routed != 0;
+            for (int c = 0; ok; ++c) {
                 AccRead r;
-                if (!read_acc(pipe, c, q, lane, false, r)) break;
+                if (!read_acc(pipe, c, q, lane, true, r)) break;
                 if (r.flags & 1) {
                     for (int g = 0; g < ((r.flags & 4) ? 2 : 1); ++g) {
-                        float colsig[kMaxB];
+                        if (r.flags & 8) {
+                            fold_s8(r, g, r.sig[g], acc);
+                        } else {
+                            float colsig[kMaxB];
 #pragma unroll
-                        for (int t = 0; t < kMaxB; ++t) colsig[t] = xsig[t * (a.H / 128) + r.gi + g];
-                        fold_s8(r, g, colsig, acc);
+                            for (int t = 0; t < kMaxB; ++t) colsig[t] = xsig[t * (a.H / 128) + r.gi + g];
+                            fold_s8(r, g, colsig, acc);
+                        }
                     }
                 } else {
                     fold_bf16(r, acc);
                 }
-                if (r.flags & 2) {
-                    // SwiGLU: gate row (lane % 16 < 8) with the up row 8 lanes up; h for the slot's tokens
+                if (!(r.flags & 2)) continue;
+                const int cnt = tb->count[r.slot], base = tb->base[r.slot];
+                if (!(r.flags & 8)) {
+                    // gate/up unit done: SwiGLU (gate row lane % 16 < 8 with the up row 8 lanes up) -> h
                     const bool gate = (lane & 15) < 8;
                     const int pair = 64 * r.rb + 8 * (row >> 4) + (row & 7);
-                    const int base = tb->base[r.slot];
 #pragma unroll
                     for (int t = 0; t < kMaxB; ++t) {
                         const float u = __shfl_xor_sync(0xffffffffu, acc[t], 8);
                         const int pos = tb->pos[r.slot][t];
                         if (gate && pos >= 0) a.h[(size_t)(base + pos) * a.I + pair] = silu(acc[t]) * u;
                         acc[t] = 0.0f;
+                    }
+                    __syncwarp();
+                    if (lane == 0) {
+                        __threadfence();
+                        atomicAdd(&a.ctl->hdone[r.slot], 1u);
+                    }
+                    ++ia;
+                } else {
+                    // down unit done: y rows; the arrival that completes the column block has this
+                    // CTA's 4 epilogue warps combine it
+#pragma unroll
+                    for (int t = 0; t < kMaxB; ++t) {
+                        if (t < cnt) a.y[(size_t)(base + t) * a.H + kRowBlock * r.rb + row] = acc[t];
+                        acc[t] = 0.0f;
+                    }
+                    __syncwarp();
+                    int setter = 0;  // this warp's arrival completed the column block
+                    if (lane == 0) {
+                        __threadfence();
+                        if (atomicAdd(&a.ctl->ydone[r.rb], 1u) + 1u == yd_target) {
+                            atomicExch(&a.ctl->ydone[r.rb], 0u);
+                            __threadfence();
+                            cs->req[ib & 1] = (ib << 8) | (r.rb + 1);
+                            setter = 1;
+                        }
+                        mbar_arrive(ubar);
+                    }
+                    setter = __shfl_sync(0xffffffffu, setter, 0);
+                    ++ib;
+                    __syncwarp();
+                    const bool met = mbar_wait_warp(ubar, (ib - 1) & 1, &abort_flag, fail);
+                    if (!met) {
+                        // a warp of this CTA is gone: a block this warp completed is written NaN by it alone
+                        if (setter) {
+                            if (lane == 0) atomicOr(&a.ctl->call_fail, 1u);
+                            __syncwarp();
+                            nan_block(a, r.rb, lane);
+                            __syncwarp();
+                            if (lane == 0) count_combined(a, 4u);
+                        }
+                        ok = false;
+                        break;
+                    }
+                    const int req = *reinterpret_cast<volatile int*>(&cs->req[(ib - 1) & 1]);
+                    const bool mine = req >= 0 && (req >> 8) == ib - 1;
+                    if (mine) {
+                        const bool failed = __ldcg(&a.ctl->call_fail) != 0u;
+                        combine_block(a, cs, (req & 255) - 1, failed, ie);
+                        __syncwarp();
+                        if (lane == 0) count_combined(a, 1u);
+                    }
+                }
+            }
+            if (routed) {
+                // wind-down after a failure: count this warp's remaining units (the call fails, so
+                // every block is written NaN), so that no CTA waits for them
+                if (ia < units.na || ib < units.nb) {
+                    if (lane == 0) atomicOr(&a.ctl->call_fail, 1u);
+                    abort_flag = 1;
+                }
+                for (; ia < units.na; ++ia) {
+                    int slot, rb;
+                    unit_a(units, a, ia, slot, rb);
+                    if (lane == 0) {
+                        __threadfence();
+                        atomicAdd(&a.ctl->hdone[slot], 1u);
+                    }
+                }
+                for (; ib < units.nb; ++ib) {
+                    int slot, rb;
+                    unit_b(units, a, ib, slot, rb);
+                    int last = 0;
+                    if (lane == 0) {
+                        __threadfence();
+                        last = atomicAdd(&a.ctl->ydone[rb], 1u) + 1u == yd_target;
+                        if (last) atomicExch(&a.ctl->ydone[rb], 0u);
+                    }
+                    if (__shfl_sync(0xffffffffu, last, 0)) {
+                        nan_block(a, rb, lane);
+                        __syncwarp();
+                        if (lane == 0) count_combined(a, 4u);
                     }
                 }
             }
@@ -811,447 +1166,22 @@ decode_gate_up_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
         tc_fence_after();
         tmem_dealloc(tmem_base, kTmemCols);
     }
-    // a failed CTA's h rows are incomplete: the down kernel learns it from k2_fail
-    if (tid == 0 && (cta_fail || abort_flag)) {
-        set_status(&a.ctl->status, cta_fail ? cta_fail : kStatusWaitTimeout);
-        atomicOr(&a.ctl->k2_fail, 1u);
-    }
-}
-
-// ======================================================================================
-// K3: down projection + combine
-// ======================================================================================
-// This CTA's share of the outputs, after every CTA's units (grid barrier): out[t][j] for the
-// flat indices [lo, hi) of the B x H output, one per thread: token t's shared rows in order,
-// then its routed rows in ascending expert id (w * y), from the slot table's row lists.
-UOCR_DEV void combine_slice(const DecodeArgs& a, const int (&trow)[kMaxB][kDecodeMaxTopk],
-                            const float (&tw)[kMaxB][kDecodeMaxTopk], int tid) {
-    const int total = a.B * a.H;
-    const int lo = (int)((long long)total * blockIdx.x / gridDim.x);
-    const int hi = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
-    for (int o = lo + tid; o < hi; o += blockDim.x) {
-        const int t = o / a.H, j = o - t * a.H;
-        float ys[kDecodeMaxShared], yr[kDecodeMaxTopk];
-#pragma unroll
-        for (int q = 0; q < kDecodeMaxShared; ++q)
-            if (q < a.S) ys[q] = __ldcg(a.y + (size_t)(q * a.B + t) * a.H + j);
-#pragma unroll
-        for (int s = 0; s < kDecodeMaxTopk; ++s)
-            if (s < a.topk) yr[s] = __ldcg(a.y + (size_t)trow[t][s] * a.H + j);
-        float acc = 0.0f;
-#pragma unroll
-        for (int q = 0; q < kDecodeMaxShared; ++q)
-            if (q < a.S) acc = __fadd_rn(acc, ys[q]);
-#pragma unroll
-        for (int s = 0; s < kDecodeMaxTopk; ++s)
-            if (s < a.topk) acc = __fmaf_rn(tw[t][s], yr[s], acc);
-        a.out[o] = acc;
-    }
-}
-
-// Units (slot, row block of 128 output rows): w2_items(I) items. A slot run's operand image
-// (int8 [I/128 groups][32 rows][128 B] or bf16 [I/64 atoms][16 rows][128 B], both I * 32
-// bytes) is double-buffered: run r uses buffer r % 2.
-__global__ void __launch_bounds__(kThreads, 1)
-decode_down_kernel(DecodeArgs a, uint32_t ring_bytes, uint32_t off_tbl, uint32_t off_meta, uint32_t off_acc,
-                   uint32_t off_hb, uint32_t off_hsig, uint32_t off_ring) {
-    extern __shared__ __align__(1024) unsigned char smem[];
-    __shared__ int abort_flag, hdesc[2];
-    __shared__ uint32_t tmem_base, cta_fail, verdict;  // cta_fail: this CTA's failure code (published at exit)
-    uint32_t* fail = &cta_fail;
-    __shared__ int trow[kMaxB][kDecodeMaxTopk];
-    __shared__ float tw[kMaxB][kDecodeMaxTopk];
-    uint64_t* full = reinterpret_cast<uint64_t*>(smem);
-    uint64_t* freed = full + kK3Desc;      // the MMAs reading the item's ring bytes are complete
-    uint64_t* empty = freed + kK3Desc;     // the MMA warp is done with the descriptor
-    uint64_t* tfull = empty + kK3Desc;     // [kAccSlots]
-    uint64_t* tfree = tfull + kAccSlots;   // [kAccSlots]
-    uint64_t* hload = tfree + kAccSlots;   // [2]: a run's first item is issued (producer)
-    uint64_t* hready = hload + 2;          // [2]: the run's operand image is staged (7 arrivals)
-    uint64_t* bfree = hready + 2;          // [2]: the MMAs reading the image are complete
-    uint64_t* mdone = bfree + 2;
-    SlotTable* tb = reinterpret_cast<SlotTable*>(smem + off_tbl);
-    ItemMeta* meta = reinterpret_cast<ItemMeta*>(smem + off_meta);
-    AccMeta* accm = reinterpret_cast<AccMeta*>(smem + off_acc);
-    unsigned char* hb = smem + off_hb;
-    float* hsig = reinterpret_cast<float*>(smem + off_hsig);  // [2][8][I / 128]
-    unsigned char* ring = smem + off_ring;
-    const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
-    const int NG3 = a.I / 128;
-    const uint32_t img_bytes = (uint32_t)a.I * 32;
-    unsigned long long* ev = a.trace ? trace_rec(a, 1, a.trace_items / 2 - 1) : nullptr;
-    if (ev && tid == 0) ev[0] = global_timer_ns();
-    if (smem_addr(smem) & 1023u) {  // as in K2: every CTA returns, so none waits at the grid barrier
-        if (tid == 0) set_status(&a.ctl->status, kStatusMisaligned);
-        return;
-    }
-    if (tid == 0) {
-        for (int s = 0; s < kK3Desc; ++s) {
-            mbar_init(&full[s], 1);
-            mbar_init(&freed[s], 1);
-            mbar_init(&empty[s], 1);
-        }
-        for (int j = 0; j < kAccSlots; ++j) {
-            mbar_init(&tfull[j], 2);
-            mbar_init(&tfree[j], 4);
-        }
-        for (int b = 0; b < 2; ++b) {
-            mbar_init(&hload[b], 1);
-            mbar_init(&hready[b], 7);
-            mbar_init(&bfree[b], 1);
-        }
-        mbar_init(mdone, 1);
-        abort_flag = 0;
-        cta_fail = 0;
-        fence_mbar_init();
-        pdl_launch_dependents();  // the next layer's kernel waits for this grid itself
-    }
-    if (warp == 0) tmem_alloc(&tmem_base, kTmemCols);
-    load_shared_slots(tb, a, tid, blockDim.x);
-    tc_fence_before();
-    __syncthreads();
-    tc_fence_after();
-    Pipe pipe{tfull, tfree, accm, tmem_base, 0, &abort_flag, fail};
-
-    if (warp == 8) {
-        // ---------------- producer ----------------
-        // Items are placed back to back in the ring at 1024-byte boundaries (wrapping to 0 when
-        // one does not fit); the first item of a slot's run carries the slot's h rows. Ring
-        // bytes retire in order as the MMAs reading them complete (`freed`); descriptors retire
-        // as the MMA warp finishes with them (`empty`). Run r + 2 starts only after run r's
-        // operand image is staged (its buffer and hdesc slot are reused).
-        uint32_t lo_b[kK3Desc], hi_b[kK3Desc];  // byte range of descriptor d's item
-        int n = 0, oldest = 0, oldest_desc = 0, runs = 0;
-        uint32_t head = 0;
-        bool ok = true;
-        pdl_wait_prior_grid();  // h and the routing table come from K2
-        if (ev && lane == 0) ev[1] = global_timer_ns();
-        load_routed_slots(tb, a, lane);
-        if (ev && lane == 0) ev[4] = global_timer_ns();
-        // units (slot, row block of 128 rows): the shared experts' split evenly, then the routed
-        // ones balanced against each CTA's shared share
-        const int nrb = a.H / kRowBlock;
-        auto unit_cost = [&](bool i8) { return (int)(w2_rb_bytes(a.I, i8) / 512); };
-        int s0, s1, r0, r1;
-        even_units(a.S * nrb, blockIdx.x, gridDim.x, s0, s1);
-        routed_units(a.S * nrb, unit_cost(false), (tb->nslot - a.S) * nrb, unit_cost(a.int8 != 0), r0, r1);
-        if (ev && lane == 0) ev[5] = global_timer_ns();
-        int prev_slot = -1;
-        auto issue_unit = [&](int slot, int rb) {
-            const bool i8 = slot >= a.S && a.int8;
-            const int nk = w2_items(a.I, i8);
-            const bool new_run = slot != prev_slot;
-            prev_slot = slot;
-            for (int ki = 0; ki < nk && ok; ++ki) {
-                const uint32_t wbytes = (uint32_t)item_bytes(w2_item_atoms(a.I, i8, ki), i8);
-                const uint32_t hoff = (wbytes + 15u) & ~15u;
-                const bool run_start = new_run && ki == 0;
-                const uint32_t hbytes = run_start ? (uint32_t)tb->count[slot] * a.I * 4 : 0u;
-                const uint32_t need = hoff + hbytes;
-                if (run_start && runs >= 2 &&
-                    !mbar_wait_warp(&hready[runs & 1], ((runs - 2) >> 1) & 1, &abort_flag, fail)) {
-                    ok = false;
-                    break;
-                }
-                head = (head + 1023u) & ~1023u;
-                if (head + need > ring_bytes) head = 0;
-                // retire ring bytes until this item's do not overlap any still being read
-                while (oldest < n) {
-                    bool clash = false;
-                    for (int m = oldest; m < n && !clash; ++m) {
-                        const int d = m % kK3Desc;
-                        clash = head < hi_b[d] && lo_b[d] < head + need;
-                    }
-                    if (!clash) break;
-                    if (!mbar_wait_warp(&freed[oldest % kK3Desc], (oldest / kK3Desc) & 1, &abort_flag,
-                                        fail)) {
-                        ok = false;
-                        break;
-                    }
-                    ++oldest;
-                }
-                // and the descriptor: item n reuses item n - kK3Desc's
-                while (ok && n - oldest_desc >= kK3Desc) {
-                    if (!mbar_wait_warp(&empty[oldest_desc % kK3Desc], (oldest_desc / kK3Desc) & 1, &abort_flag,
-                                        fail))
-                        ok = false;
-                    ++oldest_desc;
-                }
-                // a retired descriptor's bytes were freed before it: never wait on that `freed`
-                // phase again (its barrier may complete again for a later item)
-                oldest = max(oldest, oldest_desc);
-                if (!ok) break;
-                const int d = n % kK3Desc;
-                lo_b[d] = head;
-                hi_b[d] = head + need;
-                if (lane == 0) {
-                    const unsigned char* wsrc =
-                        slot < a.S ? reinterpret_cast<const unsigned char*>(a.w2_shared) +
-                                         (size_t)tb->expert[slot] * w2_expert_bytes(a.H, a.I, false)
-                                   : reinterpret_cast<const unsigned char*>(a.w2) +
-                                         (size_t)tb->expert[slot] * w2_expert_bytes(a.H, a.I, i8);
-                    wsrc += (size_t)rb * w2_rb_bytes(a.I, i8) + w2_item_offset(i8, ki);
-                    meta[d].slot = slot;
-                    meta[d].rb = rb;
-                    meta[d].ki = ki;
-                    meta[d].off = head;
-                    meta[d].hoff = hbytes ? hoff : 0u;
-                    mbar_arrive_expect_tx(&full[d], wbytes + hbytes);
-                    bulk_g2s(ring + head, wsrc, wbytes, &full[d]);
-                    if (hbytes) {
-                        bulk_g2s(ring + head + hoff, a.h + (size_t)tb->base[slot] * a.I, hbytes, &full[d]);
-                        hdesc[runs & 1] = n;
-                        mbar_arrive(&hload[runs & 1]);
-                    }
-                    unsigned long long* tr = trace_rec(a, 1, n);
-                    if (tr) tr[4] = global_timer_ns();
-                }
-                __syncwarp();
-                if (hbytes) ++runs;
-                head += need;
-                ++n;
-            }
-        };
-        for (int j = s0; j < s1 && ok; ++j) issue_unit(j / nrb, j % nrb);
-        for (int j = r0; j < r1 && ok; ++j) issue_unit(a.S + j / nrb, j % nrb);
-        if (lane == 0) {
-            if (ok) {
-                // end markers: the next descriptor once it is free, and the stagers' next run
-                if (n >= kK3Desc && !mbar_wait(&empty[n % kK3Desc], ((n / kK3Desc) - 1) & 1, fail)) {
-                    ok = false;
-                } else {
-                    meta[n % kK3Desc].slot = -1;
-                    mbar_arrive(&full[n % kK3Desc]);
-                }
-                if (ok && (runs < 2 || mbar_wait(&hready[runs & 1], ((runs - 2) >> 1) & 1, fail))) {
-                    hdesc[runs & 1] = -1;
-                    mbar_arrive(&hload[runs & 1]);
-                } else {
-                    ok = false;
-                }
-            }
-            if (!ok) {
-                abort_flag = 1;
-                for (int m = max(0, n - kK3Desc); m < n; ++m) mbar_wait(&full[m % kK3Desc], (m / kK3Desc) & 1, nullptr);
-            }
-        }
-        __syncwarp();
-    } else if (warp == 0) {
-        // ---------------- MMA warp ----------------
-        bool ok = true;
-        int cur = 0, runs = 0, b = 0;
-        const uint32_t hb_s = smem_addr(hb);
-        for (int n = 0;; ++n) {
-            const int d = n % kK3Desc;
-            unsigned long long* tr = trace_rec(a, 1, n);
-            if (tr && lane == 0) tr[0] = global_timer_ns();
-            if (!mbar_wait_warp(&full[d], (n / kK3Desc) & 1, &abort_flag, fail)) {
-                ok = false;
-                break;
-            }
-            const int slot = meta[d].slot;
-            if (slot < 0) break;
-            if (tr && lane == 0) tr[1] = global_timer_ns();
-            const int rb = meta[d].rb, ki = meta[d].ki;
-            if (meta[d].hoff) {
-                // a run starts: the previous run's image is free once its MMAs complete
-                if (runs > 0 && lane == 0) umma_commit(&bfree[(runs - 1) & 1]);
-                b = runs & 1;
-                if (!mbar_wait_warp(&hready[b], (runs >> 1) & 1, &abort_flag, fail)) {
-                    ok = false;
-                    break;
-                }
-                ++runs;
-            }
-            const bool i8 = slot >= a.S && a.int8;
-            const int nk = w2_items(a.I, i8);
-            unsigned char* item = ring + meta[d].off;
-            const uint32_t item_s = smem_addr(item), img_s = hb_s + (uint32_t)b * img_bytes;
-            if (i8) {
-                // the item's one or two groups in one accumulator (columns 0-31, 32-63)
-                const int at = w2_item_atoms(a.I, true, ki);
-                const int j = acquire_acc(pipe, slot, rb, 2 * ki, 1 | (at == 2 ? 4 : 0) | (ki == nk - 1 ? 2 : 0), lane);
-                if (j < 0) {
-                    ok = false;
-                    break;
-                }
-                const float* scl = reinterpret_cast<const float*>(item + at * kAtomBytes);
-                for (int g = 0; g < at; ++g) {
-                    float sig[kMaxB];
-#pragma unroll
-                    for (int t = 0; t < kMaxB; ++t) sig[t] = hsig[(b * kMaxB + t) * NG3 + 2 * ki + g];
-                    acc_scales(pipe, j, g, scl + g * kRowBlock, sig, lane);
-                }
-                publish_acc(pipe, j, lane);
-                if (lane == 0) {
-                    for (int g = 0; g < at; ++g)
-#pragma unroll
-                        for (int s = 0; s < 4; ++s)
-                            umma_i8(pipe.tmem + kAccCols * j + 32u * g, umma_desc_sw128(item_s + g * kAtomBytes + 32 * s),
-                                    umma_desc_sw128(img_s + (2 * ki + g) * kDigitAtomBytes + 32 * s), kIdescS8, s > 0);
-                    umma_commit(&tfull[j]);
-                }
-            } else {
-                if (ki == 0) {
-                    cur = acquire_acc(pipe, slot, rb, 0, 2, lane);
-                    if (cur < 0) {
-                        ok = false;
-                        break;
-                    }
-                    publish_acc(pipe, cur, lane);
-                }
-                if (lane == 0) {
-#pragma unroll
-                    for (int at = 0; at < 2; ++at)
-#pragma unroll
-                        for (int s = 0; s < 4; ++s)
-                            umma_f16(pipe.tmem + kAccCols * cur, umma_desc_sw128(item_s + at * kAtomBytes + 32 * s),
-                                     umma_desc_sw128(img_s + (2 * ki + at) * kTermAtomBytes + 32 * s), kIdescBf16,
-                                     (ki | at | s) != 0);
-                    if (ki == nk - 1) umma_commit(&tfull[cur]);
-                }
-            }
-            if (lane == 0) {
-                umma_commit(&freed[d]);  // the item's ring bytes are free once these MMAs complete
-                mbar_arrive(&empty[d]);  // the descriptor is no longer read
-            }
-            if (tr && lane == 0) {
-                tr[2] = global_timer_ns();
-                tr[3] = ((unsigned long long)slot << 32) | ((unsigned)rb << 16) | (unsigned)ki;
-            }
-            __syncwarp();
-        }
-        if (ok) {
-            const int j = acquire_acc(pipe, -1, 0, 0, 0, lane);  // end marker
-            if (j >= 0) {
-                publish_acc(pipe, j, lane);
-                if (lane == 0) mbar_arrive(&tfull[j]);
-            }
-        } else if (lane == 0) {
-            abort_flag = 1;
-        }
-        if (lane == 0) {
-            umma_commit(mdone);
-            mbar_wait(mdone, 0, fail);
-        }
-        __syncwarp();
-    } else {
-        // ---------------- stagers (warps 1-3, and 4-7 for the first run) and epilogue (4-7) ----------------
-        // A run's h rows -> its operand image: `nw` warps (rank 0..nw-1) share the (entry, group)
-        // tasks; hready completes after 7 arrivals (3 stager warps add 4 from rank 0).
-        // diagnostics: runs 0 and 1 of stager rank 0 {hload, data, image free, staged}
-        unsigned long long* sv = a.trace ? trace_rec(a, 1, a.trace_items / 2 - 3) : nullptr;
-        auto stage = [&](int r, int nw, int rank) -> bool {
-            const int b = r & 1;
-            unsigned long long* tv = sv && rank == 0 && lane == 0 && r < 2 ? sv + 4 * r : nullptr;
-            if (!mbar_wait_warp(&hload[b], (r >> 1) & 1, &abort_flag, fail)) return false;
-            if (tv) tv[0] = global_timer_ns();
-            const int n = hdesc[b];
-            if (n < 0) return false;
-            const int d = n % kK3Desc;
-            if (!mbar_wait_warp(&full[d], (n / kK3Desc) & 1, &abort_flag, fail)) return false;
-            if (tv) tv[1] = global_timer_ns();
-            if (r >= 2 && !mbar_wait_warp(&bfree[b], ((r - 2) >> 1) & 1, &abort_flag, fail)) return false;
-            if (tv) tv[2] = global_timer_ns();
-            const int slot = meta[d].slot, cnt = tb->count[slot];
-            const bool i8 = slot >= a.S && a.int8;
-            const float* h = reinterpret_cast<const float*>(ring + meta[d].off + meta[d].hoff);
-            unsigned char* img = hb + (size_t)b * img_bytes;
-            const int ntask = cnt * NG3;
-            for (int t0 = rank; t0 < ntask; t0 += 4 * nw) {
-                float4 v[4];  // four tasks' loads issued before any of their stores
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int task = t0 + u * nw;
-                    if (task < ntask) {
-                        const int e = task / NG3, g = task - e * NG3;
-                        v[u] = *reinterpret_cast<const float4*>(h + (size_t)e * a.I + 128 * g + 4 * lane);
-                    }
-                }
-#pragma unroll
-                for (int u = 0; u < 4; ++u) {
-                    const int task = t0 + u * nw;
-                    if (task < ntask) {
-                        const int e = task / NG3, g = task - e * NG3;
-                        if (i8) {
-                            uint32_t w[3];
-                            const float sg = group_digits(v[u], w);
-                            if (lane == 0) hsig[(b * kMaxB + e) * NG3 + g] = sg;
-                            put_digits(img, g, e, lane, w);
-                        } else {
-                            put_terms(img, g, e, lane, v[u]);
-                        }
-                    }
-                }
-            }
-            fence_proxy_async_smem();  // generic writes of the image, read next by the tensor cores
-            __syncwarp();
-            if (lane == 0) mbar_arrive_cnt(&hready[b], nw == 3 && rank == 0 ? 5u : 1u);
-            if (tv) tv[3] = global_timer_ns();
-            return true;
-        };
-        bool more = stage(0, 7, warp - 1);
-        if (warp <= 3) {
-            for (int r = 1; more; ++r) more = stage(r, 3, warp - 1);
-        } else {
-            // ---------------- epilogue ----------------
-            const int q = warp & 3, row = 32 * q + lane;
-            float acc[kMaxB];
-#pragma unroll
-            for (int t = 0; t < kMaxB; ++t) acc[t] = 0.0f;
-            for (int c = 0;; ++c) {
-                AccRead r;
-                if (!read_acc(pipe, c, q, lane, true, r)) break;
-                if (r.flags & 1) {
-                    fold_s8(r, 0, r.sig[0], acc);
-                    if (r.flags & 4) fold_s8(r, 1, r.sig[1], acc);
-                } else {
-                    fold_bf16(r, acc);
-                }
-                if (r.flags & 2) {
-                    const int cnt = tb->count[r.slot], base = tb->base[r.slot];
-#pragma unroll
-                    for (int t = 0; t < kMaxB; ++t) {
-                        if (t < cnt) a.y[(size_t)(base + t) * a.H + kRowBlock * r.rb + row] = acc[t];
-                        acc[t] = 0.0f;
-                    }
-                }
-            }
-            if (ev && tid == 128) ev[2] = global_timer_ns();
-        }
-    }
-    tc_fence_before();
-    __syncthreads();
-    if (warp == 0) {
-        tc_fence_after();
-        tmem_dealloc(tmem_base, kTmemCols);
-    }
-
-    // ---------------- combine: every CTA's y rows are written (grid barrier) ----------------
-    pdl_wait_prior_grid();  // the routing table (K2); already complete for the producer
-    const int tk = tid / kDecodeMaxTopk, ts = tid % kDecodeMaxTopk;
-    if (tk < kMaxB) {
-        const bool v = tk < a.B && ts < a.topk;
-        trow[tk][ts] = v ? __ldcg(&a.table->tok_row[tk][ts]) : 0;
-        tw[tk][ts] = v ? __ldcg(&a.table->tok_w[tk][ts]) : 0.0f;
-    }
-    // the CTAs' failures (this one's, the gate/up kernel's) ride into the barrier: the combine runs
-    // only if nothing of this call failed, else every CTA writes NaN over its share of the output
-    const uint32_t mine = cta_fail | (abort_flag ? (uint32_t)kStatusWaitTimeout : 0u) |
-                          (__ldcg(&a.ctl->k2_fail) ? (uint32_t)kStatusWaitTimeout : 0u);
-    const uint32_t bad = grid_barrier_gather(&a.ctl->bar_count, &a.ctl->bar_epoch, &a.ctl->bar_fail, a.ctl->verdict,
-                                             &a.ctl->k2_fail, gridDim.x + (uint32_t)a.bar_extra, mine, fail,
-                                             &verdict);
-    if (ev && tid == 0) ev[3] = global_timer_ns();
-    if (bad == 0) {
-        combine_slice(a, trow, tw, tid);
-    } else {
+    if (tid == 0 && cta_fail) set_status(&a.ctl->status, cta_fail);
+    if (stale) {
+        // an earlier call's failure is unread: NaN over this CTA's share of the output
         const int total = a.B * a.H;
         const int lo = (int)((long long)total * blockIdx.x / gridDim.x);
         const int hi = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
         for (int o = lo + tid; o < hi; o += blockDim.x) a.out[o] = __uint_as_float(0x7FC00000u);
+    } else if (!routed) {
+        // the routing's inputs never arrived here: this CTA cannot count its units, so it writes NaN
+        // over the whole output itself (the blocks its units belong to are never combined)
+        if (tid == 0) {
+            atomicOr(&a.ctl->call_fail, 1u);
+            set_status(&a.ctl->status, kStatusWaitTimeout);
+        }
+        for (int o = tid; o < a.B * a.H; o += blockDim.x) a.out[o] = __uint_as_float(0x7FC00000u);
     }
-    if (tid == 0 && cta_fail) set_status(&a.ctl->status, cta_fail);
 }
 
 // ======================================================================================
@@ -1287,9 +1217,9 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
     cudaDeviceGetAttribute(&max_smem, cudaDevAttrMaxSharedMemoryPerBlockOptin, dev);
     cudaDeviceGetAttribute(&sm_smem, cudaDevAttrMaxSharedMemoryPerMultiprocessor, dev);
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    // K2 / K3 leave room on their SM for their own static shared memory (< 1 KB) and their
-    // reservation, and for K1's CTAs (no shared memory, 1 KB reservation each), so K1 can start
-    // beside them. The dynamic region is 1024-byte aligned (the swizzled operands).
+    // The experts kernel leaves room on its SM for its own static shared memory (< 1 KB) and its
+    // reservation, and for the next layer's K1 CTAs (no shared memory, 1 KB reservation each), so
+    // those start beside it. The dynamic region is 1024-byte aligned (the swizzled operands).
     const int k1_ctas = a.E * 8 + kMaxB * (a.H / 128);
     const int k1_per_sm = (k1_ctas + sms - 1) / sms;
     max_smem = std::min(max_smem - 1024, sm_smem - 1024 - 1024 - 1024 * k1_per_sm);
@@ -1298,7 +1228,7 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
         a.trace = g_decode_trace;
         a.trace_items = (int)(g_decode_trace_bytes / (sizeof(unsigned long long) * 8 * (size_t)sms)) & ~1;
     }
-    a.bar_extra = g_decode_barrier_extra;
+    a.hold_extra = g_decode_wait_extra;
 
     // ---- K1: logit partials (one CTA per expert and segment) and the B operand images
     {
@@ -1306,62 +1236,39 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
         err = launch_pdl(reinterpret_cast<const void*>(decode_logits_kernel), dim3(k1_ctas), dim3(32), 0, st, args);
         if (err != cudaSuccess) return err;
     }
-    // ---- K2: route + gate/up; a stage holds one w13 item (the last one first the logit partials)
-    {
-        const uint32_t stage_bytes = (uint32_t)up(
-            std::max({w13_item_bytes(false), a.int8 ? w13_item_bytes(true) : size_t(0),
-                      sizeof(float) * kMaxB * 64 * 8}),
-            1024);
-        const size_t off_tbl = 256;
-        const size_t off_route = off_tbl + up(sizeof(SlotTable), 128);
-        const size_t off_meta = off_route + up(sizeof(RouteSmem), 128);
-        const size_t off_acc = off_meta + up(sizeof(ItemMeta) * 8, 128);
-        const size_t off_sig = off_acc + up(sizeof(AccMeta) * kAccSlots, 128);
-        const size_t off_xb = up(off_sig + sizeof(float) * kMaxB * (a.H / 128), 1024);
-        const size_t off_xd = off_xb + (size_t)a.H * 32;
-        const size_t off_stages = off_xd + (a.int8 ? (size_t)a.H * 32 : 0);
-        if ((size_t)max_smem < off_stages + 2 * (size_t)stage_bytes) return cudaErrorInvalidConfiguration;
-        int nst = (int)std::min<size_t>(8, ((size_t)max_smem - off_stages) / stage_bytes);
-        const size_t smem = off_stages + (size_t)nst * stage_bytes;
-        const void* k2 = reinterpret_cast<const void*>(decode_gate_up_kernel);
-        err = ensure_smem_optin(k2, smem);
-        if (err != cudaSuccess) return err;
-        uint32_t o[8] = {(uint32_t)off_tbl, (uint32_t)off_route, (uint32_t)off_meta, (uint32_t)off_acc,
-                         (uint32_t)off_xd,  (uint32_t)off_xb,    (uint32_t)off_sig,  (uint32_t)off_stages};
-        uint32_t sb = stage_bytes;
-        void* args[] = {&a, &nst, &sb, &o[0], &o[1], &o[2], &o[3], &o[4], &o[5], &o[6], &o[7]};
-        err = launch_pdl(k2, dim3(sms), dim3(kThreads), smem, st, args);
-        if (err != cudaSuccess) return err;
-    }
-    // ---- K3: two operand images for slot runs, the rest of shared memory is the item ring
-    {
-        const size_t off_tbl = 512;  // 3 x kK3Desc + 2 x kAccSlots + 7 mbarriers before it
-        const size_t off_meta = off_tbl + up(sizeof(SlotTable), 128);
-        const size_t off_acc = off_meta + up(sizeof(ItemMeta) * kK3Desc, 128);
-        const size_t off_hsig = off_acc + up(sizeof(AccMeta) * kAccSlots, 128);
-        const size_t off_hb = up(off_hsig + sizeof(float) * 2 * kMaxB * (a.I / 128), 1024);
-        const size_t off_ring = off_hb + 2 * (size_t)a.I * 32;
-        const size_t max_item =
-            up(std::max(item_bytes(kW2Atoms, false), a.int8 ? item_bytes(kW2Atoms, true) : size_t(0)), 16) +
-            (size_t)kMaxB * a.I * 4;
-        if ((size_t)max_smem < off_ring + max_item + 1024) return cudaErrorInvalidConfiguration;
-        uint32_t ring_bytes = (uint32_t)(((size_t)max_smem - off_ring) & ~size_t(1023));
-        const size_t smem = off_ring + ring_bytes;
-        const void* k3 = reinterpret_cast<const void*>(decode_down_kernel);
-        err = ensure_smem_optin(k3, smem);
-        if (err != cudaSuccess) return err;
-        // the grid barrier needs every CTA resident: one per SM must fit, and the launch is
-        // cooperative so that it is never run partly behind another stream's kernels
-        int per_sm = 0;
-        err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k3, kThreads, smem);
-        if (err != cudaSuccess) return err;
-        if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
-        uint32_t o[6] = {(uint32_t)off_tbl, (uint32_t)off_meta, (uint32_t)off_acc,
-                         (uint32_t)off_hb,  (uint32_t)off_hsig, (uint32_t)off_ring};
-        void* args[] = {&a, &ring_bytes, &o[0], &o[1], &o[2], &o[3], &o[4], &o[5]};
-        err = launch_pdl(k3, dim3(sms), dim3(kThreads), smem, st, args, true);
-        if (err != cudaSuccess) return err;
-    }
+    // ---- the experts kernel: a stage holds one item of either phase (the last one first the
+    // logit partials); the image region holds K1's operand images, then two run images
+    const uint32_t stage_bytes = (uint32_t)up(
+        std::max({w13_item_bytes(false), a.int8 ? w13_item_bytes(true) : size_t(0), sizeof(float) * kMaxB * 64 * 8}),
+        1024);
+    const size_t off_tbl = 512;  // the mbarriers before it
+    const size_t off_route = off_tbl + up(sizeof(SlotTable), 128);
+    const size_t off_meta = off_route + up(sizeof(RouteSmem), 128);
+    const size_t off_acc = off_meta + up(sizeof(ItemMeta) * 8, 128);
+    const size_t off_cs = off_acc + up(sizeof(AccMeta) * kAccSlots, 128);
+    const size_t off_sig = off_cs + up(sizeof(CombineSmem), 128);
+    const size_t off_hsig = off_sig + up(sizeof(float) * kMaxB * (a.H / 128), 128);
+    const size_t off_img = up(off_hsig + sizeof(float) * 2 * kMaxB * (a.I / 128), 1024);
+    const size_t img = std::max((size_t)a.H * 32 * (a.int8 ? 2 : 1), (size_t)2 * a.I * 32);
+    const size_t off_stages = up(off_img + img, 1024);
+    if ((size_t)max_smem < off_stages + 2 * (size_t)stage_bytes) return cudaErrorInvalidConfiguration;
+    int nst = (int)std::min<size_t>(8, ((size_t)max_smem - off_stages) / stage_bytes);
+    const size_t smem = off_stages + (size_t)nst * stage_bytes;
+    const void* k = reinterpret_cast<const void*>(decode_experts_kernel);
+    err = ensure_smem_optin(k, smem);
+    if (err != cudaSuccess) return err;
+    // the CTAs wait on each other's units: one per SM must fit, and the launch is cooperative so
+    // that the grid never runs partly behind another stream's kernels
+    int per_sm = 0;
+    err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem);
+    if (err != cudaSuccess) return err;
+    if (per_sm < 1) return cudaErrorCooperativeLaunchTooLarge;
+    uint32_t o[9] = {(uint32_t)off_tbl, (uint32_t)off_route, (uint32_t)off_meta, (uint32_t)off_acc, (uint32_t)off_cs,
+                     (uint32_t)off_sig, (uint32_t)off_hsig, (uint32_t)off_img, (uint32_t)off_stages};
+    uint32_t sb = stage_bytes;
+    void* args[] = {&a, &nst, &sb, &o[0], &o[1], &o[2], &o[3], &o[4], &o[5], &o[6], &o[7], &o[8]};
+    err = launch_pdl(k, dim3(sms), dim3(kThreads), smem, st, args, true);
+    if (err != cudaSuccess) return err;
     return cudaGetLastError();
 }
 

@@ -423,7 +423,7 @@ EpPeerLayout ep_peer_layout(int world, int cap, int H, int k) {
     EpPeerLayout d{};
     const size_t slots = (size_t)world * cap;
     size_t off = 0;
-    d.status = off; off += 256;
+    d.status = off; off += kCtlClearBytes;  // status region (cleared whole after a failure)
     d.sig = off; off += align256(sizeof(EpSig) * kEpMaxWorld);
     d.eid = off; off += align256(slots * k * sizeof(int32_t));
     d.w = off; off += align256(slots * k * sizeof(float));

@@ -24,43 +24,29 @@ cudaError_t launch_route(const float* x, int T, int H, const uint16_t* wg, int E
 // decode.cu
 // Control block at the start of a decode workspace, zero-filled once by the caller.
 //   status     sticky: the code of the first device-side failure of any call on this workspace,
-//              until the host reads and clears it (uocr_moe_device_status). Only reported, never
-//              used to decide anything on the device.
-//   k2_fail    this call's gate/up kernel failed (set by its CTAs at exit, read by every down-kernel
-//              CTA after its dependency wait, cleared by the down kernel's last barrier arrival).
-//   bar_*      the down kernel's grid barrier: arrivals counted modulo the grid size (the last
-//              arrival of a round subtracts the grid size), completed rounds, and the failures the
-//              CTAs carried into it; verdict[e & 1] holds round e's failures for the waiters.
-// A call whose own kernels failed writes NaN to its whole output instead of the combine, so a
-// failure never leaves stale values that look like a result; later calls are unaffected.
+//              until the host reads and clears it (uocr_moe_device_status, which also zeroes the
+//              rest of this block). While it is set, every call writes NaN and touches no counter.
+//   call_fail  this call failed somewhere (set before the failing CTA counts its remaining units).
+//   hdone[s]   gate/up units of slot s finished (4 epilogue warps each: 4 * I/64 per slot).
+//   ydone[rb]  down units of output column block rb finished (4 per unit, 4 * slots in all): the
+//              arrival that completes a block has its CTA combine it (or write it NaN).
+//   cdone      combined column blocks (4 per block); the last resets hdone, call_fail and itself,
+//              so every call starts from zero (ydone[rb] is reset by the block's completing arrival).
 struct DecodeCtl {
     uint32_t status;
-    uint32_t bar_count;
-    uint32_t bar_epoch;
-    uint32_t k2_fail;
-    uint32_t bar_fail;
-    uint32_t verdict[2];
-    uint32_t pad[57];
+    uint32_t call_fail;
+    uint32_t cdone;
+    uint32_t pad0[5];
+    uint32_t hdone[72];
+    uint32_t ydone[64];
+    uint32_t pad1[112];
 };
-// Words of the control block the host clears along with `status` (uocr_moe_device_status).
-constexpr size_t kCtlClearBytes = 7 * sizeof(uint32_t);
+// Bytes at the start of a workspace the host clears along with its status word: the whole decode
+// control block; prefill and exchange workspaces keep their status word at the start of a status
+// region of the same size.
+constexpr size_t kCtlClearBytes = 1024;
 constexpr int kDecodeMaxShared = 8;
 constexpr int kDecodeMaxTopk = 8;
-
-// The step's routing grouped by expert (written by the route kernel's last CTA). Routed slot u
-// (the u-th distinct expert, ascending id) owns rows [base[u], base[u] + count[u]) of the h and
-// y scratch; shared expert q owns rows [qB, qB + B) (row qB + t is token t).
-struct RouteTable {
-    int U;  // distinct routed experts
-    int pad[3];
-    int expert[64];
-    int count[64];
-    int base[64];
-    int token[64][8];
-    float weight[64][8];
-    int tok_row[8][kDecodeMaxTopk];    // token t's routed rows, ascending expert id
-    float tok_w[8][kDecodeMaxTopk];    // and their routing weights
-};
 
 struct DecodeArgs {
     int B, H, I, E, S, topk, G, int8;
@@ -73,7 +59,7 @@ struct DecodeArgs {
     const void* w2;
     const uint16_t* w13_shared;
     const uint16_t* w2_shared;
-    float* h;       // [(k+S)*B, I], slot-contiguous rows
+    float* h;       // [(k+S)*B, I], slot-contiguous rows (shared slot q: rows qB..qB+B-1, routed slots after)
     float* y;       // [(k+S)*B, H], slot-contiguous rows
     float* out;     // [B, H]
     DecodeCtl* ctl;
@@ -81,16 +67,16 @@ struct DecodeArgs {
     unsigned char* xd;   // [H / 128][32 rows][128 B]: x as int8 digit planes, the MMA B operand image (K1 -> K2)
     unsigned char* xb;   // [H / 64][16 rows][128 B]: x as two bf16 terms, the MMA B operand image
     float* xsig;         // [8][H / 128] scales of the digit groups
-    RouteTable* table;
     unsigned long long* trace;  // optional per-CTA item timeline (diagnostics), null = off
     int trace_items;            // items recorded per CTA
-    int bar_extra;              // test hook: the down kernel's barrier waits for this many more arrivals
+    int hold_extra;             // test hook: the down phase waits for this many more gate/up arrivals per slot
 };
 // diagnostics: the trace buffer the next decode launches record into (capi.cu)
 extern unsigned long long* g_decode_trace;
 extern size_t g_decode_trace_bytes;
-// test hook: extra arrivals the next decode launches' grid barrier waits for (capi.cu)
-extern int g_decode_barrier_extra;
+// test hook: gate/up arrivals per slot the next decode launches' down phase waits for on top of the
+// real ones (capi.cu)
+extern int g_decode_wait_extra;
 cudaError_t launch_decode_layer(const DecodeArgs& a, cudaStream_t st);
 
 // prefill.cu

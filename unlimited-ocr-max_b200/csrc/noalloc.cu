@@ -16,8 +16,8 @@
 // array is zero when the library is loaded (a __device__ array is zero-filled); a call's own
 // counters return to a state the next call accepts, and every other scratch byte a call reads
 // is written earlier in the same call. Its status word is sticky: a call whose device-side
-// bounded wait gave up writes NaN over its output and records the failure there, and
-// uocr_moe_decode_noalloc_status reads and clears it (later calls compute normally either way).
+// bounded wait gave up writes NaN over its output and records the failure there; until
+// uocr_moe_decode_noalloc_status has read (and so cleared) it, later calls write NaN too.
 //
 // The first call on each device looks up the array's device address (cudaGetSymbolAddress,
 // with that device current) and caches it; that first call should come before any stream

@@ -870,7 +870,7 @@ PrefillLayout prefill_layout(int T, int H, int I, int E, int S, int topk, bool i
     const size_t kT = (size_t)topk * T;
     const size_t nchunks = (kT + kChunk - 1) / kChunk;
     size_t off = 0;
-    d.status = off; off += 128;
+    d.status = off; off += kCtlClearBytes;  // status region (cleared whole after a failure)
     d.n_valid = off; off += 128;
     d.ids = off; off += al(sizeof(int32_t) * kT);
     d.wts = off; off += al(sizeof(float) * kT);

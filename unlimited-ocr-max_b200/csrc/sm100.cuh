@@ -173,45 +173,6 @@ UOCR_DEV bool wait_word_ne(const uint32_t* p, uint32_t old, uint32_t* status) {
     return true;
 }
 
-// Barrier over every CTA of a grid whose CTAs are all resident at once (a persistent launch of
-// one CTA per SM) that also gathers the CTAs' failures. `expected` arrivals complete a round:
-// arrivals are counted modulo `expected`, and the arrival that brings the count to a multiple of
-// it takes the failures the round's CTAs or-ed into `fail` before arriving, stores them in
-// verdict[epoch & 1], subtracts `expected` from the count and advances the epoch, which the
-// others wait for (bounded: a CTA that gives up records kStatusWaitTimeout in `cta_fail`). A
-// late CTA still completes its round when it arrives, and a round that waited for more arrivals
-// than there were (a test hook) leaves a multiple of the grid in the count, which later rounds'
-// arithmetic ignores. The completing arrival also zeroes `clear` (a per-call word every CTA read
-// before arriving). Returns the round's failures (nonzero also when this CTA gave up). All threads
-// of the CTA call it.
-UOCR_DEV uint32_t grid_barrier_gather(uint32_t* count, uint32_t* epoch, uint32_t* fail, uint32_t* verdict,
-                                      uint32_t* clear, uint32_t expected, uint32_t my_fail, uint32_t* cta_fail,
-                                      uint32_t* out_smem) {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const uint32_t e0 = ld_acquire_gpu(epoch);
-        if (my_fail) atomicOr(fail, my_fail);
-        __threadfence();  // this CTA's writes (ordered before it by __syncthreads) before the arrival
-        uint32_t v;
-        if ((atomicAdd(count, 1u) + 1u) % expected == 0u) {
-            v = atomicExch(fail, 0u);
-            verdict[e0 & 1u] = v;
-            atomicExch(clear, 0u);
-            atomicSub(count, expected);
-            __threadfence();
-            atomicAdd(epoch, 1u);
-        } else if (wait_word_ne(epoch, e0, cta_fail)) {
-            v = *reinterpret_cast<volatile uint32_t*>(&verdict[e0 & 1u]);
-        } else {
-            v = kStatusWaitTimeout;
-        }
-        __threadfence();
-        *out_smem = v | my_fail;
-    }
-    __syncthreads();
-    return *out_smem;
-}
-
 // ---- named barriers (a subset of the CTA's warps) ----------------------------------------
 UOCR_DEV void named_bar_sync(uint32_t id, uint32_t threads) {
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
