@@ -537,6 +537,15 @@ def ep_measure(args, torch, uocr, synth, dist, world, rank, device, steps: int, 
     torch.cuda.synchronize()
     if sampler:
         sampler.start()
+        t0 = time.time()
+        while True:  # untimed load so the sampler sees the clocks under load (every rank the same count)
+            for _ in range(20):
+                out = moe(x)
+            torch.cuda.synchronize()
+            go = torch.tensor([int(time.time() - t0 < args.settle)], device=device)
+            dist.all_reduce(go, op=dist.ReduceOp.MIN)
+            if not int(go.item()):
+                break
     dist.barrier()
     torch.cuda.synchronize()
     a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)

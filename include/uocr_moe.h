@@ -157,8 +157,9 @@ UOCR_API int uocr_moe_route(const float* x, int64_t T, int64_t H, const uint16_t
  * out [B, H] fp32 = routed top-k experts weighted by the router + shared experts.
  * ids_out / wts_out (nullable) receive the routing. `workspace` must hold
  * uocr_moe_decode_workspace_bytes(L, B) bytes (256-byte aligned), zero-filled once before its
- * first use. Two launches: the router logits, then one persistent experts kernel (a cooperative
- * launch: its CTAs, one per SM, wait on each other's units). Every device-side wait is bounded: a
+ * first use. Two launches: the router logits, then one persistent experts kernel (one CTA per SM,
+ * all resident: they wait on each other's units; a kernel of another stream that holds SMs makes
+ * the call fail as below, it never hangs). Every device-side wait is bounded: a
  * call in which one gave up writes NaN over `out` and sets the workspace's sticky status; until
  * uocr_moe_device_status has read (and so cleared) it, later calls on that workspace write NaN too. */
 UOCR_API size_t uocr_moe_decode_workspace_bytes(const uocr_moe_layer* L, int64_t B);

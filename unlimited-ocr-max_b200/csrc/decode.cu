@@ -183,9 +183,10 @@ struct CombineSmem {
 // buffer, which the producer fills only after the table is ready) and K1's operand images.
 // Returns false (nothing routed) if the workspace holds an unread failure (`stale`) or the inputs
 // did not arrive in time.
+// The tokens' operand images arrive on `imb` (the MMA warp waits for them), the rest on `inb`.
 UOCR_DEV bool cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* xb, float* xsig, float* part,
-                        uint64_t* inb, volatile int* abort_flag, uint32_t* fail, RouteSmem* rs, SlotTable* tb,
-                        CombineSmem* cs, int* stale, int tid, unsigned long long* ev) {
+                        uint64_t* inb, uint64_t* imb, volatile int* abort_flag, uint32_t* fail, RouteSmem* rs,
+                        SlotTable* tb, CombineSmem* cs, int* stale, int tid, unsigned long long* ev) {
     const int warp = tid >> 5, lane = tid & 31;
     const int H = a.H, B = a.B, E = a.E, k = a.topk, kB = k * B;
     unsigned long long* rv = a.trace ? trace_rec(a, 0, a.trace_items / 2 - 2) : nullptr;  // diagnostics
@@ -205,11 +206,12 @@ UOCR_DEV bool cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* x
     if (warp == 0) {
         const uint32_t pbytes = (uint32_t)B * 64 * 8 * 4, img = (uint32_t)H * 32;
         const uint32_t dbytes = a.int8 ? img : 0u, sbytes = a.int8 ? 8u * (H / 128) * 4 : 0u;
-        if (lane == 0) mbar_arrive_expect_tx(inb, pbytes + dbytes + sbytes + img);
+        if (lane == 0) mbar_arrive_expect_tx(inb, pbytes + sbytes);
+        if (lane == 1) mbar_arrive_expect_tx(imb, dbytes + img);
         __syncwarp();
         if (lane == 0) bulk_g2s(part, a.logits, pbytes, inb);
-        if (lane == 1) bulk_g2s(xb, a.xb, img, inb);
-        if (lane == 2 && dbytes) bulk_g2s(xd, a.xd, dbytes, inb);
+        if (lane == 1) bulk_g2s(xb, a.xb, img, imb);
+        if (lane == 2 && dbytes) bulk_g2s(xd, a.xd, dbytes, imb);
         if (lane == 3 && sbytes) bulk_g2s(xsig, a.xsig, sbytes, inb);
     }
     if (!mbar_wait_warp(inb, 0, abort_flag, fail)) *abort_flag = 1;
@@ -619,7 +621,7 @@ UOCR_DEV void count_combined(const DecodeArgs& a, uint32_t n) {
     }
 }
 
-// Persistent, one CTA per SM (a cooperative launch: CTAs wait on each other's units), 9 warps:
+// Persistent, one CTA per SM (every CTA resident: they wait on each other's units), 9 warps:
 // warp 8 streams items (one bulk copy each) into a ring of fixed stages, first the gate/up units
 // (phase A: shared ones while the CTA routes, then routed), then the down units (phase B); warp 0
 // issues their tcgen05 MMAs (B operand: the tokens' images from K1 in phase A, the slot run's h
@@ -647,6 +649,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
     uint64_t* hready = adone + 1;          // [2]: a run's image is staged (3 stager warps)
     uint64_t* bfree = hready + 2;          // [2]: the MMAs reading a run's image are complete
     uint64_t* ubar = bfree + 2;            // the 4 epilogue warps at a down unit's end
+    uint64_t* imb = ubar + 1;              // the tokens' operand images have arrived
     SlotTable* tb = reinterpret_cast<SlotTable*>(smem + off_tbl);
     RouteSmem* rs = reinterpret_cast<RouteSmem*>(smem + off_route);
     ItemMeta* meta = reinterpret_cast<ItemMeta*>(smem + off_meta);
@@ -686,6 +689,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             mbar_init(&bfree[b], 1);
         }
         mbar_init(ubar, 4);
+        mbar_init(imb, 1);
         abort_flag = 0;
         stale = 0;
         routed = 0;
@@ -712,6 +716,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
         int n = 0, st = 0;
         uint32_t round = 0;
         bool ok = true, waited = false;
+        const uint64_t stream_policy = l2_evict_first_policy();  // weights are read once per step
         auto wait_table = [&]() {
             if (!waited) {
                 ok = mbar_wait_warp(table_ready, 0, &abort_flag, fail) && routed;
@@ -730,7 +735,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                 meta[st].phase = phase;
                 meta[st].run = run;
                 mbar_arrive_expect_tx(&full[st], bytes);
-                bulk_g2s(stages + (size_t)st * stage_bytes, src, bytes, &full[st]);
+                bulk_g2s_hint(stages + (size_t)st * stage_bytes, src, bytes, &full[st], stream_policy);
                 unsigned long long* tr = trace_rec(a, phase, n);
                 if (tr) tr[4] = global_timer_ns();
             }
@@ -799,9 +804,8 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
         __syncwarp();
     } else {
         // ---------------- warps 0-7: route; then MMA (0), stagers (1-3), epilogue (4-7) ----------------
-        const bool ok_route =
-            cta_route(a, xd, xb, xsig, reinterpret_cast<float*>(stages + (size_t)(nst - 1) * stage_bytes), inb,
-                      &abort_flag, fail, rs, tb, cs, &stale, tid, ev);
+        float* part = reinterpret_cast<float*>(stages + (size_t)(nst - 1) * stage_bytes);
+        const bool ok_route = cta_route(a, xd, xb, xsig, part, inb, imb, &abort_flag, fail, rs, tb, cs, &stale, tid, ev);
         if (tid == 0) {
             if (ok_route) {
                 // the routed units, balanced against each CTA's shared share
@@ -828,6 +832,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             const int nk8 = w13_items(a.H, true), nk16 = w13_items(a.H, false);
             bool ok = routed != 0, b_started = false;
             int cur = 0, b = 0;
+            if (ok && !mbar_wait_warp(imb, 0, &abort_flag, fail)) ok = false;  // the tokens' operand images
             for (int n = 0; ok; ++n) {
                 const int st = n % nst;
                 const uint64_t t_wait = a.trace ? global_timer_ns() : 0;
@@ -1189,22 +1194,19 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
 // ======================================================================================
 static size_t up(size_t v, size_t a) { return (v + a - 1) / a * a; }
 
-// Launch with programmatic dependent launch allowed; `cooperative` adds the guarantee that every
-// CTA of the grid is resident at once (the launch fails instead of running a grid that does not fit).
-static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args,
-                              bool cooperative = false) {
+// Launch with programmatic dependent launch allowed (the grid may start before the previous
+// kernel of the stream has finished; it waits for it with griddepcontrol.wait).
+static cudaError_t launch_pdl(const void* fn, dim3 grid, dim3 block, size_t smem, cudaStream_t st, void** args) {
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = grid;
     cfg.blockDim = block;
     cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
-    cudaLaunchAttribute attr[2];
+    cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[0].val.programmaticStreamSerializationAllowed = 1;
-    attr[1].id = cudaLaunchAttributeCooperative;
-    attr[1].val.cooperative = 1;
     cfg.attrs = attr;
-    cfg.numAttrs = cooperative ? 2 : 1;
+    cfg.numAttrs = 1;
     return cudaLaunchKernelExC(&cfg, fn, args);
 }
 
@@ -1257,8 +1259,12 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
     const void* k = reinterpret_cast<const void*>(decode_experts_kernel);
     err = ensure_smem_optin(k, smem);
     if (err != cudaSuccess) return err;
-    // the CTAs wait on each other's units: one per SM must fit, and the launch is cooperative so
-    // that the grid never runs partly behind another stream's kernels
+    // the CTAs wait on each other's units, so all of them must be resident at once: one per SM
+    // must fit (refused otherwise). The launch is not cooperative: a cooperative grid waits for
+    // the router kernel to finish before any CTA starts, where a programmatic dependent launch
+    // lets every CTA start on the SM the previous layer's CTA leaves, route-independent shared
+    // weights streaming while the router runs. A kernel of another stream that holds SMs can
+    // keep CTAs out; the bounded waits then end the call with NaN and a status, never a hang.
     int per_sm = 0;
     err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, k, kThreads, smem);
     if (err != cudaSuccess) return err;
@@ -1267,7 +1273,7 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
                      (uint32_t)off_sig, (uint32_t)off_hsig, (uint32_t)off_img, (uint32_t)off_stages};
     uint32_t sb = stage_bytes;
     void* args[] = {&a, &nst, &sb, &o[0], &o[1], &o[2], &o[3], &o[4], &o[5], &o[6], &o[7], &o[8]};
-    err = launch_pdl(k, dim3(sms), dim3(kThreads), smem, st, args, true);
+    err = launch_pdl(k, dim3(sms), dim3(kThreads), smem, st, args);
     if (err != cudaSuccess) return err;
     return cudaGetLastError();
 }

@@ -18,7 +18,8 @@
 // and one of its threads issues tcgen05.mma (M=128, N=256, K=16 per instruction) into one of
 // two TMEM accumulators; warps 2-5 drain the other accumulator (tcgen05.ld), so the epilogue
 // of one tile overlaps the MMAs of the next. Rows of a tile past its group's end are computed
-// and discarded. No cluster multicast is used anywhere.
+// and discarded. No TMA or bulk load uses cluster multicast (each CTA loads its own tiles); the
+// CTA-pair GEMM's MMA-completion commit signals both CTAs' mbarriers with one multicast arrival.
 #include <cuda.h>
 #include <cudaTypedefs.h>
 

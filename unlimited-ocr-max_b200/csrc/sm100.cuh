@@ -103,6 +103,21 @@ UOCR_DEV void bulk_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar
         : "memory");
 }
 
+// The same with an L2 cache policy (createpolicy): streamed weights marked evict-first leave the
+// L2 to the small data every step re-reads (activations, scratch rows, counters, kernel code).
+UOCR_DEV uint64_t l2_evict_first_policy() {
+    uint64_t p;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+    return p;
+}
+UOCR_DEV void bulk_g2s_hint(void* dst, const void* src, uint32_t bytes, uint64_t* bar, uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, [%3], %4;" ::"r"(
+            smem_addr(dst)),
+        "l"(src), "r"(bytes), "r"(smem_addr(bar)), "l"(policy)
+        : "memory");
+}
+
 // ---- explicit shared-memory loads (32-bit shared addresses) --------------------------------
 // The hot loops read their stages through these so every access is an LDS, never a generic load.
 UOCR_DEV uint32_t lds_u32(uint32_t a) {
