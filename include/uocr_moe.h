@@ -289,8 +289,9 @@ UOCR_API int uocr_moe_decode_noalloc_status(uocr_stream_t stream);
 
 /* Diagnostics: record a per-CTA timeline of the work items of subsequent uocr_moe_decode
  * launches into `device_buffer` (zero-filled by the caller; per CTA two halves, gate/up items then
- * down items, per item 8 words: MMA warp wait start, data ready, MMAs issued, slot/rows, producer
- * issue time, all in global-timer ns; the last records of each half hold kernel-level events).
+ * down items, per item 8 words: MMA warp wait start, data ready, MMAs issued and committed,
+ * slot/rows, producer issue time, accumulator acquired (int8 items), MMAs issued, all in
+ * global-timer ns; the last records of each half hold kernel-level events).
  * NULL turns recording off. Not thread-safe; for profiling only. No counterpart in the
  * reference (its profiler is server-level). */
 UOCR_API int uocr_moe_decode_set_trace(void* device_buffer, size_t bytes);

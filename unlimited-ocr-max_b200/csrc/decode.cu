@@ -106,8 +106,9 @@ UOCR_DEV void load_shared_slots(SlotTable* tb, const DecodeArgs& a, int tid, int
     if (tid == 0) tb->nslot = a.S;
 }
 
-// Diagnostics timeline: per CTA `items` records of 8 words (global-timer ns); item n of K2 / K3:
-// {MMA warp wait start, data ready, MMAs issued, slot<<32|rb<<16|ki, producer issue, 0, 0, 0}.
+// Diagnostics timeline: per CTA `items` records of 8 words (global-timer ns); item n of the gate/up
+// (half 0) or down (half 1) phase: {MMA warp wait start, data ready, MMAs issued and committed,
+// slot<<32|rb<<16|ki, producer issue, accumulator acquired (int8), MMAs issued, 0}.
 UOCR_DEV unsigned long long* trace_rec(const DecodeArgs& a, int half, int n) {
     if (!a.trace || n >= a.trace_items / 2) return nullptr;
     return a.trace + ((size_t)blockIdx.x * a.trace_items + (size_t)half * (a.trace_items / 2) + n) * 8;
@@ -860,6 +861,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                             ok = false;
                             break;
                         }
+                        if (tr && lane == 0) tr[5] = global_timer_ns();
                         acc_scales(pipe, j, 0, scl, nullptr, lane);
                         acc_scales(pipe, j, 1, scl + kRowBlock, nullptr, lane);
                         publish_acc(pipe, j, lane);
@@ -916,6 +918,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                             ok = false;
                             break;
                         }
+                        if (tr && lane == 0) tr[5] = global_timer_ns();
                         const float* scl = reinterpret_cast<const float*>(item + at * kAtomBytes);
                         for (int g = 0; g < at; ++g) {
                             float sig[kMaxB];
@@ -954,6 +957,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                     }
                 }
                 __syncwarp();
+                if (tr && lane == 0) tr[6] = global_timer_ns();
                 if (lane == 0) umma_commit(&empty[st]);  // the stage is free once these MMAs complete
                 if (tr && lane == 0) {
                     tr[2] = global_timer_ns();
