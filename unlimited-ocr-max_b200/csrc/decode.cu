@@ -53,7 +53,8 @@ constexpr uint32_t kBarConsumers = 1;        // named barrier of warps 0-7
 constexpr int kAccSlots = 4;                 // TMEM accumulators of 64 columns
 constexpr uint32_t kAccCols = 64;
 constexpr uint32_t kTmemCols = kAccSlots * kAccCols;
-constexpr int kDigitAtomBytes = 32 * 128;    // int8 B operand atom: 3 digit planes x 8 tokens + 8 pad rows
+constexpr int kDigitAtomBytes = 24 * 128;    // int8 B operand group: 3 digit planes x 8 tokens (24 rows)
+constexpr int kDigitPadBytes = 8 * 128;      // an N = 32 MMA reads 8 rows past a group (ignored columns)
 constexpr int kTermAtomBytes = 16 * 128;     // bf16 B operand atom: 2 terms x 8 tokens
 constexpr uint32_t kIdescS8 = umma_idesc_s8(128, 32);
 constexpr uint32_t kIdescBf16 = umma_idesc_bf16(128, 16);
@@ -65,8 +66,6 @@ struct SlotTable {
     int expert[kMaxSlotsSm];
     int count[kMaxSlotsSm];
     int base[kMaxSlotsSm];
-    int token[kMaxSlotsSm][kMaxB];
-    float weight[kMaxSlotsSm][kMaxB];
     signed char pos[kMaxSlotsSm][kMaxB];  // pos[slot][t]: entry of token t in the slot, -1 if none
 };
 
@@ -76,7 +75,8 @@ struct ItemMeta {
     int ki;     // item (K range) within the row block
     int phase;  // 0: gate/up, 1: down
     int run;    // down: the slot run this item starts (its operand image), -1 for none
-    int pad[3];
+    int grp;    // accumulator group: an int8 item, or a bf16 unit's items (MMA warp grp % 2 issues it)
+    int pad[2];
 };
 
 // One TMEM accumulator's description, written by the MMA warp, read by the epilogue. An
@@ -98,8 +98,6 @@ UOCR_DEV void load_shared_slots(SlotTable* tb, const DecodeArgs& a, int tid, int
         tb->count[s] = a.B;
         tb->base[s] = s * a.B;
         for (int t = 0; t < kMaxB; ++t) {
-            tb->token[s][t] = t;
-            tb->weight[s][t] = 1.0f;
             tb->pos[s][t] = t < a.B ? (signed char)t : (signed char)-1;
         }
     }
@@ -132,7 +130,9 @@ UOCR_DEV float group_digits(float4 v, uint32_t (&w)[3]) {
     for (int q = 0; q < 3; ++q) w[q] = pack_s8x4(d[0][q], d[1][q], d[2][q], d[3][q]);
     return sg;
 }
-// int8 operand image [group][32 rows][128 B] (swizzled): digit plane p of column t is row 8p + t.
+// int8 operand image [group][24 rows][128 B] (swizzled, groups 3 KB apart): digit plane p of column t
+// is row 8p + t. The N = 32 MMA of a group also reads the next 8 rows (the next group's, or padding
+// after the last): their accumulator columns 24-31 are never read.
 // Lane L's words of group g, column t.
 UOCR_DEV void put_digits(unsigned char* img, int g, int t, int lane, const uint32_t (&w)[3]) {
 #pragma unroll
@@ -206,7 +206,8 @@ UOCR_DEV bool cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* x
     if (*stale) return false;
     if (warp == 0) {
         const uint32_t pbytes = (uint32_t)B * 64 * 8 * 4, img = (uint32_t)H * 32;
-        const uint32_t dbytes = a.int8 ? img : 0u, sbytes = a.int8 ? 8u * (H / 128) * 4 : 0u;
+        const uint32_t dbytes = a.int8 ? (uint32_t)((H / 128) * kDigitAtomBytes + kDigitPadBytes) : 0u;
+        const uint32_t sbytes = a.int8 ? 8u * (H / 128) * 4 : 0u;
         if (lane == 0) mbar_arrive_expect_tx(inb, pbytes + sbytes);
         if (lane == 1) mbar_arrive_expect_tx(imb, dbytes + img);
         __syncwarp();
@@ -296,8 +297,6 @@ UOCR_DEV bool cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* x
         for (unsigned long long mm = m; mm; mm &= mm - 1ull, ++n) {
             const int q = __ffsll((long long)mm) - 1, t = q / k;
             tb->pos[row][t] = (signed char)n;
-            tb->token[row][n] = t;
-            tb->weight[row][n] = rs->wts[q];
             rs->rowof[q] = base + n;
         }
     }
@@ -439,7 +438,6 @@ decode_logits_kernel(DecodeArgs a) {
             const float sg = group_digits(v, w);
             if (lane == 0) a.xsig[t * NG + g] = sg;
             put_digits(a.xd, g, t, lane, w);
-            *reinterpret_cast<uint32_t*>(a.xd + (size_t)g * kDigitAtomBytes + atom_offset(24 + t, 4 * lane)) = 0u;
         }
     }
     if (ev && lane == 0) ev[2] = global_timer_ns();
@@ -454,7 +452,6 @@ struct Pipe {
     uint64_t* tfree;   // [kAccSlots]: the 4 epilogue warps have read the accumulator
     AccMeta* acc;      // [kAccSlots]
     uint32_t tmem;     // TMEM base (kTmemCols columns)
-    int c;             // accumulators handed out (MMA warp)
     volatile int* abort_flag;
     uint32_t* status;
 };
@@ -462,9 +459,9 @@ struct Pipe {
 // MMA warp: take the next accumulator slot (waiting until the epilogue has read it) and write
 // its description; returns its index, or -1 on a timeout. publish_acc makes the description
 // visible (the first of tfull's two arrivals; the MMAs' commit is the second).
-UOCR_DEV int acquire_acc(Pipe& p, int slot, int rb, int gi, int flags, int lane) {
-    const int j = p.c % kAccSlots;
-    if (p.c >= kAccSlots && !mbar_wait_warp(&p.tfree[j], ((p.c / kAccSlots) - 1) & 1, p.abort_flag, p.status))
+UOCR_DEV int acquire_acc(Pipe& p, int grp, int slot, int rb, int gi, int flags, int lane) {
+    const int j = grp % kAccSlots;
+    if (grp >= kAccSlots && !mbar_wait_warp(&p.tfree[j], ((grp / kAccSlots) - 1) & 1, p.abort_flag, p.status))
         return -1;
     AccMeta& m = p.acc[j];
     if (lane == 0) {
@@ -474,7 +471,6 @@ UOCR_DEV int acquire_acc(Pipe& p, int slot, int rb, int gi, int flags, int lane)
         m.flags = flags;
     }
     tc_fence_after();  // the epilogue's TMEM reads precede this warp's next MMAs
-    ++p.c;
     return j;
 }
 // int8 scales of one group into the description: 128 row scales (one float4 per lane) and,
@@ -675,7 +671,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
     if (tid == 0) {
         for (int s = 0; s < nst; ++s) {
             mbar_init(&full[s], 1);
-            mbar_init(&empty[s], 1);
+            mbar_init(&empty[s], 2);  // the issuing MMA warp's commit + the other MMA warp's arrival
         }
         mbar_init(table_ready, 1);
         mbar_init(inb, 1);
@@ -683,11 +679,11 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             mbar_init(&tfull[j], 2);
             mbar_init(&tfree[j], 4);
         }
-        mbar_init(mdone, 1);
-        mbar_init(adone, 1);
+        mbar_init(mdone, 2);  // both MMA warps' commits
+        mbar_init(adone, 2);
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&hready[b], 3);
-            mbar_init(&bfree[b], 1);
+            mbar_init(&hready[b], 2);  // the 2 stager warps
+            mbar_init(&bfree[b], 2);   // both MMA warps' commits
         }
         mbar_init(ubar, 4);
         mbar_init(imb, 1);
@@ -710,7 +706,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    Pipe pipe{tfull, tfree, accm, tmem_base, 0, &abort_flag, fail};
+    Pipe pipe{tfull, tfree, accm, tmem_base, &abort_flag, fail};
 
     if (warp == 8) {
         // ---------------- producer: one bulk copy per item into the stage ring ----------------
@@ -724,7 +720,9 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                 waited = true;
             }
         };
-        auto issue = [&](const unsigned char* src, uint32_t bytes, int slot, int rb, int ki, int phase, int run) {
+        int grp = 0;  // accumulator groups handed out
+        auto issue = [&](const unsigned char* src, uint32_t bytes, int slot, int rb, int ki, int phase, int run,
+                         bool new_grp) {
             // the last stage holds the routing's logit partials until the table is ready
             if (round == 0 && st == nst - 1) wait_table();
             if (ok && round > 0 && !mbar_wait_warp(&empty[st], (round - 1) & 1, &abort_flag, fail)) ok = false;
@@ -735,12 +733,14 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                 meta[st].ki = ki;
                 meta[st].phase = phase;
                 meta[st].run = run;
+                meta[st].grp = new_grp ? grp : grp - 1;
                 mbar_arrive_expect_tx(&full[st], bytes);
                 bulk_g2s_hint(stages + (size_t)st * stage_bytes, src, bytes, &full[st], stream_policy);
                 unsigned long long* tr = trace_rec(a, phase, n);
                 if (tr) tr[4] = global_timer_ns();
             }
             __syncwarp();
+            if (new_grp) ++grp;
             ++n;
             if (++st == nst) {
                 st = 0;
@@ -757,7 +757,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                                  (size_t)tb->expert[slot] * w13_expert_bytes(a.I, a.H, i8);
             const int nk = w13_items(a.H, i8);
             for (int ki = 0; ki < nk && ok; ++ki)
-                issue(base + ((size_t)rb * nk + ki) * bytes, bytes, slot, rb, ki, 0, -1);
+                issue(base + ((size_t)rb * nk + ki) * bytes, bytes, slot, rb, ki, 0, -1, i8 || ki == 0);
         };
         const int ns_a = units.a_s1 - units.a_s0;
         for (int i = 0; i < ns_a && ok; ++i) {  // shared units: streamed while routing
@@ -788,7 +788,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                 const int nk = w2_items(a.I, i8);
                 for (int ki = 0; ki < nk && ok; ++ki)
                     issue(base + w2_item_offset(i8, ki), (uint32_t)item_bytes(w2_item_atoms(a.I, i8, ki), i8), slot,
-                          rb, ki, 1, ki == 0 ? run : -1);
+                          rb, ki, 1, ki == 0 ? run : -1, i8 || ki == 0);
             }
         }
         if (lane == 0) {
@@ -796,7 +796,8 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                 abort_flag = 1;
                 for (int q = max(0, n - nst); q < n; ++q) mbar_wait(&full[q % nst], (q / nst) & 1, nullptr);
             } else if (round == 0 || mbar_wait(&empty[st], (round - 1) & 1, fail)) {
-                meta[st].slot = -1;  // end marker
+                meta[st].slot = -1;  // end marker, published as accumulator group `grp`
+                meta[st].grp = grp;
                 mbar_arrive(&full[st]);
             } else {
                 abort_flag = 1;
@@ -827,8 +828,9 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
         }
         named_bar_sync(kBarConsumers, kCW * 32);
         if (ev && tid == 0) ev[2] = global_timer_ns();
-        if (warp == 0) {
-            // ---------------- MMA warp ----------------
+        if (warp <= 1) {
+            // ---------------- MMA warps: warp w issues the accumulator groups g with g % 2 == w ----------------
+            // Both walk every stage in order (the owner's commit and the other's arrival free it).
             const uint32_t xd_s = smem_addr(xd), xb_s = smem_addr(xb), hb_s = smem_addr(hb);
             const int nk8 = w13_items(a.H, true), nk16 = w13_items(a.H, false);
             bool ok = routed != 0, b_started = false;
@@ -841,9 +843,40 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                     ok = false;
                     break;
                 }
-                const int slot = meta[st].slot;
-                if (slot < 0) break;
+                const int slot = meta[st].slot, grp = meta[st].grp;
+                if (slot < 0) {
+                    if ((grp & 1) == warp) {  // the end marker's accumulator group is this warp's
+                        const int j = acquire_acc(pipe, grp, -1, 0, 0, 0, lane);
+                        if (j >= 0) {
+                            publish_acc(pipe, j, lane);
+                            if (lane == 0) mbar_arrive(&tfull[j]);
+                        } else {
+                            ok = false;
+                        }
+                    }
+                    break;
+                }
                 const int rb = meta[st].rb, ki = meta[st].ki, phase = meta[st].phase, run = meta[st].run;
+                if (phase == 1) {
+                    if (!b_started) {  // the image region may be restaged once every gate/up MMA is done
+                        if (lane == 0) umma_commit(adone);
+                        b_started = true;
+                    }
+                    if (run >= 0) {
+                        // a run starts: the previous run's image is free once its MMAs complete
+                        if (run > 0 && lane == 0) umma_commit(&bfree[(run - 1) & 1]);
+                        b = run & 1;
+                        if (!mbar_wait_warp(&hready[b], (run >> 1) & 1, &abort_flag, fail)) {
+                            ok = false;
+                            break;
+                        }
+                    }
+                }
+                if ((grp & 1) != warp) {  // the other MMA warp's item: done with the stage's description
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&empty[st]);
+                    continue;
+                }
                 unsigned long long* tr = a.trace ? trace_rec(a, phase, n) : nullptr;
                 if (tr && lane == 0) {
                     tr[0] = t_wait;
@@ -856,7 +889,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                     if (i8) {
                         // both groups of the item in one accumulator (columns 0-31, 32-63)
                         const float* scl = reinterpret_cast<const float*>(item + 2 * kAtomBytes);
-                        const int j = acquire_acc(pipe, slot, rb, 2 * ki, 1 | 4 | (ki == nk8 - 1 ? 2 : 0), lane);
+                        const int j = acquire_acc(pipe, grp, slot, rb, 2 * ki, 1 | 4 | (ki == nk8 - 1 ? 2 : 0), lane);
                         if (j < 0) {
                             ok = false;
                             break;
@@ -876,7 +909,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                         }
                     } else {
                         if (ki == 0) {
-                            cur = acquire_acc(pipe, slot, rb, 0, 2, lane);
+                            cur = acquire_acc(pipe, grp, slot, rb, 0, 2, lane);
                             if (cur < 0) {
                                 ok = false;
                                 break;
@@ -895,24 +928,11 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                         }
                     }
                 } else {
-                    if (!b_started) {  // the image region may be restaged once every gate/up MMA is done
-                        if (lane == 0) umma_commit(adone);
-                        b_started = true;
-                    }
-                    if (run >= 0) {
-                        // a run starts: the previous run's image is free once its MMAs complete
-                        if (run > 0 && lane == 0) umma_commit(&bfree[(run - 1) & 1]);
-                        b = run & 1;
-                        if (!mbar_wait_warp(&hready[b], (run >> 1) & 1, &abort_flag, fail)) {
-                            ok = false;
-                            break;
-                        }
-                    }
                     const int nk = w2_items(a.I, i8);
                     const uint32_t img_s = hb_s + (uint32_t)b * img_bytes;
                     if (i8) {
                         const int at = w2_item_atoms(a.I, true, ki);
-                        const int j = acquire_acc(pipe, slot, rb, 2 * ki,
+                        const int j = acquire_acc(pipe, grp, slot, rb, 2 * ki,
                                                   8 | 1 | (at == 2 ? 4 : 0) | (ki == nk - 1 ? 2 : 0), lane);
                         if (j < 0) {
                             ok = false;
@@ -937,7 +957,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                         }
                     } else {
                         if (ki == 0) {
-                            cur = acquire_acc(pipe, slot, rb, 0, 8 | 2, lane);
+                            cur = acquire_acc(pipe, grp, slot, rb, 0, 8 | 2, lane);
                             if (cur < 0) {
                                 ok = false;
                                 break;
@@ -965,15 +985,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                 }
                 __syncwarp();
             }
-            if (ok) {
-                const int j = acquire_acc(pipe, -1, 0, 0, 0, lane);  // end marker
-                if (j >= 0) {
-                    publish_acc(pipe, j, lane);
-                    if (lane == 0) mbar_arrive(&tfull[j]);
-                }
-            } else if (lane == 0) {
-                abort_flag = 1;
-            }
+            if (!ok && lane == 0) abort_flag = 1;
             if (lane == 0) {
                 if (!b_started) umma_commit(adone);
                 umma_commit(mdone);  // every MMA complete before TMEM is released
@@ -983,8 +995,8 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             if (ev && lane == 0) ev[3] = global_timer_ns();
         } else if (warp <= 3) {
             // ---------------- stagers: each slot run's h rows -> its operand image ----------------
-            // runs in the producer's order; run r uses image r % 2; hready completes after 3 arrivals
-            const int rank = warp - 1;
+            // runs in the producer's order; run r uses image r % 2; hready completes after 2 arrivals
+            const int rank = warp - 2;
             unsigned long long* sv = a.trace ? trace_rec(a, 1, a.trace_items / 2 - 3) : nullptr;
             int r = 0, prev = -1;
             bool ok = routed != 0;
@@ -1011,11 +1023,11 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                 const bool i8 = slot >= a.S && a.int8;
                 unsigned char* img = hb + (size_t)b * img_bytes;
                 const int ntask = cnt * NG3;
-                for (int t0 = rank; t0 < ntask; t0 += 4 * 3) {
+                for (int t0 = rank; t0 < ntask; t0 += 4 * 2) {
                     float4 v[4];  // four tasks' loads issued before any of their stores
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        const int task = t0 + u * 3;
+                        const int task = t0 + u * 2;
                         if (task < ntask) {
                             const int e = task / NG3, g = task - e * NG3;
                             v[u] = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)(base + e) * a.I + 128 * g + 4 * lane));
@@ -1023,7 +1035,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                     }
 #pragma unroll
                     for (int u = 0; u < 4; ++u) {
-                        const int task = t0 + u * 3;
+                        const int task = t0 + u * 2;
                         if (task < ntask) {
                             const int e = task / NG3, g = task - e * NG3;
                             if (i8) {
@@ -1255,7 +1267,10 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
     const size_t off_sig = off_cs + up(sizeof(CombineSmem), 128);
     const size_t off_hsig = off_sig + up(sizeof(float) * kMaxB * (a.H / 128), 128);
     const size_t off_img = up(off_hsig + sizeof(float) * 2 * kMaxB * (a.I / 128), 1024);
-    const size_t img = std::max((size_t)a.H * 32 * (a.int8 ? 2 : 1), (size_t)2 * a.I * 32);
+    // phase A: the bf16 terms image, then the int8 digits image; phase B: two run images (bf16 runs
+    // need I * 32 bytes, int8 runs I * 24 + 1 KB)
+    const size_t img = std::max((size_t)a.H * 32 + (a.int8 ? (size_t)(a.H / 128) * kDigitAtomBytes + kDigitPadBytes : 0),
+                                (size_t)2 * a.I * 32);
     const size_t off_stages = up(off_img + img, 1024);
     if ((size_t)max_smem < off_stages + 2 * (size_t)stage_bytes) return cudaErrorInvalidConfiguration;
     int nst = (int)std::min<size_t>(8, ((size_t)max_smem - off_stages) / stage_bytes);
