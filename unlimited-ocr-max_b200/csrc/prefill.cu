@@ -69,6 +69,7 @@ __global__ void __launch_bounds__(64) prefill_scan_kernel(const int* __restrict_
                                                           int S, int T, int topk, int* __restrict__ chunk_base,
                                                           PrefillPlan* __restrict__ plan1,
                                                           PrefillPlan* __restrict__ plan2, int* __restrict__ n_valid) {
+    // n_valid[0]: routed entries with an expert; n_valid[32 + e]: entries of expert e
     __shared__ int total[64];
     __shared__ int base[65];
     const int e = threadIdx.x;
@@ -76,6 +77,7 @@ __global__ void __launch_bounds__(64) prefill_scan_kernel(const int* __restrict_
     if (e < E)
         for (int c = 0; c < nchunks; ++c) sum += chunk_counts[c * 64 + e];
     total[e] = e < E ? sum : 0;
+    n_valid[32 + e] = total[e];
     __syncthreads();
     if (e == 0) {
         int acc = 0;
@@ -168,52 +170,74 @@ __global__ void __launch_bounds__(256) prefill_gather_kernel(const float* __rest
         return;
     }
     const float* src = x + (size_t)t * H;
-    for (int k = lane * 8; k < H; k += 256) {
-        const float4 a = *reinterpret_cast<const float4*>(src + k);
-        const float4 b = *reinterpret_cast<const float4*>(src + k + 4);
-        uint4 o;
-        o.x = (uint32_t)f32_to_bf16_rne(a.x) | ((uint32_t)f32_to_bf16_rne(a.y) << 16);
-        o.y = (uint32_t)f32_to_bf16_rne(a.z) | ((uint32_t)f32_to_bf16_rne(a.w) << 16);
-        o.z = (uint32_t)f32_to_bf16_rne(b.x) | ((uint32_t)f32_to_bf16_rne(b.y) << 16);
-        o.w = (uint32_t)f32_to_bf16_rne(b.z) | ((uint32_t)f32_to_bf16_rne(b.w) << 16);
-        *reinterpret_cast<uint4*>(dst + k) = o;
+    for (int k0 = lane * 8; k0 < H; k0 += 4 * 256) {
+        float4 a[4], b[4];  // up to four 8-element steps per lane, loads issued before the stores
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int k = k0 + u * 256;
+            if (k < H) {
+                a[u] = *reinterpret_cast<const float4*>(src + k);
+                b[u] = *reinterpret_cast<const float4*>(src + k + 4);
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int k = k0 + u * 256;
+            if (k < H) {
+                uint4 o;
+                o.x = (uint32_t)f32_to_bf16_rne(a[u].x) | ((uint32_t)f32_to_bf16_rne(a[u].y) << 16);
+                o.y = (uint32_t)f32_to_bf16_rne(a[u].z) | ((uint32_t)f32_to_bf16_rne(a[u].w) << 16);
+                o.z = (uint32_t)f32_to_bf16_rne(b[u].x) | ((uint32_t)f32_to_bf16_rne(b[u].y) << 16);
+                o.w = (uint32_t)f32_to_bf16_rne(b[u].z) | ((uint32_t)f32_to_bf16_rne(b[u].w) << 16);
+                *reinterpret_cast<uint4*>(dst + k) = o;
+            }
+        }
     }
 }
 
 // int8 items (layout.h) -> the bf16 row-block layout [row block][K / 64 atoms][128 rows][128 B]:
 // each bf16 element is bf16_rne(f32(q) * scale), int8_dequant_expert's bits
-// (kernels/moe_int8.mojo:330-340). Thread: 16 elements of one row (one 16-byte int8 chunk ->
-// two 16-byte bf16 chunks). `atoms` int8 atoms per item (w13: 2, w2: 1).
+// (kernels/moe_int8.mojo:330-340). Thread: one 128-byte bf16 atom row, 64 elements of one weight
+// row (four 16-byte int8 loads issued first, then eight 16-byte stores). `atoms` int8 atoms per
+// item (w13: 2, w2: 2, the last item of a row block possibly 1). Row blocks of experts that
+// received no rows (`expert_rows`, from the scan) are skipped: their bf16 copy is never read.
 __global__ void __launch_bounds__(256) prefill_dequant_kernel(const unsigned char* __restrict__ w, long nrb, int K,
-                                                              int atoms, unsigned char* __restrict__ out) {
+                                                              int atoms, int rb_per_expert,
+                                                              const int* __restrict__ expert_rows,
+                                                              unsigned char* __restrict__ out) {
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    const long per_rb = (long)kRowBlock * (K / 16);
+    const long per_rb = (long)kRowBlock * (K / 64);
     if (i >= nrb * per_rb) return;
     const long rb = i / per_rb;
-    const int rem = (int)(i - rb * per_rb), r = rem / (K / 16), k = 16 * (rem - r * (K / 16));
+    if (expert_rows[rb / rb_per_expert] == 0) return;
+    const int rem = (int)(i - rb * per_rb), r = rem / (K / 64), k = 64 * (rem - r * (K / 64));
     // items of `atoms` atoms of 128 elements, the last one possibly shorter (layout.h)
     const int ik = atoms * 128, ki = k / ik, a = (k % ik) / 128, c = k % 128;
     const int nitems = (K / 128 + atoms - 1) / atoms, left = K / 128 - ki * atoms;
     const int here = left < atoms ? left : atoms;  // atoms of this item
     const size_t rb_bytes = (size_t)(nitems - 1) * item_bytes(atoms, true) + item_bytes((K / 128) - (nitems - 1) * atoms, true);
     const unsigned char* item = w + (size_t)rb * rb_bytes + (size_t)ki * item_bytes(atoms, true);
-    const uint4 v = *reinterpret_cast<const uint4*>(item + (size_t)a * kAtomBytes + atom_offset(r, c));
-    const float sc = reinterpret_cast<const float*>(item + (size_t)here * kAtomBytes)[a * kRowBlock + r];
-    float f0[8], f1[8];
-    unpack_s8x8(v.x, v.y, f0);
-    unpack_s8x8(v.z, v.w, f1);
-    uint32_t o[8];
+    uint4 v[4];
 #pragma unroll
-    for (int q = 0; q < 4; ++q) {
-        o[q] = (uint32_t)f32_to_bf16_rne(__fmul_rn(f0[2 * q], sc)) |
-               ((uint32_t)f32_to_bf16_rne(__fmul_rn(f0[2 * q + 1], sc)) << 16);
-        o[4 + q] = (uint32_t)f32_to_bf16_rne(__fmul_rn(f1[2 * q], sc)) |
-                   ((uint32_t)f32_to_bf16_rne(__fmul_rn(f1[2 * q + 1], sc)) << 16);
-    }
+    for (int j = 0; j < 4; ++j) v[j] = *reinterpret_cast<const uint4*>(item + (size_t)a * kAtomBytes + atom_offset(r, c + 16 * j));
+    const float sc = reinterpret_cast<const float*>(item + (size_t)here * kAtomBytes)[a * kRowBlock + r];
     unsigned char* dst = out + ((size_t)rb * (K / 64) + k / 64) * kAtomBytes;
-    const int c2 = (k % 64) * 2;
-    *reinterpret_cast<uint4*>(dst + atom_offset(r, c2)) = make_uint4(o[0], o[1], o[2], o[3]);
-    *reinterpret_cast<uint4*>(dst + atom_offset(r, c2 + 16)) = make_uint4(o[4], o[5], o[6], o[7]);
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        float f0[8], f1[8];
+        unpack_s8x8(v[j].x, v[j].y, f0);
+        unpack_s8x8(v[j].z, v[j].w, f1);
+        uint32_t o[8];
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+            o[q] = (uint32_t)f32_to_bf16_rne(__fmul_rn(f0[2 * q], sc)) |
+                   ((uint32_t)f32_to_bf16_rne(__fmul_rn(f0[2 * q + 1], sc)) << 16);
+            o[4 + q] = (uint32_t)f32_to_bf16_rne(__fmul_rn(f1[2 * q], sc)) |
+                       ((uint32_t)f32_to_bf16_rne(__fmul_rn(f1[2 * q + 1], sc)) << 16);
+        }
+        *reinterpret_cast<uint4*>(dst + atom_offset(r, 32 * j)) = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(dst + atom_offset(r, 32 * j + 16)) = make_uint4(o[4], o[5], o[6], o[7]);
+    }
 }
 
 // out[t][j] (+)= sum_s w[t,s] * y[dest[t*k+s]][j] (entries without an expert skipped)
@@ -872,7 +896,7 @@ PrefillLayout prefill_layout(int T, int H, int I, int E, int S, int topk, bool i
     const size_t nchunks = (kT + kChunk - 1) / kChunk;
     size_t off = 0;
     d.status = off; off += kCtlClearBytes;  // status region (cleared whole after a failure)
-    d.n_valid = off; off += 128;
+    d.n_valid = off; off += 512;  // the valid-row count, then per-expert rows (from byte 128)
     d.ids = off; off += al(sizeof(int32_t) * kT);
     d.wts = off; off += al(sizeof(float) * kT);
     d.chunk_counts = off; off += al(sizeof(int) * (nchunks ? nchunks : 1) * 64);
@@ -935,11 +959,11 @@ cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& 
         unsigned char* w13d = reinterpret_cast<unsigned char*>(ws + d.w13);
         unsigned char* w2d = reinterpret_cast<unsigned char*>(ws + d.w2);
         const long nrb13 = (long)E * (2 * I / kRowBlock), nrb2 = (long)E * (H / kRowBlock);
-        const long n13 = nrb13 * kRowBlock * (H / 16), n2 = nrb2 * kRowBlock * (I / 16);
+        const long n13 = nrb13 * kRowBlock * (H / 64), n2 = nrb2 * kRowBlock * (I / 64);
         prefill_dequant_kernel<<<(unsigned)((n13 + 255) / 256), 256, 0, st>>>(
-            reinterpret_cast<const unsigned char*>(a.w13), nrb13, H, w13_atoms(), w13d);
+            reinterpret_cast<const unsigned char*>(a.w13), nrb13, H, w13_atoms(), 2 * I / kRowBlock, n_valid + 32, w13d);
         prefill_dequant_kernel<<<(unsigned)((n2 + 255) / 256), 256, 0, st>>>(
-            reinterpret_cast<const unsigned char*>(a.w2), nrb2, I, kW2Atoms, w2d);
+            reinterpret_cast<const unsigned char*>(a.w2), nrb2, I, kW2Atoms, H / kRowBlock, n_valid + 32, w2d);
         w13 = w13d;
         w2 = w2d;
     }
