@@ -197,46 +197,55 @@ __global__ void __launch_bounds__(256) prefill_gather_kernel(const float* __rest
 
 // int8 items (layout.h) -> the bf16 row-block layout [row block][K / 64 atoms][128 rows][128 B]:
 // each bf16 element is bf16_rne(f32(q) * scale), int8_dequant_expert's bits
-// (kernels/moe_int8.mojo:330-340). Thread: one 128-byte bf16 atom row, 64 elements of one weight
-// row (four 16-byte int8 loads issued first, then eight 16-byte stores). `atoms` int8 atoms per
-// item (w13: 2, w2: 2, the last item of a row block possibly 1). Row blocks of experts that
-// received no rows (`expert_rows`, from the scan) are skipped: their bf16 copy is never read.
+// (kernels/moe_int8.mojo:330-340). Thread: one 16-byte int8 chunk (16 elements) of four rows r,
+// r + 32, r + 64, r + 96 (the four loads issued first; a warp's loads are whole 128-byte row
+// segments), each to two 16-byte bf16 chunks. `atoms` int8 atoms per item (the last item of a row
+// block possibly shorter). Row blocks of experts that received no rows (`expert_rows`, from the
+// scan) are skipped: their bf16 copy is never read.
 __global__ void __launch_bounds__(256) prefill_dequant_kernel(const unsigned char* __restrict__ w, long nrb, int K,
                                                               int atoms, int rb_per_expert,
                                                               const int* __restrict__ expert_rows,
                                                               unsigned char* __restrict__ out) {
     const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
-    const long per_rb = (long)kRowBlock * (K / 64);
+    const int nk16 = K / 16;
+    const long per_rb = 32L * nk16;
     if (i >= nrb * per_rb) return;
     const long rb = i / per_rb;
     if (expert_rows[rb / rb_per_expert] == 0) return;
-    const int rem = (int)(i - rb * per_rb), r = rem / (K / 64), k = 64 * (rem - r * (K / 64));
+    const int rem = (int)(i - rb * per_rb), rq = rem / nk16, k = 16 * (rem - rq * nk16);
     // items of `atoms` atoms of 128 elements, the last one possibly shorter (layout.h)
     const int ik = atoms * 128, ki = k / ik, a = (k % ik) / 128, c = k % 128;
     const int nitems = (K / 128 + atoms - 1) / atoms, left = K / 128 - ki * atoms;
     const int here = left < atoms ? left : atoms;  // atoms of this item
     const size_t rb_bytes = (size_t)(nitems - 1) * item_bytes(atoms, true) + item_bytes((K / 128) - (nitems - 1) * atoms, true);
     const unsigned char* item = w + (size_t)rb * rb_bytes + (size_t)ki * item_bytes(atoms, true);
+    const float* scl = reinterpret_cast<const float*>(item + (size_t)here * kAtomBytes) + a * kRowBlock;
     uint4 v[4];
-#pragma unroll
-    for (int j = 0; j < 4; ++j) v[j] = *reinterpret_cast<const uint4*>(item + (size_t)a * kAtomBytes + atom_offset(r, c + 16 * j));
-    const float sc = reinterpret_cast<const float*>(item + (size_t)here * kAtomBytes)[a * kRowBlock + r];
-    unsigned char* dst = out + ((size_t)rb * (K / 64) + k / 64) * kAtomBytes;
+    float sc[4];
 #pragma unroll
     for (int j = 0; j < 4; ++j) {
+        const int r = rq + 32 * j;
+        v[j] = *reinterpret_cast<const uint4*>(item + (size_t)a * kAtomBytes + atom_offset(r, c));
+        sc[j] = scl[r];
+    }
+    unsigned char* dst = out + ((size_t)rb * (K / 64) + k / 64) * kAtomBytes;
+    const int c2 = (k % 64) * 2;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const int r = rq + 32 * j;
         float f0[8], f1[8];
         unpack_s8x8(v[j].x, v[j].y, f0);
         unpack_s8x8(v[j].z, v[j].w, f1);
         uint32_t o[8];
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
-            o[q] = (uint32_t)f32_to_bf16_rne(__fmul_rn(f0[2 * q], sc)) |
-                   ((uint32_t)f32_to_bf16_rne(__fmul_rn(f0[2 * q + 1], sc)) << 16);
-            o[4 + q] = (uint32_t)f32_to_bf16_rne(__fmul_rn(f1[2 * q], sc)) |
-                       ((uint32_t)f32_to_bf16_rne(__fmul_rn(f1[2 * q + 1], sc)) << 16);
+            o[q] = (uint32_t)f32_to_bf16_rne(__fmul_rn(f0[2 * q], sc[j])) |
+                   ((uint32_t)f32_to_bf16_rne(__fmul_rn(f0[2 * q + 1], sc[j])) << 16);
+            o[4 + q] = (uint32_t)f32_to_bf16_rne(__fmul_rn(f1[2 * q], sc[j])) |
+                       ((uint32_t)f32_to_bf16_rne(__fmul_rn(f1[2 * q + 1], sc[j])) << 16);
         }
-        *reinterpret_cast<uint4*>(dst + atom_offset(r, 32 * j)) = make_uint4(o[0], o[1], o[2], o[3]);
-        *reinterpret_cast<uint4*>(dst + atom_offset(r, 32 * j + 16)) = make_uint4(o[4], o[5], o[6], o[7]);
+        *reinterpret_cast<uint4*>(dst + atom_offset(r, c2)) = make_uint4(o[0], o[1], o[2], o[3]);
+        *reinterpret_cast<uint4*>(dst + atom_offset(r, c2 + 16)) = make_uint4(o[4], o[5], o[6], o[7]);
     }
 }
 
@@ -959,7 +968,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& 
         unsigned char* w13d = reinterpret_cast<unsigned char*>(ws + d.w13);
         unsigned char* w2d = reinterpret_cast<unsigned char*>(ws + d.w2);
         const long nrb13 = (long)E * (2 * I / kRowBlock), nrb2 = (long)E * (H / kRowBlock);
-        const long n13 = nrb13 * kRowBlock * (H / 64), n2 = nrb2 * kRowBlock * (I / 64);
+        const long n13 = nrb13 * 32 * (H / 16), n2 = nrb2 * 32 * (I / 16);
         prefill_dequant_kernel<<<(unsigned)((n13 + 255) / 256), 256, 0, st>>>(
             reinterpret_cast<const unsigned char*>(a.w13), nrb13, H, w13_atoms(), 2 * I / kRowBlock, n_valid + 32, w13d);
         prefill_dequant_kernel<<<(unsigned)((n2 + 255) / 256), 256, 0, st>>>(
