@@ -1,27 +1,30 @@
 // Decode-step MoE sublayer (MoE.decode_rows, unlimited_ocr_max/decoder.py:641-655) for B <= 8
-// tokens: three kernels chained by programmatic dependent launch (PDL); K2 and K3 are persistent
-// (one CTA per SM) and stream their weights from HBM once, through the tcgen05 tensor cores.
+// tokens: two kernels chained by programmatic dependent launch (PDL). The experts kernel is
+// persistent (one CTA per SM) and streams every weight byte of the step from HBM once, through
+// the tcgen05 tensor cores.
 //
 //   K1 logits + operands   one warp per CTA: the fp32 router logit partials of (expert,
 //              segment) in the oracle's order, and the tokens as tensor-core B operands
 //              (int8 digits, bf16 terms) in the swizzled shared-memory image.
-//   K2 route + gate/up     every CTA finishes the routing itself from K1's partials (softmax,
-//              top-k: bit-exact and identical in every CTA, so no grid-wide exchange) while its
-//              producer already streams shared-expert items; the routing groups the step by
-//              expert ("slots": 0..S-1 the shared experts, S+u the u-th distinct routed expert in
+//   experts    every CTA finishes the routing itself from K1's partials (softmax, top-k:
+//              bit-exact and identical in every CTA, so no grid-wide exchange) while its producer
+//              already streams shared-expert items; the routing groups the step by expert
+//              ("slots": 0..S-1 the shared experts, S+u the u-th distinct routed expert in
 //              ascending id), each slot owning contiguous rows of the h and y scratch.
-//              Units (slot, row block of 64 gate|up pairs) -> h[slot row][pair] = silu(g) * u.
-//   K3 down + combine      units (slot, row block of 128 output rows) -> y[slot row][j]; then a
-//              grid barrier and every CTA sums its 1/grid slice of the B x H outputs over each
-//              token's slots in a fixed order: out[t][j].
+//              Phase A, units (slot, 64 gate|up pairs) -> h[slot row][pair] = silu(g) * u, each
+//              unit counted on its slot's counter. Phase B, units (slot, 128 output rows) ->
+//              y[slot row][j]; a slot's h rows become the B operand once its counter is full.
+//              Each down unit is counted on its column block's counter; the arrival that
+//              completes a block has its CTA sum the block's B x 128 outputs over each token's
+//              slots in a fixed order: out[t][j]. No grid-wide barrier.
 //
-// Inside K2 / K3 (9 warps): warp 8 copies each item (a row block's weights over one K range,
-// layout.h) with one cp.async.bulk into shared memory; warp 0 issues the item's tcgen05.mma
-// (M = 128 weight rows, N = 32: three int8 digit planes x 8 tokens, or N = 16: two bf16 terms x
-// 8 tokens; accumulators in TMEM); warps 4-7 read the accumulators back (tcgen05.ld: one TMEM
-// lane per weight row), apply the int8 group scales and finish the row block; in K3 warps 1-3
-// convert each slot's h rows into the B operand. Work is split over the CTAs by a static
-// partition of the units weighted by their bytes.
+// Inside the experts kernel (9 warps): warp 8 copies each item (a row block's weights over one K
+// range, layout.h) with one cp.async.bulk into a ring of shared-memory stages; warps 0 and 1
+// issue the tcgen05.mma of alternate accumulator groups (M = 128 weight rows, N = 32: three int8
+// digit planes x 8 tokens, or N = 16: two bf16 terms x 8 tokens; accumulators in TMEM); warps 4-7
+// read the accumulators back (tcgen05.ld: one TMEM lane per weight row), apply the int8 group
+// scales and finish the units; warps 2-3 convert each slot's h rows into the phase-B operand.
+// Work is split over the CTAs by a static partition of the units weighted by their bytes.
 //
 // Exact activations: an fp32 value v is given to the int8 MMA as three int8 digits with a
 // power-of-two scale per (token, 128-group), v = sigma (d0 + d1/128 + d2/128^2), |d| <= 64, the
@@ -31,8 +34,9 @@
 // the batch it rides in.
 //
 // Every device-side wait is bounded (sm100.cuh, kWaitBudgetNs): on expiry the waiter records a
-// status code, the kernel winds down, and the call writes NaN over its output instead of the
-// combine (DecodeCtl in kernels.h); the sticky status word tells the host (uocr_moe_device_status).
+// status code, the kernel winds down, and the call writes NaN over its output (DecodeCtl in
+// kernels.h); the sticky status word tells the host (uocr_moe_device_status), and until it is
+// read every later call on the workspace writes NaN too.
 #include <algorithm>
 
 #include <cuda_bf16.h>
@@ -45,8 +49,8 @@
 
 namespace uocr {
 
-constexpr int kThreads = 9 * 32;             // MMA warp 0, stagers 1-3, epilogue 4-7, producer 8
-constexpr int kCW = 8;                       // warps 0-7 (K2's routing)
+constexpr int kThreads = 9 * 32;             // MMA warps 0-1, stagers 2-3, epilogue 4-7, producer 8
+constexpr int kCW = 8;                       // warps 0-7 (the routing)
 constexpr int kMaxB = 8;
 constexpr int kMaxSlotsSm = 72;              // shared (<= 8) + routed (<= 64)
 constexpr uint32_t kBarConsumers = 1;        // named barrier of warps 0-7
@@ -87,7 +91,7 @@ struct AccMeta {
     int rb;
     int gi;     // int8: the 128-group of columns 0-31 (columns 32-63: gi + 1)
     int flags;  // bit 0: int8, bit 1: the unit's last accumulator, bit 2: int8 with two groups, bit 3: down
-    float sig[2][kMaxB];       // K3 int8: digit scales of the slot's entries for each group
+    float sig[2][kMaxB];       // down, int8: digit scales of the slot's entries for each group
     float scl[2][kRowBlock];   // int8: weight scales of the 128 rows for each group
 };
 
@@ -153,8 +157,69 @@ UOCR_DEV void put_terms(unsigned char* img, int g, int t, int lane, float4 v) {
         make_uint2(*reinterpret_cast<const uint32_t*>(&b0), *reinterpret_cast<const uint32_t*>(&b1));
 }
 
+// Static partition of the work units over the CTAs, in levels. The units of a phase, in global
+// order (the shared experts' units, then the routed slots' in ascending slot, each slot's row
+// blocks in order), are dealt like list scheduling by cost: a shared unit costs r quanta, a routed
+// unit one (r = 2 for int8 routed experts beside the bf16 shared ones, else 1). Shared unit i goes
+// to CTA i % G; CTAs [m, G) (m = shared units % G) carry one shared unit less, so the first
+// r (G - m) routed units go to them, one per CTA per level, and every later level deals G routed
+// units to all CTAs. A CTA works through its units level by level, so every slot's gate/up units
+// are finished by the level that holds them, early slots first: a CTA's first down units belong to
+// slots that were complete long before its own gate/up units run out (no wait at the phase
+// change), and the costs per CTA differ by at most one quantum.
+struct Units {
+    int ca, cb;  // this CTA's shared units in each phase (indices c, c + G, ...)
+    int ma, mb;  // m of each phase
+    int ra, rb;  // r of each phase
+    int na, nb;  // this CTA's units in each phase (shared first, then routed by level)
+};
+// The routed index of this CTA's k-th routed unit (increasing in k).
+UOCR_DEV int routed_index(int k, int m, int r) {
+    const int G = gridDim.x, c = blockIdx.x;
+    if (c >= m) return k < r ? k * (G - m) + (c - m) : r * (G - m) + (k - r) * G + c;
+    return r * (G - m) + k * G + c;
+}
+// How many of n routed units this CTA takes.
+UOCR_DEV int routed_count(int n, int m, int r) {
+    int k = 0;
+    while (routed_index(k, m, r) < n) ++k;
+    return k;
+}
+// A phase's shared-unit split and cost ratio (n_s shared units of `shared_bytes`, routed units of
+// `routed_bytes`).
+UOCR_DEV void shared_split(int n_s, size_t shared_bytes, size_t routed_bytes, int& cnt, int& m, int& r) {
+    const int G = gridDim.x, c = blockIdx.x;
+    cnt = c < n_s ? (n_s - 1 - c) / G + 1 : 0;
+    m = n_s % G;
+    r = max(1, (int)((2 * shared_bytes + routed_bytes) / (2 * routed_bytes)));
+}
+UOCR_DEV void unit_a(const Units& u, const DecodeArgs& a, int i, int& slot, int& rb) {
+    const int per = a.I / 64;
+    if (i < u.ca) {
+        const int j = blockIdx.x + i * gridDim.x;
+        slot = j / per;
+        rb = j % per;
+    } else {
+        const int j = routed_index(i - u.ca, u.ma, u.ra);
+        slot = a.S + j / per;
+        rb = j % per;
+    }
+}
+UOCR_DEV void unit_b(const Units& u, const DecodeArgs& a, int i, int& slot, int& rb) {
+    const int nrb = a.H / kRowBlock;
+    if (i < u.cb) {
+        const int j = blockIdx.x + i * gridDim.x;
+        slot = j / nrb;
+        rb = j % nrb;
+    } else {
+        const int j = routed_index(i - u.cb, u.mb, u.rb);
+        slot = a.S + j / nrb;
+        rb = j % nrb;
+    }
+}
+
 // ======================================================================================
-// routing inside a CTA (warps 0-7 of K2)
+// routing inside a CTA (warps 0-7 of the experts kernel)
 // ======================================================================================
 // Scratch of the step's routing in shared memory.
 struct RouteSmem {
@@ -179,17 +244,17 @@ struct CombineSmem {
 // segment partials added in ascending order, + bias; softmax with this build's exponential and
 // a fixed butterfly sum; top-k by (p desc, index asc) — identical in every CTA. Then the slot
 // table: routed slot u is the u-th used expert; its rows start after the shared experts' S * B
-// rows, its entries in token order; and each token's rows for the combine. CTA 0 also writes ids /
-// wts. The inputs arrive by bulk copies on `inb`: the partials into `part` (the last stage
-// buffer, which the producer fills only after the table is ready) and K1's operand images.
-// Returns false (nothing routed) if the workspace holds an unread failure (`stale`) or the inputs
-// did not arrive in time.
-// The tokens' operand images arrive on `imb` (the MMA warp waits for them), the rest on `inb`.
-UOCR_DEV bool cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* xb, float* xsig, float* part,
-                        uint64_t* inb, uint64_t* imb, volatile int* abort_flag, uint32_t* fail, RouteSmem* rs,
-                        SlotTable* tb, CombineSmem* cs, int* stale, int tid, unsigned long long* ev) {
+// rows, its entries in token order; each token's rows for the combine; and this CTA's routed
+// units (`units`, from a table of every possible routed-slot count built before the dependency
+// wait). CTA 0 also writes ids / wts. The partials are read straight from L2 into registers;
+// K1's operand images arrive by bulk copies on `imb` (the MMA warps wait for them), the digit
+// scales are copied into `xsig` by plain loads. Returns false (nothing routed) if the workspace
+// holds an unread failure (`stale`).
+UOCR_DEV bool cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* xb, float* xsig, uint64_t* imb,
+                        RouteSmem* rs, SlotTable* tb, CombineSmem* cs, Units* units, int* stale, int tid,
+                        unsigned long long* ev) {
     const int warp = tid >> 5, lane = tid & 31;
-    const int H = a.H, B = a.B, E = a.E, k = a.topk, kB = k * B;
+    const int H = a.H, B = a.B, E = a.E, k = a.topk, kB = k * B, nrb = H / kRowBlock;
     unsigned long long* rv = a.trace ? trace_rec(a, 0, a.trace_items / 2 - 2) : nullptr;  // diagnostics
     // before the wait: this call's inputs that no kernel of the step writes, and scratch resets
     if (tid < 64) {
@@ -199,38 +264,44 @@ UOCR_DEV bool cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* x
     for (int i = tid; i < 64 * kMaxB; i += kCW * 32) tb->pos[a.S + i / kMaxB][i % kMaxB] = -1;
     pdl_wait_prior_grid();  // K1's partials and operands
     if (ev && tid == 0) ev[1] = global_timer_ns();
+    // the partials of (token, expert) pairs tid and tid + 256, loads issued at once
+    float4 p[2][2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int i = tid + kCW * 32 * h;
+        if (i < B * 64) {
+            p[h][0] = __ldcg(reinterpret_cast<const float4*>(a.logits + 8 * (size_t)i));
+            p[h][1] = __ldcg(reinterpret_cast<const float4*>(a.logits + 8 * (size_t)i + 4));
+        }
+    }
     // an unread failure of an earlier call leaves the counters unknown: this call only writes NaN
     // until the host reads the status (which resets the control block)
     if (tid == 0) *stale = __ldcg(&a.ctl->status) != 0u;
     named_bar_sync(kBarConsumers, kCW * 32);
     if (*stale) return false;
     if (warp == 0) {
-        const uint32_t pbytes = (uint32_t)B * 64 * 8 * 4, img = (uint32_t)H * 32;
+        const uint32_t img = (uint32_t)H * 32;
         const uint32_t dbytes = a.int8 ? (uint32_t)((H / 128) * kDigitAtomBytes + kDigitPadBytes) : 0u;
-        const uint32_t sbytes = a.int8 ? 8u * (H / 128) * 4 : 0u;
-        if (lane == 0) mbar_arrive_expect_tx(inb, pbytes + sbytes);
-        if (lane == 1) mbar_arrive_expect_tx(imb, dbytes + img);
+        if (lane == 0) mbar_arrive_expect_tx(imb, dbytes + img);
         __syncwarp();
-        if (lane == 0) bulk_g2s(part, a.logits, pbytes, inb);
         if (lane == 1) bulk_g2s(xb, a.xb, img, imb);
         if (lane == 2 && dbytes) bulk_g2s(xd, a.xd, dbytes, imb);
-        if (lane == 3 && sbytes) bulk_g2s(xsig, a.xsig, sbytes, inb);
     }
-    if (!mbar_wait_warp(inb, 0, abort_flag, fail)) *abort_flag = 1;
-    named_bar_sync(kBarConsumers, kCW * 32);
-    if (*abort_flag) return false;
+    if (a.int8 && tid < kMaxB * (H / 128)) xsig[tid] = __ldcg(a.xsig + tid);
     if (rv && tid == 0) rv[0] = global_timer_ns();
-    for (int i = tid; i < B * 64; i += kCW * 32) {
-        const float4 p0 = *reinterpret_cast<const float4*>(part + 8 * i);
-        const float4 p1 = *reinterpret_cast<const float4*>(part + 8 * i + 4);
-        float total = __fadd_rn(__fadd_rn(__fadd_rn(p0.x, p0.y), p0.z), p0.w);
-        total = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(total, p1.x), p1.y), p1.z), p1.w);
-        if (a.bias) total = __fadd_rn(total, rs->bias[i & 63]);
-        rs->logits[i >> 6][i & 63] = total;
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+        const int i = tid + kCW * 32 * h;
+        if (i < B * 64) {
+            float total = __fadd_rn(__fadd_rn(__fadd_rn(p[h][0].x, p[h][0].y), p[h][0].z), p[h][0].w);
+            total = __fadd_rn(__fadd_rn(__fadd_rn(__fadd_rn(total, p[h][1].x), p[h][1].y), p[h][1].z), p[h][1].w);
+            if (a.bias) total = __fadd_rn(total, rs->bias[i & 63]);
+            rs->logits[i >> 6][i & 63] = total;
+        }
     }
     named_bar_sync(kBarConsumers, kCW * 32);
     if (rv && tid == 0) rv[3] = global_timer_ns();
-    // softmax + top-k: warp b serves token b
+    // softmax + top-k: warp b serves token b; each pick sets bit (token * k + r) of its expert's mask
     if (warp < B) {
         const int b = warp;
         const bool v0 = lane < E, v1 = lane + 32 < E;
@@ -257,6 +328,7 @@ UOCR_DEV bool cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* x
                 const float bp = __uint_as_float(mk - 1u);
                 rs->ids[b * k + rr] = bi;
                 rs->wts[b * k + rr] = bp;
+                atomicOr(&rs->mask[bi], 1ull << (b * k + rr));
                 if (blockIdx.x == 0) {
                     a.ids[b * k + rr] = bi;
                     a.wts[b * k + rr] = bp;
@@ -266,9 +338,7 @@ UOCR_DEV bool cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* x
     }
     named_bar_sync(kBarConsumers, kCW * 32);
     if (rv && tid == 0) rv[4] = global_timer_ns();
-    // group by expert: entry q = token * k + r sets bit q of its expert's mask
-    if (tid < kB) atomicOr(&rs->mask[rs->ids[tid]], 1ull << tid);
-    named_bar_sync(kBarConsumers, kCW * 32);
+    // group by expert: the used experts in ascending id and their entry counts' prefix
     unsigned long long m = 0ull;
     int c = 0, incl = 0;
     if (tid < 64) {  // warps 0, 1: expert tid
@@ -286,6 +356,7 @@ UOCR_DEV bool cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* x
     }
     named_bar_sync(kBarConsumers, kCW * 32);
     const unsigned long long used = (unsigned long long)rs->used[0] | ((unsigned long long)rs->used[1] << 32);
+    const int nu = __popcll(used);
     if (tid < 64 && c > 0) {
         const int u = __popcll(used & ((1ull << tid) - 1ull));
         const int row = a.S + u;
@@ -300,59 +371,24 @@ UOCR_DEV bool cta_route(const DecodeArgs& a, unsigned char* xd, unsigned char* x
             rs->rowof[q] = base + n;
         }
     }
-    if (tid == 0) tb->nslot = a.S + __popcll(used);
+    if (tid == 0) {
+        tb->nslot = a.S + nu;
+        units->na = units->ca + routed_count(nu * (a.I / 64), units->ma, units->ra);
+    }
+    if (tid == 32) units->nb = units->cb + routed_count(nu * nrb, units->mb, units->rb);
     named_bar_sync(kBarConsumers, kCW * 32);
     if (rv && tid == 0) rv[5] = global_timer_ns();
-    if (tid < B) {
-        // token tid's routed rows in ascending expert id (the combine's order)
-        int ord[kDecodeMaxTopk];
-        for (int s = 0; s < k; ++s) {
-            int i = s;
-            while (i > 0 && rs->ids[tid * k + ord[i - 1]] > rs->ids[tid * k + s]) {
-                ord[i] = ord[i - 1];
-                --i;
-            }
-            ord[i] = s;
-        }
-        for (int s = 0; s < k; ++s) {
-            cs->trow[tid][s] = rs->rowof[tid * k + ord[s]];
-            cs->tw[tid][s] = rs->wts[tid * k + ord[s]];
-        }
+    if (tid < kB) {
+        // entry tid of token t: its rank among the token's entries by expert id (distinct ids)
+        const int t = tid / k, id = rs->ids[tid];
+        int rank = 0;
+        for (int j = 0; j < k; ++j) rank += rs->ids[t * k + j] < id;
+        cs->trow[t][rank] = rs->rowof[tid];
+        cs->tw[t][rank] = rs->wts[tid];
     }
-    // `part` lives in a stage buffer the producer fills next with the async proxy
-    fence_proxy_async_smem();
     named_bar_sync(kBarConsumers, kCW * 32);
     if (rv && tid == 0) rv[6] = global_timer_ns();
     return true;
-}
-
-// Static partitions of work units over the CTAs (costs in 512-byte units). All intermediate
-// values fit 32-bit integers for the decode sizes (<= 1008 units of cost <= 640, G <= 1024);
-// the one ratio is a double division (64-bit integer division is slow on the device).
-// n equal units: CTA c takes [ceil(n c / G), ceil(n (c + 1) / G)).
-UOCR_DEV void even_units(int n, int c, int G, int& j0, int& j1) {
-    j0 = (n * c + G - 1) / G;
-    j1 = (n * (c + 1) + G - 1) / G;
-}
-// The second of two phases of equal-cost units (n0 of cost u0 already split by even_units, then
-// n1 of cost u1): CTA c's quota of the second phase is max(0, total / G - p0(c)) (p0 = its
-// first-phase cost); the quotas' prefix, scaled to n1, gives contiguous ranges (neighbours
-// evaluate the same expression on the same integer prefix). A CTA's first-phase count is
-// floor(n0 / G) or one more, and the counts of CTAs [0, c) sum to ceil(n0 c / G), so the prefix
-// has a closed form.
-UOCR_DEV void routed_units(int n0, int u0, int n1, int u1, int& j0, int& j1) {
-    const int G = gridDim.x, c = blockIdx.x;
-    const long long T = (long long)n0 * u0 + (long long)n1 * u1;
-    const int lo = n0 / G;
-    const long long q_lo = max(0LL, T - (long long)G * u0 * lo), q_hi = max(0LL, T - (long long)G * u0 * (lo + 1));
-    auto before = [&](int cc) {  // quota of CTAs [0, cc)
-        const long long hi_cnt = (((long long)n0 * cc + G - 1) / G) - (long long)cc * lo;
-        return hi_cnt * q_hi + ((long long)cc - hi_cnt) * q_lo;
-    };
-    const long long total = before(G);
-    auto bound = [&](long long pre) { return total > 0 ? (int)((double)n1 * (double)pre / (double)total) : 0; };
-    j0 = bound(before(c));
-    j1 = c == G - 1 ? n1 : bound(before(c + 1));
 }
 
 // ======================================================================================
@@ -360,11 +396,11 @@ UOCR_DEV void routed_units(int n0, int u0, int n1, int u1, int& j0, int& j1) {
 // ======================================================================================
 // One warp per CTA. CTAs [0, 8E): expert e = c / 8, segment s = c % 8; lane t < B runs the
 // oracle's chain for token t over segment s (fma in ascending k from +0) and writes the
-// partial sum part[t][e][s]; K2 adds the 8 partials in ascending order plus the bias. The
+// partial sum part[t][e][s]; the experts kernel adds the 8 partials in ascending order plus the bias. The
 // router segment is fetched before the dependency wait. CTAs [8E, 8E + 8 H/128): column
 // t = d / (H/128), group g = d % (H/128): x[t][128g, 128g + 128) as int8 digits (+ the group's
-// scale) and as two bf16 terms, in K2's operand images (zeros for t >= B). Small CTAs (no
-// shared memory) so several start beside the previous layer's K3 on every SM.
+// scale) and as two bf16 terms, in the experts kernel's operand images (zeros for t >= B). Small CTAs (no
+// shared memory) so several start beside the previous layer's experts kernel on every SM.
 constexpr int kLogitSteps = 20;  // 8-element steps per segment held in registers (H <= 1280)
 
 __global__ void __launch_bounds__(32)
@@ -383,7 +419,7 @@ decode_logits_kernel(DecodeArgs a) {
             for (int i = 0; i < kLogitSteps; ++i)
                 if (i < nit) r[i] = ldg_nc_v4(w + 8 * i);
         }
-        pdl_launch_dependents();  // K2 launches now; it waits for this grid before it reads the partials
+        pdl_launch_dependents();  // the experts kernel launches now; it waits for this grid before it reads the partials
         pdl_wait_prior_grid();    // x is the previous layer's output
         if (ev && lane == 0) ev[1] = global_timer_ns();
         float acc = 0.0f;
@@ -444,7 +480,7 @@ decode_logits_kernel(DecodeArgs a) {
 }
 
 // ======================================================================================
-// the MMA warp and the epilogue warps (K2 and K3)
+// the MMA warp and the epilogue warps (experts kernel)
 // ======================================================================================
 // Shared state of the tensor-core pipeline of one CTA.
 struct Pipe {
@@ -474,7 +510,7 @@ UOCR_DEV int acquire_acc(Pipe& p, int grp, int slot, int rb, int gi, int flags, 
     return j;
 }
 // int8 scales of one group into the description: 128 row scales (one float4 per lane) and,
-// for K3, the 8 column scales.
+// for down items, the 8 column scales.
 UOCR_DEV void acc_scales(Pipe& p, int j, int g, const float* scl, const float* sig, int lane) {
     reinterpret_cast<float4*>(p.acc[j].scl[g])[lane] = reinterpret_cast<const float4*>(scl)[lane];
     if (sig && lane < kMaxB) p.acc[j].sig[g][lane] = sig[lane];
@@ -537,26 +573,6 @@ UOCR_DEV void fold_bf16(const AccRead& r, float (&acc)[kMaxB]) {
 // ======================================================================================
 // the experts kernel: route, gate/up (phase A), down (phase B), combine
 // ======================================================================================
-// This CTA's work units of both phases: shared units first (known from the shape), then routed
-// units (known once the CTA has routed), each part a contiguous range of a static partition.
-struct Units {
-    int a_s0, a_s1, a_r0, a_r1;  // gate/up units (slot, 64 pairs): shared of S * I/64, routed of U * I/64
-    int b_s0, b_s1, b_r0, b_r1;  // down units (slot, 128 rows): shared of S * H/128, routed of U * H/128
-    int na, nb;                  // units in each phase
-};
-UOCR_DEV void unit_a(const Units& u, const DecodeArgs& a, int i, int& slot, int& rb) {
-    const int per = a.I / 64, ns = u.a_s1 - u.a_s0;
-    const int j = i < ns ? u.a_s0 + i : u.a_r0 + (i - ns);
-    slot = (i < ns ? 0 : a.S) + j / per;
-    rb = j % per;
-}
-UOCR_DEV void unit_b(const Units& u, const DecodeArgs& a, int i, int& slot, int& rb) {
-    const int nrb = a.H / kRowBlock, ns = u.b_s1 - u.b_s0;
-    const int j = i < ns ? u.b_s0 + i : u.b_r0 + (i - ns);
-    slot = (i < ns ? 0 : a.S) + j / nrb;
-    rb = j % nrb;
-}
-
 // out[t][128 rb + c] for the B tokens and the block's 128 columns by the 128 epilogue threads
 // (thread i: token i / 16, the 8 columns from 8 (i % 16)): the token's shared rows in order, then
 // its routed rows in ascending expert id (w * y), rows loaded 8 at a time; NaN when the call failed.
@@ -620,12 +636,13 @@ UOCR_DEV void count_combined(const DecodeArgs& a, uint32_t n) {
 
 // Persistent, one CTA per SM (every CTA resident: they wait on each other's units), 9 warps:
 // warp 8 streams items (one bulk copy each) into a ring of fixed stages, first the gate/up units
-// (phase A: shared ones while the CTA routes, then routed), then the down units (phase B); warp 0
-// issues their tcgen05 MMAs (B operand: the tokens' images from K1 in phase A, the slot run's h
-// image in phase B); warps 4-7 drain the accumulators: phase A -> h rows (SwiGLU) and a count per
-// slot; phase B -> y rows and a count per output column block, whose completing arrival has its
-// CTA combine the block. Warps 1-3 (phase B) turn each slot run's h rows, once every CTA's gate/up
-// units of that slot are counted, into the run's operand image. Warps 0-7 route first.
+// (phase A: shared ones while the CTA routes, then routed), then the down units (phase B); warps
+// 0 and 1 issue their tcgen05 MMAs, alternate accumulator groups each (B operand: the tokens'
+// images from K1 in phase A, the slot run's h image in phase B); warps 4-7 drain the
+// accumulators: phase A -> h rows (SwiGLU) and a count per slot; phase B -> y rows and a count per
+// output column block, whose completing arrival has its CTA combine the block. Warps 2-3 (phase B)
+// turn each slot run's h rows, once every CTA's gate/up units of that slot are counted, into the
+// run's operand image. Warps 0-7 route first.
 __global__ void __launch_bounds__(kThreads, 1)
 decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_tbl, uint32_t off_route,
                       uint32_t off_meta, uint32_t off_acc, uint32_t off_cs, uint32_t off_sig, uint32_t off_hsig,
@@ -638,8 +655,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
     uint64_t* full = reinterpret_cast<uint64_t*>(smem);
     uint64_t* empty = full + nst;          // the MMAs reading the stage are complete
     uint64_t* table_ready = empty + nst;
-    uint64_t* inb = table_ready + 1;       // the routing's inputs have arrived
-    uint64_t* tfull = inb + 1;             // [kAccSlots]
+    uint64_t* tfull = table_ready + 1;     // [kAccSlots]
     uint64_t* tfree = tfull + kAccSlots;   // [kAccSlots]
     uint64_t* mdone = tfree + kAccSlots;   // the MMA warp's drain
     uint64_t* adone = mdone + 1;           // every gate/up MMA is complete (the image region is free)
@@ -674,7 +690,6 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             mbar_init(&empty[s], 2);  // the issuing MMA warp's commit + the other MMA warp's arrival
         }
         mbar_init(table_ready, 1);
-        mbar_init(inb, 1);
         for (int j = 0; j < kAccSlots; ++j) {
             mbar_init(&tfull[j], 2);
             mbar_init(&tfree[j], 4);
@@ -693,10 +708,11 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
         cta_fail = 0;
         cs->req[0] = cs->req[1] = -1;
         // the shared-expert units (known from the shape)
-        even_units(a.S * (a.I / 64), blockIdx.x, gridDim.x, units.a_s0, units.a_s1);
-        even_units(a.S * nrb, blockIdx.x, gridDim.x, units.b_s0, units.b_s1);
-        units.a_r0 = units.a_r1 = units.b_r0 = units.b_r1 = 0;
-        units.na = units.a_s1 - units.a_s0;
+        const size_t a_rt = (size_t)w13_items(a.H, a.int8 != 0) * w13_item_bytes(a.int8 != 0);
+        shared_split(a.S * (a.I / 64), (size_t)w13_items(a.H, false) * w13_item_bytes(false), a_rt, units.ca,
+                     units.ma, units.ra);
+        shared_split(a.S * nrb, w2_rb_bytes(a.I, false), w2_rb_bytes(a.I, a.int8 != 0), units.cb, units.mb, units.rb);
+        units.na = units.ca;
         units.nb = 0;
         fence_mbar_init();
         pdl_launch_dependents();  // the next layer's first kernel launches early; it waits for this grid
@@ -723,8 +739,6 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
         int grp = 0;  // accumulator groups handed out
         auto issue = [&](const unsigned char* src, uint32_t bytes, int slot, int rb, int ki, int phase, int run,
                          bool new_grp) {
-            // the last stage holds the routing's logit partials until the table is ready
-            if (round == 0 && st == nst - 1) wait_table();
             if (ok && round > 0 && !mbar_wait_warp(&empty[st], (round - 1) & 1, &abort_flag, fail)) ok = false;
             if (!ok) return;
             if (lane == 0) {
@@ -759,7 +773,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             for (int ki = 0; ki < nk && ok; ++ki)
                 issue(base + ((size_t)rb * nk + ki) * bytes, bytes, slot, rb, ki, 0, -1, i8 || ki == 0);
         };
-        const int ns_a = units.a_s1 - units.a_s0;
+        const int ns_a = units.ca;
         for (int i = 0; i < ns_a && ok; ++i) {  // shared units: streamed while routing
             int slot, rb;
             unit_a(units, a, i, slot, rb);
@@ -806,24 +820,10 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
         __syncwarp();
     } else {
         // ---------------- warps 0-7: route; then MMA (0), stagers (1-3), epilogue (4-7) ----------------
-        float* part = reinterpret_cast<float*>(stages + (size_t)(nst - 1) * stage_bytes);
-        const bool ok_route = cta_route(a, xd, xb, xsig, part, inb, imb, &abort_flag, fail, rs, tb, cs, &stale, tid, ev);
+        const bool ok_route = cta_route(a, xd, xb, xsig, imb, rs, tb, cs, &units, &stale, tid, ev);
         if (tid == 0) {
-            if (ok_route) {
-                // the routed units, balanced against each CTA's shared share
-                const int nu = tb->nslot - a.S;
-                routed_units(a.S * (a.I / 64), (int)((size_t)w13_items(a.H, false) * w13_item_bytes(false) / 512),
-                             nu * (a.I / 64),
-                             (int)((size_t)w13_items(a.H, a.int8 != 0) * w13_item_bytes(a.int8 != 0) / 512),
-                             units.a_r0, units.a_r1);
-                routed_units(a.S * nrb, (int)(w2_rb_bytes(a.I, false) / 512), nu * nrb,
-                             (int)(w2_rb_bytes(a.I, a.int8 != 0) / 512), units.b_r0, units.b_r1);
-                units.na = (units.a_s1 - units.a_s0) + (units.a_r1 - units.a_r0);
-                units.nb = (units.b_s1 - units.b_s0) + (units.b_r1 - units.b_r0);
-                routed = 1;
-            } else {
-                abort_flag = 1;
-            }
+            if (ok_route) routed = 1;
+            else abort_flag = 1;
             mbar_arrive(table_ready);
         }
         named_bar_sync(kBarConsumers, kCW * 32);
@@ -1194,14 +1194,6 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
         const int lo = (int)((long long)total * blockIdx.x / gridDim.x);
         const int hi = (int)((long long)total * (blockIdx.x + 1) / gridDim.x);
         for (int o = lo + tid; o < hi; o += blockDim.x) a.out[o] = __uint_as_float(0x7FC00000u);
-    } else if (!routed) {
-        // the routing's inputs never arrived here: this CTA cannot count its units, so it writes NaN
-        // over the whole output itself (the blocks its units belong to are never combined)
-        if (tid == 0) {
-            atomicOr(&a.ctl->call_fail, 1u);
-            set_status(&a.ctl->status, kStatusWaitTimeout);
-        }
-        for (int o = tid; o < a.B * a.H; o += blockDim.x) a.out[o] = __uint_as_float(0x7FC00000u);
     }
 }
 
@@ -1254,11 +1246,10 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
         err = launch_pdl(reinterpret_cast<const void*>(decode_logits_kernel), dim3(k1_ctas), dim3(32), 0, st, args);
         if (err != cudaSuccess) return err;
     }
-    // ---- the experts kernel: a stage holds one item of either phase (the last one first the
-    // logit partials); the image region holds K1's operand images, then two run images
-    const uint32_t stage_bytes = (uint32_t)up(
-        std::max({w13_item_bytes(false), a.int8 ? w13_item_bytes(true) : size_t(0), sizeof(float) * kMaxB * 64 * 8}),
-        1024);
+    // ---- the experts kernel: a stage holds one item of either phase; the image region holds
+    // K1's operand images, then two run images
+    const uint32_t stage_bytes =
+        (uint32_t)up(std::max(w13_item_bytes(false), a.int8 ? w13_item_bytes(true) : size_t(0)), 1024);
     const size_t off_tbl = 512;  // the mbarriers before it
     const size_t off_route = off_tbl + up(sizeof(SlotTable), 128);
     const size_t off_meta = off_route + up(sizeof(RouteSmem), 128);
