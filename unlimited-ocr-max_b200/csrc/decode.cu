@@ -79,7 +79,7 @@ struct ItemMeta {
     int ki;     // item (K range) within the row block
     int phase;  // 0: gate/up, 1: down
     int run;    // down: the slot run this item starts (its operand image), -1 for none
-    int grp;    // accumulator group: an int8 item, or a bf16 unit's items (MMA warp grp % 2 issues it)
+    int grp;    // accumulator group: an int8 item, or a bf16 unit's even or odd items (MMA warp grp % 2 issues it)
     int pad[2];
 };
 
@@ -564,10 +564,11 @@ UOCR_DEV void fold_s8(const AccRead& r, int g, const float* colsig, float (&acc)
         acc[t] = __fmaf_rn(undigit((int)r.v[g][t], (int)r.v[g][8 + t], (int)r.v[g][16 + t]),
                            __fmul_rn(r.scl[g], colsig[t]), acc[t]);
 }
-// bf16 accumulator (the whole row block): acc[t] = term-0 column + term-1 column
+// bf16 accumulator (a row block's even or odd items): acc[t] += term-0 column + term-1 column
 UOCR_DEV void fold_bf16(const AccRead& r, float (&acc)[kMaxB]) {
 #pragma unroll
-    for (int t = 0; t < kMaxB; ++t) acc[t] = __fadd_rn(__uint_as_float(r.v[0][t]), __uint_as_float(r.v[0][8 + t]));
+    for (int t = 0; t < kMaxB; ++t)
+        acc[t] = __fadd_rn(acc[t], __fadd_rn(__uint_as_float(r.v[0][t]), __uint_as_float(r.v[0][8 + t])));
 }
 
 // ======================================================================================
@@ -737,8 +738,16 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             }
         };
         int grp = 0;  // accumulator groups handed out
+        // an int8 item is a group of its own; a bf16 unit's items form two groups (even and odd
+        // items), issued by the two MMA warps in turn
+        auto item_grp = [&](bool i8, int ki, int nk) {
+            if (i8) return grp++;
+            const int g = grp + (ki & 1);
+            if (ki == nk - 1) grp += nk > 1 ? 2 : 1;
+            return g;
+        };
         auto issue = [&](const unsigned char* src, uint32_t bytes, int slot, int rb, int ki, int phase, int run,
-                         bool new_grp) {
+                         int g) {
             if (ok && round > 0 && !mbar_wait_warp(&empty[st], (round - 1) & 1, &abort_flag, fail)) ok = false;
             if (!ok) return;
             if (lane == 0) {
@@ -747,14 +756,13 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                 meta[st].ki = ki;
                 meta[st].phase = phase;
                 meta[st].run = run;
-                meta[st].grp = new_grp ? grp : grp - 1;
+                meta[st].grp = g;
                 mbar_arrive_expect_tx(&full[st], bytes);
                 bulk_g2s_hint(stages + (size_t)st * stage_bytes, src, bytes, &full[st], stream_policy);
                 unsigned long long* tr = trace_rec(a, phase, n);
                 if (tr) tr[4] = global_timer_ns();
             }
             __syncwarp();
-            if (new_grp) ++grp;
             ++n;
             if (++st == nst) {
                 st = 0;
@@ -771,7 +779,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                                  (size_t)tb->expert[slot] * w13_expert_bytes(a.I, a.H, i8);
             const int nk = w13_items(a.H, i8);
             for (int ki = 0; ki < nk && ok; ++ki)
-                issue(base + ((size_t)rb * nk + ki) * bytes, bytes, slot, rb, ki, 0, -1, i8 || ki == 0);
+                issue(base + ((size_t)rb * nk + ki) * bytes, bytes, slot, rb, ki, 0, -1, item_grp(i8, ki, nk));
         };
         const int ns_a = units.ca;
         for (int i = 0; i < ns_a && ok; ++i) {  // shared units: streamed while routing
@@ -802,7 +810,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                 const int nk = w2_items(a.I, i8);
                 for (int ki = 0; ki < nk && ok; ++ki)
                     issue(base + w2_item_offset(i8, ki), (uint32_t)item_bytes(w2_item_atoms(a.I, i8, ki), i8), slot,
-                          rb, ki, 1, ki == 0 ? run : -1, i8 || ki == 0);
+                          rb, ki, 1, ki == 0 ? run : -1, item_grp(i8, ki, nk));
             }
         }
         if (lane == 0) {
@@ -908,8 +916,8 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                             umma_commit(&tfull[j]);
                         }
                     } else {
-                        if (ki == 0) {
-                            cur = acquire_acc(pipe, grp, slot, rb, 0, 2, lane);
+                        if (ki < 2) {  // this warp's group of the unit: its even or odd items
+                            cur = acquire_acc(pipe, grp, slot, rb, 0, (ki & 1) || nk16 == 1 ? 2 : 0, lane);
                             if (cur < 0) {
                                 ok = false;
                                 break;
@@ -923,8 +931,8 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                                 for (int s = 0; s < 4; ++s)
                                     umma_f16(pipe.tmem + kAccCols * cur, umma_desc_sw128(item_s + at * kAtomBytes + 32 * s),
                                              umma_desc_sw128(xb_s + (2 * ki + at) * kTermAtomBytes + 32 * s), kIdescBf16,
-                                             (ki | at | s) != 0);
-                            if (ki == nk16 - 1) umma_commit(&tfull[cur]);
+                                             ((ki >> 1) | at | s) != 0);
+                            if (ki + 2 >= nk16) umma_commit(&tfull[cur]);
                         }
                     }
                 } else {
@@ -956,8 +964,8 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                             umma_commit(&tfull[j]);
                         }
                     } else {
-                        if (ki == 0) {
-                            cur = acquire_acc(pipe, grp, slot, rb, 0, 8 | 2, lane);
+                        if (ki < 2) {  // this warp's group of the unit: its even or odd items
+                            cur = acquire_acc(pipe, grp, slot, rb, 0, (ki & 1) || nk == 1 ? 8 | 2 : 8, lane);
                             if (cur < 0) {
                                 ok = false;
                                 break;
@@ -971,8 +979,8 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                                 for (int s = 0; s < 4; ++s)
                                     umma_f16(pipe.tmem + kAccCols * cur, umma_desc_sw128(item_s + at * kAtomBytes + 32 * s),
                                              umma_desc_sw128(img_s + (2 * ki + at) * kTermAtomBytes + 32 * s), kIdescBf16,
-                                             (ki | at | s) != 0);
-                            if (ki == nk - 1) umma_commit(&tfull[cur]);
+                                             ((ki >> 1) | at | s) != 0);
+                            if (ki + 2 >= nk) umma_commit(&tfull[cur]);
                         }
                     }
                 }
