@@ -625,8 +625,10 @@ UOCR_DEV void nan_block(const DecodeArgs& a, int rb, int lane) {
 }
 // `n` more shares of combined column blocks (4 shares a block: one per epilogue warp); the share
 // that completes the call resets the call's words for the next call.
+// No fence before the count: the call's reads of the words the last count resets (call_fail by
+// acquire loads, the slot counters long before) are ordered before it, and the output stores
+// need no order with it (the kernel's completion publishes them).
 UOCR_DEV void count_combined(const DecodeArgs& a, uint32_t n) {
-    __threadfence();
     if (atomicAdd(&a.ctl->cdone, n) + n == 4u * (uint32_t)(a.H / kRowBlock)) {
         for (int s = 0; s < 72; ++s) a.ctl->hdone[s] = 0u;
         a.ctl->call_fail = 0u;
@@ -1104,10 +1106,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                         acc[t] = 0.0f;
                     }
                     __syncwarp();
-                    if (lane == 0) {
-                        __threadfence();
-                        atomicAdd(&a.ctl->hdone[r.slot], 1u);
-                    }
+                    if (lane == 0) red_release_gpu_add(&a.ctl->hdone[r.slot], 1u);
                     ++ia;
                 } else {
                     // down unit done: y rows; the arrival that completes the column block has this
@@ -1120,10 +1119,8 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                     __syncwarp();
                     int setter = 0;  // this warp's arrival completed the column block
                     if (lane == 0) {
-                        __threadfence();
-                        if (atomicAdd(&a.ctl->ydone[r.rb], 1u) + 1u == yd_target) {
+                        if (atom_acq_rel_gpu_add(&a.ctl->ydone[r.rb], 1u) + 1u == yd_target) {
                             atomicExch(&a.ctl->ydone[r.rb], 0u);
-                            __threadfence();
                             cs->req[ib & 1] = (ib << 8) | (r.rb + 1);
                             setter = 1;
                         }
@@ -1148,7 +1145,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                     const int req = *reinterpret_cast<volatile int*>(&cs->req[(ib - 1) & 1]);
                     const bool mine = req >= 0 && (req >> 8) == ib - 1;
                     if (mine) {
-                        const bool failed = __ldcg(&a.ctl->call_fail) != 0u;
+                        const bool failed = ld_acquire_gpu(&a.ctl->call_fail) != 0u;
                         combine_block(a, cs, (req & 255) - 1, failed, ie);
                         __syncwarp();
                         if (lane == 0) count_combined(a, 1u);

@@ -142,6 +142,17 @@ UOCR_DEV float4 lds_f128(uint32_t a) {
 }
 
 // ---- global flags with gpu-scope ordering -------------------------------------------------
+// Counter arrivals that publish this thread's earlier writes (and those ordered before them, e.g.
+// by a __syncwarp): a release reduction, and an acquire-release add that also makes the other
+// arrivals' writes visible to the caller.
+UOCR_DEV void red_release_gpu_add(uint32_t* p, uint32_t v) {
+    asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+UOCR_DEV uint32_t atom_acq_rel_gpu_add(uint32_t* p, uint32_t v) {
+    uint32_t old;
+    asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+    return old;
+}
 UOCR_DEV uint32_t ld_acquire_gpu(const uint32_t* p) {
     uint32_t v;
     asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
