@@ -70,6 +70,8 @@ def parse():
                    help="EP expert->rank map: balanced from the routed loads of a calibration batch (another "
                         "seed of the same distribution), or contiguous ranges")
     p.add_argument("--tokens", type=int, default=4096, help="prefill tokens (configs[2]: 4096)")
+    p.add_argument("--prefill-int8", action="store_true",
+                   help="prefill workload with int8 routed experts (configs[2] shape, configs[1] weights)")
     return p.parse_args()
 
 
@@ -454,9 +456,10 @@ class CpuPrefill:
 
 
 def run_prefill(args, torch, uocr, synth, dist, world, rank, device):
-    """one bf16 MoE layer over 4096 tokens with an N(0, 1) expert bias."""
-    T = args.tokens
-    moe, x, out, ids, wts = prefill_case(torch, uocr, synth, False, T, device, 3000)
+    """one bf16 MoE layer over 4096 tokens with an N(0, 1) expert bias (int8 routed
+    experts with --prefill-int8)."""
+    T, int8 = args.tokens, args.prefill_int8
+    moe, x, out, ids, wts = prefill_case(torch, uocr, synth, int8, T, device, 3000)
     sampler = ClockSampler(physical_gpu_index(int(os.environ.get("LOCAL_RANK", "0"))))
     g, ms, clocks = time_prefill(torch, moe, x, out, ids, wts, args.steps, args.warmup, dist, sampler,
                                  settle_s=args.settle)
@@ -478,12 +481,15 @@ def run_prefill(args, torch, uocr, synth, dist, world, rank, device):
     if rank != 0:
         return
     line = {
-        "metric": "MoE-layer tokens/s (prefill 4096, bf16)",
+        "metric": f"MoE-layer tokens/s (prefill {T}, {'int8' if int8 else 'bf16'})",
         "value": world * T / (ms * 1e-3), "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "bf16 operands, fp32 accumulate (fp32 in/out)",
+        "vs_baseline": None,
+        "dtype": ("int8 weights dequantised to bf16 (int8_dequant_expert bits), " if int8 else "")
+        + "bf16 operands, fp32 accumulate (fp32 in/out)",
         "data": "synthetic (seeded N(0,0.02)->bf16 weights; hidden N(0,1) RMS-normalised; N(0,1) expert bias)",
-        "config": {"workload": "configs[2] prefill bf16, 4096 tokens, N(0,1) per-expert logit bias",
+        "config": {"workload": f"configs[2] prefill {'int8 routed experts' if int8 else 'bf16'}, {T} tokens, "
+                               "N(0,1) per-expert logit bias",
                    "hidden": H, "experts": E, "top_k": TOPK, "shared": S, "moe_intermediate": I, "tokens": T,
                    "l2": "each replay streams the touched experts (<= 440 MB) and ~300 MB of activations >> 126 MB L2",
                    "parallelism": f"replicas x{world}" if world > 1 else "single GPU",
@@ -494,7 +500,7 @@ def run_prefill(args, torch, uocr, synth, dist, world, rank, device):
                      "algorithmic_flop_per_step": flop, "traffic": None},
         "e2e": {"value": world * T / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                 "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
-        "gpu_launches": PREFILL_LAUNCHES * args.steps,
+        "gpu_launches": (PREFILL_LAUNCHES + 2 * int8) * args.steps,
         "clocks": clocks,
         "cpu_baseline": cpu,
         "outputs_finite": finite,
