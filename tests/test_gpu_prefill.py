@@ -97,10 +97,11 @@ def test_call_dispatches_by_length(uocr, oracle):
     assert torch.equal(moe(x), moe.prefill(x))
 
 
-@pytest.mark.parametrize("int8,T,biased", [(False, 4096, True), (True, 1000, False)])
+@pytest.mark.parametrize("int8,T,biased", [(False, 4096, True), (True, 1000, False), (True, 4096, True)])
 def test_full_size_prefill(uocr, oracle, int8, T, biased):
     """hidden 1280, 64 experts top-6 + 2 shared, I = 896; the bf16 case is BASELINE config 3
-    (T = 4096 with an N(0, 1) logit bias skewing the expert loads)."""
+    (T = 4096 with an N(0, 1) logit bias skewing the expert loads). int8 at T = 1000 takes the
+    single-CTA GEMMs, at T = 4096 the CTA-pair GEMMs, both after the dequant pass."""
     cfg, w = full_layer(oracle, int8, 0)
     moe = uocr.UocrMoE(uocr.MoEConfig(int8_experts=int8)).load_state_dict(to_state(w, cfg, int8))
     bias = np.random.default_rng(41).standard_normal(64).astype(np.float32) if biased else None
@@ -114,3 +115,26 @@ def test_full_size_prefill(uocr, oracle, int8, T, biased):
     assert np.array_equal(ids.cpu().numpy(), r.ids)
     assert np.array_equal(wts.cpu().numpy().view(np.uint32), r.weights.view(np.uint32))
     _check(oracle, got, oracle.moe_layer_fp64(cfg, w, x, r.ids, r.weights))
+
+
+def test_int8_prefill_equals_bf16_of_dequantised_weights(uocr, oracle):
+    """The int8 layer dequantises the touched experts' int8 items to bf16_rne(f32(q) * scale)
+    (int8_dequant_expert's bits) before the bf16 GEMMs: it equals, bit for bit, the bf16 layer
+    whose routed experts are the reference dequant of the same int8 stacks (oracle.dequant_bits),
+    routing, GEMM tiling and combine being the same."""
+    cfg, w = full_layer(oracle, True, 0)
+    st8 = to_state(w, cfg, True)
+    st16 = {k: v for k, v in st8.items() if not k.endswith("_scales")}
+    for name in ("gate", "up", "down"):
+        q, sc = getattr(w, name), getattr(w, f"{name}_scales")
+        bits = np.stack([oracle.dequant_bits(q, sc, e) for e in range(q.shape[0])])
+        st16[f"experts.{name}_proj"] = torch.from_numpy(bits.view(np.int16)).view(torch.bfloat16)
+    moe8 = uocr.UocrMoE(uocr.MoEConfig(int8_experts=True)).load_state_dict(st8)
+    moe16 = uocr.UocrMoE(uocr.MoEConfig()).load_state_dict(st16)
+    bias = torch.from_numpy(np.random.default_rng(41).standard_normal(64).astype(np.float32)).to(DEV)
+    moe8.bias = moe16.bias = bias
+    x = torch.from_numpy(oracle.synth_hidden(4096, cfg.hidden, 6)).to(DEV)
+    got8, got16 = moe8.prefill(x), moe16.prefill(x)
+    assert torch.isfinite(got8).all()
+    assert torch.equal(got8, got16)
+    moe8.check_status()
