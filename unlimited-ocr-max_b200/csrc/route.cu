@@ -160,12 +160,12 @@ route_kernel(const float* __restrict__ x, int T, int H, const uint16_t* __restri
 // distinct banks), then walks tiles of kRT tokens. Eight FMA warps: warp w owns segment s = w,
 // lane l experts l and l + 32, for the tile's kRT tokens (8 chains); token rows arrive by
 // cp.async one tile ahead (issued after the FMA warps' barrier that retires the buffer's previous
-// tile). Two finishing warps take each tile's segment partials from one of two buffers (handed
-// over by mbarriers) and finish tokens 2w' and 2w' + 1 (sum of the 8 partials, bias, softmax,
-// top-k), so the FMA warps never wait for a softmax. Every mbarrier wait is bounded.
+// tile). kRT finishing warps take each tile's segment partials from one of two buffers (handed
+// over by mbarriers) and finish one token each (sum of the 8 partials, bias, softmax, top-k), so
+// the FMA warps never wait for a softmax. Every mbarrier wait is bounded.
 constexpr int kRT = 4;
 constexpr int kRouteFmaThreads = 256;
-constexpr int kRouteSmemThreads = kRouteFmaThreads + 64;
+constexpr int kRouteSmemThreads = kRouteFmaThreads + 32 * kRT;
 constexpr uint32_t kRouteWaitPolls = 1u << 24;  // far beyond any legitimate wait; never hangs
 
 UOCR_DEV void route_stage_tokens(const float* __restrict__ x, int T, int H, int t0, float* dst, int tid) {
@@ -218,7 +218,7 @@ route_smem_kernel(const float* __restrict__ x, int T, int H, const uint16_t* __r
     if (tid == 0) {
         for (int i = 0; i < 2; ++i) {
             mbar_init(&segs_full[i], kRouteFmaThreads);
-            mbar_init(&segs_free[i], 64);
+            mbar_init(&segs_free[i], 32 * kRT);
         }
         fence_mbar_init();
     }
@@ -287,15 +287,14 @@ route_smem_kernel(const float* __restrict__ x, int T, int H, const uint16_t* __r
         }
         asm volatile("cp.async.wait_group 0;\n" ::: "memory");
     } else {
-        const int fw = warp - kRouteFmaThreads / 32;  // 0 or 1: tokens 2fw, 2fw + 1 of each tile
+        const int fw = warp - kRouteFmaThreads / 32;  // token fw of each tile
         int it = 0;
         for (int tile = blockIdx.x; tile < ntiles; tile += gridDim.x, ++it) {
             const int buf = it & 1;
             route_wait(&segs_full[buf], (it >> 1) & 1);
             const float* sb = segs + buf * kRT * 64 * 8;
-#pragma unroll 1
-            for (int u = 0; u < 2; ++u) {
-                const int t = 2 * fw + u, tok = tile * kRT + t;
+            {
+                const int t = fw, tok = tile * kRT + t;
                 if (tok < T)
                     route_finish_token(sb + t * 64 * 8, E, bias, topk, lane, ids_out + (size_t)tok * topk,
                                        wts_out + (size_t)tok * topk);
