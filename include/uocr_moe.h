@@ -303,7 +303,7 @@ UOCR_API int uocr_moe_decode_set_trace(void* device_buffer, size_t bytes);
 UOCR_API int uocr_moe_device_status(const void* workspace, uocr_stream_t stream);
 
 /* Test hook (no counterpart in the reference): the down phase of the next decode launches waits,
- * per slot, for `extra` gate/up arrivals that never come, so its bounded waits run out; used to
+ * per slot, for `extra` operand groups that are never written, so its bounded waits run out; used to
  * check that such a failure is reported (NaN output, UOCR_EDEVICE from the status read) and that
  * calls after the status read are correct. 0 turns it off. Not thread-safe; for tests only. */
 UOCR_API int uocr_moe_test_wait_extra(int extra);

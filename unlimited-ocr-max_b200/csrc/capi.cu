@@ -54,8 +54,8 @@ size_t g_decode_trace_bytes = 0;
 int g_decode_wait_extra = 0;
 
 // Read a workspace's status word after `stream` finished; if it is set, clear it together with the
-// control words a failed call may have left behind (decode: DecodeCtl; prefill: its first 128
-// bytes are the status region, so the clear stays inside it). Returns the code read.
+// control words a failed call may have left behind (decode: DecodeCtl; prefill and exchange
+// workspaces: a status region of the same size). Returns the code read.
 int read_clear_status(const void* workspace, cudaStream_t stream, uint32_t* code) {
     cudaError_t err = cudaStreamSynchronize(stream);
     if (err != cudaSuccess) return fail(UOCR_ECUDA, "device_status: synchronize: %s", cudaGetErrorString(err));
@@ -300,7 +300,7 @@ int uocr_moe_route(const float* x, int64_t T, int64_t H, const uint16_t* router,
 namespace {
 
 struct DecodeLayout {
-    size_t ctl, logits, xd, xb, xsig, ids, wts, h, y, total;
+    size_t ctl, logits, xd, xb, xsig, ids, wts, h, y, himg, gsig, total;
 };
 
 DecodeLayout decode_layout(const uocr_moe_layer* L, int64_t B) {
@@ -316,6 +316,8 @@ DecodeLayout decode_layout(const uocr_moe_layer* L, int64_t B) {
     d.wts = off; off += align256(sizeof(float) * (size_t)B * L->top_k);
     d.h = off; off += align256(sizeof(float) * pairs * (size_t)L->inter);
     d.y = off; off += align256(sizeof(float) * pairs * (size_t)L->hidden);
+    d.himg = off; off += align256(sizeof(float) * pairs * (size_t)L->inter);
+    d.gsig = off; off += align256(sizeof(float) * pairs * (size_t)uocr::decode_sig_stride(L->inter));
     d.total = off;
     return d;
 }
@@ -355,7 +357,8 @@ int uocr_moe_decode(const uocr_moe_layer* L, const float* x, int64_t B, const fl
     if (rc) return rc;
     if (B < 1 || B > 8) return fail(UOCR_EINVAL, "moe_decode: B=%lld outside 1..8 (use moe_prefill)", (long long)B);
     if (L->n_shared > uocr::kDecodeMaxShared) return fail(UOCR_EUNSUPPORTED, "moe_decode: more than 8 shared experts");
-    if (L->hidden > 8192 || L->inter > 8192) return fail(UOCR_EUNSUPPORTED, "moe_decode: hidden/inter above 8192");
+    if (L->hidden > 8192 || L->inter > 128 * uocr::kDecodeMaxGroups)
+        return fail(UOCR_EUNSUPPORTED, "moe_decode: hidden above 8192 or inter above %d", 128 * uocr::kDecodeMaxGroups);
     if (!x || !out || !workspace) return fail(UOCR_EINVAL, "moe_decode: null pointer");
     if (!a16(x) || !a16(out)) return fail(UOCR_EINVAL, "moe_decode: x and out must be 16-byte aligned");
     if (bias && (reinterpret_cast<uintptr_t>(bias) & 3)) return fail(UOCR_EINVAL, "moe_decode: bias must be 4-byte aligned");
@@ -374,6 +377,8 @@ int uocr_moe_decode(const uocr_moe_layer* L, const float* x, int64_t B, const fl
     a.w13_shared = L->w13_shared; a.w2_shared = L->w2_shared;
     a.h = reinterpret_cast<float*>(ws + d.h);
     a.y = reinterpret_cast<float*>(ws + d.y);
+    a.himg = reinterpret_cast<unsigned char*>(ws + d.himg);
+    a.gsig = reinterpret_cast<float*>(ws + d.gsig);
     a.out = out;
     a.ctl = reinterpret_cast<uocr::DecodeCtl*>(ws + d.ctl);
     a.logits = reinterpret_cast<float*>(ws + d.logits);

@@ -55,6 +55,7 @@ constexpr int kMaxB = 8;
 constexpr int kMaxSlotsSm = 72;              // shared (<= 8) + routed (<= 64)
 constexpr uint32_t kBarConsumers = 1;        // named barrier of warps 0-7
 constexpr int kAccSlots = 4;                 // TMEM accumulators of 64 columns
+constexpr int kMaxJobs = 64;                 // group-image jobs of one CTA (<= its gate/up units)
 constexpr uint32_t kAccCols = 64;
 constexpr uint32_t kTmemCols = kAccSlots * kAccCols;
 constexpr int kDigitAtomBytes = 24 * 128;    // int8 B operand group: 3 digit planes x 8 tokens (24 rows)
@@ -84,8 +85,8 @@ struct ItemMeta {
 };
 
 // One TMEM accumulator's description, written by the MMA warp, read by the epilogue. An
-// accumulator is 64 TMEM columns: int8 = up to two 128-groups (columns 0-31, 32-63; three digit
-// planes x 8 tokens + 8 unused each), bf16 = two terms x 8 tokens (columns 0-15).
+// accumulator is 64 TMEM columns: int8 = up to two 128-groups (columns 0-31, 32-63; column 3t + p
+// = digit plane p of token t, 8 unused each), bf16 = two terms x 8 tokens (column 2t + q, 0-15).
 struct AccMeta {
     int slot;   // < 0: end of the work
     int rb;
@@ -134,26 +135,28 @@ UOCR_DEV float group_digits(float4 v, uint32_t (&w)[3]) {
     for (int q = 0; q < 3; ++q) w[q] = pack_s8x4(d[0][q], d[1][q], d[2][q], d[3][q]);
     return sg;
 }
-// int8 operand image [group][24 rows][128 B] (swizzled, groups 3 KB apart): digit plane p of column t
-// is row 8p + t. The N = 32 MMA of a group also reads the next 8 rows (the next group's, or padding
-// after the last): their accumulator columns 24-31 are never read.
-// Lane L's words of group g, column t.
-UOCR_DEV void put_digits(unsigned char* img, int g, int t, int lane, const uint32_t (&w)[3]) {
+// int8 operand image [group][24 rows][128 B] (swizzled, groups `stride` bytes apart: 3 KB in shared
+// memory): digit plane p of column t is row 3t + p, so a column's rows are contiguous and the
+// first c columns are the group's first 3c rows. The N = 32 MMA of a group also reads the next 8
+// rows (the next group's, or padding after the last): their accumulator columns 24-31 are never
+// read. Lane L's words of group g, column t.
+UOCR_DEV void put_digits(unsigned char* img, size_t stride, int g, int t, int lane, const uint32_t (&w)[3]) {
 #pragma unroll
     for (int p = 0; p < 3; ++p)
-        *reinterpret_cast<uint32_t*>(img + (size_t)g * kDigitAtomBytes + atom_offset(8 * p + t, 4 * lane)) = w[p];
+        *reinterpret_cast<uint32_t*>(img + (size_t)g * stride + atom_offset(3 * t + p, 4 * lane)) = w[p];
 }
-// bf16 operand image [64-element atom][16 rows][128 B] (swizzled): term q of column t is row
-// 8q + t. Lane L's values [4L, 4L + 4) of 128-element chunk g of column t (atom 2g + L / 16).
-UOCR_DEV void put_terms(unsigned char* img, int g, int t, int lane, float4 v) {
+// bf16 operand image [64-element atom][16 rows][128 B] (swizzled, atoms `stride` bytes apart: 2 KB in
+// shared memory): term q of column t is row 2t + q. Lane L's values [4L, 4L + 4) of 128-element
+// chunk g of column t (atom 2g + L / 16).
+UOCR_DEV void put_terms(unsigned char* img, size_t stride, int g, int t, int lane, float4 v) {
     const __nv_bfloat162 a0 = __floats2bfloat162_rn(v.x, v.y), a1 = __floats2bfloat162_rn(v.z, v.w);
     const __nv_bfloat162 b0 = __floats2bfloat162_rn(v.x - __low2float(a0), v.y - __high2float(a0));
     const __nv_bfloat162 b1 = __floats2bfloat162_rn(v.z - __low2float(a1), v.w - __high2float(a1));
-    unsigned char* atom = img + (size_t)(2 * g + (lane >> 4)) * kTermAtomBytes;
+    unsigned char* atom = img + (size_t)(2 * g + (lane >> 4)) * stride;
     const int c = 8 * (lane & 15);
-    *reinterpret_cast<uint2*>(atom + atom_offset(t, c)) =
+    *reinterpret_cast<uint2*>(atom + atom_offset(2 * t, c)) =
         make_uint2(*reinterpret_cast<const uint32_t*>(&a0), *reinterpret_cast<const uint32_t*>(&a1));
-    *reinterpret_cast<uint2*>(atom + atom_offset(8 + t, c)) =
+    *reinterpret_cast<uint2*>(atom + atom_offset(2 * t + 1, c)) =
         make_uint2(*reinterpret_cast<const uint32_t*>(&b0), *reinterpret_cast<const uint32_t*>(&b1));
 }
 
@@ -468,12 +471,12 @@ decode_logits_kernel(DecodeArgs a) {
         const int k = 128 * g + 4 * lane;
         const float4 v = t < a.B ? __ldcg(reinterpret_cast<const float4*>(a.x + (size_t)t * H + k))
                                  : make_float4(0.f, 0.f, 0.f, 0.f);
-        put_terms(a.xb, g, t, lane, v);
+        put_terms(a.xb, kTermAtomBytes, g, t, lane, v);
         if (a.int8) {
             uint32_t w[3];
             const float sg = group_digits(v, w);
             if (lane == 0) a.xsig[t * NG + g] = sg;
-            put_digits(a.xd, g, t, lane, w);
+            put_digits(a.xd, kDigitAtomBytes, g, t, lane, w);
         }
     }
     if (ev && lane == 0) ev[2] = global_timer_ns();
@@ -561,14 +564,45 @@ UOCR_DEV bool read_acc(Pipe& p, int c, int q, int lane, bool want_sig, AccRead& 
 UOCR_DEV void fold_s8(const AccRead& r, int g, const float* colsig, float (&acc)[kMaxB]) {
 #pragma unroll
     for (int t = 0; t < kMaxB; ++t)
-        acc[t] = __fmaf_rn(undigit((int)r.v[g][t], (int)r.v[g][8 + t], (int)r.v[g][16 + t]),
+        acc[t] = __fmaf_rn(undigit((int)r.v[g][3 * t], (int)r.v[g][3 * t + 1], (int)r.v[g][3 * t + 2]),
                            __fmul_rn(r.scl[g], colsig[t]), acc[t]);
 }
 // bf16 accumulator (a row block's even or odd items): acc[t] += term-0 column + term-1 column
 UOCR_DEV void fold_bf16(const AccRead& r, float (&acc)[kMaxB]) {
 #pragma unroll
     for (int t = 0; t < kMaxB; ++t)
-        acc[t] = __fadd_rn(acc[t], __fadd_rn(__uint_as_float(r.v[0][t]), __uint_as_float(r.v[0][8 + t])));
+        acc[t] = __fadd_rn(acc[t], __fadd_rn(__uint_as_float(r.v[0][2 * t]), __uint_as_float(r.v[0][2 * t + 1])));
+}
+
+// The down operand of 128-group g of a slot (its h columns [128 g, 128 g + 128) for the slot's cnt
+// entries), by one warp, into the slot's image region
+// (DecodeArgs::himg): int8 digits (3 rows per entry) with their scales (gsig), or bf16 terms (2 rows
+// per entry in each of the group's two 64-element atoms). Four entries' loads are issued before
+// their conversions.
+UOCR_DEV void write_group_image(const DecodeArgs& a, bool i8, int cnt, int base, int g, int SG, int lane) {
+    unsigned char* img = a.himg + (size_t)base * a.I * 4;
+    for (int e0 = 0; e0 < cnt; e0 += 4) {
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int e = e0 + u;
+            if (e < cnt) v[u] = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)(base + e) * a.I + 128 * g + 4 * lane));
+        }
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+            const int e = e0 + u;
+            if (e < cnt) {
+                if (i8) {
+                    uint32_t w[3];
+                    const float sg = group_digits(v[u], w);
+                    if (lane == 0) a.gsig[(size_t)(base + e) * SG + g] = sg;
+                    put_digits(img, (size_t)cnt * 384, g, e, lane, w);
+                } else {
+                    put_terms(img, (size_t)cnt * 256, g, e, lane, v[u]);
+                }
+            }
+        }
+    }
 }
 
 // ======================================================================================
@@ -623,14 +657,27 @@ UOCR_DEV void nan_block(const DecodeArgs& a, int rb, int lane) {
     for (int t = 0; t < a.B; ++t)
         *reinterpret_cast<float4*>(a.out + (size_t)t * a.H + kRowBlock * rb + 4 * lane) = make_float4(nan, nan, nan, nan);
 }
-// `n` more shares of combined column blocks (4 shares a block: one per epilogue warp); the share
-// that completes the call resets the call's words for the next call.
+// `n` more shares of combined column blocks (4 shares a block: one per epilogue warp), counted by
+// lane 0 of the calling warp (every lane calls); the share that completes the call has the warp
+// reset the call's words for the next call.
 // No fence before the count: the call's reads of the words the last count resets (call_fail by
 // acquire loads, the slot counters long before) are ordered before it, and the output stores
 // need no order with it (the kernel's completion publishes them).
-UOCR_DEV void count_combined(const DecodeArgs& a, uint32_t n) {
-    if (atomicAdd(&a.ctl->cdone, n) + n == 4u * (uint32_t)(a.H / kRowBlock)) {
-        for (int s = 0; s < 72; ++s) a.ctl->hdone[s] = 0u;
+// Only the words of the call's nslot slots are reset: the slot counters the call used (hdone, or
+// imgdone and the I/128 group counters per slot).
+UOCR_DEV void count_combined(const DecodeArgs& a, uint32_t n, int lane, int nslot, bool img_call) {
+    int last = 0;
+    if (lane == 0) last = atomicAdd(&a.ctl->cdone, n) + n == 4u * (uint32_t)(a.H / kRowBlock);
+    if (!__shfl_sync(0xffffffffu, last, 0)) return;
+    const int NG3 = a.I / 128;
+    if (img_call) {
+        for (int i = lane; i < nslot; i += 32) a.ctl->imgdone[i] = 0u;
+        for (int i = lane; i < nslot * NG3; i += 32) a.ctl->gcnt[(i / NG3) * kDecodeMaxGroups + i % NG3] = 0u;
+    } else {
+        for (int i = lane; i < nslot; i += 32) a.ctl->hdone[i] = 0u;
+    }
+    __syncwarp();
+    if (lane == 0) {
         a.ctl->call_fail = 0u;
         __threadfence();
         atomicExch(&a.ctl->cdone, 0u);
@@ -652,6 +699,11 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                       uint32_t off_img, uint32_t off_stages) {
     extern __shared__ __align__(1024) unsigned char smem[];
     __shared__ int abort_flag, stale, routed;
+    // 128-groups whose gate/up arrivals this CTA's epilogue completed, handed to the stagers in
+    // order (a slot << 8 | group | 1 << 31 word each; 0 = not yet posted), and the epilogue warps
+    // done with their gate/up units
+    __shared__ uint32_t jobs[kMaxJobs];
+    __shared__ int njobs, a_warps_done;
     __shared__ uint32_t tmem_base, cta_fail;  // cta_fail: this CTA's failure code (published at exit)
     __shared__ Units units;
     uint32_t* fail = &cta_fail;
@@ -672,7 +724,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
     AccMeta* accm = reinterpret_cast<AccMeta*>(smem + off_acc);
     CombineSmem* cs = reinterpret_cast<CombineSmem*>(smem + off_cs);
     float* xsig = reinterpret_cast<float*>(smem + off_sig);
-    float* hsig = reinterpret_cast<float*>(smem + off_hsig);  // [2][8][I / 128]
+    float* hsig = reinterpret_cast<float*>(smem + off_hsig);  // [2][8][sig stride]
     unsigned char* xb = smem + off_img;                       // phase A: bf16 terms image
     unsigned char* xd = smem + off_img + (size_t)a.H * 32;    // phase A: int8 digits image
     unsigned char* hb = smem + off_img;                       // phase B: two run images of I * 32 bytes
@@ -680,7 +732,13 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
     const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
     const int NG3 = a.I / 128, nrb = a.H / kRowBlock;
     const uint32_t img_bytes = (uint32_t)a.I * 32;
-    const uint32_t hd_target = 4u * (uint32_t)(a.I / 64) + (uint32_t)a.hold_extra;
+    const int SG = decode_sig_stride(a.I);  // floats per row of the digit scales
+    const uint32_t hd_target = 4u * (uint32_t)(a.I / 64) + (uint32_t)a.hold_extra;  // gate/up arrivals per slot
+    const uint32_t ig_target = (uint32_t)NG3 + (uint32_t)a.hold_extra;             // written 128-groups per slot
+    // How this call makes the down operands (measured per batch): B = 8, and bf16 layers from B = 4,
+    // build each slot's image once during the gate/up phase (image warp) and bulk-copy it; smaller
+    // batches have the stagers convert each run's h rows at the phase change.
+    const bool img_call = a.B >= 8 || (!a.int8 && a.B >= 4);
     unsigned long long* ev = a.trace ? trace_rec(a, 0, a.trace_items / 2 - 1) : nullptr;
     if (ev && tid == 0) ev[0] = global_timer_ns();
     if (smem_addr(smem) & 1023u) {  // the swizzled operands need 1024-byte alignment (same in every CTA)
@@ -700,12 +758,14 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
         mbar_init(mdone, 2);  // both MMA warps' commits
         mbar_init(adone, 2);
         for (int b = 0; b < 2; ++b) {
-            mbar_init(&hready[b], 2);  // the 2 stager warps
+            mbar_init(&hready[b], img_call ? 1 : 2);  // warp 2 with a copied run's bytes, or both stagers
             mbar_init(&bfree[b], 2);   // both MMA warps' commits
         }
         mbar_init(ubar, 4);
         mbar_init(imb, 1);
         abort_flag = 0;
+        njobs = 0;
+        a_warps_done = 0;
         stale = 0;
         routed = 0;
         cta_fail = 0;
@@ -722,6 +782,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
     }
     if (warp == 0) tmem_alloc(&tmem_base, kTmemCols);
     load_shared_slots(tb, a, tid, blockDim.x);
+    for (int i = tid; i < kMaxJobs; i += blockDim.x) jobs[i] = 0u;
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
@@ -953,7 +1014,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                         for (int g = 0; g < at; ++g) {
                             float sig[kMaxB];
 #pragma unroll
-                            for (int t = 0; t < kMaxB; ++t) sig[t] = hsig[(b * kMaxB + t) * NG3 + 2 * ki + g];
+                            for (int t = 0; t < kMaxB; ++t) sig[t] = hsig[(b * kMaxB + t) * SG + 2 * ki + g];
                             acc_scales(pipe, j, g, scl + g * kRowBlock, sig, lane);
                         }
                         publish_acc(pipe, j, lane);
@@ -1004,13 +1065,54 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             __syncwarp();
             if (ev && lane == 0) ev[3] = global_timer_ns();
         } else if (warp <= 3) {
-            // ---------------- stagers: each slot run's h rows -> its operand image ----------------
-            // runs in the producer's order; run r uses image r % 2; hready completes after 2 arrivals
+            // ---------------- stagers (warps 2-3) ----------------
+            // Gate/up phase, warp 3 (the image warp): takes the 128-groups of many-entry slots this
+            // CTA's epilogue completed, in the order it posted them, writes each group's image and
+            // counts it, until every epilogue warp is past its gate/up units and no posted group is left.
+            bool ok = routed != 0;
+            if (warp == 3 && img_call) {
+                int next = 0;
+                uint64_t t0 = 0;
+                for (uint32_t spin = 0; ok; ++spin) {
+                    uint32_t job = 0;
+                    if (next < kMaxJobs) job = ld_acquire_cta_u32(&jobs[next]);
+                    if (job) {
+                        const int slot = (int)((job >> 8) & 0xFFu), g = (int)(job & 0xFFu);
+                        write_group_image(a, slot >= a.S && a.int8, tb->count[slot], tb->base[slot], g, SG, lane);
+                        __syncwarp();
+                        if (lane == 0) red_release_gpu_add(&a.ctl->imgdone[slot], 1u);
+                        ++next;
+                        continue;
+                    }
+                    if (ld_acquire_cta_u32(&a_warps_done) == 4u) {
+                        if (next >= kMaxJobs || ld_acquire_cta_u32(&jobs[next]) == 0u) break;
+                        continue;
+                    }
+                    if ((spin & 31) == 0) {
+                        int give_up = 0;
+                        if (lane == 0) {
+                            const uint64_t now = global_timer_ns();
+                            if (t0 == 0) t0 = now;
+                            const bool aborted = *reinterpret_cast<volatile int*>(&abort_flag) != 0;
+                            give_up = aborted || now - t0 > kWaitBudgetNs;
+                            if (give_up && !aborted) set_status(fail, kStatusWaitTimeout);
+                        }
+                        if (__shfl_sync(0xffffffffu, give_up, 0)) ok = false;
+                    }
+                    __nanosleep(64);
+                }
+            }
+            // Down runs in the producer's order; run r uses image r % 2. Once the image region is free:
+            //   img_call:  warp 2, when every 128-group image of the slot is written, posts the bytes
+            //              on hready and bulk-copies the slot's groups (int8: digits, then the
+            //              scales) or atoms (bf16);
+            //   otherwise: both warps, when every CTA's gate/up units of the slot are counted, turn
+            //              its h rows (L2) into int8 digit rows and their scales, or bf16 terms, and
+            //              arrive on hready.
             const int rank = warp - 2;
             unsigned long long* sv = a.trace ? trace_rec(a, 1, a.trace_items / 2 - 3) : nullptr;
             int r = 0, prev = -1;
-            bool ok = routed != 0;
-            for (int i = 0; i < units.nb && ok; ++i) {
+            for (int i = 0; i < units.nb && ok && (!img_call || warp == 2); ++i) {
                 int slot, rb;
                 unit_b(units, a, i, slot, rb);
                 if (slot == prev) continue;
@@ -1021,47 +1123,67 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                 if (r < 2) ok = mbar_wait_warp(adone, 0, &abort_flag, fail);
                 else ok = mbar_wait_warp(&bfree[b], ((r - 2) >> 1) & 1, &abort_flag, fail);
                 if (tv) tv[0] = global_timer_ns();
-                // every CTA's gate/up units of the slot are counted (their h rows written)
-                if (ok) {
+                if (!ok) break;
+                const int cnt = tb->count[slot], base = tb->base[slot];
+                const bool i8 = slot >= a.S && a.int8, bulk = img_call;
+                unsigned char* img = hb + (size_t)b * img_bytes;
+                {
                     int done = 0;
-                    if (lane == 0) done = wait_counter_geq(&a.ctl->hdone[slot], hd_target, fail);
+                    if (lane == 0)
+                        done = wait_counter_geq(bulk ? &a.ctl->imgdone[slot] : &a.ctl->hdone[slot], bulk ? ig_target : hd_target,
+                                                fail);
                     ok = __shfl_sync(0xffffffffu, done, 0) != 0;
                 }
                 if (!ok) break;
                 if (tv) tv[1] = global_timer_ns();
-                const int cnt = tb->count[slot], base = tb->base[slot];
-                const bool i8 = slot >= a.S && a.int8;
-                unsigned char* img = hb + (size_t)b * img_bytes;
-                const int ntask = cnt * NG3;
-                for (int t0 = rank; t0 < ntask; t0 += 4 * 2) {
-                    float4 v[4];  // four tasks' loads issued before any of their stores
-#pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int task = t0 + u * 2;
-                        if (task < ntask) {
-                            const int e = task / NG3, g = task - e * NG3;
-                            v[u] = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)(base + e) * a.I + 128 * g + 4 * lane));
-                        }
+                if (bulk) {
+                    const int nparts = i8 ? NG3 : 2 * NG3;  // 128-groups (int8) or 64-element atoms (bf16)
+                    const uint32_t part = (uint32_t)cnt * (i8 ? 384u : 256u);
+                    const uint32_t sbytes = i8 ? (uint32_t)(cnt * SG * 4) : 0u;
+                    const unsigned char* src = a.himg + (size_t)base * a.I * 4;
+                    if (lane == 0) {
+                        fence_proxy_async_global();  // the image warps' generic writes, read next by bulk copies
+                        fence_proxy_async_smem();    // this region's earlier generic writes and reads
+                        mbar_arrive_expect_tx(&hready[b], (uint32_t)nparts * part + sbytes);
                     }
+                    __syncwarp();
+                    for (int q = lane; q < nparts; q += 32)
+                        bulk_g2s(img + (size_t)q * (i8 ? kDigitAtomBytes : kTermAtomBytes), src + (size_t)q * part, part,
+                                 &hready[b]);
+                    if (lane == 31 && sbytes)
+                        bulk_g2s(hsig + b * kMaxB * SG, a.gsig + (size_t)base * SG, sbytes, &hready[b]);
+                } else {
+                    const int ntask = cnt * NG3;
+                    for (int t0 = rank; t0 < ntask; t0 += 4 * 2) {
+                        float4 v[4];  // four tasks' loads issued before any of their stores
 #pragma unroll
-                    for (int u = 0; u < 4; ++u) {
-                        const int task = t0 + u * 2;
-                        if (task < ntask) {
-                            const int e = task / NG3, g = task - e * NG3;
-                            if (i8) {
-                                uint32_t w[3];
-                                const float sg = group_digits(v[u], w);
-                                if (lane == 0) hsig[(b * kMaxB + e) * NG3 + g] = sg;
-                                put_digits(img, g, e, lane, w);
-                            } else {
-                                put_terms(img, g, e, lane, v[u]);
+                        for (int u = 0; u < 4; ++u) {
+                            const int task = t0 + u * 2;
+                            if (task < ntask) {
+                                const int e = task / NG3, g = task - e * NG3;
+                                v[u] = __ldcg(reinterpret_cast<const float4*>(a.h + (size_t)(base + e) * a.I + 128 * g + 4 * lane));
+                            }
+                        }
+#pragma unroll
+                        for (int u = 0; u < 4; ++u) {
+                            const int task = t0 + u * 2;
+                            if (task < ntask) {
+                                const int e = task / NG3, g = task - e * NG3;
+                                if (i8) {
+                                    uint32_t w[3];
+                                    const float sg = group_digits(v[u], w);
+                                    if (lane == 0) hsig[(b * kMaxB + e) * SG + g] = sg;
+                                    put_digits(img, kDigitAtomBytes, g, e, lane, w);
+                                } else {
+                                    put_terms(img, kTermAtomBytes, g, e, lane, v[u]);
+                                }
                             }
                         }
                     }
+                    fence_proxy_async_smem();  // generic writes of the image, read next by the tensor cores
+                    __syncwarp();
+                    if (lane == 0) mbar_arrive(&hready[b]);
                 }
-                fence_proxy_async_smem();  // generic writes of the image, read next by the tensor cores
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&hready[b]);
                 if (tv) tv[2] = global_timer_ns();
                 ++r;
             }
@@ -1074,8 +1196,14 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
             for (int t = 0; t < kMaxB; ++t) acc[t] = 0.0f;
             int ia = 0, ib = 0;  // units of each phase counted so far (in the partition's order)
             const uint32_t yd_target = 4u * (uint32_t)tb->nslot;
-            bool ok = routed != 0;
+            bool ok = routed != 0, a_signalled = false;
             for (int c = 0; ok; ++c) {
+                if (!a_signalled && ia == units.na) {
+                    // this warp's gate/up units are done (jobs posted): the stagers may move on
+                    a_signalled = true;
+                    __syncwarp();
+                    if (lane == 0) st_release_cta_add(&a_warps_done, 1);
+                }
                 AccRead r;
                 if (!read_acc(pipe, c, q, lane, true, r)) break;
                 if (r.flags & 1) {
@@ -1106,7 +1234,18 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                         acc[t] = 0.0f;
                     }
                     __syncwarp();
-                    if (lane == 0) red_release_gpu_add(&a.ctl->hdone[r.slot], 1u);
+                    if (!img_call) {
+                        // counted; the down phase's stagers make this slot's operand
+                        if (lane == 0) red_release_gpu_add(&a.ctl->hdone[r.slot], 1u);
+                    } else if (lane == 0) {
+                        // the arrival that completes the slot's 128-group hands the group to the image warp
+                        const int g = r.rb >> 1;
+                        if (atom_acq_rel_gpu_add(&a.ctl->gcnt[r.slot * kDecodeMaxGroups + g], 1u) + 1u == 8u) {
+                            const int j = atomicAdd(&njobs, 1);
+                            if (j < kMaxJobs) st_release_cta_u32(&jobs[j], (1u << 31) | ((uint32_t)r.slot << 8) | (uint32_t)g);
+                            else set_status(fail, kStatusBadCount);
+                        }
+                    }
                     ++ia;
                 } else {
                     // down unit done: y rows; the arrival that completes the column block has this
@@ -1137,7 +1276,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                             __syncwarp();
                             nan_block(a, r.rb, lane);
                             __syncwarp();
-                            if (lane == 0) count_combined(a, 4u);
+                            count_combined(a, 4u, lane, tb->nslot, img_call);
                         }
                         ok = false;
                         break;
@@ -1148,7 +1287,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                         const bool failed = ld_acquire_gpu(&a.ctl->call_fail) != 0u;
                         combine_block(a, cs, (req & 255) - 1, failed, ie);
                         __syncwarp();
-                        if (lane == 0) count_combined(a, 1u);
+                        count_combined(a, 1u, lane, tb->nslot, img_call);
                     }
                 }
             }
@@ -1164,8 +1303,13 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                     unit_a(units, a, ia, slot, rb);
                     if (lane == 0) {
                         __threadfence();
-                        atomicAdd(&a.ctl->hdone[slot], 1u);
+                        // a group this completes is counted written (the call fails: its image is not used)
+                        if (!img_call) atomicAdd(&a.ctl->hdone[slot], 1u);
+                        else if (atomicAdd(&a.ctl->gcnt[slot * kDecodeMaxGroups + (rb >> 1)], 1u) + 1u == 8u)
+                            atomicAdd(&a.ctl->imgdone[slot], 1u);
                     }
+                __syncwarp();
+                if (!a_signalled && lane == 0) st_release_cta_add(&a_warps_done, 1);
                 }
                 for (; ib < units.nb; ++ib) {
                     int slot, rb;
@@ -1179,7 +1323,7 @@ decode_experts_kernel(DecodeArgs a, int nst, uint32_t stage_bytes, uint32_t off_
                     if (__shfl_sync(0xffffffffu, last, 0)) {
                         nan_block(a, rb, lane);
                         __syncwarp();
-                        if (lane == 0) count_combined(a, 4u);
+                        count_combined(a, 4u, lane, tb->nslot, img_call);
                     }
                 }
             }
@@ -1262,7 +1406,7 @@ cudaError_t launch_decode_layer(const DecodeArgs& a_in, cudaStream_t st) {
     const size_t off_cs = off_acc + up(sizeof(AccMeta) * kAccSlots, 128);
     const size_t off_sig = off_cs + up(sizeof(CombineSmem), 128);
     const size_t off_hsig = off_sig + up(sizeof(float) * kMaxB * (a.H / 128), 128);
-    const size_t off_img = up(off_hsig + sizeof(float) * 2 * kMaxB * (a.I / 128), 1024);
+    const size_t off_img = up(off_hsig + sizeof(float) * 2 * kMaxB * decode_sig_stride(a.I), 1024);
     // phase A: the bf16 terms image, then the int8 digits image; phase B: two run images (bf16 runs
     // need I * 32 bytes, int8 runs I * 24 + 1 KB)
     const size_t img = std::max((size_t)a.H * 32 + (a.int8 ? (size_t)(a.H / 128) * kDigitAtomBytes + kDigitPadBytes : 0),

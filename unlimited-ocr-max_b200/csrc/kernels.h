@@ -27,24 +27,38 @@ cudaError_t launch_route(const float* x, int T, int H, const uint16_t* wg, int E
 //              until the host reads and clears it (uocr_moe_device_status, which also zeroes the
 //              rest of this block). While it is set, every call writes NaN and touches no counter.
 //   call_fail  this call failed somewhere (set before the failing CTA counts its remaining units).
-//   hdone[s]   gate/up units of slot s finished (4 epilogue warps each: 4 * I/64 per slot).
+//   hdone[s]   calls with B < 8 (int8) or B < 4 (bf16): gate/up units of slot s finished (4 epilogue
+//              warps each: 4 * I/64 per slot); the down phase's stagers then turn the slot's h rows
+//              into its operand themselves.
+//   gcnt[s][g] the other calls: gate/up arrivals for the 128-group g of slot s's h columns
+//              (4 epilogue warps x the group's 2 units); the arrival that completes it hands the
+//              group to its CTA's image warp, which writes the group's down-operand image (int8
+//              digits and scales, or bf16 terms) and counts it on imgdone[s] (I/128 per slot when
+//              done). The down phase copies such a slot's image in bulk.
 //   ydone[rb]  down units of output column block rb finished (4 per unit, 4 * slots in all): the
 //              arrival that completes a block has its CTA combine it (or write it NaN).
-//   cdone      combined column blocks (4 per block); the last resets hdone, call_fail and itself,
-//              so every call starts from zero (ydone[rb] is reset by the block's completing arrival).
+//   cdone      combined column blocks (4 per block); the last resets hdone, gcnt, imgdone, call_fail and
+//              itself, so every call starts from zero (ydone[rb] is reset by the block's completing
+//              arrival).
+constexpr int kDecodeMaxGroups = 16;  // 128-element groups of the intermediate size (I <= 2048)
+// floats per row of the decode digit scales (the 128-groups of I, rounded up to 16 bytes)
+__host__ __device__ inline int decode_sig_stride(int I) { return ((I / 128 + 3) / 4) * 4; }
 struct DecodeCtl {
     uint32_t status;
     uint32_t call_fail;
     uint32_t cdone;
     uint32_t pad0[5];
-    uint32_t hdone[72];
-    uint32_t ydone[64];
-    uint32_t pad1[112];
+    uint32_t hdone[72];                       // per slot (small batches): gate/up arrivals (4 per unit)
+    uint32_t imgdone[72];                     // per slot (B = 8; bf16 from B = 4): its written 128-group images
+    uint32_t ydone[64];                       // per output column block: down units written
+    uint32_t gcnt[72 * kDecodeMaxGroups];     // per slot and 128-group (same calls): gate/up arrivals
+    uint32_t pad1[2048 - 8 - 72 - 72 - 64 - 72 * kDecodeMaxGroups];
 };
 // Bytes at the start of a workspace the host clears along with its status word: the whole decode
 // control block; prefill and exchange workspaces keep their status word at the start of a status
 // region of the same size.
-constexpr size_t kCtlClearBytes = 1024;
+constexpr size_t kCtlClearBytes = 8192;
+static_assert(sizeof(DecodeCtl) == kCtlClearBytes, "the decode control block is the cleared region");
 constexpr int kDecodeMaxShared = 8;
 constexpr int kDecodeMaxTopk = 8;
 
@@ -61,6 +75,12 @@ struct DecodeArgs {
     const uint16_t* w2_shared;
     float* h;       // [(k+S)*B, I], slot-contiguous rows (shared slot q: rows qB..qB+B-1, routed slots after)
     float* y;       // [(k+S)*B, H], slot-contiguous rows
+    // The down operand of each slot, written once per call during the gate/up phase: the slot's
+    // image region starts at byte base * I * 4 (base = its first row); int8 slots hold I / 128
+    // groups of 3c rows x 128 B (c = the slot's entries), bf16 slots I / 64 atoms of 2c rows x
+    // 128 B, rows as in shared memory (decode.cu: put_digits, put_terms)
+    unsigned char* himg;
+    float* gsig;    // [(k+S)*B, decode_sig_stride(I)]: digit scales of the int8 slots' rows per 128-group
     float* out;     // [B, H]
     DecodeCtl* ctl;
     float* logits;       // [8][64][8] router logit partials (token, expert, segment)
@@ -69,12 +89,12 @@ struct DecodeArgs {
     float* xsig;         // [8][H / 128] scales of the digit groups
     unsigned long long* trace;  // optional per-CTA item timeline (diagnostics), null = off
     int trace_items;            // items recorded per CTA
-    int hold_extra;             // test hook: the down phase waits for this many more gate/up arrivals per slot
+    int hold_extra;             // test hook: the down phase waits for this many more operand groups per slot
 };
 // diagnostics: the trace buffer the next decode launches record into (capi.cu)
 extern unsigned long long* g_decode_trace;
 extern size_t g_decode_trace_bytes;
-// test hook: gate/up arrivals per slot the next decode launches' down phase waits for on top of the
+// test hook: operand groups per slot the next decode launches' down phase waits for on top of the
 // real ones (capi.cu)
 extern int g_decode_wait_extra;
 cudaError_t launch_decode_layer(const DecodeArgs& a, cudaStream_t st);

@@ -33,6 +33,19 @@ UOCR_DEV void mbar_init(uint64_t* bar, uint32_t count) {
 }
 UOCR_DEV void fence_mbar_init() { asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory"); }
 UOCR_DEV void fence_proxy_async_smem() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
+UOCR_DEV void fence_proxy_async_global() { asm volatile("fence.proxy.async.global;" ::: "memory"); }
+// Shared-memory words handed between the warps of a CTA: release stores and adds, acquire loads.
+UOCR_DEV void st_release_cta_u32(uint32_t* p, uint32_t v) {
+    asm volatile("st.release.cta.shared::cta.u32 [%0], %1;" ::"r"(smem_addr(p)), "r"(v) : "memory");
+}
+UOCR_DEV void st_release_cta_add(int* p, int v) {
+    asm volatile("red.release.cta.shared::cta.add.s32 [%0], %1;" ::"r"(smem_addr(p)), "r"(v) : "memory");
+}
+UOCR_DEV uint32_t ld_acquire_cta_u32(const void* p) {
+    uint32_t v;
+    asm volatile("ld.acquire.cta.shared::cta.u32 %0, [%1];" : "=r"(v) : "r"(smem_addr(p)) : "memory");
+    return v;
+}
 
 UOCR_DEV void mbar_arrive(uint64_t* bar) {
     asm volatile("{\n\t.reg .b64 st;\n\tmbarrier.arrive.shared::cta.b64 st, [%0];\n\t}" ::"r"(smem_addr(bar)) : "memory");
