@@ -352,7 +352,7 @@ def prefill_e2e(torch, moe, x, out, steps, warmup):
 
 #: DRAM bytes (read + write) of one ncu-captured decode_experts_kernel launch over the layer's
 #: algorithmic bytes (an ncu section capture of layer 0 of the 4-layer int8 B = 8 stack)
-TRAFFIC_RATIO = 145.63 / 145.29
+TRAFFIC_RATIO = 145.26 / 145.29
 
 #: kernels one prefill call launches: route, histogram, scan, scatter, gather, 2 GEMMs, combine
 #: (+ 2 dequant passes for int8 stacks)
@@ -791,10 +791,10 @@ def run_ours(args):
                          "peak_source": peak_src, "scope": "whole decode layer step (route+experts+combine)",
                          "algorithmic_bytes_per_step": step_bytes,
                          # an estimate: the step's algorithmic bytes x the DRAM / algorithmic ratio of
-                         # one captured experts-kernel launch (145.63 MB / 145.29 MB, layer 0 of the
+                         # one captured experts-kernel launch (145.26 MB / 145.29 MB, layer 0 of the
                          # 4-layer stack)
                          "traffic": round(step_bytes * TRAFFIC_RATIO),
-                         "traffic_source": "estimate: algorithmic bytes x 1.0023, the DRAM/algorithmic ratio "
+                         "traffic_source": "estimate: algorithmic bytes x 0.9998, the DRAM/algorithmic ratio "
                                            "of one ncu-captured decode_experts_kernel launch"},
             "e2e": {"value": world * B * L / (e2e_ms * 1e-3), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms},
