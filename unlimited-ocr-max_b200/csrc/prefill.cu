@@ -10,7 +10,7 @@
 //              A operand of both shared experts
 //   GEMM1      per group (64 routed experts + S shared): [rows, H] x w13[e]^T -> 2I packed gate|up
 //              columns, SwiGLU in the epilogue -> h[rows, I] bf16
-//   GEMM2      per group: [rows, I] x w2[e]^T -> y[rows, H] fp32
+//   GEMM2      per group: [rows, I] x w2[e]^T -> y[rows, H], rounded to bf16
 //   combine    out[t] = sum_s w[t,s] * y[dest(t,s)] + sum_q y[shared q, t] (fixed order)
 //
 // GEMM: persistent CTAs, one per SM; warp 0 issues TMA loads of A (128 x 64) and B (256 x 64)
@@ -251,32 +251,40 @@ __global__ void __launch_bounds__(256) prefill_dequant_kernel(const unsigned cha
 
 // out[t][j] (+)= sum_s w[t,s] * y[dest[t*k+s]][j] (entries without an expert skipped)
 //              + sum_q y[kT + q*T + t][j]                     (S shared experts)
-__global__ void __launch_bounds__(256) prefill_combine_kernel(const float* __restrict__ y, const float* __restrict__ wts,
+// (y is bf16; each thread 8 columns, the rows' 16-byte loads issued before the sums)
+__global__ void __launch_bounds__(256) prefill_combine_kernel(const uint16_t* __restrict__ y, const float* __restrict__ wts,
                                                               const int* __restrict__ dest, int T, int H, int topk,
                                                               int S, int accumulate, float* __restrict__ out) {
     const int t = blockIdx.x;
     const int kT = topk * T;
-    for (int j = threadIdx.x * 4; j < H; j += blockDim.x * 4) {
-        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-        if (accumulate) acc = *reinterpret_cast<const float4*>(out + (size_t)t * H + j);
+    for (int j = threadIdx.x * 8; j < H; j += blockDim.x * 8) {
+        float acc[8];
+        if (accumulate) {
+            const float4 a0 = *reinterpret_cast<const float4*>(out + (size_t)t * H + j);
+            const float4 a1 = *reinterpret_cast<const float4*>(out + (size_t)t * H + j + 4);
+            acc[0] = a0.x; acc[1] = a0.y; acc[2] = a0.z; acc[3] = a0.w;
+            acc[4] = a1.x; acc[5] = a1.y; acc[6] = a1.z; acc[7] = a1.w;
+        } else {
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = 0.0f;
+        }
         for (int s = 0; s < topk; ++s) {
             const int d = dest[t * topk + s];
             if (d < 0) continue;
             const float w = wts[t * topk + s];
-            const float4 v = *reinterpret_cast<const float4*>(y + (size_t)d * H + j);
-            acc.x = __fmaf_rn(w, v.x, acc.x);
-            acc.y = __fmaf_rn(w, v.y, acc.y);
-            acc.z = __fmaf_rn(w, v.z, acc.z);
-            acc.w = __fmaf_rn(w, v.w, acc.w);
+            float v[8];
+            unpack_bf16x8(*reinterpret_cast<const uint4*>(y + (size_t)d * H + j), v);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = __fmaf_rn(w, v[i], acc[i]);
         }
         for (int q = 0; q < S; ++q) {
-            const float4 v = *reinterpret_cast<const float4*>(y + (size_t)(kT + q * T + t) * H + j);
-            acc.x = __fadd_rn(acc.x, v.x);
-            acc.y = __fadd_rn(acc.y, v.y);
-            acc.z = __fadd_rn(acc.z, v.z);
-            acc.w = __fadd_rn(acc.w, v.w);
+            float v[8];
+            unpack_bf16x8(*reinterpret_cast<const uint4*>(y + (size_t)(kT + q * T + t) * H + j), v);
+#pragma unroll
+            for (int i = 0; i < 8; ++i) acc[i] = __fadd_rn(acc[i], v[i]);
         }
-        *reinterpret_cast<float4*>(out + (size_t)t * H + j) = acc;
+        *reinterpret_cast<float4*>(out + (size_t)t * H + j) = make_float4(acc[0], acc[1], acc[2], acc[3]);
+        *reinterpret_cast<float4*>(out + (size_t)t * H + j + 4) = make_float4(acc[4], acc[5], acc[6], acc[7]);
     }
 }
 
@@ -286,7 +294,7 @@ __global__ void __launch_bounds__(256) prefill_combine_kernel(const float* __res
 // buffer, partial slot `rank`, row r. The grid's last CTA then sets every rank q's part_flag[rank]
 // to (epoch << 1) | fail, fail when slot q's rows were not processed (its wait failed, or its count
 // was refused) or a bounded wait of these products gave up (`status`).
-__global__ void __launch_bounds__(256) ep_partials_kernel(const float* __restrict__ y, const float* __restrict__ wts,
+__global__ void __launch_bounds__(256) ep_partials_kernel(const uint16_t* __restrict__ y, const float* __restrict__ wts,
                                                           const int* __restrict__ dest, int topk, EpPeers P,
                                                           size_t part_off, size_t sig_off,
                                                           const int* __restrict__ slot_counts,
@@ -302,9 +310,8 @@ __global__ void __launch_bounds__(256) ep_partials_kernel(const float* __restric
                 const int d = dest[n * topk + s];
                 if (d < 0) continue;
                 const float w = wts[n * topk + s];
-                const float4 v0 = *reinterpret_cast<const float4*>(y + (size_t)d * H + j);
-                const float4 v1 = *reinterpret_cast<const float4*>(y + (size_t)d * H + j + 4);
-                const float v[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+                float v[8];
+                unpack_bf16x8(*reinterpret_cast<const uint4*>(y + (size_t)d * H + j), v);
 #pragma unroll
                 for (int i = 0; i < 8; ++i) acc[i] = __fmaf_rn(w, v[i], acc[i]);
             }
@@ -342,7 +349,7 @@ constexpr uint32_t kBTile = kBN * kBK * 2;  // 32 KB
 constexpr int kGemmThreads = 192;           // producer, MMA, 4 epilogue warps
 constexpr uint32_t kTmemCols = 512;         // two 256-column accumulators
 
-enum GemmEpi : int { kEpiSwiGLU = 0, kEpiF32 = 1 };
+enum GemmEpi : int { kEpiSwiGLU = 0, kEpiY = 1 };  // GEMM1: SwiGLU -> bf16 h; GEMM2: bf16 y
 constexpr uint32_t kPlanBytes = (sizeof(PrefillPlan) + 127) & ~127u;
 
 // byte offset of 16-byte chunk `ch` of row `row` in a 32 x 128-byte staging buffer
@@ -436,19 +443,30 @@ UOCR_DEV void gemm_epilogue_tile(uint32_t taddr, const PrefillGroup& G, int mloc
                 __syncwarp();
             }
         } else {
+            // y rounded to bf16: chunk c's 32 columns are half a 128-byte row segment, written out
+            // every second chunk
+            uint32_t pk[16];
 #pragma unroll
-            for (int v = 0; v < 8; ++v)
-                st_shared_v4(stage + stage_off(lane, v), rc[4 * v], rc[4 * v + 1], rc[4 * v + 2], rc[4 * v + 3]);
-            __syncwarp();
-            float* y0 = reinterpret_cast<float*>(out) + (size_t)n * kBN + c * 32;
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                const int row = i * 4 + (lane >> 3), ch = lane & 7;
-                const uint4 v = ld_shared_v4(stage + stage_off(row, ch));
-                if (quarter * 32 + row < rows_valid)
-                    *reinterpret_cast<uint4*>(y0 + (tile_row0 + row) * out_ld + ch * 4) = v;
+            for (int i = 0; i < 16; ++i) {
+                const __nv_bfloat162 yv = __floats2bfloat162_rn(__uint_as_float(rc[2 * i]), __uint_as_float(rc[2 * i + 1]));
+                pk[i] = *reinterpret_cast<const uint32_t*>(&yv);
             }
-            __syncwarp();
+            const int q = 4 * (c & 1);
+#pragma unroll
+            for (int v = 0; v < 4; ++v)
+                st_shared_v4(stage + stage_off(lane, q + v), pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+            if (c & 1) {
+                __syncwarp();
+                uint16_t* y0 = reinterpret_cast<uint16_t*>(out) + (size_t)n * kBN + (c >> 1) * 64;
+#pragma unroll
+                for (int i = 0; i < 8; ++i) {
+                    const int row = i * 4 + (lane >> 3), ch = lane & 7;
+                    const uint4 v = ld_shared_v4(stage + stage_off(row, ch));
+                    if (quarter * 32 + row < rows_valid)
+                        *reinterpret_cast<uint4*>(y0 + (tile_row0 + row) * out_ld + ch * 8) = v;
+                }
+                __syncwarp();
+            }
         }
     }
 }
@@ -820,7 +838,7 @@ static cudaError_t launch_gemm(int epi, const CUtensorMap& A, const CUtensorMap&
     cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
     const size_t smem = gemm_smem_bytes();
     const void* fn = epi == kEpiSwiGLU ? reinterpret_cast<const void*>(grouped_gemm_kernel<kEpiSwiGLU>)
-                                       : reinterpret_cast<const void*>(grouped_gemm_kernel<kEpiF32>);
+                                       : reinterpret_cast<const void*>(grouped_gemm_kernel<kEpiY>);
     cudaError_t err = ensure_smem_optin(fn, smem);
     if (err != cudaSuccess) return err;
     int grid = std::max(1, std::min(sms, max_tiles));
@@ -829,7 +847,7 @@ static cudaError_t launch_gemm(int epi, const CUtensorMap& A, const CUtensorMap&
         grouped_gemm_kernel<kEpiSwiGLU><<<grid, kGemmThreads, smem, st>>>(A, B, Bs, plan, NT, KT, b_rows_per_group, out,
                                                                          out_ld, status);
     else
-        grouped_gemm_kernel<kEpiF32><<<grid, kGemmThreads, smem, st>>>(A, B, Bs, plan, NT, KT, b_rows_per_group, out,
+        grouped_gemm_kernel<kEpiY><<<grid, kGemmThreads, smem, st>>>(A, B, Bs, plan, NT, KT, b_rows_per_group, out,
                                                                       out_ld, status);
     return cudaGetLastError();
 }
@@ -844,7 +862,7 @@ static cudaError_t launch_gemm_pair(int epi, const CUtensorMap& A, const CUtenso
                                     int out_ld, int max_pair_tiles, int max_ctas, uint32_t* status, cudaStream_t st) {
     const size_t smem = gemm_pair_smem_bytes();
     const void* fn = epi == kEpiSwiGLU ? reinterpret_cast<const void*>(grouped_gemm_pair_kernel<kEpiSwiGLU>)
-                                       : reinterpret_cast<const void*>(grouped_gemm_pair_kernel<kEpiF32>);
+                                       : reinterpret_cast<const void*>(grouped_gemm_pair_kernel<kEpiY>);
     cudaError_t err = ensure_smem_optin(fn, smem);
     if (err != cudaSuccess) return err;
     cudaLaunchAttribute attr[1];
@@ -877,7 +895,7 @@ static cudaError_t launch_gemm_pair(int epi, const CUtensorMap& A, const CUtenso
         err = cudaLaunchKernelEx(&cfg, grouped_gemm_pair_kernel<kEpiSwiGLU>, A, B, Bs, plan, NT, KT, b_rows_per_group,
                                  out, out_ld, status);
     else
-        err = cudaLaunchKernelEx(&cfg, grouped_gemm_pair_kernel<kEpiF32>, A, B, Bs, plan, NT, KT, b_rows_per_group, out,
+        err = cudaLaunchKernelEx(&cfg, grouped_gemm_pair_kernel<kEpiY>, A, B, Bs, plan, NT, KT, b_rows_per_group, out,
                                  out_ld, status);
     if (err != cudaSuccess) return err;
     return cudaGetLastError();
@@ -916,7 +934,7 @@ PrefillLayout prefill_layout(int T, int H, int I, int E, int S, int topk, bool i
     d.src_tok = off; off += al(sizeof(int) * kT);
     d.xperm = off; off += al(sizeof(uint16_t) * (kT + T) * H);
     d.h = off; off += al(sizeof(uint16_t) * (kT + (size_t)S * T) * I);
-    d.y = off; off += al(sizeof(float) * (kT + (size_t)S * T) * H);
+    d.y = off; off += al(sizeof(uint16_t) * (kT + (size_t)S * T) * H);
     d.w13 = d.w2 = 0;
     if (int8) {
         d.w13 = off; off += al(sizeof(uint16_t) * (size_t)E * 2 * I * H);
@@ -942,7 +960,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& 
     int* n_valid = reinterpret_cast<int*>(ws + d.n_valid);
     uint16_t* xperm = reinterpret_cast<uint16_t*>(ws + d.xperm);
     uint16_t* h = reinterpret_cast<uint16_t*>(ws + d.h);
-    float* y = reinterpret_cast<float*>(ws + d.y);
+    uint16_t* y = reinterpret_cast<uint16_t*>(ws + d.y);
     uint32_t* status = a.status ? a.status : reinterpret_cast<uint32_t*>(ws + d.status);
     const int cap = a.peers ? a.peers->cap : 1;
     const int* slots = a.peers ? a.slot_counts : nullptr;
@@ -1011,14 +1029,14 @@ cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& 
         err = launch_gemm_pair(kEpiSwiGLU, mA1, pB1, pBs1, plan1, (2 * I) / kBN, H / kBK, 2 * I, h, I,
                                max_pairs * ((2 * I) / kBN), a.max_ctas, status, st);
         if (err != cudaSuccess) return err;
-        err = launch_gemm_pair(kEpiF32, mA2, pB2, pBs2, plan2, H / kBN, I / kBK, H, y, H, max_pairs * (H / kBN),
+        err = launch_gemm_pair(kEpiY, mA2, pB2, pBs2, plan2, H / kBN, I / kBK, H, y, H, max_pairs * (H / kBN),
                                a.max_ctas, status, st);
         if (err != cudaSuccess) return err;
     } else {
         err = launch_gemm(kEpiSwiGLU, mA1, mB1, mBs1, plan1, (2 * I) / kBN, H / kBK, 2 * I, h, I,
                           max_mtiles * ((2 * I) / kBN), a.max_ctas, status, st);
         if (err != cudaSuccess) return err;
-        err = launch_gemm(kEpiF32, mA2, mB2, mBs2, plan2, H / kBN, I / kBK, H, y, H, max_mtiles * (H / kBN), a.max_ctas,
+        err = launch_gemm(kEpiY, mA2, mB2, mBs2, plan2, H / kBN, I / kBK, H, y, H, max_mtiles * (H / kBN), a.max_ctas,
                           status, st);
         if (err != cudaSuccess) return err;
     }
@@ -1028,7 +1046,8 @@ cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& 
                                               status, a.done);
         return cudaGetLastError();
     }
-    prefill_combine_kernel<<<T, 256, 0, st>>>(y, wts, dest, T, H, k, S, a.accumulate, a.out);
+    prefill_combine_kernel<<<T, std::min(256, (H / 8 + 31) / 32 * 32), 0, st>>>(y, wts, dest, T, H, k, S, a.accumulate,
+                                                                                 a.out);
     return cudaGetLastError();
 }
 
