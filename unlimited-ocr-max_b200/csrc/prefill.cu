@@ -65,38 +65,60 @@ __global__ void __launch_bounds__(kChunk) prefill_hist_kernel(const int32_t* __r
 }
 
 // One CTA: per expert, exclusive prefix of the chunk histograms; the group tables of both GEMMs.
-__global__ void __launch_bounds__(64) prefill_scan_kernel(const int* __restrict__ chunk_counts, int nchunks, int E,
-                                                          int S, int T, int topk, int* __restrict__ chunk_base,
-                                                          PrefillPlan* __restrict__ plan1,
-                                                          PrefillPlan* __restrict__ plan2, int* __restrict__ n_valid) {
+// Thread (part, e): expert e over a 1/kScanParts slice of the chunks (the slices' loads in flight at
+// once), the slices' sums combined per expert, then the experts' prefix by two warp scans.
+constexpr int kScanThreads = 1024, kScanParts = kScanThreads / 64;
+__global__ void __launch_bounds__(kScanThreads) prefill_scan_kernel(const int* __restrict__ chunk_counts, int nchunks,
+                                                                    int E, int S, int T, int topk,
+                                                                    int* __restrict__ chunk_base,
+                                                                    PrefillPlan* __restrict__ plan1,
+                                                                    PrefillPlan* __restrict__ plan2,
+                                                                    int* __restrict__ n_valid) {
     // n_valid[0]: routed entries with an expert; n_valid[32 + e]: entries of expert e
+    __shared__ int psum[kScanParts][64];
     __shared__ int total[64];
     __shared__ int base[65];
-    const int e = threadIdx.x;
+    __shared__ int half0;  // experts 0-31's entries
+    const int e = threadIdx.x & 63, part = threadIdx.x >> 6, lane = threadIdx.x & 31;
+    const int per = (nchunks + kScanParts - 1) / kScanParts;
+    const int c0 = min(nchunks, part * per), c1 = min(nchunks, c0 + per);
     int sum = 0;
     if (e < E)
-        for (int c = 0; c < nchunks; ++c) sum += chunk_counts[c * 64 + e];
-    total[e] = e < E ? sum : 0;
-    n_valid[32 + e] = total[e];
+        for (int c = c0; c < c1; ++c) sum += chunk_counts[c * 64 + e];
+    psum[part][e] = sum;
     __syncthreads();
-    if (e == 0) {
-        int acc = 0;
-        for (int i = 0; i < 64; ++i) {
-            base[i] = acc;
-            acc += total[i];
+    int tot = 0, incl = 0;
+    if (threadIdx.x < 64) {
+        for (int q = 0; q < kScanParts; ++q) tot += psum[q][e];
+        total[e] = tot;
+        n_valid[32 + e] = tot;
+        incl = tot;
+#pragma unroll
+        for (int off = 1; off < 32; off <<= 1) {
+            const int v = __shfl_up_sync(0xffffffffu, incl, off);
+            if (lane >= off) incl += v;
         }
-        base[64] = acc;
-        *n_valid = acc;  // routed entries with an expert: rows [0, acc) of the permuted A
+        if (e == 31) half0 = incl;
+    }
+    __syncthreads();
+    if (threadIdx.x < 64) {
+        const int excl = incl - tot + (e >= 32 ? half0 : 0);
+        base[e] = excl;
+        if (e == 63) {
+            base[64] = excl + tot;
+            *n_valid = excl + tot;  // routed entries with an expert: rows [0, n) of the permuted A
+        }
     }
     __syncthreads();
     if (e < E) {
         int acc = base[e];
-        for (int c = 0; c < nchunks; ++c) {
+        for (int q = 0; q < part; ++q) acc += psum[q][e];
+        for (int c = c0; c < c1; ++c) {
             chunk_base[c * 64 + e] = acc;
             acc += chunk_counts[c * 64 + e];
         }
     }
-    if (e == 0) {
+    if (threadIdx.x == 0) {
         const int kT = topk * T;
         int ng = 0, mt = 0;
         for (int g = 0; g < E + S; ++g) {
@@ -971,7 +993,7 @@ cudaError_t launch_prefill(const PrefillArgs& a, char* ws, const PrefillLayout& 
         if (err != cudaSuccess) return err;
     }
     if (nchunks > 0) prefill_hist_kernel<<<nchunks, kChunk, 0, st>>>(ids, kT, E, k, slots, cap, chunk_counts);
-    prefill_scan_kernel<<<1, 64, 0, st>>>(chunk_counts, nchunks, E, S, T, k, chunk_base, plan1, plan2, n_valid);
+    prefill_scan_kernel<<<1, kScanThreads, 0, st>>>(chunk_counts, nchunks, E, S, T, k, chunk_base, plan1, plan2, n_valid);
     if (nchunks > 0)
         prefill_scatter_kernel<<<nchunks, kChunk, 0, st>>>(ids, kT, E, k, slots, cap, chunk_base, dest, src_tok);
     const int grows = kT + (S ? T : 0);
