@@ -55,10 +55,11 @@ def parse():
     p.add_argument("--ep-steps", type=int, default=10, help="timed steps of the expert-parallel ride-along")
     p.add_argument("--settle", type=float, default=1.5,
                    help="seconds of untimed replays before timing, while the clock sampler runs")
-    p.add_argument("--workload", choices=["decode", "prefill", "ep"], default="decode",
+    p.add_argument("--workload", choices=["decode", "prefill", "ep", "quant"], default="decode",
                    help="decode: configs[1]/[3] int8 B=8 decode stack (the headline); "
                         "prefill: configs[2] bf16 prefill of 4096 tokens; "
-                        "ep: configs[4] expert-parallel prefill of --ep-tokens over the ranks")
+                        "ep: configs[4] expert-parallel prefill of --ep-tokens over the ranks; "
+                        "quant: the int8 checkpoint quantiser over one MoE layer's routed experts")
     p.add_argument("--ep-tokens", type=int, default=65536, help="EP prefill tokens over all ranks (configs[4])")
     p.add_argument("--ep-overlap", choices=["on", "off"], default="on",
                    help="EP: run the shared experts on a side stream during the exchanges (on) or in line (off)")
@@ -459,6 +460,61 @@ class CpuPrefill:
         return self.T * n / el, self.cores, sample
 
 
+# the int8 checkpoint quantiser: one MoE layer's routed experts, 3 x E x (I x H) bf16 elements
+def quant_row(torch, uocr, device, steps: int, warmup: int) -> dict:
+    """``uocr_quantize_int8_g128`` over one layer's 192 expert projections (440 MB of bf16, far above
+    the 126 MB L2), timed with CUDA events on the launching stream. Algorithmic bytes per element:
+    2 read + 1 written, plus 4 per 128-element group."""
+    gen = torch.Generator(device=device).manual_seed(4000)
+    rows, k = 3 * E * I, H
+    w = (torch.randn((rows, k), generator=gen, device=device) * 0.02).to(torch.bfloat16)
+    q = torch.empty((rows, k), dtype=torch.int8, device=device)
+    s = torch.empty((rows, k // 128), dtype=torch.float32, device=device)
+    flag = torch.zeros(1, dtype=torch.int32, device=device)
+    lib, st = uocr.load(), torch.cuda.current_stream(device)
+
+    def call():
+        code = lib.uocr_quantize_int8_g128(w.data_ptr(), 1, rows, k, q.data_ptr(), s.data_ptr(), flag.data_ptr(),
+                                           st.cuda_stream)
+        if code:
+            raise RuntimeError(lib.uocr_last_error().decode())
+
+    for _ in range(warmup):
+        call()
+    torch.cuda.synchronize()
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(st)
+    for _ in range(steps):
+        call()
+    t1.record(st)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / steps
+    nbytes = rows * k * 3 + rows * (k // 128) * 4
+    peak, peak_src = measured_peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    assert int(flag.item()) == 0
+    return {"value": gbs, "unit": "GB/s", "ms": ms, "bytes_per_call": nbytes, "frac": gbs / peak,
+            "peak_source": peak_src, "elements": rows * k, "launches_per_call": 1,
+            "what": f"{rows} x {k} bf16 -> int8 + fp32 scales (G=128), one MoE layer's routed experts"}
+
+
+def run_quant(args, torch, uocr, device):
+    """--workload quant: the quantiser as the headline line (a profiling target)."""
+    sampler = ClockSampler(physical_gpu_index(int(os.environ.get("LOCAL_RANK", "0"))))
+    sampler.start()
+    r = quant_row(torch, uocr, device, args.steps, max(args.warmup, 3))
+    clocks = sampler.stop()
+    print(json.dumps({
+        "metric": "int8 checkpoint quantisation GB/s (algorithmic bytes)", "value": r["value"], "unit": "GB/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": r["ms"],
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16 -> int8",
+        "data": "synthetic N(0,0.02) bf16 weights",
+        "config": {"workload": r["what"], "l2": "440 MB input >> 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": r["value"], "peak": measured_peaks()[0], "unit": "GB/s",
+                     "frac": r["frac"], "peak_source": r["peak_source"], "traffic": None},
+        "gpu_launches": args.steps, "clocks": clocks}), flush=True)
+
+
 def run_prefill(args, torch, uocr, synth, dist, world, rank, device):
     """one bf16 MoE layer over 4096 tokens with an N(0, 1) expert bias (int8 routed
     experts with --prefill-int8)."""
@@ -711,6 +767,13 @@ def run_ours(args):
         dist.barrier()
         dist.destroy_process_group()
         return
+    if args.workload == "quant":
+        if rank == 0:
+            run_quant(args, torch, uocr, device)
+        if dist:
+            dist.barrier()
+            dist.destroy_process_group()
+        return
     if args.workload == "prefill":
         run_prefill(args, torch, uocr, synth, dist, world, rank, device)
         if dist:
@@ -755,6 +818,7 @@ def run_ours(args):
             r = prefill_row(torch, uocr, synth, int8, args.tokens, psteps, max(args.warmup // 4, 3), dist, device, 3000)
             r["value"] *= world
             subs[f"prefill_{'int8' if int8 else 'bf16'}_{args.tokens}"] = r
+        subs["quantize_int8_layer"] = quant_row(torch, uocr, device, psteps, 3)
     if not args.no_ep:
         # configs[4] at this N: the expert-parallel prefill over the same ranks (a collective)
         ep = ep_measure(args, torch, uocr, synth, dist, world, rank, device, args.ep_steps, 3, True)

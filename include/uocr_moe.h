@@ -40,6 +40,9 @@ enum {
     UOCR_EUNSUPPORTED = 4 /* a configuration this build does not implement */
 };
 
+/* Element types of the entry points that take more than one (uocr_quantize_int8_g128). */
+enum { UOCR_DTYPE_F32 = 0, UOCR_DTYPE_BF16 = 1 };
+
 /* Thread-local message of the last failed call on this thread ("" if none). */
 UOCR_API const char* uocr_last_error(void);
 /* ABI version of this header (bumped on any signature change). */
@@ -88,6 +91,16 @@ UOCR_API int uocr_dense_bf16_qmv(float* out, int64_t out_rows, int64_t out_cols,
                         const float* x, int64_t x_rows, int64_t x_cols,
                         const uint16_t* w, int64_t w_kb, int64_t w_n, int64_t w_blk,
                         int tile, uocr_stream_t stream);
+
+/* quantize_per_group: the symmetric per-group int8 format of the int8 checkpoint, on the device.
+ * w is [rows, K] row-major, fp32 (w_dtype UOCR_DTYPE_F32) or bf16 (UOCR_DTYPE_BF16), K a multiple
+ * of 128; per 128-element group along K: amax = max|w|, scale = amax / 127 in fp32 (1.0 for an
+ * all-zero group), q = clip(rint(w / scale), -127, 127) with rint half to even; q int8 [rows, K],
+ * scales fp32 [rows, K/128]. Bit-identical to the reference tool's numpy arithmetic. A NaN or Inf
+ * element sets *nonfinite (a device int the caller zeroes and reads; the reference refuses such a
+ * weight). Replaces quantize_per_group, tools/quantize_int8.py:298-329. */
+UOCR_API int uocr_quantize_int8_g128(const void* w, int w_dtype, int64_t rows, int64_t K,
+                            int8_t* q, float* scales, int* nonfinite, uocr_stream_t stream);
 
 /* ------------------------------------------------------------------------------------ *
  * The MoE sublayer (MoE.decode_rows / MoE.__call__, unlimited_ocr_max/decoder.py:641-667).

@@ -5,8 +5,11 @@ not a Python identifier). Public surface:
 
 * ``MoEConfig``, ``UocrMoE`` -- the reference's ``MoE`` module surface (decoder.py:517-667);
 * ``ops`` -- the reference's custom ops ``moe_bf16_qmv``, ``moe_int8_qmv``,
-  ``int8_dequant_expert``, ``dense_bf16_qmv`` and the gate ``route``;
+  ``int8_dequant_expert``, ``dense_bf16_qmv``, the gate ``route`` and the int8 quantiser
+  ``quantize_per_group``;
 * ``ep`` -- ``ExpertParallelMoE``, the prefill with routed experts sharded over GPUs;
+* ``checkpoint`` -- safetensors reading and writing, ``load_moe_layer`` (one decoder layer's MoE
+  from the model file) and ``quantize_checkpoint`` (the int8 checkpoint, quantised on the GPU);
 * ``synth`` -- seeded synthetic weights and activations of the benchmark configs;
 * ``build`` -- compiles ``libuocr_moe.so`` in-tree.
 """

@@ -193,6 +193,24 @@ int uocr_dense_bf16_qmv(float* out, int64_t out_rows, int64_t out_cols, const fl
     return cuda_status(cudaGetLastError(), "dense_bf16_qmv: launch");
 }
 
+int uocr_quantize_int8_g128(const void* w, int w_dtype, int64_t rows, int64_t K, int8_t* q, float* scales,
+                            int* nonfinite, uocr_stream_t stream) {
+    // tools/quantize_int8.py:298-329 (quantize_per_group) and its refusals
+    if (w_dtype != UOCR_DTYPE_F32 && w_dtype != UOCR_DTYPE_BF16)
+        return fail(UOCR_EINVAL, "quantize_per_group: the weight must be fp32 or bf16 (dtype code %d)", w_dtype);
+    if (rows < 0 || K < 0) return fail(UOCR_EINVAL, "quantize_per_group: negative shape [%lld, %lld]",
+                                       (long long)rows, (long long)K);
+    if (K % 128) return fail(UOCR_EINVAL, "K=%lld is not divisible by the group size 128", (long long)K);
+    if (rows == 0 || K == 0) return ok();
+    if (!w || !q || !scales || !nonfinite) return fail(UOCR_EINVAL, "quantize_per_group: null pointer");
+    if (rows > INT64_MAX / K) return fail(UOCR_EUNSUPPORTED, "quantize_per_group: size overflows int64");
+    const bool bf16 = w_dtype == UOCR_DTYPE_BF16;
+    const bool vec = (reinterpret_cast<uintptr_t>(w) & 15) == 0 && (reinterpret_cast<uintptr_t>(q) & 7) == 0;
+    const long long groups = static_cast<long long>(rows) * (K / 128);
+    return cuda_status(uocr::launch_quantize_g128(w, bf16, groups, q, scales, nonfinite, vec, S(stream)),
+                       "quantize_per_group: launch");
+}
+
 // ---------------------------------------------------------------------------------------
 // packing
 // ---------------------------------------------------------------------------------------

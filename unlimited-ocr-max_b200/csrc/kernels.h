@@ -17,6 +17,11 @@ void launch_int8_dequant(uint16_t* out, const int8_t* w, const float* scales, co
 void launch_dense_bf16_qmv(float* out, const float* x, const uint16_t* w, int M, int N, int K, bool vec,
                            cudaStream_t st);
 
+// quant.cu: `groups` consecutive 128-element groups of w (bf16 or fp32) -> int8 q + one fp32 scale per
+// group; *nonfinite |= 1 if any element is NaN or Inf. `vec`: w 16-byte and q 8-byte aligned.
+cudaError_t launch_quantize_g128(const void* w, bool bf16, long long groups, int8_t* q, float* scales,
+                                 int* nonfinite, bool vec, cudaStream_t st);
+
 // route.cu
 cudaError_t launch_route(const float* x, int T, int H, const uint16_t* wg, int E, const float* bias, int topk,
                          int32_t* ids, float* wts, cudaStream_t st);

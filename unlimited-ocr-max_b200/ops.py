@@ -106,6 +106,52 @@ def dense_bf16_qmv(x: torch.Tensor, w: torch.Tensor, *, tile: int | None = None,
     return out
 
 
+class QuantizeError(RuntimeError):
+    """A refusal of the int8 quantiser, with the reference tool's message
+    (tools/quantize_int8.py:77-78)."""
+
+
+def quantize_per_group(w: torch.Tensor, group: int = 128, *, q: torch.Tensor | None = None,
+                       scales: torch.Tensor | None = None, check_finite: bool = True):
+    """``[..., N, K]`` bf16 or fp32 -> ``(int8 [..., N, K], fp32 [..., N, K / 128])`` on the GPU.
+
+    The symmetric per-group format of tools/quantize_int8.py:298-329 with its exact bits: amax =
+    max|w| per 128 elements along K, scale = amax / 127 (1.0 for an all-zero group), q =
+    clip(rint(w / scale), -127, 127). The reference takes one ``[N, K]`` weight; leading dims
+    here are a stack of them. ``check_finite`` reads the device's non-finite flag (one
+    synchronisation) and refuses a weight holding NaN or Inf as the reference does.
+    """
+    op = "quantize_per_group"
+    _need_cuda(op, w)
+    if w.dtype not in (torch.bfloat16, torch.float32):
+        raise TypeError(f"{op}: w must be bf16 or fp32, got {w.dtype}")
+    if w.dim() < 2:
+        raise QuantizeError(f"expected a 2-D weight, got shape {tuple(w.shape)}")
+    if group != 128:
+        raise ValueError(f"{op}: this build quantises groups of 128, got {group}")
+    k = w.shape[-1]
+    if k % group:
+        raise QuantizeError(f"K={k} is not divisible by the group size {group}")
+    w = w if w.is_contiguous() else w.contiguous()
+    rows = w.numel() // k if k else 0
+    if q is None:
+        q = torch.empty(w.shape, dtype=torch.int8, device=w.device)
+    if scales is None:
+        scales = torch.empty((*w.shape[:-1], k // group), dtype=torch.float32, device=w.device)
+    if q.dtype != torch.int8 or tuple(q.shape) != tuple(w.shape) or not q.is_contiguous():
+        raise ValueError(f"{op}: q must be a contiguous int8 tensor of shape {tuple(w.shape)}")
+    if (scales.dtype != torch.float32 or tuple(scales.shape) != (*w.shape[:-1], k // group)
+            or not scales.is_contiguous()):
+        raise ValueError(f"{op}: scales must be a contiguous fp32 tensor of shape {(*w.shape[:-1], k // group)}")
+    _need_cuda(op, w, q, scales)
+    flag = torch.zeros(1, dtype=torch.int32, device=w.device)
+    check(load().uocr_quantize_int8_g128(w.data_ptr(), 1 if w.dtype == torch.bfloat16 else 0, rows, k,
+                                         q.data_ptr(), scales.data_ptr(), flag.data_ptr(), _stream(w)))
+    if check_finite and int(flag.item()):
+        raise QuantizeError("weight holds NaN or Inf; refusing to quantise it")
+    return q, scales
+
+
 def route(x: torch.Tensor, router: torch.Tensor, bias: torch.Tensor | None = None, top_k: int = 6):
     """MoEGate.__call__ (decoder.py:509-514): ``(ids i32[T,k], weights f32[T,k])`` in score order.
 
