@@ -55,11 +55,12 @@ def parse():
     p.add_argument("--ep-steps", type=int, default=10, help="timed steps of the expert-parallel ride-along")
     p.add_argument("--settle", type=float, default=1.5,
                    help="seconds of untimed replays before timing, while the clock sampler runs")
-    p.add_argument("--workload", choices=["decode", "prefill", "ep", "quant"], default="decode",
+    p.add_argument("--workload", choices=["decode", "prefill", "ep", "quant", "dense"], default="decode",
                    help="decode: configs[1]/[3] int8 B=8 decode stack (the headline); "
                         "prefill: configs[2] bf16 prefill of 4096 tokens; "
                         "ep: configs[4] expert-parallel prefill of --ep-tokens over the ranks; "
-                        "quant: the int8 checkpoint quantiser over one MoE layer's routed experts")
+                        "quant: the int8 checkpoint quantiser over one MoE layer's routed experts; "
+                        "dense: the decode step's dense projections (attention, dense FFN, lm_head) at B=8")
     p.add_argument("--ep-tokens", type=int, default=65536, help="EP prefill tokens over all ranks (configs[4])")
     p.add_argument("--ep-overlap", choices=["on", "off"], default="on",
                    help="EP: run the shared experts on a side stream during the exchanges (on) or in line (off)")
@@ -498,6 +499,83 @@ def quant_row(torch, uocr, device, steps: int, warmup: int) -> dict:
             "what": f"{rows} x {k} bf16 -> int8 + fp32 scales (G=128), one MoE layer's routed experts"}
 
 
+# the decode step's dense projections, distinct weights: per layer (12) q/k/v fused into one
+# [3 x 1280, 1280] stream (one input row) and o [1280, 1280]; the dense FFN of layer 0 with gate|up
+# fused [2 x 6848, 1280] and down [1280, 6848]; lm_head [129280, 1280]
+DENSE_SHAPES = [(3 * H, H), (H, H)] * 12 + [(2 * 6848, H), (H, 6848), (129280, H)]
+
+
+def dense_row(torch, uocr, device, steps: int, warmup: int, B: int = 8) -> dict:
+    """One decode step's dense projections for B rows, one CUDA graph of ``DenseProjection``
+    calls, timed with CUDA events (541 MB of weights per step, far above the 126 MB L2).
+    Algorithmic bytes: every weight (N x K x 2) + the rows in and out (B x (K + N) x 4)."""
+    dense = importlib.import_module(f"{PKG}.dense")
+    gen = torch.Generator(device=device).manual_seed(5000)
+    projs, xs, outs = [], [], []
+    for n, k in DENSE_SHAPES:
+        w = (torch.randn((n, k), generator=gen, device=device) * 0.02).to(torch.bfloat16)
+        projs.append(dense.DenseProjection(k, n, kblocked=False, device=device).load_state_dict({"weight": w}))
+        del w
+        xs.append(torch.randn((B, k), generator=gen, device=device))
+        outs.append(torch.empty((B, n), device=device))
+    torch.cuda.synchronize()
+    s = torch.cuda.Stream(device)
+    s.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(s):
+        for p, x, o in zip(projs, xs, outs):
+            p.decode_rows(x, out=o)
+    torch.cuda.current_stream(device).wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for p, x, o in zip(projs, xs, outs):
+            p.decode_rows(x, out=o)
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    st = torch.cuda.current_stream(device)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(st)
+    for _ in range(steps):
+        g.replay()
+    t1.record(st)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / steps
+    for p in projs:
+        p.check_status()
+    nbytes = sum(n * k * 2 + B * (k + n) * 4 for n, k in DENSE_SHAPES)
+    lm = DENSE_SHAPES[-1]
+    peak, peak_src = measured_peaks()
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    finite = all(bool(torch.isfinite(o).all()) for o in outs)
+    del g
+    return {"value": B / (ms * 1e-3), "unit": "tokens/s", "us_per_step": ms * 1e3, "hbm_gbs": gbs,
+            "frac": gbs / peak, "peak_source": peak_src, "bytes_per_step": nbytes, "launches_per_step": len(projs),
+            "batch": B, "what": f"12 x (q|k|v [{3 * H},{H}] + o [{H},{H}]) attention, gate|up [{2 * 6848},{H}] + "
+                                f"down [{H},6848] dense FFN, [{lm[0]},{lm[1]}] lm_head; bf16 weights, fp32 rows",
+            "outputs_finite": finite}
+
+
+def run_dense(args, torch, uocr, device):
+    """--workload dense: the decode step's dense projections as the headline line (a profiling
+    target)."""
+    sampler = ClockSampler(physical_gpu_index(int(os.environ.get("LOCAL_RANK", "0"))))
+    sampler.start()
+    r = dense_row(torch, uocr, device, args.steps, max(args.warmup, 3), args.batch)
+    clocks = sampler.stop()
+    print(json.dumps({
+        "metric": "decode-step dense projections, tokens/s (B rows per step)", "value": r["value"], "unit": "tokens/s",
+        "n_gpus": 1, "steps": args.steps, "warmup": max(args.warmup, 3), "ms_per_step": r["us_per_step"] / 1e3,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "bf16 weights x fp32 rows (two bf16 terms), fp32 accumulate",
+        "data": "synthetic N(0,0.02) bf16 weights, N(0,1) rows",
+        "config": {"workload": r["what"], "batch": r["batch"], "l2": "541 MB of weights per step >> 126 MB L2"},
+        "roofline": {"bound": "hbm", "achieved": r["hbm_gbs"], "peak": measured_peaks()[0], "unit": "GB/s",
+                     "frac": r["frac"], "peak_source": r["peak_source"], "traffic": None},
+        "gpu_launches": r["launches_per_step"] * args.steps, "clocks": clocks,
+        "outputs_finite": r["outputs_finite"]}), flush=True)
+
+
 def run_quant(args, torch, uocr, device):
     """--workload quant: the quantiser as the headline line (a profiling target)."""
     sampler = ClockSampler(physical_gpu_index(int(os.environ.get("LOCAL_RANK", "0"))))
@@ -767,9 +845,9 @@ def run_ours(args):
         dist.barrier()
         dist.destroy_process_group()
         return
-    if args.workload == "quant":
+    if args.workload in ("quant", "dense"):
         if rank == 0:
-            run_quant(args, torch, uocr, device)
+            (run_quant if args.workload == "quant" else run_dense)(args, torch, uocr, device)
         if dist:
             dist.barrier()
             dist.destroy_process_group()
@@ -819,6 +897,7 @@ def run_ours(args):
             r["value"] *= world
             subs[f"prefill_{'int8' if int8 else 'bf16'}_{args.tokens}"] = r
         subs["quantize_int8_layer"] = quant_row(torch, uocr, device, psteps, 3)
+        subs["decode_projections_b8"] = dense_row(torch, uocr, device, psteps, 3)
     if not args.no_ep:
         # configs[4] at this N: the expert-parallel prefill over the same ranks (a collective)
         ep = ep_measure(args, torch, uocr, synth, dist, world, rank, device, args.ep_steps, 3, True)

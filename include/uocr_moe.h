@@ -92,6 +92,28 @@ UOCR_API int uocr_dense_bf16_qmv(float* out, int64_t out_rows, int64_t out_cols,
                         const uint16_t* w, int64_t w_kb, int64_t w_n, int64_t w_blk,
                         int tile, uocr_stream_t stream);
 
+/* Dense bf16 projections of the decode step (attention q/k/v/o, the dense FFN, lm_head) streamed
+ * through the tensor cores: replaces dense_bf16_qmv (kernels/dense_bf16.mojo:119-158, decoder.py:
+ * 166-184, 236-238) for a weight packed once at load. out[m, n] = sum_k W[n, k] x[m, k], fp32 x
+ * and out, the weight read once per 8 rows; x enters the products as two bf16 terms (to ~2^-17 of
+ * its magnitude), the products accumulate in fp32.
+ *   uocr_dense_packed_bytes(N, K)  size of the packed weight (0 for unsupported dims: N >= 1, K a
+ *                                  positive multiple of 16);
+ *   uocr_dense_pack                W [N, K] bf16 -> packed; `kblocked` = 1 takes the reference's
+ *                                  K-blocked declaration w[k/16, n, k%16] (decoder.py:201-225), 0 a
+ *                                  plain row-major [N, K]; 16-byte-aligned pointers;
+ *   uocr_dense_stream_workspace_bytes(N, K)  workspace of one call on the current device; the
+ *                                  caller zero-fills it once and may reuse it for every later
+ *                                  call of the same (N, K); its status word is read and cleared
+ *                                  by uocr_moe_device_status;
+ *   uocr_dense_stream              x [M, K] fp32 -> out [M, N] fp32, any M >= 0 (8 rows per launch). */
+UOCR_API size_t uocr_dense_packed_bytes(int64_t N, int64_t K);
+UOCR_API int uocr_dense_pack(const uint16_t* w, int kblocked, int64_t N, int64_t K, void* packed,
+                    uocr_stream_t stream);
+UOCR_API size_t uocr_dense_stream_workspace_bytes(int64_t N, int64_t K);
+UOCR_API int uocr_dense_stream(const void* packed, int64_t N, int64_t K, const float* x, int64_t M,
+                      float* out, void* workspace, size_t workspace_bytes, uocr_stream_t stream);
+
 /* quantize_per_group: the symmetric per-group int8 format of the int8 checkpoint, on the device.
  * w is [rows, K] row-major, fp32 (w_dtype UOCR_DTYPE_F32) or bf16 (UOCR_DTYPE_BF16), K a multiple
  * of 128; per 128-element group along K: amax = max|w|, scale = amax / 127 in fp32 (1.0 for an

@@ -65,6 +65,10 @@ SIGNATURES: dict[str, tuple] = {
     "uocr_int8_dequant_expert": (I32, [P, I64, I64, P, I64, I64, I64, P, I64, I64, I64, P, I64, P]),
     "uocr_dense_bf16_qmv": (I32, [P, I64, I64, P, I64, I64, P, I64, I64, I64, I32, P]),
     "uocr_quantize_int8_g128": (I32, [P, I32, I64, I64, P, P, P, P]),
+    "uocr_dense_packed_bytes": (SZ, [I64, I64]),
+    "uocr_dense_pack": (I32, [P, I32, I64, I64, P, P]),
+    "uocr_dense_stream_workspace_bytes": (SZ, [I64, I64]),
+    "uocr_dense_stream": (I32, [P, I64, I64, P, I64, P, P, SZ, P]),
     "uocr_moe_w13_bytes": (SZ, [I64, I64, I64, I64, I32]),
     "uocr_moe_w2_bytes": (SZ, [I64, I64, I64, I64, I32]),
     "uocr_moe_pack_w13": (I32, [P, P, P, P, I64, I64, I64, I64, I32, P, P]),

@@ -212,6 +212,67 @@ int uocr_quantize_int8_g128(const void* w, int w_dtype, int64_t rows, int64_t K,
 }
 
 // ---------------------------------------------------------------------------------------
+// dense projections of the decode step (tensor-core weight streaming)
+// ---------------------------------------------------------------------------------------
+static bool dense_dims_ok(int64_t N, int64_t K) {
+    return N >= 1 && K >= 16 && K % 16 == 0 && N <= (int64_t)INT32_MAX - 128 && K <= (int64_t)INT32_MAX - 128;
+}
+static int current_sms() {
+    int dev = 0, sms = 148;
+    if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    return sms;
+}
+
+size_t uocr_dense_packed_bytes(int64_t N, int64_t K) {
+    if (!dense_dims_ok(N, K)) return 0;
+    const uocr::DensePlan p = uocr::dense_plan(N, K, 1);
+    return (size_t)p.NB * p.IPR * 2 * uocr::kAtomBytes;
+}
+
+int uocr_dense_pack(const uint16_t* w, int kblocked, int64_t N, int64_t K, void* packed, uocr_stream_t stream) {
+    if (!dense_dims_ok(N, K))
+        return fail(UOCR_EINVAL, "dense_pack: need N >= 1 and K a positive multiple of 16 (KBLOCK), got [%lld, %lld]",
+                    (long long)N, (long long)K);
+    if (!w || !packed) return fail(UOCR_EINVAL, "dense_pack: null pointer");
+    if (!a16(w) || !a16(packed)) return fail(UOCR_EINVAL, "dense_pack: w and packed must be 16-byte aligned");
+    return cuda_status(uocr::launch_dense_pack(w, kblocked != 0, (int)N, (int)K, static_cast<unsigned char*>(packed),
+                                               S(stream)),
+                       "dense_pack: launch");
+}
+
+size_t uocr_dense_stream_workspace_bytes(int64_t N, int64_t K) {
+    if (!dense_dims_ok(N, K)) return 0;
+    const uocr::DensePlan p = uocr::dense_plan(N, K, current_sms());
+    return uocr::kCtlClearBytes + (p.KC > 1 ? (size_t)p.KC * 8 * p.NB * 128 * sizeof(float) : 0);
+}
+
+int uocr_dense_stream(const void* packed, int64_t N, int64_t K, const float* x, int64_t M, float* out,
+                      void* workspace, size_t workspace_bytes, uocr_stream_t stream) {
+    if (!dense_dims_ok(N, K))
+        return fail(UOCR_EINVAL, "dense_stream: need N >= 1 and K a positive multiple of 16 (KBLOCK), got [%lld, %lld]",
+                    (long long)N, (long long)K);
+    if (M < 0) return fail(UOCR_EINVAL, "dense_stream: negative row count");
+    if (M == 0) return ok();
+    if (!packed || !x || !out || !workspace) return fail(UOCR_EINVAL, "dense_stream: null pointer");
+    if (!a16(packed) || !a16(workspace)) return fail(UOCR_EINVAL, "dense_stream: packed and workspace must be 16-byte aligned");
+    const uocr::DensePlan p = uocr::dense_plan(N, K, current_sms());
+    const size_t need = uocr_dense_stream_workspace_bytes(N, K);
+    if (workspace_bytes < need)
+        return fail(UOCR_EINVAL, "dense_stream: workspace of %zu bytes, need %zu", workspace_bytes, need);
+    if (p.KC > 1 && p.NB + uocr::kDenseCtlCounters > (int)(uocr::kCtlClearBytes / 4))
+        return fail(UOCR_EUNSUPPORTED, "dense_stream: %d row blocks with split K exceed the control block", p.NB);
+    auto* ctl = static_cast<uint32_t*>(workspace);
+    float* partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + uocr::kCtlClearBytes);
+    for (int64_t m0 = 0; m0 < M; m0 += 8) {
+        const int rows = (int)std::min<int64_t>(8, M - m0);
+        cudaError_t err = uocr::launch_dense_stream(static_cast<const unsigned char*>(packed), (int)N, (int)K,
+                                                    x + m0 * K, rows, out + m0 * N, ctl, partial, p, S(stream));
+        if (err != cudaSuccess) return cuda_status(err, "dense_stream: launch");
+    }
+    return ok();
+}
+
+// ---------------------------------------------------------------------------------------
 // packing
 // ---------------------------------------------------------------------------------------
 

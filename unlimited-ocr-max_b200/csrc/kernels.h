@@ -22,6 +22,20 @@ void launch_dense_bf16_qmv(float* out, const float* x, const uint16_t* w, int M,
 cudaError_t launch_quantize_g128(const void* w, bool bf16, long long groups, int8_t* q, float* scales,
                                  int* nonfinite, bool vec, cudaStream_t st);
 
+// dense.cu: dense bf16 projections of the decode step (M <= 8 rows per launch).
+// Workspace: a control block of kCtlClearBytes (status word at [0], the split-K row-block counters
+// from word kDenseCtlCounters), then the split-K partials [NB][KC][128][8] fp32 when KC > 1.
+constexpr int kDenseMaxChunkItems = 12;  // K items (128 elements) of one CTA's x image
+constexpr int kDenseMaxSplit = 8;        // K chunks of a row block whose partials one summing pass loads at once
+constexpr int kDenseCtlCounters = 16;
+struct DensePlan {
+    int NB, IPR, KC, IPC, Gp, grid;  // row blocks, items per row block, K chunks, items per chunk, CTAs per chunk
+};
+DensePlan dense_plan(long long N, long long K, int sms);
+cudaError_t launch_dense_pack(const uint16_t* w, bool kblocked, int N, int K, unsigned char* out, cudaStream_t st);
+cudaError_t launch_dense_stream(const unsigned char* w, int N, int K, const float* x, int M, float* out,
+                                uint32_t* ctl, float* partial, const DensePlan& p, cudaStream_t st);
+
 // route.cu
 cudaError_t launch_route(const float* x, int T, int H, const uint16_t* wg, int E, const float* bias, int topk,
                          int32_t* ids, float* wts, cudaStream_t st);
