@@ -461,6 +461,39 @@ class CpuPrefill:
         return self.T * n / el, self.cores, sample
 
 
+# the MoE half of the decode step: the headline's 11 layers chained through their RMSNorms and
+# residual adds (h = h + MoE_l(RmsNorm_l(h))), one CUDA graph
+def stack_row(torch, uocr, mods, device, steps: int, warmup: int, B: int, bare_ms: float) -> dict:
+    """``MoEDecodeStack`` over the headline's layers with N(1, 0.1) bf16 norm weights, the step
+    replayed from its CUDA graph and timed with CUDA events; ``vs_bare_layers`` is the headline
+    step's time (the same layers, independent inputs, no norms) over this one."""
+    stack = importlib.import_module(f"{PKG}.stack")
+    gen = torch.Generator(device=device).manual_seed(6000)
+    gammas = [(1 + 0.1 * torch.randn(H, generator=gen, device=device)).to(torch.bfloat16) for _ in mods]
+    st = stack.MoEDecodeStack(mods, gammas)
+    g, h_io = st.graph(B)
+    h_io.copy_(3 * torch.randn((B, H), generator=gen, device=device))
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream(device)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(s)
+    for _ in range(steps):
+        g.replay()
+    t1.record(s)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / steps
+    st.check_status()
+    finite = bool(torch.isfinite(h_io).all())
+    L = len(mods)
+    del g
+    return {"value": B * L / (ms * 1e-3), "unit": "tokens/s", "us_per_layer": ms * 1e3 / L, "ms_per_step": ms,
+            "vs_bare_layers": bare_ms / ms, "launches_per_step": 3 * L + 1, "outputs_finite": finite,
+            "what": f"{L} MoE layers chained: h = h + MoE_l(RmsNorm_l(h)), int8 experts, B={B}, one CUDA graph "
+                    "(each layer's input is the previous layers' output)"}
+
+
 # the int8 checkpoint quantiser: one MoE layer's routed experts, 3 x E x (I x H) bf16 elements
 def quant_row(torch, uocr, device, steps: int, warmup: int) -> dict:
     """``uocr_quantize_int8_g128`` over one layer's 192 expert projections (440 MB of bf16, far above
@@ -872,6 +905,7 @@ def run_ours(args):
     achieved = step_bytes / (ms * 1e-3) / 1e9
     value = world * B * L / (ms * 1e-3)
     e2e_ms, h2d, d2h = time_e2e(torch, g, xs, outs, max(args.steps // 4, 10), 3)
+    stack_sub = None if args.no_sub else stack_row(torch, uocr, mods, device, max(args.steps // 4, 20), 3, B, ms)
     if dist:
         t = torch.tensor([e2e_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -896,6 +930,7 @@ def run_ours(args):
             r = prefill_row(torch, uocr, synth, int8, args.tokens, psteps, max(args.warmup // 4, 3), dist, device, 3000)
             r["value"] *= world
             subs[f"prefill_{'int8' if int8 else 'bf16'}_{args.tokens}"] = r
+        subs["decode_stack_int8_b8"] = stack_sub
         subs["quantize_int8_layer"] = quant_row(torch, uocr, device, psteps, 3)
         subs["decode_projections_b8"] = dense_row(torch, uocr, device, psteps, 3)
     if not args.no_ep:

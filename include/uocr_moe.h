@@ -114,6 +114,14 @@ UOCR_API size_t uocr_dense_stream_workspace_bytes(int64_t N, int64_t K);
 UOCR_API int uocr_dense_stream(const void* packed, int64_t N, int64_t K, const float* x, int64_t M,
                       float* out, void* workspace, size_t workspace_bytes, uocr_stream_t stream);
 
+/* The residual add and the RMSNorm around a MoE sublayer of the decode step, fused: h += add
+ * (skipped if add is NULL), then y = h / sqrt(mean(h^2) + eps) * gamma per row (skipped if y is
+ * NULL); h, add, y fp32 [B, H], gamma fp32 [H] (the bf16 norm weight cast to fp32, as RmsNorm
+ * does). Replaces x + mlp.decode_rows(post_attention_layernorm(x)) around the MoE call,
+ * decoder.py:709, and RmsNorm, decoder.py:252-261 (MAX's rms_norm). */
+UOCR_API int uocr_residual_rmsnorm(float* h, const float* add, const float* gamma, int64_t B, int64_t H,
+                          float eps, float* y, uocr_stream_t stream);
+
 /* quantize_per_group: the symmetric per-group int8 format of the int8 checkpoint, on the device.
  * w is [rows, K] row-major, fp32 (w_dtype UOCR_DTYPE_F32) or bf16 (UOCR_DTYPE_BF16), K a multiple
  * of 128; per 128-element group along K: amax = max|w|, scale = amax / 127 in fp32 (1.0 for an

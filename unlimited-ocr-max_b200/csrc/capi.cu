@@ -272,6 +272,18 @@ int uocr_dense_stream(const void* packed, int64_t N, int64_t K, const float* x, 
     return ok();
 }
 
+int uocr_residual_rmsnorm(float* h, const float* add, const float* gamma, int64_t B, int64_t H, float eps,
+                          float* y, uocr_stream_t stream) {
+    // decoder.py:702-709 (the residual add) and RmsNorm, decoder.py:252-261
+    if (B < 0 || H < 1 || H > INT32_MAX || B > INT32_MAX)
+        return fail(UOCR_EINVAL, "residual_rmsnorm: bad shape [%lld, %lld]", (long long)B, (long long)H);
+    if (!(eps >= 0.f)) return fail(UOCR_EINVAL, "residual_rmsnorm: eps must be >= 0");
+    if (B == 0) return ok();
+    if (!h || (y && !gamma)) return fail(UOCR_EINVAL, "residual_rmsnorm: null pointer");
+    return cuda_status(uocr::launch_residual_rmsnorm(h, add, gamma, (int)B, (int)H, eps, y, S(stream)),
+                       "residual_rmsnorm: launch");
+}
+
 // ---------------------------------------------------------------------------------------
 // packing
 // ---------------------------------------------------------------------------------------
