@@ -494,6 +494,43 @@ def stack_row(torch, uocr, mods, device, steps: int, warmup: int, B: int, bare_m
                     "(each layer's input is the previous layers' output)"}
 
 
+# the no-repeat-n-gram guard on a decode step's logits: B = 8 rows of the checkpoint's 129 280,
+# each against its last 128 ids (the reference's window), n = 35
+def ngram_row(torch, uocr, device, steps: int, warmup: int, B: int = 8, V: int = 129280, Hn: int = 128) -> dict:
+    """``uocr_ngram_block`` in place over ``[B, V]`` fp32 logits, 20 launches per CUDA graph replay,
+    timed with CUDA events. Algorithmic bytes: the logits read and written + the histories."""
+    ops = importlib.import_module(f"{PKG}.ops")
+    gen = torch.Generator(device=device).manual_seed(7000)
+    logits = torch.randn((B, V), generator=gen, device=device)
+    hist = torch.randint(0, V, (B, Hn), generator=gen, device=device, dtype=torch.int32)
+    hist[:, -40:] = hist[:, 20:60]  # a repeated motif: every row has bans
+    n = torch.tensor([35], dtype=torch.int32, device=device)
+    ops.ngram_block(logits, hist, n, out=logits)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(20):
+            ops.ngram_block(logits, hist, n, out=logits)
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream(device)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(s)
+    for _ in range(steps):
+        g.replay()
+    t1.record(s)
+    torch.cuda.synchronize()
+    us = t0.elapsed_time(t1) / (20 * steps) * 1e3
+    nbytes = 2 * B * V * 4 + B * Hn * 4
+    peak, peak_src = measured_peaks()
+    banned = int((logits == -3.0e38).sum())
+    del g
+    return {"value": B / (us * 1e-6), "unit": "tokens/s", "us_per_call": us, "hbm_gbs": nbytes / (us * 1e-6) / 1e9,
+            "frac": nbytes / (us * 1e-6) / 1e9 / peak, "peak_source": peak_src, "banned_logits": banned,
+            "what": f"B={B} x {V} fp32 logits in place, history {Hn} ids per row, n = 35"}
+
+
 # the int8 checkpoint quantiser: one MoE layer's routed experts, 3 x E x (I x H) bf16 elements
 def quant_row(torch, uocr, device, steps: int, warmup: int) -> dict:
     """``uocr_quantize_int8_g128`` over one layer's 192 expert projections (440 MB of bf16, far above
@@ -932,6 +969,7 @@ def run_ours(args):
             subs[f"prefill_{'int8' if int8 else 'bf16'}_{args.tokens}"] = r
         subs["decode_stack_int8_b8"] = stack_sub
         subs["quantize_int8_layer"] = quant_row(torch, uocr, device, psteps, 3)
+        subs["ngram_guard_b8"] = ngram_row(torch, uocr, device, psteps, 3)
         subs["decode_projections_b8"] = dense_row(torch, uocr, device, psteps, 3)
     if not args.no_ep:
         # configs[4] at this N: the expert-parallel prefill over the same ranks (a collective)

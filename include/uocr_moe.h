@@ -114,6 +114,16 @@ UOCR_API size_t uocr_dense_stream_workspace_bytes(int64_t N, int64_t K);
 UOCR_API int uocr_dense_stream(const void* packed, int64_t N, int64_t K, const float* x, int64_t M,
                       float* out, void* workspace, size_t workspace_bytes, uocr_stream_t stream);
 
+/* ngram_block: the no-repeat-n-gram guard on B rows of V fp32 logits. Row b is guarded against
+ * row b of history [B, H] int32 (that request's last H token ids, the newest last): every token
+ * that would complete a repeat of the last n - 1 ids inside the history is set to -3.0e38 in out,
+ * every other logit is copied bit for bit (out may be logits itself). n is read from the device
+ * int32 at `ngram` (so one captured launch serves any n); n < 1, or H < n, bans nothing. One row
+ * is B = 1. Replaces @register("ngram_block"), kernels/ngram_block.mojo:51-151 (staged by
+ * apply_ngram_guard / NgramBlocker, ngram.py:34-104). */
+UOCR_API int uocr_ngram_block(const float* logits, int64_t B, int64_t V, const int32_t* history, int64_t H,
+                     const int32_t* ngram, float* out, uocr_stream_t stream);
+
 /* The residual add and the RMSNorm around a MoE sublayer of the decode step, fused: h += add
  * (skipped if add is NULL), then y = h / sqrt(mean(h^2) + eps) * gamma per row (skipped if y is
  * NULL); h, add, y fp32 [B, H], gamma fp32 [H] (the bf16 norm weight cast to fp32, as RmsNorm

@@ -66,6 +66,7 @@ SIGNATURES: dict[str, tuple] = {
     "uocr_dense_bf16_qmv": (I32, [P, I64, I64, P, I64, I64, P, I64, I64, I64, I32, P]),
     "uocr_quantize_int8_g128": (I32, [P, I32, I64, I64, P, P, P, P]),
     "uocr_residual_rmsnorm": (I32, [P, P, P, I64, I64, ctypes.c_float, P, P]),
+    "uocr_ngram_block": (I32, [P, I64, I64, P, I64, P, P, P]),
     "uocr_dense_packed_bytes": (SZ, [I64, I64]),
     "uocr_dense_pack": (I32, [P, I32, I64, I64, P, P]),
     "uocr_dense_stream_workspace_bytes": (SZ, [I64, I64]),

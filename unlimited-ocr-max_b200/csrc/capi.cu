@@ -272,6 +272,21 @@ int uocr_dense_stream(const void* packed, int64_t N, int64_t K, const float* x, 
     return ok();
 }
 
+int uocr_ngram_block(const float* logits, int64_t B, int64_t V, const int32_t* history, int64_t H,
+                     const int32_t* ngram, float* out, uocr_stream_t stream) {
+    // kernels/ngram_block.mojo:80-105 (its shape checks), semantics :1-33
+    if (B < 0 || V < 0 || B > 65535 || V > INT32_MAX || H > INT32_MAX)
+        return fail(UOCR_EINVAL, "ngram_block: bad shape (B %lld, V %lld, H %lld)", (long long)B, (long long)V,
+                    (long long)H);
+    if (H < 1) return fail(UOCR_EINVAL, "ngram_block: history is empty");
+    if (!ngram) return fail(UOCR_EINVAL, "ngram_block: `ngram` must be a single int32");
+    if (B == 0 || V == 0) return ok();
+    if (!logits || !history || !out) return fail(UOCR_EINVAL, "ngram_block: null pointer");
+    const bool vec = a16(logits) && a16(out) && V % 4 == 0;
+    return cuda_status(uocr::launch_ngram_block(logits, (int)B, (int)V, history, (int)H, ngram, out, vec, S(stream)),
+                       "ngram_block: launch");
+}
+
 int uocr_residual_rmsnorm(float* h, const float* add, const float* gamma, int64_t B, int64_t H, float eps,
                           float* y, uocr_stream_t stream) {
     // decoder.py:702-709 (the residual add) and RmsNorm, decoder.py:252-261

@@ -36,6 +36,10 @@ cudaError_t launch_dense_pack(const uint16_t* w, bool kblocked, int N, int K, un
 cudaError_t launch_dense_stream(const unsigned char* w, int N, int K, const float* x, int M, float* out,
                                 uint32_t* ctl, float* partial, const DensePlan& p, cudaStream_t st);
 
+// ngram.cu: the no-repeat-n-gram guard on B rows of V logits (out may alias logits)
+cudaError_t launch_ngram_block(const float* logits, int B, int V, const int32_t* history, int H, const int32_t* ngram,
+                               float* out, bool vec, cudaStream_t st);
+
 // norm.cu: h += add (if add), then y = RMSNorm(h) * gamma (if y), one CTA per row
 cudaError_t launch_residual_rmsnorm(float* h, const float* add, const float* gamma, int B, int H, float eps, float* y,
                                     cudaStream_t st);

@@ -173,3 +173,30 @@ def route(x: torch.Tensor, router: torch.Tensor, bias: torch.Tensor | None = Non
     check(load().uocr_moe_route(x.data_ptr(), T, H, router.data_ptr(), E, 0 if bias is None else bias.data_ptr(),
                                 top_k, ids.data_ptr(), wts.data_ptr(), _stream(x)))
     return ids, wts
+
+
+def ngram_block(logits: torch.Tensor, history: torch.Tensor, ngram: torch.Tensor,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """``ngram_block(logits f32[V] or [B,V], history i32[H] or [B,H], ngram i32[1])`` (kernels/
+    ngram_block.mojo:51-151): row b's tokens that would repeat an n-gram of row b's history set
+    to -3.0e38, every other logit copied bit for bit. ``out`` may be ``logits`` (in place)."""
+    op = "ngram_block"
+    _need_cuda(op, logits, history, ngram)
+    if logits.dim() not in (1, 2):
+        raise ValueError(f"{op} takes one row (V,) or B rows (B, V), got shape {tuple(logits.shape)}")
+    rank = logits.dim()
+    logits = _need(op, logits, "logits", torch.float32, rank)
+    history = _need(op, history, "history", torch.int32, rank)
+    ngram = _need(op, ngram, "ngram", torch.int32, 1)
+    if ngram.shape[0] != 1:
+        raise ValueError("ngram_block: `ngram` must be a single int32")
+    if rank == 2 and history.shape[0] != logits.shape[0]:
+        raise ValueError("ngram_block: history and logits disagree on the row count")
+    if out is None:
+        out = torch.empty_like(logits)
+    if out.dtype != torch.float32 or out.shape != logits.shape or not out.is_contiguous():
+        raise ValueError("ngram_block: logits and output disagree on shape")
+    B = logits.shape[0] if rank == 2 else 1
+    check(load().uocr_ngram_block(logits.data_ptr(), B, logits.shape[-1], history.data_ptr(), history.shape[-1],
+                                  ngram.data_ptr(), out.data_ptr(), _stream(logits)))
+    return out
