@@ -12,7 +12,9 @@
 // memory, marks in a shared bitmap every banned token that falls in its chunk (the candidate's
 // last token is tested first, so nearly every start costs one comparison), then writes the chunk
 // with the banned entries replaced. n is read from device memory, so a captured launch serves
-// any n (n = 0 switches the guard off). Integer work; bound: HBM (logits read and written once).
+// any n (n = 0 switches the guard off). Integer work; bound: HBM (logits read and written once),
+// in practice launch latency: B = 8 rows of 129 280 logits (8.3 MB) take 4.0 us per launch in a
+// CUDA graph with 2048-logit chunks (512 CTAs), 4.8 us with 8192-logit chunks (128 CTAs).
 #include "common.cuh"
 #include "kernels.h"
 
@@ -20,7 +22,7 @@ namespace uocr {
 namespace {
 
 constexpr int kNgramThreads = 256;
-constexpr int kNgramChunk = 8192;                 // logits per CTA (a 1 KB bitmap)
+constexpr int kNgramChunk = 2048;                 // logits per CTA (a 256 B bitmap)
 constexpr int kNgramMaxSmemHistory = 8192;        // history entries staged in shared memory
 constexpr float kNgramBlocked = -3.0e38f;         // finite: argmax- and softmax-equivalent to -inf
 
