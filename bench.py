@@ -21,6 +21,7 @@ from __future__ import annotations
 import argparse
 import importlib
 import json
+import math
 import os
 import statistics
 import subprocess
@@ -531,6 +532,49 @@ def ngram_row(torch, uocr, device, steps: int, warmup: int, B: int = 8, V: int =
             "what": f"B={B} x {V} fp32 logits in place, history {Hn} ids per row, n = 35"}
 
 
+# paged decode attention at the model's decode shape: B = 8 requests of 512 prompt + 128 ring rows,
+# 10 heads x 128, one layer of a 12-layer fp32 page pool
+def attention_row(torch, uocr, device, steps: int, warmup: int, B: int = 8, rows: int = 640) -> dict:
+    """``uocr_paged_decode_attention`` (store the new rows + attend), 10 launches per CUDA graph
+    replay, timed with CUDA events. Algorithmic bytes: every attended k and v row read once, the
+    new rows stored, q read and out written."""
+    ops = importlib.import_module(f"{PKG}.ops")
+    heads, dim, layers, cols = 10, 128, 12, (rows + 127) // 128
+    gen = torch.Generator(device=device).manual_seed(8000)
+    pages = B * cols + 1
+    pool = torch.randn((pages, 2, layers, 128, heads, dim), generator=gen, device=device)
+    lut = torch.arange(B * cols, dtype=torch.int32, device=device).view(B, cols)
+    q, k, v = (torch.randn((B, heads, dim), generator=gen, device=device) for _ in range(3))
+    wi = torch.full((B,), rows - 1, dtype=torch.int32, device=device)
+    al = torch.full((B,), rows, dtype=torch.int32, device=device)
+    out = torch.empty_like(q)
+    scale = 1.0 / math.sqrt(dim)
+    ops.paged_decode_attention(q, k, v, pool, 5, lut, wi, al, scale, out=out)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        for _ in range(10):
+            ops.paged_decode_attention(q, k, v, pool, 5, lut, wi, al, scale, out=out)
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream(device)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(s)
+    for _ in range(steps):
+        g.replay()
+    t1.record(s)
+    torch.cuda.synchronize()
+    us = t0.elapsed_time(t1) / (10 * steps) * 1e3
+    nbytes = B * rows * heads * dim * 4 * 2 + B * heads * dim * 4 * 4
+    peak, peak_src = measured_peaks()
+    finite = bool(torch.isfinite(out).all())
+    del g, pool
+    return {"value": B / (us * 1e-6), "unit": "tokens/s", "us_per_call": us, "hbm_gbs": nbytes / (us * 1e-6) / 1e9,
+            "frac": nbytes / (us * 1e-6) / 1e9 / peak, "peak_source": peak_src, "outputs_finite": finite,
+            "what": f"B={B} requests x {rows} rows, {heads} heads x {dim}, fp32 page pool of {layers} layers"}
+
+
 # the int8 checkpoint quantiser: one MoE layer's routed experts, 3 x E x (I x H) bf16 elements
 def quant_row(torch, uocr, device, steps: int, warmup: int) -> dict:
     """``uocr_quantize_int8_g128`` over one layer's 192 expert projections (440 MB of bf16, far above
@@ -970,6 +1014,7 @@ def run_ours(args):
         subs["decode_stack_int8_b8"] = stack_sub
         subs["quantize_int8_layer"] = quant_row(torch, uocr, device, psteps, 3)
         subs["ngram_guard_b8"] = ngram_row(torch, uocr, device, psteps, 3)
+        subs["paged_attention_b8"] = attention_row(torch, uocr, device, psteps, 3)
         subs["decode_projections_b8"] = dense_row(torch, uocr, device, psteps, 3)
     if not args.no_ep:
         # configs[4] at this N: the expert-parallel prefill over the same ranks (a collective)

@@ -114,6 +114,23 @@ UOCR_API size_t uocr_dense_stream_workspace_bytes(int64_t N, int64_t K);
 UOCR_API int uocr_dense_stream(const void* packed, int64_t N, int64_t K, const float* x, int64_t M,
                       float* out, void* workspace, size_t workspace_bytes, uocr_stream_t stream);
 
+/* Paged decode attention for B requests, one new token each: replaces paged_decode_attention,
+ * decoder.py:425-437 (MAX's store_k/v_cache_ragged + flash_attention_ragged, causal) over the page
+ * pool of kv_cache.py. Pool kv_pool fp32 [pages][2 (k, v)][layers][128 rows][heads][head_dim]; request
+ * b's logical row r is row r % 128 of page lut[b * lut_cols + r / 128]. The call stores k_new[b] /
+ * v_new[b] ([B][heads][head_dim], post-RoPE) at row write_index[b] of `layer` and writes out[b] =
+ * softmax(q[b] . k^T * scale) v over rows [0, attend_len[b]) (write_index[b] < attend_len[b] <=
+ * lut_cols * 128; page ids past the pool read its last page). head_dim 128, heads <= 12. The
+ * workspace (uocr_paged_attention_workspace_bytes(B, heads, lut_cols) bytes, 16-byte aligned) is
+ * zero-filled once by the caller; its status word is read by uocr_moe_device_status. The result
+ * is deterministic (a fixed combine order). */
+UOCR_API size_t uocr_paged_attention_workspace_bytes(int64_t B, int64_t heads, int64_t lut_cols);
+UOCR_API int uocr_paged_decode_attention(const float* q, const float* k_new, const float* v_new, int64_t B,
+                                int64_t heads, int64_t head_dim, float* kv_pool, int64_t pages,
+                                int64_t layers, int64_t layer, const uint32_t* lut, int64_t lut_cols,
+                                const uint32_t* write_index, const uint32_t* attend_len, float scale,
+                                float* out, void* workspace, size_t workspace_bytes, uocr_stream_t stream);
+
 /* ngram_block: the no-repeat-n-gram guard on B rows of V fp32 logits. Row b is guarded against
  * row b of history [B, H] int32 (that request's last H token ids, the newest last): every token
  * that would complete a repeat of the last n - 1 ids inside the history is set to -3.0e38 in out,

@@ -272,6 +272,44 @@ int uocr_dense_stream(const void* packed, int64_t N, int64_t K, const float* x, 
     return ok();
 }
 
+size_t uocr_paged_attention_workspace_bytes(int64_t B, int64_t heads, int64_t lut_cols) {
+    if (B < 1 || heads < 1 || heads > 12 || lut_cols < 1 || B > 2000 || lut_cols > (1 << 20)) return 0;
+    return uocr::kCtlClearBytes + (size_t)B * lut_cols * 16 * heads * 130 * sizeof(float);
+}
+
+int uocr_paged_decode_attention(const float* q, const float* k_new, const float* v_new, int64_t B, int64_t heads,
+                                int64_t head_dim, float* kv_pool, int64_t pages, int64_t layers, int64_t layer,
+                                const uint32_t* lut, int64_t lut_cols, const uint32_t* write_index,
+                                const uint32_t* attend_len, float scale, float* out, void* workspace,
+                                size_t workspace_bytes, uocr_stream_t stream) {
+    // paged_decode_attention, decoder.py:425-437 (store_k/v_cache_ragged + flash_attention_ragged)
+    if (head_dim != 128) return fail(UOCR_EUNSUPPORTED, "paged_decode_attention: head_dim %lld (this build: 128)",
+                                     (long long)head_dim);
+    if (B < 0 || heads < 1) return fail(UOCR_EINVAL, "paged_decode_attention: bad B or heads");
+    if (heads > 12) return fail(UOCR_EUNSUPPORTED, "paged_decode_attention: %lld heads (this build: <= 12)", (long long)heads);
+    if (pages < 1 || layers < 1 || layer < 0 || layer >= layers || lut_cols < 1)
+        return fail(UOCR_EINVAL, "paged_decode_attention: bad pool (pages %lld, layers %lld, layer %lld, lut_cols %lld)",
+                    (long long)pages, (long long)layers, (long long)layer, (long long)lut_cols);
+    if (B == 0) return ok();
+    if (!q || !k_new || !v_new || !kv_pool || !lut || !write_index || !attend_len || !out || !workspace)
+        return fail(UOCR_EINVAL, "paged_decode_attention: null pointer");
+    if (!a16(q) || !a16(k_new) || !a16(v_new) || !a16(kv_pool) || !a16(out) || !a16(workspace))
+        return fail(UOCR_EINVAL, "paged_decode_attention: q, k_new, v_new, the pool, out and the workspace must be "
+                                 "16-byte aligned");
+    const size_t need = uocr_paged_attention_workspace_bytes(B, heads, lut_cols);
+    if (need == 0 || workspace_bytes < need)
+        return fail(UOCR_EINVAL, "paged_decode_attention: workspace of %zu bytes, need %zu", workspace_bytes, need);
+    auto* ctl = static_cast<uint32_t*>(workspace);
+    float* partial = reinterpret_cast<float*>(static_cast<char*>(workspace) + uocr::kCtlClearBytes);
+    return cuda_status(uocr::launch_paged_decode_attention(q, k_new, v_new, kv_pool, (int)pages, (int)layers, (int)layer,
+                                                           lut, (int)lut_cols, write_index, attend_len, out, (int)B,
+                                                           (int)heads, scale, ctl, partial,
+                                                           uocr::paged_attention_ctas((int)B, (int)lut_cols,
+                                                                                      current_sms()),
+                                                           S(stream)),
+                       "paged_decode_attention: launch");
+}
+
 int uocr_ngram_block(const float* logits, int64_t B, int64_t V, const int32_t* history, int64_t H,
                      const int32_t* ngram, float* out, uocr_stream_t stream) {
     // kernels/ngram_block.mojo:80-105 (its shape checks), semantics :1-33

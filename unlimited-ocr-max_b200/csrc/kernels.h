@@ -36,6 +36,17 @@ cudaError_t launch_dense_pack(const uint16_t* w, bool kblocked, int N, int K, un
 cudaError_t launch_dense_stream(const unsigned char* w, int N, int K, const float* x, int M, float* out,
                                 uint32_t* ctl, float* partial, const DensePlan& p, cudaStream_t st);
 
+// attention.cu: paged decode attention. Workspace: a control block of kCtlClearBytes (status word
+// at [0], per-request counters from word kAttnCtlCounters), then the partials [B][S][heads][130]
+// fp32 (S <= lut_cols x 16 CTAs per request).
+constexpr int kAttnCtlCounters = 16;
+int paged_attention_ctas(int B, int lut_cols, int sms);  // S: CTAs per request
+cudaError_t launch_paged_decode_attention(const float* q, const float* k_new, const float* v_new, float* kv,
+                                          int pages, int layers, int layer, const uint32_t* lut, int lut_cols,
+                                          const uint32_t* write_index, const uint32_t* attend_len, float* out, int B,
+                                          int heads, float scale, uint32_t* ctl, float* partial, int S,
+                                          cudaStream_t st);
+
 // ngram.cu: the no-repeat-n-gram guard on B rows of V logits (out may alias logits)
 cudaError_t launch_ngram_block(const float* logits, int B, int V, const int32_t* history, int H, const int32_t* ngram,
                                float* out, bool vec, cudaStream_t st);

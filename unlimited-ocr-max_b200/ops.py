@@ -200,3 +200,46 @@ def ngram_block(logits: torch.Tensor, history: torch.Tensor, ngram: torch.Tensor
     check(load().uocr_ngram_block(logits.data_ptr(), B, logits.shape[-1], history.data_ptr(), history.shape[-1],
                                   ngram.data_ptr(), out.data_ptr(), _stream(logits)))
     return out
+
+
+_ATTN_WS: dict[tuple, torch.Tensor] = {}
+
+
+def paged_decode_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Tensor, kv_pool: torch.Tensor,
+                           layer: int, lut: torch.Tensor, write_index: torch.Tensor, attend_len: torch.Tensor,
+                           scale: float, out: torch.Tensor | None = None) -> torch.Tensor:
+    """paged_decode_attention (decoder.py:425-437): store each request's new k/v row at its write
+    index of ``layer`` in ``kv_pool`` fp32 ``[pages, 2, layers, 128, heads, 128]`` and attend ``q``
+    ``[B, heads, 128]`` over its rows ``[0, attend_len)`` (``lut`` uint32/int32 ``[B, cols]`` page ids,
+    ``write_index`` / ``attend_len`` ``[B]``). The workspace is kept per (device, B, heads, cols)."""
+    op = "paged_decode_attention"
+    _need_cuda(op, q, k_new, v_new, kv_pool, lut, write_index, attend_len)
+    q = _need(op, q, "q", torch.float32, 3)
+    k_new = _need(op, k_new, "k_new", torch.float32, 3)
+    v_new = _need(op, v_new, "v_new", torch.float32, 3)
+    kv_pool = _need(op, kv_pool, "kv_pool", torch.float32, 6)
+    B, heads, dim = q.shape
+    if k_new.shape != q.shape or v_new.shape != q.shape:
+        raise ValueError(f"{op}: q, k_new and v_new disagree on shape")
+    pages, two, layers, rows, ph, pd = kv_pool.shape
+    if two != 2 or rows != 128 or ph != heads or pd != dim:
+        raise ValueError(f"{op}: the pool must be [pages, 2, layers, 128, {heads}, {dim}], got {tuple(kv_pool.shape)}")
+    for name, t in (("lut", lut), ("write_index", write_index), ("attend_len", attend_len)):
+        if t.dtype not in (torch.int32, torch.uint32):
+            raise TypeError(f"{op}: {name} must be int32 or uint32, got {t.dtype}")
+    lut = lut.contiguous()
+    if lut.dim() != 2 or lut.shape[0] != B or write_index.shape != (B,) or attend_len.shape != (B,):
+        raise ValueError(f"{op}: lut [B, cols], write_index [B] and attend_len [B] expected")
+    if out is None:
+        out = torch.empty_like(q)
+    key = (q.device, B, heads, lut.shape[1])
+    ws = _ATTN_WS.get(key)
+    if ws is None:
+        ws = torch.zeros(load().uocr_paged_attention_workspace_bytes(B, heads, lut.shape[1]), dtype=torch.uint8,
+                         device=q.device)
+        _ATTN_WS[key] = ws
+    check(load().uocr_paged_decode_attention(
+        q.data_ptr(), k_new.data_ptr(), v_new.data_ptr(), B, heads, dim, kv_pool.data_ptr(), pages, layers, layer,
+        lut.data_ptr(), lut.shape[1], write_index.contiguous().data_ptr(), attend_len.contiguous().data_ptr(),
+        float(scale), out.data_ptr(), ws.data_ptr(), ws.numel(), _stream(q)))
+    return out
