@@ -7,10 +7,10 @@
 // [0, attend_len[b]) with scores q.k * scale and a softmax in fp32.
 //
 // Flash-decoding over the rows: S CTAs per request (S = min(sub-chunks, 148 / B)); CTA (s, b) walks
-// the 8-row sub-chunks s, s + S, ... of request b, warp h head h (lane l dims 4l..4l+3). A
+// the 4-row sub-chunks s, s + S, ... of request b, warp h head h (lane l dims 4l..4l+3). A
 // sub-chunk's rows of every head are contiguous in one page, so two bulk copies (k and v, heads x
-// 4 KB each) bring it into one of two shared-memory stages on that stage's mbarrier, the next
-// sub-chunk's copies in flight while the current one is computed; the warp keeps an online softmax
+// 2 KB each) bring it into one of four shared-memory stages on that stage's mbarrier, the next
+// three sub-chunks' copies in flight while the current one is computed; the warp keeps an online softmax
 // (max m, sum l = sum exp(s - m), acc = sum exp(s - m) v) in registers across its sub-chunks and
 // writes it to the workspace at the end. The row at write_index is taken from k_new / v_new once
 // its sub-chunk has landed and stored into the pool by the CTA that owns it (no CTA reads the pool
@@ -25,7 +25,8 @@
 namespace uocr {
 namespace {
 
-constexpr int kAttnSub = 8;       // rows per sub-chunk (one pair of bulk copies)
+constexpr int kAttnSub = 4;       // rows per sub-chunk (one pair of bulk copies)
+constexpr int kAttnStages = 4;    // shared-memory stages (copies in flight while one is computed)
 constexpr int kAttnDim = 128;     // head dim (lane x 4)
 constexpr int kAttnPage = 128;    // rows per page
 constexpr int kAttnCombine = 8;   // partials the combining CTA loads at once
@@ -52,8 +53,8 @@ __device__ __forceinline__ size_t pool_index(const AttnArgs& a, uint32_t page, i
 }
 
 __global__ void paged_decode_attention_kernel(AttnArgs a) {
-    extern __shared__ float4 attn_smem[];  // 2 stages x (k [8][heads][32 float4], v the same)
-    __shared__ uint64_t full[2];
+    extern __shared__ float4 attn_smem[];  // kAttnStages x (k [4][heads][32 float4], v the same)
+    __shared__ uint64_t full[kAttnStages];
     __shared__ int last;
     const int s = blockIdx.x, b = blockIdx.y;
     const int h = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -70,22 +71,20 @@ __global__ void paged_decode_attention_kernel(AttnArgs a) {
     const uint32_t* lut = a.lut + (size_t)b * a.lut_cols;
     const size_t stage_f4 = (size_t)2 * kAttnSub * a.heads * 32;  // float4s per stage (k then v)
 
-    auto issue = [&](int it) {  // thread 0: the copies of this CTA's it-th sub-chunk into stage it & 1
+    auto issue = [&](int it) {  // thread 0: the copies of this CTA's it-th sub-chunk into its stage
         const int r0 = (s + it * a.S) * kAttnSub, nr = min(n_rows, r0 + kAttnSub) - r0;
         const uint32_t page = lut[r0 / kAttnPage];
         const uint32_t bytes = (uint32_t)nr * a.heads * kAttnDim * 4;
-        float4* sk = attn_smem + (it & 1) * stage_f4;
+        float4* sk = attn_smem + (it % kAttnStages) * stage_f4;
         float4* sv = sk + (size_t)kAttnSub * a.heads * 32;
-        mbar_arrive_expect_tx(&full[it & 1], 2 * bytes);
-        bulk_g2s(sk, a.kv + pool_index(a, page, 0, r0 % kAttnPage, 0), bytes, &full[it & 1]);
-        bulk_g2s(sv, a.kv + pool_index(a, page, 1, r0 % kAttnPage, 0), bytes, &full[it & 1]);
+        mbar_arrive_expect_tx(&full[it % kAttnStages], 2 * bytes);
+        bulk_g2s(sk, a.kv + pool_index(a, page, 0, r0 % kAttnPage, 0), bytes, &full[it % kAttnStages]);
+        bulk_g2s(sv, a.kv + pool_index(a, page, 1, r0 % kAttnPage, 0), bytes, &full[it % kAttnStages]);
     };
     if (threadIdx.x == 0) {
-        mbar_init(&full[0], 1);
-        mbar_init(&full[1], 1);
+        for (int st = 0; st < kAttnStages; ++st) mbar_init(&full[st], 1);
         fence_mbar_init();
-        issue(0);
-        if (my_subs > 1) issue(1);
+        for (int it = 0; it < kAttnStages && it < my_subs; ++it) issue(it);
     }
     __syncthreads();
 
@@ -94,11 +93,11 @@ __global__ void paged_decode_attention_kernel(AttnArgs a) {
     bool landed = true;
     for (int it = 0; it < my_subs; ++it) {
         const int r0 = (s + it * a.S) * kAttnSub, nr = min(n_rows, r0 + kAttnSub) - r0;
-        float4* sk = attn_smem + (it & 1) * stage_f4;
+        float4* sk = attn_smem + (it % kAttnStages) * stage_f4;
         float4* sv = sk + (size_t)kAttnSub * a.heads * 32;
         // a wait that gave up (status recorded) leaves the rest of this warp's rows out, but the
         // warp still takes part in the CTA's barriers below
-        if (landed) landed = mbar_wait_warp(&full[it & 1], (it >> 1) & 1, nullptr, a.ctl);
+        if (landed) landed = mbar_wait_warp(&full[it % kAttnStages], (it / kAttnStages) & 1, nullptr, a.ctl);
         const int rows = landed ? nr : 0;
         if (landed && wi >= r0 && wi < r0 + nr) {
             // the new row: into this warp's shared rows (head h), and into the pool
@@ -141,7 +140,7 @@ __global__ void paged_decode_attention_kernel(AttnArgs a) {
             m = mn;
         }
         __syncthreads();  // every warp is done with this stage
-        if (threadIdx.x == 0 && it + 2 < my_subs) issue(it + 2);
+        if (threadIdx.x == 0 && it + kAttnStages < my_subs) issue(it + kAttnStages);
     }
 
     float* part = a.partial + (((size_t)b * a.S + s) * a.heads + h) * (kAttnDim + 2);
@@ -205,7 +204,7 @@ cudaError_t launch_paged_decode_attention(const float* q, const float* k_new, co
     if (B <= 0) return cudaSuccess;
     AttnArgs a{q, k_new, v_new, kv, lut, write_index, attend_len, out, partial, ctl,
                heads, pages, layers, layer, lut_cols, S, scale};
-    const size_t smem = (size_t)2 * 2 * kAttnSub * heads * kAttnDim * 4;
+    const size_t smem = (size_t)kAttnStages * 2 * kAttnSub * heads * kAttnDim * 4;
     cudaError_t err = ensure_smem_optin(reinterpret_cast<const void*>(paged_decode_attention_kernel), smem);
     if (err != cudaSuccess) return err;
     paged_decode_attention_kernel<<<dim3(S, B), 32 * heads, smem, st>>>(a);

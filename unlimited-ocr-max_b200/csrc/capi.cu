@@ -274,7 +274,7 @@ int uocr_dense_stream(const void* packed, int64_t N, int64_t K, const float* x, 
 
 size_t uocr_paged_attention_workspace_bytes(int64_t B, int64_t heads, int64_t lut_cols) {
     if (B < 1 || heads < 1 || heads > 12 || lut_cols < 1 || B > 2000 || lut_cols > (1 << 20)) return 0;
-    return uocr::kCtlClearBytes + (size_t)B * lut_cols * 16 * heads * 130 * sizeof(float);
+    return uocr::kCtlClearBytes + (size_t)B * lut_cols * 32 * heads * 130 * sizeof(float);
 }
 
 int uocr_paged_decode_attention(const float* q, const float* k_new, const float* v_new, int64_t B, int64_t heads,

@@ -38,7 +38,7 @@ cudaError_t launch_dense_stream(const unsigned char* w, int N, int K, const floa
 
 // attention.cu: paged decode attention. Workspace: a control block of kCtlClearBytes (status word
 // at [0], per-request counters from word kAttnCtlCounters), then the partials [B][S][heads][130]
-// fp32 (S <= lut_cols x 16 CTAs per request).
+// fp32 (S <= lut_cols x 32 CTAs per request).
 constexpr int kAttnCtlCounters = 16;
 int paged_attention_ctas(int B, int lut_cols, int sms);  // S: CTAs per request
 cudaError_t launch_paged_decode_attention(const float* q, const float* k_new, const float* v_new, float* kv,
