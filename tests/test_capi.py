@@ -165,3 +165,42 @@ def test_ep_dispatch_combine_refusals(uocr):
     assert lib.uocr_moe_ep_combine(None, 4, None, 16, 0, 1280, None, None, None) == 4 and "world=0" in err()
     assert lib.uocr_moe_ep_combine(None, 4, None, 16, 2, 1280, None, None, None) == 1 and "null" in err()
     assert lib.uocr_moe_ep_combine(None, 0, None, 0, 2, 1280, None, None, None) == 0
+
+
+def test_widening_entry_points_refuse_before_any_launch(uocr):
+    """The quantiser, dense stream, norm, n-gram guard and paged attention check their arguments on
+    the host (null device pointers are fine: nothing is launched)."""
+    lib = uocr.load()
+    rc, err = _null_call(lib, "uocr_quantize_int8_g128", None, 1, 4, 200, None, None, None, None)
+    assert rc == 1 and err == "K=200 is not divisible by the group size 128"
+    rc, err = _null_call(lib, "uocr_quantize_int8_g128", None, 7, 4, 256, None, None, None, None)
+    assert rc == 1 and "fp32 or bf16" in err
+    assert _null_call(lib, "uocr_quantize_int8_g128", None, 1, 0, 256, None, None, None, None)[0] == 0  # no rows
+
+    assert lib.uocr_dense_packed_bytes(1280, 1280) == 10 * 10 * 32768
+    assert lib.uocr_dense_packed_bytes(300, 272) == 3 * 3 * 32768  # rows and K padded to 128
+    assert lib.uocr_dense_packed_bytes(16, 20) == 0  # K not a multiple of 16
+    rc, err = _null_call(lib, "uocr_dense_pack", None, 1, 64, 100, None, None)
+    assert rc == 1 and "multiple of 16" in err
+    rc, err = _null_call(lib, "uocr_dense_stream", None, 64, 256, None, 2, None, None, 0, None)
+    assert rc == 1 and err == "dense_stream: null pointer"
+    assert _null_call(lib, "uocr_dense_stream", None, 64, 256, None, 0, None, None, 0, None)[0] == 0  # M = 0
+
+    rc, err = _null_call(lib, "uocr_residual_rmsnorm", None, None, None, 2, 0, ctypes.c_float(1e-6), None, None)
+    assert rc == 1 and "bad shape" in err
+    rc, err = _null_call(lib, "uocr_residual_rmsnorm", None, None, None, 2, 8, ctypes.c_float(-1.0), None, None)
+    assert rc == 1 and "eps" in err
+
+    rc, err = _null_call(lib, "uocr_ngram_block", None, 2, 100, None, 0, None, None, None)
+    assert rc == 1 and err == "ngram_block: history is empty"
+    rc, err = _null_call(lib, "uocr_ngram_block", None, 2, 100, None, 8, None, None, None)
+    assert rc == 1 and err == "ngram_block: `ngram` must be a single int32"
+
+    assert lib.uocr_paged_attention_workspace_bytes(8, 10, 5) > 8192
+    assert lib.uocr_paged_attention_workspace_bytes(8, 13, 5) == 0
+    rc, err = _null_call(lib, "uocr_paged_decode_attention", None, None, None, 8, 10, 64, None, 4, 2, 0, None, 5,
+                         None, None, ctypes.c_float(0.1), None, None, 0, None)
+    assert rc == 4 and "head_dim" in err
+    rc, err = _null_call(lib, "uocr_paged_decode_attention", None, None, None, 8, 10, 128, None, 4, 2, 2, None, 5,
+                         None, None, ctypes.c_float(0.1), None, None, 0, None)
+    assert rc == 1 and "bad pool" in err
