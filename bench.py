@@ -575,6 +575,50 @@ def attention_row(torch, uocr, device, steps: int, warmup: int, B: int = 8, rows
             "what": f"B={B} requests x {rows} rows, {heads} heads x {dim}, fp32 page pool of {layers} layers"}
 
 
+# the decoder layers' decode step composed from the library's kernels: the headline's 11 MoE layers,
+# each with its norms, fused q|k|v, RoPE, paged attention over B = 8 requests of 640 cached rows, o
+def decoder_layers_row(torch, uocr, mods, device, steps: int, warmup: int, B: int = 8, rows: int = 640) -> dict:
+    """``DecoderDecodeStack`` over the headline's MoE layers with random bf16 attention weights and
+    norms, one CUDA graph per step, timed with CUDA events."""
+    dl = importlib.import_module(f"{PKG}.decode_layer")
+    gen = torch.Generator(device=device).manual_seed(9000)
+    heads, dim, cols = 10, 128, (rows + 127) // 128
+    layers = []
+    for i, m in enumerate(mods):
+        w = [(torch.randn((H, H), generator=gen, device=device) * 0.02).to(torch.bfloat16) for _ in range(4)]
+        gm = [(1 + 0.1 * torch.randn(H, generator=gen, device=device)).to(torch.bfloat16) for _ in range(2)]
+        layers.append(dl.DecoderLayerDecode(m, layer_idx=i, heads=heads, q_proj=w[0], k_proj=w[1], v_proj=w[2],
+                                            o_proj=w[3], input_norm=gm[0], post_norm=gm[1], kblocked=False))
+    stack = dl.DecoderDecodeStack(layers)
+    pages = B * cols + 1
+    pool = torch.randn((pages, 2, len(mods), 128, heads, dim), generator=gen, device=device)
+    cos_t, sin_t = dl.rope_tables(head_dim=dim, seq_len=rows, theta=10000.0)
+    step = {"cos": torch.from_numpy(cos_t[[rows - 1] * B]).to(device), "sin": torch.from_numpy(sin_t[[rows - 1] * B]).to(device),
+            "kv_pool": pool, "lut": torch.arange(B * cols, dtype=torch.int32, device=device).view(B, cols),
+            "write_index": torch.full((B,), rows - 1, dtype=torch.int32, device=device),
+            "attend_len": torch.full((B,), rows, dtype=torch.int32, device=device)}
+    h = 3 * torch.randn((B, H), generator=gen, device=device)
+    g = stack.graph(h, **step)
+    for _ in range(warmup):
+        g.replay()
+    torch.cuda.synchronize()
+    s = torch.cuda.current_stream(device)
+    t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    t0.record(s)
+    for _ in range(steps):
+        g.replay()
+    t1.record(s)
+    torch.cuda.synchronize()
+    ms = t0.elapsed_time(t1) / steps
+    stack.check_status()
+    L = len(mods)
+    del g, pool
+    return {"value": B / (ms * 1e-3), "unit": "tokens/s (decode steps/s x B)", "ms_per_step": ms,
+            "us_per_layer": ms * 1e3 / L, "launches_per_step": 9 * L, "outputs_finite": bool(torch.isfinite(h).all()),
+            "what": f"{L} decoder layers (norms, q|k|v, RoPE, paged attention over {rows} rows, o, int8 MoE), "
+                    f"B={B}, one CUDA graph"}
+
+
 # the int8 checkpoint quantiser: one MoE layer's routed experts, 3 x E x (I x H) bf16 elements
 def quant_row(torch, uocr, device, steps: int, warmup: int) -> dict:
     """``uocr_quantize_int8_g128`` over one layer's 192 expert projections (440 MB of bf16, far above
@@ -987,6 +1031,7 @@ def run_ours(args):
     value = world * B * L / (ms * 1e-3)
     e2e_ms, h2d, d2h = time_e2e(torch, g, xs, outs, max(args.steps // 4, 10), 3)
     stack_sub = None if args.no_sub else stack_row(torch, uocr, mods, device, max(args.steps // 4, 20), 3, B, ms)
+    layers_sub = None if args.no_sub else decoder_layers_row(torch, uocr, mods, device, max(args.steps // 4, 20), 3, B)
     if dist:
         t = torch.tensor([e2e_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -1012,6 +1057,7 @@ def run_ours(args):
             r["value"] *= world
             subs[f"prefill_{'int8' if int8 else 'bf16'}_{args.tokens}"] = r
         subs["decode_stack_int8_b8"] = stack_sub
+        subs["decoder_layers_b8"] = layers_sub
         subs["quantize_int8_layer"] = quant_row(torch, uocr, device, psteps, 3)
         subs["ngram_guard_b8"] = ngram_row(torch, uocr, device, psteps, 3)
         subs["paged_attention_b8"] = attention_row(torch, uocr, device, psteps, 3)

@@ -131,6 +131,14 @@ UOCR_API int uocr_paged_decode_attention(const float* q, const float* k_new, con
                                 const uint32_t* write_index, const uint32_t* attend_len, float scale,
                                 float* out, void* workspace, size_t workspace_bytes, uocr_stream_t stream);
 
+/* RoPE on the decode step's fused q|k|v projection output qkv [B][3 x heads x head_dim] (q, then k,
+ * then v, each heads x head_dim): q = x_q cos + rotate_half(x_q) sin, k likewise, v copied, into
+ * q, k, v [B][heads][head_dim]; cos, sin [B][head_dim] are the rotary table's rows at each row's
+ * position; each product and the sum rounded separately in fp32. Replaces Attention._rope on q and
+ * k in Attention.decode, decoder.py:459-462, 478-493. */
+UOCR_API int uocr_rope_qkv(const float* qkv, int64_t B, int64_t heads, int64_t head_dim, const float* cos,
+                  const float* sin, float* q, float* k, float* v, uocr_stream_t stream);
+
 /* ngram_block: the no-repeat-n-gram guard on B rows of V fp32 logits. Row b is guarded against
  * row b of history [B, H] int32 (that request's last H token ids, the newest last): every token
  * that would complete a repeat of the last n - 1 ids inside the history is set to -3.0e38 in out,

@@ -310,6 +310,18 @@ int uocr_paged_decode_attention(const float* q, const float* k_new, const float*
                        "paged_decode_attention: launch");
 }
 
+int uocr_rope_qkv(const float* qkv, int64_t B, int64_t heads, int64_t head_dim, const float* cos, const float* sin,
+                  float* q, float* k, float* v, uocr_stream_t stream) {
+    // Attention._rope / Attention.decode, decoder.py:459-462, 478-493
+    if (B < 0 || heads < 1 || head_dim < 2 || head_dim % 2 || (long long)B * heads * head_dim * 3 > INT32_MAX)
+        return fail(UOCR_EINVAL, "rope_qkv: bad shape (B %lld, heads %lld, head_dim %lld)", (long long)B,
+                    (long long)heads, (long long)head_dim);
+    if (B == 0) return ok();
+    if (!qkv || !cos || !sin || !q || !k || !v) return fail(UOCR_EINVAL, "rope_qkv: null pointer");
+    return cuda_status(uocr::launch_rope_qkv(qkv, (int)B, (int)heads, (int)head_dim, cos, sin, q, k, v, S(stream)),
+                       "rope_qkv: launch");
+}
+
 int uocr_ngram_block(const float* logits, int64_t B, int64_t V, const int32_t* history, int64_t H,
                      const int32_t* ngram, float* out, uocr_stream_t stream) {
     // kernels/ngram_block.mojo:80-105 (its shape checks), semantics :1-33

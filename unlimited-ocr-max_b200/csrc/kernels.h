@@ -47,6 +47,10 @@ cudaError_t launch_paged_decode_attention(const float* q, const float* k_new, co
                                           int heads, float scale, uint32_t* ctl, float* partial, int S,
                                           cudaStream_t st);
 
+// rope.cu: RoPE on the fused q|k|v rows [B, 3 x heads x dim] -> q, k (rotated), v, each [B, heads, dim]
+cudaError_t launch_rope_qkv(const float* qkv, int B, int heads, int dim, const float* cos, const float* sin, float* q,
+                            float* k, float* v, cudaStream_t st);
+
 // ngram.cu: the no-repeat-n-gram guard on B rows of V logits (out may alias logits)
 cudaError_t launch_ngram_block(const float* logits, int B, int V, const int32_t* history, int H, const int32_t* ngram,
                                float* out, bool vec, cudaStream_t st);
