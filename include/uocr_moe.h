@@ -139,6 +139,15 @@ UOCR_API int uocr_paged_decode_attention(const float* q, const float* k_new, con
 UOCR_API int uocr_rope_qkv(const float* qkv, int64_t B, int64_t heads, int64_t head_dim, const float* cos,
                   const float* sin, float* q, float* k, float* v, uocr_stream_t stream);
 
+/* The token embedding of the decode step: out[b] = fp32(table[clamp(ids[b], 0, vocab - 1)]) for a
+ * bf16 table [vocab, hidden]. Replaces EmbeddingTable, decoder.py:241-249 (a gather). */
+UOCR_API int uocr_embed_rows(const uint16_t* table, int64_t vocab, int64_t hidden, const int32_t* ids, int64_t B,
+                    float* out, uocr_stream_t stream);
+/* The dense FFN's activation on the fused gate|up output gate_up [B][2 x inter] (gate, then up):
+ * out[b][j] = silu(g) * u with silu(g) = g / (1 + e^-g) in fp32. Replaces ops.silu(gate) * up in
+ * GatedMlp.decode_rows, decoder.py:276-278. */
+UOCR_API int uocr_silu_mul(const float* gate_up, int64_t B, int64_t inter, float* out, uocr_stream_t stream);
+
 /* ngram_block: the no-repeat-n-gram guard on B rows of V fp32 logits. Row b is guarded against
  * row b of history [B, H] int32 (that request's last H token ids, the newest last): every token
  * that would complete a repeat of the last n - 1 ids inside the history is set to -3.0e38 in out,

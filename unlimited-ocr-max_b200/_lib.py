@@ -68,6 +68,8 @@ SIGNATURES: dict[str, tuple] = {
     "uocr_residual_rmsnorm": (I32, [P, P, P, I64, I64, ctypes.c_float, P, P]),
     "uocr_ngram_block": (I32, [P, I64, I64, P, I64, P, P, P]),
     "uocr_rope_qkv": (I32, [P, I64, I64, I64, P, P, P, P, P, P]),
+    "uocr_embed_rows": (I32, [P, I64, I64, P, I64, P, P]),
+    "uocr_silu_mul": (I32, [P, I64, I64, P, P]),
     "uocr_paged_attention_workspace_bytes": (SZ, [I64, I64, I64]),
     "uocr_paged_decode_attention": (I32, [P, P, P, I64, I64, I64, P, I64, I64, I64, P, I64, P, P, ctypes.c_float, P, P,
                                           SZ, P]),

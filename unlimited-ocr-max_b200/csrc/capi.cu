@@ -322,6 +322,27 @@ int uocr_rope_qkv(const float* qkv, int64_t B, int64_t heads, int64_t head_dim, 
                        "rope_qkv: launch");
 }
 
+int uocr_embed_rows(const uint16_t* table, int64_t vocab, int64_t hidden, const int32_t* ids, int64_t B, float* out,
+                    uocr_stream_t stream) {
+    // EmbeddingTable, decoder.py:241-249
+    if (vocab < 1 || hidden < 1 || B < 0 || vocab > INT32_MAX || (long long)B * hidden > INT32_MAX)
+        return fail(UOCR_EINVAL, "embed_rows: bad shape (vocab %lld, hidden %lld, B %lld)", (long long)vocab,
+                    (long long)hidden, (long long)B);
+    if (B == 0) return ok();
+    if (!table || !ids || !out) return fail(UOCR_EINVAL, "embed_rows: null pointer");
+    return cuda_status(uocr::launch_embed_rows(table, (int)vocab, (int)hidden, ids, (int)B, out, S(stream)),
+                       "embed_rows: launch");
+}
+
+int uocr_silu_mul(const float* gate_up, int64_t B, int64_t inter, float* out, uocr_stream_t stream) {
+    // GatedMlp.decode_rows, decoder.py:276-278
+    if (B < 0 || inter < 1 || (long long)B * inter * 2 > INT32_MAX)
+        return fail(UOCR_EINVAL, "silu_mul: bad shape (B %lld, inter %lld)", (long long)B, (long long)inter);
+    if (B == 0) return ok();
+    if (!gate_up || !out) return fail(UOCR_EINVAL, "silu_mul: null pointer");
+    return cuda_status(uocr::launch_silu_mul(gate_up, (int)B, (int)inter, out, S(stream)), "silu_mul: launch");
+}
+
 int uocr_ngram_block(const float* logits, int64_t B, int64_t V, const int32_t* history, int64_t H,
                      const int32_t* ngram, float* out, uocr_stream_t stream) {
     // kernels/ngram_block.mojo:80-105 (its shape checks), semantics :1-33

@@ -51,6 +51,11 @@ cudaError_t launch_paged_decode_attention(const float* q, const float* k_new, co
 cudaError_t launch_rope_qkv(const float* qkv, int B, int heads, int dim, const float* cos, const float* sin, float* q,
                             float* k, float* v, cudaStream_t st);
 
+// step.cu: the token embedding (bf16 table rows -> fp32, ids clamped) and the dense FFN's silu(g) * u
+cudaError_t launch_embed_rows(const uint16_t* table, int V, int H, const int32_t* ids, int B, float* out,
+                              cudaStream_t st);
+cudaError_t launch_silu_mul(const float* gu, int B, int I, float* out, cudaStream_t st);
+
 // ngram.cu: the no-repeat-n-gram guard on B rows of V logits (out may alias logits)
 cudaError_t launch_ngram_block(const float* logits, int B, int V, const int32_t* history, int H, const int32_t* ngram,
                                float* out, bool vec, cudaStream_t st);

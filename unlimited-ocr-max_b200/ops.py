@@ -243,3 +243,31 @@ def paged_decode_attention(q: torch.Tensor, k_new: torch.Tensor, v_new: torch.Te
         lut.data_ptr(), lut.shape[1], write_index.contiguous().data_ptr(), attend_len.contiguous().data_ptr(),
         float(scale), out.data_ptr(), ws.data_ptr(), ws.numel(), _stream(q)))
     return out
+
+
+def embed_rows(table: torch.Tensor, ids: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """The token embedding (EmbeddingTable, decoder.py:241-249): fp32 rows of the bf16 ``table
+    [vocab, hidden]`` at ``ids [B]`` (int32, clamped into the vocabulary)."""
+    op = "embed_rows"
+    _need_cuda(op, table, ids)
+    table = _need(op, table, "table", torch.bfloat16, 2)
+    ids = _need(op, ids, "ids", torch.int32, 1)
+    if out is None:
+        out = torch.empty((ids.shape[0], table.shape[1]), dtype=torch.float32, device=table.device)
+    check(load().uocr_embed_rows(table.data_ptr(), table.shape[0], table.shape[1], ids.data_ptr(), ids.shape[0],
+                                 out.data_ptr(), _stream(table)))
+    return out
+
+
+def silu_mul(gate_up: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """silu(g) * u on the fused gate|up rows ``[B, 2 x inter]`` (GatedMlp.decode_rows, decoder.py:276-278)."""
+    op = "silu_mul"
+    _need_cuda(op, gate_up)
+    gate_up = _need(op, gate_up, "gate_up", torch.float32, 2)
+    if gate_up.shape[1] % 2:
+        raise ValueError(f"{op}: gate_up must hold gate and up halves, got {gate_up.shape[1]} columns")
+    inter = gate_up.shape[1] // 2
+    if out is None:
+        out = torch.empty((gate_up.shape[0], inter), dtype=torch.float32, device=gate_up.device)
+    check(load().uocr_silu_mul(gate_up.data_ptr(), gate_up.shape[0], inter, out.data_ptr(), _stream(gate_up)))
+    return out
