@@ -619,6 +619,53 @@ def decoder_layers_row(torch, uocr, mods, device, steps: int, warmup: int, B: in
                     f"B={B}, one CUDA graph"}
 
 
+# the whole decode step at the model's shapes: token ids -> embedding -> layer 0 (dense FFN) + the
+# headline's 11 MoE layers (each with its attention over 640 cached rows) -> final norm -> lm_head ->
+# n-gram guard (window 128, n = 35), one CUDA graph, B = 1 and B = 8
+def decode_step_row(torch, uocr, mods, device, steps: int, warmup: int, rows: int = 640) -> dict:
+    dl = importlib.import_module(f"{PKG}.decode_layer")
+    gen = torch.Generator(device=device).manual_seed(9500)
+    w = lambda *s: (torch.randn(s, generator=gen, device=device) * 0.02).to(torch.bfloat16)  # noqa: E731
+    gm = lambda: (1 + 0.1 * torch.randn(H, generator=gen, device=device)).to(torch.bfloat16)  # noqa: E731
+    heads, dim, vocab, inter0, cols = 10, 128, 129280, 6848, (rows + 127) // 128
+    mlps = [dl.DenseFfn(w(inter0, H), w(inter0, H), w(H, inter0), device=device, kblocked=False)] + list(mods)
+    layers = [dl.DecoderLayerDecode(m, layer_idx=i, heads=heads, q_proj=w(H, H), k_proj=w(H, H), v_proj=w(H, H),
+                                    o_proj=w(H, H), input_norm=gm(), post_norm=gm(), kblocked=False)
+              for i, m in enumerate(mlps)]
+    step_fn = dl.DecoderDecodeStep(w(vocab, H), layers, gm(), w(vocab, H), kblocked=False)
+    cos_t, sin_t = dl.rope_tables(head_dim=dim, seq_len=rows, theta=10000.0)
+    out = {}
+    for B in (1, 8):
+        pool = torch.randn((B * cols + 1, 2, len(layers), 128, heads, dim), generator=gen, device=device)
+        step = {"cos": torch.from_numpy(cos_t[[rows - 1] * B]).to(device),
+                "sin": torch.from_numpy(sin_t[[rows - 1] * B]).to(device), "kv_pool": pool,
+                "lut": torch.arange(B * cols, dtype=torch.int32, device=device).view(B, cols),
+                "write_index": torch.full((B,), rows - 1, dtype=torch.int32, device=device),
+                "attend_len": torch.full((B,), rows, dtype=torch.int32, device=device),
+                "history": torch.randint(0, vocab, (B, 128), generator=gen, device=device, dtype=torch.int32),
+                "ngram": torch.tensor([35], dtype=torch.int32, device=device)}
+        ids = torch.randint(0, vocab, (B,), generator=gen, device=device, dtype=torch.int32)
+        g = step_fn.graph(ids, **step)
+        for _ in range(warmup):
+            g.replay()
+        torch.cuda.synchronize()
+        s = torch.cuda.current_stream(device)
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(s)
+        for _ in range(steps):
+            g.replay()
+        t1.record(s)
+        torch.cuda.synchronize()
+        ms = t0.elapsed_time(t1) / steps
+        out[f"b{B}"] = {"tokens_per_s": B / (ms * 1e-3), "ms_per_step": ms,
+                        "logits_finite": bool(torch.isfinite(step_fn.buffers(B)["logits"]).all())}
+        del g, pool
+    step_fn.check_status()
+    return {"value": out["b8"]["tokens_per_s"], "unit": "tokens/s (B = 8)", "by_batch": out,
+            "what": f"token ids -> embedding -> 12 decoder layers (layer 0 dense FFN, 11 int8 MoE; attention over "
+                    f"{rows} cached rows) -> final norm -> lm_head [{vocab}, {H}] -> n-gram guard, one CUDA graph"}
+
+
 # the int8 checkpoint quantiser: one MoE layer's routed experts, 3 x E x (I x H) bf16 elements
 def quant_row(torch, uocr, device, steps: int, warmup: int) -> dict:
     """``uocr_quantize_int8_g128`` over one layer's 192 expert projections (440 MB of bf16, far above
@@ -1032,6 +1079,7 @@ def run_ours(args):
     e2e_ms, h2d, d2h = time_e2e(torch, g, xs, outs, max(args.steps // 4, 10), 3)
     stack_sub = None if args.no_sub else stack_row(torch, uocr, mods, device, max(args.steps // 4, 20), 3, B, ms)
     layers_sub = None if args.no_sub else decoder_layers_row(torch, uocr, mods, device, max(args.steps // 4, 20), 3, B)
+    step_sub = None if args.no_sub else decode_step_row(torch, uocr, mods, device, max(args.steps // 10, 10), 3)
     if dist:
         t = torch.tensor([e2e_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -1058,6 +1106,7 @@ def run_ours(args):
             subs[f"prefill_{'int8' if int8 else 'bf16'}_{args.tokens}"] = r
         subs["decode_stack_int8_b8"] = stack_sub
         subs["decoder_layers_b8"] = layers_sub
+        subs["decode_step"] = step_sub
         subs["quantize_int8_layer"] = quant_row(torch, uocr, device, psteps, 3)
         subs["ngram_guard_b8"] = ngram_row(torch, uocr, device, psteps, 3)
         subs["paged_attention_b8"] = attention_row(torch, uocr, device, psteps, 3)
