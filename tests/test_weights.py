@@ -253,3 +253,20 @@ def test_uocr_moe_takes_the_reference_constructor_keywords(uocr):
         uocr.UocrMoE(cfg, device="cuda", norm_router_dtype="int8")
     with pytest.raises(ValueError, match="CUDA device only"):
         uocr.UocrMoE(cfg, dtype=torch.bfloat16, device="cpu")
+
+
+def test_rope_tables_follow_the_rotary_formula():
+    """The rotary table (decoder.py:115-123): position 0 is the identity, each column pair repeats,
+    angles grow as position x theta^(-2i/dim), cos^2 + sin^2 = 1."""
+    import importlib
+
+    import numpy as np
+
+    dl = importlib.import_module("unlimited-ocr-max_b200.decode_layer")
+    cos, sin = dl.rope_tables(head_dim=128, seq_len=64, theta=10000.0)
+    assert cos.shape == sin.shape == (64, 128) and cos.dtype == np.float32
+    assert np.array_equal(cos[0], np.ones(128, np.float32)) and np.array_equal(sin[0], np.zeros(128, np.float32))
+    assert np.array_equal(cos[:, :64], cos[:, 64:]) and np.array_equal(sin[:, :64], sin[:, 64:])
+    assert np.allclose(cos ** 2 + sin ** 2, 1.0, atol=1e-6)
+    ang = np.arange(64)[:, None] * (10000.0 ** (-np.arange(0, 128, 2) / 128.0))[None, :]
+    assert np.allclose(cos[:, :64], np.cos(ang), atol=2e-5) and np.allclose(sin[:, :64], np.sin(ang), atol=2e-5)
